@@ -1,0 +1,121 @@
+"""ctypes front end of the CPU oracle (test infrastructure only).
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline / reference
+legs import this module, and only as the checker.  The product's CUDA path
+never imports it.
+"""
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIBRARY = os.path.join(HERE, "_build", "libzlib_oracle.so")
+MAX_CANDIDATES = 262144
+MAX_BLOCKS = 262144
+
+_lib = None
+
+
+def build():
+    """Compile the oracle with gcc (make), if it is missing or stale."""
+    source = os.path.join(HERE, "zlib_oracle.c")
+    if (not os.path.exists(LIBRARY)
+            or os.path.getmtime(LIBRARY) < os.path.getmtime(source)):
+        subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIBRARY
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        build()
+        handle = ctypes.CDLL(LIBRARY)
+        u8p = ctypes.POINTER(ctypes.c_uint8)
+        u32p = ctypes.POINTER(ctypes.c_uint32)
+        handle.oracle_adler32.argtypes = [u8p, ctypes.c_uint64]
+        handle.oracle_adler32.restype = ctypes.c_uint32
+        handle.oracle_inflate_serial.argtypes = [u8p, ctypes.c_uint64, u8p, ctypes.c_uint64,
+                                                 ctypes.c_uint32]
+        handle.oracle_inflate_serial.restype = ctypes.c_uint32
+        handle.oracle_inflate_general.argtypes = [u8p, ctypes.c_uint64, u8p, ctypes.c_uint64,
+                                                  ctypes.c_uint32, ctypes.c_uint32]
+        handle.oracle_inflate_general.restype = ctypes.c_uint32
+        handle.oracle_decompress.argtypes = [u8p, ctypes.c_uint64, u8p, ctypes.c_uint64,
+                                             ctypes.c_uint32, ctypes.c_uint32]
+        handle.oracle_decompress.restype = ctypes.c_uint32
+        handle.oracle_compress.argtypes = [u8p, ctypes.c_uint64, ctypes.c_uint32, u8p,
+                                           ctypes.c_uint64, u32p]
+        handle.oracle_compress.restype = ctypes.c_uint32
+        handle.oracle_compress_chunks.argtypes = [u8p, ctypes.c_uint64, ctypes.c_uint32,
+                                                  ctypes.c_uint64, ctypes.c_uint64, u8p,
+                                                  ctypes.c_uint32, u32p]
+        handle.oracle_compress_chunks.restype = ctypes.c_uint32
+        _lib = handle
+    return _lib
+
+
+def _u8(array):
+    return array.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8))
+
+
+def _view(data):
+    array = np.frombuffer(data, dtype=np.uint8) if not isinstance(data, np.ndarray) else data
+    return np.ascontiguousarray(array, dtype=np.uint8)
+
+
+def adler32(data):
+    array = _view(data)
+    return lib().oracle_adler32(_u8(array), array.size)
+
+
+def decompress(payload, expected, max_candidates=MAX_CANDIDATES, max_blocks=MAX_BLOCKS):
+    """Single-stream decode with the reference's route semantics: (bytes, status)."""
+    source = _view(payload)
+    out = np.zeros(max(1, expected), dtype=np.uint8)
+    status = lib().oracle_decompress(_u8(source), source.size, _u8(out), expected,
+                                     max_candidates, max_blocks)
+    return out[:expected].tobytes(), int(status)
+
+
+def inflate_serial(payload, expected, max_blocks=MAX_BLOCKS):
+    """Serial-route decode (small streams, every batch file): (bytes, status)."""
+    source = _view(payload)
+    out = np.zeros(max(1, expected), dtype=np.uint8)
+    status = lib().oracle_inflate_serial(_u8(source), source.size, _u8(out), expected,
+                                         max_blocks)
+    if status:
+        out[:] = 0
+    return out[:expected].tobytes(), int(status)
+
+
+def inflate_general(payload, expected, max_candidates=MAX_CANDIDATES, max_blocks=MAX_BLOCKS):
+    source = _view(payload)
+    out = np.zeros(max(1, expected), dtype=np.uint8)
+    status = lib().oracle_inflate_general(_u8(source), source.size, _u8(out), expected,
+                                          max_candidates, max_blocks)
+    return out[:expected].tobytes(), int(status)
+
+
+def capacity(size, chunk_bytes=32768):
+    chunks = max(1, (size + chunk_bytes - 1) // chunk_bytes)
+    return size + 5 * chunks + 6
+
+
+def compress_padded(data, chunk_bytes=32768):
+    """Reference encoder restated: (padded buffer, [encoded_length, status])."""
+    source = _view(data)
+    cap = capacity(source.size, chunk_bytes)
+    out = np.zeros(cap, dtype=np.uint8)
+    meta = np.zeros(2, dtype=np.uint32)
+    lib().oracle_compress(_u8(source), source.size, chunk_bytes, _u8(out), cap,
+                          meta.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)))
+    return out, meta
+
+
+def compress(data, chunk_bytes=32768):
+    out, meta = compress_padded(data, chunk_bytes)
+    if meta[1]:
+        raise ValueError("oracle compression status %d" % meta[1])
+    return out[:meta[0]].tobytes()
