@@ -1,0 +1,452 @@
+// Host orchestration and the C ABI (include/cuda_zlib_b200.h).
+//
+// Mirrors the reference's handler layer (src/cuda_zlib/native/codec_ffi.cu):
+// argument validation with the same statuses and error returns, a per-device
+// stream-ordered scratch pool with a release threshold and stats/trim
+// controls, and route selection for single-stream decode.  Unlike the
+// reference, compression never reads its chunk sizes back to the host: the
+// sizes are scanned on the device, so every call is asynchronous.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <array>
+#include <cstdint>
+#include <mutex>
+#include <numeric>
+#include <vector>
+
+#include "../../include/cuda_zlib_b200.h"
+#include "kernels.h"
+
+namespace cz {
+namespace {
+
+constexpr u32 kMaxBytes = 1u << 28;
+constexpr u32 kMaxBlocks = 262144;
+constexpr u32 kMaxCandidates = 262144;
+constexpr u32 kTruncatedZlib = 14;
+constexpr u32 kInvalidBounds = 23;
+constexpr int kMaxDevices = 64;
+
+#define CZ_TRY(expression)                     \
+  do {                                         \
+    cudaError_t error_ = (expression);         \
+    if (error_ != cudaSuccess) return error_;  \
+  } while (false)
+
+// ---------------------------------------------------------------------------
+// Per-device state: launch facts and the scratch pool.
+// ---------------------------------------------------------------------------
+struct DeviceState {
+  bool ready = false;
+  DeviceInfo info{};
+  cudaMemPool_t pool = nullptr;
+};
+
+struct Registry {
+  std::mutex mutex;
+  u64 retention = 1ull << 30;
+  bool pools_created = false;
+  std::array<DeviceState, kMaxDevices> devices;
+};
+
+Registry& registry() {
+  static Registry* r = new Registry;  // process lifetime, no teardown CUDA calls
+  return *r;
+}
+
+cudaError_t device_state(int device, DeviceState** out) {
+  if (device < 0 || device >= kMaxDevices) return cudaErrorInvalidDevice;
+  Registry& r = registry();
+  std::lock_guard<std::mutex> lock(r.mutex);
+  DeviceState& d = r.devices[device];
+  if (!d.ready) {
+    DeviceInfo info{};
+    info.device = device;
+    CZ_TRY(cudaDeviceGetAttribute(&info.sms, cudaDevAttrMultiProcessorCount, device));
+    CZ_TRY(configure_serial_inflate(&info.serial_per_sm));
+    CZ_TRY(configure_encode(&info.encode_smem_limit));
+    cudaMemPoolProps props{};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.handleTypes = cudaMemHandleTypeNone;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = device;
+    cudaMemPool_t pool = nullptr;
+    CZ_TRY(cudaMemPoolCreate(&pool, &props));
+    cudaError_t e = cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &r.retention);
+    if (e != cudaSuccess) {
+      cudaMemPoolDestroy(pool);
+      return e;
+    }
+    d.info = info;
+    d.pool = pool;
+    d.ready = true;
+    r.pools_created = true;
+  }
+  *out = &d;
+  return cudaSuccess;
+}
+
+// Makes the stream's device current for the call and restores the caller's.
+class DeviceScope {
+ public:
+  explicit DeviceScope(cudaStream_t stream) {
+    error_ = cudaGetDevice(&previous_);
+    if (error_ != cudaSuccess) return;
+    device_ = previous_;
+    if (stream) {
+      error_ = cudaStreamGetDevice(stream, &device_);
+      if (error_ != cudaSuccess) return;
+    }
+    if (device_ != previous_) {
+      error_ = cudaSetDevice(device_);
+      switched_ = error_ == cudaSuccess;
+    }
+  }
+  ~DeviceScope() {
+    if (switched_) cudaSetDevice(previous_);
+  }
+  cudaError_t error() const { return error_; }
+  int device() const { return device_; }
+
+ private:
+  int previous_ = 0, device_ = 0;
+  bool switched_ = false;
+  cudaError_t error_ = cudaSuccess;
+};
+
+// Stream-ordered scratch for one call; freed on the same stream.
+class Workspace {
+ public:
+  Workspace(cudaMemPool_t pool, cudaStream_t stream) : pool_(pool), stream_(stream) {}
+  ~Workspace() { release(); }
+  template <typename T>
+  cudaError_t allocate(T** out, size_t count) {
+    void* p = nullptr;
+    CZ_TRY(cudaMallocFromPoolAsync(&p, std::max<size_t>(1, count) * sizeof(T), pool_, stream_));
+    held_.push_back(p);
+    *out = static_cast<T*>(p);
+    return cudaSuccess;
+  }
+  cudaError_t release() {
+    cudaError_t first = cudaSuccess;
+    while (!held_.empty()) {
+      cudaError_t e = cudaFreeAsync(held_.back(), stream_);
+      if (first == cudaSuccess) first = e;
+      held_.pop_back();
+    }
+    return first;
+  }
+
+ private:
+  cudaMemPool_t pool_;
+  cudaStream_t stream_;
+  std::vector<void*> held_;
+};
+
+__global__ void set_meta_kernel(u32* meta, u32 first, u32 second) {
+  meta[0] = first;
+  meta[1] = second;
+}
+
+cudaError_t set_meta(u32* meta, u32 first, u32 second, cudaStream_t stream) {
+  set_meta_kernel<<<1, 1, 0, stream>>>(meta, first, second);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t upload(Workspace& ws, T** out, const std::vector<T>& host, cudaStream_t stream) {
+  CZ_TRY(ws.allocate(out, host.size()));
+  if (host.empty()) return cudaSuccess;
+  // Pageable source: the copy stages the bytes before returning, so the
+  // vector may be released right after.
+  return cudaMemcpyAsync(*out, host.data(), host.size() * sizeof(T), cudaMemcpyHostToDevice,
+                         stream);
+}
+
+// ---------------------------------------------------------------------------
+// Encode (single stream and batch share one path).
+// ---------------------------------------------------------------------------
+cudaError_t encode_files(const DeviceState& dev, const u8* in, u64 in_bytes,
+                         std::vector<EncodeFile>& files, u32 chunk_bytes, u32 total_chunks,
+                         u8* out, u32* meta, cudaStream_t stream) {
+  Workspace ws(dev.pool, stream);
+  EncodeFile* d_files = nullptr;
+  u8* slots = nullptr;
+  u32 *sizes = nullptr, *status = nullptr;
+  u64 *adler = nullptr, *offsets = nullptr;
+  u16* spill_prev = nullptr;
+  u8* spill_len = nullptr;
+  CZ_TRY(upload(ws, &d_files, files, stream));
+  CZ_TRY(ws.allocate(&slots, in_bytes + 96 * (u64(total_chunks) + 2)));
+  CZ_TRY(ws.allocate(&sizes, total_chunks));
+  CZ_TRY(ws.allocate(&status, total_chunks));
+  CZ_TRY(ws.allocate(&adler, 2 * u64(total_chunks)));
+  CZ_TRY(ws.allocate(&offsets, total_chunks));
+  if (!encode_in_smem(chunk_bytes, dev.info)) {
+    const u64 entries = in_bytes + 16 * (u64(total_chunks) + 2);
+    CZ_TRY(ws.allocate(&spill_prev, entries));
+    CZ_TRY(ws.allocate(&spill_len, entries));
+  }
+  CZ_TRY(launch_encode(in, d_files, u32(files.size()), chunk_bytes, total_chunks, slots, sizes,
+                       status, adler, offsets, spill_prev, spill_len, out, meta, dev.info,
+                       stream));
+  return ws.release();
+}
+
+// ---------------------------------------------------------------------------
+// Entry point bodies (validation follows codec_ffi.cu line for line in effect).
+// ---------------------------------------------------------------------------
+cudaError_t compress(const u8* in, u64 size, int64_t chunk_bytes, u8* out, u64 capacity,
+                     u32* meta, cudaStream_t stream) {
+  if (!meta) return cudaErrorInvalidValue;
+  DeviceScope scope(stream);
+  CZ_TRY(scope.error());
+  DeviceState* dev = nullptr;
+  CZ_TRY(device_state(scope.device(), &dev));
+  // Compress (codec_ffi.cu:551-571): output bound, then zero, then input and
+  // chunk bounds; any violation is metadata [0, 23].
+  if (capacity > kMaxBytes) return set_meta(meta, 0, kInvalidBounds, stream);
+  if (capacity) {
+    if (!out) return cudaErrorInvalidValue;
+    CZ_TRY(cudaMemsetAsync(out, 0, capacity, stream));
+  }
+  if (size > kMaxBytes || chunk_bytes < 256 || chunk_bytes > 65535 || (size && !in))
+    return set_meta(meta, 0, kInvalidBounds, stream);
+  const u32 chunk = u32(chunk_bytes);
+  const u64 chunks = std::max<u64>(1, (size + chunk - 1) / chunk);
+  if (2 * chunks - 1 > kMaxBlocks || size + chunks * 5 + 6 > kMaxBytes ||
+      capacity != size + chunks * 5 + 6)
+    return set_meta(meta, 0, kInvalidBounds, stream);
+  std::vector<EncodeFile> files(1);
+  files[0] = EncodeFile{0, size, 0, capacity, 0, u32(chunks), chunk, 0};
+  return encode_files(*dev, in, size, files, chunk, u32(chunks), out, meta, stream);
+}
+
+cudaError_t compress_batch(const u8* in, u64 in_bytes, const int64_t* sizes, u64 count,
+                           int64_t chunk_bytes, u8* out, u64 out_bytes, u32* meta,
+                           cudaStream_t stream) {
+  // CompressBatchImpl (codec_ffi.cu:1002-1063).
+  if (!count || count > kMaxBlocks || !sizes || !meta) return cudaErrorInvalidValue;
+  if (in_bytes > kMaxBytes || out_bytes > kMaxBytes || chunk_bytes < 256 || chunk_bytes > 65535)
+    return cudaErrorInvalidValue;
+  const u32 chunk = u32(chunk_bytes);
+  std::vector<EncodeFile> files(count);
+  u64 in_extent = 0, out_extent = 0, total_chunks = 0;
+  for (u64 i = 0; i < count; ++i) {
+    const int64_t size = sizes[i];
+    if (size < 0 || size > int64_t(kMaxBytes)) return cudaErrorInvalidValue;
+    const u64 n = std::max<u64>(1, (u64(size) + chunk - 1) / chunk);
+    const u64 cap = u64(size) + n * 5 + 6;
+    if (2 * n - 1 > kMaxBlocks || in_extent + u64(size) > kMaxBytes ||
+        out_extent + cap > kMaxBytes || total_chunks + n > kMaxBlocks)
+      return cudaErrorInvalidValue;
+    files[i] = EncodeFile{in_extent, u64(size), out_extent, cap, u32(total_chunks), u32(n), chunk,
+                          0};
+    in_extent += u64(size);
+    out_extent += cap;
+    total_chunks += n;
+  }
+  if (in_extent != in_bytes || out_extent != out_bytes) return cudaErrorInvalidValue;
+  if ((in_bytes && !in) || !out) return cudaErrorInvalidValue;
+  DeviceScope scope(stream);
+  CZ_TRY(scope.error());
+  DeviceState* dev = nullptr;
+  CZ_TRY(device_state(scope.device(), &dev));
+  CZ_TRY(cudaMemsetAsync(out, 0, out_bytes, stream));
+  return encode_files(*dev, in, in_bytes, files, chunk, u32(total_chunks), out, meta, stream);
+}
+
+cudaError_t decompress(const u8* in, u64 size, int64_t max_candidates, int64_t max_blocks,
+                       u8* out, u64 expected, u32* meta, cudaStream_t stream) {
+  if (!meta) return cudaErrorInvalidValue;
+  DeviceScope scope(stream);
+  CZ_TRY(scope.error());
+  DeviceState* dev = nullptr;
+  CZ_TRY(device_state(scope.device(), &dev));
+  // Decompress (codec_ffi.cu:662-680).
+  if (expected > kMaxBytes) return set_meta(meta, kInvalidBounds, 0, stream);
+  if (expected && !out) return cudaErrorInvalidValue;
+  auto fail = [&](u32 status) -> cudaError_t {
+    if (expected) CZ_TRY(cudaMemsetAsync(out, 0, expected, stream));
+    return set_meta(meta, status, 0, stream);
+  };
+  if (size > kMaxBytes || max_candidates < 1 || max_candidates > int64_t(kMaxCandidates) ||
+      max_blocks < 1 || max_blocks > int64_t(kMaxBlocks))
+    return fail(kInvalidBounds);
+  if (size < 8) return fail(kTruncatedZlib);
+  if (!in) return cudaErrorInvalidValue;
+  const StreamDesc single{0, size, 0, expected};
+  const bool defaults = max_candidates == int64_t(kMaxCandidates) &&
+                        max_blocks == int64_t(kMaxBlocks);
+  Workspace ws(dev->pool, stream);
+  u32* counter = nullptr;
+  CZ_TRY(ws.allocate(&counter, 1));
+  CZ_TRY(cudaMemsetAsync(counter, 0, sizeof(u32), stream));
+  if (expected <= 65536 && size <= 131072 && defaults) {
+    // Small route: serial semantics (codec_ffi.cu:681-695).
+    CZ_TRY(launch_serial_inflate(in, out, nullptr, single, 1, nullptr, counter, meta, nullptr,
+                                 u32(max_blocks), dev->info, stream));
+    return ws.release();
+  }
+  // General route: candidate discovery (always: its count alone can fail a
+  // valid stream), a fast decode, then the route's exact status on failure.
+  const u64 body = size - 6;
+  u32 *bitmap = nullptr, *count = nullptr;
+  const u64 words = (body * 8 + 31) / 32 + 1;
+  CZ_TRY(ws.allocate(&bitmap, words));
+  CZ_TRY(ws.allocate(&count, 1));
+  CZ_TRY(cudaMemsetAsync(bitmap, 0, words * sizeof(u32), stream));
+  CZ_TRY(cudaMemsetAsync(count, 0, sizeof(u32), stream));
+  CZ_TRY(launch_discover(in, size, bitmap, count, nullptr, dev->info, stream));
+  CZ_TRY(launch_serial_inflate(in, out, nullptr, single, 1, nullptr, counter, meta, nullptr,
+                               u32(max_blocks), dev->info, stream));
+  CZ_TRY(launch_general_status(in, size, expected, u32(max_candidates), u32(max_blocks), bitmap,
+                               count, meta, out, stream));
+  return ws.release();
+}
+
+cudaError_t decompress_batch(const u8* in, u64 in_bytes, const int64_t* in_sizes,
+                             const int64_t* out_sizes, u64 count, const u32* encoded, u8* out,
+                             u64 out_bytes, u32* meta, cudaStream_t stream) {
+  // DecompressBatchImpl (codec_ffi.cu:1065-1107).
+  if (!count || count > kMaxBlocks || !in_sizes || !out_sizes || !meta)
+    return cudaErrorInvalidValue;
+  if (in_bytes > kMaxBytes || out_bytes > kMaxBytes) return cudaErrorInvalidValue;
+  std::vector<StreamDesc> descs(count);
+  u64 in_extent = 0, out_extent = 0;
+  for (u64 i = 0; i < count; ++i) {
+    const int64_t size = in_sizes[i], want = out_sizes[i];
+    if (size < 0 || want < 0 || size > int64_t(kMaxBytes) || want > int64_t(kMaxBytes) ||
+        in_extent + u64(size) > kMaxBytes || out_extent + u64(want) > kMaxBytes)
+      return cudaErrorInvalidValue;
+    descs[i] = StreamDesc{in_extent, u64(size), out_extent, u64(want)};
+    in_extent += u64(size);
+    out_extent += u64(want);
+  }
+  if (in_extent != in_bytes || out_extent != out_bytes) return cudaErrorInvalidValue;
+  if ((in_bytes && !in) || (out_bytes && !out)) return cudaErrorInvalidValue;
+  // Largest outputs first, so long streams start early.
+  std::vector<u32> order(count);
+  std::iota(order.begin(), order.end(), 0u);
+  std::stable_sort(order.begin(), order.end(), [&](u32 a, u32 b) {
+    return descs[a].out_size + descs[a].in_size > descs[b].out_size + descs[b].in_size;
+  });
+  DeviceScope scope(stream);
+  CZ_TRY(scope.error());
+  DeviceState* dev = nullptr;
+  CZ_TRY(device_state(scope.device(), &dev));
+  Workspace ws(dev->pool, stream);
+  StreamDesc* d_descs = nullptr;
+  u32 *d_order = nullptr, *counter = nullptr;
+  CZ_TRY(upload(ws, &d_descs, descs, stream));
+  CZ_TRY(upload(ws, &d_order, order, stream));
+  CZ_TRY(ws.allocate(&counter, 1));
+  CZ_TRY(cudaMemsetAsync(counter, 0, sizeof(u32), stream));
+  CZ_TRY(launch_serial_inflate(in, out, d_descs, descs[0], u32(count), d_order, counter, meta,
+                               encoded, kMaxBlocks, dev->info, stream));
+  return ws.release();
+}
+
+cudaError_t inspect_pools(int device, u64* stats, bool trim) {
+  Registry& r = registry();
+  cudaMemPool_t pool = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(r.mutex);
+    stats[0] = r.retention;
+    stats[1] = stats[2] = stats[3] = 0;
+    if (device >= 0 && device < kMaxDevices && r.devices[device].ready)
+      pool = r.devices[device].pool;
+  }
+  if (!pool) return cudaSuccess;
+  if (trim) CZ_TRY(cudaMemPoolTrimTo(pool, 0));
+  u64 reserved = 0, used = 0;
+  CZ_TRY(cudaMemPoolGetAttribute(pool, cudaMemPoolAttrReservedMemCurrent, &reserved));
+  CZ_TRY(cudaMemPoolGetAttribute(pool, cudaMemPoolAttrUsedMemCurrent, &used));
+  stats[1] = reserved;
+  stats[2] = used;
+  stats[3] = 1;
+  return cudaSuccess;
+}
+
+}  // namespace
+}  // namespace cz
+
+extern "C" {
+
+int cuda_zlib_compress(const uint8_t* input, uint64_t size, int64_t chunk_bytes, uint8_t* output,
+                       uint64_t capacity, uint32_t* metadata, void* stream) {
+  try {
+    return int(cz::compress(input, size, chunk_bytes, output, capacity, metadata,
+                            static_cast<cudaStream_t>(stream)));
+  } catch (...) {
+    return int(cudaErrorUnknown);
+  }
+}
+
+int cuda_zlib_decompress(const uint8_t* input, uint64_t size, int64_t max_candidates,
+                         int64_t max_blocks, uint8_t* output, uint64_t expected,
+                         uint32_t* metadata, void* stream) {
+  try {
+    return int(cz::decompress(input, size, max_candidates, max_blocks, output, expected, metadata,
+                              static_cast<cudaStream_t>(stream)));
+  } catch (...) {
+    return int(cudaErrorUnknown);
+  }
+}
+
+int cuda_zlib_compress_batch(const uint8_t* input, uint64_t input_bytes,
+                             const int64_t* input_sizes, uint64_t files, int64_t chunk_bytes,
+                             uint8_t* output, uint64_t output_bytes, uint32_t* metadata,
+                             void* stream) {
+  try {
+    return int(cz::compress_batch(input, input_bytes, input_sizes, files, chunk_bytes, output,
+                                  output_bytes, metadata, static_cast<cudaStream_t>(stream)));
+  } catch (...) {
+    return int(cudaErrorUnknown);
+  }
+}
+
+int cuda_zlib_decompress_batch(const uint8_t* input, uint64_t input_bytes,
+                               const int64_t* input_sizes, const int64_t* output_sizes,
+                               uint64_t files, const uint32_t* encoded_metadata, uint8_t* output,
+                               uint64_t output_bytes, uint32_t* metadata, void* stream) {
+  try {
+    return int(cz::decompress_batch(input, input_bytes, input_sizes, output_sizes, files,
+                                    encoded_metadata, output, output_bytes, metadata,
+                                    static_cast<cudaStream_t>(stream)));
+  } catch (...) {
+    return int(cudaErrorUnknown);
+  }
+}
+
+int CudaZlibSetWorkspaceRetention(uint64_t bytes) {
+  cz::Registry& r = cz::registry();
+  std::lock_guard<std::mutex> lock(r.mutex);
+  if (r.pools_created) return int(cudaErrorInvalidValue);
+  r.retention = bytes;
+  return int(cudaSuccess);
+}
+
+int CudaZlibWorkspacePoolStats(int device, uint64_t* stats) {
+  if (device < 0 || !stats) return int(cudaErrorInvalidValue);
+  try {
+    return int(cz::inspect_pools(device, stats, false));
+  } catch (...) {
+    return int(cudaErrorUnknown);
+  }
+}
+
+int CudaZlibTrimWorkspacePool(int device) {
+  if (device < 0) return int(cudaErrorInvalidValue);
+  try {
+    uint64_t stats[4];
+    return int(cz::inspect_pools(device, stats, true));
+  } catch (...) {
+    return int(cudaErrorUnknown);
+  }
+}
+
+const char* cuda_zlib_b200_version(void) { return "0.1.0"; }
+
+}  // extern "C"

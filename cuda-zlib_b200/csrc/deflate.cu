@@ -1,0 +1,773 @@
+// Chunk-parallel Deflate encoder, byte-identical to the reference encoder.
+//
+// The reference (encode_chunk, src/cuda_zlib/_encode_kernels.py:283-400)
+// parses each chunk greedily with a one-candidate hash table in which every
+// position is inserted in order.  The candidate of position p is therefore a
+// pure function of the data: the last earlier position q with the same 13-bit
+// hash (enc_hash, :47-51).  This kernel exploits that:
+//
+//   1. stage the chunk in shared memory and fuse its Adler-32 partial sums;
+//   2. one warp computes every position's candidate with __match_any_sync
+//      over 32 positions at a time (lanes sharing a hash see each other);
+//   3. 256 threads each walk the greedy parse from the start of their own
+//      segment of the chunk, speculatively;
+//   4. one thread stitches the segments: an entry point that differs from the
+//      speculative start is re-walked until it meets the speculative chain,
+//      which greedy parsing does within a token or two;
+//   5. all threads build the literal/length and distance histograms;
+//   6. the trees follow enc_tree (:65-157) exactly: the reference pops its
+//      heap by (weight, node id); a two-queue merge over leaves sorted by
+//      (weight, id) and internal nodes in creation order picks the same pair
+//      at every step, so depths, flattening retries and codes are identical;
+//   7. the exact stored/fixed/dynamic extents (:312-356) choose the block;
+//   8. a block-wide prefix sum over per-segment bit counts places every
+//      token, and threads pack their segments into 32-bit words in parallel
+//      (word edges shared with a neighbour use atomicOr).
+//
+// A nonfinal chunk ends with an empty stored block so chunks concatenate
+// byte-aligned (:384-388).  Finish kernels scan the chunk sizes on the device
+// (no host round trip, unlike CompressionPrefix + ReadWords, codec_ffi.cu:
+// 362-390,590-595), combine the Adler partials and pack the slots.
+#include "kernels.h"
+#include "common.cuh"
+
+namespace cz {
+
+constexpr u32 kEncThreads = 256;
+constexpr u32 kHashSlots = 8192;
+
+__constant__ u16 kLenBase[29] = {3,  4,  5,  6,  7,  8,  9,  10, 11,  13,  15,  17,  19,  23, 27,
+                                 31, 35, 43, 51, 59, 67, 83, 99, 115, 131, 163, 195, 227, 258};
+__constant__ u8 kLenExtra[29] = {0, 0, 0, 0, 0, 0, 0, 0, 1, 1, 1, 1, 2, 2, 2,
+                                 2, 3, 3, 3, 3, 4, 4, 4, 4, 5, 5, 5, 5, 0};
+__constant__ u16 kDistBase[30] = {1,    2,    3,    4,    5,    7,     9,     13,    17,  25,
+                                  33,   49,   65,   97,   129,  193,   257,   385,   513, 769,
+                                  1025, 1537, 2049, 3073, 4097, 6145, 8193, 12289, 16385, 24577};
+__constant__ u8 kDistExtra[30] = {0, 0, 0, 0, 1, 1, 2, 2,  3,  3,  4,  4,  5,  5,  6,
+                                  6, 7, 7, 8, 8, 9, 9, 10, 10, 11, 11, 12, 12, 13, 13};
+__constant__ u8 kClOrder[19] = {16, 17, 18, 0, 8, 7, 9, 6, 10, 5, 11, 4, 12, 3, 13, 2, 14, 1, 15};
+
+__device__ __forceinline__ u32 hash3(const u8* d, u32 p) {
+  const u32 v = u32(d[p]) | (u32(d[p + 1]) << 8) | (u32(d[p + 2]) << 16);
+  return (v * 2654435761u) >> 19;
+}
+__device__ __forceinline__ u32 length_symbol(u32 len) {  // index 0..28 for 3..258
+  if (len == 258) return 28;
+  if (len <= 10) return len - 3;
+  const u32 x = len - 3, b = 31 - __clz(x);
+  return 4 * (b - 1) + ((x >> (b - 2)) & 3u);
+}
+__device__ __forceinline__ u32 dist_symbol(u32 dist) {  // index 0..29 for 1..32768
+  if (dist <= 4) return dist - 1;
+  const u32 x = dist - 1, b = 31 - __clz(x);
+  return 2 * b + ((x >> (b - 1)) & 1u);
+}
+__device__ __forceinline__ u32 reverse_bits(u32 x, u32 n) { return n ? __brev(x) >> (32 - n) : 0; }
+__device__ __forceinline__ u32 fixed_ll_len(u32 s) {
+  return s <= 143 ? 8u : s <= 255 ? 9u : s <= 279 ? 7u : 8u;
+}
+__device__ __forceinline__ u32 fixed_ll_code(u32 s) {  // bit-reversed, ready to put
+  u32 code;
+  if (s <= 143) code = 0x30u + s;
+  else if (s <= 255) code = 0x190u + s - 144u;
+  else if (s <= 279) code = s - 256u;
+  else code = 0xc0u + s - 280u;
+  return reverse_bits(code, fixed_ll_len(s));
+}
+__device__ __forceinline__ u32 extent_of(u32 bits, bool final) {
+  return final ? (bits + 7) / 8 : (bits + 3 + 7) / 8 + 4;
+}
+
+// Shared state of one chunk (beyond the dynamically sized arrays).
+struct EncodeShared {
+  u32 freq[335];        // 0..285 lit/len, 286..315 dist, 316..334 code-length
+  u8 lengths[336];
+  u16 codes[336];
+  u32 weight[576];
+  u16 parent[576];
+  u16 sorted[288];
+  u8 depth[576];
+  u8 rle_sym[320];
+  u8 rle_extra[320];
+  u32 seg_exit[kEncThreads];
+  u32 seg_bits[kEncThreads];
+  u32 warp_sums[kEncThreads / 32];
+  u64 adler_s1[kEncThreads / 32];
+  u64 adler_s2[kEncThreads / 32];
+  u32 extra_bits, token_count, dist_tokens;
+  u32 mode, extent, status, ok, nll, ndist, ncl, rle_size, header_bits, leaves;
+};
+
+// Two-queue Huffman build with the reference's (weight, id) order and
+// flattening retries.  All threads call; thread 0 merges.  Returns on all
+// threads whether a tree within `limit` was found.
+__device__ bool cta_tree(EncodeShared& s, const u32* freq, u32 alphabet, u32 limit, u8* lengths,
+                         u16* codes) {
+  const u32 tid = threadIdx.x;
+  for (u32 shift = 0; shift <= 16; ++shift) {
+    for (u32 i = tid; i < alphabet; i += kEncThreads) {
+      lengths[i] = 0;
+      codes[i] = 0;
+      s.weight[i] = freq[i] ? ((freq[i] + (1u << shift) - 1u) >> shift) : 0u;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      // Leaf set, with the reference's dummy leaves for empty and one-symbol
+      // alphabets (a complete tree is always produced).
+      u32 m = 0, only = 0;
+      for (u32 i = 0; i < alphabet; ++i)
+        if (s.weight[i]) { ++m; only = i; }
+      if (!m) { s.weight[0] = 1; m = 1; only = 0; }
+      if (m == 1) {
+        const u32 dummy = only ? 0u : 1u;
+        s.weight[dummy] = 1;
+        m = 2;
+      }
+      s.leaves = m;
+    }
+    __syncthreads();
+    // Rank leaves by (weight, id).
+    for (u32 i = tid; i < alphabet; i += kEncThreads) {
+      const u32 w = s.weight[i];
+      if (!w) continue;
+      u32 rank = 0;
+      for (u32 j = 0; j < alphabet; ++j) {
+        const u32 v = s.weight[j];
+        rank += (v && (v < w || (v == w && j < i))) ? 1u : 0u;
+      }
+      s.sorted[rank] = u16(i);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      const u32 m = s.leaves;
+      u32 leaf = 0, inner = alphabet, next = alphabet;
+      for (u32 step = 0; step + 1 < m; ++step) {
+        u32 pick[2];
+        for (u32 k = 0; k < 2; ++k) {
+          bool take_leaf;
+          if (leaf >= m) take_leaf = false;
+          else if (inner == next) take_leaf = true;
+          else {
+            const u32 a = s.sorted[leaf];
+            const u32 wa = s.weight[a], wb = s.weight[inner];
+            take_leaf = wa < wb || (wa == wb && a < inner);
+          }
+          pick[k] = take_leaf ? u32(s.sorted[leaf++]) : inner++;
+        }
+        s.weight[next] = s.weight[pick[0]] + s.weight[pick[1]];
+        s.parent[pick[0]] = u16(next);
+        s.parent[pick[1]] = u16(next);
+        ++next;
+      }
+      // Depths from the root down (parents are created after children).
+      const u32 root = next - 1;
+      s.depth[root] = 0;
+      for (u32 node = root; node-- > alphabet;) s.depth[node] = s.depth[s.parent[node]] + 1;
+      u32 overlong = 0;
+      u32 count[16];
+      for (u32 l = 0; l < 16; ++l) count[l] = 0;
+      for (u32 i = 0; i < alphabet; ++i) {
+        if (!s.weight[i]) continue;
+        const u32 d = s.depth[s.parent[i]] + 1u;
+        if (d > limit) { overlong = 1; continue; }
+        lengths[i] = u8(d);
+        ++count[d];
+      }
+      if (!overlong) {
+        u32 first[16];
+        u32 code = 0;
+        first[0] = 0;
+        for (u32 b = 1; b <= limit; ++b) {
+          code = (code + count[b - 1]) << 1;
+          first[b] = code;
+        }
+        for (u32 i = 0; i < alphabet; ++i)
+          if (lengths[i]) codes[i] = u16(reverse_bits(first[lengths[i]]++, lengths[i]));
+      }
+      s.ok = overlong ? 0u : 1u;
+    }
+    __syncthreads();
+    if (s.ok) return true;
+  }
+  return false;
+}
+
+// Append `n` bits of `value` to the packing accumulator; full 32-bit words
+// go to `words` (little-endian bit order, LSB first).  Edge words are ORed.
+struct Packer {
+  u32* words;
+  u64 acc;
+  u32 nacc;   // bits in acc
+  u64 word;   // index of the word acc starts at
+  u64 first_word, last_word;  // this thread's shared edge words
+  u64 limit;  // words past the slot are dropped (the size check then fails)
+
+  __device__ __forceinline__ void start(u32* w, u64 bit, u64 end_bit, u64 limit_words) {
+    limit = limit_words;
+    words = w;
+    word = bit >> 5;
+    nacc = u32(bit & 31);
+    acc = 0;
+    first_word = word;
+    last_word = end_bit ? (end_bit - 1) >> 5 : 0;
+  }
+  __device__ __forceinline__ void flush_word(u32 v) {
+    if (word < limit) {
+      if (word == first_word || word == last_word) atomicOr(words + word, v);
+      else words[word] = v;
+    }
+    ++word;
+  }
+  __device__ __forceinline__ void put(u32 value, u32 n) {
+    acc |= u64(value) << nacc;
+    nacc += n;
+    if (nacc >= 32) {
+      flush_word(u32(acc));
+      acc >>= 32;
+      nacc -= 32;
+    }
+  }
+  __device__ __forceinline__ void finish() {
+    if (nacc && word < limit) atomicOr(words + word, u32(acc));
+  }
+};
+
+// Slot of chunk g: starts at 16-aligned (input position + 96 g), so a slot
+// holds at least n + 80 bytes and all slots fit in in_bytes + 96 (chunks+1).
+__device__ __forceinline__ u64 slot_start(u64 in_pos, u32 g) {
+  return ((in_pos + 15) & ~u64(15)) + 96 * u64(g);
+}
+
+__global__ void __launch_bounds__(kEncThreads)
+encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ files, u32 nfiles,
+                     u32 chunk_bytes, u32 total_chunks, u8* slots, u32* sizes, u32* status,
+                     u64* adler, u16* spill_prev, u8* spill_len, u32 in_smem) {
+  extern __shared__ __align__(16) u8 smem[];
+  __shared__ EncodeShared s;
+  const u32 tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+  const u32 g = blockIdx.x;
+  if (g >= total_chunks) return;
+  // File of this chunk (files are sorted by first_chunk).
+  u32 lo = 0, hi = nfiles;
+  while (hi - lo > 1) {
+    const u32 mid = (lo + hi) >> 1;
+    if (files[mid].first_chunk <= g) lo = mid;
+    else hi = mid;
+  }
+  const EncodeFile f = files[lo];
+  const u32 local = g - f.first_chunk;
+  const u64 start = u64(local) * chunk_bytes;
+  const u32 n = u32(min_u64(f.in_size - min_u64(start, f.in_size), chunk_bytes));
+  const bool final = local + 1 == f.chunks;
+  const u8* src = in + f.in_offset + start;
+
+  // Shared layout: data | member bits | match bits | hash table | prev | len.
+  const u32 data_bytes = (chunk_bytes + 16 + 15) & ~15u;
+  const u32 bit_words = (chunk_bytes + 31) / 32 + 1;
+  u8* data = smem;
+  u32* member = reinterpret_cast<u32*>(smem + data_bytes);
+  u32* ismatch = member + bit_words;
+  u16* table = reinterpret_cast<u16*>(ismatch + bit_words);
+  u16* prev;
+  u8* lenv;
+  if (in_smem) {
+    prev = table + kHashSlots;
+    lenv = reinterpret_cast<u8*>(prev + ((chunk_bytes + 7) & ~7u));
+  } else {
+    const u64 at = f.in_offset + start + 16 * u64(g);
+    prev = spill_prev + at;
+    lenv = spill_len + at;
+  }
+
+  // 1. Stage the chunk (zero padded) and its Adler-32 partial sums.
+  u64 s1 = 0, s2 = 0;
+  for (u32 i = tid; i < data_bytes; i += kEncThreads) {
+    const u32 x = i < n ? u32(src[i]) : 0u;
+    data[i] = u8(x);
+    s1 += x;
+    s2 += u64(n - i) * x;  // x == 0 beyond n
+  }
+  for (u32 i = tid; i < bit_words; i += kEncThreads) { member[i] = 0; ismatch[i] = 0; }
+  for (u32 i = tid; i < kHashSlots; i += kEncThreads) table[i] = 0;
+  for (u32 i = tid; i < 335; i += kEncThreads) s.freq[i] = 0;
+  for (u32 o = 16; o; o >>= 1) {
+    s1 += __shfl_xor_sync(kFullMask, s1, o);
+    s2 += __shfl_xor_sync(kFullMask, s2, o);
+  }
+  if (lane == 0) { s.adler_s1[warp] = s1; s.adler_s2[warp] = s2; }
+  if (tid == 0) { s.extra_bits = 0; s.token_count = 0; s.dist_tokens = 0; s.status = 0; }
+  __syncthreads();
+  if (tid == 0) {
+    u64 a = 0, b = 0;
+    for (u32 w = 0; w < kEncThreads / 32; ++w) { a += s.adler_s1[w]; b += s.adler_s2[w]; }
+    adler[2 * u64(g)] = a;
+    adler[2 * u64(g) + 1] = b;
+  }
+
+  // 2. Candidates: prev[p] = 1 + last earlier position with hash(p), or 0.
+  const u32 hashed = n >= 3 ? n - 2 : 0;  // positions 0..n-3 are hashed
+  if (warp == 0) {
+    for (u32 base = 0; base < hashed; base += 32) {
+      const u32 p = base + lane;
+      const bool valid = p < hashed;
+      const u32 h = valid ? hash3(data, p) : (kHashSlots + lane);
+      const u32 group = __match_any_sync(kFullMask, h);
+      const u32 lower = group & ((1u << lane) - 1u);
+      u32 candidate = 0;
+      if (valid) candidate = lower ? base + (31 - __clz(lower)) + 1 : table[h];
+      __syncwarp();
+      const u32 higher = lane == 31 ? 0u : (group >> (lane + 1));
+      if (valid && !higher) table[h] = u16(p + 1);
+      if (valid) prev[p] = u16(candidate);
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+
+  // 3. Speculative greedy walks, one segment per thread.
+  const u32 seg = (n + kEncThreads - 1) / kEncThreads;
+  auto token_at = [&](u32 p) -> u32 {  // match length at p, or 0 for a literal
+    if (p >= hashed) return 0;
+    const u32 c = prev[p];
+    if (!c) return 0;
+    const u32 q = c - 1, dist = p - q;
+    if (dist > 32768u || data[q] != data[p] || data[q + 1] != data[p + 1] ||
+        data[q + 2] != data[p + 2])
+      return 0;
+    const u32 limit = min_u32(n - p, 258u);
+    u32 m = 3;
+    while (m < limit && data[q + m] == data[p + m]) ++m;
+    return m;
+  };
+  {
+    const u32 a = min_u32(tid * seg, n), b = min_u32(a + seg, n);
+    u32 p = a;
+    while (p < b) {
+      const u32 m = token_at(p);
+      atomicOr(&member[p >> 5], 1u << (p & 31));
+      if (m) {
+        atomicOr(&ismatch[p >> 5], 1u << (p & 31));
+        lenv[p] = u8(m - 3);
+        p += m;
+      } else {
+        ++p;
+      }
+    }
+    s.seg_exit[tid] = p;
+  }
+  __syncthreads();
+
+  // 4. Stitch the segments in order.
+  if (tid == 0) {
+    u32 entry = 0;
+    for (u32 t = 0; t < kEncThreads; ++t) {
+      const u32 a = min_u32(t * seg, n), b = min_u32(a + seg, n);
+      if (a >= b) break;
+      if (entry >= b) {
+        // The previous token covers this whole segment.
+        for (u32 p = a; p < b; ++p) member[p >> 5] &= ~(1u << (p & 31));
+        continue;
+      }
+      for (u32 p = a; p < entry; ++p) member[p >> 5] &= ~(1u << (p & 31));
+      u32 p = entry;
+      while (p < b && !((member[p >> 5] >> (p & 31)) & 1u)) {
+        const u32 m = token_at(p);
+        member[p >> 5] |= 1u << (p & 31);
+        if (m) {
+          ismatch[p >> 5] |= 1u << (p & 31);
+          lenv[p] = u8(m - 3);
+          for (u32 k = p + 1; k < p + m && k < b; ++k) member[k >> 5] &= ~(1u << (k & 31));
+          p += m;
+        } else {
+          ismatch[p >> 5] &= ~(1u << (p & 31));
+          ++p;
+        }
+      }
+      entry = p < b ? s.seg_exit[t] : p;
+    }
+  }
+  __syncthreads();
+
+  // 5. Histograms over this thread's segment.
+  const u32 a = min_u32(tid * seg, n), b = min_u32(a + seg, n);
+  {
+    u32 extra = 0, tokens = 0, dists = 0;
+    for (u32 p = a; p < b; ++p) {
+      if (!((member[p >> 5] >> (p & 31)) & 1u)) continue;
+      ++tokens;
+      if ((ismatch[p >> 5] >> (p & 31)) & 1u) {
+        const u32 m = u32(lenv[p]) + 3, dist = p - (u32(prev[p]) - 1);
+        const u32 li = length_symbol(m), di = dist_symbol(dist);
+        atomicAdd(&s.freq[257 + li], 1u);
+        atomicAdd(&s.freq[286 + di], 1u);
+        extra += kLenExtra[li] + kDistExtra[di];
+        ++dists;
+      } else {
+        atomicAdd(&s.freq[data[p]], 1u);
+      }
+    }
+    atomicAdd(&s.extra_bits, extra);
+    atomicAdd(&s.token_count, tokens);
+    atomicAdd(&s.dist_tokens, dists);
+  }
+  __syncthreads();
+
+  // 6-7. Block type by exact extent (encode_chunk, _encode_kernels.py:312-356).
+  if (tid == 0) {
+    s.freq[256] += 1;
+    u32 fixed_bits = 3 + s.extra_bits;
+    for (u32 i = 0; i < 286; ++i) fixed_bits += s.freq[i] * fixed_ll_len(i);
+    fixed_bits += s.dist_tokens * 5;
+    s.mode = 0;
+    s.extent = n + 5;
+    const u32 fixed_extent = extent_of(fixed_bits, final);
+    if (fixed_extent < s.extent) { s.extent = fixed_extent; s.mode = 1; }
+    s.ok = extent_of(29 + s.extra_bits + s.token_count + 1 + s.dist_tokens, final) < s.extent;
+  }
+  __syncthreads();
+  bool trees = true;
+  bool dynamic = s.ok != 0;
+  if (dynamic) {
+    trees = cta_tree(s, s.freq, 286, 15, s.lengths, s.codes);
+    if (tid == 0) {
+      u32 ll_bits = 0;
+      for (u32 i = 0; i < 286; ++i) ll_bits += s.freq[i] * s.lengths[i];
+      s.header_bits = ll_bits;  // reused below as ll_bits
+      s.ok = extent_of(29 + s.extra_bits + ll_bits + s.dist_tokens, final) < s.extent;
+    }
+    __syncthreads();
+    dynamic = s.ok != 0;
+  }
+  if (trees && dynamic) {
+    trees = cta_tree(s, s.freq + 286, 30, 15, s.lengths + 286, s.codes + 286);
+    if (tid == 0) {
+      u32 nll = 286, ndist = 30;
+      while (nll > 257 && !s.lengths[nll - 1]) --nll;
+      while (ndist > 1 && !s.lengths[286 + ndist - 1]) --ndist;
+      // Run-length code the code lengths (enc_rle, _encode_kernels.py:163-191).
+      const u32 total = nll + ndist;
+      u32 i = 0, size = 0;
+      u32* cf = s.freq + 316;
+      while (i < total) {
+        const u32 value = i < nll ? s.lengths[i] : s.lengths[286 + i - nll];
+        u32 run = 1;
+        while (i + run < total &&
+               (i + run < nll ? s.lengths[i + run] : s.lengths[286 + i + run - nll]) == value)
+          ++run;
+        i += run;
+        if (value) {
+          s.rle_sym[size] = u8(value); s.rle_extra[size++] = 0; ++cf[value]; --run;
+          while (run >= 3) {
+            const u32 take = run < 6 ? run : 6;
+            s.rle_sym[size] = 16; s.rle_extra[size++] = u8(take - 3); ++cf[16]; run -= take;
+          }
+        } else {
+          while (run >= 11) {
+            const u32 take = run < 138 ? run : 138;
+            s.rle_sym[size] = 18; s.rle_extra[size++] = u8(take - 11); ++cf[18]; run -= take;
+          }
+          if (run >= 3) {
+            s.rle_sym[size] = 17; s.rle_extra[size++] = u8(run - 3); ++cf[17]; run = 0;
+          }
+        }
+        while (run) { s.rle_sym[size] = u8(value); s.rle_extra[size++] = 0; ++cf[value]; --run; }
+      }
+      s.nll = nll;
+      s.ndist = ndist;
+      s.rle_size = size;
+    }
+    __syncthreads();
+    if (trees) trees = cta_tree(s, s.freq + 316, 19, 7, s.lengths + 316, s.codes + 316);
+    if (tid == 0) {
+      u32 ncl = 19;
+      while (ncl > 4 && !s.lengths[316 + kClOrder[ncl - 1]]) --ncl;
+      s.ncl = ncl;
+    }
+    __syncthreads();
+  }
+  if (tid == 0) {
+    if (!trees) {
+      s.mode = 3;
+      s.status = 1;
+    } else if (dynamic) {
+      u32 bits = 17 + 3 * s.ncl + s.extra_bits + s.header_bits;
+      for (u32 i = 0; i < 30; ++i) bits += s.freq[286 + i] * s.lengths[286 + i];
+      for (u32 i = 0; i < 19; ++i)
+        bits += s.freq[316 + i] *
+                (s.lengths[316 + i] + (i == 16 ? 2u : i == 17 ? 3u : i == 18 ? 7u : 0u));
+      const u32 dyn_extent = extent_of(bits, final);
+      if (dyn_extent < s.extent) { s.extent = dyn_extent; s.mode = 2; }
+    }
+  }
+  __syncthreads();
+  u8* slot = slots + slot_start(f.in_offset + start, g);
+  const u32 slot_bytes = n + 80;
+  const u32 mode = s.mode;
+  if (mode == 3) {
+    if (tid == 0) { status[g] = 1; sizes[g] = 0; }
+    return;
+  }
+  if (mode == 0) {
+    for (u32 i = tid; i < n; i += kEncThreads) slot[5 + i] = data[i];
+    if (tid == 0) {
+      slot[0] = final ? 1 : 0;
+      slot[1] = u8(n);
+      slot[2] = u8(n >> 8);
+      const u32 c = n ^ 0xffffu;
+      slot[3] = u8(c);
+      slot[4] = u8(c >> 8);
+      sizes[g] = n + 5;
+      status[g] = 0;
+    }
+    return;
+  }
+
+  // 8. Parallel bit packing.
+  const bool dyn = mode == 2;
+  u32 my_bits = 0;
+  for (u32 p = a; p < b; ++p) {
+    if (!((member[p >> 5] >> (p & 31)) & 1u)) continue;
+    if ((ismatch[p >> 5] >> (p & 31)) & 1u) {
+      const u32 m = u32(lenv[p]) + 3, dist = p - (u32(prev[p]) - 1);
+      const u32 li = length_symbol(m), di = dist_symbol(dist);
+      my_bits += (dyn ? s.lengths[257 + li] : fixed_ll_len(257 + li)) + kLenExtra[li] +
+                 (dyn ? s.lengths[286 + di] : 5u) + kDistExtra[di];
+    } else {
+      my_bits += dyn ? s.lengths[data[p]] : fixed_ll_len(data[p]);
+    }
+  }
+  // Header size.
+  if (tid == 0) {
+    u32 hb = 3;
+    if (dyn) {
+      hb += 14 + 3 * s.ncl;
+      for (u32 i = 0; i < s.rle_size; ++i) {
+        const u32 sym = s.rle_sym[i];
+        hb += s.lengths[316 + sym] + (sym == 16 ? 2u : sym == 17 ? 3u : sym == 18 ? 7u : 0u);
+      }
+    }
+    s.header_bits = hb;
+  }
+  // Exclusive block scan of my_bits.
+  u32 incl = my_bits;
+  for (u32 o = 1; o < 32; o <<= 1) {
+    const u32 v = __shfl_up_sync(kFullMask, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) s.warp_sums[warp] = incl;
+  // Zero the slot words the packed block occupies (edge words are ORed).
+  u32* words = reinterpret_cast<u32*>(slot);
+  const u32 used_words = min_u32((s.extent + 3) / 4 + 1, slot_bytes / 4);
+  for (u32 i = tid; i < used_words; i += kEncThreads) words[i] = 0;
+  __syncthreads();
+  u32 before = 0;
+  for (u32 w = 0; w < warp; ++w) before += s.warp_sums[w];
+  u32 body_bits = 0;
+  for (u32 w = 0; w < kEncThreads / 32; ++w) body_bits += s.warp_sums[w];
+  const u32 header_bits = s.header_bits;
+  const u32 my_start = header_bits + before + incl - my_bits;
+  if (tid == 0) {
+    Packer pk;
+    pk.start(words, 0, header_bits, used_words);
+    pk.put((final ? 1u : 0u) | (dyn ? 4u : 2u), 3);
+    if (dyn) {
+      pk.put(s.nll - 257, 5);
+      pk.put(s.ndist - 1, 5);
+      pk.put(s.ncl - 4, 4);
+      for (u32 i = 0; i < s.ncl; ++i) pk.put(s.lengths[316 + kClOrder[i]], 3);
+      for (u32 i = 0; i < s.rle_size; ++i) {
+        const u32 sym = s.rle_sym[i];
+        pk.put(s.codes[316 + sym], s.lengths[316 + sym]);
+        if (sym >= 16) pk.put(s.rle_extra[i], sym == 16 ? 2u : sym == 17 ? 3u : 7u);
+      }
+    }
+    pk.first_word = 0;  // the header's own words may be shared with token words
+    pk.last_word = ~0ull;
+    pk.finish();
+  }
+  {
+    Packer pk;
+    pk.start(words, my_start, my_start + my_bits, used_words);
+    for (u32 p = a; p < b; ++p) {
+      if (!((member[p >> 5] >> (p & 31)) & 1u)) continue;
+      if ((ismatch[p >> 5] >> (p & 31)) & 1u) {
+        const u32 m = u32(lenv[p]) + 3, dist = p - (u32(prev[p]) - 1);
+        const u32 li = length_symbol(m), di = dist_symbol(dist);
+        if (dyn) pk.put(s.codes[257 + li], s.lengths[257 + li]);
+        else pk.put(fixed_ll_code(257 + li), fixed_ll_len(257 + li));
+        pk.put(m - kLenBase[li], kLenExtra[li]);
+        if (dyn) pk.put(s.codes[286 + di], s.lengths[286 + di]);
+        else pk.put(reverse_bits(di, 5), 5);
+        pk.put(dist - kDistBase[di], kDistExtra[di]);
+      } else {
+        const u32 lit = data[p];
+        if (dyn) pk.put(s.codes[lit], s.lengths[lit]);
+        else pk.put(fixed_ll_code(lit), fixed_ll_len(lit));
+      }
+    }
+    pk.finish();
+  }
+  if (tid == kEncThreads - 1) {
+    // End of block, then the empty stored block that realigns a nonfinal chunk.
+    const u32 at = header_bits + body_bits;
+    Packer pk;
+    u32 tail_bits = dyn ? s.lengths[256] : 7u;
+    pk.start(words, at, at + tail_bits + 3, used_words);
+    pk.first_word = pk.word;
+    pk.last_word = ~0ull;
+    if (dyn) pk.put(s.codes[256], s.lengths[256]);
+    else pk.put(fixed_ll_code(256), 7);
+    u32 end = at + tail_bits;
+    if (!final) {
+      pk.put(0, 3);
+      end += 3;
+    }
+    pk.finish();
+    s.ok = (end + 7) / 8;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    u32 bytes = s.ok;
+    bool good = bytes + 8 <= slot_bytes;
+    if (good && !final) {
+      // LEN = 0, NLEN = 0xffff of the realigning empty stored block.
+      slot[bytes] = 0;
+      slot[bytes + 1] = 0;
+      slot[bytes + 2] = 0xff;
+      slot[bytes + 3] = 0xff;
+      bytes += 4;
+    }
+    good = good && bytes == s.extent;
+    sizes[g] = good ? bytes : 0;
+    status[g] = good ? 0u : 1u;
+  }
+}
+
+// Finish, one warp per file: scan chunk sizes, check statuses and capacity,
+// combine Adler partials, write the wrapper bytes and metadata
+// [encoded_length, status] (FinishEncodedFile, batch_encode.cuh:39-112).
+__global__ void encode_finish_kernel(const EncodeFile* files, u32 nfiles, const u32* sizes,
+                                     const u32* status, const u64* adler, u64* offsets,
+                                     u8* out, u32* meta) {
+  const u32 lane = threadIdx.x & 31u;
+  const u32 f = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  if (f >= nfiles) return;
+  const EncodeFile file = files[f];
+  u64 running = 2;  // after the two-byte zlib header
+  u32 bad = 0;
+  u64 s1 = 0, s2 = 0;
+  for (u32 base = 0; base < file.chunks; base += 32) {
+    const u32 c = base + lane;
+    u32 size = 0, st = 0;
+    u64 a1 = 0, a2 = 0;
+    u64 after = 0;
+    if (c < file.chunks) {
+      const u32 g = file.first_chunk + c;
+      size = sizes[g];
+      st = status[g];
+      a1 = adler[2 * u64(g)] % kAdlerMod;
+      a2 = adler[2 * u64(g) + 1] % kAdlerMod;
+      const u64 chunk_end = min_u64(u64(c + 1) * file.chunk_bytes, file.in_size);
+      after = (file.in_size - chunk_end) % kAdlerMod;
+    }
+    bad |= __ballot_sync(kFullMask, st != 0);
+    u64 incl = size;
+    for (u32 o = 1; o < 32; o <<= 1) {
+      const u64 v = __shfl_up_sync(kFullMask, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (c < file.chunks) offsets[file.first_chunk + c] = running + incl - size;
+    running += __shfl_sync(kFullMask, incl, 31);
+    s1 += a1;
+    s2 += (a2 + a1 * after) % kAdlerMod;
+  }
+  for (u32 o = 16; o; o >>= 1) {
+    s1 += __shfl_xor_sync(kFullMask, s1, o);
+    s2 += __shfl_xor_sync(kFullMask, s2, o);
+  }
+  const u64 total = running + 4;
+  u32 st = bad ? u32(kCompressionOverflow) : 0u;
+  if (!st && total > file.capacity) st = kCompressionOverflow;
+  if (lane == 0) {
+    u8* dst = out + file.out_offset;
+    if (!st) {
+      const u32 checksum = adler_finish(s1, s2, file.in_size);
+      dst[0] = 0x78;
+      dst[1] = 0x01;
+      dst[total - 4] = u8(checksum >> 24);
+      dst[total - 3] = u8(checksum >> 16);
+      dst[total - 2] = u8(checksum >> 8);
+      dst[total - 1] = u8(checksum);
+    }
+    meta[2 * f] = st ? 0u : u32(total);
+    meta[2 * f + 1] = st;
+  }
+}
+
+// Copy every chunk's slot to its place in its file's output (skipped for
+// files whose finish reported an error).
+__global__ void encode_pack_kernel(const EncodeFile* files, u32 nfiles, const u8* slots,
+                                   const u32* sizes, const u64* offsets, const u32* meta, u8* out,
+                                   u32 chunk_bytes, u32 total_chunks) {
+  const u32 g = blockIdx.x;
+  if (g >= total_chunks) return;
+  u32 lo = 0, hi = nfiles;
+  while (hi - lo > 1) {
+    const u32 mid = (lo + hi) >> 1;
+    if (files[mid].first_chunk <= g) lo = mid;
+    else hi = mid;
+  }
+  if (meta[2 * lo + 1]) return;
+  const u32 size = sizes[g];
+  const u64 start = u64(g - files[lo].first_chunk) * chunk_bytes;
+  const u8* src = slots + slot_start(files[lo].in_offset + start, g);
+  u8* dst = out + files[lo].out_offset + offsets[g];
+  for (u32 i = threadIdx.x; i < size; i += blockDim.x) dst[i] = src[i];
+}
+
+size_t encode_smem_bytes(u32 chunk_bytes, bool in_smem) {
+  const size_t data_bytes = (chunk_bytes + 16 + 15) & ~15u;
+  const size_t bit_words = (chunk_bytes + 31) / 32 + 1;
+  size_t bytes = data_bytes + 2 * bit_words * 4 + kHashSlots * 2;
+  if (in_smem) bytes += ((chunk_bytes + 7) & ~7u) * 2 + chunk_bytes + 16;
+  return (bytes + 15) & ~size_t(15);
+}
+
+cudaError_t configure_encode(int* max_dynamic_smem) {
+  int device = 0, optin = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return e;
+  e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+  if (e != cudaSuccess) return e;
+  const int limit = optin - int(sizeof(EncodeShared)) - 1024;
+  e = cudaFuncSetAttribute(encode_chunks_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           limit);
+  *max_dynamic_smem = limit;
+  return e;
+}
+
+cudaError_t launch_encode(const u8* in, const EncodeFile* files, u32 nfiles, u32 chunk_bytes,
+                          u32 total_chunks, u8* slots, u32* sizes, u32* status, u64* adler,
+                          u64* offsets, u16* spill_prev, u8* spill_len, u8* out, u32* meta,
+                          const DeviceInfo& dev, cudaStream_t stream) {
+  const bool in_smem = encode_in_smem(chunk_bytes, dev);
+  const size_t smem = encode_smem_bytes(chunk_bytes, in_smem);
+  encode_chunks_kernel<<<total_chunks, kEncThreads, smem, stream>>>(
+      in, files, nfiles, chunk_bytes, total_chunks, slots, sizes, status, adler, spill_prev,
+      spill_len, in_smem ? 1u : 0u);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  encode_finish_kernel<<<(nfiles + 7) / 8, 256, 0, stream>>>(files, nfiles, sizes, status, adler,
+                                                            offsets, out, meta);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  encode_pack_kernel<<<total_chunks, 256, 0, stream>>>(files, nfiles, slots, sizes, offsets, meta,
+                                                       out, chunk_bytes, total_chunks);
+  return cudaGetLastError();
+}
+
+bool encode_in_smem(u32 chunk_bytes, const DeviceInfo& dev) {
+  return encode_smem_bytes(chunk_bytes, true) <= size_t(dev.encode_smem_limit);
+}
+
+}  // namespace cz

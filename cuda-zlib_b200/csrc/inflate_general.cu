@@ -1,0 +1,543 @@
+// General-route semantics for single streams outside the small route.
+//
+// The reference decodes large streams speculatively (codec_ffi.cu:755-950):
+// it discovers candidate block starts, describes every candidate, walks the
+// exact block chain (with a fixed-Huffman tile retry), emits with history and
+// finally checks Adler-32.  Its statuses therefore follow that order: framing
+// (14-17), candidate overflow (18), the first structural error of the chain
+// (parse_block semantics: output bound before window; undiscovered dynamic
+// headers are status 10), then history/window errors (6), then Adler (21).
+//
+// Here the fast decode path owns success; this file provides
+//   * discover_kernel: the reference's candidate rule and raw event count
+//     (discover, _decode_kernels.py:998-1054), always run, because a count
+//     above the capacity fails even a valid stream with status 18;
+//   * general_status_kernel: one thread restating the chain walk and the
+//     emission history check, run only after the fast path failed, to report
+//     the status the reference's route reports.
+#include "kernels.h"
+#include "inflate_core.cuh"
+
+namespace cz {
+
+// ---------------------------------------------------------------------------
+// Candidate discovery
+// ---------------------------------------------------------------------------
+// Validity of a dynamic header at `start` (BTYPE 2 and dynamic_tables()==0);
+// per-thread, no tables kept (dynamic_valid, _decode_kernels.py:359-366).
+__device__ bool dynamic_header_valid(const u8* body, u64 bytes, u64 start) {
+  BitCursor c;
+  c.init(body, bytes, start);
+  u32 err = 0;
+  c.take(1, &err);
+  const u32 type = c.take(2, &err);
+  if (err || type != 2) return false;
+  const u32 nl = c.take(5, &err) + 257, nd = c.take(5, &err) + 1, nc = c.take(4, &err) + 4;
+  if (err || nl > 286) return false;
+  const u8 order[19] = {16, 17, 18, 0, 8, 7, 9, 6, 10, 5, 11, 4, 12, 3, 13, 2, 14, 1, 15};
+  u8 clens[19];
+  for (u32 i = 0; i < 19; ++i) clens[i] = 0;
+  for (u32 i = 0; i < nc; ++i) clens[order[i]] = u8(c.take(3, &err));
+  if (err) return false;
+  // Complete code-length code (Kraft sum exactly one, in units of 2^-7).
+  u32 kraft = 0, count[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  for (u32 i = 0; i < 19; ++i)
+    if (clens[i]) { kraft += 128u >> clens[i]; ++count[clens[i]]; }
+  if (kraft != 128) return false;
+  // Canonical decode of the code lengths, bit by bit.
+  u32 first[8], offs[8];
+  u8 sorted[19];
+  {
+    u32 code = 0, off = 0;
+    count[0] = 0;
+    for (u32 l = 1; l < 8; ++l) {
+      code = (code + count[l - 1]) << 1;
+      first[l] = code;
+      offs[l] = off;
+      off += count[l];
+    }
+    u32 cursor[8];
+    for (u32 l = 1; l < 8; ++l) cursor[l] = offs[l];
+    for (u32 i = 0; i < 19; ++i)
+      if (clens[i]) sorted[cursor[clens[i]]++] = u8(i);
+  }
+  u8 lens[320];
+  u32 i = 0;
+  while (i < nl + nd) {
+    u32 code = 0, sym = 0xffffffffu;
+    for (u32 l = 1; l < 8; ++l) {
+      code = (code << 1) | c.take(1, &err);
+      if (err) return false;
+      if (code - first[l] < count[l]) { sym = sorted[offs[l] + code - first[l]]; break; }
+    }
+    if (sym == 0xffffffffu) return false;
+    if (sym < 16) { lens[i++] = u8(sym); continue; }
+    u32 repeat, value;
+    if (sym == 16) {
+      if (!i) return false;
+      repeat = c.take(2, &err) + 3;
+      value = lens[i - 1];
+    } else if (sym == 17) {
+      repeat = c.take(3, &err) + 3;
+      value = 0;
+    } else {
+      repeat = c.take(7, &err) + 11;
+      value = 0;
+    }
+    if (err || repeat > nl + nd - i) return false;
+    for (u32 j = 0; j < repeat; ++j) lens[i++] = u8(value);
+  }
+  if (!lens[256]) return false;
+  // Literal/length: nonempty; complete, or a single length-1 code.
+  // Distance: may be empty; otherwise the same rule.
+  for (u32 part = 0; part < 2; ++part) {
+    const u32 from = part ? nl : 0, n = part ? nd : nl;
+    u32 cnt[16];
+    for (u32 l = 0; l < 16; ++l) cnt[l] = 0;
+    u32 maximum = 0;
+    for (u32 k = 0; k < n; ++k) {
+      const u32 l = lens[from + k];
+      ++cnt[l];
+      if (l > maximum) maximum = l;
+    }
+    if (!maximum) {
+      if (part == 0) return false;
+      continue;
+    }
+    int left = 1;
+    for (u32 l = 1; l < 16; ++l) {
+      left = (left << 1) - int(cnt[l]);
+      if (left < 0) return false;
+    }
+    if (left && !(maximum == 1 && cnt[1] == 1)) return false;
+  }
+  return true;
+}
+
+// Stored-block endpoint seed at body byte `byte` (discover, :1009-1035).
+__device__ bool stored_seed(const u8* body, u64 bytes, u64 byte, u64* endpoint) {
+  const u64 available = bytes - byte;
+  if (!byte || available < 5) return false;
+  const u32 n = u32(body[byte]) | (u32(body[byte + 1]) << 8);
+  const u32 comp = u32(body[byte + 2]) | (u32(body[byte + 3]) << 8);
+  if ((n ^ comp) != 0xffffu || u64(n) + 4 >= available) return false;
+  u32 before = u32(body[byte - 1]) << 8;
+  if (byte >= 2) before |= body[byte - 2];
+  bool possible = false;
+  for (u32 gap = 3; gap <= 10; ++gap)
+    if (byte * 8 >= gap && ((before >> (17 - gap)) & 3u) == 0) possible = true;
+  const u64 e = byte + 4 + n;
+  if (!possible || ((body[e] >> 1) & 3u) != 1) return false;
+  *endpoint = e;
+  return true;
+}
+
+// One thread per body byte: eight bit offsets plus the stored seed.  Sets
+// candidate bits (bit offset b -> bitmap[b >> 5] bit b & 31) and adds the raw
+// event count.  Skipped when `gate` (framing status) is nonzero.
+__global__ void discover_kernel(const u8* in, u64 in_size, u32* bitmap, u32* count,
+                                const u32* gate) {
+  if (gate && *gate) return;
+  if (in_size < 8) return;
+  const u8* body = in + 2;
+  const u64 bytes = in_size - 6;
+  u32 events = 0;
+  const u64 stride = u64(gridDim.x) * blockDim.x;
+  for (u64 byte = u64(blockIdx.x) * blockDim.x + threadIdx.x; byte < bytes; byte += stride) {
+    u64 e;
+    if (stored_seed(body, bytes, byte, &e)) {
+      ++events;
+      atomicOr(&bitmap[(e * 8) >> 5], 1u << ((e * 8) & 31));
+    }
+    // Cheap prefilter on the three header bits of each offset: BTYPE must be
+    // 2 (bits 1-2 of the offset), except bit offset 0 which always counts.
+    const u32 w = u32(body[byte]) | (byte + 1 < bytes ? u32(body[byte + 1]) << 8 : 0u);
+    u32 mask = 0;
+    for (u32 bit = 0; bit < 8; ++bit) {
+      const u64 start = byte * 8 + bit;
+      bool valid = start == 0;
+      if (!valid && ((w >> (bit + 1)) & 3u) == 2u) valid = dynamic_header_valid(body, bytes, start);
+      if (valid) mask |= 1u << bit;
+    }
+    if (mask) {
+      events += __popc(mask);
+      atomicOr(&bitmap[(byte * 8) >> 5], mask << ((byte * 8) & 31));
+    }
+  }
+  for (u32 o = 16; o; o >>= 1) events += __shfl_xor_sync(kFullMask, events, o);
+  if ((threadIdx.x & 31) == 0 && events) atomicAdd(count, events);
+}
+
+// ---------------------------------------------------------------------------
+// Exact general-route status (one thread)
+// ---------------------------------------------------------------------------
+// Serial table builder (same validation and layout as warp_build).
+template <int Primary, int MaxSymbols, typename EntryFn>
+__device__ u32 serial_build(Huffman<Primary, MaxSymbols>& t, const u8* lens, u32 n, bool empty_ok,
+                            bool single_ok, EntryFn make) {
+  u32 cnt[16];
+  for (u32 l = 0; l < 16; ++l) cnt[l] = 0;
+  u32 maximum = 0;
+  for (u32 i = 0; i < n; ++i) {
+    ++cnt[lens[i]];
+    if (lens[i] > maximum) maximum = lens[i];
+  }
+  cnt[0] = 0;
+  for (u32 l = 0; l < 16; ++l) t.count[l] = u16(cnt[l]);
+  t.maxlen = maximum;
+  if (!maximum) {
+    for (u32 k = 0; k < (1u << Primary); ++k) t.lut[k] = make_entry(kEmpty, 0, 0, 0);
+    return empty_ok ? 0u : u32(kBadTree);
+  }
+  int left = 1;
+  for (u32 l = 1; l < 16; ++l) {
+    left = (left << 1) - int(cnt[l]);
+    if (left < 0) return kBadTree;
+  }
+  if (left && !(single_ok && maximum == 1 && cnt[1] == 1)) return kBadTree;
+  u32 code = 0, offset = 0, cursor[16];
+  for (u32 l = 1; l < 16; ++l) {
+    code = (code + cnt[l - 1]) << 1;
+    t.first[l] = code;
+    t.offs[l] = u16(offset);
+    cursor[l] = offset;
+    offset += cnt[l];
+  }
+  for (u32 i = 0; i < n; ++i)
+    if (lens[i]) t.symbols[cursor[lens[i]]++] = u16(i);
+  for (u32 k = 0; k < (1u << Primary); ++k) {
+    const u32 v = __brev(k) >> (32 - Primary);
+    u32 entry = make_entry(maximum > u32(Primary) ? kLong : kHole, 0, 0, 0);
+    const u32 top = maximum < u32(Primary) ? maximum : u32(Primary);
+    for (u32 L = 1; L <= top; ++L) {
+      const u32 i = (v >> (Primary - L)) - t.first[L];
+      if (i < t.count[L]) { entry = make(t.symbols[t.offs[L] + i], L); break; }
+    }
+    t.lut[k] = entry;
+  }
+  return 0;
+}
+
+__device__ u32 serial_dynamic_header(BitCursor& c, Tables& t) {
+  u32 err = 0;
+  const u32 nl = c.take(5, &err) + 257, nd = c.take(5, &err) + 1, nc = c.take(4, &err) + 4;
+  if (err) return err;
+  if (nl > 286) return kBadTree;
+  const u8 order[19] = {16, 17, 18, 0, 8, 7, 9, 6, 10, 5, 11, 4, 12, 3, 13, 2, 14, 1, 15};
+  for (u32 i = 0; i < 19; ++i) t.lens[i] = 0;
+  for (u32 i = 0; i < nc; ++i) t.lens[order[i]] = u8(c.take(3, &err));
+  if (err) return err;
+  err = serial_build(t.cl, t.lens, 19, false, false, CLFn());
+  if (err) return err;
+  u32 i = 0;
+  while (i < nl + nd) {
+    const u32 e = t.cl.lut[c.peek() & 127u];
+    if (entry_len(e) > c.avail()) return kTruncated;
+    c.skip(entry_len(e));
+    const u32 sym = entry_value(e);
+    if (sym < 16) { t.lens[i++] = u8(sym); continue; }
+    u32 repeat, value;
+    if (sym == 16) {
+      if (!i) return kBadRepeat;
+      repeat = c.take(2, &err) + 3;
+      value = t.lens[i - 1];
+    } else if (sym == 17) {
+      repeat = c.take(3, &err) + 3;
+      value = 0;
+    } else {
+      repeat = c.take(7, &err) + 11;
+      value = 0;
+    }
+    if (err) return err;
+    if (repeat > nl + nd - i) return kBadRepeat;
+    for (u32 j = 0; j < repeat; ++j) t.lens[i++] = u8(value);
+  }
+  if (!t.lens[256]) return kBadTree;
+  err = serial_build(t.ll, t.lens, nl, false, true, LLFn());
+  if (err) return err;
+  for (u32 k = 0; k < nd; ++k) t.lens[288 + k] = t.lens[nl + k];
+  return serial_build(t.d, t.lens + 288, nd, true, true, DFn());
+}
+
+struct BlockInfo {
+  u64 end;
+  u32 size, final, status;
+};
+
+// parse_block<false> (_decode_kernels.py:683-781): no history, `limit`
+// output bytes, window 32768, optional fixed budget (status 13).
+__device__ BlockInfo parse_block(const u8* body, u64 bytes, u64 start, u32 limit, u32 budget,
+                                 const Tables& fixed, Tables& dyn) {
+  BitCursor c;
+  c.init(body, bytes, start);
+  BlockInfo b = {start, 0, 0, 0};
+  u32 err = 0;
+  b.final = c.take(1, &err);
+  const u32 type = c.take(2, &err);
+  if (err) { b.status = err; return b; }
+  if (type == 3) { b.status = kReservedType; return b; }
+  u32 produced = 0;
+  if (type == 0) {
+    c.seek((c.pos + 7) & ~7ull);
+    const u32 n = c.take(16, &err), comp = c.take(16, &err);
+    if (err) { b.status = err; return b; }
+    if ((n ^ comp) != 0xffffu) { b.status = kBadSymbol; return b; }
+    if (n > limit) { b.status = kOutputOverflow; return b; }
+    if (c.pos > c.end || u64(n) * 8 > c.end - c.pos) { b.status = kTruncated; return b; }
+    b.end = c.pos + u64(n) * 8;
+    b.size = n;
+    return b;
+  }
+  if (type == 2) {
+    err = serial_dynamic_header(c, dyn);
+    if (err) { b.status = err; return b; }
+  }
+  const Tables& t = type == 2 ? dyn : fixed;
+  for (;;) {
+    if (type == 1 && budget && (produced >= budget || c.pos - start >= u64(budget) * 8)) {
+      err = kFixedTiles;
+      break;
+    }
+    const Token tok = decode_token(c, t);
+    if (tok.kind == kTokError) { err = tok.error; break; }
+    c.skip(tok.bits);
+    if (tok.kind == kTokEnd) break;
+    if (tok.kind == kTokLiteral) {
+      if (produced >= limit) { err = kOutputOverflow; break; }
+      ++produced;
+      continue;
+    }
+    if (tok.length > limit - produced) { err = kOutputOverflow; break; }
+    if (tok.dist > 32768u) { err = kBadDistance; break; }
+    produced += tok.length;
+  }
+  b.end = c.pos;
+  b.size = produced;
+  b.status = err;
+  return b;
+}
+
+struct Summary {
+  u64 end, first_end;
+  u32 size, first_size, flags, status;
+};
+
+// scan_fixed_region (_decode_kernels.py:444-472), window checked in-token.
+__device__ Summary scan_fixed(const u8* body, u64 bytes, u64 entry, u64 tile_end,
+                              const Tables& fixed) {
+  BitCursor c;
+  c.init(body, bytes, entry);
+  u32 err = entry >= bytes * 8 ? u32(kTruncated) : 0u;
+  Summary s = {entry, ~0ull, 0, 0, 0, 0};
+  u32 ended = 0, final = 2, kind = 0;
+  while (c.pos < tile_end && !err) {
+    const Token tok = decode_token(c, fixed);
+    if (tok.kind == kTokError) { err = tok.error; break; }
+    c.skip(tok.bits);
+    if (tok.kind != kTokEnd) {
+      s.size += tok.kind == kTokLiteral ? 1u : tok.length;
+      continue;
+    }
+    if (s.first_end == ~0ull) { s.first_end = c.pos; s.first_size = s.size; }
+    ++ended;
+    if (final == 1) { kind = 2; break; }
+    if (c.pos >= tile_end) { kind = 1; break; }
+    const u64 header = c.pos;
+    const u32 next_final = c.take(1, &err), type = c.take(2, &err);
+    if (err) break;
+    if (type != 1) { c.seek(header); kind = 1; break; }
+    final = next_final;
+  }
+  s.end = c.pos;
+  s.flags = kind | (final << 2) | (ended << 4);
+  s.status = err;
+  return s;
+}
+
+constexpr u64 kTileBits = 2048ull * 8;
+
+// select_chain_impl (_decode_kernels.py:1226-1408); `tiles` selects the
+// fixed-summary retry pass.
+__device__ u32 chain_walk(const u8* body, u64 bytes, const u32* bitmap, u32 expected,
+                          u32 max_blocks, bool tiles, const Tables& fixed, Tables& dyn) {
+  const u64 bits = bytes * 8;
+  u64 next = 0;
+  u32 output = 0, n = 0, real_blocks = 0;
+  for (;;) {
+    if (n >= max_blocks) return kBlockLimit;
+    BitCursor h;
+    h.init(body, bytes, next);
+    u32 err = 0;
+    u32 final = h.take(1, &err);
+    const u32 type = h.take(2, &err);
+    if (err) return err;
+    if (type == 3) return kReservedType;
+    if (type == 1 && tiles) {
+      u64 cursor = h.pos;
+      for (;;) {
+        if (cursor >= bits) return kTruncated;
+        u64 tile_end = (cursor / kTileBits + 1) * kTileBits;
+        if (tile_end > bits) tile_end = bits;
+        Summary s = scan_fixed(body, bytes, cursor, tile_end, fixed);
+        u32 kind = s.flags & 3u, ended = s.flags >> 4;
+        if (final && s.first_end != ~0ull) {
+          s.end = s.first_end;
+          s.size = s.first_size;
+          s.status = 0;
+          kind = 2;
+          ended = 1;
+        }
+        if (s.status) return s.status;
+        if (s.end <= cursor || s.end > bits) return kExtentMismatch;
+        if (s.size > expected - output) return kOutputOverflow;
+        if (n >= max_blocks || ended > max_blocks - real_blocks) return kBlockLimit;
+        output += s.size;
+        real_blocks += ended;
+        ++n;
+        cursor = s.end;
+        if (kind == 2) {
+          if (output != expected) return kSizeMismatch;
+          if ((cursor + 7) / 8 != bytes) return kExtentMismatch;
+          return 0;
+        }
+        if (kind == 1) { next = cursor; break; }
+        const u32 carried = (s.flags >> 2) & 3u;
+        if (carried < 2) final = carried;
+      }
+      continue;
+    }
+    BlockInfo info;
+    const bool candidate = (bitmap[next >> 5] >> (next & 31)) & 1u;
+    if (candidate) {
+      info = parse_block(body, bytes, next, expected, 65536, fixed, dyn);
+    } else {
+      if (type == 1) return kFixedTiles;
+      if (type == 2) return kUndiscovered;
+      info = parse_block(body, bytes, next, expected - output, 0, fixed, dyn);
+    }
+    if (info.status) return info.status;
+    if (info.end <= next || info.end > bits) return kExtentMismatch;
+    if (info.size > expected - output) return kOutputOverflow;
+    if (real_blocks >= max_blocks) return kBlockLimit;
+    output += info.size;
+    ++real_blocks;
+    ++n;
+    next = info.end;
+    if (info.final) {
+      if (output != expected) return kSizeMismatch;
+      if ((next + 7) / 8 != bytes) return kExtentMismatch;
+      return 0;
+    }
+  }
+}
+
+// Emission history check on an accepted chain: any distance beyond the
+// declared window or before the stream start is status 6.
+__device__ u32 history_walk(const u8* body, u64 bytes, u32 window, const Tables& fixed,
+                            Tables& dyn) {
+  BitCursor c;
+  c.init(body, bytes, 0);
+  u64 produced = 0;
+  for (;;) {
+    u32 err = 0;
+    const u32 final = c.take(1, &err);
+    const u32 type = c.take(2, &err);
+    if (err) return 0;  // cannot happen after an accepted chain
+    if (type == 0) {
+      c.seek((c.pos + 7) & ~7ull);
+      const u32 n = c.take(16, &err);
+      c.take(16, &err);
+      produced += n;
+      c.seek(c.pos + u64(n) * 8);
+    } else {
+      if (type == 2 && serial_dynamic_header(c, dyn)) return 0;
+      const Tables& t = type == 2 ? dyn : fixed;
+      for (;;) {
+        const Token tok = decode_token(c, t);
+        if (tok.kind == kTokError) return 0;
+        c.skip(tok.bits);
+        if (tok.kind == kTokEnd) break;
+        if (tok.kind == kTokLiteral) { ++produced; continue; }
+        if (tok.dist > window || tok.dist > produced) return kBadDistance;
+        produced += tok.length;
+      }
+    }
+    if (final) return 0;
+  }
+}
+
+struct GeneralShared {
+  Tables fixed;
+  Tables dyn;
+};
+
+// meta[0] holds the fast path's status on entry.  count/bitmap come from
+// discover_kernel.  Writes the reference route's status to meta[0].
+__global__ void general_status_kernel(const u8* in, u64 in_size, u64 expected, u32 max_candidates,
+                                      u32 max_blocks, const u32* bitmap, const u32* count,
+                                      u32* meta) {
+  __shared__ GeneralShared sh;
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  const u32 fast = meta[0];
+  u32 window = 0, wanted = 0;
+  u32 status = zlib_framing(in, in_size, &window, &wanted);
+  if (!status) {
+    const u64 body_bytes = in_size - 6;
+    const u64 capacity = min_u64(u64(max_candidates), body_bytes * 9 + 1);
+    if (*count > capacity) status = kCandidateOverflow;
+    else if (!*count) status = kInitialBlockMissing;
+  }
+  if (!status && fast) {
+    const u8* body = in + 2;
+    const u64 bytes = in_size - 6;
+    for (u32 i = 0; i < 288; ++i) sh.fixed.lens[i] = i < 144 ? 8 : i < 256 ? 9 : i < 280 ? 7 : 8;
+    serial_build(sh.fixed.ll, sh.fixed.lens, 288, false, true, LLFn());
+    for (u32 i = 0; i < 32; ++i) sh.fixed.lens[i] = 5;
+    serial_build(sh.fixed.d, sh.fixed.lens, 32, false, true, DFn());
+    status = chain_walk(body, bytes, bitmap, u32(expected), max_blocks, false, sh.fixed, sh.dyn);
+    if (status == kFixedTiles)
+      status = chain_walk(body, bytes, bitmap, u32(expected), max_blocks, true, sh.fixed, sh.dyn);
+    if (!status) status = history_walk(body, bytes, window, sh.fixed, sh.dyn);
+    // An accepted chain with valid history fails only on its checksum.
+    if (!status) status = fast == kAdlerMismatch ? u32(kAdlerMismatch) : fast;
+  }
+  meta[0] = status;
+  meta[1] = 0;
+}
+
+// Zero a failed output (grid-stride).
+__global__ void clear_on_failure_kernel(const u32* meta, u8* out, u64 n) {
+  if (!meta[0]) return;
+  const u64 stride = u64(gridDim.x) * blockDim.x;
+  for (u64 i = u64(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) out[i] = 0;
+}
+
+cudaError_t launch_discover(const u8* in, u64 in_size, u32* bitmap, u32* count, const u32* gate,
+                            const DeviceInfo& dev, cudaStream_t stream) {
+  if (in_size < 8) return cudaSuccess;
+  const u64 bytes = in_size - 6;
+  u64 blocks = (bytes + 255) / 256;
+  const u64 cap = u64(dev.sms) * 16;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  discover_kernel<<<u32(blocks), 256, 0, stream>>>(in, in_size, bitmap, count, gate);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_general_status(const u8* in, u64 in_size, u64 expected, u32 max_candidates,
+                                  u32 max_blocks, const u32* bitmap, const u32* count, u32* meta,
+                                  u8* out, cudaStream_t stream) {
+  general_status_kernel<<<1, 32, 0, stream>>>(in, in_size, expected, max_candidates, max_blocks,
+                                              bitmap, count, meta);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  if (expected) {
+    u64 blocks = (expected + 255) / 256;
+    if (blocks > 4096) blocks = 4096;
+    clear_on_failure_kernel<<<u32(blocks), 256, 0, stream>>>(meta, out, expected);
+    e = cudaGetLastError();
+  }
+  return e;
+}
+
+}  // namespace cz

@@ -1,0 +1,70 @@
+// Host-side launchers of the codec kernels (internal to the library).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+
+namespace cz {
+
+typedef uint8_t u8;
+typedef uint16_t u16;
+typedef uint32_t u32;
+typedef uint64_t u64;
+
+// One independent zlib stream of a decode call: input and output byte
+// ranges inside the call's packed buffers.
+struct StreamDesc {
+  u64 in_offset, in_size, out_offset, out_size;
+};
+
+// Per-device launch facts, filled once per device by the host layer.
+struct DeviceInfo {
+  int device;
+  int sms;
+  int serial_per_sm;    // resident CTAs of the warp-per-stream inflate kernel
+  int encode_smem_limit;  // dynamic shared memory available to the chunk encoder
+};
+
+// One file of an encode call.  Chunks of all files are numbered
+// consecutively; files are ordered by first_chunk.
+struct EncodeFile {
+  u64 in_offset, in_size;    // input bytes
+  u64 out_offset, capacity;  // padded output slot: size + 5 * chunks + 6
+  u32 first_chunk, chunks, chunk_bytes, pad;
+};
+
+// Warp-per-stream inflate (serial route semantics).  `next` is a zeroed
+// device counter; `order` (optional) lists stream indices largest first;
+// `encoded` (optional) holds compression metadata [length, status] per
+// stream, whose lengths replace desc.in_size.  meta receives [status, 0].
+cudaError_t configure_serial_inflate(int* per_sm);
+cudaError_t launch_serial_inflate(const u8* in, u8* out, const StreamDesc* descs,
+                                  const StreamDesc& single, u32 count, const u32* order, u32* next,
+                                  u32* meta, const u32* encoded, u32 max_blocks,
+                                  const DeviceInfo& dev, cudaStream_t stream);
+
+// Chunk encoder + device-side finish.  Slots: in_bytes + 96 * (chunks + 1)
+// bytes; `sizes`, `status` per chunk; `adler` 2 u64 per chunk; `offsets` 1 u64
+// per chunk.  When encode_in_smem() is false the per-position arrays live in
+// `spill_prev` (u16) and `spill_len` (u8), in_bytes + 16 * (chunks + 1)
+// entries each.  `out` must be zeroed; `meta` receives [encoded_length,
+// status] per file.
+cudaError_t configure_encode(int* max_dynamic_smem);
+bool encode_in_smem(u32 chunk_bytes, const DeviceInfo& dev);
+cudaError_t launch_encode(const u8* in, const EncodeFile* files, u32 nfiles, u32 chunk_bytes,
+                          u32 total_chunks, u8* slots, u32* sizes, u32* status, u64* adler,
+                          u64* offsets, u16* spill_prev, u8* spill_len, u8* out, u32* meta,
+                          const DeviceInfo& dev, cudaStream_t stream);
+
+// General-route status path (single streams outside the small route).
+// bitmap: one bit per body bit offset, zeroed; count: zeroed u32.
+cudaError_t launch_discover(const u8* in, u64 in_size, u32* bitmap, u32* count, const u32* gate,
+                            const DeviceInfo& dev, cudaStream_t stream);
+// meta[0] holds the fast path status; rewritten with the route's status;
+// a failed output is zeroed.
+cudaError_t launch_general_status(const u8* in, u64 in_size, u64 expected, u32 max_candidates,
+                                  u32 max_blocks, const u32* bitmap, const u32* count, u32* meta,
+                                  u8* out, cudaStream_t stream);
+
+}  // namespace cz

@@ -1,0 +1,25 @@
+"""B200-native zlib/Deflate codec with the cuda_zlib Python API.
+
+Importing this package does not initialize CUDA.  The API mirrors
+xangma/cuda-zlib (src/cuda_zlib/__init__.py:14-20): the same functions,
+bounds, errors and metadata layouts, with PyTorch CUDA tensors where the
+reference returns JAX arrays.  Every codec call runs hand-written sm_100a
+kernels through libcuda_zlib_b200.so; there is no CPU codec fallback.
+"""
+
+from ._codec import (compress_zlib, decompress_zlib, compile_kernels,
+                     compress_zlib_padded, decompress_zlib_checked,
+                     decompress_zlib_host, workspace_pool_stats, trim_workspace_pool)
+from ._codec import (compress_zlib_batch_padded, decompress_zlib_batch_checked,
+                     compress_zlib_batch, decompress_zlib_batch,
+                     compress_zlib_batch_host, decompress_zlib_batch_host)
+from ._errors import BackendUnavailable, CodecError, UnsupportedStream
+
+__all__ = ["compress_zlib", "decompress_zlib", "compile_kernels",
+           "compress_zlib_padded", "decompress_zlib_checked", "decompress_zlib_host",
+           "workspace_pool_stats", "trim_workspace_pool",
+           "compress_zlib_batch_padded", "decompress_zlib_batch_checked",
+           "compress_zlib_batch", "decompress_zlib_batch",
+           "compress_zlib_batch_host", "decompress_zlib_batch_host",
+           "BackendUnavailable", "CodecError", "UnsupportedStream"]
+__version__ = "0.1.0"

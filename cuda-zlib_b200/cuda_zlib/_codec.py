@@ -1,0 +1,447 @@
+"""Bounded RFC 1950 codec on B200 through the native C ABI.
+
+Mirrors xangma/cuda-zlib's API module (src/cuda_zlib/_codec.py): the same
+bounds (2**28 bytes, 262144 blocks and files), the same validation order and
+errors, the same padded-slot formula and metadata layouts
+([encoded_length, status] for compression, [status, 0] for decompression).
+Device arrays are PyTorch CUDA tensors; host results are read-only NumPy
+arrays backed by pinned memory.  Calls run on the device's current PyTorch
+stream; the *_padded / *_checked variants never synchronize the host.
+"""
+import numpy as np
+
+from . import _native
+from ._errors import BackendUnavailable, CodecError, UnsupportedStream
+
+_MAX_BYTES = 2**28
+_MAX_CANDIDATES = 262144
+_MAX_BLOCKS = 262144
+_MESSAGES = {
+    0: "success",
+    1: "truncated Deflate payload",
+    2: "reserved Deflate block type",
+    3: "invalid Huffman tree",
+    4: "invalid or reserved Huffman symbol",
+    5: "invalid code-length repeat",
+    6: "invalid backward distance or history",
+    7: "decoded output exceeds the declared bound",
+    9: "Deflate block workspace capacity exceeded",
+    10: "dynamic block boundary was not discovered",
+    11: "final decoded size differs from the declared size",
+    12: "block endpoint or payload extent mismatch",
+    13: "fixed-block tile summaries required",
+    14: "truncated zlib payload", 15: "invalid zlib CMF/FLG header",
+    16: "native CUDA codec supports RFC 1950 zlib",
+    17: "zlib preset dictionaries are unsupported",
+    18: "Deflate candidate workspace overflow", 19: "Deflate initial block missing",
+    20: "Deflate back-reference depth exceeded", 21: "CUDA Adler32 mismatch",
+    22: "CUDA compression workspace overflow", 23: "invalid codec bounds",
+}
+
+
+def _torch():
+    try:
+        import torch
+    except ImportError as exc:  # pragma: no cover - torch is part of the image
+        raise BackendUnavailable("the CUDA codec requires PyTorch for device memory") from exc
+    return torch
+
+
+def _validate_size(size):
+    if type(size) is not int or not 0 <= size <= _MAX_BYTES:
+        raise ValueError("expected_bytes must be an integer in [0, 2**28]")
+
+
+def _validate_device(device):
+    torch = _torch()
+    if type(device) is int:
+        if device >= 0:
+            return
+    elif isinstance(device, torch.device) and device.type == "cuda":
+        return
+    raise BackendUnavailable("device must be a nonnegative CUDA ordinal or CUDA torch device")
+
+
+def _select_device(device):
+    """Return a torch.device('cuda', i) for an ordinal or CUDA device."""
+    _validate_device(device)
+    torch = _torch()
+    if not torch.cuda.is_available():
+        raise BackendUnavailable("CUDA backend unavailable")
+    index = device if type(device) is int else (device.index if device.index is not None
+                                               else torch.cuda.current_device())
+    if index >= torch.cuda.device_count():
+        raise BackendUnavailable("requested CUDA device is unavailable")
+    return torch.device("cuda", index)
+
+
+def _is_tensor(data):
+    return type(data).__module__.startswith("torch") and hasattr(data, "dtype")
+
+
+def _input_size(data, label="input"):
+    if isinstance(data, (bytes, bytearray, memoryview)):
+        size = memoryview(data).nbytes
+    elif isinstance(data, np.ndarray) or _is_tensor(data):
+        torch = _torch() if _is_tensor(data) else None
+        dtype_ok = data.dtype == (torch.uint8 if torch else np.uint8)
+        if not dtype_ok or data.ndim != 1:
+            raise TypeError("array input must be one-dimensional uint8")
+        size = int(data.shape[0])
+    else:
+        raise TypeError(label + " must be bytes or a one-dimensional uint8 array or tensor")
+    if size > _MAX_BYTES:
+        raise ValueError(label + " exceeds size limit (2**28 bytes)")
+    return size
+
+
+def _stream(device):
+    torch = _torch()
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _pinned_copy(data, device):
+    """Host bytes -> device tensor through one pinned staging buffer."""
+    torch = _torch()
+    view = np.frombuffer(data, dtype=np.uint8) if not isinstance(data, np.ndarray) else data
+    view = np.ascontiguousarray(view, dtype=np.uint8)
+    staging = torch.empty(view.size, dtype=torch.uint8, pin_memory=True)
+    if view.size:
+        staging.numpy()[:] = view
+    return staging.to(device, non_blocking=True)
+
+
+def _device_input(data, device):
+    torch = _torch()
+    if _is_tensor(data):
+        if data.device.type == "cuda":
+            if data.device != device:
+                raise ValueError("input array and requested CUDA device differ")
+            return data.contiguous()
+        return data.contiguous().to(device, non_blocking=False)
+    if isinstance(data, (bytes, bytearray, memoryview, np.ndarray)):
+        return _pinned_copy(data, device)
+    raise TypeError("input must be bytes or a one-dimensional uint8 array or tensor")
+
+
+def _check_framing(payload, expected_bytes):
+    view = memoryview(payload).cast("B")
+    _validate_size(expected_bytes)
+    if view.nbytes < 8:
+        raise CodecError("truncated zlib payload")
+    if view.nbytes > _MAX_BYTES:
+        raise ValueError("compressed payload exceeds 2**28 bytes")
+    cmf, flg = view[0], view[1]
+    if cmf == 0x1F and flg == 0x8B:
+        raise UnsupportedStream("native CUDA codec supports RFC 1950 zlib")
+    if cmf & 15 != 8 or cmf >> 4 > 7 or (cmf * 256 + flg) % 31:
+        raise CodecError("invalid zlib CMF/FLG header")
+    if flg & 32:
+        raise UnsupportedStream("zlib preset dictionaries are unsupported")
+
+
+def _check_value(value, operation):
+    if value:
+        message = _MESSAGES.get(value, "unknown error")
+        error = UnsupportedStream if value in (16, 17) else CodecError
+        raise error("%s: %s (Deflate status %d)" % (operation, message, value))
+
+
+def _ptr(tensor):
+    return tensor.data_ptr() if tensor.numel() else None
+
+
+def compile_kernels(device=0):
+    """Load the native library and prepare `device` (pool, kernel attributes)."""
+    selected = _select_device(device)
+    torch = _torch()
+    lib = _native.library()
+    with torch.cuda.device(selected):
+        meta = torch.empty(2, dtype=torch.uint32, device=selected)
+        out = torch.empty(11, dtype=torch.uint8, device=selected)
+        _native.check(lib.cuda_zlib_compress(None, 0, 32768, out.data_ptr(), 11, meta.data_ptr(),
+                                             _stream(selected)), "CUDA compression")
+
+
+def workspace_pool_stats(device=0):
+    """Return retention, reserved/live bytes and pool count for a CUDA device.
+
+    Scratch pools retain up to a 1 GiB release threshold by default. Set
+    CUDA_ZLIB_WORKSPACE_RETENTION_BYTES before the first call to change it;
+    zero disables retention. The threshold is not a hard allocation cap.
+    """
+    import ctypes
+    selected = _select_device(device)
+    values = (ctypes.c_uint64 * 4)()
+    _native._check_pool_error(_native.library().CudaZlibWorkspacePoolStats(selected.index, values))
+    return dict(zip(("retention_bytes", "reserved_bytes", "used_bytes", "pool_count"), values))
+
+
+def trim_workspace_pool(device=0):
+    """Try to release unused codec scratch memory on the requested device."""
+    selected = _select_device(device)
+    _native._check_pool_error(_native.library().CudaZlibTrimWorkspacePool(selected.index))
+
+
+def _capacity(size, chunk_bytes):
+    chunks = max(1, (size + chunk_bytes - 1) // chunk_bytes)
+    return size + chunks * 5 + 6, chunks
+
+
+def compress_zlib_padded(data, device=0, *, chunk_bytes=32768):
+    """Return ``(buffer, [encoded_length, status])`` without a host sync.
+
+    The fixed-size buffer holds a zlib stream followed by zero padding.
+    Status zero means success; check it before using the stream.
+    """
+    if type(chunk_bytes) is not int or not 256 <= chunk_bytes <= 65535:
+        raise ValueError("chunk_bytes must be an integer in [256, 65535]")
+    size = _input_size(data)
+    capacity, chunks = _capacity(size, chunk_bytes)
+    if 2 * chunks - 1 > _MAX_BLOCKS:
+        raise ValueError("chunk count exceeds decoder block limit")
+    if capacity > _MAX_BYTES:
+        raise ValueError("worst-case compressed extent exceeds 2**28 bytes")
+    selected = _select_device(device)
+    torch = _torch()
+    lib = _native.library()
+    raw = _device_input(data, selected)
+    with torch.cuda.device(selected):
+        output = torch.empty(capacity, dtype=torch.uint8, device=selected)
+        metadata = torch.empty(2, dtype=torch.uint32, device=selected)
+        _native.check(lib.cuda_zlib_compress(_ptr(raw), size, chunk_bytes, output.data_ptr(),
+                                             capacity, metadata.data_ptr(), _stream(selected)),
+                      "CUDA compression")
+    return output, metadata
+
+
+def _batch_sizes(sizes, label):
+    if not isinstance(sizes, (tuple, list)) or not 1 <= len(sizes) <= _MAX_BLOCKS:
+        raise ValueError(label + " must contain between 1 and 262144 static sizes")
+    sizes = tuple(sizes)
+    if any(type(size) is not int or not 0 <= size <= _MAX_BYTES for size in sizes):
+        raise ValueError(label + " must contain integers in [0, 2**28]")
+    if sum(sizes) > _MAX_BYTES:
+        raise ValueError(label + " total exceeds 2**28 bytes")
+    return sizes
+
+
+def _batch_capacities(sizes, chunk_bytes):
+    if type(chunk_bytes) is not int or not 256 <= chunk_bytes <= 65535:
+        raise ValueError("chunk_bytes must be an integer in [256, 65535]")
+    chunks = tuple(max(1, (size + chunk_bytes - 1) // chunk_bytes) for size in sizes)
+    if sum(chunks) > _MAX_BLOCKS or any(2 * n - 1 > _MAX_BLOCKS for n in chunks):
+        raise ValueError("batch chunk count exceeds workspace limit")
+    capacities = tuple(size + n * 5 + 6 for size, n in zip(sizes, chunks))
+    if sum(capacities) > _MAX_BYTES:
+        raise ValueError("batch compressed capacity exceeds 2**28 bytes")
+    return capacities
+
+
+def _i64_array(values):
+    import ctypes
+    array = (ctypes.c_int64 * len(values))(*values)
+    return array
+
+
+def compress_zlib_batch_padded(data, input_sizes, device=0, *, chunk_bytes=32768):
+    """Compress packed independent files in one call, without a host sync.
+
+    ``input_sizes`` lists the file lengths (their sum is len(data)).  Returns a
+    flat uint8 buffer of consecutive padded slots and uint32 metadata of shape
+    (files, 2) with [encoded_length, status] per file.  A slot has
+    ``size + 5 * max(1, ceil(size / chunk_bytes)) + 6`` bytes.
+    """
+    sizes = _batch_sizes(input_sizes, "input_sizes")
+    if _input_size(data) != sum(sizes):
+        raise ValueError("packed input length differs from input_sizes total")
+    capacities = _batch_capacities(sizes, chunk_bytes)
+    selected = _select_device(device)
+    torch = _torch()
+    lib = _native.library()
+    raw = _device_input(data, selected)
+    total = sum(capacities)
+    with torch.cuda.device(selected):
+        output = torch.empty(total, dtype=torch.uint8, device=selected)
+        metadata = torch.empty((len(sizes), 2), dtype=torch.uint32, device=selected)
+        _native.check(lib.cuda_zlib_compress_batch(
+            _ptr(raw), sum(sizes), _i64_array(sizes), len(sizes), chunk_bytes,
+            _ptr(output), total, metadata.data_ptr(), _stream(selected)),
+            "CUDA batch compression")
+    return output, metadata
+
+
+def decompress_zlib_batch_checked(payload, input_sizes, expected_sizes, device=0,
+                                  *, encoded_metadata=None):
+    """Decode packed independent streams in one call, without a host sync.
+
+    Input streams and returned outputs are packed back to back.  To decode
+    padded compression slots directly, pass their capacities as input_sizes
+    and compression's (files, 2) uint32 metadata as encoded_metadata.
+    Returns a flat output and (files, 2) uint32 [status, 0] metadata.
+    """
+    sizes = _batch_sizes(input_sizes, "input_sizes")
+    expected = _batch_sizes(expected_sizes, "expected_sizes")
+    if len(sizes) != len(expected):
+        raise ValueError("input_sizes and expected_sizes must have matching lengths")
+    if _input_size(payload, "compressed payload") != sum(sizes):
+        raise ValueError("packed input length differs from input_sizes total")
+    selected = _select_device(device)
+    torch = _torch()
+    lib = _native.library()
+    raw = _device_input(payload, selected)
+    lengths = None
+    if encoded_metadata is not None:
+        if (not _is_tensor(encoded_metadata) or encoded_metadata.dtype != torch.uint32 or
+                tuple(encoded_metadata.shape) != (len(sizes), 2)):
+            raise TypeError("encoded_metadata must be a uint32 tensor with shape (files, 2)")
+        if encoded_metadata.device != selected:
+            raise ValueError("input array and requested CUDA device differ")
+        lengths = encoded_metadata.contiguous()
+    total = sum(expected)
+    with torch.cuda.device(selected):
+        output = torch.empty(total, dtype=torch.uint8, device=selected)
+        metadata = torch.empty((len(sizes), 2), dtype=torch.uint32, device=selected)
+        _native.check(lib.cuda_zlib_decompress_batch(
+            _ptr(raw), sum(sizes), _i64_array(sizes), _i64_array(expected), len(sizes),
+            None if lengths is None else lengths.data_ptr(), _ptr(output), total,
+            metadata.data_ptr(), _stream(selected)), "CUDA batch decompression")
+    return output, metadata
+
+
+def _pack_batch(inputs, device):
+    if not isinstance(inputs, (tuple, list)) or not inputs:
+        raise ValueError("inputs must be a nonempty sequence of files")
+    sizes = _batch_sizes(tuple(_input_size(data) for data in inputs), "input_sizes")
+    if all(isinstance(data, (bytes, bytearray, memoryview)) for data in inputs):
+        return b"".join(bytes(data) for data in inputs), sizes
+    torch = _torch()
+    parts = [_device_input(data, device) for data in inputs]
+    return torch.cat(parts) if parts else torch.empty(0, dtype=torch.uint8, device=device), sizes
+
+
+def _check_batch(metadata, operation, compression=False):
+    metadata = metadata.cpu().numpy()
+    for i, row in enumerate(metadata):
+        _check_value(int(row[1 if compression else 0]), "%s file %d" % (operation, i))
+    return metadata
+
+
+def _split_batch(buffer, sizes, extents=None):
+    offset = 0
+    results = []
+    for i, size in enumerate(sizes):
+        length = size if extents is None else int(extents[i])
+        results.append(buffer[offset:offset + length])
+        offset += size
+    return tuple(results)
+
+
+def _to_pinned_host(tensor):
+    """One D2H transfer into pinned memory; returns a read-only NumPy view."""
+    torch = _torch()
+    host = torch.empty(tensor.numel(), dtype=torch.uint8, pin_memory=True)
+    if tensor.numel():
+        host.copy_(tensor, non_blocking=True)
+    torch.cuda.current_stream(tensor.device).synchronize()
+    array = host.numpy()
+    array.flags.writeable = False
+    return array
+
+
+def compress_zlib_batch(inputs, device=0, *, chunk_bytes=32768):
+    """Return completed exact-length device streams for a sequence of files."""
+    selected = _select_device(device)
+    packed, sizes = _pack_batch(inputs, selected)
+    output, metadata = compress_zlib_batch_padded(packed, sizes, selected, chunk_bytes=chunk_bytes)
+    lengths = _check_batch(metadata, "CUDA batch compression", True)[:, 0]
+    return _split_batch(output, _batch_capacities(sizes, chunk_bytes), lengths)
+
+
+def decompress_zlib_batch(payloads, expected_sizes, device=0):
+    """Return completed device outputs for independent streams; checks statuses once."""
+    selected = _select_device(device)
+    packed, sizes = _pack_batch(payloads, selected)
+    expected = _batch_sizes(expected_sizes, "expected_sizes")
+    output, metadata = decompress_zlib_batch_checked(packed, sizes, expected, selected)
+    _check_batch(metadata, "CUDA batch decompression")
+    return _split_batch(output, expected)
+
+
+def compress_zlib_batch_host(inputs, device=0, *, chunk_bytes=32768):
+    """Return a tuple of bytes streams, using one packed output transfer."""
+    selected = _select_device(device)
+    packed, sizes = _pack_batch(inputs, selected)
+    capacities = _batch_capacities(sizes, chunk_bytes)
+    output, metadata = compress_zlib_batch_padded(packed, sizes, selected, chunk_bytes=chunk_bytes)
+    lengths = _check_batch(metadata, "CUDA batch compression", True)[:, 0]
+    host = _to_pinned_host(output)
+    return tuple(view.tobytes() for view in _split_batch(host, capacities, lengths))
+
+
+def decompress_zlib_batch_host(payloads, expected_sizes, device=0):
+    """Return read-only NumPy views backed by one packed pinned-host transfer.
+
+    Every stream is decoded and checked independently on CUDA.
+    """
+    selected = _select_device(device)
+    packed, sizes = _pack_batch(payloads, selected)
+    expected = _batch_sizes(expected_sizes, "expected_sizes")
+    if len(sizes) != len(expected):
+        raise ValueError("input_sizes and expected_sizes must have matching lengths")
+    output, metadata = decompress_zlib_batch_checked(packed, sizes, expected, selected)
+    _check_batch(metadata, "CUDA batch decompression")
+    return _split_batch(_to_pinned_host(output), expected)
+
+
+def decompress_zlib_checked(payload, expected_bytes, device=0, *,
+                            max_candidates=_MAX_CANDIDATES, max_blocks=_MAX_BLOCKS):
+    """Return ``(output, [status, 0])`` without a host sync.
+
+    Status zero validates the stream, the output extent and Adler-32; check it
+    before using the output.  A failed output is all zero.  max_candidates
+    and max_blocks are the reference handler's attributes (default 262144).
+    """
+    _validate_size(expected_bytes)
+    size = _input_size(payload, "compressed payload")
+    if isinstance(payload, (bytes, bytearray, memoryview)):
+        _check_framing(payload, expected_bytes)
+    elif size < 8:
+        raise CodecError("truncated zlib payload")
+    selected = _select_device(device)
+    torch = _torch()
+    lib = _native.library()
+    raw = _device_input(payload, selected)
+    with torch.cuda.device(selected):
+        output = torch.empty(expected_bytes, dtype=torch.uint8, device=selected)
+        metadata = torch.empty(2, dtype=torch.uint32, device=selected)
+        _native.check(lib.cuda_zlib_decompress(_ptr(raw), size, int(max_candidates),
+                                               int(max_blocks), _ptr(output), expected_bytes,
+                                               metadata.data_ptr(), _stream(selected)),
+                      "CUDA decompression")
+    return output, metadata
+
+
+def compress_zlib(data, device=0, *, chunk_bytes=32768):
+    """Encode bytes/uint8 data to a completed, exact-length CUDA tensor."""
+    output, metadata = compress_zlib_padded(data, device, chunk_bytes=chunk_bytes)
+    length, status = (int(v) for v in metadata.cpu().numpy())
+    _check_value(status, "CUDA compression")
+    return output[:length]
+
+
+def decompress_zlib(payload, expected_bytes, device=0):
+    """Decode to a completed CUDA tensor; every call checks Adler-32."""
+    output, metadata = decompress_zlib_checked(payload, expected_bytes, device)
+    _check_value(int(metadata.cpu().numpy()[0]), "CUDA decompression")
+    return output
+
+
+def decompress_zlib_host(payload, expected_bytes, device=0) -> np.ndarray:
+    """Decode to a completed, read-only, contiguous NumPy uint8 array.
+
+    Same decoding, limits and validation as decompress_zlib, then one transfer
+    into pinned host memory that the returned array keeps alive.
+    """
+    output = decompress_zlib(payload, expected_bytes, device)
+    return _to_pinned_host(output)

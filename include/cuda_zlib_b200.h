@@ -1,0 +1,89 @@
+/*
+ * cuda_zlib_b200.h -- C ABI of the B200 (sm_100a) zlib/Deflate codec.
+ *
+ * The four codec entry points are the reference's four XLA FFI handlers
+ * (xangma/cuda-zlib, src/cuda_zlib/native/codec_ffi.cu) with the FFI buffers
+ * and attributes spelled out as plain pointers and sizes:
+ *
+ *   - input, output and metadata are DEVICE pointers on the device that
+ *     owns `stream` (a cudaStream_t passed as void*; NULL = legacy stream);
+ *   - size lists (the handlers' span attributes) are HOST arrays;
+ *   - codec results go to device metadata exactly as in the reference:
+ *     compression [encoded_length, status], decompression [status, 0], one
+ *     pair per file for the batch calls;
+ *   - the return value is a cudaError_t: 0 on success, cudaErrorInvalidValue
+ *     (1) where the reference handler returns ffi::Error::InvalidArgument or
+ *     cudaErrorInvalidValue, other CUDA errors as-is.  A nonzero return means
+ *     the metadata was not written.
+ *
+ * Calls are asynchronous on `stream` (one host read of nothing; scratch comes
+ * from a per-device stream-ordered pool, like the reference's
+ * cudaMemPool workspace, codec_ffi.cu:132-273).  Concurrent calls from
+ * several host threads are allowed.
+ *
+ * Status codes: 0 ok; 1-13 Deflate parser (_decode_kernels.py:36-50);
+ * 14 truncated zlib, 15 bad CMF/FLG, 16 gzip, 17 preset dictionary,
+ * 18 candidate overflow, 19 initial block missing, 20 reference depth,
+ * 21 Adler-32 mismatch, 22 compression overflow, 23 invalid bounds
+ * (codec_ffi.cu:51-62).
+ */
+#ifndef CUDA_ZLIB_B200_H
+#define CUDA_ZLIB_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Replaces CudaZlibCompress / CompressImpl (codec_ffi.cu:1144-1151, 981-988,
+ * 551-612).  output must have capacity = size + 5*max(1,ceil(size/chunk))+6
+ * bytes (compress_zlib_padded, _codec.py:151-177); it is zero-filled past
+ * the stream.  metadata: u32[2] = [encoded_length, status]. */
+int cuda_zlib_compress(const uint8_t* input, uint64_t size, int64_t chunk_bytes,
+                       uint8_t* output, uint64_t capacity, uint32_t* metadata, void* stream);
+
+/* Replaces CudaZlibDecompress / DecompressImpl (codec_ffi.cu:1153-1161,
+ * 990-998, 662-950).  expected = exact output size; max_candidates and
+ * max_blocks in [1, 262144] (defaults 262144 select the small route for
+ * outputs <= 64 KiB with inputs <= 128 KiB).  metadata: u32[2] =
+ * [status, 0].  A failed output is all zero. */
+int cuda_zlib_decompress(const uint8_t* input, uint64_t size, int64_t max_candidates,
+                         int64_t max_blocks, uint8_t* output, uint64_t expected,
+                         uint32_t* metadata, void* stream);
+
+/* Replaces CudaZlibCompressBatch / CompressBatchImpl (codec_ffi.cu:1163-1171,
+ * 1002-1063).  input: the files packed back to back; input_sizes: host
+ * int64[files].  output: consecutive padded slots of size_i + 5*chunks_i + 6
+ * bytes; metadata: u32[files][2] = [encoded_length, status]. */
+int cuda_zlib_compress_batch(const uint8_t* input, uint64_t input_bytes,
+                             const int64_t* input_sizes, uint64_t files, int64_t chunk_bytes,
+                             uint8_t* output, uint64_t output_bytes, uint32_t* metadata,
+                             void* stream);
+
+/* Replaces CudaZlibDecompressBatch / DecompressBatchImpl (codec_ffi.cu:
+ * 1173-1182, 1065-1107).  input_sizes / output_sizes: host int64[files]
+ * (packed layouts).  encoded_metadata: NULL, or a device u32[files][2] of
+ * compression metadata whose encoded lengths replace input_sizes (slots
+ * keep their static offsets).  metadata: u32[files][2] = [status, 0]. */
+int cuda_zlib_decompress_batch(const uint8_t* input, uint64_t input_bytes,
+                               const int64_t* input_sizes, const int64_t* output_sizes,
+                               uint64_t files, const uint32_t* encoded_metadata, uint8_t* output,
+                               uint64_t output_bytes, uint32_t* metadata, void* stream);
+
+/* Workspace pool controls, same names and meaning as the reference's C
+ * exports (codec_ffi.cu:1113-1142).  Retention is the pools' release
+ * threshold in bytes (default 1 GiB); it can only be set before the first
+ * pool exists.  stats: [retention, reserved bytes, used bytes, pool count]. */
+int CudaZlibSetWorkspaceRetention(uint64_t bytes);
+int CudaZlibWorkspacePoolStats(int device, uint64_t* stats);
+int CudaZlibTrimWorkspacePool(int device);
+
+/* Library version string, e.g. "0.1.0". */
+const char* cuda_zlib_b200_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CUDA_ZLIB_B200_H */
