@@ -255,7 +255,9 @@ __device__ u32 serial_dynamic_header(BitCursor& c, Tables& t) {
   if (!t.lens[256]) return kBadTree;
   err = serial_build(t.ll, t.lens, nl, false, true, LLFn());
   if (err) return err;
-  for (u32 k = 0; k < nd; ++k) t.lens[288 + k] = t.lens[nl + k];
+  // Move the distance lengths to lens[288..): the ranges can overlap and the
+  // destination is higher, so copy from the top down.
+  for (u32 k = nd; k-- > 0;) t.lens[288 + k] = t.lens[nl + k];
   return serial_build(t.d, t.lens + 288, nd, true, true, DFn());
 }
 
