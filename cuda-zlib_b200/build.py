@@ -18,7 +18,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIBRARY = os.path.join(HERE, "cuda_zlib", "libcuda_zlib_b200.so")
-SOURCES = ["codec.cu", "deflate.cu", "inflate_serial.cu", "inflate_general.cu"]
+SOURCES = ["codec.cu", "deflate.cu", "inflate_serial.cu", "inflate_general.cu",
+           "inflate_parallel.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
          "--expt-relaxed-constexpr"]

@@ -13,6 +13,7 @@
 #include <cstdint>
 #include <mutex>
 #include <numeric>
+#include <string>
 #include <vector>
 
 #include "../../include/cuda_zlib_b200.h"
@@ -66,6 +67,7 @@ cudaError_t device_state(int device, DeviceState** out) {
     CZ_TRY(cudaDeviceGetAttribute(&info.sms, cudaDevAttrMultiProcessorCount, device));
     CZ_TRY(configure_serial_inflate(&info.serial_per_sm));
     CZ_TRY(configure_encode(&info.encode_smem_limit));
+    CZ_TRY(configure_parallel_inflate(&info.emit_per_sm));
     cudaMemPoolProps props{};
     props.allocType = cudaMemAllocationTypePinned;
     props.handleTypes = cudaMemHandleTypeNone;
@@ -143,6 +145,80 @@ class Workspace {
   cudaStream_t stream_;
   std::vector<void*> held_;
 };
+
+// ---------------------------------------------------------------------------
+// Opt-in kernel timing.
+// ---------------------------------------------------------------------------
+struct ProfileRecord {
+  const char* kernel;
+  cudaEvent_t start, stop;
+};
+struct ProfileTotals {
+  std::string kernel;
+  double ms = 0;
+  u64 launches = 0;
+};
+struct Profiler {
+  std::mutex mutex;
+  bool enabled = false;
+  std::vector<ProfileRecord> pending;
+  std::vector<ProfileTotals> totals;
+};
+Profiler& profiler() {
+  static Profiler* p = new Profiler;
+  return *p;
+}
+thread_local ProfileRecord open_record{nullptr, nullptr, nullptr};
+
+// Fold completed records into the totals (waits for their stop events).
+cudaError_t profile_drain(Profiler& p) {
+  for (ProfileRecord& r : p.pending) {
+    CZ_TRY(cudaEventSynchronize(r.stop));
+    float ms = 0;
+    CZ_TRY(cudaEventElapsedTime(&ms, r.start, r.stop));
+    auto it = std::find_if(p.totals.begin(), p.totals.end(),
+                           [&](const ProfileTotals& t) { return t.kernel == r.kernel; });
+    if (it == p.totals.end()) {
+      p.totals.push_back(ProfileTotals{r.kernel, 0, 0});
+      it = p.totals.end() - 1;
+    }
+    it->ms += ms;
+    it->launches += 1;
+    cudaEventDestroy(r.start);
+    cudaEventDestroy(r.stop);
+  }
+  p.pending.clear();
+  return cudaSuccess;
+}
+
+}  // namespace
+
+void profile_begin(const char* kernel, cudaStream_t stream) {
+  Profiler& p = profiler();
+  {
+    std::lock_guard<std::mutex> lock(p.mutex);
+    if (!p.enabled) return;
+  }
+  ProfileRecord r{kernel, nullptr, nullptr};
+  if (cudaEventCreate(&r.start) != cudaSuccess) return;
+  if (cudaEventCreate(&r.stop) != cudaSuccess) {
+    cudaEventDestroy(r.start);
+    return;
+  }
+  cudaEventRecord(r.start, stream);
+  open_record = r;
+}
+
+void profile_end(cudaStream_t stream) {
+  if (!open_record.kernel) return;
+  cudaEventRecord(open_record.stop, stream);
+  Profiler& p = profiler();
+  std::lock_guard<std::mutex> lock(p.mutex);
+  p.pending.push_back(open_record);
+  open_record = ProfileRecord{nullptr, nullptr, nullptr};
+}
+
+namespace {
 
 __global__ void set_meta_kernel(u32* meta, u32 first, u32 second) {
   meta[0] = first;
@@ -290,18 +366,40 @@ cudaError_t decompress(const u8* in, u64 size, int64_t max_candidates, int64_t m
     return ws.release();
   }
   // General route: candidate discovery (always: its count alone can fail a
-  // valid stream), a fast decode, then the route's exact status on failure.
+  // valid stream), the block-parallel decode, then the route's exact status
+  // if the fast path failed.
   const u64 body = size - 6;
-  u32 *bitmap = nullptr, *count = nullptr;
-  const u64 words = (body * 8 + 31) / 32 + 1;
-  CZ_TRY(ws.allocate(&bitmap, words));
+  const u32 capacity = u32(std::min<u64>(u64(max_candidates), body * 9 + 1));
+  const ParallelScratch layout = parallel_scratch_layout(size, expected, capacity);
+  ParallelBuffers b{};
+  u32* count = nullptr;
+  CZ_TRY(ws.allocate(&b.bitmap, layout.bitmap_words));
   CZ_TRY(ws.allocate(&count, 1));
-  CZ_TRY(cudaMemsetAsync(bitmap, 0, words * sizeof(u32), stream));
+  CZ_TRY(ws.allocate(&b.block_counts, layout.compact_blocks));
+  CZ_TRY(ws.allocate(&b.total, 1));
+  CZ_TRY(ws.allocate(&b.cands, capacity));
+  CZ_TRY(ws.allocate(&b.ends, capacity));
+  CZ_TRY(ws.allocate(&b.sizes, capacity));
+  CZ_TRY(ws.allocate(&b.blocks, capacity));
+  CZ_TRY(ws.allocate(&b.infos, capacity));
+  CZ_TRY(ws.allocate(&b.jump, (u64(capacity) + 2) * layout.levels));
+  CZ_TRY(ws.allocate(&b.path, capacity));
+  CZ_TRY(ws.allocate(&b.prefix, capacity));
+  CZ_TRY(ws.allocate(&b.state, 2));
+  CZ_TRY(ws.allocate(&b.counters, 2));
+  CZ_TRY(ws.allocate(&b.source, expected));
+  CZ_TRY(ws.allocate(&b.unresolved, layout.out_words));
+  CZ_TRY(ws.allocate(&b.parts, 2 * u64(layout.segments)));
+  CZ_TRY(ws.allocate(&b.fail, 1));
+  CZ_TRY(cudaMemsetAsync(b.bitmap, 0, layout.bitmap_words * sizeof(u32), stream));
   CZ_TRY(cudaMemsetAsync(count, 0, sizeof(u32), stream));
-  CZ_TRY(launch_discover(in, size, bitmap, count, nullptr, dev->info, stream));
-  CZ_TRY(launch_serial_inflate(in, out, nullptr, single, 1, nullptr, counter, meta, nullptr,
-                               u32(max_blocks), dev->info, stream));
-  CZ_TRY(launch_general_status(in, size, expected, u32(max_candidates), u32(max_blocks), bitmap,
+  CZ_TRY(cudaMemsetAsync(b.counters, 0, 2 * sizeof(u32), stream));
+  CZ_TRY(cudaMemsetAsync(b.unresolved, 0, layout.out_words * sizeof(u32), stream));
+  CZ_TRY(cudaMemsetAsync(b.fail, 0, sizeof(u32), stream));
+  CZ_TRY(launch_discover(in, size, b.bitmap, count, nullptr, dev->info, stream));
+  CZ_TRY(launch_parallel_inflate(in, size, out, expected, u32(max_blocks), layout, b, meta,
+                                 dev->info, stream));
+  CZ_TRY(launch_general_status(in, size, expected, u32(max_candidates), u32(max_blocks), b.bitmap,
                                count, meta, out, stream));
   return ws.release();
 }
@@ -448,5 +546,30 @@ int CudaZlibTrimWorkspacePool(int device) {
 }
 
 const char* cuda_zlib_b200_version(void) { return "0.1.0"; }
+
+int cuda_zlib_b200_profile(int enable) {
+  cz::Profiler& p = cz::profiler();
+  std::lock_guard<std::mutex> lock(p.mutex);
+  cudaError_t e = cz::profile_drain(p);
+  p.totals.clear();
+  p.enabled = enable != 0;
+  return int(e);
+}
+
+int cuda_zlib_b200_profile_read(const char* kernel, double* total_ms, uint64_t* launches) {
+  if (!kernel || !total_ms || !launches) return int(cudaErrorInvalidValue);
+  cz::Profiler& p = cz::profiler();
+  std::lock_guard<std::mutex> lock(p.mutex);
+  cudaError_t e = cz::profile_drain(p);
+  *total_ms = 0;
+  *launches = 0;
+  for (const cz::ProfileTotals& t : p.totals) {
+    if (t.kernel == kernel) {
+      *total_ms = t.ms;
+      *launches = t.launches;
+    }
+  }
+  return int(e);
+}
 
 }  // extern "C"

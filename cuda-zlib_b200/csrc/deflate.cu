@@ -752,17 +752,21 @@ cudaError_t launch_encode(const u8* in, const EncodeFile* files, u32 nfiles, u32
                           const DeviceInfo& dev, cudaStream_t stream) {
   const bool in_smem = encode_in_smem(chunk_bytes, dev);
   const size_t smem = encode_smem_bytes(chunk_bytes, in_smem);
+  profile_begin("encode_chunks_kernel", stream);
   encode_chunks_kernel<<<total_chunks, kEncThreads, smem, stream>>>(
       in, files, nfiles, chunk_bytes, total_chunks, slots, sizes, status, adler, spill_prev,
       spill_len, in_smem ? 1u : 0u);
+  profile_end(stream);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   encode_finish_kernel<<<(nfiles + 7) / 8, 256, 0, stream>>>(files, nfiles, sizes, status, adler,
                                                             offsets, out, meta);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
+  profile_begin("encode_pack_kernel", stream);
   encode_pack_kernel<<<total_chunks, 256, 0, stream>>>(files, nfiles, slots, sizes, offsets, meta,
                                                        out, chunk_bytes, total_chunks);
+  profile_end(stream);
   return cudaGetLastError();
 }
 

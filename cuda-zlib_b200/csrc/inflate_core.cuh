@@ -86,6 +86,76 @@ struct BitCursor {
 };
 
 // ---------------------------------------------------------------------------
+// Bits: the hot-loop reader.  A 64-bit accumulator holds 33..64 unread bits
+// after refill(), filled from 4-byte-aligned 32-bit words; positions are u32
+// (streams are at most 2^28 bytes, so 2^31 bits).  The token loops read
+// fields straight from the low word of the accumulator.
+// ---------------------------------------------------------------------------
+struct Bits {
+  const u32* words;  // 4-byte aligned, at or below the first body byte
+  u32 shift;         // bit offset of body bit 0 inside words[0]
+  u32 last;          // index of the last word holding a body byte
+  u32 end;           // body length in bits
+  u32 idx;           // next word to load
+  u32 nbits;         // valid bits in buf
+  u64 buf;
+
+  __device__ __forceinline__ u32 load(u32 i) const { return i <= last ? __ldg(words + i) : 0u; }
+
+  __device__ __forceinline__ void init(const u8* body, u32 bytes) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(body);
+    words = reinterpret_cast<const u32*>(a & ~uintptr_t(3));
+    shift = u32(a & 3) * 8;
+    end = bytes * 8;
+    last = bytes ? (shift + end - 1) >> 5 : 0;
+    seek(0);
+  }
+  // Absolute position of the next unread body bit.
+  __device__ __forceinline__ u32 pos() const { return idx * 32 - nbits - shift; }
+  __device__ __forceinline__ u32 avail() const {
+    const u32 p = pos();
+    return p <= end ? end - p : 0;
+  }
+  __device__ __forceinline__ void seek(u32 p) {
+    const u32 a = shift + p;
+    idx = a >> 5;
+    const u32 off = a & 31;
+    buf = u64(load(idx)) >> off;
+    nbits = 32 - off;
+    ++idx;
+    refill();
+  }
+  __device__ __forceinline__ void refill() {
+    if (nbits <= 32) {
+      buf |= u64(load(idx)) << nbits;
+      ++idx;
+      nbits += 32;
+    }
+  }
+  // Unguarded refill: only while idx + 1 < last is known (fast loop).
+  __device__ __forceinline__ void refill_fast() {
+    if (nbits <= 32) {
+      buf |= u64(__ldg(words + idx)) << nbits;
+      ++idx;
+      nbits += 32;
+    }
+  }
+  __device__ __forceinline__ void consume(u32 n) {
+    buf >>= n;
+    nbits -= n;
+  }
+  // Bounded read of n <= 16 bits (BitReader::take semantics).
+  __device__ __forceinline__ u32 take(u32 n, u32* error) {
+    if (*error) return 0;
+    if (n > avail()) { *error = kTruncated; return 0; }
+    refill();
+    const u32 v = u32(buf) & ((1u << n) - 1u);
+    consume(n);
+    return v;
+  }
+};
+
+// ---------------------------------------------------------------------------
 // Huffman tables
 // ---------------------------------------------------------------------------
 // Entry layout: [value:16][kind:4][extra:4][length:8].
@@ -281,6 +351,9 @@ __device__ inline void warp_build_fixed(Tables& t) {
   warp_build(t.d, t.lens, 32, false, true, t.scratch, DFn());
 }
 
+// Rendezvous actions: lane 0 parses, then the whole warp performs one action.
+enum Action : u32 { kNone = 0, kStored = 1, kCopy = 2, kDynamic = 3, kFlush = 4 };
+
 // ---------------------------------------------------------------------------
 // Token decode
 // ---------------------------------------------------------------------------
@@ -358,10 +431,88 @@ __device__ __forceinline__ Token decode_token(const BitCursor& c, const Tables& 
   return tok;
 }
 
+// Exact token decode on Bits, consuming it.  Same status precedence as
+// decode_token; after an error the reader state is unspecified (errors end
+// the stream).
+__device__ __forceinline__ Token take_token(Bits& b, const Tables& t) {
+  Token tok;
+  tok.kind = kTokError;
+  tok.value = tok.length = tok.dist = tok.bits = 0;
+  tok.error = 0;
+  const u32 avail = b.avail();
+  b.refill();
+  u32 v = u32(b.buf);
+  u32 e = t.ll.lut[v & 1023u];
+  u32 kind = entry_kind(e);
+  if (kind == kLong) {
+    e = decode_long(t.ll, v, LLFn());
+    kind = entry_kind(e);
+  }
+  if (kind == kHole) {
+    tok.error = avail >= t.ll.maxlen ? kBadSymbol : kTruncated;
+    return tok;
+  }
+  const u32 L = entry_len(e);
+  if (L > avail) { tok.error = kTruncated; return tok; }
+  if (kind == kLiteral || kind == kEnd) {
+    tok.kind = kind == kLiteral ? kTokLiteral : kTokEnd;
+    tok.value = entry_value(e);
+    tok.bits = L;
+    b.consume(L);
+    return tok;
+  }
+  if (kind == kReserved) { tok.error = kBadSymbol; return tok; }
+  const u32 E = entry_extra(e);
+  if (L + E > avail) { tok.error = kTruncated; return tok; }
+  tok.length = entry_value(e) + ((v >> L) & ((1u << E) - 1u));
+  b.consume(L + E);
+  const u32 left = avail - (L + E);
+  b.refill();
+  v = u32(b.buf);
+  u32 d = t.d.lut[v & 255u];
+  u32 dk = entry_kind(d);
+  if (dk == kLong) {
+    d = decode_long(t.d, v, DFn());
+    dk = entry_kind(d);
+  }
+  if (dk == kEmpty) { tok.error = kBadSymbol; return tok; }
+  if (dk == kHole) {
+    tok.error = left >= t.d.maxlen ? kBadSymbol : kTruncated;
+    return tok;
+  }
+  const u32 Ld = entry_len(d);
+  if (Ld > left) { tok.error = kTruncated; return tok; }
+  if (dk == kReserved) { tok.error = kBadSymbol; return tok; }
+  const u32 Ed = entry_extra(d);
+  if (Ld + Ed > left) { tok.error = kTruncated; return tok; }
+  tok.dist = entry_value(d) + ((v >> Ld) & ((1u << Ed) - 1u));
+  b.consume(Ld + Ed);
+  tok.bits = L + E + Ld + Ed;
+  tok.kind = kTokMatch;
+  return tok;
+}
+
 // Dynamic block header, lane 0 reading and the warp building tables
 // (dynamic_tables, _decode_kernels.py:240-287).  All lanes call; lane 0's
 // cursor is the one that advances.  Returns the status on every lane.
-__device__ inline u32 warp_dynamic_header(BitCursor& c, Tables& t) {
+// One code-length symbol (complete 7-bit table); 1 if it does not fit.
+__device__ __forceinline__ u32 cl_symbol(BitCursor& c, const Tables& t, u32* err) {
+  const u32 e = t.cl.lut[c.peek() & 127u];
+  if (entry_len(e) > c.avail()) { *err = kTruncated; return 0; }
+  c.skip(entry_len(e));
+  return entry_value(e);
+}
+__device__ __forceinline__ u32 cl_symbol(Bits& c, const Tables& t, u32* err) {
+  const u32 avail = c.avail();
+  c.refill();
+  const u32 e = t.cl.lut[u32(c.buf) & 127u];
+  if (entry_len(e) > avail) { *err = kTruncated; return 0; }
+  c.consume(entry_len(e));
+  return entry_value(e);
+}
+
+template <typename Reader>
+__device__ u32 warp_dynamic_header(Reader& c, Tables& t) {
   const u32 lane = threadIdx.x & 31u;
   u32 err = 0, nl = 0, nd = 0, nc = 0;
   if (lane == 0) {
@@ -387,12 +538,8 @@ __device__ inline u32 warp_dynamic_header(BitCursor& c, Tables& t) {
   if (lane == 0) {
     u32 i = 0;
     while (i < nl + nd) {
-      const u64 v = c.peek();
-      const u32 e = t.cl.lut[v & 127u];
-      const u32 L = entry_len(e);
-      if (L > c.avail()) { err = kTruncated; break; }
-      c.skip(L);
-      const u32 sym = entry_value(e);
+      const u32 sym = cl_symbol(c, t, &err);
+      if (err) break;
       if (sym < 16) { t.lens[i++] = u8(sym); continue; }
       u32 repeat, value;
       if (sym == 16) {

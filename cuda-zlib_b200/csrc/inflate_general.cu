@@ -522,7 +522,9 @@ cudaError_t launch_discover(const u8* in, u64 in_size, u32* bitmap, u32* count, 
   const u64 cap = u64(dev.sms) * 16;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
+  profile_begin("discover_kernel", stream);
   discover_kernel<<<u32(blocks), 256, 0, stream>>>(in, in_size, bitmap, count, gate);
+  profile_end(stream);
   return cudaGetLastError();
 }
 

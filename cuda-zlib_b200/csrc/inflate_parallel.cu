@@ -1,0 +1,710 @@
+// Block-parallel inflate of one large zlib stream.
+//
+// A Deflate stream is serial inside a block but its blocks can be decoded
+// independently once their start bits and output offsets are known, except
+// for back-references that reach into earlier blocks.  The pipeline:
+//
+//   candidates  the reference's candidate rule (bit 0, every bit offset that
+//               parses as a valid dynamic header, stored-block endpoint
+//               seeds; discover_kernel) compacted into a sorted list;
+//   describe    one warp per candidate decodes without output from the
+//               candidate through any following stored/fixed blocks up to
+//               the next dynamic header ("node"): end bit, output size,
+//               block count, final flag.  Every valid dynamic header is a
+//               candidate, so the true chain is a path of nodes;
+//   chain       one CTA links each node to the candidate at its end bit and
+//               extracts the path from bit 0 by pointer doubling, with
+//               output prefixes, extent and block-count checks;
+//   emit        one warp per path node decodes into a shared-memory ring of
+//               u16 symbols: a byte, or 256 + k for "the byte k+1 positions
+//               before this node's start" (a reference into an earlier
+//               node; copies propagate the marker).  Flushes write bytes to
+//               the output and, for markers, the absolute source position
+//               plus a bit in an unresolved-position bitmap;
+//   resolve     each unresolved position follows source positions until it
+//               reaches a byte decoded directly (positions strictly
+//               decrease, so every chase ends);
+//   adler       a segmented reduction over the output, then the checksum
+//               and status.
+//
+// This is the marker method of published parallel gzip decoders (pugz,
+// rapidgzip) applied with the chain known exactly, so no speculation is
+// ever wrong: the output is exact or the stream is reported failed.  Any
+// failure hands over to general_status_kernel, which reports the status
+// the reference's route reports.
+#include "kernels.h"
+#include "inflate_core.cuh"
+
+namespace cz {
+
+constexpr u32 kNodeWarps = 4;      // warps per CTA in describe/emit
+constexpr u32 kEmitRing = 8192;    // u16 history entries per emitting warp
+constexpr u32 kEmitMask = kEmitRing - 1;
+constexpr u32 kEmitFlush = 2048;   // pending symbols that trigger a flush
+constexpr u32 kInfoFinal = 1u, kInfoOk = 2u;
+
+struct DescribeShared {
+  Tables fixed;
+  Tables dyn[kNodeWarps];
+};
+struct EmitShared {
+  Tables fixed;
+  Tables dyn[kNodeWarps];
+  __align__(16) u16 ring[kNodeWarps][kEmitRing];
+};
+
+// ---------------------------------------------------------------------------
+// Candidate compaction: bitmap over body bit offsets -> sorted u32 list.
+// ---------------------------------------------------------------------------
+constexpr u32 kCompactWords = 4096;  // bitmap words per CTA (131072 offsets)
+
+__global__ void cand_count_kernel(const u32* bitmap, u32 words, u32* block_counts) {
+  __shared__ u32 warp_sum[8];
+  const u32 base = blockIdx.x * kCompactWords;
+  u32 count = 0;
+  for (u32 i = threadIdx.x; i < kCompactWords && base + i < words; i += blockDim.x)
+    count += __popc(bitmap[base + i]);
+  for (u32 o = 16; o; o >>= 1) count += __shfl_xor_sync(kFullMask, count, o);
+  if ((threadIdx.x & 31) == 0) warp_sum[threadIdx.x >> 5] = count;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    u32 total = 0;
+    for (u32 w = 0; w < blockDim.x / 32; ++w) total += warp_sum[w];
+    block_counts[blockIdx.x] = total;
+  }
+}
+
+// Exclusive scan of block_counts in place (one CTA); total -> *total.
+__global__ void cand_scan_kernel(u32* block_counts, u32 blocks, u32* total) {
+  __shared__ u32 carry;
+  __shared__ u32 warp_sum[32];
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  for (u32 base = 0; base < blocks; base += blockDim.x) {
+    const u32 i = base + threadIdx.x;
+    const u32 v = i < blocks ? block_counts[i] : 0;
+    u32 incl = v;
+    for (u32 o = 1; o < 32; o <<= 1) {
+      const u32 t = __shfl_up_sync(kFullMask, incl, o);
+      if ((threadIdx.x & 31) >= o) incl += t;
+    }
+    if ((threadIdx.x & 31) == 31) warp_sum[threadIdx.x >> 5] = incl;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      u32 w = threadIdx.x < blockDim.x / 32 ? warp_sum[threadIdx.x] : 0;
+      for (u32 o = 1; o < 32; o <<= 1) {
+        const u32 t = __shfl_up_sync(kFullMask, w, o);
+        if (threadIdx.x >= o) w += t;
+      }
+      warp_sum[threadIdx.x] = w;  // inclusive per warp
+    }
+    __syncthreads();
+    const u32 warp = threadIdx.x >> 5;
+    const u32 before = carry + (warp ? warp_sum[warp - 1] : 0) + incl - v;
+    if (i < blocks) block_counts[i] = before;
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) carry = before + v;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *total = carry;
+}
+
+__global__ void cand_write_kernel(const u32* bitmap, u32 words, const u32* block_offsets,
+                                  u32* cands, u32 capacity) {
+  __shared__ u32 warp_sum[8];
+  const u32 base = blockIdx.x * kCompactWords;
+  const u32 per = kCompactWords / blockDim.x;  // contiguous words per thread
+  const u32 first = base + threadIdx.x * per;
+  u32 count = 0;
+  for (u32 k = 0; k < per; ++k)
+    if (first + k < words) count += __popc(bitmap[first + k]);
+  u32 incl = count;
+  for (u32 o = 1; o < 32; o <<= 1) {
+    const u32 t = __shfl_up_sync(kFullMask, incl, o);
+    if ((threadIdx.x & 31) >= o) incl += t;
+  }
+  if ((threadIdx.x & 31) == 31) warp_sum[threadIdx.x >> 5] = incl;
+  __syncthreads();
+  u32 before = block_offsets[blockIdx.x] + incl - count;
+  for (u32 w = 0; w < (threadIdx.x >> 5); ++w) before += warp_sum[w];
+  for (u32 k = 0; k < per; ++k) {
+    if (first + k >= words) break;
+    u32 bits = bitmap[first + k];
+    while (bits) {
+      const u32 b = __ffs(bits) - 1;
+      bits &= bits - 1;
+      if (before < capacity) cands[before] = (first + k) * 32 + b;
+      ++before;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Node walk (describe and emit share it).
+// ---------------------------------------------------------------------------
+struct NodeResult {
+  u32 end, size, blocks, info;
+};
+
+// Flush ring symbols [from, to) of a node whose output starts at `prefix`:
+// bytes to `out`, markers to `source` + the `unresolved` bitmap.
+__device__ void flush_symbols(const u16* ring, u8* out, u32* source, u32* unresolved, u32 prefix,
+                              u32 from, u32 to) {
+  const u32 lane = threadIdx.x & 31u;
+  for (u32 p = from + lane; p < to; p += 32) {
+    const u32 v = ring[p & kEmitMask];
+    const u32 at = prefix + p;
+    if (v < 256) {
+      out[at] = u8(v);
+    } else {
+      out[at] = 0;
+      source[at] = prefix - 1 - (v - 256);
+      atomicOr(&unresolved[at >> 5], 1u << (at & 31));
+    }
+  }
+}
+
+// Symbol of node-local position q (already flushed) from global memory.
+__device__ __forceinline__ u32 flushed_symbol(const u8* out, const u32* source,
+                                              const u32* unresolved, u32 prefix, u32 q) {
+  const u32 at = prefix + q;
+  if ((unresolved[at >> 5] >> (at & 31)) & 1u) return 256 + (prefix - 1 - source[at]);
+  return out[at];
+}
+
+template <bool kEmit>
+__device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expected, u32 window,
+                                const Tables& fixed, Tables& dyn, u16* ring, u8* out,
+                                u32* source, u32* unresolved, u32 prefix) {
+  const u32 lane = threadIdx.x & 31u;
+  NodeResult r{start, 0, 0, 0};
+  Bits c;
+  u32 produced = 0, flushed = 0, final = 0, blocks = 0, full_words = 0;
+  u32 fail = 0, stop = 0;
+  bool need_header = true, use_dyn = false;
+  if (lane == 0) {
+    c.init(body, bytes);
+    c.seek(start);
+    full_words = (c.shift + c.end) >> 5;
+  }
+  const u32 limit = kEmit ? expected - prefix : expected;  // output bound of this node
+  for (;;) {
+    u32 action = kNone, len = 0, dist = 0, src = 0, dst = 0;
+    if (lane == 0) {
+      while (!fail && !stop) {
+        if (kEmit && produced - flushed >= kEmitFlush) { action = kFlush; break; }
+        if (need_header) {
+          const u32 header = c.pos();
+          u32 err = 0;
+          const u32 f = c.take(1, &err), type = c.take(2, &err);
+          if (err || type == 3) { fail = 1; break; }
+          if (type == 2 && blocks) {  // the next node starts here
+            c.seek(header);
+            stop = 1;
+            break;
+          }
+          final = f;
+          ++blocks;
+          if (type == 0) {
+            c.seek((c.pos() + 7) & ~7u);
+            const u32 n = c.take(16, &err), comp = c.take(16, &err);
+            const u32 at = c.pos();
+            if (err || (n ^ comp) != 0xffffu || n > limit - produced || at > c.end ||
+                n * 8 > c.end - at) { fail = 1; break; }
+            if (kEmit) {
+              action = kStored;
+              src = at >> 3;
+              dst = produced;
+              len = n;
+            }
+            produced += n;
+            c.seek(at + n * 8);
+            if (final) stop = 1;
+            if (kEmit) break;
+            continue;
+          }
+          if (type == 2) { action = kDynamic; break; }
+          use_dyn = false;
+          need_header = false;
+        }
+        const Tables& t = use_dyn ? dyn : fixed;
+        while (c.idx + 2 <= full_words && produced + 258 <= limit &&
+               (!kEmit || produced - flushed < kEmitFlush)) {
+          c.refill_fast();
+          const u32 v = u32(c.buf);
+          const u32 e = t.ll.lut[v & 1023u];
+          const u32 kind = entry_kind(e);
+          if (kind == kLiteral) {
+            c.consume(entry_len(e));
+            if (kEmit) ring[produced & kEmitMask] = u16(entry_value(e));
+            ++produced;
+            continue;
+          }
+          if (kind != kLength) break;
+          const u64 saved_buf = c.buf;
+          const u32 saved_bits = c.nbits, saved_idx = c.idx;
+          const u32 L = entry_len(e), E = entry_extra(e);
+          const u32 length = entry_value(e) + ((v >> L) & ((1u << E) - 1u));
+          c.consume(L + E);
+          c.refill_fast();
+          const u32 w = u32(c.buf);
+          const u32 d = t.d.lut[w & 255u];
+          const u32 Ld = entry_len(d), Ed = entry_extra(d);
+          const u32 span = entry_value(d) + ((w >> Ld) & ((1u << Ed) - 1u));
+          if (entry_kind(d) != kLiteral || span > window) {
+            c.buf = saved_buf;
+            c.nbits = saved_bits;
+            c.idx = saved_idx;
+            break;
+          }
+          c.consume(Ld + Ed);
+          if (kEmit) {
+            if (span > prefix + produced) { fail = 1; break; }
+            if (length >= 32) {
+              action = kCopy;
+              dst = produced;
+              len = length;
+              dist = span;
+              produced += length;
+              break;
+            }
+            for (u32 j = 0; j < length; ++j) {
+              const u32 p = produced + j;
+              u32 sym;
+              if (span > p) sym = 256 + (span - p - 1);
+              else if (span + 258 <= kEmitRing) sym = ring[(p - span) & kEmitMask];
+              else sym = flushed_symbol(out, source, unresolved, prefix, p - span);
+              ring[p & kEmitMask] = u16(sym);
+            }
+          }
+          produced += length;
+        }
+        if (action != kNone || fail) break;
+        if (kEmit && produced - flushed >= kEmitFlush) continue;
+        const Token tok = take_token(c, t);
+        if (tok.kind == kTokError) { fail = 1; break; }
+        if (tok.kind == kTokEnd) {
+          need_header = true;
+          if (final) stop = 1;
+          continue;
+        }
+        const u32 size = tok.kind == kTokLiteral ? 1u : tok.length;
+        if (size > limit - produced) { fail = 1; break; }
+        if (tok.kind == kTokLiteral) {
+          if (kEmit) ring[produced & kEmitMask] = u16(tok.value);
+          ++produced;
+          continue;
+        }
+        if (tok.dist > window) { fail = 1; break; }
+        if (kEmit) {
+          if (tok.dist > prefix + produced) { fail = 1; break; }
+          if (tok.length >= 32) {
+            action = kCopy;
+            dst = produced;
+            len = tok.length;
+            dist = tok.dist;
+            produced += tok.length;
+            break;
+          }
+          for (u32 j = 0; j < tok.length; ++j) {
+            const u32 p = produced + j;
+            u32 sym;
+            if (tok.dist > p) sym = 256 + (tok.dist - p - 1);
+            else if (tok.dist + 258 <= kEmitRing) sym = ring[(p - tok.dist) & kEmitMask];
+            else sym = flushed_symbol(out, source, unresolved, prefix, p - tok.dist);
+            ring[p & kEmitMask] = u16(sym);
+          }
+        }
+        produced += tok.length;
+      }
+    }
+    fail = __shfl_sync(kFullMask, fail, 0);
+    if (fail) break;
+    action = __shfl_sync(kFullMask, action, 0);
+    const u32 now = __shfl_sync(kFullMask, produced, 0);
+    const bool done = __shfl_sync(kFullMask, stop, 0) != 0;
+    if (action == kDynamic) {
+      const u32 st = warp_dynamic_header(c, dyn);
+      if (st) { fail = 1; break; }
+      if (lane == 0) { use_dyn = true; need_header = false; }
+    } else if (kEmit && action == kFlush) {
+      const u32 to = now;
+      flush_symbols(ring, out, source, unresolved, prefix, flushed, to);
+      flushed = to;
+    } else if (kEmit && action == kStored) {
+      len = __shfl_sync(kFullMask, len, 0);
+      src = __shfl_sync(kFullMask, src, 0);
+      dst = __shfl_sync(kFullMask, dst, 0);
+      flush_symbols(ring, out, source, unresolved, prefix, flushed, dst);
+      for (u32 j = lane; j < len; j += 32) {
+        const u8 b = body[src + j];
+        out[prefix + dst + j] = b;
+        ring[(dst + j) & kEmitMask] = b;
+      }
+      flushed = dst + len;
+    } else if (kEmit && action == kCopy) {
+      len = __shfl_sync(kFullMask, len, 0);
+      dst = __shfl_sync(kFullMask, dst, 0);
+      dist = __shfl_sync(kFullMask, dist, 0);
+      // Seeds before dst only; markers for positions before the node start.
+      const bool from_ring = dist + 258 <= kEmitRing;
+      u32 s = lane % dist;
+      const u32 step = 32 % dist;
+      for (u32 j = lane; j < len; j += 32) {
+        const u32 q = dst + s - dist;  // wraps when the seed precedes the node
+        u32 sym;
+        if (dist > dst + s) sym = 256 + (dist - dst - s - 1);
+        else if (from_ring) sym = ring[q & kEmitMask];
+        else sym = flushed_symbol(out, source, unresolved, prefix, q);
+        ring[(dst + j) & kEmitMask] = u16(sym);
+        s += step;
+        if (s >= dist) s -= dist;
+      }
+    }
+    __syncwarp();
+    if (done) break;
+  }
+  if (!fail && kEmit) flush_symbols(ring, out, source, unresolved, prefix, flushed,
+                                    __shfl_sync(kFullMask, produced, 0));
+  r.end = __shfl_sync(kFullMask, c.pos(), 0);
+  r.size = __shfl_sync(kFullMask, produced, 0);
+  r.blocks = __shfl_sync(kFullMask, blocks, 0);
+  r.info = (fail ? 0u : kInfoOk) | (__shfl_sync(kFullMask, final, 0) ? kInfoFinal : 0u);
+  return r;
+}
+
+// Describe every candidate (warp per candidate, work stealing).
+__global__ void __launch_bounds__(kNodeWarps * 32)
+describe_kernel(const u8* in, u32 in_size, u64 expected, const u32* cands, const u32* total,
+                u32 capacity, u32* next_item, u32* ends, u32* sizes, u32* blocks, u32* infos) {
+  __shared__ DescribeShared sh;
+  const u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  u32 window = 0, wanted = 0;
+  if (zlib_framing(in, in_size, &window, &wanted)) return;
+  const u32 count = min_u32(*total, capacity);
+  if (warp == 0) warp_build_fixed(sh.fixed);
+  __syncthreads();
+  for (;;) {
+    u32 item = 0;
+    if (lane == 0) item = atomicAdd(next_item, 1u);
+    item = __shfl_sync(kFullMask, item, 0);
+    if (item >= count) break;
+    const NodeResult r = warp_node<false>(in + 2, in_size - 6, cands[item], u32(expected), window,
+                                          sh.fixed, sh.dyn[warp], nullptr, nullptr, nullptr,
+                                          nullptr, 0);
+    if (lane == 0) {
+      ends[item] = r.end;
+      sizes[item] = r.size;
+      blocks[item] = r.blocks;
+      infos[item] = r.info;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Chain: successor links, pointer doubling from bit 0, prefixes and checks.
+// One CTA.  state[0] = path length, state[1] = chain ok.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024)
+chain_kernel(const u8* in, u32 in_size, u64 expected, u32 max_blocks, const u32* cands,
+             const u32* total, u32 capacity, const u32* ends, const u32* sizes,
+             const u32* blocks, const u32* infos, u32* jump, u32 levels, u32* path, u32* prefix,
+             u32* state) {
+  __shared__ u32 warp_sum[32];
+  __shared__ u32 s_len, s_ok, s_carry, s_blocks;
+  const u32 tid = threadIdx.x;
+  u32 window = 0, wanted = 0;
+  const u32 count = min_u32(*total, capacity);
+  if (zlib_framing(in, in_size, &window, &wanted) || *total > capacity || !count ||
+      cands[0] != 0) {
+    if (tid == 0) { state[0] = 0; state[1] = 0; }
+    return;
+  }
+  const u32 end_node = count, bad_node = count + 1, nodes = count + 2;
+  // Level 0: successors.
+  for (u32 i = tid; i < nodes; i += blockDim.x) {
+    u32 next = bad_node;
+    if (i == end_node) next = end_node;
+    else if (i < count) {
+      const u32 info = infos[i];
+      if (info & kInfoOk) {
+        if (info & kInfoFinal) {
+          next = end_node;
+        } else {
+          const u32 target = ends[i];
+          u32 lo = i + 1, hi = count;  // successors start strictly later
+          while (lo < hi) {
+            const u32 mid = (lo + hi) >> 1;
+            if (cands[mid] < target) lo = mid + 1;
+            else hi = mid;
+          }
+          if (lo < count && cands[lo] == target) next = lo;
+        }
+      }
+    }
+    jump[i] = next;
+  }
+  __syncthreads();
+  for (u32 k = 1; k < levels; ++k) {
+    const u32* prev = jump + u64(k - 1) * nodes;
+    u32* cur = jump + u64(k) * nodes;
+    for (u32 i = tid; i < nodes; i += blockDim.x) cur[i] = prev[prev[i]];
+    __syncthreads();
+  }
+  if (tid == 0) {
+    // Nodes on the path from node 0 (bit 0), excluding the terminal sink.
+    u32 node = 0, len = 1;
+    for (u32 k = levels; k-- > 0;) {
+      const u32 n = jump[u64(k) * nodes + node];
+      if (n < count) {
+        node = n;
+        len += 1u << k;
+      }
+    }
+    const u32 terminal = jump[node];
+    s_len = len;
+    s_ok = terminal == end_node;
+    s_carry = 0;
+    s_blocks = 0;
+  }
+  __syncthreads();
+  const u32 len = s_len;
+  if (!s_ok) {
+    if (tid == 0) { state[0] = 0; state[1] = 0; }
+    return;
+  }
+  for (u32 base = 0; base < len; base += blockDim.x) {
+    const u32 m = base + tid;
+    u32 node = 0, size = 0, nb = 0;
+    if (m < len) {
+      for (u32 k = 0; k < levels; ++k)
+        if ((m >> k) & 1u) node = jump[u64(k) * nodes + node];
+      path[m] = node;
+      size = sizes[node];
+      nb = blocks[node];
+    }
+    u32 incl = size, bincl = nb;
+    for (u32 o = 1; o < 32; o <<= 1) {
+      const u32 t = __shfl_up_sync(kFullMask, incl, o);
+      const u32 tb = __shfl_up_sync(kFullMask, bincl, o);
+      if ((tid & 31) >= o) { incl += t; bincl += tb; }
+    }
+    if ((tid & 31) == 31) warp_sum[tid >> 5] = incl;
+    __syncthreads();
+    u32 before = s_carry + incl - size;
+    for (u32 w = 0; w < (tid >> 5); ++w) before += warp_sum[w];
+    if (m < len) prefix[m] = before;
+    if ((tid & 31) == 31) atomicAdd(&s_blocks, bincl);
+    __syncthreads();
+    if (tid == blockDim.x - 1 || m == len - 1) s_carry = before + size;
+    __syncthreads();
+  }
+  if (tid == 0) {
+    const u32 last = path[len - 1];
+    const u32 body = in_size - 6;
+    const bool ok = u64(s_carry) == expected && (ends[last] + 7) / 8 == body &&
+                    s_blocks <= max_blocks;
+    state[0] = ok ? len : 0;
+    state[1] = ok ? 1u : 0u;
+  }
+}
+
+// Emit every path node (warp per node, work stealing).
+__global__ void __launch_bounds__(kNodeWarps * 32)
+emit_kernel(const u8* in, u32 in_size, u64 expected, const u32* cands, const u32* path,
+            const u32* prefix, const u32* sizes, const u32* state, u32* next_item, u8* out,
+            u32* source, u32* unresolved, u32* fail_flag) {
+  extern __shared__ __align__(16) u8 smem[];
+  EmitShared& sh = *reinterpret_cast<EmitShared*>(smem);
+  const u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  if (!state[1]) return;
+  const u32 len = state[0];
+  u32 window = 0, wanted = 0;
+  zlib_framing(in, in_size, &window, &wanted);
+  if (warp == 0) warp_build_fixed(sh.fixed);
+  __syncthreads();
+  for (;;) {
+    u32 item = 0;
+    if (lane == 0) item = atomicAdd(next_item, 1u);
+    item = __shfl_sync(kFullMask, item, 0);
+    if (item >= len) break;
+    const u32 node = path[item];
+    const NodeResult r = warp_node<true>(in + 2, in_size - 6, cands[node], u32(expected), window,
+                                         sh.fixed, sh.dyn[warp], sh.ring[warp], out, source,
+                                         unresolved, prefix[item]);
+    if (lane == 0 && (!(r.info & kInfoOk) || r.size != sizes[node])) atomicOr(fail_flag, 1u);
+  }
+}
+
+// Resolve unresolved positions by chasing source positions.
+__global__ void resolve_kernel(const u32* state, u32 words, const u32* unresolved,
+                               const u32* source, u8* out) {
+  if (!state[1]) return;
+  const u64 stride = u64(gridDim.x) * blockDim.x;
+  for (u64 w = u64(blockIdx.x) * blockDim.x + threadIdx.x; w < words; w += stride) {
+    u32 bits = unresolved[w];
+    while (bits) {
+      const u32 b = __ffs(bits) - 1;
+      bits &= bits - 1;
+      const u32 at = u32(w) * 32 + b;
+      u32 q = source[at];
+      // Sources strictly decrease along a chase, so it ends at a position
+      // that emission wrote directly.
+      while ((unresolved[q >> 5] >> (q & 31)) & 1u) q = source[q];
+      out[at] = out[q];
+    }
+  }
+}
+
+// Adler-32 partials over 64 KiB segments: (s1, s2 with segment-local weights).
+constexpr u32 kAdlerSegment = 65536;
+
+__global__ void adler_parts_kernel(const u32* state, const u8* out, u32 n, u64* parts) {
+  if (!state[1]) return;
+  __shared__ u64 a1[8], a2[8];
+  const u32 seg = blockIdx.x;
+  const u32 base = seg * kAdlerSegment;
+  const u32 len = min_u32(kAdlerSegment, n - base);
+  u64 s1 = 0, s2 = 0;
+  const bool vec = (reinterpret_cast<uintptr_t>(out + base) & 15u) == 0;
+  if (vec) {
+    for (u32 p = threadIdx.x * 16; p + 16 <= len; p += blockDim.x * 16) {
+      const uint4 v = *reinterpret_cast<const uint4*>(out + base + p);
+      const u32 words[4] = {v.x, v.y, v.z, v.w};
+      for (u32 k = 0; k < 4; ++k) {
+        const u32 w = words[k];
+        const u32 b0 = w & 255u, b1 = (w >> 8) & 255u, b2 = (w >> 16) & 255u, b3 = w >> 24;
+        const u32 sum = b0 + b1 + b2 + b3;
+        const u32 weight = len - p - 4 * k;
+        s1 += sum;
+        s2 += u64(weight) * sum - (b1 + 2 * b2 + 3 * b3);
+      }
+    }
+    for (u32 p = (len & ~15u) + threadIdx.x; p < len; p += blockDim.x) {
+      const u32 x = out[base + p];
+      s1 += x;
+      s2 += u64(len - p) * x;
+    }
+  } else {
+    for (u32 p = threadIdx.x; p < len; p += blockDim.x) {
+      const u32 x = out[base + p];
+      s1 += x;
+      s2 += u64(len - p) * x;
+    }
+  }
+  for (u32 o = 16; o; o >>= 1) {
+    s1 += __shfl_xor_sync(kFullMask, s1, o);
+    s2 += __shfl_xor_sync(kFullMask, s2, o);
+  }
+  if ((threadIdx.x & 31) == 0) { a1[threadIdx.x >> 5] = s1; a2[threadIdx.x >> 5] = s2; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    u64 t1 = 0, t2 = 0;
+    for (u32 w = 0; w < blockDim.x / 32; ++w) { t1 += a1[w]; t2 += a2[w]; }
+    parts[2 * seg] = t1 % kAdlerMod;
+    parts[2 * seg + 1] = t2 % kAdlerMod;
+  }
+}
+
+// Fast-path verdict into meta[0] (0 or 1), for general_status_kernel.
+__global__ void parallel_finish_kernel(const u8* in, u32 in_size, const u32* state,
+                                       const u32* fail_flag, const u64* parts, u32 segments,
+                                       u32 n, u32* meta) {
+  __shared__ u64 a1[32], a2[32];
+  u32 window = 0, wanted = 0;
+  const bool framed = zlib_framing(in, in_size, &window, &wanted) == 0;
+  const bool ok = framed && state[1] && !*fail_flag;
+  u64 s1 = 0, s2 = 0;
+  if (ok) {
+    for (u32 s = threadIdx.x; s < segments; s += blockDim.x) {
+      const u32 end = min_u32((s + 1) * kAdlerSegment, n);
+      const u64 after = (n - end) % kAdlerMod;
+      s1 += parts[2 * s];
+      s2 += (parts[2 * s + 1] + parts[2 * s] * after) % kAdlerMod;
+    }
+    s1 %= kAdlerMod;
+    s2 %= kAdlerMod;
+  }
+  for (u32 o = 16; o; o >>= 1) {
+    s1 += __shfl_xor_sync(kFullMask, s1, o);
+    s2 += __shfl_xor_sync(kFullMask, s2, o);
+  }
+  if ((threadIdx.x & 31) == 0) { a1[threadIdx.x >> 5] = s1; a2[threadIdx.x >> 5] = s2; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    u64 t1 = 0, t2 = 0;
+    for (u32 w = 0; w < blockDim.x / 32; ++w) { t1 += a1[w]; t2 += a2[w]; }
+    u32 status = 1;
+    if (ok) status = adler_finish(t1, t2, n) == wanted ? 0u : u32(kAdlerMismatch);
+    meta[0] = status;
+    meta[1] = 0;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+size_t parallel_inflate_emit_smem() { return sizeof(EmitShared); }
+
+cudaError_t configure_parallel_inflate(int* emit_per_sm) {
+  cudaError_t e = cudaFuncSetAttribute(emit_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(sizeof(EmitShared)));
+  if (e != cudaSuccess) return e;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(emit_per_sm, emit_kernel,
+                                                       kNodeWarps * 32, sizeof(EmitShared));
+}
+
+u32 chain_levels(u32 capacity) {
+  u32 levels = 1;
+  while ((1ull << (levels - 1)) < u64(capacity) + 2) ++levels;
+  return levels;
+}
+
+ParallelScratch parallel_scratch_layout(u64 in_size, u64 expected, u32 capacity) {
+  ParallelScratch s{};
+  const u64 body = in_size - 6;
+  s.bitmap_words = (body * 8 + 31) / 32 + 1;
+  s.compact_blocks = u32((s.bitmap_words + kCompactWords - 1) / kCompactWords);
+  s.capacity = capacity;
+  s.levels = chain_levels(capacity);
+  s.out_words = (expected + 31) / 32 + 1;
+  s.segments = u32((expected + kAdlerSegment - 1) / kAdlerSegment);
+  return s;
+}
+
+cudaError_t launch_parallel_inflate(const u8* in, u64 in_size, u8* out, u64 expected,
+                                    u32 max_blocks, const ParallelScratch& s,
+                                    const ParallelBuffers& b, u32* meta, const DeviceInfo& dev,
+                                    cudaStream_t stream) {
+  const u32 nodes = s.capacity + 2;
+  cand_count_kernel<<<s.compact_blocks, 256, 0, stream>>>(b.bitmap, u32(s.bitmap_words),
+                                                          b.block_counts);
+  cand_scan_kernel<<<1, 1024, 0, stream>>>(b.block_counts, s.compact_blocks, b.total);
+  cand_write_kernel<<<s.compact_blocks, 256, 0, stream>>>(b.bitmap, u32(s.bitmap_words),
+                                                          b.block_counts, b.cands, s.capacity);
+  const u32 node_grid = u32(dev.sms) * 4;
+  profile_begin("describe_kernel", stream);
+  describe_kernel<<<node_grid, kNodeWarps * 32, 0, stream>>>(
+      in, u32(in_size), expected, b.cands, b.total, s.capacity, b.counters, b.ends, b.sizes,
+      b.blocks, b.infos);
+  profile_end(stream);
+  chain_kernel<<<1, 1024, 0, stream>>>(in, u32(in_size), expected, max_blocks, b.cands, b.total,
+                                       s.capacity, b.ends, b.sizes, b.blocks, b.infos, b.jump,
+                                       s.levels, b.path, b.prefix, b.state);
+  (void)nodes;
+  const u32 emit_grid = u32(dev.sms) * u32(dev.emit_per_sm > 0 ? dev.emit_per_sm : 1);
+  profile_begin("emit_kernel", stream);
+  emit_kernel<<<emit_grid, kNodeWarps * 32, sizeof(EmitShared), stream>>>(
+      in, u32(in_size), expected, b.cands, b.path, b.prefix, b.sizes, b.state, b.counters + 1,
+      out, b.source, b.unresolved, b.fail);
+  profile_end(stream);
+  resolve_kernel<<<u32(dev.sms) * 8, 256, 0, stream>>>(b.state, u32(s.out_words), b.unresolved,
+                                                       b.source, out);
+  if (s.segments)
+    adler_parts_kernel<<<s.segments, 256, 0, stream>>>(b.state, out, u32(expected), b.parts);
+  parallel_finish_kernel<<<1, 1024, 0, stream>>>(in, u32(in_size), b.state, b.fail, b.parts,
+                                                 s.segments, u32(expected), meta);
+  return cudaGetLastError();
+}
+
+}  // namespace cz

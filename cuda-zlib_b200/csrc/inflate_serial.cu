@@ -21,39 +21,69 @@
 namespace cz {
 
 constexpr u32 kSerialWarps = 4;
-constexpr u32 kRing = 8192;
+constexpr u32 kRing = 16384;      // history bytes cached per warp (power of two)
 constexpr u32 kRingMask = kRing - 1;
+constexpr u32 kFlushBytes = 2048; // produced bytes that trigger a warp flush
 
 struct SerialShared {
   Tables fixed;
   Tables dyn[kSerialWarps];
-  u8 ring[kSerialWarps][kRing];
+  __align__(16) u8 ring[kSerialWarps][kRing];
 };
 
-enum Action : u32 { kNone = 0, kStored = 1, kCopy = 2, kDynamic = 3 };
-
-// Adler-32 of data[0..n) by one warp (lanes stride bytes; coalesced).
-__device__ u32 warp_adler(const u8* data, u64 n) {
-  const u32 lane = threadIdx.x & 31u;
+// Adler-32 partial sums of one lane: s1 = sum x, s2 = sum (n - p) x over the
+// positions p this lane flushed.  Kept reduced so they never overflow.
+struct AdlerLane {
   u64 s1 = 0, s2 = 0;
-  u32 since = 0;
-  for (u64 i = lane; i < n; i += 32) {
-    const u32 x = data[i];
+  __device__ __forceinline__ void add(u32 x, u32 weight) {
     s1 += x;
-    s2 += (n - i) * x;
-    if (++since == (1u << 16)) {  // keep the sums far from 2^64 for any n
-      s1 %= kAdlerMod;
-      s2 %= kAdlerMod;
-      since = 0;
-    }
+    s2 += u64(weight) * x;
   }
-  s1 %= kAdlerMod;
-  s2 %= kAdlerMod;
-  for (u32 o = 16; o; o >>= 1) {
-    s1 += __shfl_xor_sync(kFullMask, s1, o);
-    s2 += __shfl_xor_sync(kFullMask, s2, o);
+  __device__ __forceinline__ void reduce() {
+    s1 %= kAdlerMod;
+    s2 %= kAdlerMod;
   }
-  return adler_finish(s1, s2, n);
+};
+
+__device__ __forceinline__ void add_word(AdlerLane& a, u32 w, u32 weight) {
+  // Four bytes at positions with weights weight, weight-1, weight-2, weight-3.
+  const u32 b0 = w & 255u, b1 = (w >> 8) & 255u, b2 = (w >> 16) & 255u, b3 = w >> 24;
+  const u32 sum = b0 + b1 + b2 + b3;
+  a.s1 += sum;
+  a.s2 += u64(weight) * sum - (b1 + 2 * b2 + 3 * b3);
+}
+
+// Copy output [from, to) from the ring to global memory with the whole warp,
+// adding every byte to the lanes' Adler sums.  16-byte vectors when `out` is
+// 16-byte aligned; bytes at the ragged ends.
+__device__ void warp_flush(const u8* ring, u8* out, u32 from, u32 to, u32 n, AdlerLane& adler,
+                           bool vec) {
+  const u32 lane = threadIdx.x & 31u;
+  if (from >= to) return;
+  u32 head_end = to, tail_start = to;
+  if (vec) {
+    head_end = min_u32(to, (from + 15) & ~15u);
+    tail_start = head_end + ((to - head_end) & ~15u);
+  }
+  for (u32 p = from + lane; p < head_end; p += 32) {
+    const u8 b = ring[p & kRingMask];
+    out[p] = b;
+    adler.add(b, n - p);
+  }
+  for (u32 p = head_end + 16 * lane; p < tail_start; p += 512) {
+    const uint4 v = *reinterpret_cast<const uint4*>(ring + (p & kRingMask));
+    *reinterpret_cast<uint4*>(out + p) = v;
+    add_word(adler, v.x, n - p);
+    add_word(adler, v.y, n - p - 4);
+    add_word(adler, v.z, n - p - 8);
+    add_word(adler, v.w, n - p - 12);
+  }
+  for (u32 p = tail_start + lane; p < to; p += 32) {
+    const u8 b = ring[p & kRingMask];
+    out[p] = b;
+    adler.add(b, n - p);
+  }
+  adler.reduce();
 }
 
 __device__ void warp_fill_zero(u8* out, u64 n) {
@@ -62,23 +92,31 @@ __device__ void warp_fill_zero(u8* out, u64 n) {
 }
 
 // Decode one stream.  All 32 lanes call; returns the status on every lane.
-__device__ u32 warp_inflate_one(const u8* in, u64 in_size, u8* out, u64 out_size, u32 max_blocks,
-                                const Tables& fixed, Tables& dyn, u8* ring) {
+// Output bytes are staged in `ring` and flushed by the warp; `produced -
+// flushed` stays below kFlushBytes + 258, so every byte older than the ring
+// is already in global memory when a far match reads it.
+__device__ u32 warp_inflate_one(const u8* in, u64 in_size64, u8* out, u64 out_size64,
+                                u32 max_blocks, const Tables& fixed, Tables& dyn, u8* ring) {
   const u32 lane = threadIdx.x & 31u;
-  if (in_size > kMaxBytes || out_size > kMaxBytes || !max_blocks || max_blocks > kMaxBlocks)
+  if (in_size64 > kMaxBytes || out_size64 > kMaxBytes || !max_blocks || max_blocks > kMaxBlocks)
     return kInvalidBounds;
+  const u32 in_size = u32(in_size64), out_size = u32(out_size64);
   u32 window = 0, wanted = 0;
   u32 error = zlib_framing(in, in_size, &window, &wanted);
-  BitCursor c;
-  u64 produced = 0;
-  u32 blocks = 0, final = 0;
+  Bits c;
+  u32 produced = 0, flushed = 0, blocks = 0, final = 0, full_words = 0;
   bool need_header = true, complete = false, use_dyn = false;
-  if (!error && lane == 0) c.init(in + 2, in_size - 6, 0);
+  AdlerLane adler;
+  const bool vec = (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
+  if (!error && lane == 0) {
+    c.init(in + 2, in_size - 6);
+    full_words = (c.shift + c.end) >> 5;
+  }
   while (!error) {
-    u32 action = kNone, len = 0, dist = 0;
-    u64 src = 0, dst = 0;
+    u32 action = kNone, len = 0, dist = 0, src = 0, dst = 0;
     if (lane == 0) {
       while (!complete) {
+        if (produced - flushed >= kFlushBytes) { action = kFlush; break; }
         if (need_header) {
           if (blocks >= max_blocks) { error = kBlockLimit; break; }
           ++blocks;
@@ -87,18 +125,19 @@ __device__ u32 warp_inflate_one(const u8* in, u64 in_size, u8* out, u64 out_size
           if (error) break;
           if (type == 3) { error = kReservedType; break; }
           if (type == 0) {
-            c.seek((c.pos + 7) & ~7ull);
+            c.seek((c.pos() + 7) & ~7u);
             const u32 n = c.take(16, &error), comp = c.take(16, &error);
             if (error) break;
             if ((n ^ comp) != 0xffffu) { error = kBadSymbol; break; }
             if (n > out_size - produced) { error = kOutputOverflow; break; }
-            if (c.pos > c.end || u64(n) * 8 > c.end - c.pos) { error = kTruncated; break; }
+            const u32 at = c.pos();
+            if (at > c.end || n * 8 > c.end - at) { error = kTruncated; break; }
             action = kStored;
-            src = 2 + (c.pos >> 3);
+            src = 2 + (at >> 3);
             dst = produced;
             len = n;
             produced += n;
-            c.seek(c.pos + u64(n) * 8);
+            c.seek(at + n * 8);
             complete = final != 0;
             break;
           }
@@ -106,10 +145,64 @@ __device__ u32 warp_inflate_one(const u8* in, u64 in_size, u8* out, u64 out_size
           use_dyn = false;
           need_header = false;
         }
-        const Token tok = decode_token(c, use_dyn ? dyn : fixed);
+        const Tables& t = use_dyn ? dyn : fixed;
+        // Fast loop: every bit it reads lies inside the body and every token
+        // fits the output, so only history and table kinds are checked.
+        // Anything unusual goes to the exact path below, unconsumed.
+        while (c.idx + 2 <= full_words && produced + 258 <= out_size &&
+               produced - flushed < kFlushBytes) {
+          c.refill_fast();
+          const u32 v = u32(c.buf);
+          const u32 e = t.ll.lut[v & 1023u];
+          const u32 kind = entry_kind(e);
+          if (kind == kLiteral) {
+            c.consume(entry_len(e));
+            ring[produced & kRingMask] = u8(entry_value(e));
+            ++produced;
+            continue;
+          }
+          if (kind != kLength) break;
+          const u64 saved_buf = c.buf;
+          const u32 saved_bits = c.nbits, saved_idx = c.idx;
+          const u32 L = entry_len(e), E = entry_extra(e);
+          const u32 length = entry_value(e) + ((v >> L) & ((1u << E) - 1u));
+          c.consume(L + E);
+          c.refill_fast();
+          const u32 w = u32(c.buf);
+          const u32 d = t.d.lut[w & 255u];
+          const u32 Ld = entry_len(d), Ed = entry_extra(d);
+          const u32 span = entry_value(d) + ((w >> Ld) & ((1u << Ed) - 1u));
+          if (entry_kind(d) != kLiteral || span > window || span > produced) {
+            c.buf = saved_buf;
+            c.nbits = saved_bits;
+            c.idx = saved_idx;
+            break;
+          }
+          c.consume(Ld + Ed);
+          if (length >= 32) {
+            action = kCopy;
+            dst = produced;
+            len = length;
+            dist = span;
+            produced += length;
+            break;
+          }
+          const u32 from = produced - span;
+          if (span <= kRing) {
+            for (u32 j = 0; j < length; ++j)
+              ring[(produced + j) & kRingMask] = ring[(from + j) & kRingMask];
+          } else {
+            for (u32 j = 0; j < length; ++j) ring[(produced + j) & kRingMask] = out[from + j];
+          }
+          produced += length;
+        }
+        if (action != kNone) break;
+        if (produced - flushed >= kFlushBytes) continue;
+        // Exact path: one token with the serial route's checks and order
+        // (DecodeOneFile, batch_decode.cuh:230-283).
+        const Token tok = take_token(c, t);
         if (tok.kind == kTokError) { error = tok.error; break; }
         if (tok.kind == kTokMatch && tok.dist > window) { error = kBadDistance; break; }
-        c.skip(tok.bits);
         if (tok.kind == kTokEnd) {
           complete = final != 0;
           need_header = true;
@@ -117,9 +210,7 @@ __device__ u32 warp_inflate_one(const u8* in, u64 in_size, u8* out, u64 out_size
         }
         if (tok.kind == kTokLiteral) {
           if (produced >= out_size) { error = kOutputOverflow; break; }
-          const u8 b = u8(tok.value);
-          out[produced] = b;
-          ring[produced & kRingMask] = b;
+          ring[produced & kRingMask] = u8(tok.value);
           ++produced;
           continue;
         }
@@ -133,19 +224,12 @@ __device__ u32 warp_inflate_one(const u8* in, u64 in_size, u8* out, u64 out_size
           produced += tok.length;
           break;
         }
-        const u64 from = produced - tok.dist;
+        const u32 from = produced - tok.dist;
         if (tok.dist <= kRing) {
-          for (u32 j = 0; j < tok.length; ++j) {
-            const u8 b = ring[(from + j) & kRingMask];
-            ring[(produced + j) & kRingMask] = b;
-            out[produced + j] = b;
-          }
+          for (u32 j = 0; j < tok.length; ++j)
+            ring[(produced + j) & kRingMask] = ring[(from + j) & kRingMask];
         } else {
-          for (u32 j = 0; j < tok.length; ++j) {
-            const u8 b = out[from + j];
-            ring[(produced + j) & kRingMask] = b;
-            out[produced + j] = b;
-          }
+          for (u32 j = 0; j < tok.length; ++j) ring[(produced + j) & kRingMask] = out[from + j];
         }
         produced += tok.length;
       }
@@ -153,50 +237,64 @@ __device__ u32 warp_inflate_one(const u8* in, u64 in_size, u8* out, u64 out_size
     error = __shfl_sync(kFullMask, error, 0);
     if (error) break;
     action = __shfl_sync(kFullMask, action, 0);
+    const u32 now = __shfl_sync(kFullMask, produced, 0);
     const bool done = __shfl_sync(kFullMask, complete ? 1u : 0u, 0) != 0;
     if (action == kDynamic) {
       const u32 st = warp_dynamic_header(c, dyn);
       if (st) { error = st; break; }
       if (lane == 0) { use_dyn = true; need_header = false; }
-    } else if (action != kNone) {
+    } else if (action == kFlush) {
+      const u32 to = now & ~15u;
+      warp_flush(ring, out, flushed, to, out_size, adler, vec);
+      flushed = to;
+    } else if (action == kStored) {
       len = __shfl_sync(kFullMask, len, 0);
       src = __shfl_sync(kFullMask, src, 0);
       dst = __shfl_sync(kFullMask, dst, 0);
-      if (action == kStored) {
-        for (u32 j = lane; j < len; j += 32) {
-          const u8 b = in[src + j];
-          out[dst + j] = b;
-          ring[(dst + j) & kRingMask] = b;
-        }
-      } else {
-        dist = __shfl_sync(kFullMask, dist, 0);
-        // Only the dist-byte seed before dst is read, so lanes never read a
-        // byte another lane writes in this copy.  Near-ring distances read
-        // global memory so no ring slot is overwritten before it is read.
-        const u64 first = dst - dist;
-        const bool from_ring = dist + 258 <= kRing;
-        u32 s = lane % dist;
-        const u32 step = 32 % dist;
-        for (u32 j = lane; j < len; j += 32) {
-          const u8 b = from_ring ? ring[(first + s) & kRingMask] : out[first + s];
-          out[dst + j] = b;
-          ring[(dst + j) & kRingMask] = b;
-          s += step;
-          if (s >= dist) s -= dist;
-        }
+      warp_flush(ring, out, flushed, dst, out_size, adler, vec);
+      for (u32 j = lane; j < len; j += 32) {
+        const u8 b = in[src + j];
+        out[dst + j] = b;
+        ring[(dst + j) & kRingMask] = b;
+        adler.add(b, out_size - (dst + j));
+      }
+      adler.reduce();
+      flushed = dst + len;
+    } else if (action == kCopy) {
+      len = __shfl_sync(kFullMask, len, 0);
+      dst = __shfl_sync(kFullMask, dst, 0);
+      dist = __shfl_sync(kFullMask, dist, 0);
+      // Only the dist-byte seed before dst is read, so lanes never read a
+      // byte another lane writes in this copy.  Near-ring distances read the
+      // flushed global copy, so no ring slot is overwritten before it is read.
+      const u32 first = dst - dist;
+      const bool from_ring = dist + 258 <= kRing;
+      u32 s = lane % dist;
+      const u32 step = 32 % dist;
+      for (u32 j = lane; j < len; j += 32) {
+        const u8 b = from_ring ? ring[(first + s) & kRingMask] : out[first + s];
+        ring[(dst + j) & kRingMask] = b;
+        s += step;
+        if (s >= dist) s -= dist;
       }
     }
     __syncwarp();
     if (done) break;
   }
-  if (!error && lane == 0) {
-    if (produced != out_size) error = kSizeMismatch;
-    else if ((c.pos + 7) / 8 != in_size - 6) error = kExtentMismatch;
-  }
-  error = __shfl_sync(kFullMask, error, 0);
   if (!error) {
-    __syncwarp();
-    if (warp_adler(out, out_size) != wanted) error = kAdlerMismatch;
+    const u32 end_bits = __shfl_sync(kFullMask, c.pos(), 0);
+    const u32 total = __shfl_sync(kFullMask, produced, 0);
+    if (total != out_size) error = kSizeMismatch;
+    else if ((end_bits + 7) / 8 != in_size - 6) error = kExtentMismatch;
+  }
+  if (!error) {
+    warp_flush(ring, out, flushed, out_size, out_size, adler, vec);
+    u64 s1 = adler.s1, s2 = adler.s2;
+    for (u32 o = 16; o; o >>= 1) {
+      s1 += __shfl_xor_sync(kFullMask, s1, o);
+      s2 += __shfl_xor_sync(kFullMask, s2, o);
+    }
+    if (adler_finish(s1, s2, out_size) != wanted) error = kAdlerMismatch;
   }
   return error;
 }
@@ -259,8 +357,10 @@ cudaError_t launch_serial_inflate(const u8* in, u8* out, const StreamDesc* descs
   const u32 needed = (count + kSerialWarps - 1) / kSerialWarps;
   if (grid > needed) grid = needed;
   if (grid < 1) grid = 1;
+  profile_begin("serial_inflate_kernel", stream);
   serial_inflate_kernel<<<grid, kSerialWarps * 32, smem, stream>>>(
       in, out, descs, single, count, order, next, meta, encoded, max_blocks);
+  profile_end(stream);
   return cudaGetLastError();
 }
 

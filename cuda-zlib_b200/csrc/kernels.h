@@ -18,12 +18,19 @@ struct StreamDesc {
   u64 in_offset, in_size, out_offset, out_size;
 };
 
+// Opt-in kernel timing (cuda_zlib_b200_profile): when enabled, launchers
+// bracket their kernels with CUDA events on the launching stream.  No-ops
+// otherwise.  begin/end pairs must come from the same host thread.
+void profile_begin(const char* kernel, cudaStream_t stream);
+void profile_end(cudaStream_t stream);
+
 // Per-device launch facts, filled once per device by the host layer.
 struct DeviceInfo {
   int device;
   int sms;
   int serial_per_sm;    // resident CTAs of the warp-per-stream inflate kernel
   int encode_smem_limit;  // dynamic shared memory available to the chunk encoder
+  int emit_per_sm;        // resident CTAs of the block-parallel emit kernel
 };
 
 // One file of an encode call.  Chunks of all files are numbered
@@ -56,6 +63,38 @@ cudaError_t launch_encode(const u8* in, const EncodeFile* files, u32 nfiles, u32
                           u32 total_chunks, u8* slots, u32* sizes, u32* status, u64* adler,
                           u64* offsets, u16* spill_prev, u8* spill_len, u8* out, u32* meta,
                           const DeviceInfo& dev, cudaStream_t stream);
+
+// Block-parallel inflate of one large stream (inflate_parallel.cu).
+struct ParallelScratch {
+  u64 bitmap_words;   // candidate bitmap words (one bit per body bit offset)
+  u32 compact_blocks; // CTAs of the candidate compaction
+  u32 capacity;       // candidate capacity = min(max_candidates, 9 * body + 1)
+  u32 levels;         // pointer-doubling levels over capacity + 2 nodes
+  u64 out_words;      // unresolved-position bitmap words
+  u32 segments;       // Adler-32 segments of the output
+};
+struct ParallelBuffers {
+  u32* bitmap;        // bitmap_words, from discover_kernel
+  u32* block_counts;  // compact_blocks
+  u32* total;         // 1: distinct candidates
+  u32* cands;         // capacity
+  u32 *ends, *sizes, *blocks, *infos;  // capacity each
+  u32* jump;          // (capacity + 2) * levels
+  u32 *path, *prefix; // capacity each
+  u32* state;         // 2: path length, chain ok
+  u32* counters;      // 2, zeroed: describe / emit work counters
+  u32* source;        // expected: absolute source of unresolved positions
+  u32* unresolved;    // out_words, zeroed
+  u64* parts;         // 2 * segments
+  u32* fail;          // 1, zeroed
+};
+ParallelScratch parallel_scratch_layout(u64 in_size, u64 expected, u32 capacity);
+cudaError_t configure_parallel_inflate(int* emit_per_sm);
+// Writes the fast-path verdict to meta[0]: 0 ok, 21 checksum, 1 other failure.
+cudaError_t launch_parallel_inflate(const u8* in, u64 in_size, u8* out, u64 expected,
+                                    u32 max_blocks, const ParallelScratch& s,
+                                    const ParallelBuffers& b, u32* meta, const DeviceInfo& dev,
+                                    cudaStream_t stream);
 
 // General-route status path (single streams outside the small route).
 // bitmap: one bit per body bit offset, zeroed; count: zeroed u32.
