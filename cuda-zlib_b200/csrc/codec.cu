@@ -68,6 +68,9 @@ cudaError_t device_state(int device, DeviceState** out) {
     CZ_TRY(configure_serial_inflate(&info.serial_per_sm));
     CZ_TRY(configure_encode(&info.encode_smem_limit));
     CZ_TRY(configure_parallel_inflate(&info.emit_per_sm));
+    void* fixed = nullptr;
+    CZ_TRY(build_fixed_tables(&fixed));
+    info.fixed_tables = fixed;
     cudaMemPoolProps props{};
     props.allocType = cudaMemAllocationTypePinned;
     props.handleTypes = cudaMemHandleTypeNone;

@@ -23,8 +23,10 @@ namespace cz {
 // ---------------------------------------------------------------------------
 // Candidate discovery
 // ---------------------------------------------------------------------------
-// Validity of a dynamic header at `start` (BTYPE 2 and dynamic_tables()==0);
-// per-thread, no tables kept (dynamic_valid, _decode_kernels.py:359-366).
+// Validity of a dynamic header at `start` (BTYPE 2 and dynamic_tables()==0;
+// dynamic_valid, _decode_kernels.py:359-366), per thread and without tables:
+// the code lengths are checked as they are decoded, so a random bit pattern
+// is usually rejected after a few symbols (an over-subscribed code).
 __device__ bool dynamic_header_valid(const u8* body, u64 bytes, u64 start) {
   BitCursor c;
   c.init(body, bytes, start);
@@ -61,8 +63,11 @@ __device__ bool dynamic_header_valid(const u8* body, u64 bytes, u64 start) {
     for (u32 i = 0; i < 19; ++i)
       if (clens[i]) sorted[cursor[clens[i]]++] = u8(i);
   }
-  u8 lens[320];
-  u32 i = 0;
+  // Literal/length lengths i < nl, distance lengths after; per part the
+  // Kraft sum (units of 2^-15), nonzero count and maximum.
+  u32 ksum[2] = {0, 0}, nonzero[2] = {0, 0}, maxlen[2] = {0, 0};
+  u32 i = 0, previous = 0;
+  bool eob = false;
   while (i < nl + nd) {
     u32 code = 0, sym = 0xffffffffu;
     for (u32 l = 1; l < 8; ++l) {
@@ -71,45 +76,42 @@ __device__ bool dynamic_header_valid(const u8* body, u64 bytes, u64 start) {
       if (code - first[l] < count[l]) { sym = sorted[offs[l] + code - first[l]]; break; }
     }
     if (sym == 0xffffffffu) return false;
-    if (sym < 16) { lens[i++] = u8(sym); continue; }
-    u32 repeat, value;
+    u32 repeat = 1, value = sym;
     if (sym == 16) {
       if (!i) return false;
       repeat = c.take(2, &err) + 3;
-      value = lens[i - 1];
+      value = previous;
     } else if (sym == 17) {
       repeat = c.take(3, &err) + 3;
       value = 0;
-    } else {
+    } else if (sym == 18) {
       repeat = c.take(7, &err) + 11;
       value = 0;
     }
     if (err || repeat > nl + nd - i) return false;
-    for (u32 j = 0; j < repeat; ++j) lens[i++] = u8(value);
-  }
-  if (!lens[256]) return false;
-  // Literal/length: nonempty; complete, or a single length-1 code.
-  // Distance: may be empty; otherwise the same rule.
-  for (u32 part = 0; part < 2; ++part) {
-    const u32 from = part ? nl : 0, n = part ? nd : nl;
-    u32 cnt[16];
-    for (u32 l = 0; l < 16; ++l) cnt[l] = 0;
-    u32 maximum = 0;
-    for (u32 k = 0; k < n; ++k) {
-      const u32 l = lens[from + k];
-      ++cnt[l];
-      if (l > maximum) maximum = l;
+    if (value) {
+      for (u32 j = 0; j < repeat; ++j, ++i) {
+        const u32 part = i < nl ? 0u : 1u;
+        ksum[part] += 32768u >> value;
+        ++nonzero[part];
+        if (value > maxlen[part]) maxlen[part] = value;
+        if (ksum[part] > 32768u) return false;  // over-subscribed
+        if (i == 256) eob = true;
+      }
+    } else {
+      i += repeat;
     }
-    if (!maximum) {
+    previous = value;
+  }
+  if (!eob) return false;
+  // Literal/length: complete, or a single length-1 code.  Distance: empty,
+  // complete, or a single length-1 code.
+  for (u32 part = 0; part < 2; ++part) {
+    if (!nonzero[part]) {
       if (part == 0) return false;
       continue;
     }
-    int left = 1;
-    for (u32 l = 1; l < 16; ++l) {
-      left = (left << 1) - int(cnt[l]);
-      if (left < 0) return false;
-    }
-    if (left && !(maximum == 1 && cnt[1] == 1)) return false;
+    if (ksum[part] != 32768u && !(maxlen[part] == 1 && nonzero[part] == 1)) return false;
   }
   return true;
 }
@@ -132,37 +134,90 @@ __device__ bool stored_seed(const u8* body, u64 bytes, u64 byte, u64* endpoint) 
   return true;
 }
 
-// One thread per body byte: eight bit offsets plus the stored seed.  Sets
-// candidate bits (bit offset b -> bitmap[b >> 5] bit b & 31) and adds the raw
-// event count.  Skipped when `gate` (framing status) is nonzero.
-__global__ void discover_kernel(const u8* in, u64 in_size, u32* bitmap, u32* count,
-                                const u32* gate) {
+constexpr u32 kDiscoverTile = 4096;     // body bytes per CTA step
+constexpr u32 kDiscoverThreads = 256;   // each thread scans 16 consecutive bytes
+
+// Candidates of every body bit offset (discover, _decode_kernels.py:
+// 998-1054): bit 0; offsets whose three header bits are BTYPE 2 and whose
+// dynamic header is valid; stored-block endpoint seeds.  Sets bit b of
+// bitmap[b >> 5] per candidate offset and adds the raw event count
+// (duplicates included).  The tile and a 16-byte halo are staged in shared
+// memory; each byte's eight offsets share one 128-bit register window, and
+// the code-length code's completeness is prefiltered with a table of
+// Kraft sums of three packed 3-bit lengths before full validation.
+__global__ void __launch_bounds__(kDiscoverThreads)
+discover_kernel(const u8* in, u64 in_size, u32* bitmap, u32* count, const u32* gate) {
+  __shared__ __align__(16) u8 tile[kDiscoverTile + 32];
+  __shared__ u8 kraft3[512];
   if (gate && *gate) return;
   if (in_size < 8) return;
   const u8* body = in + 2;
   const u64 bytes = in_size - 6;
+  for (u32 t = threadIdx.x; t < 512; t += blockDim.x) {
+    u32 sum = 0;
+    for (u32 k = 0; k < 3; ++k) {
+      const u32 L = (t >> (3 * k)) & 7u;
+      sum += L ? (128u >> L) : 0u;
+    }
+    kraft3[t] = u8(sum);
+  }
   u32 events = 0;
-  const u64 stride = u64(gridDim.x) * blockDim.x;
-  for (u64 byte = u64(blockIdx.x) * blockDim.x + threadIdx.x; byte < bytes; byte += stride) {
-    u64 e;
-    if (stored_seed(body, bytes, byte, &e)) {
-      ++events;
-      atomicOr(&bitmap[(e * 8) >> 5], 1u << ((e * 8) & 31));
+  for (u64 base = u64(blockIdx.x) * kDiscoverTile; base < bytes;
+       base += u64(gridDim.x) * kDiscoverTile) {
+    __syncthreads();
+    for (u32 j = threadIdx.x; j < kDiscoverTile + 32; j += blockDim.x)
+      tile[j] = base + j < bytes ? body[base + j] : u8(0);
+    __syncthreads();
+    const u32 j0 = threadIdx.x * 16;
+    // 128-bit window of the 16 bytes starting at byte j0 + k.
+    u64 lo = 0, hi = 0;
+    for (u32 k = 0; k < 8; ++k) lo |= u64(tile[j0 + k]) << (8 * k);
+    for (u32 k = 0; k < 8; ++k) hi |= u64(tile[j0 + 8 + k]) << (8 * k);
+    u32 word_bits[4] = {0, 0, 0, 0};
+    for (u32 k = 0; k < 16; ++k) {
+      const u64 byte = base + j0 + k;
+      if (byte < bytes) {
+        // Stored seed: LEN/NLEN complements at this byte.
+        if ((((lo >> 16) ^ lo) & 0xffffu) == 0xffffu) {
+          u64 e;
+          if (stored_seed(body, bytes, byte, &e)) {
+            ++events;
+            atomicOr(&bitmap[(e * 8) >> 5], 1u << ((e * 8) & 31));
+          }
+        }
+        // BTYPE 2 at offset b: bit b+1 clear, bit b+2 set.
+        u32 mask = u32((~lo >> 1) & (lo >> 2)) & 0xffu;
+        u32 valid = byte == 0 ? 1u : 0u;
+        if (byte == 0) mask &= ~1u;
+        while (mask) {
+          const u32 b = __ffs(mask) - 1;
+          mask &= mask - 1;
+          const u64 x = (lo >> (b + 3)) | (hi << (61 - b));          // from HLIT
+          if ((x & 31u) > 29u) continue;
+          const u32 nc = u32((x >> 10) & 15u) + 4;
+          const u32 s = b + 17;
+          u64 y = (lo >> s) | (hi << (64 - s));                       // CL lengths
+          u32 kraft = 0;
+          for (u32 i = 0; i < nc && kraft <= 128; i += 3) {
+            u32 packed = u32(y) & 511u;
+            const u32 left = nc - i;
+            if (left < 3) packed &= (1u << (3 * left)) - 1u;
+            kraft += kraft3[packed];
+            y >>= 9;
+          }
+          if (kraft != 128) continue;
+          if (dynamic_header_valid(body, bytes, byte * 8 + b)) valid |= 1u << b;
+        }
+        if (valid) {
+          events += __popc(valid);
+          word_bits[k >> 2] |= valid << ((k & 3) * 8);
+        }
+      }
+      lo = (lo >> 8) | (hi << 56);
+      hi = (hi >> 8) | (u64(tile[j0 + 16 + k]) << 56);
     }
-    // Cheap prefilter on the three header bits of each offset: BTYPE must be
-    // 2 (bits 1-2 of the offset), except bit offset 0 which always counts.
-    const u32 w = u32(body[byte]) | (byte + 1 < bytes ? u32(body[byte + 1]) << 8 : 0u);
-    u32 mask = 0;
-    for (u32 bit = 0; bit < 8; ++bit) {
-      const u64 start = byte * 8 + bit;
-      bool valid = start == 0;
-      if (!valid && ((w >> (bit + 1)) & 3u) == 2u) valid = dynamic_header_valid(body, bytes, start);
-      if (valid) mask |= 1u << bit;
-    }
-    if (mask) {
-      events += __popc(mask);
-      atomicOr(&bitmap[(byte * 8) >> 5], mask << ((byte * 8) & 31));
-    }
+    for (u32 w = 0; w < 4; ++w)
+      if (word_bits[w]) atomicOr(&bitmap[((base + j0) * 8 >> 5) + w], word_bits[w]);
   }
   for (u32 o = 16; o; o >>= 1) events += __shfl_xor_sync(kFullMask, events, o);
   if ((threadIdx.x & 31) == 0 && events) atomicAdd(count, events);
@@ -518,12 +573,12 @@ cudaError_t launch_discover(const u8* in, u64 in_size, u32* bitmap, u32* count, 
                             const DeviceInfo& dev, cudaStream_t stream) {
   if (in_size < 8) return cudaSuccess;
   const u64 bytes = in_size - 6;
-  u64 blocks = (bytes + 255) / 256;
-  const u64 cap = u64(dev.sms) * 16;
+  u64 blocks = (bytes + kDiscoverTile - 1) / kDiscoverTile;
+  const u64 cap = u64(dev.sms) * 8;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
   profile_begin("discover_kernel", stream);
-  discover_kernel<<<u32(blocks), 256, 0, stream>>>(in, in_size, bitmap, count, gate);
+  discover_kernel<<<u32(blocks), kDiscoverThreads, 0, stream>>>(in, in_size, bitmap, count, gate);
   profile_end(stream);
   return cudaGetLastError();
 }

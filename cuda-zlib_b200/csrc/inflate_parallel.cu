@@ -38,17 +38,15 @@
 namespace cz {
 
 constexpr u32 kNodeWarps = 4;      // warps per CTA in describe/emit
-constexpr u32 kEmitRing = 8192;    // u16 history entries per emitting warp
+constexpr u32 kEmitRing = 4096;    // u16 history entries per emitting warp
 constexpr u32 kEmitMask = kEmitRing - 1;
 constexpr u32 kEmitFlush = 2048;   // pending symbols that trigger a flush
 constexpr u32 kInfoFinal = 1u, kInfoOk = 2u;
 
 struct DescribeShared {
-  Tables fixed;
   Tables dyn[kNodeWarps];
 };
 struct EmitShared {
-  Tables fixed;
   Tables dyn[kNodeWarps];
   __align__(16) u16 ring[kNodeWarps][kEmitRing];
 };
@@ -228,8 +226,12 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
           need_header = false;
         }
         const Tables& t = use_dyn ? dyn : fixed;
-        while (c.idx + 2 <= full_words && produced + 258 <= limit &&
-               (!kEmit || produced - flushed < kEmitFlush)) {
+        // One bound for the fast loop: room for a maximal match and, when
+        // emitting, a flush before the ring can wrap onto unflushed symbols.
+        u32 stop_at = limit >= 258 ? limit - 258 : 0;
+        if (kEmit) stop_at = min_u32(stop_at, flushed + kEmitFlush);
+        const u32 idx_limit = full_words >= 2 ? full_words - 1 : 0;
+        while (c.idx < idx_limit && produced < stop_at) {
           c.refill_fast();
           const u32 v = u32(c.buf);
           const u32 e = t.ll.lut[v & 1023u];
@@ -268,13 +270,18 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
               produced += length;
               break;
             }
-            for (u32 j = 0; j < length; ++j) {
-              const u32 p = produced + j;
-              u32 sym;
-              if (span > p) sym = 256 + (span - p - 1);
-              else if (span + 258 <= kEmitRing) sym = ring[(p - span) & kEmitMask];
-              else sym = flushed_symbol(out, source, unresolved, prefix, p - span);
-              ring[p & kEmitMask] = u16(sym);
+            if (span <= produced && span + 258 <= kEmitRing) {
+              for (u32 j = 0; j < length; ++j)
+                ring[(produced + j) & kEmitMask] = ring[(produced + j - span) & kEmitMask];
+            } else {
+              for (u32 j = 0; j < length; ++j) {
+                const u32 p = produced + j;
+                u32 sym;
+                if (span > p) sym = 256 + (span - p - 1);
+                else if (span + 258 <= kEmitRing) sym = ring[(p - span) & kEmitMask];
+                else sym = flushed_symbol(out, source, unresolved, prefix, p - span);
+                ring[p & kEmitMask] = u16(sym);
+              }
             }
           }
           produced += length;
@@ -376,21 +383,20 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
 // Describe every candidate (warp per candidate, work stealing).
 __global__ void __launch_bounds__(kNodeWarps * 32)
 describe_kernel(const u8* in, u32 in_size, u64 expected, const u32* cands, const u32* total,
-                u32 capacity, u32* next_item, u32* ends, u32* sizes, u32* blocks, u32* infos) {
+                u32 capacity, u32* next_item, u32* ends, u32* sizes, u32* blocks, u32* infos,
+                const Tables* fixed) {
   __shared__ DescribeShared sh;
   const u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   u32 window = 0, wanted = 0;
   if (zlib_framing(in, in_size, &window, &wanted)) return;
   const u32 count = min_u32(*total, capacity);
-  if (warp == 0) warp_build_fixed(sh.fixed);
-  __syncthreads();
   for (;;) {
     u32 item = 0;
     if (lane == 0) item = atomicAdd(next_item, 1u);
     item = __shfl_sync(kFullMask, item, 0);
     if (item >= count) break;
     const NodeResult r = warp_node<false>(in + 2, in_size - 6, cands[item], u32(expected), window,
-                                          sh.fixed, sh.dyn[warp], nullptr, nullptr, nullptr,
+                                          *fixed, sh.dyn[warp], nullptr, nullptr, nullptr,
                                           nullptr, 0);
     if (lane == 0) {
       ends[item] = r.end;
@@ -513,7 +519,7 @@ chain_kernel(const u8* in, u32 in_size, u64 expected, u32 max_blocks, const u32*
 __global__ void __launch_bounds__(kNodeWarps * 32)
 emit_kernel(const u8* in, u32 in_size, u64 expected, const u32* cands, const u32* path,
             const u32* prefix, const u32* sizes, const u32* state, u32* next_item, u8* out,
-            u32* source, u32* unresolved, u32* fail_flag) {
+            u32* source, u32* unresolved, u32* fail_flag, const Tables* fixed) {
   extern __shared__ __align__(16) u8 smem[];
   EmitShared& sh = *reinterpret_cast<EmitShared*>(smem);
   const u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
@@ -521,8 +527,6 @@ emit_kernel(const u8* in, u32 in_size, u64 expected, const u32* cands, const u32
   const u32 len = state[0];
   u32 window = 0, wanted = 0;
   zlib_framing(in, in_size, &window, &wanted);
-  if (warp == 0) warp_build_fixed(sh.fixed);
-  __syncthreads();
   for (;;) {
     u32 item = 0;
     if (lane == 0) item = atomicAdd(next_item, 1u);
@@ -530,7 +534,7 @@ emit_kernel(const u8* in, u32 in_size, u64 expected, const u32* cands, const u32
     if (item >= len) break;
     const u32 node = path[item];
     const NodeResult r = warp_node<true>(in + 2, in_size - 6, cands[node], u32(expected), window,
-                                         sh.fixed, sh.dyn[warp], sh.ring[warp], out, source,
+                                         *fixed, sh.dyn[warp], sh.ring[warp], out, source,
                                          unresolved, prefix[item]);
     if (lane == 0 && (!(r.info & kInfoOk) || r.size != sizes[node])) atomicOr(fail_flag, 1u);
   }
@@ -641,10 +645,24 @@ __global__ void parallel_finish_kernel(const u8* in, u32 in_size, const u32* sta
   }
 }
 
+// The fixed Huffman tables, built once per device into global memory.
+__global__ void build_fixed_kernel(Tables* fixed) { warp_build_fixed(*fixed); }
+
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
 size_t parallel_inflate_emit_smem() { return sizeof(EmitShared); }
+
+cudaError_t build_fixed_tables(void** out) {
+  Tables* fixed = nullptr;
+  cudaError_t e = cudaMalloc(&fixed, sizeof(Tables));
+  if (e != cudaSuccess) return e;
+  build_fixed_kernel<<<1, 32>>>(fixed);
+  e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return e;
+  *out = fixed;
+  return cudaSuccess;
+}
 
 cudaError_t configure_parallel_inflate(int* emit_per_sm) {
   cudaError_t e = cudaFuncSetAttribute(emit_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -686,7 +704,7 @@ cudaError_t launch_parallel_inflate(const u8* in, u64 in_size, u8* out, u64 expe
   profile_begin("describe_kernel", stream);
   describe_kernel<<<node_grid, kNodeWarps * 32, 0, stream>>>(
       in, u32(in_size), expected, b.cands, b.total, s.capacity, b.counters, b.ends, b.sizes,
-      b.blocks, b.infos);
+      b.blocks, b.infos, static_cast<const Tables*>(dev.fixed_tables));
   profile_end(stream);
   chain_kernel<<<1, 1024, 0, stream>>>(in, u32(in_size), expected, max_blocks, b.cands, b.total,
                                        s.capacity, b.ends, b.sizes, b.blocks, b.infos, b.jump,
@@ -696,7 +714,7 @@ cudaError_t launch_parallel_inflate(const u8* in, u64 in_size, u8* out, u64 expe
   profile_begin("emit_kernel", stream);
   emit_kernel<<<emit_grid, kNodeWarps * 32, sizeof(EmitShared), stream>>>(
       in, u32(in_size), expected, b.cands, b.path, b.prefix, b.sizes, b.state, b.counters + 1,
-      out, b.source, b.unresolved, b.fail);
+      out, b.source, b.unresolved, b.fail, static_cast<const Tables*>(dev.fixed_tables));
   profile_end(stream);
   resolve_kernel<<<u32(dev.sms) * 8, 256, 0, stream>>>(b.state, u32(s.out_words), b.unresolved,
                                                        b.source, out);

@@ -26,7 +26,6 @@ constexpr u32 kRingMask = kRing - 1;
 constexpr u32 kFlushBytes = 2048; // produced bytes that trigger a warp flush
 
 struct SerialShared {
-  Tables fixed;
   Tables dyn[kSerialWarps];
   __align__(16) u8 ring[kSerialWarps][kRing];
 };
@@ -149,8 +148,10 @@ __device__ u32 warp_inflate_one(const u8* in, u64 in_size64, u8* out, u64 out_si
         // Fast loop: every bit it reads lies inside the body and every token
         // fits the output, so only history and table kinds are checked.
         // Anything unusual goes to the exact path below, unconsumed.
-        while (c.idx + 2 <= full_words && produced + 258 <= out_size &&
-               produced - flushed < kFlushBytes) {
+        const u32 stop_at =
+            min_u32(out_size >= 258 ? out_size - 258 : 0, flushed + kFlushBytes);
+        const u32 idx_limit = full_words >= 2 ? full_words - 1 : 0;
+        while (c.idx < idx_limit && produced < stop_at) {
           c.refill_fast();
           const u32 v = u32(c.buf);
           const u32 e = t.ll.lut[v & 1023u];
@@ -302,12 +303,10 @@ __device__ u32 warp_inflate_one(const u8* in, u64 in_size64, u8* out, u64 out_si
 __global__ void __launch_bounds__(kSerialWarps * 32)
 serial_inflate_kernel(const u8* in, u8* out, const StreamDesc* descs, StreamDesc single,
                       u32 count, const u32* order, u32* next, u32* meta, const u32* encoded,
-                      u32 max_blocks) {
+                      u32 max_blocks, const Tables* fixed) {
   extern __shared__ __align__(16) u8 smem_raw[];
   SerialShared& sh = *reinterpret_cast<SerialShared*>(smem_raw);
   const u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-  if (warp == 0) warp_build_fixed(sh.fixed);
-  __syncthreads();
   for (;;) {
     u32 item = 0;
     if (lane == 0) item = atomicAdd(next, 1u);
@@ -328,7 +327,7 @@ serial_inflate_kernel(const u8* in, u8* out, const StreamDesc* descs, StreamDesc
     }
     if (!status)
       status = warp_inflate_one(in + d.in_offset, in_size, out + d.out_offset, d.out_size,
-                                max_blocks, sh.fixed, sh.dyn[warp], sh.ring[warp]);
+                                max_blocks, *fixed, sh.dyn[warp], sh.ring[warp]);
     // A failed stream publishes an all-zero output.
     if (status && d.out_size <= kMaxBytes) warp_fill_zero(out + d.out_offset, d.out_size);
     if (lane == 0) {
@@ -359,7 +358,8 @@ cudaError_t launch_serial_inflate(const u8* in, u8* out, const StreamDesc* descs
   if (grid < 1) grid = 1;
   profile_begin("serial_inflate_kernel", stream);
   serial_inflate_kernel<<<grid, kSerialWarps * 32, smem, stream>>>(
-      in, out, descs, single, count, order, next, meta, encoded, max_blocks);
+      in, out, descs, single, count, order, next, meta, encoded, max_blocks,
+      static_cast<const Tables*>(dev.fixed_tables));
   profile_end(stream);
   return cudaGetLastError();
 }

@@ -31,6 +31,7 @@ struct DeviceInfo {
   int serial_per_sm;    // resident CTAs of the warp-per-stream inflate kernel
   int encode_smem_limit;  // dynamic shared memory available to the chunk encoder
   int emit_per_sm;        // resident CTAs of the block-parallel emit kernel
+  const void* fixed_tables;  // device copy of the fixed Huffman tables
 };
 
 // One file of an encode call.  Chunks of all files are numbered
@@ -89,6 +90,8 @@ struct ParallelBuffers {
   u32* fail;          // 1, zeroed
 };
 ParallelScratch parallel_scratch_layout(u64 in_size, u64 expected, u32 capacity);
+// Allocates and builds the fixed Huffman tables on the current device.
+cudaError_t build_fixed_tables(void** out);
 cudaError_t configure_parallel_inflate(int* emit_per_sm);
 // Writes the fast-path verdict to meta[0]: 0 ok, 21 checksum, 1 other failure.
 cudaError_t launch_parallel_inflate(const u8* in, u64 in_size, u8* out, u64 expected,
