@@ -7,7 +7,7 @@
 //    the stream's last byte.  A peek returns 64 bits, enough for any whole
 //    token (at most 15+5+15+13 = 48 bits), so one peek serves one token.
 //  * Huffman tables: canonical codes, built cooperatively by one warp into
-//    shared memory.  Literal/length codes use a 10-bit primary table, distance
+//    shared memory.  Literal/length codes use a 9-bit primary table, distance
 //    codes 8 bits, code-length codes a complete 7-bit table; codes longer than
 //    the primary width decode canonically from the bit-reversed window.
 //  * Token decode with the reference's exact status precedence
@@ -17,6 +17,8 @@
 //    past the end of the Deflate body is status 1, an unusable code status 4,
 //    reserved symbols status 4.
 #pragma once
+
+#include <cstddef>
 
 #include "common.cuh"
 
@@ -97,8 +99,8 @@ struct Bits {
   u32 last;          // index of the last word holding a body byte
   u32 end;           // body length in bits
   u32 idx;           // next word to load
-  u32 nbits;         // valid bits in buf
-  u64 buf;
+  u32 nbits;         // valid bits in (hi:lo)
+  u32 lo, hi;        // 64-bit accumulator; lo holds the next bits
 
   __device__ __forceinline__ u32 load(u32 i) const { return i <= last ? __ldg(words + i) : 0u; }
 
@@ -120,28 +122,35 @@ struct Bits {
     const u32 a = shift + p;
     idx = a >> 5;
     const u32 off = a & 31;
-    buf = u64(load(idx)) >> off;
+    lo = load(idx) >> off;
+    hi = 0;
     nbits = 32 - off;
     ++idx;
     refill();
   }
+  // Append one 32-bit word at bit nbits (nbits <= 32).
+  __device__ __forceinline__ void append(u32 w) {
+    lo |= w << nbits;                      // shifts of 32 give 0
+    hi |= __funnelshift_lc(w, 0u, nbits);  // high word of w << nbits
+    nbits += 32;
+  }
   __device__ __forceinline__ void refill() {
     if (nbits <= 32) {
-      buf |= u64(load(idx)) << nbits;
+      append(load(idx));
       ++idx;
-      nbits += 32;
     }
   }
-  // Unguarded refill: only while idx + 1 < last is known (fast loop).
+  // Unguarded refill: only while idx < last is known (fast loops).
   __device__ __forceinline__ void refill_fast() {
     if (nbits <= 32) {
-      buf |= u64(__ldg(words + idx)) << nbits;
+      append(__ldg(words + idx));
       ++idx;
-      nbits += 32;
     }
   }
+  // Drop n < 32 bits.
   __device__ __forceinline__ void consume(u32 n) {
-    buf >>= n;
+    lo = __funnelshift_r(lo, hi, n);
+    hi >>= n;
     nbits -= n;
   }
   // Bounded read of n <= 16 bits (BitReader::take semantics).
@@ -149,7 +158,7 @@ struct Bits {
     if (*error) return 0;
     if (n > avail()) { *error = kTruncated; return 0; }
     refill();
-    const u32 v = u32(buf) & ((1u << n) - 1u);
+    const u32 v = lo & ((1u << n) - 1u);
     consume(n);
     return v;
   }
@@ -213,7 +222,9 @@ struct Huffman {
   u32 maxlen;
 };
 
-typedef Huffman<10, 288> LLTable;
+constexpr u32 kLLBits = 9;  // literal/length primary table width
+constexpr u32 kLLMask = (1u << kLLBits) - 1u;
+typedef Huffman<kLLBits, 288> LLTable;
 typedef Huffman<8, 32> DTable;
 typedef Huffman<7, 19> CLTable;
 
@@ -352,7 +363,18 @@ __device__ inline void warp_build_fixed(Tables& t) {
 }
 
 // Rendezvous actions: lane 0 parses, then the whole warp performs one action.
-enum Action : u32 { kNone = 0, kStored = 1, kCopy = 2, kDynamic = 3, kFlush = 4 };
+enum Action : u32 { kNone = 0, kStored = 1, kCopy = 2, kDynamic = 3, kFlush = 4, kFixed = 5 };
+
+// Copy the decode part of the fixed tables (literal/length and distance)
+// into a warp's shared-memory tables, so hot loops only read shared memory.
+__device__ inline void warp_load_fixed(Tables& dst, const Tables& fixed) {
+  const u32 lane = threadIdx.x & 31u;
+  const u32* from = reinterpret_cast<const u32*>(&fixed);
+  u32* to = reinterpret_cast<u32*>(&dst);
+  const u32 words = (offsetof(Tables, cl) + 3) / 4;
+  for (u32 i = lane; i < words; i += 32) to[i] = __ldg(from + i);
+  __syncwarp();
+}
 
 // ---------------------------------------------------------------------------
 // Token decode
@@ -381,7 +403,7 @@ __device__ __forceinline__ Token decode_token(const BitCursor& c, const Tables& 
   tok.error = 0;
   const u64 v = c.peek();
   const u64 avail = c.avail();
-  u32 e = t.ll.lut[v & 1023u];
+  u32 e = t.ll.lut[v & kLLMask];
   u32 kind = entry_kind(e);
   if (kind == kLong) {
     e = decode_long(t.ll, v, LLFn());
@@ -441,8 +463,8 @@ __device__ __forceinline__ Token take_token(Bits& b, const Tables& t) {
   tok.error = 0;
   const u32 avail = b.avail();
   b.refill();
-  u32 v = u32(b.buf);
-  u32 e = t.ll.lut[v & 1023u];
+  u32 v = b.lo;
+  u32 e = t.ll.lut[v & kLLMask];
   u32 kind = entry_kind(e);
   if (kind == kLong) {
     e = decode_long(t.ll, v, LLFn());
@@ -468,7 +490,7 @@ __device__ __forceinline__ Token take_token(Bits& b, const Tables& t) {
   b.consume(L + E);
   const u32 left = avail - (L + E);
   b.refill();
-  v = u32(b.buf);
+  v = b.lo;
   u32 d = t.d.lut[v & 255u];
   u32 dk = entry_kind(d);
   if (dk == kLong) {
@@ -505,7 +527,7 @@ __device__ __forceinline__ u32 cl_symbol(BitCursor& c, const Tables& t, u32* err
 __device__ __forceinline__ u32 cl_symbol(Bits& c, const Tables& t, u32* err) {
   const u32 avail = c.avail();
   c.refill();
-  const u32 e = t.cl.lut[u32(c.buf) & 127u];
+  const u32 e = t.cl.lut[c.lo & 127u];
   if (entry_len(e) > avail) { *err = kTruncated; return 0; }
   c.consume(entry_len(e));
   return entry_value(e);

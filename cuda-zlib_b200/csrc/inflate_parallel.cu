@@ -37,7 +37,8 @@
 
 namespace cz {
 
-constexpr u32 kNodeWarps = 4;      // warps per CTA in describe/emit
+constexpr u32 kNodeWarps = 4;      // warps per CTA in describe
+constexpr u32 kEmitWarps = 1;      // warps per CTA in emit (fine-grained residency)
 constexpr u32 kEmitRing = 4096;    // u16 history entries per emitting warp
 constexpr u32 kEmitMask = kEmitRing - 1;
 constexpr u32 kEmitFlush = 2048;   // pending symbols that trigger a flush
@@ -47,8 +48,8 @@ struct DescribeShared {
   Tables dyn[kNodeWarps];
 };
 struct EmitShared {
-  Tables dyn[kNodeWarps];
-  __align__(16) u16 ring[kNodeWarps][kEmitRing];
+  Tables dyn[kEmitWarps];
+  __align__(16) u16 ring[kEmitWarps][kEmitRing];
 };
 
 // ---------------------------------------------------------------------------
@@ -179,7 +180,7 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
   Bits c;
   u32 produced = 0, flushed = 0, final = 0, blocks = 0, full_words = 0;
   u32 fail = 0, stop = 0;
-  bool need_header = true, use_dyn = false;
+  bool need_header = true;
   if (lane == 0) {
     c.init(body, bytes);
     c.seek(start);
@@ -221,11 +222,10 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
             if (kEmit) break;
             continue;
           }
-          if (type == 2) { action = kDynamic; break; }
-          use_dyn = false;
-          need_header = false;
+          action = type == 2 ? kDynamic : kFixed;
+          break;
         }
-        const Tables& t = use_dyn ? dyn : fixed;
+        const Tables& t = dyn;
         // One bound for the fast loop: room for a maximal match and, when
         // emitting, a flush before the ring can wrap onto unflushed symbols.
         u32 stop_at = limit >= 258 ? limit - 258 : 0;
@@ -233,8 +233,8 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
         const u32 idx_limit = full_words >= 2 ? full_words - 1 : 0;
         while (c.idx < idx_limit && produced < stop_at) {
           c.refill_fast();
-          const u32 v = u32(c.buf);
-          const u32 e = t.ll.lut[v & 1023u];
+          const u32 v = c.lo;
+          const u32 e = t.ll.lut[v & kLLMask];
           const u32 kind = entry_kind(e);
           if (kind == kLiteral) {
             c.consume(entry_len(e));
@@ -243,18 +243,19 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
             continue;
           }
           if (kind != kLength) break;
-          const u64 saved_buf = c.buf;
+          const u32 saved_lo = c.lo, saved_hi = c.hi;
           const u32 saved_bits = c.nbits, saved_idx = c.idx;
           const u32 L = entry_len(e), E = entry_extra(e);
           const u32 length = entry_value(e) + ((v >> L) & ((1u << E) - 1u));
           c.consume(L + E);
           c.refill_fast();
-          const u32 w = u32(c.buf);
+          const u32 w = c.lo;
           const u32 d = t.d.lut[w & 255u];
           const u32 Ld = entry_len(d), Ed = entry_extra(d);
           const u32 span = entry_value(d) + ((w >> Ld) & ((1u << Ed) - 1u));
           if (entry_kind(d) != kLiteral || span > window) {
-            c.buf = saved_buf;
+            c.lo = saved_lo;
+            c.hi = saved_hi;
             c.nbits = saved_bits;
             c.idx = saved_idx;
             break;
@@ -333,7 +334,10 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
     if (action == kDynamic) {
       const u32 st = warp_dynamic_header(c, dyn);
       if (st) { fail = 1; break; }
-      if (lane == 0) { use_dyn = true; need_header = false; }
+      if (lane == 0) need_header = false;
+    } else if (action == kFixed) {
+      warp_load_fixed(dyn, fixed);
+      if (lane == 0) need_header = false;
     } else if (kEmit && action == kFlush) {
       const u32 to = now;
       flush_symbols(ring, out, source, unresolved, prefix, flushed, to);
@@ -516,7 +520,7 @@ chain_kernel(const u8* in, u32 in_size, u64 expected, u32 max_blocks, const u32*
 }
 
 // Emit every path node (warp per node, work stealing).
-__global__ void __launch_bounds__(kNodeWarps * 32)
+__global__ void __launch_bounds__(kEmitWarps * 32)
 emit_kernel(const u8* in, u32 in_size, u64 expected, const u32* cands, const u32* path,
             const u32* prefix, const u32* sizes, const u32* state, u32* next_item, u8* out,
             u32* source, u32* unresolved, u32* fail_flag, const Tables* fixed) {
@@ -669,7 +673,7 @@ cudaError_t configure_parallel_inflate(int* emit_per_sm) {
                                        int(sizeof(EmitShared)));
   if (e != cudaSuccess) return e;
   return cudaOccupancyMaxActiveBlocksPerMultiprocessor(emit_per_sm, emit_kernel,
-                                                       kNodeWarps * 32, sizeof(EmitShared));
+                                                       kEmitWarps * 32, sizeof(EmitShared));
 }
 
 u32 chain_levels(u32 capacity) {
@@ -712,7 +716,7 @@ cudaError_t launch_parallel_inflate(const u8* in, u64 in_size, u8* out, u64 expe
   (void)nodes;
   const u32 emit_grid = u32(dev.sms) * u32(dev.emit_per_sm > 0 ? dev.emit_per_sm : 1);
   profile_begin("emit_kernel", stream);
-  emit_kernel<<<emit_grid, kNodeWarps * 32, sizeof(EmitShared), stream>>>(
+  emit_kernel<<<emit_grid, kEmitWarps * 32, sizeof(EmitShared), stream>>>(
       in, u32(in_size), expected, b.cands, b.path, b.prefix, b.sizes, b.state, b.counters + 1,
       out, b.source, b.unresolved, b.fail, static_cast<const Tables*>(dev.fixed_tables));
   profile_end(stream);

@@ -104,7 +104,7 @@ __device__ u32 warp_inflate_one(const u8* in, u64 in_size64, u8* out, u64 out_si
   u32 error = zlib_framing(in, in_size, &window, &wanted);
   Bits c;
   u32 produced = 0, flushed = 0, blocks = 0, final = 0, full_words = 0;
-  bool need_header = true, complete = false, use_dyn = false;
+  bool need_header = true, complete = false;
   AdlerLane adler;
   const bool vec = (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
   if (!error && lane == 0) {
@@ -140,11 +140,10 @@ __device__ u32 warp_inflate_one(const u8* in, u64 in_size64, u8* out, u64 out_si
             complete = final != 0;
             break;
           }
-          if (type == 2) { action = kDynamic; break; }
-          use_dyn = false;
-          need_header = false;
+          action = type == 2 ? kDynamic : kFixed;
+          break;
         }
-        const Tables& t = use_dyn ? dyn : fixed;
+        const Tables& t = dyn;
         // Fast loop: every bit it reads lies inside the body and every token
         // fits the output, so only history and table kinds are checked.
         // Anything unusual goes to the exact path below, unconsumed.
@@ -153,8 +152,8 @@ __device__ u32 warp_inflate_one(const u8* in, u64 in_size64, u8* out, u64 out_si
         const u32 idx_limit = full_words >= 2 ? full_words - 1 : 0;
         while (c.idx < idx_limit && produced < stop_at) {
           c.refill_fast();
-          const u32 v = u32(c.buf);
-          const u32 e = t.ll.lut[v & 1023u];
+          const u32 v = c.lo;
+          const u32 e = t.ll.lut[v & kLLMask];
           const u32 kind = entry_kind(e);
           if (kind == kLiteral) {
             c.consume(entry_len(e));
@@ -163,18 +162,19 @@ __device__ u32 warp_inflate_one(const u8* in, u64 in_size64, u8* out, u64 out_si
             continue;
           }
           if (kind != kLength) break;
-          const u64 saved_buf = c.buf;
+          const u32 saved_lo = c.lo, saved_hi = c.hi;
           const u32 saved_bits = c.nbits, saved_idx = c.idx;
           const u32 L = entry_len(e), E = entry_extra(e);
           const u32 length = entry_value(e) + ((v >> L) & ((1u << E) - 1u));
           c.consume(L + E);
           c.refill_fast();
-          const u32 w = u32(c.buf);
+          const u32 w = c.lo;
           const u32 d = t.d.lut[w & 255u];
           const u32 Ld = entry_len(d), Ed = entry_extra(d);
           const u32 span = entry_value(d) + ((w >> Ld) & ((1u << Ed) - 1u));
           if (entry_kind(d) != kLiteral || span > window || span > produced) {
-            c.buf = saved_buf;
+            c.lo = saved_lo;
+            c.hi = saved_hi;
             c.nbits = saved_bits;
             c.idx = saved_idx;
             break;
@@ -243,7 +243,10 @@ __device__ u32 warp_inflate_one(const u8* in, u64 in_size64, u8* out, u64 out_si
     if (action == kDynamic) {
       const u32 st = warp_dynamic_header(c, dyn);
       if (st) { error = st; break; }
-      if (lane == 0) { use_dyn = true; need_header = false; }
+      if (lane == 0) need_header = false;
+    } else if (action == kFixed) {
+      warp_load_fixed(dyn, fixed);
+      if (lane == 0) need_header = false;
     } else if (action == kFlush) {
       const u32 to = now & ~15u;
       warp_flush(ring, out, flushed, to, out_size, adler, vec);
