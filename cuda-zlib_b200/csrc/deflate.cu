@@ -28,8 +28,11 @@
 // byte-aligned (:384-388).  Finish kernels scan the chunk sizes on the device
 // (no host round trip, unlike CompressionPrefix + ReadWords, codec_ffi.cu:
 // 362-390,590-595), combine the Adler partials and pack the slots.
+#include <mutex>
+
 #include "kernels.h"
 #include "common.cuh"
+#include "../../include/cuda_zlib_b200.h"
 
 namespace cz {
 
@@ -775,3 +778,139 @@ bool encode_in_smem(u32 chunk_bytes, const DeviceInfo& dev) {
 }
 
 }  // namespace cz
+
+// ---------------------------------------------------------------------------
+// Compression without device allocation (cuda_zlib_compress_noalloc).
+//
+// Some callers cannot allocate device memory while they compress: a service
+// whose allocator has reserved the whole device up front and hands out only
+// its own buffers, or a latency-critical loop that must not wait on an
+// allocation or a pool release.  For them this entry point runs the same
+// encoder with its scratch in one file-scope device array, sized for the
+// largest admitted call, which every GPU that loads the library keeps until
+// the process exits.  Calls share that array: two calls that overlap on the
+// GPU (different streams, or different host threads without ordering) race
+// and may corrupt each other's output.  No scratch needs clearing between
+// calls: every scratch word a call reads is written earlier in that call
+// (the encoder zeroes the slot words it packs into).
+// ---------------------------------------------------------------------------
+namespace cz {
+namespace {
+
+constexpr u64 kNoAllocMaxInput = CUDA_ZLIB_NOALLOC_MAX_INPUT;
+constexpr u32 kNoAllocMaxChunk = CUDA_ZLIB_NOALLOC_MAX_CHUNK;
+constexpr u64 kNoAllocMaxChunks = (kNoAllocMaxInput + 255) / 256;
+
+// Scratch layout for n input bytes in c chunks; offsets 256-byte aligned.
+struct NoAllocLayout {
+  u64 files, sizes, status, offsets, adler, slots, end;
+};
+constexpr u64 align256(u64 v) { return (v + 255) & ~u64(255); }
+constexpr NoAllocLayout noalloc_layout(u64 n, u64 c) {
+  NoAllocLayout l{};
+  l.files = 0;
+  l.sizes = align256(sizeof(EncodeFile));
+  l.status = align256(l.sizes + 4 * c);
+  l.offsets = align256(l.status + 4 * c);
+  l.adler = align256(l.offsets + 8 * c);
+  l.slots = align256(l.adler + 16 * c);
+  l.end = align256(l.slots + n + 96 * (c + 2));
+  return l;
+}
+constexpr u64 kNoAllocScratchBytes = noalloc_layout(kNoAllocMaxInput, kNoAllocMaxChunks).end;
+
+static __device__ __align__(256) u8 noalloc_scratch[kNoAllocScratchBytes];
+
+struct NoAllocDevice {
+  bool ready = false;
+  u8* scratch = nullptr;  // device address of noalloc_scratch on this device
+  DeviceInfo info{};
+};
+std::mutex noalloc_mutex;
+NoAllocDevice noalloc_devices[64];
+
+__global__ void noalloc_set_file_kernel(EncodeFile* dst, EncodeFile file) { *dst = file; }
+
+// One-time set-up per device, called with that device current: the array's
+// device address (the host-side symbol is not one) and kernel attributes.
+cudaError_t noalloc_device(int device, NoAllocDevice** out) {
+  if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(noalloc_mutex);
+  NoAllocDevice& d = noalloc_devices[device];
+  if (!d.ready) {
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    DeviceInfo info{};
+    info.device = device;
+    e = cudaDeviceGetAttribute(&info.sms, cudaDevAttrMultiProcessorCount, device);
+    if (e != cudaSuccess) return e;
+    e = configure_encode(&info.encode_smem_limit);
+    if (e != cudaSuccess) return e;
+    d.scratch = static_cast<u8*>(ptr);
+    d.info = info;
+    d.ready = true;
+  }
+  *out = &d;
+  return cudaSuccess;
+}
+
+cudaError_t compress_noalloc(const u8* in, u64 size, int64_t chunk_bytes, u8* out, u64 capacity,
+                             u32* meta, cudaStream_t stream) {
+  if (!meta || !out) return cudaErrorInvalidValue;
+  if (size > kNoAllocMaxInput || chunk_bytes < 256 || chunk_bytes > int64_t(kNoAllocMaxChunk) ||
+      (size && !in))
+    return cudaErrorInvalidValue;
+  const u32 chunk = u32(chunk_bytes);
+  const u64 chunks = size ? (size + chunk - 1) / chunk : 1;
+  if (capacity != size + chunks * 5 + 6) return cudaErrorInvalidValue;
+  int previous = 0;
+  cudaError_t e = cudaGetDevice(&previous);
+  if (e != cudaSuccess) return e;
+  int device = previous;
+  if (stream) {
+    e = cudaStreamGetDevice(stream, &device);
+    if (e != cudaSuccess) return e;
+  }
+  if (device != previous) {
+    e = cudaSetDevice(device);
+    if (e != cudaSuccess) return e;
+  }
+  NoAllocDevice* d = nullptr;
+  e = noalloc_device(device, &d);
+  if (e == cudaSuccess && !encode_in_smem(chunk, d->info)) e = cudaErrorInvalidValue;
+  if (e == cudaSuccess) {
+    const NoAllocLayout l = noalloc_layout(size, chunks);
+    u8* base = d->scratch;
+    EncodeFile* files = reinterpret_cast<EncodeFile*>(base + l.files);
+    const EncodeFile file{0, size, 0, capacity, 0, u32(chunks), chunk, 0};
+    e = cudaMemsetAsync(out, 0, capacity, stream);
+    if (e == cudaSuccess) {
+      noalloc_set_file_kernel<<<1, 1, 0, stream>>>(files, file);
+      e = cudaGetLastError();
+    }
+    if (e == cudaSuccess)
+      e = launch_encode(in, files, 1, chunk, u32(chunks), base + l.slots,
+                        reinterpret_cast<u32*>(base + l.sizes),
+                        reinterpret_cast<u32*>(base + l.status),
+                        reinterpret_cast<u64*>(base + l.adler),
+                        reinterpret_cast<u64*>(base + l.offsets), nullptr, nullptr, out, meta,
+                        d->info, stream);
+  }
+  if (device != previous) cudaSetDevice(previous);
+  return e;
+}
+
+}  // namespace
+}  // namespace cz
+
+extern "C" int cuda_zlib_compress_noalloc(const uint8_t* input, uint64_t size,
+                                          int64_t chunk_bytes, uint8_t* output,
+                                          uint64_t capacity, uint32_t* metadata, void* stream) {
+  try {
+    return int(cz::compress_noalloc(input, size, chunk_bytes, output, capacity, metadata,
+                                    static_cast<cudaStream_t>(stream)));
+  } catch (...) {
+    return int(cudaErrorUnknown);
+  }
+}

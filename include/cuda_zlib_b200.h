@@ -71,6 +71,27 @@ int cuda_zlib_decompress_batch(const uint8_t* input, uint64_t input_bytes,
                                uint64_t files, const uint32_t* encoded_metadata, uint8_t* output,
                                uint64_t output_bytes, uint32_t* metadata, void* stream);
 
+/* Compression that allocates no device memory.  No counterpart in the
+ * reference: it exists for callers that cannot allocate while they run, such
+ * as a service whose allocator reserves the whole device at start-up and
+ * lends out only its own buffers, or a latency-critical loop that must not
+ * wait on an allocation.  Same arguments, output and metadata as
+ * cuda_zlib_compress (byte-identical streams), restricted to
+ * size <= CUDA_ZLIB_NOALLOC_MAX_INPUT and
+ * 256 <= chunk_bytes <= CUDA_ZLIB_NOALLOC_MAX_CHUNK; anything else returns
+ * cudaErrorInvalidValue (1) and leaves output and metadata untouched.
+ * Scratch lives in one static device array (about 1.6 MB) that every GPU
+ * loading the library keeps until exit.  All calls share it: calls that
+ * overlap on the GPU race with each other, so order them (one stream, or
+ * events).  The first call on a device also looks up that array's device
+ * address and sets kernel attributes for that device; make that first call
+ * before any stream capture. */
+#define CUDA_ZLIB_NOALLOC_MAX_INPUT (1u << 20)
+#define CUDA_ZLIB_NOALLOC_MAX_CHUNK 32768
+int cuda_zlib_compress_noalloc(const uint8_t* input, uint64_t size, int64_t chunk_bytes,
+                               uint8_t* output, uint64_t capacity, uint32_t* metadata,
+                               void* stream);
+
 /* Workspace pool controls, same names and meaning as the reference's C
  * exports (codec_ffi.cu:1113-1142).  Retention is the pools' release
  * threshold in bytes (default 1 GiB); it can only be set before the first
