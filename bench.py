@@ -62,8 +62,8 @@ def zlib_stream(raw, level, strategy=zlib.Z_DEFAULT_STRATEGY):
     return c.compress(raw) + c.flush()
 
 
-def workload():
-    raw = config1_float32()
+def workload(size_mib=64):
+    raw = config1_float32()[:size_mib * MIB]
     streams = {}
 
     def make(level):
@@ -246,7 +246,7 @@ def run_gpu(args, rank, world):
     torch.cuda.set_device(rank % torch.cuda.device_count())
     device = torch.device("cuda", torch.cuda.current_device())
     codec.compile_kernels(device)
-    raw, l1, l6 = workload()
+    raw, l1, l6 = workload(args.size_mib)
     U = len(raw)
     raw_dev = torch.frombuffer(bytearray(raw), dtype=torch.uint8).to(device)
     l1_dev = torch.frombuffer(bytearray(l1), dtype=torch.uint8).to(device)
@@ -325,9 +325,11 @@ def run_gpu(args, rank, world):
 
     # End to end through the host-buffer API.
     e2e_times = []
+    if args.no_e2e:
+        e2e_times.append(float("nan"))
     e2e_start = torch.cuda.Event(enable_timing=True)
     e2e_end = torch.cuda.Event(enable_timing=True)
-    for k in range(max(1, args.steps)):
+    for k in range(0 if args.no_e2e else max(1, args.steps)):
         flush.fill_(k & 255)
         torch.cuda.synchronize()
         e2e_start.record(stream)
@@ -338,7 +340,8 @@ def run_gpu(args, rank, world):
         e2e_end.record(stream)
         torch.cuda.synchronize()
         e2e_times.append(e2e_start.elapsed_time(e2e_end) / 1e3)
-    assert h1.tobytes() == raw and h6.tobytes() == raw and host_stream.numel() == length
+    if not args.no_e2e:
+        assert h1.tobytes() == raw and h6.tobytes() == raw and host_stream.numel() == length
     e2e_seconds = sum(e2e_times) / len(e2e_times)
     if world > 1:
         t = torch.tensor([e2e_seconds], dtype=torch.float64, device=device)
@@ -362,7 +365,8 @@ def run_gpu(args, rank, world):
         "metric": METRIC, "value": round(value, 4), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step * 1e3, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
-        "data": "synthetic", "config": dict(CONFIG, parallelism="replicas" if world > 1 else "1 GPU",
+        "data": "synthetic", "config": dict(CONFIG, uncompressed_bytes_per_step=3 * U,
+                                            parallelism="replicas" if world > 1 else "1 GPU",
                                             compression_ratio=round(ratio, 5),
                                             zlib_l1_ratio=round(len(l1) / U, 5),
                                             zlib_l6_ratio=round(len(l6) / U, 5)),
@@ -373,9 +377,10 @@ def run_gpu(args, rank, world):
                      "algorithmic_bytes_per_launch": int(bytes_per_launch),
                      "launch_ms": round(total_ms / launches, 4)},
         "kernels_ms_per_step": {k: round(v[0] / args.steps, 3) for k, v in kernels.items()},
-        "e2e": {"value": round(e2e_value, 4), "unit": "GB/s",
-                "h2d_bytes_per_step": len(l1) + len(l6) + U,
-                "d2h_bytes_per_step": 2 * U + length + 16},
+        "e2e": None if args.no_e2e else {
+            "value": round(e2e_value, 4), "unit": "GB/s",
+            "h2d_bytes_per_step": len(l1) + len(l6) + U,
+            "d2h_bytes_per_step": 2 * U + length + 16},
         "cpu_baseline": cpu,
         "clocks": clocks.summary(),
         "gpu_launches": sum(v[1] for v in kernels.values()) // max(1, args.steps) * args.steps,
@@ -390,6 +395,10 @@ def main():
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    parser.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg")
+    parser.add_argument("--size-mib", type=int, default=64,
+                        help="leading MiB of the config-1 array (64 = the full workload; "
+                             "smaller sizes are for profiler captures)")
     args = parser.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
