@@ -11,6 +11,7 @@
 #include <algorithm>
 #include <array>
 #include <cstdint>
+#include <atomic>
 #include <mutex>
 #include <numeric>
 #include <string>
@@ -196,6 +197,12 @@ cudaError_t profile_drain(Profiler& p) {
 
 }  // namespace
 
+namespace {
+std::atomic<uint64_t> launches_issued{0};
+}
+
+void note_launch() { launches_issued.fetch_add(1, std::memory_order_relaxed); }
+
 void profile_begin(const char* kernel, cudaStream_t stream) {
   Profiler& p = profiler();
   {
@@ -229,6 +236,7 @@ __global__ void set_meta_kernel(u32* meta, u32 first, u32 second) {
 }
 
 cudaError_t set_meta(u32* meta, u32 first, u32 second, cudaStream_t stream) {
+  note_launch();
   set_meta_kernel<<<1, 1, 0, stream>>>(meta, first, second);
   return cudaGetLastError();
 }
@@ -557,6 +565,10 @@ int cuda_zlib_b200_profile(int enable) {
   p.totals.clear();
   p.enabled = enable != 0;
   return int(e);
+}
+
+uint64_t cuda_zlib_b200_launches(void) {
+  return cz::launches_issued.load(std::memory_order_relaxed);
 }
 
 int cuda_zlib_b200_profile_read(const char* kernel, double* total_ms, uint64_t* launches) {

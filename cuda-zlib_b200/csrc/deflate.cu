@@ -756,17 +756,20 @@ cudaError_t launch_encode(const u8* in, const EncodeFile* files, u32 nfiles, u32
   const bool in_smem = encode_in_smem(chunk_bytes, dev);
   const size_t smem = encode_smem_bytes(chunk_bytes, in_smem);
   profile_begin("encode_chunks_kernel", stream);
+  note_launch();
   encode_chunks_kernel<<<total_chunks, kEncThreads, smem, stream>>>(
       in, files, nfiles, chunk_bytes, total_chunks, slots, sizes, status, adler, spill_prev,
       spill_len, in_smem ? 1u : 0u);
   profile_end(stream);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
+  note_launch();
   encode_finish_kernel<<<(nfiles + 7) / 8, 256, 0, stream>>>(files, nfiles, sizes, status, adler,
                                                             offsets, out, meta);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   profile_begin("encode_pack_kernel", stream);
+  note_launch();
   encode_pack_kernel<<<total_chunks, 256, 0, stream>>>(files, nfiles, slots, sizes, offsets, meta,
                                                        out, chunk_bytes, total_chunks);
   profile_end(stream);
@@ -886,6 +889,7 @@ cudaError_t compress_noalloc(const u8* in, u64 size, int64_t chunk_bytes, u8* ou
     const EncodeFile file{0, size, 0, capacity, 0, u32(chunks), chunk, 0};
     e = cudaMemsetAsync(out, 0, capacity, stream);
     if (e == cudaSuccess) {
+      note_launch();
       noalloc_set_file_kernel<<<1, 1, 0, stream>>>(files, file);
       e = cudaGetLastError();
     }

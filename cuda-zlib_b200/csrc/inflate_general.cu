@@ -578,6 +578,7 @@ cudaError_t launch_discover(const u8* in, u64 in_size, u32* bitmap, u32* count, 
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
   profile_begin("discover_kernel", stream);
+  note_launch();
   discover_kernel<<<u32(blocks), kDiscoverThreads, 0, stream>>>(in, in_size, bitmap, count, gate);
   profile_end(stream);
   return cudaGetLastError();
@@ -586,6 +587,7 @@ cudaError_t launch_discover(const u8* in, u64 in_size, u32* bitmap, u32* count, 
 cudaError_t launch_general_status(const u8* in, u64 in_size, u64 expected, u32 max_candidates,
                                   u32 max_blocks, const u32* bitmap, const u32* count, u32* meta,
                                   u8* out, cudaStream_t stream) {
+  note_launch();
   general_status_kernel<<<1, 32, 0, stream>>>(in, in_size, expected, max_candidates, max_blocks,
                                               bitmap, count, meta);
   cudaError_t e = cudaGetLastError();
@@ -593,6 +595,7 @@ cudaError_t launch_general_status(const u8* in, u64 in_size, u64 expected, u32 m
   if (expected) {
     u64 blocks = (expected + 255) / 256;
     if (blocks > 4096) blocks = 4096;
+    note_launch();
     clear_on_failure_kernel<<<u32(blocks), 256, 0, stream>>>(meta, out, expected);
     e = cudaGetLastError();
   }

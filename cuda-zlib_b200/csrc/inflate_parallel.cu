@@ -661,6 +661,7 @@ cudaError_t build_fixed_tables(void** out) {
   Tables* fixed = nullptr;
   cudaError_t e = cudaMalloc(&fixed, sizeof(Tables));
   if (e != cudaSuccess) return e;
+  note_launch();
   build_fixed_kernel<<<1, 32>>>(fixed);
   e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return e;
@@ -699,31 +700,41 @@ cudaError_t launch_parallel_inflate(const u8* in, u64 in_size, u8* out, u64 expe
                                     const ParallelBuffers& b, u32* meta, const DeviceInfo& dev,
                                     cudaStream_t stream) {
   const u32 nodes = s.capacity + 2;
+  note_launch();
   cand_count_kernel<<<s.compact_blocks, 256, 0, stream>>>(b.bitmap, u32(s.bitmap_words),
                                                           b.block_counts);
+  note_launch();
   cand_scan_kernel<<<1, 1024, 0, stream>>>(b.block_counts, s.compact_blocks, b.total);
+  note_launch();
   cand_write_kernel<<<s.compact_blocks, 256, 0, stream>>>(b.bitmap, u32(s.bitmap_words),
                                                           b.block_counts, b.cands, s.capacity);
   const u32 node_grid = u32(dev.sms) * 4;
   profile_begin("describe_kernel", stream);
+  note_launch();
   describe_kernel<<<node_grid, kNodeWarps * 32, 0, stream>>>(
       in, u32(in_size), expected, b.cands, b.total, s.capacity, b.counters, b.ends, b.sizes,
       b.blocks, b.infos, static_cast<const Tables*>(dev.fixed_tables));
   profile_end(stream);
+  note_launch();
   chain_kernel<<<1, 1024, 0, stream>>>(in, u32(in_size), expected, max_blocks, b.cands, b.total,
                                        s.capacity, b.ends, b.sizes, b.blocks, b.infos, b.jump,
                                        s.levels, b.path, b.prefix, b.state);
   (void)nodes;
   const u32 emit_grid = u32(dev.sms) * u32(dev.emit_per_sm > 0 ? dev.emit_per_sm : 1);
   profile_begin("emit_kernel", stream);
+  note_launch();
   emit_kernel<<<emit_grid, kEmitWarps * 32, sizeof(EmitShared), stream>>>(
       in, u32(in_size), expected, b.cands, b.path, b.prefix, b.sizes, b.state, b.counters + 1,
       out, b.source, b.unresolved, b.fail, static_cast<const Tables*>(dev.fixed_tables));
   profile_end(stream);
+  note_launch();
   resolve_kernel<<<u32(dev.sms) * 8, 256, 0, stream>>>(b.state, u32(s.out_words), b.unresolved,
                                                        b.source, out);
-  if (s.segments)
+  if (s.segments) {
+    note_launch();
     adler_parts_kernel<<<s.segments, 256, 0, stream>>>(b.state, out, u32(expected), b.parts);
+  }
+  note_launch();
   parallel_finish_kernel<<<1, 1024, 0, stream>>>(in, u32(in_size), b.state, b.fail, b.parts,
                                                  s.segments, u32(expected), meta);
   return cudaGetLastError();

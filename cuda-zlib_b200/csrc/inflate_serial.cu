@@ -360,6 +360,7 @@ cudaError_t launch_serial_inflate(const u8* in, u8* out, const StreamDesc* descs
   if (grid > needed) grid = needed;
   if (grid < 1) grid = 1;
   profile_begin("serial_inflate_kernel", stream);
+  note_launch();
   serial_inflate_kernel<<<grid, kSerialWarps * 32, smem, stream>>>(
       in, out, descs, single, count, order, next, meta, encoded, max_blocks,
       static_cast<const Tables*>(dev.fixed_tables));

@@ -21,6 +21,8 @@ struct StreamDesc {
 // Opt-in kernel timing (cuda_zlib_b200_profile): when enabled, launchers
 // bracket their kernels with CUDA events on the launching stream.  No-ops
 // otherwise.  begin/end pairs must come from the same host thread.
+// Counts every kernel launch this library issues (cuda_zlib_b200_launches).
+void note_launch();
 void profile_begin(const char* kernel, cudaStream_t stream);
 void profile_end(cudaStream_t stream);
 

@@ -7,7 +7,7 @@ reference returns JAX arrays.  Every codec call runs hand-written sm_100a
 kernels through libcuda_zlib_b200.so; there is no CPU codec fallback.
 """
 
-from ._codec import (compress_zlib, decompress_zlib, compile_kernels,
+from ._codec import (compress_zlib, compress_zlib_host, decompress_zlib, compile_kernels,
                      compress_zlib_padded, decompress_zlib_checked,
                      decompress_zlib_host, workspace_pool_stats, trim_workspace_pool)
 from ._codec import (compress_zlib_batch_padded, decompress_zlib_batch_checked,
@@ -15,7 +15,7 @@ from ._codec import (compress_zlib_batch_padded, decompress_zlib_batch_checked,
                      compress_zlib_batch_host, decompress_zlib_batch_host)
 from ._errors import BackendUnavailable, CodecError, UnsupportedStream
 
-__all__ = ["compress_zlib", "decompress_zlib", "compile_kernels",
+__all__ = ["compress_zlib", "compress_zlib_host", "decompress_zlib", "compile_kernels",
            "compress_zlib_padded", "decompress_zlib_checked", "decompress_zlib_host",
            "workspace_pool_stats", "trim_workspace_pool",
            "compress_zlib_batch_padded", "decompress_zlib_batch_checked",

@@ -8,6 +8,11 @@ Device arrays are PyTorch CUDA tensors; host results are read-only NumPy
 arrays backed by pinned memory.  Calls run on the device's current PyTorch
 stream; the *_padded / *_checked variants never synchronize the host.
 """
+import os
+import threading
+import warnings
+from concurrent.futures import ThreadPoolExecutor
+
 import numpy as np
 
 from . import _native
@@ -100,15 +105,57 @@ def _stream(device):
     return torch.cuda.current_stream(device).cuda_stream
 
 
+_STAGE_PIECE = 4 << 20   # bytes per staging-copy task
+_stage_pool = None
+_stage_lock = threading.Lock()
+
+
+def _staging_pool():
+    """Host threads that fill pinned staging buffers (NumPy copies drop the GIL)."""
+    global _stage_pool
+    if _stage_pool is None:
+        with _stage_lock:
+            if _stage_pool is None:
+                workers = max(1, min(16, (os.cpu_count() or 1)))
+                _stage_pool = ThreadPoolExecutor(max_workers=workers,
+                                                 thread_name_prefix="cuda_zlib_stage")
+    return _stage_pool
+
+
 def _pinned_copy(data, device):
-    """Host bytes -> device tensor through one pinned staging buffer."""
+    """Pageable host bytes -> device tensor through one pinned staging buffer.
+
+    Large inputs are copied into the staging buffer by several host threads,
+    since one thread's memcpy is several times slower than the H2D link.
+    """
     torch = _torch()
     view = np.frombuffer(data, dtype=np.uint8) if not isinstance(data, np.ndarray) else data
     view = np.ascontiguousarray(view, dtype=np.uint8)
     staging = torch.empty(view.size, dtype=torch.uint8, pin_memory=True)
-    if view.size:
-        staging.numpy()[:] = view
+    host = staging.numpy()
+    if view.size >= 2 * _STAGE_PIECE:
+        pieces = range(0, view.size, _STAGE_PIECE)
+
+        def fill(start):
+            host[start:start + _STAGE_PIECE] = view[start:start + _STAGE_PIECE]
+
+        for future in [_staging_pool().submit(fill, start) for start in pieces]:
+            future.result()
+    elif view.size:
+        host[:] = view
     return staging.to(device, non_blocking=True)
+
+
+def _pinned_tensor(data):
+    """A CPU tensor over `data` when it already lives in page-locked memory."""
+    torch = _torch()
+    if not (isinstance(data, np.ndarray) and data.size and data.flags.c_contiguous):
+        return None
+    with warnings.catch_warnings():
+        # Read-only arrays (e.g. a *_host result) are only read here.
+        warnings.simplefilter("ignore", UserWarning)
+        tensor = torch.from_numpy(data)
+    return tensor if tensor.is_pinned() else None
 
 
 def _device_input(data, device):
@@ -118,7 +165,12 @@ def _device_input(data, device):
             if data.device != device:
                 raise ValueError("input array and requested CUDA device differ")
             return data.contiguous()
+        # Pinned CPU tensors go straight to the device by DMA.
         return data.contiguous().to(device, non_blocking=False)
+    if isinstance(data, np.ndarray):
+        pinned = _pinned_tensor(data)
+        if pinned is not None:
+            return pinned.to(device, non_blocking=False)
     if isinstance(data, (bytes, bytearray, memoryview, np.ndarray)):
         return _pinned_copy(data, device)
     raise TypeError("input must be bytes or a one-dimensional uint8 array or tensor")
@@ -428,6 +480,19 @@ def compress_zlib(data, device=0, *, chunk_bytes=32768):
     length, status = (int(v) for v in metadata.cpu().numpy())
     _check_value(status, "CUDA compression")
     return output[:length]
+
+
+def compress_zlib_host(data, device=0, *, chunk_bytes=32768) -> np.ndarray:
+    """Encode to a completed, read-only NumPy uint8 array in pinned memory.
+
+    The single-stream counterpart of compress_zlib_batch_host (the reference
+    has no single-stream host variant): same encoding as compress_zlib, then
+    one transfer of exactly the encoded length into pinned host memory.
+    """
+    output, metadata = compress_zlib_padded(data, device, chunk_bytes=chunk_bytes)
+    length, status = (int(v) for v in metadata.cpu().numpy())
+    _check_value(status, "CUDA compression")
+    return _to_pinned_host(output[:length])
 
 
 def decompress_zlib(payload, expected_bytes, device=0):

@@ -238,3 +238,32 @@ def test_workspace_pool_stats_and_trim(codec):
     after = codec.workspace_pool_stats(0)
     assert after["retention_bytes"] == before["retention_bytes"]
     assert after["reserved_bytes"] <= before["reserved_bytes"] and after["used_bytes"] == 0
+
+
+# ---------------------------------------------------------------- host I/O
+def test_compress_host_returns_pinned_exact_stream(codec):
+    import torch
+    raw = bytes(range(256)) * 5000 + random.Random(5).randbytes(70000)
+    host = codec.compress_zlib_host(raw, 0, chunk_bytes=16384)
+    assert isinstance(host, np.ndarray) and not host.flags.writeable
+    assert torch.from_numpy(host.copy()).numel() == host.size
+    assert host.tobytes() == oracle.compress(raw, 16384)
+
+
+def test_pinned_inputs_skip_staging_and_match(codec):
+    import torch
+    raw = random.Random(6).randbytes(300000) + b"q" * 200000
+    payload = zlib.compress(raw, 6)
+    pinned = torch.frombuffer(bytearray(payload), dtype=torch.uint8).pin_memory()
+    assert codec.decompress_zlib_host(pinned, len(raw), 0).tobytes() == raw
+    # A *_host result is page-locked memory and is accepted as input directly.
+    stream = codec.compress_zlib_host(raw, 0)
+    assert codec.decompress_zlib_host(stream, len(raw), 0).tobytes() == raw
+
+
+def test_large_bytes_input_uses_threaded_staging(codec):
+    rng = random.Random(8)
+    raw = bytes(rng.choices(range(12), k=12 << 20))   # above two staging pieces
+    payload = zlib.compress(raw, 1)
+    assert codec.decompress_zlib_host(payload, len(raw), 0).tobytes() == raw
+    assert codec.compress_zlib_host(raw, 0).tobytes() == oracle.compress(raw)
