@@ -256,7 +256,7 @@ cudaError_t upload(Workspace& ws, T** out, const std::vector<T>& host, cudaStrea
 // ---------------------------------------------------------------------------
 cudaError_t encode_files(const DeviceState& dev, const u8* in, u64 in_bytes,
                          std::vector<EncodeFile>& files, u32 chunk_bytes, u32 total_chunks,
-                         u8* out, u32* meta, cudaStream_t stream) {
+                         u8* out, u32* meta, cudaStream_t stream, u32* range_adler = nullptr) {
   Workspace ws(dev.pool, stream);
   EncodeFile* d_files = nullptr;
   u8* slots = nullptr;
@@ -277,7 +277,7 @@ cudaError_t encode_files(const DeviceState& dev, const u8* in, u64 in_bytes,
   }
   CZ_TRY(launch_encode(in, d_files, u32(files.size()), chunk_bytes, total_chunks, slots, sizes,
                        status, adler, offsets, spill_prev, spill_len, out, meta, dev.info,
-                       stream));
+                       stream, range_adler));
   return ws.release();
 }
 
@@ -308,6 +308,32 @@ cudaError_t compress(const u8* in, u64 size, int64_t chunk_bytes, u8* out, u64 c
   std::vector<EncodeFile> files(1);
   files[0] = EncodeFile{0, size, 0, capacity, 0, u32(chunks), chunk, 0};
   return encode_files(*dev, in, size, files, chunk, u32(chunks), out, meta, stream);
+}
+
+// One contiguous range of a longer stream: raw Deflate chunks, the last one
+// nonfinal unless `last`, and the range's Adler-32 in meta[2].  Splicing the
+// ranges of a stream (header + bodies + combined Adler-32) gives exactly the
+// stream that compress() makes of the whole input, since chunks are encoded
+// independently.
+cudaError_t compress_range(const u8* in, u64 size, int64_t chunk_bytes, int last, u8* out,
+                           u64 capacity, u32* meta, cudaStream_t stream) {
+  if (!meta || !out || (size && !in)) return cudaErrorInvalidValue;
+  if (size > kMaxBytes || chunk_bytes < 256 || chunk_bytes > 65535)
+    return cudaErrorInvalidValue;
+  const u32 chunk = u32(chunk_bytes);
+  const u64 chunks = std::max<u64>(1, (size + chunk - 1) / chunk);
+  if (2 * chunks - 1 > kMaxBlocks || capacity != size + chunks * 5 + 6 ||
+      capacity > kMaxBytes || (!last && size % chunk))
+    return cudaErrorInvalidValue;
+  DeviceScope scope(stream);
+  CZ_TRY(scope.error());
+  DeviceState* dev = nullptr;
+  CZ_TRY(device_state(scope.device(), &dev));
+  CZ_TRY(cudaMemsetAsync(out, 0, capacity, stream));
+  std::vector<EncodeFile> files(1);
+  files[0] = EncodeFile{0, size, 0, capacity, 0, u32(chunks), chunk,
+                        kEncodeRaw | (last ? 0u : kEncodeNotLast)};
+  return encode_files(*dev, in, size, files, chunk, u32(chunks), out, meta, stream, meta + 2);
 }
 
 cudaError_t compress_batch(const u8* in, u64 in_bytes, const int64_t* sizes, u64 count,
@@ -488,6 +514,17 @@ int cuda_zlib_compress(const uint8_t* input, uint64_t size, int64_t chunk_bytes,
   try {
     return int(cz::compress(input, size, chunk_bytes, output, capacity, metadata,
                             static_cast<cudaStream_t>(stream)));
+  } catch (...) {
+    return int(cudaErrorUnknown);
+  }
+}
+
+int cuda_zlib_compress_range(const uint8_t* input, uint64_t size, int64_t chunk_bytes,
+                             int32_t last, uint8_t* output, uint64_t capacity, uint32_t* metadata,
+                             void* stream) {
+  try {
+    return int(cz::compress_range(input, size, chunk_bytes, last, output, capacity, metadata,
+                                  static_cast<cudaStream_t>(stream)));
   } catch (...) {
     return int(cudaErrorUnknown);
   }

@@ -261,7 +261,7 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
   const u32 local = g - f.first_chunk;
   const u64 start = u64(local) * chunk_bytes;
   const u32 n = u32(min_u64(f.in_size - min_u64(start, f.in_size), chunk_bytes));
-  const bool final = local + 1 == f.chunks;
+  const bool final = local + 1 == f.chunks && !(f.flags & kEncodeNotLast);
   const u8* src = in + f.in_offset + start;
 
   // Shared layout: data | member bits | match bits | hash table | prev | len.
@@ -651,12 +651,13 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
 // [encoded_length, status] (FinishEncodedFile, batch_encode.cuh:39-112).
 __global__ void encode_finish_kernel(const EncodeFile* files, u32 nfiles, const u32* sizes,
                                      const u32* status, const u64* adler, u64* offsets,
-                                     u8* out, u32* meta) {
+                                     u8* out, u32* meta, u32* range_adler) {
   const u32 lane = threadIdx.x & 31u;
   const u32 f = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   if (f >= nfiles) return;
   const EncodeFile file = files[f];
-  u64 running = 2;  // after the two-byte zlib header
+  const bool raw = (file.flags & kEncodeRaw) != 0;
+  u64 running = raw ? 0 : 2;  // after the two-byte zlib header
   u32 bad = 0;
   u64 s1 = 0, s2 = 0;
   for (u32 base = 0; base < file.chunks; base += 32) {
@@ -688,13 +689,14 @@ __global__ void encode_finish_kernel(const EncodeFile* files, u32 nfiles, const 
     s1 += __shfl_xor_sync(kFullMask, s1, o);
     s2 += __shfl_xor_sync(kFullMask, s2, o);
   }
-  const u64 total = running + 4;
+  const u64 total = running + (raw ? 0 : 4);
   u32 st = bad ? u32(kCompressionOverflow) : 0u;
   if (!st && total > file.capacity) st = kCompressionOverflow;
   if (lane == 0) {
     u8* dst = out + file.out_offset;
-    if (!st) {
-      const u32 checksum = adler_finish(s1, s2, file.in_size);
+    const u32 checksum = adler_finish(s1, s2, file.in_size);
+    if (range_adler) range_adler[f] = st ? 0u : checksum;
+    if (!st && !raw) {
       dst[0] = 0x78;
       dst[1] = 0x01;
       dst[total - 4] = u8(checksum >> 24);
@@ -752,7 +754,7 @@ cudaError_t configure_encode(int* max_dynamic_smem) {
 cudaError_t launch_encode(const u8* in, const EncodeFile* files, u32 nfiles, u32 chunk_bytes,
                           u32 total_chunks, u8* slots, u32* sizes, u32* status, u64* adler,
                           u64* offsets, u16* spill_prev, u8* spill_len, u8* out, u32* meta,
-                          const DeviceInfo& dev, cudaStream_t stream) {
+                          const DeviceInfo& dev, cudaStream_t stream, u32* range_adler) {
   const bool in_smem = encode_in_smem(chunk_bytes, dev);
   const size_t smem = encode_smem_bytes(chunk_bytes, in_smem);
   profile_begin("encode_chunks_kernel", stream);
@@ -765,7 +767,7 @@ cudaError_t launch_encode(const u8* in, const EncodeFile* files, u32 nfiles, u32
   if (e != cudaSuccess) return e;
   note_launch();
   encode_finish_kernel<<<(nfiles + 7) / 8, 256, 0, stream>>>(files, nfiles, sizes, status, adler,
-                                                            offsets, out, meta);
+                                                            offsets, out, meta, range_adler);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   profile_begin("encode_pack_kernel", stream);

@@ -41,8 +41,12 @@ struct DeviceInfo {
 struct EncodeFile {
   u64 in_offset, in_size;    // input bytes
   u64 out_offset, capacity;  // padded output slot: size + 5 * chunks + 6
-  u32 first_chunk, chunks, chunk_bytes, pad;
+  u32 first_chunk, chunks, chunk_bytes, flags;
 };
+// EncodeFile::flags.  A range of a longer stream leaves its last chunk
+// nonfinal (the stream continues) and/or omits the zlib header and trailer.
+constexpr uint32_t kEncodeNotLast = 1u;
+constexpr uint32_t kEncodeRaw = 2u;
 
 // Warp-per-stream inflate (serial route semantics).  `next` is a zeroed
 // device counter; `order` (optional) lists stream indices largest first;
@@ -59,13 +63,15 @@ cudaError_t launch_serial_inflate(const u8* in, u8* out, const StreamDesc* descs
 // per chunk.  When encode_in_smem() is false the per-position arrays live in
 // `spill_prev` (u16) and `spill_len` (u8), in_bytes + 16 * (chunks + 1)
 // entries each.  `out` must be zeroed; `meta` receives [encoded_length,
-// status] per file.
+// status] per file, and `range_adler` (optional) the Adler-32 of each
+// file's input bytes.
 cudaError_t configure_encode(int* max_dynamic_smem);
 bool encode_in_smem(u32 chunk_bytes, const DeviceInfo& dev);
 cudaError_t launch_encode(const u8* in, const EncodeFile* files, u32 nfiles, u32 chunk_bytes,
                           u32 total_chunks, u8* slots, u32* sizes, u32* status, u64* adler,
                           u64* offsets, u16* spill_prev, u8* spill_len, u8* out, u32* meta,
-                          const DeviceInfo& dev, cudaStream_t stream);
+                          const DeviceInfo& dev, cudaStream_t stream,
+                          u32* range_adler = nullptr);
 
 // Block-parallel inflate of one large stream (inflate_parallel.cu).
 struct ParallelScratch {

@@ -43,8 +43,11 @@ def _configure(library):
     library.cuda_zlib_decompress_batch.argtypes = [_u8p, ctypes.c_uint64, _i64p, _i64p,
                                                    ctypes.c_uint64, _u8p, _u8p, ctypes.c_uint64,
                                                    _u8p, ctypes.c_void_p]
+    library.cuda_zlib_compress_range.argtypes = [_u8p, ctypes.c_uint64, ctypes.c_int64,
+                                                 ctypes.c_int32, _u8p, ctypes.c_uint64, _u8p,
+                                                 ctypes.c_void_p]
     for name in ("cuda_zlib_compress", "cuda_zlib_decompress", "cuda_zlib_compress_batch",
-                 "cuda_zlib_decompress_batch"):
+                 "cuda_zlib_decompress_batch", "cuda_zlib_compress_range"):
         getattr(library, name).restype = ctypes.c_int
     library.CudaZlibSetWorkspaceRetention.argtypes = [ctypes.c_uint64]
     library.CudaZlibSetWorkspaceRetention.restype = ctypes.c_int

@@ -43,6 +43,20 @@ extern "C" {
 int cuda_zlib_compress(const uint8_t* input, uint64_t size, int64_t chunk_bytes,
                        uint8_t* output, uint64_t capacity, uint32_t* metadata, void* stream);
 
+/* One contiguous range of a longer stream, for splitting a stream's chunks
+ * across GPUs.  No counterpart in the reference, which compresses a stream
+ * on one device.  Writes the range's raw Deflate chunks with no zlib header
+ * or trailer; the last chunk is final only when `last` is nonzero, and a
+ * range that is not last must hold a whole number of chunks.  Capacity as
+ * for cuda_zlib_compress.  metadata: u32[3] = [body_length, status,
+ * adler32 of the range's input].  Bodies of consecutive ranges, with the
+ * two-byte header before them and the combined Adler-32 after, are
+ * byte-identical to cuda_zlib_compress on the whole input.  Invalid bounds
+ * return cudaErrorInvalidValue (1). */
+int cuda_zlib_compress_range(const uint8_t* input, uint64_t size, int64_t chunk_bytes,
+                             int32_t last, uint8_t* output, uint64_t capacity,
+                             uint32_t* metadata, void* stream);
+
 /* Replaces CudaZlibDecompress / DecompressImpl (codec_ffi.cu:1153-1161,
  * 990-998, 662-950).  expected = exact output size; max_candidates and
  * max_blocks in [1, 262144] (defaults 262144 select the small route for
