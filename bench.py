@@ -117,6 +117,7 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+        time.sleep(0.5)  # nvidia-smi's first sample lands before the timed region
         return self
 
     def __exit__(self, *exc):
@@ -397,6 +398,404 @@ def run_gpu(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------ configs 0, 2, 3
+def zipf_vocabulary(seed=0):
+    """Config 0 vocabulary: 4096 random lowercase words of 3-10 letters and
+    their Zipf(s=1.1) rank weights."""
+    rng = np.random.default_rng(seed)
+    lengths = rng.integers(3, 11, 4096)
+    letters = rng.integers(97, 123, (4096, 10), dtype=np.uint8)
+    weights = np.arange(1, 4097, dtype=np.float64) ** -1.1
+    return letters, lengths, weights / weights.sum(), rng
+
+
+def zipf_text(size, seed=0):
+    """Config 0 corpus: Zipf words joined by single spaces, '\n' with p = 1/12."""
+    letters, lengths, p, rng = zipf_vocabulary(seed)
+    n = size // 6 + 64
+    while True:
+        idx = rng.choice(4096, n, p=p)
+        word_len = lengths[idx]
+        starts = np.concatenate(([0], np.cumsum(word_len + 1)[:-1]))
+        buf = np.empty(int(starts[-1] + word_len[-1] + 1), dtype=np.uint8)
+        for j in range(10):
+            m = word_len > j
+            buf[starts[m] + j] = letters[idx[m], j]
+        buf[starts + word_len] = np.where(rng.random(n) < 1 / 12, 10, 32).astype(np.uint8)
+        if buf.size >= size:
+            return buf[:size].tobytes()
+        n *= 2
+
+
+def config2_files(count=4096, seed=2):
+    """Config 2: log-uniform sizes on 256 B-256 KiB (1% empty); 50% slices of
+    the config-0 corpus, 25% uniform random bytes, 25% runs (geometric mean
+    length 64, values 0-15)."""
+    rng = np.random.default_rng(seed)
+    sizes = np.exp(rng.uniform(np.log(256), np.log(262144), count)).astype(np.int64)
+    sizes[rng.choice(count, count // 100, replace=False)] = 0
+    kinds = rng.choice(3, count, p=[0.5, 0.25, 0.25])
+    corpus = np.frombuffer(zipf_text(16 * MIB, 0), dtype=np.uint8)
+    files = []
+    for n, kind in zip(sizes.tolist(), kinds.tolist()):
+        if kind == 0:
+            start = int(rng.integers(0, corpus.size - n + 1))
+            data = corpus[start:start + n]
+        elif kind == 1:
+            data = rng.integers(0, 256, n, dtype=np.uint8)
+        else:
+            runs = rng.geometric(1 / 64, n // 32 + 64)
+            while runs.sum() < n:
+                runs = np.concatenate((runs, rng.geometric(1 / 64, n // 32 + 64)))
+            data = np.repeat(rng.integers(0, 16, runs.size, dtype=np.uint8), runs)[:n]
+        files.append(data.tobytes())
+    return files
+
+
+def config3_records(size=1 << 30, seed=3):
+    """Config 3: 64-byte records (i32 id, i32 timestamp += U{1..10}, 4 x i16
+    U[-100, 100], a 20-byte config-0 word, zero padded, 28 zero bytes)."""
+    n = size // 64
+    rng = np.random.default_rng(seed)
+    rec = np.zeros(n, dtype=[("id", "<i4"), ("ts", "<i4"), ("f", "<i2", (4,)),
+                             ("word", "S20"), ("pad", "V28")])
+    rec["id"] = np.arange(n, dtype=np.int32)
+    rec["ts"] = np.cumsum(rng.integers(1, 11, n), dtype=np.int64).astype(np.int32)
+    rec["f"] = rng.integers(-100, 101, (n, 4), dtype=np.int16)
+    letters, lengths, p, _ = zipf_vocabulary(0)
+    vocab = np.array([letters[i, :lengths[i]].tobytes() for i in range(4096)], dtype="S20")
+    rec["word"] = vocab[rng.choice(4096, n, p=p)]
+    return rec.view(np.uint8)
+
+
+def _parallel_map(fn, items, threads):
+    from concurrent.futures import ThreadPoolExecutor
+    with ThreadPoolExecutor(max_workers=threads) as pool:
+        return list(pool.map(fn, items))
+
+
+# ------------------------------------------------------------------ sharded workloads
+BATCH_METRIC = ("decompress & compress GB/s (uncompressed bytes; config-2 batch of 4096 "
+                "files: zlib L6 batch decode + chunk-32768 batch compress)")
+RECORDS_METRIC = ("compress GB/s (uncompressed bytes; config-3 1 GiB record stream, "
+                  "chunk-32768 ranges)")
+
+
+def batch_inputs():
+    files = config2_files()
+    streams = _parallel_map(lambda f: zlib_stream(f, 6), files, os.cpu_count() or 1)
+    return files, streams
+
+
+def cpu_batch(files, streams, threads):
+    """Oracle port over a file sample: serial-route decode and compress per file."""
+    from oracle import oracle
+
+    def one(k):
+        out, status = oracle.inflate_serial(streams[k], len(files[k]))
+        assert status == 0 and out == files[k]
+        oracle.compress(files[k], CHUNK)
+
+    start = time.perf_counter()
+    _parallel_map(one, range(len(files)), threads)
+    return time.perf_counter() - start
+
+
+def cpu_records(sample, threads):
+    """Oracle port: chunk-parallel compress of a record sample at 32 KiB."""
+    from oracle import oracle
+    import ctypes
+    lib = oracle.lib()
+    chunks = -(-len(sample) // CHUNK)
+    slot = (CHUNK * 9 + 7) // 8 + 16
+    slots = np.zeros(chunks * slot, dtype=np.uint8)
+    sizes = np.zeros(chunks, dtype=np.uint32)
+    src = np.frombuffer(sample, dtype=np.uint8)
+    per = -(-chunks // threads)
+
+    def encode(first):
+        count = min(per, chunks - first)
+        lib.oracle_compress_chunks(
+            src.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)), len(sample), CHUNK, first, count,
+            slots[first * slot:].ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)), slot,
+            sizes[first:].ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)))
+
+    start = time.perf_counter()
+    _parallel_map(encode, range(0, chunks, per), threads)
+    return time.perf_counter() - start
+
+
+def run_reference_sharded(args, rank, world):
+    if rank != 0:
+        return
+    from oracle import oracle
+    oracle.build()
+    threads = os.cpu_count() or 1
+    if args.workload == "batch":
+        files, streams = batch_inputs()
+        k = 512
+        files, streams = files[:k], streams[:k]
+        unit_bytes = 2 * sum(len(f) for f in files)
+        run = lambda: cpu_batch(files, streams, threads)
+        metric, sample = BATCH_METRIC, ("first 512 of the 4096 config-2 files: serial-route "
+                                        "decode + compress per file, oracle port, one file "
+                                        "per thread")
+    else:
+        data = config3_records(64 * MIB)
+        unit_bytes = data.size
+        run = lambda: cpu_records(data.tobytes(), threads)
+        metric, sample = RECORDS_METRIC, ("64 MiB of config-3 records, chunk-parallel "
+                                          "compress at 32 KiB, oracle port")
+    for _ in range(args.warmup):
+        run()
+    seconds = sum(run() for _ in range(args.steps)) / args.steps
+    value = unit_bytes / seconds / 1e9
+    print(json.dumps({
+        "impl": "reference", "metric": metric, "value": round(value, 4), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(seconds * 1e3, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+        "config": {"workload": args.workload},
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0}}), flush=True)
+
+
+def _timed_steps(torch, args, step, stream, flush, device, world):
+    """K steps bracketed by barrier + synchronize; returns (seconds, clocks)."""
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with ClockSampler(device.index) as clocks:
+        for k in range(args.steps):
+            flush.fill_(k & 255)
+            starts[k].record(stream)
+            step()
+            ends[k].record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    return sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / 1e3, clocks
+
+
+def _max_over_ranks(torch, value, device, world):
+    if world > 1:
+        t = torch.tensor([value], dtype=torch.float64, device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        value = float(t.item())
+    return value
+
+
+def _kernel_times(lib, names):
+    import ctypes
+    kernels = {}
+    for name in names:
+        total, launches = ctypes.c_double(), ctypes.c_uint64()
+        lib.cuda_zlib_b200_profile_read(name.encode(), ctypes.byref(total), ctypes.byref(launches))
+        if launches.value:
+            kernels[name] = (total.value, launches.value)
+    return kernels
+
+
+def run_gpu_sharded(args, rank, world):
+    import ctypes
+    import torch
+    import cuda_zlib as codec
+    from cuda_zlib import _native, sharding
+
+    torch.cuda.set_device(rank % torch.cuda.device_count())
+    device = torch.device("cuda", torch.cuda.current_device())
+    codec.compile_kernels(device)
+    stream = torch.cuda.current_stream(device)
+    flush = torch.empty(256 * MIB, dtype=torch.uint8, device=device)
+    lib = _native.library()
+    lib.cuda_zlib_b200_profile.argtypes = [ctypes.c_int]
+    lib.cuda_zlib_b200_profile_read.argtypes = [ctypes.c_char_p, ctypes.POINTER(ctypes.c_double),
+                                                ctypes.POINTER(ctypes.c_uint64)]
+    lib.cuda_zlib_b200_launches.restype = ctypes.c_uint64
+
+    if args.workload == "batch":
+        files, streams = batch_inputs()
+        total_units = 2 * sum(len(f) for f in files)
+        mine = sharding.rank_files([len(f) + len(s) for f, s in zip(files, streams)], rank, world)
+        my_files = [files[i] for i in mine] or [b""]
+        my_streams = [streams[i] for i in mine] or [zlib_stream(b"", 6)]
+        sizes = [len(f) for f in my_files]
+        in_sizes = [len(s) for s in my_streams]
+        packed_raw = b"".join(my_files)
+        packed_z = b"".join(my_streams)
+        raw_dev = torch.frombuffer(bytearray(packed_raw + b"\0"), dtype=torch.uint8)[:len(packed_raw)].to(device)
+        z_dev = torch.frombuffer(bytearray(packed_z), dtype=torch.uint8).to(device)
+
+        def step(raw_in=raw_dev, z_in=z_dev):
+            out, meta = codec.decompress_zlib_batch_checked(z_in, in_sizes, sizes, device)
+            slots, emeta = codec.compress_zlib_batch_padded(raw_in, sizes, device,
+                                                            chunk_bytes=CHUNK)
+            return out, meta, slots, emeta
+
+        def verify(result):
+            out, meta, slots, emeta = result
+            assert not meta.cpu().numpy().any()
+            assert out.cpu().numpy().tobytes() == packed_raw
+            emeta = emeta.cpu().numpy()
+            assert not emeta[:, 1].any()
+            host = slots.cpu().numpy().tobytes()
+            offset = 0
+            for f, (length, _) in zip(my_files, emeta):
+                assert zlib.decompress(host[offset:offset + int(length)]) == f
+                offset += len(f) + 5 * max(1, -(-len(f) // CHUNK)) + 6
+            return float(emeta[:, 0].sum()) / max(1, sum(sizes))
+
+        h2d = len(packed_raw) + len(packed_z)
+        d2h = sum(sizes) + sum(len(f) + 5 * max(1, -(-len(f) // CHUNK)) + 6 for f in my_files)
+        raw_pin = torch.frombuffer(bytearray(packed_raw + b"\0"), dtype=torch.uint8)[:len(packed_raw)].pin_memory()
+        z_pin = torch.frombuffer(bytearray(packed_z), dtype=torch.uint8).pin_memory()
+
+        def e2e_step():
+            out, meta, slots, emeta = step(raw_pin, z_pin)
+            host_out = torch.empty(out.numel(), dtype=torch.uint8, pin_memory=True)
+            host_out.copy_(out, non_blocking=True)
+            host_slots = torch.empty(slots.numel(), dtype=torch.uint8, pin_memory=True)
+            host_slots.copy_(slots, non_blocking=True)
+            m, em = meta.cpu().numpy(), emeta.cpu().numpy()
+            assert not m.any() and not em[:, 1].any()
+
+        algorithmic = {"serial_inflate_kernel": len(packed_z) + sum(sizes),
+                       "encode_chunks_kernel": sum(sizes)}
+        names = ("serial_inflate_kernel", "encode_chunks_kernel", "encode_pack_kernel")
+        metric = BATCH_METRIC
+        config = {"workload": "config2: 4096 files (seed 2), log-uniform 256 B-256 KiB, 1% empty; "
+                              "50% Zipf text, 25% random, 25% runs; zlib L6 decode + compress "
+                              "at chunk_bytes=32768",
+                  "files": len(files), "uncompressed_bytes_per_step": total_units,
+                  "parallelism": "files LPT-sharded over %d GPU(s)" % world,
+                  "l2": "flushed between steps (256 MiB write)"}
+    else:
+        data = config3_records()
+        total_units = data.size
+        max_range = ((1 << 28) - 6) * CHUNK // (CHUNK + 5)
+        ranges = sharding.rank_ranges(data.size, CHUNK, rank, world, max_range)
+        lo, hi = ranges[0][0], ranges[-1][1]
+        last_rank = max(r for r in range(world)
+                        if sharding.rank_ranges(data.size, CHUNK, r, world, max_range))
+        mine = torch.from_numpy(data[lo:hi])
+        src_dev = mine.to(device)
+        outs, metas = [], []
+        for start, stop in ranges:
+            n = stop - start
+            cap = n + 5 * max(1, -(-n // CHUNK)) + 6
+            outs.append(torch.empty(cap, dtype=torch.uint8, device=device))
+            metas.append(torch.zeros(3, dtype=torch.uint32, device=device))
+
+        def step(src=src_dev):
+            for k, (start, stop) in enumerate(ranges):
+                last = rank == last_rank and k == len(ranges) - 1
+                piece = src[start - lo:stop - lo]
+                if piece.device.type == "cpu":
+                    piece = piece.to(device)
+                _native.check(lib.cuda_zlib_compress_range(
+                    piece.data_ptr(), stop - start, CHUNK, int(last), outs[k].data_ptr(),
+                    outs[k].numel(), metas[k].data_ptr(), stream.cuda_stream), "range")
+            return outs, metas
+
+        def verify(result):
+            total = 0
+            for (start, stop), out, meta in zip(ranges, *result):
+                length, status, adler = (int(v) for v in meta.cpu())
+                assert status == 0 and adler == zlib.adler32(data[start:stop])
+                body = out[:length].cpu().numpy().tobytes()
+                d = zlib.decompressobj(-15)
+                assert d.decompress(body) == data[start:stop].tobytes()
+                total += length
+            return total / max(1, hi - lo)
+
+        h2d = hi - lo
+        d2h = sum(o.numel() for o in outs)
+        src_pin = mine.pin_memory()
+
+        def e2e_step():
+            step(src_pin)
+            for out, meta in zip(outs, metas):
+                length = int(meta[0].item())
+                host = torch.empty(length, dtype=torch.uint8, pin_memory=True)
+                host.copy_(out[:length])
+
+        algorithmic = {"encode_chunks_kernel": hi - lo}
+        names = ("encode_chunks_kernel", "encode_pack_kernel")
+        metric = RECORDS_METRIC
+        config = {"workload": "config3: 1 GiB of 64-byte records (seed 3), compressed as "
+                              "chunk-aligned ranges at chunk_bytes=32768 (the 262144 chunk of "
+                              "the config is outside the reference's [256, 65535] bound)",
+                  "uncompressed_bytes_per_step": total_units,
+                  "parallelism": "chunk ranges over %d GPU(s)" % world,
+                  "l2": "inputs larger than L2; also flushed between steps"}
+
+    for _ in range(args.warmup):
+        result = step()
+    torch.cuda.synchronize()
+    ratio = verify(result)
+    lib.cuda_zlib_b200_profile(1)
+    launches_before = lib.cuda_zlib_b200_launches()
+    seconds, clocks = _timed_steps(torch, args, step, stream, flush, device, world)
+    launched = lib.cuda_zlib_b200_launches() - launches_before
+    kernels = _kernel_times(lib, names)
+    lib.cuda_zlib_b200_profile(0)
+    seconds = _max_over_ranks(torch, seconds, device, world)
+    per_step = seconds / args.steps
+    value = total_units / per_step / 1e9
+
+    e2e_times = []
+    for k in range(max(args.warmup, 1) + args.steps):
+        flush.fill_(k & 255)
+        torch.cuda.synchronize()
+        start = time.perf_counter()
+        e2e_step()
+        torch.cuda.synchronize()
+        if k >= max(args.warmup, 1):
+            e2e_times.append(time.perf_counter() - start)
+    e2e_seconds = _max_over_ranks(torch, sum(e2e_times) / len(e2e_times), device, world)
+    roofline = None
+    if kernels:
+        name, (total_ms, launches) = max(kernels.items(), key=lambda kv: kv[1][0])
+        per_launch = algorithmic.get(name, 0) / max(1, launches // args.steps)
+        achieved = per_launch / (total_ms / launches / 1e3) / 1e9
+        peak, peak_kind = measured_peak()
+        roofline = {"bound": "hbm", "kernel": name, "achieved": round(achieved, 2),
+                    "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                    "frac": round(achieved / peak, 5), "traffic": committed_traffic(name),
+                    "algorithmic_bytes_per_launch": int(per_launch),
+                    "launch_ms": round(total_ms / launches, 4)}
+    if rank != 0:
+        return
+    cpu = None
+    if world == 1 and not args.no_cpu:
+        threads = os.cpu_count() or 1
+        if args.workload == "batch":
+            k = 512
+            t = cpu_batch(files[:k], streams[:k], threads)
+            cpu = {"value": round(2 * sum(len(f) for f in files[:k]) / t / 1e9, 4),
+                   "sample": "first 512 config-2 files, decode + compress per file"}
+        else:
+            sample = data[:64 * MIB].tobytes()
+            t = cpu_records(sample, threads)
+            cpu = {"value": round(len(sample) / t / 1e9, 4),
+                   "sample": "64 MiB of config-3 records, chunk-parallel compress"}
+        cpu.update(unit="GB/s", cores=threads, kind="port")
+    config["compression_ratio_rank0"] = round(ratio, 5)
+    print(json.dumps({
+        "metric": metric, "value": round(value, 4), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step * 1e3, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8",
+        "data": "synthetic", "config": config, "roofline": roofline,
+        "kernels_ms_per_step": {k: round(v[0] / args.steps, 3) for k, v in kernels.items()},
+        "e2e": {"value": round(total_units / e2e_seconds / 1e9, 4), "unit": "GB/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "timer": "host wall clock"},
+        "cpu_baseline": cpu, "clocks": clocks.summary(), "gpu_launches": launched}), flush=True)
+
+
 def main():
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     parser.add_argument("--gpus", type=int, default=1)
@@ -405,6 +804,10 @@ def main():
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     parser.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg")
+    parser.add_argument("--workload", choices=["config1", "batch", "records"], default="config1",
+                        help="config1 (default; replicas at N>1), batch (config 2, files "
+                             "LPT-sharded over ranks) or records (config 3, chunk ranges "
+                             "sharded over ranks)")
     parser.add_argument("--size-mib", type=int, default=64,
                         help="leading MiB of the config-1 array (64 = the full workload; "
                              "smaller sizes are for profiler captures)")
@@ -412,7 +815,10 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":
-        run_reference(args, rank, world)
+        if args.workload == "config1":
+            run_reference(args, rank, world)
+        else:
+            run_reference_sharded(args, rank, world)
         return
     if world > 1:
         import datetime
@@ -420,7 +826,10 @@ def main():
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     try:
-        run_gpu(args, rank, world)
+        if args.workload == "config1":
+            run_gpu(args, rank, world)
+        else:
+            run_gpu_sharded(args, rank, world)
     finally:
         if world > 1:
             import torch
