@@ -36,24 +36,26 @@
 
 namespace cz {
 
-constexpr u32 kEncThreads = 256;
+constexpr u32 kEncThreads = 512;
+constexpr u32 kEncWarps = kEncThreads / 32;
+constexpr u32 kOwnerBits = 4;  // log2(kEncWarps): hash slots are split over the warps
+static_assert((1u << kOwnerBits) == kEncWarps, "one slot class per warp");
+constexpr u32 kRing = 256;     // per-warp ring of owned positions (a power of two)
 constexpr u32 kHashSlots = 8192;
 
-__constant__ u16 kLenBase[29] = {3,  4,  5,  6,  7,  8,  9,  10, 11,  13,  15,  17,  19,  23, 27,
-                                 31, 35, 43, 51, 59, 67, 83, 99, 115, 131, 163, 195, 227, 258};
-__constant__ u8 kLenExtra[29] = {0, 0, 0, 0, 0, 0, 0, 0, 1, 1, 1, 1, 2, 2, 2,
-                                 2, 3, 3, 3, 3, 4, 4, 4, 4, 5, 5, 5, 5, 0};
-__constant__ u16 kDistBase[30] = {1,    2,    3,    4,    5,    7,     9,     13,    17,  25,
-                                  33,   49,   65,   97,   129,  193,   257,   385,   513, 769,
-                                  1025, 1537, 2049, 3073, 4097, 6145, 8193, 12289, 16385, 24577};
-__constant__ u8 kDistExtra[30] = {0, 0, 0, 0, 1, 1, 2, 2,  3,  3,  4,  4,  5,  5,  6,
-                                  6, 7, 7, 8, 8, 9, 9, 10, 10, 11, 11, 12, 12, 13, 13};
+// Extra bits of a length or distance code (RFC 1951 section 3.2.5), by
+// arithmetic rather than table lookups: the lanes of a warp look up different
+// codes, which a __constant__ table would serialize.  Length symbols 8..27
+// carry (symbol - 4) / 4 extra bits and distance symbols 4..29 carry
+// (symbol - 2) / 2; the extra value is the low bits of (length - 3) or
+// (distance - 1), whose high bits the symbol itself encodes.
+__device__ __forceinline__ u32 length_extra_bits(u32 li) {
+  return (li >= 8 && li < 28) ? (li - 4) >> 2 : 0u;
+}
+__device__ __forceinline__ u32 dist_extra_bits(u32 di) { return di >= 4 ? (di - 2) >> 1 : 0u; }
+__device__ __forceinline__ u32 low_bits(u32 x, u32 n) { return x & ((1u << n) - 1u); }
 __constant__ u8 kClOrder[19] = {16, 17, 18, 0, 8, 7, 9, 6, 10, 5, 11, 4, 12, 3, 13, 2, 14, 1, 15};
 
-__device__ __forceinline__ u32 hash3(const u8* d, u32 p) {
-  const u32 v = u32(d[p]) | (u32(d[p + 1]) << 8) | (u32(d[p + 2]) << 16);
-  return (v * 2654435761u) >> 19;
-}
 __device__ __forceinline__ u32 length_symbol(u32 len) {  // index 0..28 for 3..258
   if (len == 258) return 28;
   if (len <= 10) return len - 3;
@@ -88,42 +90,55 @@ struct EncodeShared {
   u16 codes[336];
   u32 weight[576];
   u16 parent[576];
+  u16 ancestor[2][576];
   u16 sorted[288];
-  u8 depth[576];
+  u32 leafw[288];      // weights in leaf rank order
+  u8 depth[2][576];
   u8 rle_sym[320];
   u8 rle_extra[320];
+  u16 owned[kEncWarps][kRing];  // per-warp ring of positions awaiting a batch
   u32 seg_exit[kEncThreads];
+  u32 seg_entry[kEncThreads];
   u32 seg_bits[kEncThreads];
-  u32 warp_sums[kEncThreads / 32];
-  u64 adler_s1[kEncThreads / 32];
-  u64 adler_s2[kEncThreads / 32];
+  u32 warp_sums[kEncWarps];
+  u64 adler_s1[kEncWarps];
+  u64 adler_s2[kEncWarps];
   u32 extra_bits, token_count, dist_tokens;
-  u32 mode, extent, status, ok, nll, ndist, ncl, rle_size, header_bits, leaves;
+  u32 mode, extent, status, ok, nll, ndist, ncl, rle_size, header_bits, leaves, only;
+  u32 first_fail, more, lcount[16];
 };
 
 // Two-queue Huffman build with the reference's (weight, id) order and
-// flattening retries.  All threads call; thread 0 merges.  Returns on all
-// threads whether a tree within `limit` was found.
+// flattening retries.  All threads call; the merge itself runs on thread 0
+// with both queue heads in registers, and everything around it (leaf
+// ranking, depths by pointer doubling, length counts, canonical codes) is
+// spread over the block.  Returns on all threads whether a tree within
+// `limit` was found.
 __device__ bool cta_tree(EncodeShared& s, const u32* freq, u32 alphabet, u32 limit, u8* lengths,
                          u16* codes) {
   const u32 tid = threadIdx.x;
   for (u32 shift = 0; shift <= 16; ++shift) {
+    if (tid == 0) { s.leaves = 0; s.only = 0; }
+    if (tid < 16) s.lcount[tid] = 0;
+    __syncthreads();
     for (u32 i = tid; i < alphabet; i += kEncThreads) {
       lengths[i] = 0;
       codes[i] = 0;
-      s.weight[i] = freq[i] ? ((freq[i] + (1u << shift) - 1u) >> shift) : 0u;
+      const u32 w = freq[i] ? ((freq[i] + (1u << shift) - 1u) >> shift) : 0u;
+      s.weight[i] = w;
+      if (w) {
+        atomicAdd(&s.leaves, 1u);
+        atomicMax(&s.only, i);
+      }
     }
     __syncthreads();
     if (tid == 0) {
-      // Leaf set, with the reference's dummy leaves for empty and one-symbol
-      // alphabets (a complete tree is always produced).
-      u32 m = 0, only = 0;
-      for (u32 i = 0; i < alphabet; ++i)
-        if (s.weight[i]) { ++m; only = i; }
+      // The reference's dummy leaves for empty and one-symbol alphabets (a
+      // complete tree is always produced).
+      u32 m = s.leaves, only = s.only;
       if (!m) { s.weight[0] = 1; m = 1; only = 0; }
       if (m == 1) {
-        const u32 dummy = only ? 0u : 1u;
-        s.weight[dummy] = 1;
+        s.weight[only ? 0u : 1u] = 1;
         m = 2;
       }
       s.leaves = m;
@@ -139,58 +154,81 @@ __device__ bool cta_tree(EncodeShared& s, const u32* freq, u32 alphabet, u32 lim
         rank += (v && (v < w || (v == w && j < i))) ? 1u : 0u;
       }
       s.sorted[rank] = u16(i);
+      s.leafw[rank] = w;
     }
     __syncthreads();
+    const u32 m = s.leaves;
+    const u32 nodes = alphabet + m - 1;  // leaves' ids stay below alphabet
     if (tid == 0) {
-      const u32 m = s.leaves;
+      // Leaf ids are below every inner id, so equal weights take the leaf.
       u32 leaf = 0, inner = alphabet, next = alphabet;
+      u32 leaf_id = s.sorted[0], leaf_w = s.leafw[0], inner_w = 0;
       for (u32 step = 0; step + 1 < m; ++step) {
-        u32 pick[2];
+        u32 pick[2], picked_w[2];
         for (u32 k = 0; k < 2; ++k) {
-          bool take_leaf;
-          if (leaf >= m) take_leaf = false;
-          else if (inner == next) take_leaf = true;
-          else {
-            const u32 a = s.sorted[leaf];
-            const u32 wa = s.weight[a], wb = s.weight[inner];
-            take_leaf = wa < wb || (wa == wb && a < inner);
+          const bool take_leaf = leaf < m && (inner == next || leaf_w <= inner_w);
+          if (take_leaf) {
+            pick[k] = leaf_id;
+            picked_w[k] = leaf_w;
+            if (++leaf < m) { leaf_id = s.sorted[leaf]; leaf_w = s.leafw[leaf]; }
+          } else {
+            pick[k] = inner;
+            picked_w[k] = inner_w;
+            if (++inner < next) inner_w = s.weight[inner];
           }
-          pick[k] = take_leaf ? u32(s.sorted[leaf++]) : inner++;
         }
-        s.weight[next] = s.weight[pick[0]] + s.weight[pick[1]];
+        const u32 w = picked_w[0] + picked_w[1];
+        s.weight[next] = w;
         s.parent[pick[0]] = u16(next);
         s.parent[pick[1]] = u16(next);
+        if (inner == next) inner_w = w;
         ++next;
       }
-      // Depths from the root down (parents are created after children).
-      const u32 root = next - 1;
-      s.depth[root] = 0;
-      for (u32 node = root; node-- > alphabet;) s.depth[node] = s.depth[s.parent[node]] + 1;
-      u32 overlong = 0;
-      u32 count[16];
-      for (u32 l = 0; l < 16; ++l) count[l] = 0;
-      for (u32 i = 0; i < alphabet; ++i) {
-        if (!s.weight[i]) continue;
-        const u32 d = s.depth[s.parent[i]] + 1u;
-        if (d > limit) { overlong = 1; continue; }
-        lengths[i] = u8(d);
-        ++count[d];
-      }
-      if (!overlong) {
-        u32 first[16];
-        u32 code = 0;
-        first[0] = 0;
-        for (u32 b = 1; b <= limit; ++b) {
-          code = (code + count[b - 1]) << 1;
-          first[b] = code;
-        }
-        for (u32 i = 0; i < alphabet; ++i)
-          if (lengths[i]) codes[i] = u16(reverse_bits(first[lengths[i]]++, lengths[i]));
-      }
-      s.ok = overlong ? 0u : 1u;
     }
     __syncthreads();
-    if (s.ok) return true;
+    // Depth of every node by pointer doubling towards the root.
+    const u32 root = nodes - 1;
+    for (u32 i = tid; i < nodes; i += kEncThreads) {
+      const bool live = i >= alphabet || s.weight[i];
+      const bool top = i == root || !live;
+      s.ancestor[0][i] = u16(top ? root : s.parent[i]);
+      s.depth[0][i] = top ? 0 : 1;
+    }
+    u32 cur = 0;
+    for (;;) {
+      __syncthreads();
+      bool moved = false;
+      for (u32 i = tid; i < nodes; i += kEncThreads) {
+        const u32 up = s.ancestor[cur][i];
+        s.depth[cur ^ 1][i] = u8(s.depth[cur][i] + (up == root ? 0u : s.depth[cur][up]));
+        s.ancestor[cur ^ 1][i] = up == root ? u16(root) : s.ancestor[cur][up];
+        moved |= up != root;
+      }
+      cur ^= 1;
+      if (!__syncthreads_or(moved)) break;
+    }
+    bool overlong = false;
+    for (u32 i = tid; i < alphabet; i += kEncThreads) {
+      if (!s.weight[i]) continue;
+      const u32 d = s.depth[cur][i];
+      if (d > limit) { overlong = true; continue; }
+      lengths[i] = u8(d);
+      atomicAdd(&s.lcount[d], 1u);
+    }
+    if (__syncthreads_or(overlong)) continue;
+    // Canonical codes: first code of each length, then the rank of a symbol
+    // among the lower symbols of its length.
+    for (u32 i = tid; i < alphabet; i += kEncThreads) {
+      const u32 len = lengths[i];
+      if (!len) continue;
+      u32 code = 0;  // lcount[0] is zero: no leaf sits at the root
+      for (u32 b = 1; b <= len; ++b) code = (code + s.lcount[b - 1]) << 1;
+      u32 rank = 0;
+      for (u32 j = 0; j < i; ++j) rank += lengths[j] == len ? 1u : 0u;
+      codes[i] = u16(reverse_bits(code + rank, len));
+    }
+    __syncthreads();
+    return true;
   }
   return false;
 }
@@ -235,6 +273,24 @@ struct Packer {
   }
 };
 
+// Calls f(p, is_match) for every token start p in [a, b), in order, reading
+// the membership and match bitmaps a word at a time.
+template <class F>
+__device__ __forceinline__ void for_each_token(const u32* member, const u32* ismatch, u32 a,
+                                               u32 b, F f) {
+  for (u32 lo = a & ~31u; lo < b; lo += 32) {
+    u32 bits = member[lo >> 5];
+    const u32 matches = ismatch[lo >> 5];
+    if (lo < a) bits &= ~0u << (a - lo);
+    if (b - lo < 32) bits &= (1u << (b - lo)) - 1u;
+    while (bits) {
+      const u32 k = __ffs(bits) - 1;
+      bits &= bits - 1;
+      f(lo + k, ((matches >> k) & 1u) != 0);
+    }
+  }
+}
+
 // Slot of chunk g: starts at 16-aligned (input position + 96 g), so a slot
 // holds at least n + 80 bytes and all slots fit in in_bytes + 96 (chunks+1).
 __device__ __forceinline__ u64 slot_start(u64 in_pos, u32 g) {
@@ -277,7 +333,9 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
     prev = table + kHashSlots;
     lenv = reinterpret_cast<u8*>(prev + ((chunk_bytes + 7) & ~7u));
   } else {
-    const u64 at = f.in_offset + start + 16 * u64(g);
+    // 16-byte aligned (lenv is read as words); at + n stays below the
+    // in_bytes + 16 * (chunks + 2) spill entries.
+    const u64 at = ((f.in_offset + start + 15) & ~u64(15)) + 16 * u64(g);
     prev = spill_prev + at;
     lenv = spill_len + at;
   }
@@ -302,28 +360,81 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
   __syncthreads();
   if (tid == 0) {
     u64 a = 0, b = 0;
-    for (u32 w = 0; w < kEncThreads / 32; ++w) { a += s.adler_s1[w]; b += s.adler_s2[w]; }
+    for (u32 w = 0; w < kEncWarps; ++w) { a += s.adler_s1[w]; b += s.adler_s2[w]; }
     adler[2 * u64(g)] = a;
     adler[2 * u64(g) + 1] = b;
   }
 
   // 2. Candidates: prev[p] = 1 + last earlier position with hash(p), or 0.
+  // First every position's hash goes to prev[p] (its low byte also to
+  // lenv[p]).  Then warp w handles the table slots h with h % 8 == w: it
+  // gathers the positions it owns in order into batches of 32 and, per
+  // batch, finds equal hashes among the lanes by ballots over the hash bits.
+  // A lane's candidate is its last earlier equal lane, else the table; the
+  // last lane of each hash writes the table.  Slots are disjoint between
+  // warps, so the eight warps never wait on one another.
   const u32 hashed = n >= 3 ? n - 2 : 0;  // positions 0..n-3 are hashed
-  if (warp == 0) {
-    for (u32 base = 0; base < hashed; base += 32) {
-      const u32 p = base + lane;
-      const bool valid = p < hashed;
-      const u32 h = valid ? hash3(data, p) : (kHashSlots + lane);
-      const u32 group = __match_any_sync(kFullMask, h);
-      const u32 lower = group & ((1u << lane) - 1u);
-      u32 candidate = 0;
-      if (valid) candidate = lower ? base + (31 - __clz(lower)) + 1 : table[h];
-      __syncwarp();
-      const u32 higher = lane == 31 ? 0u : (group >> (lane + 1));
-      if (valid && !higher) table[h] = u16(p + 1);
-      if (valid) prev[p] = u16(candidate);
-      __syncwarp();
+  {
+    const u32* words = reinterpret_cast<const u32*>(data);
+    for (u32 p = tid; p < hashed; p += kEncThreads) {
+      const u32 lo = words[p >> 2], hi = words[(p >> 2) + 1];
+      const u32 v = __funnelshift_r(lo, hi, (p & 3u) * 8u) & 0xffffffu;
+      const u32 h = (v * 2654435761u) >> 19;
+      prev[p] = u16(h);
+      lenv[p] = u8(h);
     }
+    __syncthreads();
+    u16* ring = s.owned[warp];
+    u32 head = 0, fill = 0;
+    auto batch = [&](u32 count) {
+      const bool valid = lane < count;
+      const u32 pos = valid ? ring[(head + lane) & (kRing - 1)] : 0u;
+      const u32 h = valid ? prev[pos] : 0u;
+      const u32 key = h >> kOwnerBits;  // the low bits equal the warp index
+      u32 same = __ballot_sync(kFullMask, valid);
+      for (u32 bit = 0; bit < 13 - kOwnerBits; ++bit) {
+        const u32 ones = __ballot_sync(kFullMask, valid && ((key >> bit) & 1u));
+        same &= ((key >> bit) & 1u) ? ones : ~ones;
+      }
+      const u32 lower = same & ((1u << lane) - 1u);
+      const u32 from = __shfl_sync(kFullMask, pos, lower ? 31 - __clz(lower) : lane);
+      u32 candidate = 0;
+      if (valid) candidate = lower ? from + 1 : table[h];
+      __syncwarp();
+      if (valid) {
+        if (!(same & ~((2u << lane) - 1u))) table[h] = u16(pos + 1);
+        prev[pos] = u16(candidate);
+      }
+      __syncwarp();
+      head = (head + count) & (kRing - 1);
+    };
+    // Lane i looks at positions base + 4i .. base + 4i + 3 (one word of
+    // lenv); a position's rank among the owned ones follows from four
+    // ballots, one per byte of the word.
+    const u32* low_bytes = reinterpret_cast<const u32*>(lenv);
+    const u32 below = (1u << lane) - 1u;
+    for (u32 base = 0; base < hashed; base += 128) {
+      const u32 p0 = base + 4 * lane;
+      const u32 word = p0 < hashed ? low_bytes[p0 >> 2] : 0u;
+      u32 own[4], before = 0, total = 0;
+      for (u32 k = 0; k < 4; ++k) {
+        own[k] = (p0 + k < hashed && ((word >> (8 * k)) & (kEncWarps - 1)) == warp) ? 1u : 0u;
+        const u32 ballot = __ballot_sync(kFullMask, own[k]);
+        before += __popc(ballot & below);
+        total += __popc(ballot);
+      }
+      for (u32 k = 0; k < 4; ++k) {
+        if (own[k]) ring[(head + fill + before) & (kRing - 1)] = u16(p0 + k);
+        before += own[k];
+      }
+      fill += total;
+      __syncwarp();
+      while (fill >= 32) {
+        batch(32);
+        fill -= 32;
+      }
+    }
+    if (fill) batch(fill);
   }
   __syncthreads();
 
@@ -360,26 +471,90 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
   }
   __syncthreads();
 
-  // 4. Stitch the segments in order.
+  // 4. Stitch.  The true entry of a segment is the first token boundary at
+  // or after its start on the chain from position 0.  A re-walk from a wrong
+  // start meets the true chain within a token or two, so assume every
+  // segment's re-walk merges into its speculative chain: then each entry
+  // follows from the speculative exits alone (thread 0, a scan of 256
+  // values), every segment checks its assumption in parallel, and segments
+  // before the first failed check apply their re-walk in parallel.  From the
+  // first failure on, segments are stitched in order as a fallback.
+  auto is_member = [&](u32 p) { return ((member[p >> 5] >> (p & 31)) & 1u) != 0; };
+  auto clear_members = [&](u32 from, u32 to) {  // member bits of [from, to)
+    while (from < to) {
+      const u32 word = from >> 5, lo = from & 31u;
+      const u32 hi = min_u32(to - (from & ~31u), 32u);
+      const u32 mask = (hi == 32 ? ~0u : ((1u << hi) - 1u)) & ~((1u << lo) - 1u);
+      atomicAnd(&member[word], ~mask);
+      from = (from & ~31u) + hi;
+    }
+  };
+  const u32 nseg = seg ? (n + seg - 1) / seg : 0;
   if (tid == 0) {
-    u32 entry = 0;
-    for (u32 t = 0; t < kEncThreads; ++t) {
-      const u32 a = min_u32(t * seg, n), b = min_u32(a + seg, n);
-      if (a >= b) break;
+    u32 exit = nseg ? s.seg_exit[0] : 0;
+    for (u32 t = 1; t < nseg; ++t) {
+      s.seg_entry[t] = exit;
+      const u32 b_t = min_u32((t + 1) * seg, n);
+      if (exit < b_t) exit = s.seg_exit[t];
+    }
+    s.first_fail = nseg;
+  }
+  __syncthreads();
+  const u32 my_a = min_u32(tid * seg, n), my_b = min_u32(my_a + seg, n);
+  u32 merge_at = my_b;
+  if (tid > 0 && tid < nseg) {
+    const u32 entry = s.seg_entry[tid];
+    if (entry < my_b) {
+      u32 p = entry;
+      while (p < my_b && !is_member(p)) {
+        const u32 m = token_at(p);
+        p += m ? m : 1u;
+      }
+      merge_at = p;
+      if (p >= my_b) atomicMin(&s.first_fail, tid);
+    }
+  }
+  __syncthreads();
+  if (tid > 0 && tid < s.first_fail) {
+    const u32 entry = s.seg_entry[tid];
+    if (entry >= my_b) {
+      clear_members(my_a, my_b);  // one earlier token covers the segment
+    } else {
+      clear_members(my_a, entry);
+      for (u32 p = entry; p < merge_at;) {
+        const u32 m = token_at(p);
+        atomicOr(&member[p >> 5], 1u << (p & 31));
+        if (m) {
+          atomicOr(&ismatch[p >> 5], 1u << (p & 31));
+          lenv[p] = u8(m - 3);
+          clear_members(p + 1, min_u32(p + m, my_b));
+          p += m;
+        } else {
+          atomicAnd(&ismatch[p >> 5], ~(1u << (p & 31)));
+          ++p;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (tid == 0 && s.first_fail < nseg) {
+    const u32 f = s.first_fail;
+    u32 entry = s.seg_entry[f];
+    for (u32 t = f; t < nseg; ++t) {
+      const u32 a = t * seg, b = min_u32(a + seg, n);
       if (entry >= b) {
-        // The previous token covers this whole segment.
-        for (u32 p = a; p < b; ++p) member[p >> 5] &= ~(1u << (p & 31));
+        clear_members(a, b);
         continue;
       }
-      for (u32 p = a; p < entry; ++p) member[p >> 5] &= ~(1u << (p & 31));
+      clear_members(a, entry);
       u32 p = entry;
-      while (p < b && !((member[p >> 5] >> (p & 31)) & 1u)) {
+      while (p < b && !is_member(p)) {
         const u32 m = token_at(p);
         member[p >> 5] |= 1u << (p & 31);
         if (m) {
           ismatch[p >> 5] |= 1u << (p & 31);
           lenv[p] = u8(m - 3);
-          for (u32 k = p + 1; k < p + m && k < b; ++k) member[k >> 5] &= ~(1u << (k & 31));
+          clear_members(p + 1, min_u32(p + m, b));
           p += m;
         } else {
           ismatch[p >> 5] &= ~(1u << (p & 31));
@@ -395,20 +570,19 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
   const u32 a = min_u32(tid * seg, n), b = min_u32(a + seg, n);
   {
     u32 extra = 0, tokens = 0, dists = 0;
-    for (u32 p = a; p < b; ++p) {
-      if (!((member[p >> 5] >> (p & 31)) & 1u)) continue;
+    for_each_token(member, ismatch, a, b, [&](u32 p, bool match) {
       ++tokens;
-      if ((ismatch[p >> 5] >> (p & 31)) & 1u) {
+      if (match) {
         const u32 m = u32(lenv[p]) + 3, dist = p - (u32(prev[p]) - 1);
         const u32 li = length_symbol(m), di = dist_symbol(dist);
         atomicAdd(&s.freq[257 + li], 1u);
         atomicAdd(&s.freq[286 + di], 1u);
-        extra += kLenExtra[li] + kDistExtra[di];
+        extra += length_extra_bits(li) + dist_extra_bits(di);
         ++dists;
       } else {
         atomicAdd(&s.freq[data[p]], 1u);
       }
-    }
+    });
     atomicAdd(&s.extra_bits, extra);
     atomicAdd(&s.token_count, tokens);
     atomicAdd(&s.dist_tokens, dists);
@@ -528,17 +702,16 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
   // 8. Parallel bit packing.
   const bool dyn = mode == 2;
   u32 my_bits = 0;
-  for (u32 p = a; p < b; ++p) {
-    if (!((member[p >> 5] >> (p & 31)) & 1u)) continue;
-    if ((ismatch[p >> 5] >> (p & 31)) & 1u) {
+  for_each_token(member, ismatch, a, b, [&](u32 p, bool match) {
+    if (match) {
       const u32 m = u32(lenv[p]) + 3, dist = p - (u32(prev[p]) - 1);
       const u32 li = length_symbol(m), di = dist_symbol(dist);
-      my_bits += (dyn ? s.lengths[257 + li] : fixed_ll_len(257 + li)) + kLenExtra[li] +
-                 (dyn ? s.lengths[286 + di] : 5u) + kDistExtra[di];
+      my_bits += (dyn ? s.lengths[257 + li] : fixed_ll_len(257 + li)) + length_extra_bits(li) +
+                 (dyn ? s.lengths[286 + di] : 5u) + dist_extra_bits(di);
     } else {
       my_bits += dyn ? s.lengths[data[p]] : fixed_ll_len(data[p]);
     }
-  }
+  });
   // Header size.
   if (tid == 0) {
     u32 hb = 3;
@@ -566,7 +739,7 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
   u32 before = 0;
   for (u32 w = 0; w < warp; ++w) before += s.warp_sums[w];
   u32 body_bits = 0;
-  for (u32 w = 0; w < kEncThreads / 32; ++w) body_bits += s.warp_sums[w];
+  for (u32 w = 0; w < kEncWarps; ++w) body_bits += s.warp_sums[w];
   const u32 header_bits = s.header_bits;
   const u32 my_start = header_bits + before + incl - my_bits;
   if (tid == 0) {
@@ -591,23 +764,24 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
   {
     Packer pk;
     pk.start(words, my_start, my_start + my_bits, used_words);
-    for (u32 p = a; p < b; ++p) {
-      if (!((member[p >> 5] >> (p & 31)) & 1u)) continue;
-      if ((ismatch[p >> 5] >> (p & 31)) & 1u) {
+    for_each_token(member, ismatch, a, b, [&](u32 p, bool match) {
+      if (match) {
         const u32 m = u32(lenv[p]) + 3, dist = p - (u32(prev[p]) - 1);
         const u32 li = length_symbol(m), di = dist_symbol(dist);
         if (dyn) pk.put(s.codes[257 + li], s.lengths[257 + li]);
         else pk.put(fixed_ll_code(257 + li), fixed_ll_len(257 + li));
-        pk.put(m - kLenBase[li], kLenExtra[li]);
+        const u32 le = length_extra_bits(li);
+        pk.put(low_bits(m - 3, le), le);
         if (dyn) pk.put(s.codes[286 + di], s.lengths[286 + di]);
         else pk.put(reverse_bits(di, 5), 5);
-        pk.put(dist - kDistBase[di], kDistExtra[di]);
+        const u32 de = dist_extra_bits(di);
+        pk.put(low_bits(dist - 1, de), de);
       } else {
         const u32 lit = data[p];
         if (dyn) pk.put(s.codes[lit], s.lengths[lit]);
         else pk.put(fixed_ll_code(lit), fixed_ll_len(lit));
       }
-    }
+    });
     pk.finish();
   }
   if (tid == kEncThreads - 1) {
