@@ -363,7 +363,9 @@ __device__ inline void warp_build_fixed(Tables& t) {
 }
 
 // Rendezvous actions: lane 0 parses, then the whole warp performs one action.
-enum Action : u32 { kNone = 0, kStored = 1, kCopy = 2, kDynamic = 3, kFlush = 4, kFixed = 5 };
+enum Action : u32 {
+  kNone = 0, kStored = 1, kCopy = 2, kDynamic = 3, kFlush = 4, kFixed = 5, kRound = 6
+};
 
 // Copy the decode part of the fixed tables (literal/length and distance)
 // into a warp's shared-memory tables, so hot loops only read shared memory.

@@ -44,8 +44,217 @@ constexpr u32 kEmitMask = kEmitRing - 1;
 constexpr u32 kEmitFlush = 2048;   // pending symbols that trigger a flush
 constexpr u32 kInfoFinal = 1u, kInfoOk = 2u;
 
+// ---------------------------------------------------------------------------
+// Lane-parallel rounds over a Huffman block body.
+// ---------------------------------------------------------------------------
+// A round gives lane j the window [start + jW, start + (j+1)W) of the body.
+// Lane 0 starts on the true token chain; the others start at an arbitrary
+// bit and decode speculatively (phase 1), marking where their tokens start.
+// Huffman decoding resynchronizes: a lane that runs on past its window
+// (phase 2) soon lands on a position some later lane marked, and from there
+// that lane's chain is its own.  Lane 0 links the lanes in order from the
+// true start, which gives each lane a region between two boundaries known to
+// be on the true chain; phase 3 decodes every region again, now exactly.  A
+// code the exact decoder must judge (or too few bits left) ends the round at
+// that token, and the serial decoder carries on from there, so statuses
+// stay the serial decoder's.  On config-1 streams half the lanes resynchronize
+// within 64 bits and the share left halves every further 64 bits, so a
+// whole window of marks almost never runs out.
+constexpr u32 kRoundWindow = 1024;  // body bits per lane per round
+constexpr u32 kMarkWords = kRoundWindow / 32;
+
+enum LaneEnd : u32 {
+  kLaneWindow = 0,     // reached the window end / a boundary past the round
+  kLaneBlockEnd = 1,   // end-of-block code at the recorded position
+  kLaneIrregular = 2,  // a token for the serial decoder at the recorded position
+  kLaneMerged = 3,     // landed on a later lane's mark
+};
+enum RoundOutcome : u32 { kRoundMore = 0, kRoundBlockEnd = 1, kRoundFallback = 2 };
+
+struct RoundShared {
+  u32 marks[32][kMarkWords];
+  u32 stop[32];      // phase 1: kLaneWindow or where and why it stopped early
+  u32 stop_at[32];
+  u32 link[32];      // phase 2: kLaneMerged / kLaneWindow (past the round) / stop
+  u32 link_at[32];   // position reached
+  u32 link_to[32];   // lane merged with
+  u32 region_from[32], region_to[32], region_end[32];  // set by the walk
+};
+
+// One token.  Returns kLaneWindow (decoded, *bytes output bytes),
+// kLaneBlockEnd (end-of-block code, consumed) or kLaneIrregular (a code the
+// serial decoder must judge, a distance beyond the window, or fewer than 48
+// body bits left, so every token taken here lies wholly inside the body;
+// nothing consumed that matters).
+__device__ __forceinline__ u32 count_token(Bits& c, const Tables& t, u32 window, u32* bytes) {
+  if (c.avail() < 48) return kLaneIrregular;
+  c.refill();
+  u32 v = c.lo;
+  u32 e = t.ll.lut[v & kLLMask];
+  u32 kind = entry_kind(e);
+  if (kind == kLong) {
+    e = decode_long(t.ll, v, LLFn());
+    kind = entry_kind(e);
+  }
+  if (kind == kLiteral) {
+    c.consume(entry_len(e));
+    *bytes = 1;
+    return kLaneWindow;
+  }
+  if (kind == kEnd) {
+    c.consume(entry_len(e));
+    return kLaneBlockEnd;
+  }
+  if (kind != kLength) return kLaneIrregular;
+  const u32 L = entry_len(e), E = entry_extra(e);
+  const u32 length = entry_value(e) + ((v >> L) & ((1u << E) - 1u));
+  c.consume(L + E);
+  c.refill();
+  v = c.lo;
+  u32 d = t.d.lut[v & 255u];
+  u32 dk = entry_kind(d);
+  if (dk == kLong) {
+    d = decode_long(t.d, v, DFn());
+    dk = entry_kind(d);
+  }
+  if (dk != kLiteral) return kLaneIrregular;
+  const u32 Ld = entry_len(d), Ed = entry_extra(d);
+  const u32 span = entry_value(d) + ((v >> Ld) & ((1u << Ed) - 1u));
+  if (span > window) return kLaneIrregular;
+  c.consume(Ld + Ed);
+  *bytes = length;
+  return kLaneWindow;
+}
+
+struct RoundResult {
+  u32 pos, bytes, outcome;
+};
+
+// One round from the token boundary `start` (the same on every lane).  On
+// lane 0: the committed position, the output bytes before it and whether
+// the block continues, ended (position after its end-of-block code) or
+// goes to the serial decoder at that position.
+__device__ RoundResult warp_round(const u8* body, u32 body_bytes, u32 start, u32 window,
+                                  const Tables& t, RoundShared& r) {
+  const u32 lane = threadIdx.x & 31u;
+  const u32 s = start + lane * kRoundWindow, wend = s + kRoundWindow;
+  const u32 round_end = start + 32 * kRoundWindow;
+  u32* my_marks = r.marks[lane];
+  for (u32 k = 0; k < kMarkWords; ++k) my_marks[k] = 0;
+  Bits c;
+  c.init(body, body_bytes);
+  // Phase 1: speculative decode of the window, marking token starts.
+  u32 stop = kLaneIrregular, stop_at = s;
+  if (s < c.end) {
+    c.seek(s);
+    for (;;) {
+      const u32 p = c.pos();
+      if (p >= wend) {
+        stop = kLaneWindow;
+        stop_at = p;
+        break;
+      }
+      my_marks[(p - s) >> 5] |= 1u << ((p - s) & 31);
+      u32 bytes = 0;
+      const u32 st = count_token(c, t, window, &bytes);
+      if (st != kLaneWindow) {
+        stop = st;
+        stop_at = p;
+        break;
+      }
+    }
+  }
+  r.stop[lane] = stop;
+  r.stop_at[lane] = stop_at;
+  __syncwarp();
+  // Phase 2: run on until landing on a later lane's mark (or past the round).
+  u32 link = stop, link_at = stop_at, link_to = lane;
+  if (stop == kLaneWindow) {
+    for (;;) {
+      const u32 p = c.pos();
+      if (p >= round_end) {
+        link = kLaneWindow;
+        link_at = p;
+        break;
+      }
+      const u32 to = (p - start) / kRoundWindow, off = p - (start + to * kRoundWindow);
+      if ((r.marks[to][off >> 5] >> (off & 31)) & 1u) {
+        link = kLaneMerged;
+        link_at = p;
+        link_to = to;
+        break;
+      }
+      u32 bytes = 0;
+      const u32 st = count_token(c, t, window, &bytes);
+      if (st != kLaneWindow) {
+        link = st;
+        link_at = p;
+        break;
+      }
+    }
+  }
+  r.link[lane] = link;
+  r.link_at[lane] = link_at;
+  r.link_to[lane] = link_to;
+  r.region_to[lane] = 0;
+  r.region_end[lane] = kLaneIrregular;
+  r.region_from[lane] = 1;  // empty region (from > to)
+  __syncwarp();
+  // Walk: the true chain from lane 0, lane to lane.
+  if (lane == 0) {
+    u32 j = 0, from = start;
+    for (;;) {
+      r.region_from[j] = from;
+      const u32 kind = r.link[j];
+      r.region_to[j] = r.link_at[j];
+      r.region_end[j] = kind;
+      if (kind != kLaneMerged) break;
+      from = r.link_at[j];
+      j = r.link_to[j];
+    }
+  }
+  __syncwarp();
+  // Phase 3: decode this lane's region exactly.
+  const u32 from = r.region_from[lane], to = r.region_to[lane], end = r.region_end[lane];
+  u32 total = 0, finish = to, broken = 0;
+  if (from <= to) {
+    c.seek(from);
+    // The same tokens phases 1 and 2 took; any other answer would be a
+    // decoder fault, and the round is then dropped.
+    while (c.pos() < to) {
+      u32 bytes = 0;
+      if (count_token(c, t, window, &bytes) != kLaneWindow) {
+        broken = 1;
+        break;
+      }
+      total += bytes;
+    }
+    if (!broken && c.pos() != to) broken = 1;
+    if (!broken && end == kLaneBlockEnd) {
+      u32 bytes = 0;
+      if (count_token(c, t, window, &bytes) != kLaneBlockEnd) broken = 1;
+      finish = c.pos();
+    }
+  }
+  for (u32 o = 16; o; o >>= 1) total += __shfl_xor_sync(kFullMask, total, o);
+  // The lane whose region ends the walk holds the round's end.
+  const u32 enders = __ballot_sync(kFullMask, from <= to && end != kLaneMerged);
+  RoundResult out{start, 0, kRoundFallback};
+  if (enders && !__any_sync(kFullMask, broken)) {
+    const u32 who = __ffs(enders) - 1;
+    const u32 outcome_end = __shfl_sync(kFullMask, end, who);
+    out.pos = __shfl_sync(kFullMask, finish, who);
+    out.bytes = total;
+    out.outcome = outcome_end == kLaneWindow ? kRoundMore
+                : outcome_end == kLaneBlockEnd ? kRoundBlockEnd : kRoundFallback;
+  }
+  __syncwarp();
+  return out;
+}
+
 struct DescribeShared {
   Tables dyn[kNodeWarps];
+  RoundShared round[kNodeWarps];
 };
 struct EmitShared {
   Tables dyn[kEmitWarps];
@@ -174,13 +383,14 @@ __device__ __forceinline__ u32 flushed_symbol(const u8* out, const u32* source,
 template <bool kEmit>
 __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expected, u32 window,
                                 const Tables& fixed, Tables& dyn, u16* ring, u8* out,
-                                u32* source, u32* unresolved, u32 prefix) {
+                                u32* source, u32* unresolved, u32 prefix, RoundShared* rounds) {
   const u32 lane = threadIdx.x & 31u;
   NodeResult r{start, 0, 0, 0};
   Bits c;
   u32 produced = 0, flushed = 0, final = 0, blocks = 0, full_words = 0;
   u32 fail = 0, stop = 0;
   bool need_header = true;
+  bool parallel = false;  // this block's body goes through lane-parallel rounds
   if (lane == 0) {
     c.init(body, bytes);
     c.seek(start);
@@ -223,6 +433,10 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
             continue;
           }
           action = type == 2 ? kDynamic : kFixed;
+          break;
+        }
+        if (parallel) {
+          action = kRound;
           break;
         }
         const Tables& t = dyn;
@@ -334,10 +548,39 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
     if (action == kDynamic) {
       const u32 st = warp_dynamic_header(c, dyn);
       if (st) { fail = 1; break; }
-      if (lane == 0) need_header = false;
+      if (lane == 0) {
+        need_header = false;
+        parallel = rounds != nullptr;
+      }
     } else if (action == kFixed) {
       warp_load_fixed(dyn, fixed);
-      if (lane == 0) need_header = false;
+      if (lane == 0) {
+        need_header = false;
+        parallel = rounds != nullptr;
+      }
+    } else if (action == kRound) {
+      const u32 from = __shfl_sync(kFullMask, lane == 0 ? c.pos() : 0u, 0);
+      const RoundResult rr = warp_round(body, bytes, from, window, dyn, rounds[threadIdx.x >> 5]);
+      if (lane == 0) {
+        if (rr.outcome == kRoundFallback || rr.bytes > limit - produced) {
+          // The serial decoder takes the rest of the block from the last
+          // boundary known to be on the true chain (the round's start when
+          // the round would pass the output bound).
+          parallel = false;
+          if (rr.bytes <= limit - produced) {
+            produced += rr.bytes;
+            c.seek(rr.pos);
+          }
+        } else {
+          produced += rr.bytes;
+          c.seek(rr.pos);
+          if (rr.outcome == kRoundBlockEnd) {
+            need_header = true;
+            parallel = false;
+            if (final) stop = 1;
+          }
+        }
+      }
     } else if (kEmit && action == kFlush) {
       const u32 to = now;
       flush_symbols(ring, out, source, unresolved, prefix, flushed, to);
@@ -401,7 +644,7 @@ describe_kernel(const u8* in, u32 in_size, u64 expected, const u32* cands, const
     if (item >= count) break;
     const NodeResult r = warp_node<false>(in + 2, in_size - 6, cands[item], u32(expected), window,
                                           *fixed, sh.dyn[warp], nullptr, nullptr, nullptr,
-                                          nullptr, 0);
+                                          nullptr, 0, sh.round);
     if (lane == 0) {
       ends[item] = r.end;
       sizes[item] = r.size;
@@ -539,7 +782,7 @@ emit_kernel(const u8* in, u32 in_size, u64 expected, const u32* cands, const u32
     const u32 node = path[item];
     const NodeResult r = warp_node<true>(in + 2, in_size - 6, cands[node], u32(expected), window,
                                          *fixed, sh.dyn[warp], sh.ring[warp], out, source,
-                                         unresolved, prefix[item]);
+                                         unresolved, prefix[item], nullptr);
     if (lane == 0 && (!(r.info & kInfoOk) || r.size != sizes[node])) atomicOr(fail_flag, 1u);
   }
 }
