@@ -136,19 +136,24 @@ __device__ bool stored_seed(const u8* body, u64 bytes, u64 byte, u64* endpoint) 
 
 constexpr u32 kDiscoverTile = 4096;     // body bytes per CTA step
 constexpr u32 kDiscoverThreads = 256;   // each thread scans 16 consecutive bytes
+constexpr u32 kDiscoverQueue = 4096;    // prefiltered offsets awaiting validation per tile
 
 // Candidates of every body bit offset (discover, _decode_kernels.py:
 // 998-1054): bit 0; offsets whose three header bits are BTYPE 2 and whose
 // dynamic header is valid; stored-block endpoint seeds.  Sets bit b of
 // bitmap[b >> 5] per candidate offset and adds the raw event count
-// (duplicates included).  The tile and a 16-byte halo are staged in shared
-// memory; each byte's eight offsets share one 128-bit register window, and
-// the code-length code's completeness is prefiltered with a table of
-// Kraft sums of three packed 3-bit lengths before full validation.
+// (duplicates included).  Per tile (staged in shared memory with a 32-byte
+// halo), every thread first scans its 16 bytes' 128 offsets with cheap
+// filters: BTYPE 2, HLIT at most 29, and a complete code-length code (Kraft
+// sums of three packed 3-bit lengths from a table).  The few offsets that
+// pass go to a queue, and then the whole CTA validates queued headers one
+// per thread, instead of one lane validating while its warp waits.
 __global__ void __launch_bounds__(kDiscoverThreads)
 discover_kernel(const u8* in, u64 in_size, u32* bitmap, u32* count, const u32* gate) {
   __shared__ __align__(16) u8 tile[kDiscoverTile + 32];
   __shared__ u8 kraft3[512];
+  __shared__ u16 queue[kDiscoverQueue];  // tile-relative bit offsets
+  __shared__ u32 queued;
   if (gate && *gate) return;
   if (in_size < 8) return;
   const u8* body = in + 2;
@@ -167,6 +172,7 @@ discover_kernel(const u8* in, u64 in_size, u32* bitmap, u32* count, const u32* g
     __syncthreads();
     for (u32 j = threadIdx.x; j < kDiscoverTile + 32; j += blockDim.x)
       tile[j] = base + j < bytes ? body[base + j] : u8(0);
+    if (threadIdx.x == 0) queued = 0;
     __syncthreads();
     const u32 j0 = threadIdx.x * 16;
     // 128-bit window of the 16 bytes starting at byte j0 + k.
@@ -187,8 +193,11 @@ discover_kernel(const u8* in, u64 in_size, u32* bitmap, u32* count, const u32* g
         }
         // BTYPE 2 at offset b: bit b+1 clear, bit b+2 set.
         u32 mask = u32((~lo >> 1) & (lo >> 2)) & 0xffu;
-        u32 valid = byte == 0 ? 1u : 0u;
-        if (byte == 0) mask &= ~1u;
+        if (byte == 0) {
+          mask &= ~1u;
+          ++events;  // bit 0 is always a candidate
+          word_bits[k >> 2] |= 1u << ((k & 3) * 8);
+        }
         while (mask) {
           const u32 b = __ffs(mask) - 1;
           mask &= mask - 1;
@@ -206,11 +215,13 @@ discover_kernel(const u8* in, u64 in_size, u32* bitmap, u32* count, const u32* g
             y >>= 9;
           }
           if (kraft != 128) continue;
-          if (dynamic_header_valid(body, bytes, byte * 8 + b)) valid |= 1u << b;
-        }
-        if (valid) {
-          events += __popc(valid);
-          word_bits[k >> 2] |= valid << ((k & 3) * 8);
+          const u32 at = atomicAdd(&queued, 1u);
+          if (at < kDiscoverQueue) {
+            queue[at] = u16((j0 + k) * 8 + b);
+          } else if (dynamic_header_valid(body, bytes, byte * 8 + b)) {
+            ++events;  // queue full: validate here
+            word_bits[k >> 2] |= 1u << ((k & 3) * 8 + b);
+          }
         }
       }
       lo = (lo >> 8) | (hi << 56);
@@ -218,6 +229,15 @@ discover_kernel(const u8* in, u64 in_size, u32* bitmap, u32* count, const u32* g
     }
     for (u32 w = 0; w < 4; ++w)
       if (word_bits[w]) atomicOr(&bitmap[((base + j0) * 8 >> 5) + w], word_bits[w]);
+    __syncthreads();
+    const u32 pending = min_u32(queued, kDiscoverQueue);
+    for (u32 i = threadIdx.x; i < pending; i += kDiscoverThreads) {
+      const u64 bit = base * 8 + queue[i];
+      if (dynamic_header_valid(body, bytes, bit)) {
+        ++events;
+        atomicOr(&bitmap[bit >> 5], 1u << (bit & 31));
+      }
+    }
   }
   for (u32 o = 16; o; o >>= 1) events += __shfl_xor_sync(kFullMask, events, o);
   if ((threadIdx.x & 31) == 0 && events) atomicAdd(count, events);

@@ -71,8 +71,10 @@ enum LaneEnd : u32 {
 };
 enum RoundOutcome : u32 { kRoundMore = 0, kRoundBlockEnd = 1, kRoundFallback = 2 };
 
+// Mark rows are padded by a word: lanes work through their windows in near
+// lockstep, and rows 32 words apart would put them all in one bank.
 struct RoundShared {
-  u32 marks[32][kMarkWords];
+  u32 marks[32][kMarkWords + 1];
   u32 stop[32];      // phase 1: kLaneWindow or where and why it stopped early
   u32 stop_at[32];
   u32 link[32];      // phase 2: kLaneMerged / kLaneWindow (past the round) / stop
