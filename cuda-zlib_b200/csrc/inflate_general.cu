@@ -26,8 +26,11 @@ namespace cz {
 // Validity of a dynamic header at `start` (BTYPE 2 and dynamic_tables()==0;
 // dynamic_valid, _decode_kernels.py:359-366), per thread and without tables:
 // the code lengths are checked as they are decoded, so a random bit pattern
-// is usually rejected after a few symbols (an over-subscribed code).
-__device__ bool dynamic_header_valid(const u8* body, u64 bytes, u64 start) {
+// is usually rejected after a few symbols (an over-subscribed code).  The
+// code-length code is kept in registers and decoded through `lut`, 128
+// bytes of the caller's scratch; every rejection is the one the reference's
+// bitwise reads and checks make, in the same cases.
+__device__ bool dynamic_header_valid(const u8* body, u64 bytes, u64 start, u8* lut) {
   BitCursor c;
   c.init(body, bytes, start);
   u32 err = 0;
@@ -36,83 +39,95 @@ __device__ bool dynamic_header_valid(const u8* body, u64 bytes, u64 start) {
   if (err || type != 2) return false;
   const u32 nl = c.take(5, &err) + 257, nd = c.take(5, &err) + 1, nc = c.take(4, &err) + 4;
   if (err || nl > 286) return false;
-  const u8 order[19] = {16, 17, 18, 0, 8, 7, 9, 6, 10, 5, 11, 4, 12, 3, 13, 2, 14, 1, 15};
-  u8 clens[19];
-  for (u32 i = 0; i < 19; ++i) clens[i] = 0;
-  for (u32 i = 0; i < nc; ++i) clens[order[i]] = u8(c.take(3, &err));
-  if (err) return false;
+  // Code-length code lengths: 3 bits each, in the RFC 1951 order, read at once.
+  if (c.avail() < 3 * nc) return false;
+  const u64 fields = c.peek() & ((1ull << (3 * nc)) - 1);
+  c.skip(3 * nc);
+  // Position of symbol s in the transmission order 16 17 18 0 8 7 9 6 10 5 11 4 12 3 13 2 14 1 15.
+  constexpr u32 kOrderPos[19] = {3, 17, 15, 13, 11, 9, 7, 5, 4, 6, 8, 10, 12, 14, 16, 18, 0, 1, 2};
+  u32 clen[19];
+  u32 kraft = 0;
+#pragma unroll
+  for (u32 s = 0; s < 19; ++s) {
+    clen[s] = u32(fields >> (3 * kOrderPos[s])) & 7u;  // zero beyond nc: masked above
+    kraft += clen[s] ? 128u >> clen[s] : 0u;
+  }
   // Complete code-length code (Kraft sum exactly one, in units of 2^-7).
-  u32 kraft = 0, count[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  for (u32 i = 0; i < 19; ++i)
-    if (clens[i]) { kraft += 128u >> clens[i]; ++count[clens[i]]; }
   if (kraft != 128) return false;
-  // Canonical decode of the code lengths, bit by bit.
-  u32 first[8], offs[8];
-  u8 sorted[19];
-  {
-    u32 code = 0, off = 0;
-    count[0] = 0;
-    for (u32 l = 1; l < 8; ++l) {
-      code = (code + count[l - 1]) << 1;
-      first[l] = code;
-      offs[l] = off;
-      off += count[l];
+  // Canonical codes, then the 7-bit lookup: entry = symbol | length << 5.
+  u32 first = 0, prior = 0;
+#pragma unroll
+  for (u32 l = 1; l < 8; ++l) {
+    u32 count = 0;
+#pragma unroll
+    for (u32 s = 0; s < 19; ++s) count += clen[s] == l ? 1u : 0u;
+    first = (first + prior) << 1;  // first code of length l
+    u32 next = first;
+#pragma unroll
+    for (u32 s = 0; s < 19; ++s) {
+      if (clen[s] == l) {
+        const u32 lo = next << (7 - l), hi = (next + 1) << (7 - l);
+        for (u32 k = lo; k < hi; ++k) lut[k] = u8(s | (l << 5));
+        ++next;
+      }
     }
-    u32 cursor[8];
-    for (u32 l = 1; l < 8; ++l) cursor[l] = offs[l];
-    for (u32 i = 0; i < 19; ++i)
-      if (clens[i]) sorted[cursor[clens[i]]++] = u8(i);
+    prior = count;
   }
   // Literal/length lengths i < nl, distance lengths after; per part the
-  // Kraft sum (units of 2^-15), nonzero count and maximum.
-  u32 ksum[2] = {0, 0}, nonzero[2] = {0, 0}, maxlen[2] = {0, 0};
+  // Kraft sum (units of 2^-15), nonzero count and maximum.  Each code-length
+  // symbol and its extra bits come from one 64-bit peek; a symbol whose bits
+  // (code and extra) run past the body end fails as the bitwise reads would.
+  u32 ks0 = 0, ks1 = 0, nz0 = 0, nz1 = 0, mx0 = 0, mx1 = 0;
   u32 i = 0, previous = 0;
   bool eob = false;
   while (i < nl + nd) {
-    u32 code = 0, sym = 0xffffffffu;
-    for (u32 l = 1; l < 8; ++l) {
-      code = (code << 1) | c.take(1, &err);
-      if (err) return false;
-      if (code - first[l] < count[l]) { sym = sorted[offs[l] + code - first[l]]; break; }
-    }
-    if (sym == 0xffffffffu) return false;
-    u32 repeat = 1, value = sym;
+    const u64 w = c.peek();
+    const u64 avail = c.avail();
+    const u32 e = lut[__brev(u32(w)) >> 25];  // first 7 bits, MSB-first
+    const u32 sym = e & 31u, len = e >> 5;
+    if (len > avail) return false;
+    u32 repeat = 1, value = sym, extra = 0;
     if (sym == 16) {
       if (!i) return false;
-      repeat = c.take(2, &err) + 3;
+      extra = 2;
+      repeat = u32((w >> len) & 3u) + 3;
       value = previous;
     } else if (sym == 17) {
-      repeat = c.take(3, &err) + 3;
+      extra = 3;
+      repeat = u32((w >> len) & 7u) + 3;
       value = 0;
     } else if (sym == 18) {
-      repeat = c.take(7, &err) + 11;
+      extra = 7;
+      repeat = u32((w >> len) & 127u) + 11;
       value = 0;
     }
-    if (err || repeat > nl + nd - i) return false;
+    if (len + extra > avail) return false;
+    c.skip(len + extra);
+    if (repeat > nl + nd - i) return false;
     if (value) {
-      for (u32 j = 0; j < repeat; ++j, ++i) {
-        const u32 part = i < nl ? 0u : 1u;
-        ksum[part] += 32768u >> value;
-        ++nonzero[part];
-        if (value > maxlen[part]) maxlen[part] = value;
-        if (ksum[part] > 32768u) return false;  // over-subscribed
-        if (i == 256) eob = true;
-      }
-    } else {
-      i += repeat;
+      // The run [i, i + repeat) splits at most once at nl.  Kraft sums only
+      // grow, so checking after the run rejects exactly when some element
+      // of it would have over-subscribed.
+      const u32 n0 = i < nl ? min_u32(repeat, nl - i) : 0u, n1 = repeat - n0;
+      const u32 weight = 32768u >> value;
+      ks0 += n0 * weight;
+      ks1 += n1 * weight;
+      nz0 += n0;
+      nz1 += n1;
+      if (n0 && value > mx0) mx0 = value;
+      if (n1 && value > mx1) mx1 = value;
+      if (ks0 > 32768u || ks1 > 32768u) return false;  // over-subscribed
+      if (i <= 256 && 256 < i + repeat) eob = true;
     }
+    i += repeat;
     previous = value;
   }
   if (!eob) return false;
   // Literal/length: complete, or a single length-1 code.  Distance: empty,
   // complete, or a single length-1 code.
-  for (u32 part = 0; part < 2; ++part) {
-    if (!nonzero[part]) {
-      if (part == 0) return false;
-      continue;
-    }
-    if (ksum[part] != 32768u && !(maxlen[part] == 1 && nonzero[part] == 1)) return false;
-  }
+  if (!nz0) return false;
+  if (ks0 != 32768u && !(mx0 == 1 && nz0 == 1)) return false;
+  if (nz1 && ks1 != 32768u && !(mx1 == 1 && nz1 == 1)) return false;
   return true;
 }
 
@@ -154,6 +169,7 @@ discover_kernel(const u8* in, u64 in_size, u32* bitmap, u32* count, const u32* g
   __shared__ u8 kraft3[512];
   __shared__ u16 queue[kDiscoverQueue];  // tile-relative bit offsets
   __shared__ u32 queued;
+  __shared__ u8 cl_lut[kDiscoverThreads][128];  // per-thread code-length lookup
   if (gate && *gate) return;
   if (in_size < 8) return;
   const u8* body = in + 2;
@@ -218,7 +234,7 @@ discover_kernel(const u8* in, u64 in_size, u32* bitmap, u32* count, const u32* g
           const u32 at = atomicAdd(&queued, 1u);
           if (at < kDiscoverQueue) {
             queue[at] = u16((j0 + k) * 8 + b);
-          } else if (dynamic_header_valid(body, bytes, byte * 8 + b)) {
+          } else if (dynamic_header_valid(body, bytes, byte * 8 + b, cl_lut[threadIdx.x])) {
             ++events;  // queue full: validate here
             word_bits[k >> 2] |= 1u << ((k & 3) * 8 + b);
           }
@@ -233,7 +249,7 @@ discover_kernel(const u8* in, u64 in_size, u32* bitmap, u32* count, const u32* g
     const u32 pending = min_u32(queued, kDiscoverQueue);
     for (u32 i = threadIdx.x; i < pending; i += kDiscoverThreads) {
       const u64 bit = base * 8 + queue[i];
-      if (dynamic_header_valid(body, bytes, bit)) {
+      if (dynamic_header_valid(body, bytes, bit, cl_lut[threadIdx.x])) {
         ++events;
         atomicOr(&bitmap[bit >> 5], 1u << (bit & 31));
       }
