@@ -297,7 +297,8 @@ def run_gpu(args, rank, world):
     if world > 1:
         torch.distributed.barrier()
     kernels = {}
-    for name in ("serial_inflate_kernel", "discover_kernel", "describe_kernel", "emit_kernel",
+    for name in ("serial_inflate_kernel", "discover_kernel", "describe_kernel", "symbols_kernel",
+                 "expand_kernel",
                  "encode_chunks_kernel", "encode_pack_kernel"):
         total, launches = ctypes.c_double(), ctypes.c_uint64()
         lib.cuda_zlib_b200_profile_read(name.encode(), ctypes.byref(total), ctypes.byref(launches))
@@ -315,7 +316,8 @@ def run_gpu(args, rank, world):
     # Dominant kernel's roofline: algorithmic bytes (U + C per launch).
     algorithmic = {
         "serial_inflate_kernel": (U + len(l1), U + len(l6)),
-        "emit_kernel": (U + len(l1), U + len(l6)),
+        "symbols_kernel": (len(l1), len(l6)),
+        "expand_kernel": (U, U),
         "describe_kernel": (len(l1), len(l6)),
         "encode_chunks_kernel": (U + length,),
         "encode_pack_kernel": (2 * length,),

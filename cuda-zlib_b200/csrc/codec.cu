@@ -419,18 +419,21 @@ cudaError_t decompress(const u8* in, u64 size, int64_t max_candidates, int64_t m
   CZ_TRY(ws.allocate(&b.sizes, capacity));
   CZ_TRY(ws.allocate(&b.blocks, capacity));
   CZ_TRY(ws.allocate(&b.infos, capacity));
+  CZ_TRY(ws.allocate(&b.tokens, capacity));
   CZ_TRY(ws.allocate(&b.jump, (u64(capacity) + 2) * layout.levels));
   CZ_TRY(ws.allocate(&b.path, capacity));
   CZ_TRY(ws.allocate(&b.prefix, capacity));
+  CZ_TRY(ws.allocate(&b.tprefix, capacity));
+  CZ_TRY(ws.allocate(&b.syms, layout.symbol_words));
   CZ_TRY(ws.allocate(&b.state, 2));
-  CZ_TRY(ws.allocate(&b.counters, 2));
+  CZ_TRY(ws.allocate(&b.counters, 3));
   CZ_TRY(ws.allocate(&b.source, expected));
   CZ_TRY(ws.allocate(&b.unresolved, layout.out_words));
   CZ_TRY(ws.allocate(&b.parts, 2 * u64(layout.segments)));
   CZ_TRY(ws.allocate(&b.fail, 1));
   CZ_TRY(cudaMemsetAsync(b.bitmap, 0, layout.bitmap_words * sizeof(u32), stream));
   CZ_TRY(cudaMemsetAsync(count, 0, sizeof(u32), stream));
-  CZ_TRY(cudaMemsetAsync(b.counters, 0, 2 * sizeof(u32), stream));
+  CZ_TRY(cudaMemsetAsync(b.counters, 0, 3 * sizeof(u32), stream));
   CZ_TRY(cudaMemsetAsync(b.unresolved, 0, layout.out_words * sizeof(u32), stream));
   CZ_TRY(cudaMemsetAsync(b.fail, 0, sizeof(u32), stream));
   CZ_TRY(launch_discover(in, size, b.bitmap, count, nullptr, dev->info, stream));

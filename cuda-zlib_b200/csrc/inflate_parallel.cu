@@ -38,7 +38,7 @@
 namespace cz {
 
 constexpr u32 kNodeWarps = 4;      // warps per CTA in describe
-constexpr u32 kEmitWarps = 1;      // warps per CTA in emit (fine-grained residency)
+constexpr u32 kExpandWarps = 4;    // warps per CTA in expand
 constexpr u32 kEmitRing = 4096;    // u16 history entries per emitting warp
 constexpr u32 kEmitMask = kEmitRing - 1;
 constexpr u32 kEmitFlush = 2048;   // pending symbols that trigger a flush
@@ -128,16 +128,89 @@ __device__ __forceinline__ u32 count_token(Bits& c, const Tables& t, u32 window,
   return kLaneWindow;
 }
 
+// A node's tokens as the symbols kernel writes them: a literal byte;
+// kMatchFlag | distance << 9 | length; or kStoredFlag | length followed by a
+// word with the stored bytes' body offset.  Empty stored blocks write none.
+constexpr u32 kMatchFlag = 0x80000000u;
+constexpr u32 kStoredFlag = 0x40000000u;
+
 struct RoundResult {
-  u32 pos, bytes, outcome;
+  u32 pos, bytes, tokens, outcome;
 };
 
+// Token bits of a match.
+__device__ __forceinline__ u32 match_symbol(u32 length, u32 dist) {
+  return kMatchFlag | (dist << 9) | length;
+}
+
+// One token, as count_token, also returning its symbol word.
+__device__ __forceinline__ u32 symbol_token(Bits& c, const Tables& t, u32 window, u32* bytes,
+                                            u32* sym) {
+  if (c.avail() < 48) return kLaneIrregular;
+  c.refill();
+  u32 v = c.lo;
+  u32 e = t.ll.lut[v & kLLMask];
+  u32 kind = entry_kind(e);
+  if (kind == kLong) {
+    e = decode_long(t.ll, v, LLFn());
+    kind = entry_kind(e);
+  }
+  if (kind == kLiteral) {
+    c.consume(entry_len(e));
+    *bytes = 1;
+    *sym = entry_value(e);
+    return kLaneWindow;
+  }
+  if (kind == kEnd) {
+    c.consume(entry_len(e));
+    return kLaneBlockEnd;
+  }
+  if (kind != kLength) return kLaneIrregular;
+  const u32 L = entry_len(e), E = entry_extra(e);
+  const u32 length = entry_value(e) + ((v >> L) & ((1u << E) - 1u));
+  c.consume(L + E);
+  c.refill();
+  v = c.lo;
+  u32 d = t.d.lut[v & 255u];
+  u32 dk = entry_kind(d);
+  if (dk == kLong) {
+    d = decode_long(t.d, v, DFn());
+    dk = entry_kind(d);
+  }
+  if (dk != kLiteral) return kLaneIrregular;
+  const u32 Ld = entry_len(d), Ed = entry_extra(d);
+  const u32 span = entry_value(d) + ((v >> Ld) & ((1u << Ed) - 1u));
+  if (span > window) return kLaneIrregular;
+  c.consume(Ld + Ed);
+  *bytes = length;
+  *sym = match_symbol(length, span);
+  return kLaneWindow;
+}
+
+// Marks of one lane's row in [a, b) (bit offsets within its window).
+__device__ __forceinline__ u32 marks_between(const u32* row, u32 a, u32 b) {
+  u32 n = 0;
+  for (u32 k = a >> 5; k < kMarkWords && (k << 5) < b; ++k) {
+    u32 w = row[k];
+    const u32 lo = k << 5;
+    if (lo < a) w &= ~0u << (a - lo);
+    if (b - lo < 32) w &= (1u << (b - lo)) - 1u;
+    n += __popc(w);
+  }
+  return n;
+}
+
 // One round from the token boundary `start` (the same on every lane).  On
-// lane 0: the committed position, the output bytes before it and whether
-// the block continues, ended (position after its end-of-block code) or
-// goes to the serial decoder at that position.
+// every lane: the committed position, the output bytes and tokens before
+// it, and whether the block continues, ended (position after its
+// end-of-block code) or goes to the serial decoder at that position.  With
+// `syms` (room for `room` words), the round's tokens are written there in
+// order: each lane's region holds as many tokens as it marked after its
+// entry plus those it decoded past its window, so a warp scan places every
+// lane's tokens before phase 3 decodes them again.
+template <bool kWrite>
 __device__ RoundResult warp_round(const u8* body, u32 body_bytes, u32 start, u32 window,
-                                  const Tables& t, RoundShared& r) {
+                                  const Tables& t, RoundShared& r, u32* syms, u32 room) {
   const u32 lane = threadIdx.x & 31u;
   const u32 s = start + lane * kRoundWindow, wend = s + kRoundWindow;
   const u32 round_end = start + 32 * kRoundWindow;
@@ -145,6 +218,7 @@ __device__ RoundResult warp_round(const u8* body, u32 body_bytes, u32 start, u32
   for (u32 k = 0; k < kMarkWords; ++k) my_marks[k] = 0;
   Bits c;
   c.init(body, body_bytes);
+  u32 bytes = 0, sym = 0;
   // Phase 1: speculative decode of the window, marking token starts.
   u32 stop = kLaneIrregular, stop_at = s;
   if (s < c.end) {
@@ -157,8 +231,7 @@ __device__ RoundResult warp_round(const u8* body, u32 body_bytes, u32 start, u32
         break;
       }
       my_marks[(p - s) >> 5] |= 1u << ((p - s) & 31);
-      u32 bytes = 0;
-      const u32 st = count_token(c, t, window, &bytes);
+      const u32 st = symbol_token(c, t, window, &bytes, &sym);
       if (st != kLaneWindow) {
         stop = st;
         stop_at = p;
@@ -166,11 +239,9 @@ __device__ RoundResult warp_round(const u8* body, u32 body_bytes, u32 start, u32
       }
     }
   }
-  r.stop[lane] = stop;
-  r.stop_at[lane] = stop_at;
   __syncwarp();
   // Phase 2: run on until landing on a later lane's mark (or past the round).
-  u32 link = stop, link_at = stop_at, link_to = lane;
+  u32 link = stop, link_at = stop_at, link_to = lane, cont_tokens = 0;
   if (stop == kLaneWindow) {
     for (;;) {
       const u32 p = c.pos();
@@ -186,13 +257,13 @@ __device__ RoundResult warp_round(const u8* body, u32 body_bytes, u32 start, u32
         link_to = to;
         break;
       }
-      u32 bytes = 0;
-      const u32 st = count_token(c, t, window, &bytes);
+      const u32 st = symbol_token(c, t, window, &bytes, &sym);
       if (st != kLaneWindow) {
         link = st;
         link_at = p;
         break;
       }
+      ++cont_tokens;
     }
   }
   r.link[lane] = link;
@@ -202,7 +273,7 @@ __device__ RoundResult warp_round(const u8* body, u32 body_bytes, u32 start, u32
   r.region_end[lane] = kLaneIrregular;
   r.region_from[lane] = 1;  // empty region (from > to)
   __syncwarp();
-  // Walk: the true chain from lane 0, lane to lane.
+  // Walk: the true chain from lane 0, lane to lane (always to higher lanes).
   if (lane == 0) {
     u32 j = 0, from = start;
     for (;;) {
@@ -216,37 +287,59 @@ __device__ RoundResult warp_round(const u8* body, u32 body_bytes, u32 start, u32
     }
   }
   __syncwarp();
-  // Phase 3: decode this lane's region exactly.
   const u32 from = r.region_from[lane], to = r.region_to[lane], end = r.region_end[lane];
-  u32 total = 0, finish = to, broken = 0;
-  if (from <= to) {
+  const bool visited = from <= to;
+  // Tokens of the region: marks from the entry on (up to the early stop when
+  // phase 1 ended the region), plus the tokens phase 2 decoded.
+  u32 expect = 0;
+  if (visited) {
+    expect = stop == kLaneWindow ? marks_between(my_marks, from - s, kRoundWindow) + cont_tokens
+                                 : marks_between(my_marks, from - s, stop_at - s);
+  }
+  u32 before = expect;
+  for (u32 o = 1; o < 32; o <<= 1) {
+    const u32 v = __shfl_up_sync(kFullMask, before, o);
+    if (lane >= o) before += v;
+  }
+  before -= expect;
+  // Phase 3: decode this lane's region again, exactly.
+  u32 total = 0, tokens = 0, finish = to, broken = 0;
+  if (visited) {
     c.seek(from);
     // The same tokens phases 1 and 2 took; any other answer would be a
     // decoder fault, and the round is then dropped.
     while (c.pos() < to) {
-      u32 bytes = 0;
-      if (count_token(c, t, window, &bytes) != kLaneWindow) {
+      if (symbol_token(c, t, window, &bytes, &sym) != kLaneWindow || tokens == expect) {
         broken = 1;
         break;
       }
+      if (kWrite) {
+        if (before + tokens < room) syms[before + tokens] = sym;
+        else broken = 1;
+      }
+      ++tokens;
       total += bytes;
     }
-    if (!broken && c.pos() != to) broken = 1;
+    if (!broken && (c.pos() != to || tokens != expect)) broken = 1;
     if (!broken && end == kLaneBlockEnd) {
-      u32 bytes = 0;
-      if (count_token(c, t, window, &bytes) != kLaneBlockEnd) broken = 1;
+      if (symbol_token(c, t, window, &bytes, &sym) != kLaneBlockEnd) broken = 1;
       finish = c.pos();
     }
   }
-  for (u32 o = 16; o; o >>= 1) total += __shfl_xor_sync(kFullMask, total, o);
+  u32 count = tokens;
+  for (u32 o = 16; o; o >>= 1) {
+    total += __shfl_xor_sync(kFullMask, total, o);
+    count += __shfl_xor_sync(kFullMask, count, o);
+  }
   // The lane whose region ends the walk holds the round's end.
-  const u32 enders = __ballot_sync(kFullMask, from <= to && end != kLaneMerged);
-  RoundResult out{start, 0, kRoundFallback};
+  const u32 enders = __ballot_sync(kFullMask, visited && end != kLaneMerged);
+  RoundResult out{start, 0, 0, kRoundFallback};
   if (enders && !__any_sync(kFullMask, broken)) {
     const u32 who = __ffs(enders) - 1;
     const u32 outcome_end = __shfl_sync(kFullMask, end, who);
     out.pos = __shfl_sync(kFullMask, finish, who);
     out.bytes = total;
+    out.tokens = count;
     out.outcome = outcome_end == kLaneWindow ? kRoundMore
                 : outcome_end == kLaneBlockEnd ? kRoundBlockEnd : kRoundFallback;
   }
@@ -254,13 +347,12 @@ __device__ RoundResult warp_round(const u8* body, u32 body_bytes, u32 start, u32
   return out;
 }
 
-struct DescribeShared {
+struct NodeShared {
   Tables dyn[kNodeWarps];
   RoundShared round[kNodeWarps];
 };
-struct EmitShared {
-  Tables dyn[kEmitWarps];
-  __align__(16) u16 ring[kEmitWarps][kEmitRing];
+struct ExpandShared {
+  __align__(16) u16 ring[kExpandWarps][kEmitRing];
 };
 
 // ---------------------------------------------------------------------------
@@ -350,46 +442,22 @@ __global__ void cand_write_kernel(const u32* bitmap, u32 words, const u32* block
 }
 
 // ---------------------------------------------------------------------------
-// Node walk (describe and emit share it).
+// Node walk: decode from a candidate through any following stored/fixed
+// blocks up to the next dynamic header.  Describe counts; the symbols
+// kernel also writes the node's tokens to `syms` (room for `room` words).
 // ---------------------------------------------------------------------------
 struct NodeResult {
-  u32 end, size, blocks, info;
+  u32 end, size, blocks, info, tokens;
 };
 
-// Flush ring symbols [from, to) of a node whose output starts at `prefix`:
-// bytes to `out`, markers to `source` + the `unresolved` bitmap.
-__device__ void flush_symbols(const u16* ring, u8* out, u32* source, u32* unresolved, u32 prefix,
-                              u32 from, u32 to) {
-  const u32 lane = threadIdx.x & 31u;
-  for (u32 p = from + lane; p < to; p += 32) {
-    const u32 v = ring[p & kEmitMask];
-    const u32 at = prefix + p;
-    if (v < 256) {
-      out[at] = u8(v);
-    } else {
-      out[at] = 0;
-      source[at] = prefix - 1 - (v - 256);
-      atomicOr(&unresolved[at >> 5], 1u << (at & 31));
-    }
-  }
-}
-
-// Symbol of node-local position q (already flushed) from global memory.
-__device__ __forceinline__ u32 flushed_symbol(const u8* out, const u32* source,
-                                              const u32* unresolved, u32 prefix, u32 q) {
-  const u32 at = prefix + q;
-  if ((unresolved[at >> 5] >> (at & 31)) & 1u) return 256 + (prefix - 1 - source[at]);
-  return out[at];
-}
-
-template <bool kEmit>
+template <bool kWrite>
 __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expected, u32 window,
-                                const Tables& fixed, Tables& dyn, u16* ring, u8* out,
-                                u32* source, u32* unresolved, u32 prefix, RoundShared* rounds) {
+                                const Tables& fixed, Tables& dyn, RoundShared& rounds, u32* syms,
+                                u32 room) {
   const u32 lane = threadIdx.x & 31u;
-  NodeResult r{start, 0, 0, 0};
+  NodeResult r{start, 0, 0, 0, 0};
   Bits c;
-  u32 produced = 0, flushed = 0, final = 0, blocks = 0, full_words = 0;
+  u32 produced = 0, tokens = 0, final = 0, blocks = 0, full_words = 0;
   u32 fail = 0, stop = 0;
   bool need_header = true;
   bool parallel = false;  // this block's body goes through lane-parallel rounds
@@ -398,12 +466,19 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
     c.seek(start);
     full_words = (c.shift + c.end) >> 5;
   }
-  const u32 limit = kEmit ? expected - prefix : expected;  // output bound of this node
+  const u32 limit = expected;  // output bound of a node
+  // Lane 0 appends one symbol word (writing only with kWrite, within room).
+  auto put = [&](u32 word) {
+    if (kWrite) {
+      if (tokens < room) syms[tokens] = word;
+      else fail = 1;
+    }
+    ++tokens;
+  };
   for (;;) {
-    u32 action = kNone, len = 0, dist = 0, src = 0, dst = 0;
+    u32 action = kNone;
     if (lane == 0) {
       while (!fail && !stop) {
-        if (kEmit && produced - flushed >= kEmitFlush) { action = kFlush; break; }
         if (need_header) {
           const u32 header = c.pos();
           u32 err = 0;
@@ -422,16 +497,13 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
             const u32 at = c.pos();
             if (err || (n ^ comp) != 0xffffu || n > limit - produced || at > c.end ||
                 n * 8 > c.end - at) { fail = 1; break; }
-            if (kEmit) {
-              action = kStored;
-              src = at >> 3;
-              dst = produced;
-              len = n;
+            if (n) {
+              put(kStoredFlag | n);
+              put(at >> 3);
             }
             produced += n;
             c.seek(at + n * 8);
             if (final) stop = 1;
-            if (kEmit) break;
             continue;
           }
           action = type == 2 ? kDynamic : kFixed;
@@ -442,10 +514,8 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
           break;
         }
         const Tables& t = dyn;
-        // One bound for the fast loop: room for a maximal match and, when
-        // emitting, a flush before the ring can wrap onto unflushed symbols.
-        u32 stop_at = limit >= 258 ? limit - 258 : 0;
-        if (kEmit) stop_at = min_u32(stop_at, flushed + kEmitFlush);
+        // One bound for the fast loop: room for a maximal match.
+        const u32 stop_at = limit >= 258 ? limit - 258 : 0;
         const u32 idx_limit = full_words >= 2 ? full_words - 1 : 0;
         while (c.idx < idx_limit && produced < stop_at) {
           c.refill_fast();
@@ -454,7 +524,7 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
           const u32 kind = entry_kind(e);
           if (kind == kLiteral) {
             c.consume(entry_len(e));
-            if (kEmit) ring[produced & kEmitMask] = u16(entry_value(e));
+            put(entry_value(e));
             ++produced;
             continue;
           }
@@ -477,34 +547,10 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
             break;
           }
           c.consume(Ld + Ed);
-          if (kEmit) {
-            if (span > prefix + produced) { fail = 1; break; }
-            if (length >= 32) {
-              action = kCopy;
-              dst = produced;
-              len = length;
-              dist = span;
-              produced += length;
-              break;
-            }
-            if (span <= produced && span + 258 <= kEmitRing) {
-              for (u32 j = 0; j < length; ++j)
-                ring[(produced + j) & kEmitMask] = ring[(produced + j - span) & kEmitMask];
-            } else {
-              for (u32 j = 0; j < length; ++j) {
-                const u32 p = produced + j;
-                u32 sym;
-                if (span > p) sym = 256 + (span - p - 1);
-                else if (span + 258 <= kEmitRing) sym = ring[(p - span) & kEmitMask];
-                else sym = flushed_symbol(out, source, unresolved, prefix, p - span);
-                ring[p & kEmitMask] = u16(sym);
-              }
-            }
-          }
+          put(match_symbol(length, span));
           produced += length;
         }
-        if (action != kNone || fail) break;
-        if (kEmit && produced - flushed >= kEmitFlush) continue;
+        if (fail) break;
         const Token tok = take_token(c, t);
         if (tok.kind == kTokError) { fail = 1; break; }
         if (tok.kind == kTokEnd) {
@@ -515,116 +561,65 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
         const u32 size = tok.kind == kTokLiteral ? 1u : tok.length;
         if (size > limit - produced) { fail = 1; break; }
         if (tok.kind == kTokLiteral) {
-          if (kEmit) ring[produced & kEmitMask] = u16(tok.value);
+          put(tok.value);
           ++produced;
           continue;
         }
         if (tok.dist > window) { fail = 1; break; }
-        if (kEmit) {
-          if (tok.dist > prefix + produced) { fail = 1; break; }
-          if (tok.length >= 32) {
-            action = kCopy;
-            dst = produced;
-            len = tok.length;
-            dist = tok.dist;
-            produced += tok.length;
-            break;
-          }
-          for (u32 j = 0; j < tok.length; ++j) {
-            const u32 p = produced + j;
-            u32 sym;
-            if (tok.dist > p) sym = 256 + (tok.dist - p - 1);
-            else if (tok.dist + 258 <= kEmitRing) sym = ring[(p - tok.dist) & kEmitMask];
-            else sym = flushed_symbol(out, source, unresolved, prefix, p - tok.dist);
-            ring[p & kEmitMask] = u16(sym);
-          }
-        }
+        put(match_symbol(tok.length, tok.dist));
         produced += tok.length;
       }
     }
     fail = __shfl_sync(kFullMask, fail, 0);
     if (fail) break;
     action = __shfl_sync(kFullMask, action, 0);
-    const u32 now = __shfl_sync(kFullMask, produced, 0);
     const bool done = __shfl_sync(kFullMask, stop, 0) != 0;
     if (action == kDynamic) {
       const u32 st = warp_dynamic_header(c, dyn);
       if (st) { fail = 1; break; }
       if (lane == 0) {
         need_header = false;
-        parallel = rounds != nullptr;
+        parallel = true;
       }
     } else if (action == kFixed) {
       warp_load_fixed(dyn, fixed);
       if (lane == 0) {
         need_header = false;
-        parallel = rounds != nullptr;
+        parallel = true;
       }
     } else if (action == kRound) {
       const u32 from = __shfl_sync(kFullMask, lane == 0 ? c.pos() : 0u, 0);
-      const RoundResult rr = warp_round(body, bytes, from, window, dyn, rounds[threadIdx.x >> 5]);
+      const u32 base = __shfl_sync(kFullMask, tokens, 0);
+      const RoundResult rr = warp_round<kWrite>(body, bytes, from, window, dyn, rounds,
+                                                syms + base, room > base ? room - base : 0u);
       if (lane == 0) {
-        if (rr.outcome == kRoundFallback || rr.bytes > limit - produced) {
-          // The serial decoder takes the rest of the block from the last
-          // boundary known to be on the true chain (the round's start when
-          // the round would pass the output bound).
+        if (rr.bytes > limit - produced) {
+          // The round would pass the output bound: the serial decoder takes
+          // the block from the round's start and reports it exactly.
           parallel = false;
-          if (rr.bytes <= limit - produced) {
-            produced += rr.bytes;
-            c.seek(rr.pos);
-          }
         } else {
           produced += rr.bytes;
+          tokens += rr.tokens;
           c.seek(rr.pos);
-          if (rr.outcome == kRoundBlockEnd) {
+          if (rr.outcome == kRoundFallback) {
+            // The serial decoder takes the rest of the block from the last
+            // boundary known to be on the true chain.
+            parallel = false;
+          } else if (rr.outcome == kRoundBlockEnd) {
             need_header = true;
             parallel = false;
             if (final) stop = 1;
           }
         }
       }
-    } else if (kEmit && action == kFlush) {
-      const u32 to = now;
-      flush_symbols(ring, out, source, unresolved, prefix, flushed, to);
-      flushed = to;
-    } else if (kEmit && action == kStored) {
-      len = __shfl_sync(kFullMask, len, 0);
-      src = __shfl_sync(kFullMask, src, 0);
-      dst = __shfl_sync(kFullMask, dst, 0);
-      flush_symbols(ring, out, source, unresolved, prefix, flushed, dst);
-      for (u32 j = lane; j < len; j += 32) {
-        const u8 b = body[src + j];
-        out[prefix + dst + j] = b;
-        ring[(dst + j) & kEmitMask] = b;
-      }
-      flushed = dst + len;
-    } else if (kEmit && action == kCopy) {
-      len = __shfl_sync(kFullMask, len, 0);
-      dst = __shfl_sync(kFullMask, dst, 0);
-      dist = __shfl_sync(kFullMask, dist, 0);
-      // Seeds before dst only; markers for positions before the node start.
-      const bool from_ring = dist + 258 <= kEmitRing;
-      u32 s = lane % dist;
-      const u32 step = 32 % dist;
-      for (u32 j = lane; j < len; j += 32) {
-        const u32 q = dst + s - dist;  // wraps when the seed precedes the node
-        u32 sym;
-        if (dist > dst + s) sym = 256 + (dist - dst - s - 1);
-        else if (from_ring) sym = ring[q & kEmitMask];
-        else sym = flushed_symbol(out, source, unresolved, prefix, q);
-        ring[(dst + j) & kEmitMask] = u16(sym);
-        s += step;
-        if (s >= dist) s -= dist;
-      }
     }
     __syncwarp();
     if (done) break;
   }
-  if (!fail && kEmit) flush_symbols(ring, out, source, unresolved, prefix, flushed,
-                                    __shfl_sync(kFullMask, produced, 0));
   r.end = __shfl_sync(kFullMask, c.pos(), 0);
   r.size = __shfl_sync(kFullMask, produced, 0);
   r.blocks = __shfl_sync(kFullMask, blocks, 0);
+  r.tokens = __shfl_sync(kFullMask, tokens, 0);
   r.info = (fail ? 0u : kInfoOk) | (__shfl_sync(kFullMask, final, 0) ? kInfoFinal : 0u);
   return r;
 }
@@ -633,8 +628,8 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
 __global__ void __launch_bounds__(kNodeWarps * 32)
 describe_kernel(const u8* in, u32 in_size, u64 expected, const u32* cands, const u32* total,
                 u32 capacity, u32* next_item, u32* ends, u32* sizes, u32* blocks, u32* infos,
-                const Tables* fixed) {
-  __shared__ DescribeShared sh;
+                u32* tokens, const Tables* fixed) {
+  __shared__ NodeShared sh;
   const u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   u32 window = 0, wanted = 0;
   if (zlib_framing(in, in_size, &window, &wanted)) return;
@@ -645,13 +640,13 @@ describe_kernel(const u8* in, u32 in_size, u64 expected, const u32* cands, const
     item = __shfl_sync(kFullMask, item, 0);
     if (item >= count) break;
     const NodeResult r = warp_node<false>(in + 2, in_size - 6, cands[item], u32(expected), window,
-                                          *fixed, sh.dyn[warp], nullptr, nullptr, nullptr,
-                                          nullptr, 0, sh.round);
+                                          *fixed, sh.dyn[warp], sh.round[warp], nullptr, 0);
     if (lane == 0) {
       ends[item] = r.end;
       sizes[item] = r.size;
       blocks[item] = r.blocks;
       infos[item] = r.info;
+      tokens[item] = r.tokens;
     }
   }
 }
@@ -663,10 +658,10 @@ describe_kernel(const u8* in, u32 in_size, u64 expected, const u32* cands, const
 __global__ void __launch_bounds__(1024)
 chain_kernel(const u8* in, u32 in_size, u64 expected, u32 max_blocks, const u32* cands,
              const u32* total, u32 capacity, const u32* ends, const u32* sizes,
-             const u32* blocks, const u32* infos, u32* jump, u32 levels, u32* path, u32* prefix,
-             u32* state) {
-  __shared__ u32 warp_sum[32];
-  __shared__ u32 s_len, s_ok, s_carry, s_blocks;
+             const u32* blocks, const u32* infos, const u32* tokens, u32* jump, u32 levels,
+             u32* path, u32* prefix, u32* tprefix, u32* state) {
+  __shared__ u32 warp_sum[32], warp_tsum[32];
+  __shared__ u32 s_len, s_ok, s_carry, s_tcarry, s_blocks;
   const u32 tid = threadIdx.x;
   u32 window = 0, wanted = 0;
   const u32 count = min_u32(*total, capacity);
@@ -720,6 +715,7 @@ chain_kernel(const u8* in, u32 in_size, u64 expected, u32 max_blocks, const u32*
     s_len = len;
     s_ok = terminal == end_node;
     s_carry = 0;
+    s_tcarry = 0;
     s_blocks = 0;
   }
   __syncthreads();
@@ -730,28 +726,42 @@ chain_kernel(const u8* in, u32 in_size, u64 expected, u32 max_blocks, const u32*
   }
   for (u32 base = 0; base < len; base += blockDim.x) {
     const u32 m = base + tid;
-    u32 node = 0, size = 0, nb = 0;
+    u32 node = 0, size = 0, nb = 0, nt = 0;
     if (m < len) {
       for (u32 k = 0; k < levels; ++k)
         if ((m >> k) & 1u) node = jump[u64(k) * nodes + node];
       path[m] = node;
       size = sizes[node];
       nb = blocks[node];
+      nt = tokens[node];
     }
-    u32 incl = size, bincl = nb;
+    u32 incl = size, bincl = nb, tincl = nt;
     for (u32 o = 1; o < 32; o <<= 1) {
       const u32 t = __shfl_up_sync(kFullMask, incl, o);
       const u32 tb = __shfl_up_sync(kFullMask, bincl, o);
-      if ((tid & 31) >= o) { incl += t; bincl += tb; }
+      const u32 tt = __shfl_up_sync(kFullMask, tincl, o);
+      if ((tid & 31) >= o) { incl += t; bincl += tb; tincl += tt; }
     }
-    if ((tid & 31) == 31) warp_sum[tid >> 5] = incl;
+    if ((tid & 31) == 31) {
+      warp_sum[tid >> 5] = incl;
+      warp_tsum[tid >> 5] = tincl;
+    }
     __syncthreads();
-    u32 before = s_carry + incl - size;
-    for (u32 w = 0; w < (tid >> 5); ++w) before += warp_sum[w];
-    if (m < len) prefix[m] = before;
+    u32 before = s_carry + incl - size, tbefore = s_tcarry + tincl - nt;
+    for (u32 w = 0; w < (tid >> 5); ++w) {
+      before += warp_sum[w];
+      tbefore += warp_tsum[w];
+    }
+    if (m < len) {
+      prefix[m] = before;
+      tprefix[m] = tbefore;
+    }
     if ((tid & 31) == 31) atomicAdd(&s_blocks, bincl);
     __syncthreads();
-    if (tid == blockDim.x - 1 || m == len - 1) s_carry = before + size;
+    if (tid == blockDim.x - 1 || m == len - 1) {
+      s_carry = before + size;
+      s_tcarry = tbefore + nt;
+    }
     __syncthreads();
   }
   if (tid == 0) {
@@ -764,13 +774,13 @@ chain_kernel(const u8* in, u32 in_size, u64 expected, u32 max_blocks, const u32*
   }
 }
 
-// Emit every path node (warp per node, work stealing).
-__global__ void __launch_bounds__(kEmitWarps * 32)
-emit_kernel(const u8* in, u32 in_size, u64 expected, const u32* cands, const u32* path,
-            const u32* prefix, const u32* sizes, const u32* state, u32* next_item, u8* out,
-            u32* source, u32* unresolved, u32* fail_flag, const Tables* fixed) {
-  extern __shared__ __align__(16) u8 smem[];
-  EmitShared& sh = *reinterpret_cast<EmitShared*>(smem);
+// Decode every path node again, writing its tokens at its place in the
+// symbol arena (warp per node, work stealing).
+__global__ void __launch_bounds__(kNodeWarps * 32)
+symbols_kernel(const u8* in, u32 in_size, u64 expected, const u32* cands, const u32* path,
+               const u32* tprefix, const u32* sizes, const u32* tokens, const u32* state,
+               u32* next_item, u32* syms, u32* fail_flag, const Tables* fixed) {
+  __shared__ NodeShared sh;
   const u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   if (!state[1]) return;
   const u32 len = state[0];
@@ -783,9 +793,162 @@ emit_kernel(const u8* in, u32 in_size, u64 expected, const u32* cands, const u32
     if (item >= len) break;
     const u32 node = path[item];
     const NodeResult r = warp_node<true>(in + 2, in_size - 6, cands[node], u32(expected), window,
-                                         *fixed, sh.dyn[warp], sh.ring[warp], out, source,
-                                         unresolved, prefix[item], nullptr);
-    if (lane == 0 && (!(r.info & kInfoOk) || r.size != sizes[node])) atomicOr(fail_flag, 1u);
+                                         *fixed, sh.dyn[warp], sh.round[warp],
+                                         syms + tprefix[item], tokens[node]);
+    if (lane == 0 && (!(r.info & kInfoOk) || r.size != sizes[node] || r.tokens != tokens[node]))
+      atomicOr(fail_flag, 1u);
+  }
+}
+
+// Flush ring symbols [from, to) of a node whose output starts at `prefix`:
+// bytes to `out`, markers to `source` + the `unresolved` bitmap.
+__device__ void flush_symbols(const u16* ring, u8* out, u32* source, u32* unresolved, u32 prefix,
+                              u32 from, u32 to) {
+  const u32 lane = threadIdx.x & 31u;
+  for (u32 p = from + lane; p < to; p += 32) {
+    const u32 v = ring[p & kEmitMask];
+    const u32 at = prefix + p;
+    if (v < 256) {
+      out[at] = u8(v);
+    } else {
+      out[at] = 0;
+      source[at] = prefix - 1 - (v - 256);
+      atomicOr(&unresolved[at >> 5], 1u << (at & 31));
+    }
+  }
+}
+
+// Symbol of node-local position q (already flushed) from global memory.
+__device__ __forceinline__ u32 flushed_symbol(const u8* out, const u32* source,
+                                              const u32* unresolved, u32 prefix, u32 q) {
+  const u32 at = prefix + q;
+  if ((unresolved[at >> 5] >> (at & 31)) & 1u) return 256 + (prefix - 1 - source[at]);
+  return out[at];
+}
+
+// Expand every path node's tokens into the output (warp per node, work
+// stealing).  The warp takes 32 tokens at a time: a scan of their sizes
+// places them, literals land in parallel, short copies that read only
+// earlier output go one per lane, and the other copies follow in order,
+// each across the warp.  The ring holds the node's recent output as u16
+// symbols: a byte, or 256 + k for the byte k + 1 positions before the node
+// start (a reference into an earlier node; copies propagate it); full
+// stretches of the ring flush to the output, markers as source positions in
+// `source` plus a bit in `unresolved`.
+__global__ void __launch_bounds__(kExpandWarps * 32)
+expand_kernel(const u8* in, u32 in_size, const u32* path, const u32* prefix,
+              const u32* tprefix, const u32* sizes, const u32* tokens, const u32* state,
+              const u32* syms, u32* next_item, u8* out, u32* source, u32* unresolved,
+              u32* fail_flag) {
+  __shared__ ExpandShared sh;
+  const u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  // A failed chain or symbol pass leaves nothing to expand (the status path
+  // reports the stream).
+  if (!state[1] || *fail_flag) return;
+  const u32 len = state[0];
+  const u8* body = in + 2;
+  u16* ring = sh.ring[warp];
+  for (;;) {
+    u32 item = 0;
+    if (lane == 0) item = atomicAdd(next_item, 1u);
+    item = __shfl_sync(kFullMask, item, 0);
+    if (item >= len) break;
+    const u32 node = path[item], start = prefix[item];
+    const u32* sy = syms + tprefix[item];
+    const u32 n = tokens[node];
+    u32 pos = 0, flushed = 0, bad = 0;
+    for (u32 first = 0; first < n && !bad;) {
+      if (pos - flushed >= kEmitFlush) {
+        flush_symbols(ring, out, source, unresolved, start, flushed, pos);
+        flushed = pos;
+      }
+      const u32 head = sy[first];
+      if (head & kStoredFlag && !(head & kMatchFlag)) {
+        // Stored bytes: flush, then copy straight from the input.
+        const u32 count = head & 0xffffu, src = sy[first + 1];
+        flush_symbols(ring, out, source, unresolved, start, flushed, pos);
+        for (u32 j = lane; j < count; j += 32) {
+          const u8 v = body[src + j];
+          out[start + pos + j] = v;
+          ring[(pos + j) & kEmitMask] = v;
+        }
+        pos += count;
+        flushed = pos;
+        first += 2;
+        __syncwarp();
+        continue;
+      }
+      // Up to 32 tokens, stopping before a stored block.
+      const u32 k = first + lane;
+      const u32 tk = k < n ? sy[k] : kStoredFlag;
+      const bool stored = (tk & kStoredFlag) && !(tk & kMatchFlag);
+      const u32 stops = __ballot_sync(kFullMask, stored);
+      const u32 avail = stops ? __ffs(stops) - 1 : 32u;
+      const bool valid = lane < avail, match = valid && (tk & kMatchFlag);
+      const u32 size = !valid ? 0u : match ? (tk & 511u) : 1u;
+      u32 incl = size;
+      for (u32 o = 1; o < 32; o <<= 1) {
+        const u32 v = __shfl_up_sync(kFullMask, incl, o);
+        if (lane >= o) incl += v;
+      }
+      // Tokens whose output fits without wrapping onto unflushed entries.
+      const u32 budget = kEmitRing - (pos - flushed);
+      const u32 m = __popc(__ballot_sync(kFullMask, valid && incl <= budget));
+      const bool take = lane < m;
+      const u32 chunk_end = pos + __shfl_sync(kFullMask, incl, m - 1);
+      const u32 at = pos + incl - size;
+      if (take && !match) ring[at & kEmitMask] = u16(tk & 255u);
+      __syncwarp();
+      // Symbol of node position dst + j - dist for a copy: a marker before
+      // the node start, the ring while the entry is still there (nothing at
+      // or past chunk_end is written), else the output.
+      auto source_symbol = [&](u32 dst, u32 dist, u32 j) -> u32 {
+        if (dist > dst + j) return 256 + (dist - dst - j - 1);
+        const u32 q = dst + j - dist;
+        if (q + kEmitRing >= chunk_end) return ring[q & kEmitMask];
+        return flushed_symbol(out, source, unresolved, start, q);
+      };
+      const u32 length = tk & 511u, dist = (tk >> 9) & 0xffffu;
+      // Short copies that read nothing this chunk writes (or only their own
+      // bytes, when first in the chunk) go one per lane.
+      const bool own = take && match && length <= 32 &&
+                       (length <= dist ? at + length <= pos + dist : at == pos);
+      if (take && match && dist > start + at) bad = 1;
+      if (own && !bad)
+        for (u32 j = 0; j < length; ++j) ring[(at + j) & kEmitMask] = u16(source_symbol(at, dist, j));
+      if (__any_sync(kFullMask, bad)) {
+        bad = 1;
+        break;
+      }
+      __syncwarp();
+      u32 copies = __ballot_sync(kFullMask, take && match && !own);
+      while (copies) {
+        const u32 who = __ffs(copies) - 1;
+        copies &= copies - 1;
+        const u32 dst = __shfl_sync(kFullMask, at, who);
+        const u32 c_len = __shfl_sync(kFullMask, length, who);
+        const u32 c_dist = __shfl_sync(kFullMask, dist, who);
+        if (c_len <= c_dist) {
+          for (u32 j = lane; j < c_len; j += 32)
+            ring[(dst + j) & kEmitMask] = u16(source_symbol(dst, c_dist, j));
+        } else {
+          // Periodic seeds from before dst.
+          u32 sd = lane % c_dist;
+          const u32 step = 32 % c_dist;
+          for (u32 j = lane; j < c_len; j += 32) {
+            ring[(dst + j) & kEmitMask] = u16(source_symbol(dst, c_dist, sd));
+            sd += step;
+            if (sd >= c_dist) sd -= c_dist;
+          }
+        }
+        __syncwarp();
+      }
+      pos = chunk_end;
+      first += m;
+    }
+    if (!bad) flush_symbols(ring, out, source, unresolved, start, flushed, pos);
+    __syncwarp();
+    if (lane == 0 && (bad || pos != sizes[node])) atomicOr(fail_flag, 1u);
   }
 }
 
@@ -900,7 +1063,6 @@ __global__ void build_fixed_kernel(Tables* fixed) { warp_build_fixed(*fixed); }
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-size_t parallel_inflate_emit_smem() { return sizeof(EmitShared); }
 
 cudaError_t build_fixed_tables(void** out) {
   Tables* fixed = nullptr;
@@ -915,11 +1077,8 @@ cudaError_t build_fixed_tables(void** out) {
 }
 
 cudaError_t configure_parallel_inflate(int* emit_per_sm) {
-  cudaError_t e = cudaFuncSetAttribute(emit_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       int(sizeof(EmitShared)));
-  if (e != cudaSuccess) return e;
-  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(emit_per_sm, emit_kernel,
-                                                       kEmitWarps * 32, sizeof(EmitShared));
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(emit_per_sm, expand_kernel,
+                                                       kExpandWarps * 32, 0);
 }
 
 u32 chain_levels(u32 capacity) {
@@ -937,6 +1096,9 @@ ParallelScratch parallel_scratch_layout(u64 in_size, u64 expected, u32 capacity)
   s.levels = chain_levels(capacity);
   s.out_words = (expected + 31) / 32 + 1;
   s.segments = u32((expected + kAdlerSegment - 1) / kAdlerSegment);
+  // Path tokens of a chain that passes its checks: at most one per output
+  // byte, plus two words per stored block (at most kMaxBlocks blocks).
+  s.symbol_words = expected + 2 * u64(kMaxBlocks) + 64;
   return s;
 }
 
@@ -958,19 +1120,25 @@ cudaError_t launch_parallel_inflate(const u8* in, u64 in_size, u8* out, u64 expe
   note_launch();
   describe_kernel<<<node_grid, kNodeWarps * 32, 0, stream>>>(
       in, u32(in_size), expected, b.cands, b.total, s.capacity, b.counters, b.ends, b.sizes,
-      b.blocks, b.infos, static_cast<const Tables*>(dev.fixed_tables));
+      b.blocks, b.infos, b.tokens, static_cast<const Tables*>(dev.fixed_tables));
   profile_end(stream);
   note_launch();
   chain_kernel<<<1, 1024, 0, stream>>>(in, u32(in_size), expected, max_blocks, b.cands, b.total,
-                                       s.capacity, b.ends, b.sizes, b.blocks, b.infos, b.jump,
-                                       s.levels, b.path, b.prefix, b.state);
+                                       s.capacity, b.ends, b.sizes, b.blocks, b.infos, b.tokens,
+                                       b.jump, s.levels, b.path, b.prefix, b.tprefix, b.state);
   (void)nodes;
-  const u32 emit_grid = u32(dev.sms) * u32(dev.emit_per_sm > 0 ? dev.emit_per_sm : 1);
-  profile_begin("emit_kernel", stream);
+  profile_begin("symbols_kernel", stream);
   note_launch();
-  emit_kernel<<<emit_grid, kEmitWarps * 32, sizeof(EmitShared), stream>>>(
-      in, u32(in_size), expected, b.cands, b.path, b.prefix, b.sizes, b.state, b.counters + 1,
-      out, b.source, b.unresolved, b.fail, static_cast<const Tables*>(dev.fixed_tables));
+  symbols_kernel<<<node_grid, kNodeWarps * 32, 0, stream>>>(
+      in, u32(in_size), expected, b.cands, b.path, b.tprefix, b.sizes, b.tokens, b.state,
+      b.counters + 1, b.syms, b.fail, static_cast<const Tables*>(dev.fixed_tables));
+  profile_end(stream);
+  const u32 expand_grid = u32(dev.sms) * u32(dev.emit_per_sm > 0 ? dev.emit_per_sm : 1);
+  profile_begin("expand_kernel", stream);
+  note_launch();
+  expand_kernel<<<expand_grid, kExpandWarps * 32, 0, stream>>>(
+      in, u32(in_size), b.path, b.prefix, b.tprefix, b.sizes, b.tokens, b.state, b.syms,
+      b.counters + 2, out, b.source, b.unresolved, b.fail);
   profile_end(stream);
   note_launch();
   resolve_kernel<<<u32(dev.sms) * 8, 256, 0, stream>>>(b.state, u32(s.out_words), b.unresolved,

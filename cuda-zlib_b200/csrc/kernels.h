@@ -81,17 +81,19 @@ struct ParallelScratch {
   u32 levels;         // pointer-doubling levels over capacity + 2 nodes
   u64 out_words;      // unresolved-position bitmap words
   u32 segments;       // Adler-32 segments of the output
+  u64 symbol_words;   // token arena of the path nodes
 };
 struct ParallelBuffers {
   u32* bitmap;        // bitmap_words, from discover_kernel
   u32* block_counts;  // compact_blocks
   u32* total;         // 1: distinct candidates
   u32* cands;         // capacity
-  u32 *ends, *sizes, *blocks, *infos;  // capacity each
+  u32 *ends, *sizes, *blocks, *infos, *tokens;  // capacity each
   u32* jump;          // (capacity + 2) * levels
-  u32 *path, *prefix; // capacity each
+  u32 *path, *prefix, *tprefix;  // capacity each: path nodes, output and token offsets
   u32* state;         // 2: path length, chain ok
-  u32* counters;      // 2, zeroed: describe / emit work counters
+  u32* counters;      // 3, zeroed: describe / symbols / expand work counters
+  u32* syms;          // symbol_words: the path nodes' tokens
   u32* source;        // expected: absolute source of unresolved positions
   u32* unresolved;    // out_words, zeroed
   u64* parts;         // 2 * segments
