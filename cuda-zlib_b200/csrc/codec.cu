@@ -11,6 +11,7 @@
 #include <algorithm>
 #include <array>
 #include <cstdint>
+#include <cstdlib>
 #include <atomic>
 #include <mutex>
 #include <numeric>
@@ -281,6 +282,21 @@ cudaError_t encode_files(const DeviceState& dev, const u8* in, u64 in_bytes,
   return ws.release();
 }
 
+// Extra words of the token arena beyond the exact bound of the path's tokens
+// (CUDA_ZLIB_TOKEN_ARENA_SLACK, default 8 Mi words): room for the partial
+// last page of every candidate.  When it runs out the stream is still decoded
+// exactly, with a second decoding pass into the exact layout.
+u64 token_arena_slack() {
+  const char* text = std::getenv("CUDA_ZLIB_TOKEN_ARENA_SLACK");
+  u64 value = u64(1) << 23;
+  if (text && *text) {
+    char* end = nullptr;
+    const unsigned long long v = std::strtoull(text, &end, 10);
+    if (end && !*end && v <= (u64(1) << 32)) value = v;
+  }
+  return value;
+}
+
 // ---------------------------------------------------------------------------
 // Entry point bodies (validation follows codec_ffi.cu line for line in effect).
 // ---------------------------------------------------------------------------
@@ -407,7 +423,8 @@ cudaError_t decompress(const u8* in, u64 size, int64_t max_candidates, int64_t m
   // if the fast path failed.
   const u64 body = size - 6;
   const u32 capacity = u32(std::min<u64>(u64(max_candidates), body * 9 + 1));
-  const ParallelScratch layout = parallel_scratch_layout(size, expected, capacity);
+  const ParallelScratch layout = parallel_scratch_layout(size, expected, capacity,
+                                                         token_arena_slack());
   ParallelBuffers b{};
   u32* count = nullptr;
   CZ_TRY(ws.allocate(&b.bitmap, layout.bitmap_words));
@@ -424,8 +441,12 @@ cudaError_t decompress(const u8* in, u64 size, int64_t max_candidates, int64_t m
   CZ_TRY(ws.allocate(&b.path, capacity));
   CZ_TRY(ws.allocate(&b.prefix, capacity));
   CZ_TRY(ws.allocate(&b.tprefix, capacity));
-  CZ_TRY(ws.allocate(&b.syms, layout.symbol_words));
-  CZ_TRY(ws.allocate(&b.state, 2));
+  CZ_TRY(ws.allocate(&b.syms, u64(layout.pages) * 1024));
+  CZ_TRY(ws.allocate(&b.first_page, capacity));
+  CZ_TRY(ws.allocate(&b.page_next, layout.pages));
+  CZ_TRY(ws.allocate(&b.page_used, layout.pages));
+  CZ_TRY(ws.allocate(&b.page_cursor, 1));
+  CZ_TRY(ws.allocate(&b.state, 3));
   CZ_TRY(ws.allocate(&b.counters, 3));
   CZ_TRY(ws.allocate(&b.source, expected));
   CZ_TRY(ws.allocate(&b.unresolved, layout.out_words));
@@ -434,6 +455,7 @@ cudaError_t decompress(const u8* in, u64 size, int64_t max_candidates, int64_t m
   CZ_TRY(cudaMemsetAsync(b.bitmap, 0, layout.bitmap_words * sizeof(u32), stream));
   CZ_TRY(cudaMemsetAsync(count, 0, sizeof(u32), stream));
   CZ_TRY(cudaMemsetAsync(b.counters, 0, 3 * sizeof(u32), stream));
+  CZ_TRY(cudaMemsetAsync(b.page_cursor, 0, sizeof(u32), stream));
   CZ_TRY(cudaMemsetAsync(b.unresolved, 0, layout.out_words * sizeof(u32), stream));
   CZ_TRY(cudaMemsetAsync(b.fail, 0, sizeof(u32), stream));
   CZ_TRY(launch_discover(in, size, b.bitmap, count, nullptr, dev->info, stream));

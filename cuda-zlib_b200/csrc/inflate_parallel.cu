@@ -42,7 +42,10 @@ constexpr u32 kExpandWarps = 4;    // warps per CTA in expand
 constexpr u32 kEmitRing = 4096;    // u16 history entries per emitting warp
 constexpr u32 kEmitMask = kEmitRing - 1;
 constexpr u32 kEmitFlush = 2048;   // pending symbols that trigger a flush
-constexpr u32 kInfoFinal = 1u, kInfoOk = 2u;
+constexpr u32 kInfoFinal = 1u, kInfoOk = 2u, kInfoSpilled = 4u;
+constexpr u32 kPageWords = 1024;   // token words per arena page
+constexpr u32 kNoPage = 0xffffffffu;
+constexpr u32 kPassPages = 40;     // pages one pass can reach (32 Ki tokens)
 
 // ---------------------------------------------------------------------------
 // Lane-parallel rounds over a Huffman block body.
@@ -81,6 +84,96 @@ struct RoundShared {
   u32 link_at[32];   // position reached
   u32 link_to[32];   // lane merged with
   u32 region_from[32], region_to[32], region_end[32];  // set by the walk
+  // Where the pass's tokens go (set by lane 0 before phase 3): pages[k] holds
+  // tokens fill0 + [1024k, 1024(k+1)) of the pass, or `word` is the first
+  // contiguous word; `drop` when there is no room.
+  u32 pages[kPassPages];
+  u32 fill0, word, drop;
+};
+
+// Where a node's tokens go: nowhere (count only), one contiguous run (the
+// layout by path token prefixes), or a chain of arena pages allocated as the
+// node grows (describe, before the path is known).  Lane 0 owns the state.
+struct SymbolSink {
+  enum Mode : u32 { kNoWrite = 0, kContiguous = 1, kPages = 2 };
+  u32 mode;
+  u32* pool;       // arena words (page k at pool + k * kPageWords)
+  u32 room;        // contiguous: words available at pool
+  u32* next;       // pages: next page of a chain (kNoPage ends it)
+  u32* used;       // pages: words used per page
+  u32* cursor;     // pages: next free page
+  u32 npages;
+  u32 page, fill;  // current page (kNoPage before the first) and its words
+  u32 first;       // the node's first page
+  u32 written;     // words appended
+  u32 spilled;     // a word could not be stored
+
+  __device__ void new_page() {
+    const u32 idx = atomicAdd(cursor, 1u);
+    if (idx >= npages) {
+      spilled = 1;
+      return;
+    }
+    if (page == kNoPage) first = idx;
+    else { used[page] = fill; next[page] = idx; }
+    page = idx;
+    fill = 0;
+  }
+  // Lane 0: append one word, or two that stay on one page.
+  __device__ void put(u32 word) {
+    if (mode == kContiguous) {
+      if (written < room) pool[written] = word;
+      else spilled = 1;
+    } else if (mode == kPages && !spilled) {
+      if (page == kNoPage || fill == kPageWords) new_page();
+      if (!spilled) pool[u64(page) * kPageWords + fill++] = word;
+    }
+    ++written;
+  }
+  __device__ void put_pair(u32 a, u32 b) {
+    if (mode == kPages && !spilled && (page == kNoPage || fill + 2 > kPageWords)) new_page();
+    put(a);
+    put(b);
+  }
+  // Lane 0: room for a pass's `count` words, described in r for the lanes.
+  __device__ void reserve(u32 count, RoundShared& r) {
+    r.drop = 0;
+    if (mode == kContiguous) {
+      r.word = written;
+      if (written + count > room) { r.drop = 1; spilled = 1; }
+    } else if (mode == kPages) {
+      if (!spilled && count && (page == kNoPage || fill == kPageWords)) new_page();
+      r.fill0 = fill;
+      u32 k = 0, left = count;
+      if (!spilled) {
+        r.pages[k++] = page;
+        u32 space = kPageWords - fill;
+        while (left > space && !spilled && k < kPassPages) {
+          left -= space;
+          fill = kPageWords;
+          new_page();
+          if (!spilled) r.pages[k++] = page;
+          space = kPageWords;
+        }
+        if (left > space) spilled = 1;
+        else fill += left;
+      }
+      r.drop = spilled;
+    }
+    written += count;
+  }
+  // Address of word g of the current pass (after reserve), or nullptr.
+  __device__ __forceinline__ u32* slot(const RoundShared& r, u32 g) const {
+    if (mode == kContiguous) return pool + r.word + g;
+    const u32 a = r.fill0 + g;
+    return pool + u64(r.pages[a / kPageWords]) * kPageWords + a % kPageWords;
+  }
+  __device__ void finish() {
+    if (mode == kPages && page != kNoPage) {
+      used[page] = fill;
+      next[page] = kNoPage;
+    }
+  }
 };
 
 // One token.  Returns kLaneWindow (decoded, *bytes output bytes),
@@ -210,7 +303,7 @@ __device__ __forceinline__ u32 marks_between(const u32* row, u32 a, u32 b) {
 // lane's tokens before phase 3 decodes them again.
 template <bool kWrite>
 __device__ RoundResult warp_round(const u8* body, u32 body_bytes, u32 start, u32 window,
-                                  const Tables& t, RoundShared& r, u32* syms, u32 room) {
+                                  const Tables& t, RoundShared& r, SymbolSink& sink) {
   const u32 lane = threadIdx.x & 31u;
   const u32 s = start + lane * kRoundWindow, wend = s + kRoundWindow;
   const u32 round_end = start + 32 * kRoundWindow;
@@ -302,6 +395,12 @@ __device__ RoundResult warp_round(const u8* body, u32 body_bytes, u32 start, u32
     if (lane >= o) before += v;
   }
   before -= expect;
+  if (kWrite) {
+    const u32 all = __shfl_sync(kFullMask, before + expect, 31);
+    if (lane == 0) sink.reserve(all, r);
+    __syncwarp();
+  }
+  const bool drop = kWrite && r.drop;
   // Phase 3: decode this lane's region again, exactly.
   u32 total = 0, tokens = 0, finish = to, broken = 0;
   if (visited) {
@@ -313,10 +412,7 @@ __device__ RoundResult warp_round(const u8* body, u32 body_bytes, u32 start, u32
         broken = 1;
         break;
       }
-      if (kWrite) {
-        if (before + tokens < room) syms[before + tokens] = sym;
-        else broken = 1;
-      }
+      if (kWrite && !drop) *sink.slot(r, before + tokens) = sym;
       ++tokens;
       total += bytes;
     }
@@ -452,8 +548,8 @@ struct NodeResult {
 
 template <bool kWrite>
 __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expected, u32 window,
-                                const Tables& fixed, Tables& dyn, RoundShared& rounds, u32* syms,
-                                u32 room) {
+                                const Tables& fixed, Tables& dyn, RoundShared& rounds,
+                                SymbolSink& sink) {
   const u32 lane = threadIdx.x & 31u;
   NodeResult r{start, 0, 0, 0, 0};
   Bits c;
@@ -467,12 +563,9 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
     full_words = (c.shift + c.end) >> 5;
   }
   const u32 limit = expected;  // output bound of a node
-  // Lane 0 appends one symbol word (writing only with kWrite, within room).
+  // Lane 0 appends one symbol word.
   auto put = [&](u32 word) {
-    if (kWrite) {
-      if (tokens < room) syms[tokens] = word;
-      else fail = 1;
-    }
+    if (kWrite) sink.put(word);
     ++tokens;
   };
   for (;;) {
@@ -498,8 +591,8 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
             if (err || (n ^ comp) != 0xffffu || n > limit - produced || at > c.end ||
                 n * 8 > c.end - at) { fail = 1; break; }
             if (n) {
-              put(kStoredFlag | n);
-              put(at >> 3);
+              if (kWrite) sink.put_pair(kStoredFlag | n, at >> 3);
+              tokens += 2;
             }
             produced += n;
             c.seek(at + n * 8);
@@ -589,9 +682,7 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
       }
     } else if (action == kRound) {
       const u32 from = __shfl_sync(kFullMask, lane == 0 ? c.pos() : 0u, 0);
-      const u32 base = __shfl_sync(kFullMask, tokens, 0);
-      const RoundResult rr = warp_round<kWrite>(body, bytes, from, window, dyn, rounds,
-                                                syms + base, room > base ? room - base : 0u);
+      const RoundResult rr = warp_round<kWrite>(body, bytes, from, window, dyn, rounds, sink);
       if (lane == 0) {
         if (rr.bytes > limit - produced) {
           // The round would pass the output bound: the serial decoder takes
@@ -616,11 +707,14 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
     __syncwarp();
     if (done) break;
   }
+  if (kWrite && lane == 0) sink.finish();
   r.end = __shfl_sync(kFullMask, c.pos(), 0);
   r.size = __shfl_sync(kFullMask, produced, 0);
   r.blocks = __shfl_sync(kFullMask, blocks, 0);
   r.tokens = __shfl_sync(kFullMask, tokens, 0);
-  r.info = (fail ? 0u : kInfoOk) | (__shfl_sync(kFullMask, final, 0) ? kInfoFinal : 0u);
+  const u32 spilled = kWrite ? __shfl_sync(kFullMask, sink.spilled, 0) : 0u;
+  r.info = (fail ? 0u : kInfoOk) | (__shfl_sync(kFullMask, final, 0) ? kInfoFinal : 0u) |
+           (spilled ? kInfoSpilled : 0u);
   return r;
 }
 
@@ -628,7 +722,8 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
 __global__ void __launch_bounds__(kNodeWarps * 32)
 describe_kernel(const u8* in, u32 in_size, u64 expected, const u32* cands, const u32* total,
                 u32 capacity, u32* next_item, u32* ends, u32* sizes, u32* blocks, u32* infos,
-                u32* tokens, const Tables* fixed) {
+                u32* tokens, u32* first_page, u32* pool, u32* page_next, u32* page_used,
+                u32* page_cursor, u32 npages, const Tables* fixed) {
   __shared__ NodeShared sh;
   const u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   u32 window = 0, wanted = 0;
@@ -639,9 +734,12 @@ describe_kernel(const u8* in, u32 in_size, u64 expected, const u32* cands, const
     if (lane == 0) item = atomicAdd(next_item, 1u);
     item = __shfl_sync(kFullMask, item, 0);
     if (item >= count) break;
-    const NodeResult r = warp_node<false>(in + 2, in_size - 6, cands[item], u32(expected), window,
-                                          *fixed, sh.dyn[warp], sh.round[warp], nullptr, 0);
+    SymbolSink sink{SymbolSink::kPages, pool, 0, page_next, page_used, page_cursor, npages,
+                    kNoPage, 0, kNoPage, 0, 0};
+    const NodeResult r = warp_node<true>(in + 2, in_size - 6, cands[item], u32(expected), window,
+                                         *fixed, sh.dyn[warp], sh.round[warp], sink);
     if (lane == 0) {
+      first_page[item] = sink.first;
       ends[item] = r.end;
       sizes[item] = r.size;
       blocks[item] = r.blocks;
@@ -653,7 +751,8 @@ describe_kernel(const u8* in, u32 in_size, u64 expected, const u32* cands, const
 
 // ---------------------------------------------------------------------------
 // Chain: successor links, pointer doubling from bit 0, prefixes and checks.
-// One CTA.  state[0] = path length, state[1] = chain ok.
+// One CTA.  state[0] = path length, state[1] = chain ok, state[2] = some path
+// node spilled its tokens (use the contiguous layout).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(1024)
 chain_kernel(const u8* in, u32 in_size, u64 expected, u32 max_blocks, const u32* cands,
@@ -667,7 +766,7 @@ chain_kernel(const u8* in, u32 in_size, u64 expected, u32 max_blocks, const u32*
   const u32 count = min_u32(*total, capacity);
   if (zlib_framing(in, in_size, &window, &wanted) || *total > capacity || !count ||
       cands[0] != 0) {
-    if (tid == 0) { state[0] = 0; state[1] = 0; }
+    if (tid == 0) { state[0] = 0; state[1] = 0; state[2] = 0; }
     return;
   }
   const u32 end_node = count, bad_node = count + 1, nodes = count + 2;
@@ -721,7 +820,7 @@ chain_kernel(const u8* in, u32 in_size, u64 expected, u32 max_blocks, const u32*
   __syncthreads();
   const u32 len = s_len;
   if (!s_ok) {
-    if (tid == 0) { state[0] = 0; state[1] = 0; }
+    if (tid == 0) { state[0] = 0; state[1] = 0; state[2] = 0; }
     return;
   }
   for (u32 base = 0; base < len; base += blockDim.x) {
@@ -772,6 +871,12 @@ chain_kernel(const u8* in, u32 in_size, u64 expected, u32 max_blocks, const u32*
     state[0] = ok ? len : 0;
     state[1] = ok ? 1u : 0u;
   }
+  // Any path node whose tokens did not all fit the page arena sends the whole
+  // stream through the contiguous layout (symbols_kernel decodes again).
+  if (tid == 0) state[2] = 0;
+  __syncthreads();
+  for (u32 m = tid; m < len; m += blockDim.x)
+    if (infos[path[m]] & kInfoSpilled) state[2] = 1;
 }
 
 // Decode every path node again, writing its tokens at its place in the
@@ -782,7 +887,7 @@ symbols_kernel(const u8* in, u32 in_size, u64 expected, const u32* cands, const 
                u32* next_item, u32* syms, u32* fail_flag, const Tables* fixed) {
   __shared__ NodeShared sh;
   const u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-  if (!state[1]) return;
+  if (!state[1] || !state[2]) return;
   const u32 len = state[0];
   u32 window = 0, wanted = 0;
   zlib_framing(in, in_size, &window, &wanted);
@@ -792,10 +897,12 @@ symbols_kernel(const u8* in, u32 in_size, u64 expected, const u32* cands, const 
     item = __shfl_sync(kFullMask, item, 0);
     if (item >= len) break;
     const u32 node = path[item];
+    SymbolSink sink{SymbolSink::kContiguous, syms + tprefix[item], tokens[node], nullptr, nullptr,
+                    nullptr, 0, kNoPage, 0, kNoPage, 0, 0};
     const NodeResult r = warp_node<true>(in + 2, in_size - 6, cands[node], u32(expected), window,
-                                         *fixed, sh.dyn[warp], sh.round[warp],
-                                         syms + tprefix[item], tokens[node]);
-    if (lane == 0 && (!(r.info & kInfoOk) || r.size != sizes[node] || r.tokens != tokens[node]))
+                                         *fixed, sh.dyn[warp], sh.round[warp], sink);
+    if (lane == 0 && (!(r.info & kInfoOk) || (r.info & kInfoSpilled) || r.size != sizes[node] ||
+                      r.tokens != tokens[node]))
       atomicOr(fail_flag, 1u);
   }
 }
@@ -838,8 +945,9 @@ __device__ __forceinline__ u32 flushed_symbol(const u8* out, const u32* source,
 __global__ void __launch_bounds__(kExpandWarps * 32)
 expand_kernel(const u8* in, u32 in_size, const u32* path, const u32* prefix,
               const u32* tprefix, const u32* sizes, const u32* tokens, const u32* state,
-              const u32* syms, u32* next_item, u8* out, u32* source, u32* unresolved,
-              u32* fail_flag) {
+              const u32* syms, const u32* first_page, const u32* page_next,
+              const u32* page_used, u32 npages, u32* next_item, u8* out, u32* source,
+              u32* unresolved, u32* fail_flag) {
   __shared__ ExpandShared sh;
   const u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   // A failed chain or symbol pass leaves nothing to expand (the status path
@@ -854,9 +962,24 @@ expand_kernel(const u8* in, u32 in_size, const u32* path, const u32* prefix,
     item = __shfl_sync(kFullMask, item, 0);
     if (item >= len) break;
     const u32 node = path[item], start = prefix[item];
-    const u32* sy = syms + tprefix[item];
-    const u32 n = tokens[node];
+    // The node's tokens: one contiguous run, or its chain of arena pages
+    // (allocated in order, so page numbers strictly increase along it).
+    const bool contiguous = state[2] != 0;
+    u32 page = contiguous ? kNoPage : first_page[node], last_page = 0;
     u32 pos = 0, flushed = 0, bad = 0;
+    for (bool first_run = true;; first_run = false) {
+    const u32* sy = syms + tprefix[item];
+    u32 n = tokens[node];
+    if (!contiguous) {
+      if (page == kNoPage) break;
+      if (page >= npages || (!first_run && page <= last_page) || page_used[page] > kPageWords) {
+        bad = 1;
+        break;
+      }
+      sy = syms + u64(page) * kPageWords;
+      n = page_used[page];
+      last_page = page;
+    }
     for (u32 first = 0; first < n && !bad;) {
       if (pos - flushed >= kEmitFlush) {
         flush_symbols(ring, out, source, unresolved, start, flushed, pos);
@@ -945,6 +1068,9 @@ expand_kernel(const u8* in, u32 in_size, const u32* path, const u32* prefix,
       }
       pos = chunk_end;
       first += m;
+    }
+    if (contiguous || bad) break;
+    page = page_next[page];
     }
     if (!bad) flush_symbols(ring, out, source, unresolved, start, flushed, pos);
     __syncwarp();
@@ -1087,7 +1213,8 @@ u32 chain_levels(u32 capacity) {
   return levels;
 }
 
-ParallelScratch parallel_scratch_layout(u64 in_size, u64 expected, u32 capacity) {
+ParallelScratch parallel_scratch_layout(u64 in_size, u64 expected, u32 capacity,
+                                        u64 arena_slack) {
   ParallelScratch s{};
   const u64 body = in_size - 6;
   s.bitmap_words = (body * 8 + 31) / 32 + 1;
@@ -1099,6 +1226,11 @@ ParallelScratch parallel_scratch_layout(u64 in_size, u64 expected, u32 capacity)
   // Path tokens of a chain that passes its checks: at most one per output
   // byte, plus two words per stored block (at most kMaxBlocks blocks).
   s.symbol_words = expected + 2 * u64(kMaxBlocks) + 64;
+  // The page arena holds every candidate's tokens before the path is known:
+  // the path's words plus `arena_slack` words for partial last pages and the
+  // few tokens false candidates decode.  It also serves as the contiguous
+  // layout, so it is never smaller than that.
+  s.pages = u32((s.symbol_words + arena_slack + kPageWords - 1) / kPageWords);
   return s;
 }
 
@@ -1120,7 +1252,8 @@ cudaError_t launch_parallel_inflate(const u8* in, u64 in_size, u8* out, u64 expe
   note_launch();
   describe_kernel<<<node_grid, kNodeWarps * 32, 0, stream>>>(
       in, u32(in_size), expected, b.cands, b.total, s.capacity, b.counters, b.ends, b.sizes,
-      b.blocks, b.infos, b.tokens, static_cast<const Tables*>(dev.fixed_tables));
+      b.blocks, b.infos, b.tokens, b.first_page, b.syms, b.page_next, b.page_used,
+      b.page_cursor, s.pages, static_cast<const Tables*>(dev.fixed_tables));
   profile_end(stream);
   note_launch();
   chain_kernel<<<1, 1024, 0, stream>>>(in, u32(in_size), expected, max_blocks, b.cands, b.total,
@@ -1138,7 +1271,8 @@ cudaError_t launch_parallel_inflate(const u8* in, u64 in_size, u8* out, u64 expe
   note_launch();
   expand_kernel<<<expand_grid, kExpandWarps * 32, 0, stream>>>(
       in, u32(in_size), b.path, b.prefix, b.tprefix, b.sizes, b.tokens, b.state, b.syms,
-      b.counters + 2, out, b.source, b.unresolved, b.fail);
+      b.first_page, b.page_next, b.page_used, s.pages, b.counters + 2, out, b.source,
+      b.unresolved, b.fail);
   profile_end(stream);
   note_launch();
   resolve_kernel<<<u32(dev.sms) * 8, 256, 0, stream>>>(b.state, u32(s.out_words), b.unresolved,

@@ -81,7 +81,8 @@ struct ParallelScratch {
   u32 levels;         // pointer-doubling levels over capacity + 2 nodes
   u64 out_words;      // unresolved-position bitmap words
   u32 segments;       // Adler-32 segments of the output
-  u64 symbol_words;   // token arena of the path nodes
+  u64 symbol_words;   // contiguous token layout of the path nodes
+  u32 pages;          // token arena pages (1024 words each, at least symbol_words)
 };
 struct ParallelBuffers {
   u32* bitmap;        // bitmap_words, from discover_kernel
@@ -91,15 +92,18 @@ struct ParallelBuffers {
   u32 *ends, *sizes, *blocks, *infos, *tokens;  // capacity each
   u32* jump;          // (capacity + 2) * levels
   u32 *path, *prefix, *tprefix;  // capacity each: path nodes, output and token offsets
-  u32* state;         // 2: path length, chain ok
+  u32* state;         // 3: path length, chain ok, contiguous-layout fallback
   u32* counters;      // 3, zeroed: describe / symbols / expand work counters
-  u32* syms;          // symbol_words: the path nodes' tokens
+  u32* syms;          // pages * 1024 words: the token arena
+  u32 *first_page, *page_next, *page_used;  // capacity, pages, pages
+  u32* page_cursor;   // 1, zeroed: next free arena page
   u32* source;        // expected: absolute source of unresolved positions
   u32* unresolved;    // out_words, zeroed
   u64* parts;         // 2 * segments
   u32* fail;          // 1, zeroed
 };
-ParallelScratch parallel_scratch_layout(u64 in_size, u64 expected, u32 capacity);
+ParallelScratch parallel_scratch_layout(u64 in_size, u64 expected, u32 capacity,
+                                        u64 arena_slack);
 // Allocates and builds the fixed Huffman tables on the current device.
 cudaError_t build_fixed_tables(void** out);
 cudaError_t configure_parallel_inflate(int* emit_per_sm);

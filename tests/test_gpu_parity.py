@@ -267,3 +267,47 @@ def test_large_bytes_input_uses_threaded_staging(codec):
     payload = zlib.compress(raw, 1)
     assert codec.decompress_zlib_host(payload, len(raw), 0).tobytes() == raw
     assert codec.compress_zlib_host(raw, 0).tobytes() == oracle.compress(raw)
+
+
+# ---------------------------------------------------------------- token arena
+def _flushed_stream(raw, every, level=6):
+    """A stream cut into many blocks by full flushes (a block + an empty stored block each)."""
+    c = zlib.compressobj(level)
+    parts = []
+    for i in range(0, len(raw), every):
+        parts.append(c.compress(raw[i:i + every]))
+        parts.append(c.flush(zlib.Z_FULL_FLUSH))
+    parts.append(c.flush())
+    return b"".join(parts)
+
+
+def test_token_arena_overflow_falls_back_to_exact_layout(codec, monkeypatch):
+    """Many small blocks leave a partial arena page each; with no slack the
+    arena runs out and the second decoding pass must give the same bytes."""
+    import ctypes
+    from cuda_zlib import _native
+    lib = _native.library()
+    lib.cuda_zlib_b200_profile.argtypes = [ctypes.c_int]
+    lib.cuda_zlib_b200_profile_read.argtypes = [ctypes.c_char_p, ctypes.POINTER(ctypes.c_double),
+                                                ctypes.POINTER(ctypes.c_uint64)]
+    rng = random.Random(21)
+    raw = bytes(rng.choices(range(64), k=4 << 20))
+    payload = _flushed_stream(raw, 1500)
+    times = {}
+    for slack in (None, "0"):
+        if slack is None:
+            monkeypatch.delenv("CUDA_ZLIB_TOKEN_ARENA_SLACK", raising=False)
+        else:
+            monkeypatch.setenv("CUDA_ZLIB_TOKEN_ARENA_SLACK", slack)
+        lib.cuda_zlib_b200_profile(1)
+        out, meta = codec.decompress_zlib_checked(payload, len(raw), 0)
+        assert _meta(meta) == [0, 0]
+        assert _bytes(out) == raw
+        total, launches = ctypes.c_double(), ctypes.c_uint64()
+        lib.cuda_zlib_b200_profile_read(b"symbols_kernel", ctypes.byref(total),
+                                        ctypes.byref(launches))
+        lib.cuda_zlib_b200_profile(0)
+        assert launches.value == 1
+        times[slack] = total.value
+    # Without slack the second pass decodes every node; with it, it returns at once.
+    assert times["0"] > 5 * times[None]
