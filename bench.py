@@ -297,7 +297,8 @@ def run_gpu(args, rank, world):
     if world > 1:
         torch.distributed.barrier()
     kernels = {}
-    for name in ("serial_inflate_kernel", "discover_kernel", "describe_kernel", "symbols_kernel",
+    for name in ("serial_inflate_kernel", "discover_kernel", "validate_kernel", "describe_kernel",
+                 "symbols_kernel",
                  "expand_kernel",
                  "encode_chunks_kernel", "encode_pack_kernel"):
         total, launches = ctypes.c_double(), ctypes.c_uint64()
@@ -322,6 +323,7 @@ def run_gpu(args, rank, world):
         "encode_chunks_kernel": (U + length,),
         "encode_pack_kernel": (2 * length,),
         "discover_kernel": (len(l1), len(l6)),
+        "validate_kernel": (len(l1), len(l6)),
     }
     name, (total_ms, launches) = max(kernels.items(), key=lambda kv: kv[1][0])
     per_launch = algorithmic.get(name, (U,))

@@ -429,6 +429,10 @@ cudaError_t decompress(const u8* in, u64 size, int64_t max_candidates, int64_t m
   u32* count = nullptr;
   CZ_TRY(ws.allocate(&b.bitmap, layout.bitmap_words));
   CZ_TRY(ws.allocate(&count, 1));
+  const u32 queue_cap = discover_queue_capacity(size);
+  u32 *queue = nullptr, *queued = nullptr;
+  CZ_TRY(ws.allocate(&queue, queue_cap));
+  CZ_TRY(ws.allocate(&queued, 1));
   CZ_TRY(ws.allocate(&b.block_counts, layout.compact_blocks));
   CZ_TRY(ws.allocate(&b.total, 1));
   CZ_TRY(ws.allocate(&b.cands, capacity));
@@ -454,11 +458,13 @@ cudaError_t decompress(const u8* in, u64 size, int64_t max_candidates, int64_t m
   CZ_TRY(ws.allocate(&b.fail, 1));
   CZ_TRY(cudaMemsetAsync(b.bitmap, 0, layout.bitmap_words * sizeof(u32), stream));
   CZ_TRY(cudaMemsetAsync(count, 0, sizeof(u32), stream));
+  CZ_TRY(cudaMemsetAsync(queued, 0, sizeof(u32), stream));
   CZ_TRY(cudaMemsetAsync(b.counters, 0, 3 * sizeof(u32), stream));
   CZ_TRY(cudaMemsetAsync(b.page_cursor, 0, sizeof(u32), stream));
   CZ_TRY(cudaMemsetAsync(b.unresolved, 0, layout.out_words * sizeof(u32), stream));
   CZ_TRY(cudaMemsetAsync(b.fail, 0, sizeof(u32), stream));
-  CZ_TRY(launch_discover(in, size, b.bitmap, count, nullptr, dev->info, stream));
+  CZ_TRY(launch_discover(in, size, b.bitmap, count, queue, queue_cap, queued, nullptr,
+                         dev->info, stream));
   CZ_TRY(launch_parallel_inflate(in, size, out, expected, u32(max_blocks), layout, b, meta,
                                  dev->info, stream));
   CZ_TRY(launch_general_status(in, size, expected, u32(max_candidates), u32(max_blocks), b.bitmap,

@@ -15,6 +15,8 @@
 //   * general_status_kernel: one thread restating the chain walk and the
 //     emission history check, run only after the fast path failed, to report
 //     the status the reference's route reports.
+#include <algorithm>
+
 #include "kernels.h"
 #include "inflate_core.cuh"
 
@@ -151,25 +153,25 @@ __device__ bool stored_seed(const u8* body, u64 bytes, u64 byte, u64* endpoint) 
 
 constexpr u32 kDiscoverTile = 4096;     // body bytes per CTA step
 constexpr u32 kDiscoverThreads = 256;   // each thread scans 16 consecutive bytes
-constexpr u32 kDiscoverQueue = 4096;    // prefiltered offsets awaiting validation per tile
 
 // Candidates of every body bit offset (discover, _decode_kernels.py:
 // 998-1054): bit 0; offsets whose three header bits are BTYPE 2 and whose
 // dynamic header is valid; stored-block endpoint seeds.  Sets bit b of
 // bitmap[b >> 5] per candidate offset and adds the raw event count
 // (duplicates included).  Per tile (staged in shared memory with a 32-byte
-// halo), every thread first scans its 16 bytes' 128 offsets with cheap
-// filters: BTYPE 2, HLIT at most 29, and a complete code-length code (Kraft
-// sums of three packed 3-bit lengths from a table).  The few offsets that
-// pass go to a queue, and then the whole CTA validates queued headers one
-// per thread, instead of one lane validating while its warp waits.
+// halo), every thread scans its 16 bytes' 128 offsets with cheap filters:
+// BTYPE 2, HLIT at most 29, and a complete code-length code (Kraft sums of
+// three packed 3-bit lengths from a table).  The few offsets that pass go to
+// a global queue that validate_kernel works through one per thread, so the
+// long validations of true headers run side by side across the GPU instead
+// of holding up their tiles.  Offsets beyond the queue's capacity are
+// validated here.
 __global__ void __launch_bounds__(kDiscoverThreads)
-discover_kernel(const u8* in, u64 in_size, u32* bitmap, u32* count, const u32* gate) {
+discover_kernel(const u8* in, u64 in_size, u32* bitmap, u32* count, u32* queue, u32 queue_cap,
+                u32* queued, const u32* gate) {
   __shared__ __align__(16) u8 tile[kDiscoverTile + 32];
   __shared__ u8 kraft3[512];
-  __shared__ u16 queue[kDiscoverQueue];  // tile-relative bit offsets
-  __shared__ u32 queued;
-  __shared__ u8 cl_lut[kDiscoverThreads][128];  // per-thread code-length lookup
+  __shared__ u8 cl_lut[kDiscoverThreads][128];  // per-thread code-length lookup (overflow only)
   if (gate && *gate) return;
   if (in_size < 8) return;
   const u8* body = in + 2;
@@ -188,7 +190,6 @@ discover_kernel(const u8* in, u64 in_size, u32* bitmap, u32* count, const u32* g
     __syncthreads();
     for (u32 j = threadIdx.x; j < kDiscoverTile + 32; j += blockDim.x)
       tile[j] = base + j < bytes ? body[base + j] : u8(0);
-    if (threadIdx.x == 0) queued = 0;
     __syncthreads();
     const u32 j0 = threadIdx.x * 16;
     // 128-bit window of the 16 bytes starting at byte j0 + k.
@@ -231,10 +232,11 @@ discover_kernel(const u8* in, u64 in_size, u32* bitmap, u32* count, const u32* g
             y >>= 9;
           }
           if (kraft != 128) continue;
-          const u32 at = atomicAdd(&queued, 1u);
-          if (at < kDiscoverQueue) {
-            queue[at] = u16((j0 + k) * 8 + b);
-          } else if (dynamic_header_valid(body, bytes, byte * 8 + b, cl_lut[threadIdx.x])) {
+          const u64 bit = byte * 8 + b;
+          const u32 at = atomicAdd(queued, 1u);
+          if (at < queue_cap) {
+            queue[at] = u32(bit);
+          } else if (dynamic_header_valid(body, bytes, bit, cl_lut[threadIdx.x])) {
             ++events;  // queue full: validate here
             word_bits[k >> 2] |= 1u << ((k & 3) * 8 + b);
           }
@@ -245,14 +247,27 @@ discover_kernel(const u8* in, u64 in_size, u32* bitmap, u32* count, const u32* g
     }
     for (u32 w = 0; w < 4; ++w)
       if (word_bits[w]) atomicOr(&bitmap[((base + j0) * 8 >> 5) + w], word_bits[w]);
-    __syncthreads();
-    const u32 pending = min_u32(queued, kDiscoverQueue);
-    for (u32 i = threadIdx.x; i < pending; i += kDiscoverThreads) {
-      const u64 bit = base * 8 + queue[i];
-      if (dynamic_header_valid(body, bytes, bit, cl_lut[threadIdx.x])) {
-        ++events;
-        atomicOr(&bitmap[bit >> 5], 1u << (bit & 31));
-      }
+  }
+  for (u32 o = 16; o; o >>= 1) events += __shfl_xor_sync(kFullMask, events, o);
+  if ((threadIdx.x & 31) == 0 && events) atomicAdd(count, events);
+}
+
+// Full validation of the queued offsets, one per thread.
+__global__ void __launch_bounds__(kDiscoverThreads)
+validate_kernel(const u8* in, u64 in_size, const u32* queue, u32 queue_cap, const u32* queued,
+                u32* bitmap, u32* count, const u32* gate) {
+  __shared__ u8 cl_lut[kDiscoverThreads][128];
+  if (gate && *gate) return;
+  if (in_size < 8) return;
+  const u8* body = in + 2;
+  const u64 bytes = in_size - 6;
+  const u32 n = min_u32(*queued, queue_cap);
+  u32 events = 0;
+  for (u32 i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const u32 bit = queue[i];
+    if (dynamic_header_valid(body, bytes, bit, cl_lut[threadIdx.x])) {
+      ++events;
+      atomicOr(&bitmap[bit >> 5], 1u << (bit & 31));
     }
   }
   for (u32 o = 16; o; o >>= 1) events += __shfl_xor_sync(kFullMask, events, o);
@@ -605,8 +620,9 @@ __global__ void clear_on_failure_kernel(const u32* meta, u8* out, u64 n) {
   for (u64 i = u64(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) out[i] = 0;
 }
 
-cudaError_t launch_discover(const u8* in, u64 in_size, u32* bitmap, u32* count, const u32* gate,
-                            const DeviceInfo& dev, cudaStream_t stream) {
+cudaError_t launch_discover(const u8* in, u64 in_size, u32* bitmap, u32* count, u32* queue,
+                            u32 queue_cap, u32* queued, const u32* gate, const DeviceInfo& dev,
+                            cudaStream_t stream) {
   if (in_size < 8) return cudaSuccess;
   const u64 bytes = in_size - 6;
   u64 blocks = (bytes + kDiscoverTile - 1) / kDiscoverTile;
@@ -615,9 +631,24 @@ cudaError_t launch_discover(const u8* in, u64 in_size, u32* bitmap, u32* count, 
   if (blocks < 1) blocks = 1;
   profile_begin("discover_kernel", stream);
   note_launch();
-  discover_kernel<<<u32(blocks), kDiscoverThreads, 0, stream>>>(in, in_size, bitmap, count, gate);
+  discover_kernel<<<u32(blocks), kDiscoverThreads, 0, stream>>>(in, in_size, bitmap, count, queue,
+                                                                queue_cap, queued, gate);
+  profile_end(stream);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  profile_begin("validate_kernel", stream);
+  note_launch();
+  validate_kernel<<<u32(dev.sms) * 8, kDiscoverThreads, 0, stream>>>(
+      in, in_size, queue, queue_cap, queued, bitmap, count, gate);
   profile_end(stream);
   return cudaGetLastError();
+}
+
+// Queue of prefiltered offsets: generous for any stream (config-1 streams
+// queue one offset per ~160 body bytes); overflow is validated in place.
+u32 discover_queue_capacity(u64 in_size) {
+  const u64 body = in_size > 6 ? in_size - 6 : 0;
+  return u32(std::min<u64>(body / 16 + 4096, u64(1) << 26));
 }
 
 cudaError_t launch_general_status(const u8* in, u64 in_size, u64 expected, u32 max_candidates,

@@ -115,8 +115,11 @@ cudaError_t launch_parallel_inflate(const u8* in, u64 in_size, u8* out, u64 expe
 
 // General-route status path (single streams outside the small route).
 // bitmap: one bit per body bit offset, zeroed; count: zeroed u32.
-cudaError_t launch_discover(const u8* in, u64 in_size, u32* bitmap, u32* count, const u32* gate,
-                            const DeviceInfo& dev, cudaStream_t stream);
+// queue: discover_queue_capacity(in_size) u32; queued: zeroed u32.
+u32 discover_queue_capacity(u64 in_size);
+cudaError_t launch_discover(const u8* in, u64 in_size, u32* bitmap, u32* count, u32* queue,
+                            u32 queue_cap, u32* queued, const u32* gate, const DeviceInfo& dev,
+                            cudaStream_t stream);
 // meta[0] holds the fast path status; rewritten with the route's status;
 // a failed output is zeroed.
 cudaError_t launch_general_status(const u8* in, u64 in_size, u64 expected, u32 max_candidates,
