@@ -176,52 +176,7 @@ struct SymbolSink {
   }
 };
 
-// One token.  Returns kLaneWindow (decoded, *bytes output bytes),
-// kLaneBlockEnd (end-of-block code, consumed) or kLaneIrregular (a code the
-// serial decoder must judge, a distance beyond the window, or fewer than 48
-// body bits left, so every token taken here lies wholly inside the body;
-// nothing consumed that matters).
-__device__ __forceinline__ u32 count_token(Bits& c, const Tables& t, u32 window, u32* bytes) {
-  if (c.avail() < 48) return kLaneIrregular;
-  c.refill();
-  u32 v = c.lo;
-  u32 e = t.ll.lut[v & kLLMask];
-  u32 kind = entry_kind(e);
-  if (kind == kLong) {
-    e = decode_long(t.ll, v, LLFn());
-    kind = entry_kind(e);
-  }
-  if (kind == kLiteral) {
-    c.consume(entry_len(e));
-    *bytes = 1;
-    return kLaneWindow;
-  }
-  if (kind == kEnd) {
-    c.consume(entry_len(e));
-    return kLaneBlockEnd;
-  }
-  if (kind != kLength) return kLaneIrregular;
-  const u32 L = entry_len(e), E = entry_extra(e);
-  const u32 length = entry_value(e) + ((v >> L) & ((1u << E) - 1u));
-  c.consume(L + E);
-  c.refill();
-  v = c.lo;
-  u32 d = t.d.lut[v & 255u];
-  u32 dk = entry_kind(d);
-  if (dk == kLong) {
-    d = decode_long(t.d, v, DFn());
-    dk = entry_kind(d);
-  }
-  if (dk != kLiteral) return kLaneIrregular;
-  const u32 Ld = entry_len(d), Ed = entry_extra(d);
-  const u32 span = entry_value(d) + ((v >> Ld) & ((1u << Ed) - 1u));
-  if (span > window) return kLaneIrregular;
-  c.consume(Ld + Ed);
-  *bytes = length;
-  return kLaneWindow;
-}
-
-// A node's tokens as the symbols kernel writes them: a literal byte;
+// A node's tokens as the decoder writes them: a literal byte;
 // kMatchFlag | distance << 9 | length; or kStoredFlag | length followed by a
 // word with the stored bytes' body offset.  Empty stored blocks write none.
 constexpr u32 kMatchFlag = 0x80000000u;
@@ -236,8 +191,58 @@ __device__ __forceinline__ u32 match_symbol(u32 length, u32 dist) {
   return kMatchFlag | (dist << 9) | length;
 }
 
-// One token, as count_token, also returning its symbol word.
-__device__ __forceinline__ u32 symbol_token(Bits& c, const Tables& t, u32 window, u32* bytes,
+// Bit reader of the passes: Bits with the next word already requested, so a
+// refill does not wait for a load it could have issued a word earlier.
+struct AheadBits {
+  const u32* words;  // 4-byte aligned, at or below the first body byte
+  u32 shift, last, end;  // as in Bits
+  u32 idx;           // index of `next`, the word appended at the next refill
+  u32 nbits, lo, hi, next;
+
+  __device__ __forceinline__ u32 load(u32 i) const { return i <= last ? __ldg(words + i) : 0u; }
+  __device__ __forceinline__ void init(const u8* body, u32 bytes) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(body);
+    words = reinterpret_cast<const u32*>(a & ~uintptr_t(3));
+    shift = u32(a & 3) * 8;
+    end = bytes * 8;
+    last = bytes ? (shift + end - 1) >> 5 : 0;
+  }
+  __device__ __forceinline__ u32 pos() const { return idx * 32 - nbits - shift; }
+  __device__ __forceinline__ u32 avail() const {
+    const u32 p = pos();
+    return p <= end ? end - p : 0;
+  }
+  __device__ __forceinline__ void seek(u32 p) {
+    const u32 a = shift + p;
+    idx = (a >> 5) + 1;
+    lo = load(idx - 1) >> (a & 31);
+    hi = 0;
+    nbits = 32 - (a & 31);
+    next = load(idx);
+    refill();
+  }
+  __device__ __forceinline__ void refill() {
+    if (nbits <= 32) {
+      lo |= next << nbits;                      // shifts of 32 give 0
+      hi |= __funnelshift_lc(next, 0u, nbits);  // high word of next << nbits
+      nbits += 32;
+      next = load(++idx);
+    }
+  }
+  __device__ __forceinline__ void consume(u32 n) {
+    lo = __funnelshift_r(lo, hi, n);
+    hi >>= n;
+    nbits -= n;
+  }
+};
+
+// One token.  Returns kLaneWindow (decoded: *bytes output bytes, *sym its
+// symbol word), kLaneBlockEnd (end-of-block code, consumed) or
+// kLaneIrregular (a code the serial decoder must judge, a distance beyond
+// the window, or fewer than 48 body bits left, so every token taken here
+// lies wholly inside the body).
+template <typename Reader>
+__device__ __forceinline__ u32 symbol_token(Reader& c, const Tables& t, u32 window, u32* bytes,
                                             u32* sym) {
   if (c.avail() < 48) return kLaneIrregular;
   c.refill();
@@ -309,7 +314,7 @@ __device__ RoundResult warp_round(const u8* body, u32 body_bytes, u32 start, u32
   const u32 round_end = start + 32 * kRoundWindow;
   u32* my_marks = r.marks[lane];
   for (u32 k = 0; k < kMarkWords; ++k) my_marks[k] = 0;
-  Bits c;
+  AheadBits c;
   c.init(body, body_bytes);
   u32 bytes = 0, sym = 0;
   // Phase 1: speculative decode of the window, marking token starts.
@@ -980,12 +985,19 @@ expand_kernel(const u8* in, u32 in_size, const u32* path, const u32* prefix,
       n = page_used[page];
       last_page = page;
     }
+    // Tokens of the chunk after the current one are loaded while the current
+    // one is expanded (chunks usually take 32 tokens).
+    u32 ahead_at = 0, ahead = lane < n ? sy[lane] : kStoredFlag;
     for (u32 first = 0; first < n && !bad;) {
       if (pos - flushed >= kEmitFlush) {
         flush_symbols(ring, out, source, unresolved, start, flushed, pos);
         flushed = pos;
       }
-      const u32 head = sy[first];
+      const u32 k = first + lane;
+      const u32 tk = first == ahead_at ? ahead : (k < n ? sy[k] : kStoredFlag);
+      ahead_at = first + 32;
+      ahead = ahead_at + lane < n ? sy[ahead_at + lane] : kStoredFlag;
+      const u32 head = __shfl_sync(kFullMask, tk, 0);
       if (head & kStoredFlag && !(head & kMatchFlag)) {
         // Stored bytes: flush, then copy straight from the input.
         const u32 count = head & 0xffffu, src = sy[first + 1];
@@ -1002,8 +1014,6 @@ expand_kernel(const u8* in, u32 in_size, const u32* path, const u32* prefix,
         continue;
       }
       // Up to 32 tokens, stopping before a stored block.
-      const u32 k = first + lane;
-      const u32 tk = k < n ? sy[k] : kStoredFlag;
       const bool stored = (tk & kStoredFlag) && !(tk & kMatchFlag);
       const u32 stops = __ballot_sync(kFullMask, stored);
       const u32 avail = stops ? __ffs(stops) - 1 : 32u;
