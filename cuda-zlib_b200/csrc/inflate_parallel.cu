@@ -934,8 +934,10 @@ __device__ void flush_symbols(const u16* ring, u8* out, u32* source, u32* unreso
 __device__ __forceinline__ u32 flushed_symbol(const u8* out, const u32* source,
                                               const u32* unresolved, u32 prefix, u32 q) {
   const u32 at = prefix + q;
-  if ((unresolved[at >> 5] >> (at & 31)) & 1u) return 256 + (prefix - 1 - source[at]);
-  return out[at];
+  const u32 word = unresolved[at >> 5];
+  const u32 byte = out[at];  // issued alongside the bitmap load
+  if ((word >> (at & 31)) & 1u) return 256 + (prefix - 1 - source[at]);
+  return byte;
 }
 
 // Expand every path node's tokens into the output (warp per node, work
@@ -1030,8 +1032,6 @@ expand_kernel(const u8* in, u32 in_size, const u32* path, const u32* prefix,
       const bool take = lane < m;
       const u32 chunk_end = pos + __shfl_sync(kFullMask, incl, m - 1);
       const u32 at = pos + incl - size;
-      if (take && !match) ring[at & kEmitMask] = u16(tk & 255u);
-      __syncwarp();
       // Symbol of node position dst + j - dist for a copy: a marker before
       // the node start, the ring while the entry is still there (nothing at
       // or past chunk_end is written), else the output.
@@ -1042,16 +1042,43 @@ expand_kernel(const u8* in, u32 in_size, const u32* path, const u32* prefix,
         return flushed_symbol(out, source, unresolved, start, q);
       };
       const u32 length = tk & 511u, dist = (tk >> 9) & 0xffffu;
-      // Short copies that read nothing this chunk writes (or only their own
-      // bytes, when first in the chunk) go one per lane.
-      const bool own = take && match && length <= 32 &&
-                       (length <= dist ? at + length <= pos + dist : at == pos);
       if (take && match && dist > start + at) bad = 1;
-      if (own && !bad)
-        for (u32 j = 0; j < length; ++j) ring[(at + j) & kEmitMask] = u16(source_symbol(at, dist, j));
       if (__any_sync(kFullMask, bad)) {
         bad = 1;
         break;
+      }
+      // Copies that read nothing this chunk writes: their source ends before
+      // the chunk, or (a copy overlapping itself) their period lies before it.
+      const bool own = take && match &&
+                       (length <= dist ? at + length <= pos + dist : at == pos);
+      // Output-byte parallel pass: lane b takes chunk bytes pos + b,
+      // pos + b + 32, ...; the token covering a byte comes from a binary
+      // search over the scanned ends, and literal bytes and bytes of the
+      // copies above are written at once, whatever the copies' lengths.
+      const u32 direct = __ballot_sync(kFullMask, take && (!match || own));
+      const u32 total = chunk_end - pos;
+      for (u32 base_b = 0; base_b < total; base_b += 32) {
+        const u32 b = base_b + lane;
+        u32 t = 0;  // tokens that end at or before byte b
+        for (u32 step = 16; step; step >>= 1) {
+          const u32 probe = t + step - 1;
+          const u32 end_at = __shfl_sync(kFullMask, incl, probe < 32 ? probe : 31u);
+          if (probe < m && end_at <= b) t += step;
+        }
+        const u32 src = t < 32 ? t : 31u;
+        const u32 t_tok = __shfl_sync(kFullMask, tk, src);
+        const u32 t_at = __shfl_sync(kFullMask, at, src);
+        if (b < total && ((direct >> src) & 1u)) {
+          u32 v;
+          if (!(t_tok & kMatchFlag)) {
+            v = t_tok & 255u;
+          } else {
+            const u32 t_len = t_tok & 511u, t_dist = (t_tok >> 9) & 0xffffu;
+            const u32 j = pos + b - t_at;
+            v = source_symbol(t_at, t_dist, t_len <= t_dist ? j : j % t_dist);
+          }
+          ring[(pos + b) & kEmitMask] = u16(v);
+        }
       }
       __syncwarp();
       u32 copies = __ballot_sync(kFullMask, take && match && !own);
