@@ -101,6 +101,7 @@ struct EncodeShared {
   u32 seg_entry[kEncThreads];
   u32 seg_bits[kEncThreads];
   u32 warp_sums[kEncWarps];
+  u32 rle_sums[kEncWarps];
   u64 adler_s1[kEncWarps];
   u64 adler_s2[kEncWarps];
   u32 extra_bits, token_count, dist_tokens;
@@ -621,38 +622,78 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
       u32 nll = 286, ndist = 30;
       while (nll > 257 && !s.lengths[nll - 1]) --nll;
       while (ndist > 1 && !s.lengths[286 + ndist - 1]) --ndist;
-      // Run-length code the code lengths (enc_rle, _encode_kernels.py:163-191).
-      const u32 total = nll + ndist;
-      u32 i = 0, size = 0;
-      u32* cf = s.freq + 316;
-      while (i < total) {
-        const u32 value = i < nll ? s.lengths[i] : s.lengths[286 + i - nll];
-        u32 run = 1;
-        while (i + run < total &&
-               (i + run < nll ? s.lengths[i + run] : s.lengths[286 + i + run - nll]) == value)
-          ++run;
-        i += run;
-        if (value) {
-          s.rle_sym[size] = u8(value); s.rle_extra[size++] = 0; ++cf[value]; --run;
-          while (run >= 3) {
-            const u32 take = run < 6 ? run : 6;
-            s.rle_sym[size] = 16; s.rle_extra[size++] = u8(take - 3); ++cf[16]; run -= take;
-          }
-        } else {
-          while (run >= 11) {
-            const u32 take = run < 138 ? run : 138;
-            s.rle_sym[size] = 18; s.rle_extra[size++] = u8(take - 11); ++cf[18]; run -= take;
-          }
-          if (run >= 3) {
-            s.rle_sym[size] = 17; s.rle_extra[size++] = u8(run - 3); ++cf[17]; run = 0;
-          }
-        }
-        while (run) { s.rle_sym[size] = u8(value); s.rle_extra[size++] = 0; ++cf[value]; --run; }
-      }
       s.nll = nll;
       s.ndist = ndist;
-      s.rle_size = size;
     }
+    __syncthreads();
+    // Run-length code the code lengths (enc_rle, _encode_kernels.py:163-191):
+    // the thread at the start of each run of equal lengths emits that run's
+    // symbols, in the reference's order, at the place a block scan gives.
+    const u32 nll = s.nll, total = nll + s.ndist;
+    auto code_length = [&](u32 i) -> u32 {
+      return i < nll ? s.lengths[i] : s.lengths[286 + i - nll];
+    };
+    u32 value = 0, run = 0, count = 0;
+    const bool first = tid < total && (tid == 0 || code_length(tid) != code_length(tid - 1));
+    if (first) {
+      value = code_length(tid);
+      run = 1;
+      while (tid + run < total && code_length(tid + run) == value) ++run;
+      if (value) {
+        // The length, then repeats of 3..6 (code 16), then single lengths.
+        const u32 r = run - 1, tail = r % 6;
+        count = 1 + r / 6 + (tail >= 3 ? 1u : tail);
+      } else {
+        // Zero runs of 11..138 (code 18), then one of 3..10 (code 17), then
+        // single zeros.
+        const u32 tail = run % 138;
+        count = run / 138 + (tail >= 11 ? 1u : tail >= 3 ? 1u : tail);
+      }
+    }
+    u32 incl_count = count;
+    for (u32 o = 1; o < 32; o <<= 1) {
+      const u32 v = __shfl_up_sync(kFullMask, incl_count, o);
+      if (lane >= o) incl_count += v;
+    }
+    if (lane == 31) s.warp_sums[warp] = incl_count;
+    __syncthreads();
+    u32 at = incl_count - count, rle_size = 0;
+    for (u32 w = 0; w < kEncWarps; ++w) {
+      if (w < warp) at += s.warp_sums[w];
+      rle_size += s.warp_sums[w];
+    }
+    if (first) {
+      u32* cf = s.freq + 316;
+      auto emit = [&](u32 sym, u32 extra) {
+        s.rle_sym[at] = u8(sym);
+        s.rle_extra[at] = u8(extra);
+        atomicAdd(&cf[sym], 1u);
+        ++at;
+      };
+      if (value) {
+        emit(value, 0);
+        u32 left = run - 1;
+        while (left >= 3) {
+          const u32 take = left < 6 ? left : 6;
+          emit(16, take - 3);
+          left -= take;
+        }
+        while (left--) emit(value, 0);
+      } else {
+        u32 left = run;
+        while (left >= 11) {
+          const u32 take = left < 138 ? left : 138;
+          emit(18, take - 11);
+          left -= take;
+        }
+        if (left >= 3) {
+          emit(17, left - 3);
+          left = 0;
+        }
+        while (left--) emit(0, 0);
+      }
+    }
+    if (tid == 0) s.rle_size = rle_size;
     __syncthreads();
     if (trees) trees = cta_tree(s, s.freq + 316, 19, 7, s.lengths + 316, s.codes + 316);
     if (tid == 0) {
@@ -712,53 +753,65 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
       my_bits += dyn ? s.lengths[data[p]] : fixed_ll_len(data[p]);
     }
   });
-  // Header size.
-  if (tid == 0) {
-    u32 hb = 3;
-    if (dyn) {
-      hb += 14 + 3 * s.ncl;
-      for (u32 i = 0; i < s.rle_size; ++i) {
-        const u32 sym = s.rle_sym[i];
-        hb += s.lengths[316 + sym] + (sym == 16 ? 2u : sym == 17 ? 3u : sym == 18 ? 7u : 0u);
-      }
-    }
-    s.header_bits = hb;
+  // Bits of this thread's run-length coded length (a dynamic header codes at
+  // most 320 of them, fewer than the threads); a block scan places them.
+  u32 rle_bits = 0;
+  if (dyn && tid < s.rle_size) {
+    const u32 sym = s.rle_sym[tid];
+    rle_bits = s.lengths[316 + sym] + (sym == 16 ? 2u : sym == 17 ? 3u : sym == 18 ? 7u : 0u);
   }
-  // Exclusive block scan of my_bits.
-  u32 incl = my_bits;
+  // Exclusive block scans of my_bits and rle_bits.
+  u32 incl = my_bits, rle_incl = rle_bits;
   for (u32 o = 1; o < 32; o <<= 1) {
     const u32 v = __shfl_up_sync(kFullMask, incl, o);
-    if (lane >= o) incl += v;
+    const u32 rv = __shfl_up_sync(kFullMask, rle_incl, o);
+    if (lane >= o) {
+      incl += v;
+      rle_incl += rv;
+    }
   }
-  if (lane == 31) s.warp_sums[warp] = incl;
+  if (lane == 31) {
+    s.warp_sums[warp] = incl;
+    s.rle_sums[warp] = rle_incl;
+  }
   // Zero the slot words the packed block occupies (edge words are ORed).
   u32* words = reinterpret_cast<u32*>(slot);
   const u32 used_words = min_u32((s.extent + 3) / 4 + 1, slot_bytes / 4);
   for (u32 i = tid; i < used_words; i += kEncThreads) words[i] = 0;
   __syncthreads();
-  u32 before = 0;
-  for (u32 w = 0; w < warp; ++w) before += s.warp_sums[w];
-  u32 body_bits = 0;
-  for (u32 w = 0; w < kEncWarps; ++w) body_bits += s.warp_sums[w];
-  const u32 header_bits = s.header_bits;
+  u32 before = 0, rle_before = 0, body_bits = 0, rle_total = 0;
+  for (u32 w = 0; w < kEncWarps; ++w) {
+    if (w < warp) {
+      before += s.warp_sums[w];
+      rle_before += s.rle_sums[w];
+    }
+    body_bits += s.warp_sums[w];
+    rle_total += s.rle_sums[w];
+  }
+  // Block header, then (dynamic) the three counts and the code-length lengths.
+  const u32 fixed_head = dyn ? 17 + 3 * s.ncl : 3;
+  const u32 header_bits = fixed_head + (dyn ? rle_total : 0u);
   const u32 my_start = header_bits + before + incl - my_bits;
   if (tid == 0) {
     Packer pk;
-    pk.start(words, 0, header_bits, used_words);
+    pk.start(words, 0, fixed_head, used_words);
     pk.put((final ? 1u : 0u) | (dyn ? 4u : 2u), 3);
     if (dyn) {
       pk.put(s.nll - 257, 5);
       pk.put(s.ndist - 1, 5);
       pk.put(s.ncl - 4, 4);
       for (u32 i = 0; i < s.ncl; ++i) pk.put(s.lengths[316 + kClOrder[i]], 3);
-      for (u32 i = 0; i < s.rle_size; ++i) {
-        const u32 sym = s.rle_sym[i];
-        pk.put(s.codes[316 + sym], s.lengths[316 + sym]);
-        if (sym >= 16) pk.put(s.rle_extra[i], sym == 16 ? 2u : sym == 17 ? 3u : 7u);
-      }
     }
-    pk.first_word = 0;  // the header's own words may be shared with token words
-    pk.last_word = ~0ull;
+    pk.finish();
+  }
+  // The run-length coded lengths, one per thread.
+  if (rle_bits) {
+    const u32 at = fixed_head + rle_before + rle_incl - rle_bits;
+    const u32 sym = s.rle_sym[tid];
+    Packer pk;
+    pk.start(words, at, at + rle_bits, used_words);
+    pk.put(s.codes[316 + sym], s.lengths[316 + sym]);
+    if (sym >= 16) pk.put(s.rle_extra[tid], sym == 16 ? 2u : sym == 17 ? 3u : 7u);
     pk.finish();
   }
   {
