@@ -162,27 +162,39 @@ __device__ bool cta_tree(EncodeShared& s, const u32* freq, u32 alphabet, u32 lim
     const u32 nodes = alphabet + m - 1;  // leaves' ids stay below alphabet
     if (tid == 0) {
       // Leaf ids are below every inner id, so equal weights take the leaf.
+      // The head of each queue and the element after it stay in registers,
+      // so a pick compares registers and the shared-memory load it starts
+      // is needed only a pick later.
       u32 leaf = 0, inner = alphabet, next = alphabet;
-      u32 leaf_id = s.sorted[0], leaf_w = s.leafw[0], inner_w = 0;
+      u32 leaf_id = s.sorted[0], leaf_w = s.leafw[0];
+      u32 leaf2_id = m > 1 ? u32(s.sorted[1]) : 0u, leaf2_w = m > 1 ? s.leafw[1] : 0u;
+      u32 inner_w = 0, inner2_w = 0;  // nodes `inner` and `inner + 1`, when they exist
       for (u32 step = 0; step + 1 < m; ++step) {
         u32 pick[2], picked_w[2];
+#pragma unroll
         for (u32 k = 0; k < 2; ++k) {
           const bool take_leaf = leaf < m && (inner == next || leaf_w <= inner_w);
           if (take_leaf) {
             pick[k] = leaf_id;
             picked_w[k] = leaf_w;
-            if (++leaf < m) { leaf_id = s.sorted[leaf]; leaf_w = s.leafw[leaf]; }
+            ++leaf;
+            leaf_id = leaf2_id;
+            leaf_w = leaf2_w;
+            if (leaf + 1 < m) { leaf2_id = s.sorted[leaf + 1]; leaf2_w = s.leafw[leaf + 1]; }
           } else {
             pick[k] = inner;
             picked_w[k] = inner_w;
-            if (++inner < next) inner_w = s.weight[inner];
+            ++inner;
+            inner_w = inner2_w;
+            if (inner + 1 < next) inner2_w = s.weight[inner + 1];
           }
         }
         const u32 w = picked_w[0] + picked_w[1];
         s.weight[next] = w;
         s.parent[pick[0]] = u16(next);
         s.parent[pick[1]] = u16(next);
-        if (inner == next) inner_w = w;
+        if (inner == next) inner_w = w;             // the queue was empty
+        else if (inner + 1 == next) inner2_w = w;   // it follows the head
         ++next;
       }
     }
