@@ -152,30 +152,38 @@ __device__ bool stored_seed(const u8* body, u64 bytes, u64 byte, u64* endpoint) 
 }
 
 constexpr u32 kDiscoverTile = 4096;     // body bytes per CTA step
-constexpr u32 kDiscoverThreads = 256;   // each thread scans 16 consecutive bytes
+constexpr u32 kDiscoverThreads = 256;
+constexpr u32 kDiscoverWarps = kDiscoverThreads / 32;
+// Tile bytes per warp, scanned in two rounds of 64 words (two per lane).
+constexpr u32 kDiscoverWarpWords = kDiscoverTile / 4 / kDiscoverWarps;
+// Offsets a round can pass: at most every other bit offset passes the BTYPE
+// filter (bit b+1 clear and bit b+2 set), so 16 of a word's 32.
+constexpr u32 kDiscoverPending = 2 * 32 * 16;
 
 // Candidates of every body bit offset (discover, _decode_kernels.py:
 // 998-1054): bit 0; offsets whose three header bits are BTYPE 2 and whose
 // dynamic header is valid; stored-block endpoint seeds.  Sets bit b of
 // bitmap[b >> 5] per candidate offset and adds the raw event count
 // (duplicates included).  Per tile (staged in shared memory with a 32-byte
-// halo), every thread scans its 16 bytes' 128 offsets with cheap filters:
-// BTYPE 2, HLIT at most 29, and a complete code-length code (Kraft sums of
-// three packed 3-bit lengths from a table).  The few offsets that pass go to
-// a global queue that validate_kernel works through one per thread, so the
-// long validations of true headers run side by side across the GPU instead
-// of holding up their tiles.  Offsets beyond the queue's capacity are
-// validated here.
+// halo), each lane filters the 32 offsets of a tile word at once with word
+// operations (BTYPE 2, HLIT at most 29), the warp gathers the survivors, and
+// then tests them 32 at a time, all lanes busy, for a complete code-length
+// code (Kraft sums of three packed 3-bit lengths from a table).  The few
+// offsets that pass go to a global queue, one atomic per warp batch, that
+// validate_kernel works through one per thread, so the long validations of
+// true headers run side by side across the GPU.  Offsets beyond the queue's
+// capacity are validated here.
 __global__ void __launch_bounds__(kDiscoverThreads)
 discover_kernel(const u8* in, u64 in_size, u32* bitmap, u32* count, u32* queue, u32 queue_cap,
                 u32* queued, const u32* gate) {
-  __shared__ __align__(16) u8 tile[kDiscoverTile + 32];
+  __shared__ u32 tile[kDiscoverTile / 4 + 8];
   __shared__ u8 kraft3[512];
-  __shared__ u8 cl_lut[kDiscoverThreads][128];  // per-thread code-length lookup (overflow only)
+  __shared__ u16 pending[kDiscoverWarps][kDiscoverPending];  // tile bit offsets
   if (gate && *gate) return;
   if (in_size < 8) return;
   const u8* body = in + 2;
   const u64 bytes = in_size - 6;
+  const u32 lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (u32 t = threadIdx.x; t < 512; t += blockDim.x) {
     u32 sum = 0;
     for (u32 k = 0; k < 3; ++k) {
@@ -184,69 +192,108 @@ discover_kernel(const u8* in, u64 in_size, u32* bitmap, u32* count, u32* queue, 
     }
     kraft3[t] = u8(sum);
   }
+  u8* const tile_bytes = reinterpret_cast<u8*>(tile);
   u32 events = 0;
   for (u64 base = u64(blockIdx.x) * kDiscoverTile; base < bytes;
        base += u64(gridDim.x) * kDiscoverTile) {
     __syncthreads();
     for (u32 j = threadIdx.x; j < kDiscoverTile + 32; j += blockDim.x)
-      tile[j] = base + j < bytes ? body[base + j] : u8(0);
+      tile_bytes[j] = base + j < bytes ? body[base + j] : u8(0);
     __syncthreads();
-    const u32 j0 = threadIdx.x * 16;
-    // 128-bit window of the 16 bytes starting at byte j0 + k.
-    u64 lo = 0, hi = 0;
-    for (u32 k = 0; k < 8; ++k) lo |= u64(tile[j0 + k]) << (8 * k);
-    for (u32 k = 0; k < 8; ++k) hi |= u64(tile[j0 + 8 + k]) << (8 * k);
-    u32 word_bits[4] = {0, 0, 0, 0};
-    for (u32 k = 0; k < 16; ++k) {
-      const u64 byte = base + j0 + k;
-      if (byte < bytes) {
-        // Stored seed: LEN/NLEN complements at this byte.
-        if ((((lo >> 16) ^ lo) & 0xffffu) == 0xffffu) {
-          u64 e;
-          if (stored_seed(body, bytes, byte, &e)) {
-            ++events;
-            atomicOr(&bitmap[(e * 8) >> 5], 1u << ((e * 8) & 31));
+    const u64 left = bytes - base;  // body bytes from the tile start (> 0)
+    for (u32 round = 0; round < 2; ++round) {
+      u32 masks[2];
+      u32 mine = 0;
+#pragma unroll
+      for (u32 h = 0; h < 2; ++h) {
+        const u32 wi = warp * kDiscoverWarpWords + round * 64 + h * 32 + lane;
+        const u32 w0 = tile[wi], w1 = tile[wi + 1];
+        const u64 x = u64(w0) | (u64(w1) << 32);
+        // BTYPE 2 at offset b: bit b+1 clear, bit b+2 set; HLIT (bits
+        // b+3..b+7) at most 29, i.e. not all of bits b+4..b+7 set.
+        u64 all4 = x & (x >> 1);
+        all4 &= all4 >> 2;
+        u32 m = u32(~x >> 1) & u32(x >> 2) & ~u32(all4 >> 4);
+        // Offsets at or past the body end are not candidates.
+        const u64 first = u64(wi) * 4;
+        if (first + 4 > left) m = first >= left ? 0u : m & ((1u << (8 * u32(left - first))) - 1u);
+        if (base == 0 && wi == 0) {
+          m &= ~1u;  // bit 0 is always a candidate
+          ++events;
+          atomicOr(&bitmap[0], 1u);
+        }
+        // Stored seed: LEN/NLEN complements at one of the word's bytes.
+#pragma unroll
+        for (u32 k = 0; k < 4; ++k) {
+          const u32 v = __funnelshift_r(w0, w1, 8 * k);
+          if (((v ^ (v >> 16)) & 0xffffu) == 0xffffu && first + k < left) {
+            u64 e;
+            if (stored_seed(body, bytes, base + first + k, &e)) {
+              ++events;
+              atomicOr(&bitmap[(e * 8) >> 5], 1u << ((e * 8) & 31));
+            }
           }
         }
-        // BTYPE 2 at offset b: bit b+1 clear, bit b+2 set.
-        u32 mask = u32((~lo >> 1) & (lo >> 2)) & 0xffu;
-        if (byte == 0) {
-          mask &= ~1u;
-          ++events;  // bit 0 is always a candidate
-          word_bits[k >> 2] |= 1u << ((k & 3) * 8);
+        masks[h] = m;
+        mine += __popc(m);
+      }
+      // Gather the survivors of the warp's 64 words in order.
+      u32 incl = mine;
+#pragma unroll
+      for (u32 o = 1; o < 32; o <<= 1) {
+        const u32 v = __shfl_up_sync(kFullMask, incl, o);
+        if (lane >= o) incl += v;
+      }
+      const u32 total = __shfl_sync(kFullMask, incl, 31);
+      u32 at = incl - mine;
+#pragma unroll
+      for (u32 h = 0; h < 2; ++h) {
+        const u32 bit0 = (warp * kDiscoverWarpWords + round * 64 + h * 32 + lane) * 32;
+        u32 m = masks[h];
+        while (m) {
+          pending[warp][at++] = u16(bit0 + __ffs(m) - 1);
+          m &= m - 1;
         }
-        while (mask) {
-          const u32 b = __ffs(mask) - 1;
-          mask &= mask - 1;
-          const u64 x = (lo >> (b + 3)) | (hi << (61 - b));          // from HLIT
-          if ((x & 31u) > 29u) continue;
-          const u32 nc = u32((x >> 10) & 15u) + 4;
-          const u32 s = b + 17;
-          u64 y = (lo >> s) | (hi << (64 - s));                       // CL lengths
+      }
+      __syncwarp();
+      for (u32 batch = 0; batch < total; batch += 32) {
+        const u32 i = batch + lane;
+        bool pass = false;
+        u32 p = 0;
+        if (i < total) {
+          p = pending[warp][i];
+          // HCLEN and the code-length code lengths: 64 bits from p + 13.
+          const u32 q = p + 13, wq = q >> 5, sh = q & 31;
+          const u32 a = tile[wq], b = tile[wq + 1], c = tile[wq + 2];
+          const u64 x = u64(__funnelshift_r(a, b, sh)) | (u64(__funnelshift_r(b, c, sh)) << 32);
+          const u32 nc = u32(x & 15u) + 4;
+          const u64 y = (x >> 4) & ((1ull << (3 * nc)) - 1);  // lengths beyond nc read as 0
           u32 kraft = 0;
-          for (u32 i = 0; i < nc && kraft <= 128; i += 3) {
-            u32 packed = u32(y) & 511u;
-            const u32 left = nc - i;
-            if (left < 3) packed &= (1u << (3 * left)) - 1u;
-            kraft += kraft3[packed];
-            y >>= 9;
-          }
-          if (kraft != 128) continue;
-          const u64 bit = byte * 8 + b;
-          const u32 at = atomicAdd(queued, 1u);
-          if (at < queue_cap) {
-            queue[at] = u32(bit);
-          } else if (dynamic_header_valid(body, bytes, bit, cl_lut[threadIdx.x])) {
-            ++events;  // queue full: validate here
-            word_bits[k >> 2] |= 1u << ((k & 3) * 8 + b);
+#pragma unroll
+          for (u32 g = 0; g < 7; ++g) kraft += kraft3[u32(y >> (9 * g)) & 511u];
+          pass = kraft == 128;  // complete code-length code
+        }
+        const u32 ballot = __ballot_sync(kFullMask, pass);
+        if (ballot) {
+          u32 slot = 0;
+          if (lane == 0) slot = atomicAdd(queued, u32(__popc(ballot)));
+          slot = __shfl_sync(kFullMask, slot, 0) + __popc(ballot & ((1u << lane) - 1u));
+          if (pass) {
+            const u64 bit = base * 8 + p;
+            if (slot < queue_cap) {
+              queue[slot] = u32(bit);
+            } else {
+              u8 lut[128];  // queue full: validate here
+              if (dynamic_header_valid(body, bytes, bit, lut)) {
+                ++events;
+                atomicOr(&bitmap[bit >> 5], 1u << (bit & 31));
+              }
+            }
           }
         }
       }
-      lo = (lo >> 8) | (hi << 56);
-      hi = (hi >> 8) | (u64(tile[j0 + 16 + k]) << 56);
+      __syncwarp();
     }
-    for (u32 w = 0; w < 4; ++w)
-      if (word_bits[w]) atomicOr(&bitmap[((base + j0) * 8 >> 5) + w], word_bits[w]);
   }
   for (u32 o = 16; o; o >>= 1) events += __shfl_xor_sync(kFullMask, events, o);
   if ((threadIdx.x & 31) == 0 && events) atomicAdd(count, events);

@@ -117,15 +117,16 @@ int CudaZlibTrimWorkspacePool(int device);
 /* Library version string, e.g. "0.1.0".  No reference counterpart. */
 const char* cuda_zlib_b200_version(void);
 
+/* Kernel launches this library has issued since it was loaded, all devices
+ * and threads together (benchmarks report it per timed region). */
+uint64_t cuda_zlib_b200_launches(void);
+
 /* Opt-in kernel timing, no reference counterpart (the reference profiles
  * with Nsight Systems only, PROFILING.md).  enable != 0 clears the totals and
  * brackets every named kernel launch with CUDA events on its stream;
  * profile_read waits for the recorded events and returns the summed device
  * time and launch count of one kernel ("serial_inflate_kernel",
  * "encode_chunks_kernel", ...).  Off by default; costs two events a launch. */
-/* Kernel launches this library has issued since it was loaded, all devices
- * and threads together (benchmarks report it per timed region). */
-uint64_t cuda_zlib_b200_launches(void);
 int cuda_zlib_b200_profile(int enable);
 int cuda_zlib_b200_profile_read(const char* kernel, double* total_ms, uint64_t* launches);
 
