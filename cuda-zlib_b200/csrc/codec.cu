@@ -456,6 +456,7 @@ cudaError_t decompress(const u8* in, u64 size, int64_t max_candidates, int64_t m
   CZ_TRY(ws.allocate(&b.unresolved, layout.out_words));
   CZ_TRY(ws.allocate(&b.parts, 2 * u64(layout.segments)));
   CZ_TRY(ws.allocate(&b.fail, 1));
+  CZ_TRY(ws.allocate(&b.stash, round_stash_words(dev->info)));
   CZ_TRY(cudaMemsetAsync(b.bitmap, 0, layout.bitmap_words * sizeof(u32), stream));
   CZ_TRY(cudaMemsetAsync(count, 0, sizeof(u32), stream));
   CZ_TRY(cudaMemsetAsync(queued, 0, sizeof(u32), stream));

@@ -421,30 +421,53 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
       __syncwarp();
       head = (head + count) & (kRing - 1);
     };
-    // Lane i looks at positions base + 4i .. base + 4i + 3 (one word of
-    // lenv); a position's rank among the owned ones follows from four
-    // ballots, one per byte of the word.
+    // An iteration covers 512 positions: lane i looks at the words of lenv
+    // holding positions base + 128 j + 4 i .. + 3 (j = 0..3).  A byte is
+    // owned when its low kOwnerBits bits equal the warp index: with those
+    // bits xor-ed with the index and the others masked off, adding 0x7f to
+    // each byte sets its top bit exactly when the byte is nonzero.  The four
+    // per-word counts (at most 4 each, 128 over the warp) are packed in one
+    // word, so one warp scan places every owned position in order.
     const u32* low_bytes = reinterpret_cast<const u32*>(lenv);
-    const u32 below = (1u << lane) - 1u;
-    for (u32 base = 0; base < hashed; base += 128) {
-      const u32 p0 = base + 4 * lane;
-      const u32 word = p0 < hashed ? low_bytes[p0 >> 2] : 0u;
-      u32 own[4], before = 0, total = 0;
-      for (u32 k = 0; k < 4; ++k) {
-        own[k] = (p0 + k < hashed && ((word >> (8 * k)) & (kEncWarps - 1)) == warp) ? 1u : 0u;
-        const u32 ballot = __ballot_sync(kFullMask, own[k]);
-        before += __popc(ballot & below);
-        total += __popc(ballot);
+    const u32 pattern = warp * 0x01010101u;
+    constexpr u32 kOwnerMask = (kEncWarps - 1) * 0x01010101u;
+    for (u32 base = 0; base < hashed; base += 512) {
+      u32 owned[4], packed = 0;
+#pragma unroll
+      for (u32 j = 0; j < 4; ++j) {
+        const u32 q = base + 128 * j + 4 * lane;
+        u32 m = 0;
+        if (q < hashed) {
+          const u32 x = (low_bytes[q >> 2] ^ pattern) & kOwnerMask;
+          m = ~(x + 0x7f7f7f7fu) & 0x80808080u;
+          if (hashed - q < 4) m &= (1u << (8 * (hashed - q))) - 1u;
+        }
+        owned[j] = m;
+        packed |= u32(__popc(m)) << (8 * j);
       }
-      for (u32 k = 0; k < 4; ++k) {
-        if (own[k]) ring[(head + fill + before) & (kRing - 1)] = u16(p0 + k);
-        before += own[k];
+      u32 incl = packed;
+#pragma unroll
+      for (u32 o = 1; o < 32; o <<= 1) {
+        const u32 v = __shfl_up_sync(kFullMask, incl, o);
+        if (lane >= o) incl += v;
       }
-      fill += total;
-      __syncwarp();
-      while (fill >= 32) {
-        batch(32);
-        fill -= 32;
+      const u32 totals = __shfl_sync(kFullMask, incl, 31), excl = incl - packed;
+#pragma unroll
+      for (u32 j = 0; j < 4; ++j) {
+        // fill < 32 here and a word adds at most 128: the ring never wraps
+        // onto positions still waiting.
+        u32 at = head + fill + ((excl >> (8 * j)) & 0xffu);
+        u32 m = owned[j];
+        while (m) {
+          ring[at++ & (kRing - 1)] = u16(base + 128 * j + 4 * lane + ((__ffs(m) - 1) >> 3));
+          m &= m - 1;
+        }
+        fill += (totals >> (8 * j)) & 0xffu;
+        __syncwarp();
+        while (fill >= 32) {
+          batch(32);
+          fill -= 32;
+        }
       }
     }
     if (fill) batch(fill);

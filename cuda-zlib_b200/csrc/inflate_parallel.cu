@@ -65,6 +65,10 @@ constexpr u32 kPassPages = 40;     // pages one pass can reach (32 Ki tokens)
 // whole window of marks almost never runs out.
 constexpr u32 kRoundWindow = 1024;  // body bits per lane per round
 constexpr u32 kMarkWords = kRoundWindow / 32;
+// Tokens a lane keeps from phases 1 and 2 of a round (a config-1 window
+// holds about 150).  Phase 3 copies a region's tokens from there instead of
+// decoding them again, unless the lane decoded more than this.
+constexpr u32 kStash = 256;
 
 enum LaneEnd : u32 {
   kLaneWindow = 0,     // reached the window end / a boundary past the round
@@ -302,14 +306,21 @@ __device__ __forceinline__ u32 marks_between(const u32* row, u32 a, u32 b) {
 // every lane: the committed position, the output bytes and tokens before
 // it, and whether the block continues, ended (position after its
 // end-of-block code) or goes to the serial decoder at that position.  With
-// `syms` (room for `room` words), the round's tokens are written there in
-// order: each lane's region holds as many tokens as it marked after its
-// entry plus those it decoded past its window, so a warp scan places every
-// lane's tokens before phase 3 decodes them again.
+// kWrite, the round's tokens go to the sink in order: each lane's region
+// holds as many tokens as it marked after its entry plus those it decoded
+// past its window, so a warp scan places every lane's tokens before phase 3
+// writes them.  `stash` (the warp's kStash * 32 words, or null) keeps every
+// lane's decoded tokens, token k of lane i at word 32 k + i, so that the
+// stores of one loop step are coalesced; phase 3 copies a region from there,
+// starting at the token its entry mark counts to.
 template <bool kWrite>
 __device__ RoundResult warp_round(const u8* body, u32 body_bytes, u32 start, u32 window,
-                                  const Tables& t, RoundShared& r, SymbolSink& sink) {
+                                  const Tables& t, RoundShared& r, SymbolSink& sink,
+                                  u32* stash) {
   const u32 lane = threadIdx.x & 31u;
+  u32* const kept_at = stash ? stash + lane : nullptr;
+  u32 kept = 0;         // tokens decoded in phases 1 and 2
+  u32 block_end = 0;    // position after an end-of-block code either phase met
   const u32 s = start + lane * kRoundWindow, wend = s + kRoundWindow;
   const u32 round_end = start + 32 * kRoundWindow;
   u32* my_marks = r.marks[lane];
@@ -333,8 +344,11 @@ __device__ RoundResult warp_round(const u8* body, u32 body_bytes, u32 start, u32
       if (st != kLaneWindow) {
         stop = st;
         stop_at = p;
+        if (st == kLaneBlockEnd) block_end = c.pos();
         break;
       }
+      if (kept_at && kept < kStash) kept_at[kept * 32] = sym;
+      ++kept;
     }
   }
   __syncwarp();
@@ -359,8 +373,11 @@ __device__ RoundResult warp_round(const u8* body, u32 body_bytes, u32 start, u32
       if (st != kLaneWindow) {
         link = st;
         link_at = p;
+        if (st == kLaneBlockEnd) block_end = c.pos();
         break;
       }
+      if (kept_at && kept < kStash) kept_at[kept * 32] = sym;
+      ++kept;
       ++cont_tokens;
     }
   }
@@ -406,9 +423,19 @@ __device__ RoundResult warp_round(const u8* body, u32 body_bytes, u32 start, u32
     __syncwarp();
   }
   const bool drop = kWrite && r.drop;
-  // Phase 3: decode this lane's region again, exactly.
+  // Phase 3: the region's tokens, copied from the stash when the lane kept
+  // them all (its tokens before the entry are the marks before it), else
+  // decoded again.
   u32 total = 0, tokens = 0, finish = to, broken = 0;
-  if (visited) {
+  const u32 entry = visited && kept_at ? marks_between(my_marks, 0, from - s) : 0u;
+  if (visited && kept_at && kept <= kStash) {
+    for (; tokens < expect; ++tokens) {
+      const u32 word = kept_at[(entry + tokens) * 32];
+      if (kWrite && !drop) *sink.slot(r, before + tokens) = word;
+      total += word & kMatchFlag ? word & 511u : 1u;
+    }
+    if (end == kLaneBlockEnd) finish = block_end;
+  } else if (visited) {
     c.seek(from);
     // The same tokens phases 1 and 2 took; any other answer would be a
     // decoder fault, and the round is then dropped.
@@ -554,7 +581,7 @@ struct NodeResult {
 template <bool kWrite>
 __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expected, u32 window,
                                 const Tables& fixed, Tables& dyn, RoundShared& rounds,
-                                SymbolSink& sink) {
+                                SymbolSink& sink, u32* stash) {
   const u32 lane = threadIdx.x & 31u;
   NodeResult r{start, 0, 0, 0, 0};
   Bits c;
@@ -687,7 +714,8 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
       }
     } else if (action == kRound) {
       const u32 from = __shfl_sync(kFullMask, lane == 0 ? c.pos() : 0u, 0);
-      const RoundResult rr = warp_round<kWrite>(body, bytes, from, window, dyn, rounds, sink);
+      const RoundResult rr = warp_round<kWrite>(body, bytes, from, window, dyn, rounds, sink,
+                                                stash);
       if (lane == 0) {
         if (rr.bytes > limit - produced) {
           // The round would pass the output bound: the serial decoder takes
@@ -728,9 +756,10 @@ __global__ void __launch_bounds__(kNodeWarps * 32)
 describe_kernel(const u8* in, u32 in_size, u64 expected, const u32* cands, const u32* total,
                 u32 capacity, u32* next_item, u32* ends, u32* sizes, u32* blocks, u32* infos,
                 u32* tokens, u32* first_page, u32* pool, u32* page_next, u32* page_used,
-                u32* page_cursor, u32 npages, const Tables* fixed) {
+                u32* page_cursor, u32 npages, const Tables* fixed, u32* stash) {
   __shared__ NodeShared sh;
   const u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  u32* const warp_stash = stash + (u64(blockIdx.x) * kNodeWarps + warp) * (32 * kStash);
   u32 window = 0, wanted = 0;
   if (zlib_framing(in, in_size, &window, &wanted)) return;
   const u32 count = min_u32(*total, capacity);
@@ -742,7 +771,7 @@ describe_kernel(const u8* in, u32 in_size, u64 expected, const u32* cands, const
     SymbolSink sink{SymbolSink::kPages, pool, 0, page_next, page_used, page_cursor, npages,
                     kNoPage, 0, kNoPage, 0, 0};
     const NodeResult r = warp_node<true>(in + 2, in_size - 6, cands[item], u32(expected), window,
-                                         *fixed, sh.dyn[warp], sh.round[warp], sink);
+                                         *fixed, sh.dyn[warp], sh.round[warp], sink, warp_stash);
     if (lane == 0) {
       first_page[item] = sink.first;
       ends[item] = r.end;
@@ -889,9 +918,10 @@ chain_kernel(const u8* in, u32 in_size, u64 expected, u32 max_blocks, const u32*
 __global__ void __launch_bounds__(kNodeWarps * 32)
 symbols_kernel(const u8* in, u32 in_size, u64 expected, const u32* cands, const u32* path,
                const u32* tprefix, const u32* sizes, const u32* tokens, const u32* state,
-               u32* next_item, u32* syms, u32* fail_flag, const Tables* fixed) {
+               u32* next_item, u32* syms, u32* fail_flag, const Tables* fixed, u32* stash) {
   __shared__ NodeShared sh;
   const u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  u32* const warp_stash = stash + (u64(blockIdx.x) * kNodeWarps + warp) * (32 * kStash);
   if (!state[1] || !state[2]) return;
   const u32 len = state[0];
   u32 window = 0, wanted = 0;
@@ -905,7 +935,7 @@ symbols_kernel(const u8* in, u32 in_size, u64 expected, const u32* cands, const 
     SymbolSink sink{SymbolSink::kContiguous, syms + tprefix[item], tokens[node], nullptr, nullptr,
                     nullptr, 0, kNoPage, 0, kNoPage, 0, 0};
     const NodeResult r = warp_node<true>(in + 2, in_size - 6, cands[node], u32(expected), window,
-                                         *fixed, sh.dyn[warp], sh.round[warp], sink);
+                                         *fixed, sh.dyn[warp], sh.round[warp], sink, warp_stash);
     if (lane == 0 && (!(r.info & kInfoOk) || (r.info & kInfoSpilled) || r.size != sizes[node] ||
                       r.tokens != tokens[node]))
       atomicOr(fail_flag, 1u);
@@ -1271,6 +1301,12 @@ ParallelScratch parallel_scratch_layout(u64 in_size, u64 expected, u32 capacity,
   return s;
 }
 
+// CTAs of describe_kernel and symbols_kernel, and the stash their warps use.
+static u32 node_ctas(const DeviceInfo& dev) { return u32(dev.sms) * 4; }
+u64 round_stash_words(const DeviceInfo& dev) {
+  return u64(node_ctas(dev)) * kNodeWarps * 32 * kStash;
+}
+
 cudaError_t launch_parallel_inflate(const u8* in, u64 in_size, u8* out, u64 expected,
                                     u32 max_blocks, const ParallelScratch& s,
                                     const ParallelBuffers& b, u32* meta, const DeviceInfo& dev,
@@ -1284,13 +1320,13 @@ cudaError_t launch_parallel_inflate(const u8* in, u64 in_size, u8* out, u64 expe
   note_launch();
   cand_write_kernel<<<s.compact_blocks, 256, 0, stream>>>(b.bitmap, u32(s.bitmap_words),
                                                           b.block_counts, b.cands, s.capacity);
-  const u32 node_grid = u32(dev.sms) * 4;
+  const u32 node_grid = node_ctas(dev);
   profile_begin("describe_kernel", stream);
   note_launch();
   describe_kernel<<<node_grid, kNodeWarps * 32, 0, stream>>>(
       in, u32(in_size), expected, b.cands, b.total, s.capacity, b.counters, b.ends, b.sizes,
       b.blocks, b.infos, b.tokens, b.first_page, b.syms, b.page_next, b.page_used,
-      b.page_cursor, s.pages, static_cast<const Tables*>(dev.fixed_tables));
+      b.page_cursor, s.pages, static_cast<const Tables*>(dev.fixed_tables), b.stash);
   profile_end(stream);
   note_launch();
   chain_kernel<<<1, 1024, 0, stream>>>(in, u32(in_size), expected, max_blocks, b.cands, b.total,
@@ -1301,7 +1337,7 @@ cudaError_t launch_parallel_inflate(const u8* in, u64 in_size, u8* out, u64 expe
   note_launch();
   symbols_kernel<<<node_grid, kNodeWarps * 32, 0, stream>>>(
       in, u32(in_size), expected, b.cands, b.path, b.tprefix, b.sizes, b.tokens, b.state,
-      b.counters + 1, b.syms, b.fail, static_cast<const Tables*>(dev.fixed_tables));
+      b.counters + 1, b.syms, b.fail, static_cast<const Tables*>(dev.fixed_tables), b.stash);
   profile_end(stream);
   const u32 expand_grid = u32(dev.sms) * u32(dev.emit_per_sm > 0 ? dev.emit_per_sm : 1);
   profile_begin("expand_kernel", stream);

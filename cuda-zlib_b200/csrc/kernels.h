@@ -101,9 +101,11 @@ struct ParallelBuffers {
   u32* unresolved;    // out_words, zeroed
   u64* parts;         // 2 * segments
   u32* fail;          // 1, zeroed
+  u32* stash;         // round_stash_words: tokens the node warps keep per round
 };
 ParallelScratch parallel_scratch_layout(u64 in_size, u64 expected, u32 capacity,
                                         u64 arena_slack);
+u64 round_stash_words(const DeviceInfo& dev);
 // Allocates and builds the fixed Huffman tables on the current device.
 cudaError_t build_fixed_tables(void** out);
 cudaError_t configure_parallel_inflate(int* emit_per_sm);
