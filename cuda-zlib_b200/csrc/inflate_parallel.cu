@@ -39,6 +39,14 @@ namespace cz {
 
 constexpr u32 kNodeWarps = 4;      // warps per CTA in describe
 constexpr u32 kExpandWarps = 4;    // warps per CTA in expand
+constexpr u32 kLaneTokens = 4;     // consecutive tokens per lane in an expand chunk
+constexpr u32 kChunkTokens = 32 * kLaneTokens;
+// Ring entry of a copy byte not yet known: kPending | r, the symbol r
+// positions back (r < 8192; bytes are below 256, markers below 33024).
+constexpr u32 kPending = 0xe000u;
+// Token flag, in the chunk's shared copy only: the copy reads nothing the
+// chunk writes.
+constexpr u32 kOwnFlag = 0x20000000u;
 constexpr u32 kEmitRing = 4096;    // u16 history entries per emitting warp
 constexpr u32 kEmitMask = kEmitRing - 1;
 constexpr u32 kEmitFlush = 2048;   // pending symbols that trigger a flush
@@ -481,6 +489,8 @@ struct NodeShared {
 };
 struct ExpandShared {
   __align__(16) u16 ring[kExpandWarps][kEmitRing];
+  u32 token[kExpandWarps][kChunkTokens];  // the chunk's tokens and output offsets
+  u32 at[kExpandWarps][kChunkTokens];
 };
 
 // ---------------------------------------------------------------------------
@@ -971,10 +981,10 @@ __device__ __forceinline__ u32 flushed_symbol(const u8* out, const u32* source,
 }
 
 // Expand every path node's tokens into the output (warp per node, work
-// stealing).  The warp takes 32 tokens at a time: a scan of their sizes
-// places them, literals land in parallel, short copies that read only
-// earlier output go one per lane, and the other copies follow in order,
-// each across the warp.  The ring holds the node's recent output as u16
+// stealing).  The warp takes kChunkTokens tokens at a time, kLaneTokens
+// consecutive ones per lane: a scan of their sizes places them, then every
+// output byte of the chunk is written in parallel, copies that read the
+// chunk's own output through pending entries resolved in a second pass.  The ring holds the node's recent output as u16
 // symbols: a byte, or 256 + k for the byte k + 1 positions before the node
 // start (a reference into an earlier node; copies propagate it); full
 // stretches of the ring flush to the output, markers as source positions in
@@ -1018,18 +1028,32 @@ expand_kernel(const u8* in, u32 in_size, const u32* path, const u32* prefix,
       last_page = page;
     }
     // Tokens of the chunk after the current one are loaded while the current
-    // one is expanded (chunks usually take 32 tokens).
-    u32 ahead_at = 0, ahead = lane < n ? sy[lane] : kStoredFlag;
+    // one is expanded (chunks usually take kChunkTokens tokens).
+    auto load_tokens = [&](u32* t, u32 from) {
+#pragma unroll
+      for (u32 k = 0; k < kLaneTokens; ++k) {
+        const u32 i = from + kLaneTokens * lane + k;
+        t[k] = i < n ? sy[i] : kStoredFlag;
+      }
+    };
+    u32 ahead[kLaneTokens];
+    u32 ahead_at = 0;
+    load_tokens(ahead, 0);
     for (u32 first = 0; first < n && !bad;) {
       if (pos - flushed >= kEmitFlush) {
         flush_symbols(ring, out, source, unresolved, start, flushed, pos);
         flushed = pos;
       }
-      const u32 k = first + lane;
-      const u32 tk = first == ahead_at ? ahead : (k < n ? sy[k] : kStoredFlag);
-      ahead_at = first + 32;
-      ahead = ahead_at + lane < n ? sy[ahead_at + lane] : kStoredFlag;
-      const u32 head = __shfl_sync(kFullMask, tk, 0);
+      u32 tk[kLaneTokens];
+      if (first == ahead_at) {
+#pragma unroll
+        for (u32 k = 0; k < kLaneTokens; ++k) tk[k] = ahead[k];
+      } else {
+        load_tokens(tk, first);
+      }
+      ahead_at = first + kChunkTokens;
+      load_tokens(ahead, ahead_at);
+      const u32 head = __shfl_sync(kFullMask, tk[0], 0);
       if (head & kStoredFlag && !(head & kMatchFlag)) {
         // Stored bytes: flush, then copy straight from the input.
         const u32 count = head & 0xffffu, src = sy[first + 1];
@@ -1045,23 +1069,66 @@ expand_kernel(const u8* in, u32 in_size, const u32* path, const u32* prefix,
         __syncwarp();
         continue;
       }
-      // Up to 32 tokens, stopping before a stored block.
-      const bool stored = (tk & kStoredFlag) && !(tk & kMatchFlag);
-      const u32 stops = __ballot_sync(kFullMask, stored);
-      const u32 avail = stops ? __ffs(stops) - 1 : 32u;
-      const bool valid = lane < avail, match = valid && (tk & kMatchFlag);
-      const u32 size = !valid ? 0u : match ? (tk & 511u) : 1u;
-      u32 incl = size;
+      // The chunk's tokens stop before a stored block: lane i holds tokens
+      // first + kLaneTokens i + k, valid up to the first stored one.
+      u32 mine = kLaneTokens;
+#pragma unroll
+      for (u32 k = kLaneTokens; k-- > 0;)
+        if ((tk[k] & kStoredFlag) && !(tk[k] & kMatchFlag)) mine = k;
+      const u32 stops = __ballot_sync(kFullMask, mine < kLaneTokens);
+      const u32 stop_lane = stops ? __ffs(stops) - 1 : 32u;
+      const u32 valid = lane < stop_lane ? kLaneTokens : lane == stop_lane ? mine : 0u;
+      // Output offsets: the lane's own prefix, then a warp scan.
+      u32 size[kLaneTokens], lane_bytes = 0;
+#pragma unroll
+      for (u32 k = 0; k < kLaneTokens; ++k) {
+        size[k] = k >= valid ? 0u : (tk[k] & kMatchFlag) ? (tk[k] & 511u) : 1u;
+        lane_bytes += size[k];
+      }
+      u32 incl = lane_bytes;
+#pragma unroll
       for (u32 o = 1; o < 32; o <<= 1) {
         const u32 v = __shfl_up_sync(kFullMask, incl, o);
         if (lane >= o) incl += v;
       }
-      // Tokens whose output fits without wrapping onto unflushed entries.
+      // Tokens whose output fits without wrapping onto unflushed entries
+      // (a prefix of the chunk: ends only grow).
       const u32 budget = kEmitRing - (pos - flushed);
-      const u32 m = __popc(__ballot_sync(kFullMask, valid && incl <= budget));
-      const bool take = lane < m;
-      const u32 chunk_end = pos + __shfl_sync(kFullMask, incl, m - 1);
-      const u32 at = pos + incl - size;
+      u32 at[kLaneTokens], taken = 0, end = incl - lane_bytes, last_end = 0;
+#pragma unroll
+      for (u32 k = 0; k < kLaneTokens; ++k) {
+        at[k] = pos + end;
+        end += size[k];
+        if (k < valid && end <= budget) {
+          taken = k + 1;
+          last_end = end;
+        }
+      }
+      const u32 chunk_end = pos + __reduce_max_sync(kFullMask, last_end);
+      const u32 m = __reduce_add_sync(kFullMask, taken);
+      // The chunk's tokens for the byte pass, copies flagged when they read
+      // nothing the chunk writes (their source ends before the chunk, or,
+      // overlapping themselves, their period lies before it).
+      bool broken = false, outside = false;
+#pragma unroll
+      for (u32 k = 0; k < kLaneTokens; ++k) {
+        if (k >= taken) continue;
+        u32 t = tk[k];
+        if (t & kMatchFlag) {
+          const u32 length = t & 511u, dist = (t >> 9) & 0xffffu;
+          if (dist > start + at[k]) broken = true;
+          if (length <= dist ? at[k] + length <= pos + dist : at[k] == pos) t |= kOwnFlag;
+          else outside = true;
+        }
+        sh.token[warp][kLaneTokens * lane + k] = t;
+        sh.at[warp][kLaneTokens * lane + k] = at[k];
+      }
+      if (__any_sync(kFullMask, broken)) {
+        bad = 1;
+        break;
+      }
+      const bool waits = __any_sync(kFullMask, outside);
+      __syncwarp();
       // Symbol of node position dst + j - dist for a copy: a marker before
       // the node start, the ring while the entry is still there (nothing at
       // or past chunk_end is written), else the output.
@@ -1071,68 +1138,64 @@ expand_kernel(const u8* in, u32 in_size, const u32* path, const u32* prefix,
         if (q + kEmitRing >= chunk_end) return ring[q & kEmitMask];
         return flushed_symbol(out, source, unresolved, start, q);
       };
-      const u32 length = tk & 511u, dist = (tk >> 9) & 0xffffu;
-      if (take && match && dist > start + at) bad = 1;
-      if (__any_sync(kFullMask, bad)) {
-        bad = 1;
-        break;
-      }
-      // Copies that read nothing this chunk writes: their source ends before
-      // the chunk, or (a copy overlapping itself) their period lies before it.
-      const bool own = take && match &&
-                       (length <= dist ? at + length <= pos + dist : at == pos);
-      // Output-byte parallel pass: lane b takes chunk bytes pos + b,
-      // pos + b + 32, ...; the token covering a byte comes from a binary
-      // search over the scanned ends, and literal bytes and bytes of the
-      // copies above are written at once, whatever the copies' lengths.
-      const u32 direct = __ballot_sync(kFullMask, take && (!match || own));
+      // Output-byte parallel pass: lane b takes chunk bytes 32 w + b.  The
+      // token covering a byte is the last one starting at or before it: the
+      // lanes OR their tokens' start bits of the window into one word, whose
+      // popcount below the byte adds to the starts of earlier windows.  A
+      // copy that reads the chunk's own output leaves a pending entry,
+      // kPending | r, whose r reaches past the copy (a periodic copy points
+      // into its seed period).
       const u32 total = chunk_end - pos;
-      for (u32 base_b = 0; base_b < total; base_b += 32) {
-        const u32 b = base_b + lane;
-        u32 t = 0;  // tokens that end at or before byte b
-        for (u32 step = 16; step; step >>= 1) {
-          const u32 probe = t + step - 1;
-          const u32 end_at = __shfl_sync(kFullMask, incl, probe < 32 ? probe : 31u);
-          if (probe < m && end_at <= b) t += step;
+      u32 starts = 0;
+      for (u32 w = 0; w * 32 < total; ++w) {
+        u32 mine_bits = 0;
+#pragma unroll
+        for (u32 k = 0; k < kLaneTokens; ++k) {
+          const u32 o = at[k] - pos;
+          if (k < taken && (o >> 5) == w) mine_bits |= 1u << (o & 31);
         }
-        const u32 src = t < 32 ? t : 31u;
-        const u32 t_tok = __shfl_sync(kFullMask, tk, src);
-        const u32 t_at = __shfl_sync(kFullMask, at, src);
-        if (b < total && ((direct >> src) & 1u)) {
+        const u32 word = __reduce_or_sync(kFullMask, mine_bits);
+        const u32 t = starts + __popc(word & ((2u << lane) - 1u)) - 1;
+        starts += __popc(word);
+        const u32 b = w * 32 + lane;
+        if (b < total) {
+          const u32 tw = sh.token[warp][t];
           u32 v;
-          if (!(t_tok & kMatchFlag)) {
-            v = t_tok & 255u;
+          if (!(tw & kMatchFlag)) {
+            v = tw & 255u;
           } else {
-            const u32 t_len = t_tok & 511u, t_dist = (t_tok >> 9) & 0xffffu;
-            const u32 j = pos + b - t_at;
-            v = source_symbol(t_at, t_dist, t_len <= t_dist ? j : j % t_dist);
+            const u32 t_len = tw & 511u, t_dist = (tw >> 9) & 0xffffu;
+            const u32 j = pos + b - sh.at[warp][t];
+            if (tw & kOwnFlag) v = source_symbol(pos + b - j, t_dist, t_len <= t_dist ? j : j % t_dist);
+            else v = kPending | (t_len <= t_dist ? t_dist : t_dist * (j / t_dist + 1));
+          }
+          ring[(pos + b) & kEmitMask] = u16(v);
+        }
+      }
+      if (waits) {
+        // Pending entries to symbols: each follows its chain, which only
+        // steps back and leaves a copy at every step.  An entry another lane
+        // resolves at the same time reads as either form; both lead to the
+        // same symbol.
+        __syncwarp();
+        for (u32 b = lane; b < total; b += 32) {
+          u32 x = pos + b;
+          u32 v = ring[x & kEmitMask];
+          if (v < kPending) continue;
+          u32 r = v - kPending;
+          for (;;) {
+            if (r > x) { v = 256 + (r - x - 1); break; }  // before the node start
+            const u32 q = x - r;
+            if (q + kEmitRing < chunk_end) { v = flushed_symbol(out, source, unresolved, start, q); break; }
+            v = ring[q & kEmitMask];
+            if (v < kPending) break;
+            x = q;
+            r = v - kPending;
           }
           ring[(pos + b) & kEmitMask] = u16(v);
         }
       }
       __syncwarp();
-      u32 copies = __ballot_sync(kFullMask, take && match && !own);
-      while (copies) {
-        const u32 who = __ffs(copies) - 1;
-        copies &= copies - 1;
-        const u32 dst = __shfl_sync(kFullMask, at, who);
-        const u32 c_len = __shfl_sync(kFullMask, length, who);
-        const u32 c_dist = __shfl_sync(kFullMask, dist, who);
-        if (c_len <= c_dist) {
-          for (u32 j = lane; j < c_len; j += 32)
-            ring[(dst + j) & kEmitMask] = u16(source_symbol(dst, c_dist, j));
-        } else {
-          // Periodic seeds from before dst.
-          u32 sd = lane % c_dist;
-          const u32 step = 32 % c_dist;
-          for (u32 j = lane; j < c_len; j += 32) {
-            ring[(dst + j) & kEmitMask] = u16(source_symbol(dst, c_dist, sd));
-            sd += step;
-            if (sd >= c_dist) sd -= c_dist;
-          }
-        }
-        __syncwarp();
-      }
       pos = chunk_end;
       first += m;
     }
