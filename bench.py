@@ -304,8 +304,7 @@ def run_gpu(args, rank, world):
         torch.distributed.barrier()
     kernels = {}
     for name in ("serial_inflate_kernel", "discover_kernel", "validate_kernel", "describe_kernel",
-                 "symbols_kernel",
-                 "expand_kernel",
+                 "symbols_kernel", "expand_kernel", "resolve_kernel",
                  "encode_chunks_kernel", "encode_pack_kernel"):
         total, launches = ctypes.c_double(), ctypes.c_uint64()
         lib.cuda_zlib_b200_profile_read(name.encode(), ctypes.byref(total), ctypes.byref(launches))
@@ -325,6 +324,7 @@ def run_gpu(args, rank, world):
         "serial_inflate_kernel": (U + len(l1), U + len(l6)),
         "symbols_kernel": (len(l1), len(l6)),
         "expand_kernel": (U, U),
+        "resolve_kernel": (U // 8, U // 8),
         "describe_kernel": (len(l1), len(l6)),
         "encode_chunks_kernel": (U + length,),
         "encode_pack_kernel": (2 * length,),

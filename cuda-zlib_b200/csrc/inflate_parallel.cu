@@ -1208,22 +1208,51 @@ expand_kernel(const u8* in, u32 in_size, const u32* path, const u32* prefix,
   }
 }
 
-// Resolve unresolved positions by chasing source positions.
+// Resolve unresolved positions by chasing source positions.  Markers come
+// in runs (a node's first window reads the node before it), so a warp takes
+// 32 bitmap words and resolves the positions of up to four nonzero words at
+// once, one lane per bit position, the four chases interleaved so their
+// loads overlap.
+constexpr u32 kResolveWays = 4;
 __global__ void resolve_kernel(const u32* state, u32 words, const u32* unresolved,
                                const u32* source, u8* out) {
   if (!state[1]) return;
-  const u64 stride = u64(gridDim.x) * blockDim.x;
-  for (u64 w = u64(blockIdx.x) * blockDim.x + threadIdx.x; w < words; w += stride) {
-    u32 bits = unresolved[w];
-    while (bits) {
-      const u32 b = __ffs(bits) - 1;
-      bits &= bits - 1;
-      const u32 at = u32(w) * 32 + b;
-      u32 q = source[at];
-      // Sources strictly decrease along a chase, so it ends at a position
+  const u32 lane = threadIdx.x & 31u;
+  const u64 warp = (u64(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const u64 warps = (u64(gridDim.x) * blockDim.x) >> 5;
+  auto marked = [&](u32 q) { return ((unresolved[q >> 5] >> (q & 31)) & 1u) != 0; };
+  for (u64 w0 = warp * 32; w0 < words; w0 += warps * 32) {
+    const u32 mine = w0 + lane < words ? unresolved[w0 + lane] : 0u;
+    for (u32 nonzero = __ballot_sync(kFullMask, mine != 0); nonzero;) {
+      u32 at[kResolveWays], q[kResolveWays];
+      bool live[kResolveWays];
+#pragma unroll
+      for (u32 k = 0; k < kResolveWays; ++k) {
+        const u32 i = nonzero ? __ffs(nonzero) - 1 : 0u;
+        const u32 bits = __shfl_sync(kFullMask, mine, i);
+        live[k] = nonzero && ((bits >> lane) & 1u);
+        nonzero &= nonzero - 1;
+        at[k] = u32(w0 + i) * 32 + lane;
+        q[k] = live[k] ? source[at[k]] : 0u;
+      }
+      // Sources strictly decrease along a chase, so each ends at a position
       // that emission wrote directly.
-      while ((unresolved[q >> 5] >> (q & 31)) & 1u) q = source[q];
-      out[at] = out[q];
+      for (bool more = true; more;) {
+        bool step[kResolveWays];
+#pragma unroll
+        for (u32 k = 0; k < kResolveWays; ++k) step[k] = live[k] && marked(q[k]);
+        more = false;
+#pragma unroll
+        for (u32 k = 0; k < kResolveWays; ++k) {
+          if (step[k]) {
+            q[k] = source[q[k]];
+            more = true;
+          }
+        }
+      }
+#pragma unroll
+      for (u32 k = 0; k < kResolveWays; ++k)
+        if (live[k]) out[at[k]] = out[q[k]];
     }
   }
 }
@@ -1410,9 +1439,11 @@ cudaError_t launch_parallel_inflate(const u8* in, u64 in_size, u8* out, u64 expe
       b.first_page, b.page_next, b.page_used, s.pages, b.counters + 2, out, b.source,
       b.unresolved, b.fail);
   profile_end(stream);
+  profile_begin("resolve_kernel", stream);
   note_launch();
   resolve_kernel<<<u32(dev.sms) * 8, 256, 0, stream>>>(b.state, u32(s.out_words), b.unresolved,
                                                        b.source, out);
+  profile_end(stream);
   if (s.segments) {
     note_launch();
     adler_parts_kernel<<<s.segments, 256, 0, stream>>>(b.state, out, u32(expected), b.parts);
