@@ -432,7 +432,7 @@ cudaError_t decompress(const u8* in, u64 size, int64_t max_candidates, int64_t m
   const u32 queue_cap = discover_queue_capacity(size);
   u32 *queue = nullptr, *queued = nullptr;
   CZ_TRY(ws.allocate(&queue, queue_cap));
-  CZ_TRY(ws.allocate(&queued, 1));
+  CZ_TRY(ws.allocate(&queued, 2));
   CZ_TRY(ws.allocate(&b.block_counts, layout.compact_blocks));
   CZ_TRY(ws.allocate(&b.total, 1));
   CZ_TRY(ws.allocate(&b.cands, capacity));
@@ -459,7 +459,7 @@ cudaError_t decompress(const u8* in, u64 size, int64_t max_candidates, int64_t m
   CZ_TRY(ws.allocate(&b.stash, round_stash_words(dev->info)));
   CZ_TRY(cudaMemsetAsync(b.bitmap, 0, layout.bitmap_words * sizeof(u32), stream));
   CZ_TRY(cudaMemsetAsync(count, 0, sizeof(u32), stream));
-  CZ_TRY(cudaMemsetAsync(queued, 0, sizeof(u32), stream));
+  CZ_TRY(cudaMemsetAsync(queued, 0, 2 * sizeof(u32), stream));
   CZ_TRY(cudaMemsetAsync(b.counters, 0, 3 * sizeof(u32), stream));
   CZ_TRY(cudaMemsetAsync(b.page_cursor, 0, sizeof(u32), stream));
   CZ_TRY(cudaMemsetAsync(b.unresolved, 0, layout.out_words * sizeof(u32), stream));

@@ -31,18 +31,30 @@ namespace cz {
 // is usually rejected after a few symbols (an over-subscribed code).  The
 // code-length code is kept in registers and decoded through `lut`, 128
 // bytes of the caller's scratch; every rejection is the one the reference's
-// bitwise reads and checks make, in the same cases.
-__device__ bool dynamic_header_valid(const u8* body, u64 bytes, u64 start, u8* lut) {
+// bitwise reads and checks make, in the same cases.  The check runs as
+// init (the header and the code-length code) and then one step per
+// code-length symbol, so a warp can keep its lanes on different offsets.
+struct HeaderCheck {
   BitCursor c;
+  u32 nl, nd, i, previous;
+  u32 ks0, ks1, nz0, nz1, mx0, mx1;  // per part: Kraft sum (2^-15 units), nonzero count, maximum
+  bool eob;
+};
+enum HeaderStep : u32 { kHeaderMore = 0, kHeaderBad = 1, kHeaderGood = 2 };
+
+__device__ u32 header_init(HeaderCheck& h, const u8* body, u64 bytes, u64 start, u8* lut) {
+  BitCursor& c = h.c;
   c.init(body, bytes, start);
   u32 err = 0;
   c.take(1, &err);
   const u32 type = c.take(2, &err);
-  if (err || type != 2) return false;
-  const u32 nl = c.take(5, &err) + 257, nd = c.take(5, &err) + 1, nc = c.take(4, &err) + 4;
-  if (err || nl > 286) return false;
+  if (err || type != 2) return kHeaderBad;
+  h.nl = c.take(5, &err) + 257;
+  h.nd = c.take(5, &err) + 1;
+  const u32 nc = c.take(4, &err) + 4;
+  if (err || h.nl > 286) return kHeaderBad;
   // Code-length code lengths: 3 bits each, in the RFC 1951 order, read at once.
-  if (c.avail() < 3 * nc) return false;
+  if (c.avail() < 3 * nc) return kHeaderBad;
   const u64 fields = c.peek() & ((1ull << (3 * nc)) - 1);
   c.skip(3 * nc);
   // Position of symbol s in the transmission order 16 17 18 0 8 7 9 6 10 5 11 4 12 3 13 2 14 1 15.
@@ -55,7 +67,7 @@ __device__ bool dynamic_header_valid(const u8* body, u64 bytes, u64 start, u8* l
     kraft += clen[s] ? 128u >> clen[s] : 0u;
   }
   // Complete code-length code (Kraft sum exactly one, in units of 2^-7).
-  if (kraft != 128) return false;
+  if (kraft != 128) return kHeaderBad;
   // Canonical codes, then the 7-bit lookup: entry = symbol | length << 5.
   u32 first = 0, prior = 0;
 #pragma unroll
@@ -75,62 +87,76 @@ __device__ bool dynamic_header_valid(const u8* body, u64 bytes, u64 start, u8* l
     }
     prior = count;
   }
-  // Literal/length lengths i < nl, distance lengths after; per part the
-  // Kraft sum (units of 2^-15), nonzero count and maximum.  Each code-length
-  // symbol and its extra bits come from one 64-bit peek; a symbol whose bits
-  // (code and extra) run past the body end fails as the bitwise reads would.
-  u32 ks0 = 0, ks1 = 0, nz0 = 0, nz1 = 0, mx0 = 0, mx1 = 0;
-  u32 i = 0, previous = 0;
-  bool eob = false;
-  while (i < nl + nd) {
-    const u64 w = c.peek();
-    const u64 avail = c.avail();
-    const u32 e = lut[__brev(u32(w)) >> 25];  // first 7 bits, MSB-first
-    const u32 sym = e & 31u, len = e >> 5;
-    if (len > avail) return false;
-    u32 repeat = 1, value = sym, extra = 0;
-    if (sym == 16) {
-      if (!i) return false;
-      extra = 2;
-      repeat = u32((w >> len) & 3u) + 3;
-      value = previous;
-    } else if (sym == 17) {
-      extra = 3;
-      repeat = u32((w >> len) & 7u) + 3;
-      value = 0;
-    } else if (sym == 18) {
-      extra = 7;
-      repeat = u32((w >> len) & 127u) + 11;
-      value = 0;
-    }
-    if (len + extra > avail) return false;
-    c.skip(len + extra);
-    if (repeat > nl + nd - i) return false;
-    if (value) {
-      // The run [i, i + repeat) splits at most once at nl.  Kraft sums only
-      // grow, so checking after the run rejects exactly when some element
-      // of it would have over-subscribed.
-      const u32 n0 = i < nl ? min_u32(repeat, nl - i) : 0u, n1 = repeat - n0;
-      const u32 weight = 32768u >> value;
-      ks0 += n0 * weight;
-      ks1 += n1 * weight;
-      nz0 += n0;
-      nz1 += n1;
-      if (n0 && value > mx0) mx0 = value;
-      if (n1 && value > mx1) mx1 = value;
-      if (ks0 > 32768u || ks1 > 32768u) return false;  // over-subscribed
-      if (i <= 256 && 256 < i + repeat) eob = true;
-    }
-    i += repeat;
-    previous = value;
+  h.i = 0;
+  h.previous = 0;
+  h.ks0 = h.ks1 = h.nz0 = h.nz1 = h.mx0 = h.mx1 = 0;
+  h.eob = false;
+  return kHeaderMore;
+}
+
+// One code-length symbol (literal/length lengths i < nl, distance lengths
+// after).  Each symbol and its extra bits come from one 64-bit peek; a
+// symbol whose bits (code and extra) run past the body end fails as the
+// bitwise reads would.
+__device__ u32 header_step(HeaderCheck& h, const u8* lut) {
+  BitCursor& c = h.c;
+  const u32 total = h.nl + h.nd;
+  const u64 w = c.peek();
+  const u64 avail = c.avail();
+  const u32 e = lut[__brev(u32(w)) >> 25];  // first 7 bits, MSB-first
+  const u32 sym = e & 31u, len = e >> 5;
+  if (len > avail) return kHeaderBad;
+  u32 repeat = 1, value = sym, extra = 0;
+  if (sym == 16) {
+    if (!h.i) return kHeaderBad;
+    extra = 2;
+    repeat = u32((w >> len) & 3u) + 3;
+    value = h.previous;
+  } else if (sym == 17) {
+    extra = 3;
+    repeat = u32((w >> len) & 7u) + 3;
+    value = 0;
+  } else if (sym == 18) {
+    extra = 7;
+    repeat = u32((w >> len) & 127u) + 11;
+    value = 0;
   }
-  if (!eob) return false;
+  if (len + extra > avail) return kHeaderBad;
+  c.skip(len + extra);
+  const u32 i = h.i;
+  if (repeat > total - i) return kHeaderBad;
+  if (value) {
+    // The run [i, i + repeat) splits at most once at nl.  Kraft sums only
+    // grow, so checking after the run rejects exactly when some element
+    // of it would have over-subscribed.
+    const u32 n0 = i < h.nl ? min_u32(repeat, h.nl - i) : 0u, n1 = repeat - n0;
+    const u32 weight = 32768u >> value;
+    h.ks0 += n0 * weight;
+    h.ks1 += n1 * weight;
+    h.nz0 += n0;
+    h.nz1 += n1;
+    if (n0 && value > h.mx0) h.mx0 = value;
+    if (n1 && value > h.mx1) h.mx1 = value;
+    if (h.ks0 > 32768u || h.ks1 > 32768u) return kHeaderBad;  // over-subscribed
+    if (i <= 256 && 256 < i + repeat) h.eob = true;
+  }
+  h.i = i + repeat;
+  h.previous = value;
+  if (h.i < total) return kHeaderMore;
+  if (!h.eob) return kHeaderBad;
   // Literal/length: complete, or a single length-1 code.  Distance: empty,
   // complete, or a single length-1 code.
-  if (!nz0) return false;
-  if (ks0 != 32768u && !(mx0 == 1 && nz0 == 1)) return false;
-  if (nz1 && ks1 != 32768u && !(mx1 == 1 && nz1 == 1)) return false;
-  return true;
+  if (!h.nz0) return kHeaderBad;
+  if (h.ks0 != 32768u && !(h.mx0 == 1 && h.nz0 == 1)) return kHeaderBad;
+  if (h.nz1 && h.ks1 != 32768u && !(h.mx1 == 1 && h.nz1 == 1)) return kHeaderBad;
+  return kHeaderGood;
+}
+
+__device__ bool dynamic_header_valid(const u8* body, u64 bytes, u64 start, u8* lut) {
+  HeaderCheck h;
+  u32 st = header_init(h, body, bytes, start, lut);
+  while (st == kHeaderMore) st = header_step(h, lut);
+  return st == kHeaderGood;
 }
 
 // Stored-block endpoint seed at body byte `byte` (discover, :1009-1035).
@@ -299,23 +325,62 @@ discover_kernel(const u8* in, u64 in_size, u32* bitmap, u32* count, u32* queue, 
   if ((threadIdx.x & 31) == 0 && events) atomicAdd(count, events);
 }
 
-// Full validation of the queued offsets, one per thread.
+// Full validation of the queued offsets.  Validations take from a few to a
+// few hundred steps, so each lane holds its own offset and, whenever half
+// of the warp has finished, the idle lanes take the next offsets together
+// (one atomic on cursor[0] for the warp) and build their lookups side by
+// side.  Lookup rows are padded by a word, so that lanes building or
+// reading the same entry hit different banks.
+constexpr u32 kLutStride = 132;
 __global__ void __launch_bounds__(kDiscoverThreads)
 validate_kernel(const u8* in, u64 in_size, const u32* queue, u32 queue_cap, const u32* queued,
                 u32* bitmap, u32* count, const u32* gate) {
-  __shared__ u8 cl_lut[kDiscoverThreads][128];
+  __shared__ __align__(4) u8 cl_lut[kDiscoverThreads * kLutStride];
   if (gate && *gate) return;
   if (in_size < 8) return;
   const u8* body = in + 2;
   const u64 bytes = in_size - 6;
-  const u32 n = min_u32(*queued, queue_cap);
-  u32 events = 0;
-  for (u32 i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-    const u32 bit = queue[i];
-    if (dynamic_header_valid(body, bytes, bit, cl_lut[threadIdx.x])) {
-      ++events;
-      atomicOr(&bitmap[bit >> 5], 1u << (bit & 31));
+  const u32 n = min_u32(queued[0], queue_cap);
+  u32* cursor = const_cast<u32*>(queued) + 1;
+  const u32 lane = threadIdx.x & 31u;
+  u8* lut = cl_lut + threadIdx.x * kLutStride;
+  HeaderCheck h;
+  u32 bit = 0, events = 0;
+  bool busy = false, drained = false;
+  for (;;) {
+    const u32 idle = __ballot_sync(kFullMask, !busy);
+    if (!drained && __popc(idle) >= 16) {
+      // Refill the idle lanes.
+      u32 base = 0;
+      if (lane == __ffs(idle) - 1) base = atomicAdd(cursor, u32(__popc(idle)));
+      base = __shfl_sync(kFullMask, base, __ffs(idle) - 1);
+      if (base + __popc(idle) >= n) drained = true;
+      if (!busy) {
+        const u32 slot = base + __popc(idle & ((1u << lane) - 1u));
+        if (slot < n) {
+          bit = queue[slot];
+          busy = header_init(h, body, bytes, bit, lut) == kHeaderMore;
+        }
+      }
     }
+    if (!__any_sync(kFullMask, busy)) {
+      if (drained) break;
+      continue;
+    }
+    // Steps until half of the warp is idle again (or, once the queue is
+    // drained, until every lane is).
+    do {
+      if (busy) {
+        const u32 st = header_step(h, lut);
+        if (st != kHeaderMore) {
+          busy = false;
+          if (st == kHeaderGood) {
+            ++events;
+            atomicOr(&bitmap[bit >> 5], 1u << (bit & 31));
+          }
+        }
+      }
+    } while (__popc(__ballot_sync(kFullMask, busy)) > (drained ? 0 : 16));
   }
   for (u32 o = 16; o; o >>= 1) events += __shfl_xor_sync(kFullMask, events, o);
   if ((threadIdx.x & 31) == 0 && events) atomicAdd(count, events);

@@ -117,7 +117,8 @@ cudaError_t launch_parallel_inflate(const u8* in, u64 in_size, u8* out, u64 expe
 
 // General-route status path (single streams outside the small route).
 // bitmap: one bit per body bit offset, zeroed; count: zeroed u32.
-// queue: discover_queue_capacity(in_size) u32; queued: zeroed u32.
+// queue: discover_queue_capacity(in_size) u32; queued: zeroed u32[2] (offsets
+// queued, validation cursor).
 u32 discover_queue_capacity(u64 in_size);
 cudaError_t launch_discover(const u8* in, u64 in_size, u32* bitmap, u32* count, u32* queue,
                             u32 queue_cap, u32* queued, const u32* gate, const DeviceInfo& dev,
