@@ -252,11 +252,12 @@ struct AheadBits {
 // symbol word), kLaneBlockEnd (end-of-block code, consumed) or
 // kLaneIrregular (a code the serial decoder must judge, a distance beyond
 // the window, or fewer than 48 body bits left, so every token taken here
-// lies wholly inside the body).
-template <typename Reader>
+// lies wholly inside the body).  kChecked = false skips the 48-bit check
+// for callers that know the token starts at least 48 bits before the end.
+template <bool kChecked = true, typename Reader>
 __device__ __forceinline__ u32 symbol_token(Reader& c, const Tables& t, u32 window, u32* bytes,
                                             u32* sym) {
-  if (c.avail() < 48) return kLaneIrregular;
+  if (kChecked && c.avail() < 48) return kLaneIrregular;
   c.refill();
   u32 v = c.lo;
   u32 e = t.ll.lut[v & kLLMask];
@@ -310,6 +311,79 @@ __device__ __forceinline__ u32 marks_between(const u32* row, u32 a, u32 b) {
   return n;
 }
 
+// Phase 1 of a round on one lane: decode its window from s, marking token
+// starts and keeping the tokens; stop/stop_at say where and why it ended.
+// The mark word being filled stays in a register until the tokens move past
+// it.  kChecked = false when the window ends 48 bits or more before the
+// body end, so no token needs the end check.
+template <bool kChecked>
+__device__ __forceinline__ void window_pass(AheadBits& c, const Tables& t, u32 window, u32 s,
+                                            u32 wend, u32* my_marks, u32* kept_at, u32& kept,
+                                            u32& stop, u32& stop_at, u32& block_end) {
+  u32 mark_index = 0, mark_word = 0, bytes = 0, sym = 0;
+  for (;;) {
+    const u32 p = c.pos();
+    if (p >= wend) {
+      stop = kLaneWindow;
+      stop_at = p;
+      break;
+    }
+    const u32 off = p - s;
+    if ((off >> 5) != mark_index) {
+      my_marks[mark_index] = mark_word;
+      mark_index = off >> 5;
+      mark_word = 0;
+    }
+    mark_word |= 1u << (off & 31);
+    const u32 st = symbol_token<kChecked>(c, t, window, &bytes, &sym);
+    if (st != kLaneWindow) {
+      stop = st;
+      stop_at = p;
+      if (st == kLaneBlockEnd) block_end = c.pos();
+      break;
+    }
+    if (kept_at && kept < kStash) kept_at[kept * 32] = sym;
+    ++kept;
+  }
+  my_marks[mark_index] = mark_word;
+}
+
+// Phase 2 on one lane: decode on past the window until landing on a later
+// lane's mark, passing the round's end, or stopping; link/link_at/link_to
+// say which.  kChecked as for window_pass, over the whole round.
+template <bool kChecked>
+__device__ __forceinline__ void run_on(AheadBits& c, const Tables& t, u32 window, u32 start,
+                                       u32 round_end, const RoundShared& r, u32* kept_at,
+                                       u32& kept, u32& cont_tokens, u32& link, u32& link_at,
+                                       u32& link_to, u32& block_end) {
+  u32 bytes = 0, sym = 0;
+  for (;;) {
+    const u32 p = c.pos();
+    if (p >= round_end) {
+      link = kLaneWindow;
+      link_at = p;
+      break;
+    }
+    const u32 to = (p - start) / kRoundWindow, off = p - (start + to * kRoundWindow);
+    if ((r.marks[to][off >> 5] >> (off & 31)) & 1u) {
+      link = kLaneMerged;
+      link_at = p;
+      link_to = to;
+      break;
+    }
+    const u32 st = symbol_token<kChecked>(c, t, window, &bytes, &sym);
+    if (st != kLaneWindow) {
+      link = st;
+      link_at = p;
+      if (st == kLaneBlockEnd) block_end = c.pos();
+      break;
+    }
+    if (kept_at && kept < kStash) kept_at[kept * 32] = sym;
+    ++kept;
+    ++cont_tokens;
+  }
+}
+
 // One round from the token boundary `start` (the same on every lane).  On
 // every lane: the committed position, the output bytes and tokens before
 // it, and whether the block continues, ended (position after its
@@ -336,58 +410,28 @@ __device__ RoundResult warp_round(const u8* body, u32 body_bytes, u32 start, u32
   AheadBits c;
   c.init(body, body_bytes);
   u32 bytes = 0, sym = 0;
-  // Phase 1: speculative decode of the window, marking token starts.
+  // Phase 1: speculative decode of the window, marking token starts.  The
+  // mark word being filled stays in a register until the tokens move past
+  // it; windows ending 48 bits or more before the body end skip the
+  // per-token end check.
   u32 stop = kLaneIrregular, stop_at = s;
   if (s < c.end) {
     c.seek(s);
-    for (;;) {
-      const u32 p = c.pos();
-      if (p >= wend) {
-        stop = kLaneWindow;
-        stop_at = p;
-        break;
-      }
-      my_marks[(p - s) >> 5] |= 1u << ((p - s) & 31);
-      const u32 st = symbol_token(c, t, window, &bytes, &sym);
-      if (st != kLaneWindow) {
-        stop = st;
-        stop_at = p;
-        if (st == kLaneBlockEnd) block_end = c.pos();
-        break;
-      }
-      if (kept_at && kept < kStash) kept_at[kept * 32] = sym;
-      ++kept;
-    }
+    if (wend + 48 <= c.end)
+      window_pass<false>(c, t, window, s, wend, my_marks, kept_at, kept, stop, stop_at, block_end);
+    else
+      window_pass<true>(c, t, window, s, wend, my_marks, kept_at, kept, stop, stop_at, block_end);
   }
   __syncwarp();
   // Phase 2: run on until landing on a later lane's mark (or past the round).
   u32 link = stop, link_at = stop_at, link_to = lane, cont_tokens = 0;
   if (stop == kLaneWindow) {
-    for (;;) {
-      const u32 p = c.pos();
-      if (p >= round_end) {
-        link = kLaneWindow;
-        link_at = p;
-        break;
-      }
-      const u32 to = (p - start) / kRoundWindow, off = p - (start + to * kRoundWindow);
-      if ((r.marks[to][off >> 5] >> (off & 31)) & 1u) {
-        link = kLaneMerged;
-        link_at = p;
-        link_to = to;
-        break;
-      }
-      const u32 st = symbol_token(c, t, window, &bytes, &sym);
-      if (st != kLaneWindow) {
-        link = st;
-        link_at = p;
-        if (st == kLaneBlockEnd) block_end = c.pos();
-        break;
-      }
-      if (kept_at && kept < kStash) kept_at[kept * 32] = sym;
-      ++kept;
-      ++cont_tokens;
-    }
+    if (round_end + 48 <= c.end)
+      run_on<false>(c, t, window, start, round_end, r, kept_at, kept, cont_tokens, link, link_at,
+                    link_to, block_end);
+    else
+      run_on<true>(c, t, window, start, round_end, r, kept_at, kept, cont_tokens, link, link_at,
+                   link_to, block_end);
   }
   r.link[lane] = link;
   r.link_at[lane] = link_at;
@@ -437,6 +481,19 @@ __device__ RoundResult warp_round(const u8* body, u32 body_bytes, u32 start, u32
   u32 total = 0, tokens = 0, finish = to, broken = 0;
   const u32 entry = visited && kept_at ? marks_between(my_marks, 0, from - s) : 0u;
   if (visited && kept_at && kept <= kStash) {
+    // Loads in groups of eight, ahead of the stores, so the copy waits on
+    // memory once per group rather than once per token.
+    constexpr u32 kGroup = 8;
+    for (; tokens + kGroup <= expect; tokens += kGroup) {
+      u32 word[kGroup];
+#pragma unroll
+      for (u32 g = 0; g < kGroup; ++g) word[g] = kept_at[(entry + tokens + g) * 32];
+#pragma unroll
+      for (u32 g = 0; g < kGroup; ++g) {
+        if (kWrite && !drop) *sink.slot(r, before + tokens + g) = word[g];
+        total += word[g] & kMatchFlag ? word[g] & 511u : 1u;
+      }
+    }
     for (; tokens < expect; ++tokens) {
       const u32 word = kept_at[(entry + tokens) * 32];
       if (kWrite && !drop) *sink.slot(r, before + tokens) = word;
