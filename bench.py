@@ -10,11 +10,12 @@ outside the timed region.  A step decodes both streams
 
   value  = uncompressed GB/s (1e9 B/s) with inputs resident in HBM, timed
            with CUDA events on the codec's stream, L2 flushed between steps;
-  e2e    = the same step through the host-buffer API (decompress_zlib_host
-           and compress_zlib_host on inputs in pinned host memory, the three
-           calls from three host threads), with the H2D copies of the inputs
-           and the D2H copies of the results inside the timed region (host
-           wall clock);
+  e2e    = the same step from inputs in pinned host memory to results
+           (and statuses) in pinned host memory, with the H2D copies of the
+           inputs and the D2H copies of the results inside the timed region
+           (host wall clock): copies in on one stream, the three codec calls
+           in order on a compute stream, results out on a third stream as each
+           call finishes;
   roofline = the dominant kernel's algorithmic bytes (U + C per launch)
            over its event-timed device time, against the measured HBM copy
            bandwidth;
@@ -342,35 +343,66 @@ def run_gpu(args, rank, world):
     e2e_times = []
     if args.no_e2e:
         e2e_times.append(float("nan"))
-    # Step inputs sit in pinned host memory (page-locked CPU tensors).  The
-    # three calls run from three host threads, each on its own CUDA stream, so
-    # one part's copies overlap another's kernels; the host wall clock spans
-    # the step from the first call to the last result in host memory.
+    # Step inputs sit in pinned host memory (page-locked CPU tensors) and the
+    # results end there.  The step is the pipeline a user of the device API
+    # writes: the inputs go in on a copy stream, the three codec calls run in
+    # order on one compute stream (each waiting for its own input only), and
+    # each result goes out on a third stream as soon as its call finishes, so
+    # copies overlap compute.  The compressed stream goes out at its exact
+    # length, read from the call's metadata.  The host wall clock spans the
+    # step from the first copy to the last result and status in host memory.
     l1_host = torch.frombuffer(bytearray(l1), dtype=torch.uint8).pin_memory()
     l6_host = torch.frombuffer(bytearray(l6), dtype=torch.uint8).pin_memory()
     raw_host = torch.frombuffer(bytearray(raw), dtype=torch.uint8).pin_memory()
-    from concurrent.futures import ThreadPoolExecutor
-    host_parts = (lambda: codec.decompress_zlib_host(l1_host, U, device),
-                  lambda: codec.decompress_zlib_host(l6_host, U, device),
-                  lambda: codec.compress_zlib_host(raw_host, device, chunk_bytes=CHUNK))
+    out1_host = torch.empty(U, dtype=torch.uint8).pin_memory()
+    out6_host = torch.empty(U, dtype=torch.uint8).pin_memory()
+    comp_host = torch.empty(U + 5 * (U // CHUNK + 1) + 6, dtype=torch.uint8).pin_memory()
+    meta_host = torch.empty(6, dtype=torch.int32).pin_memory()
+    copy_in, compute, copy_out = (torch.cuda.Stream(device) for _ in range(3))
 
-    def on_lane(lane_stream, part):
-        with torch.cuda.device(device), torch.cuda.stream(lane_stream):
-            return part()
+    def e2e_step():
+        inputs, results = [], []
+        with torch.cuda.stream(copy_in):
+            for host in (l1_host, l6_host, raw_host):
+                ready = torch.cuda.Event()
+                inputs.append((host.to(device, non_blocking=True), ready))
+                ready.record(copy_in)
+        with torch.cuda.stream(compute):
+            for k, (data, ready) in enumerate(inputs):
+                compute.wait_event(ready)
+                out, meta = (codec.decompress_zlib_checked(data, U, device) if k < 2 else
+                             codec.compress_zlib_padded(data, device, chunk_bytes=CHUNK))
+                done = torch.cuda.Event()
+                done.record(compute)
+                results.append((out, meta, done))
+        with torch.cuda.stream(copy_out):
+            for k, (out, meta, done) in enumerate(results[:2]):
+                copy_out.wait_event(done)
+                (out1_host, out6_host)[k].copy_(out, non_blocking=True)
+                meta_host[2 * k:2 * k + 2].copy_(meta.view(torch.int32), non_blocking=True)
+            c_out, c_meta, c_done = results[2]
+            copy_out.wait_event(c_done)
+            meta_host[4:6].copy_(c_meta.view(torch.int32), non_blocking=True)
+            copy_out.synchronize()
+            length = int(meta_host[4])
+            comp_host[:length].copy_(c_out[:length], non_blocking=True)
+            copy_out.synchronize()
+        status = meta_host.tolist()
+        assert status[0] == 0 and status[2] == 0 and status[5] == 0, status
+        return length
 
-    with ThreadPoolExecutor(max_workers=3) as workers:
-        for k in range(0 if args.no_e2e else max(args.warmup, 1) + args.steps):
-            flush.fill_(k & 255)
-            torch.cuda.synchronize()
-            begin = time.perf_counter()
-            futures = [workers.submit(on_lane, ls, part) for ls, part in zip(lanes, host_parts)]
-            h1, h6, host_stream = (f.result() for f in futures)
-            elapsed = time.perf_counter() - begin
-            if k >= max(args.warmup, 1):
-                e2e_times.append(elapsed)
+    e2e_length = 0
+    for k in range(0 if args.no_e2e else max(args.warmup, 1) + args.steps):
+        flush.fill_(k & 255)
+        torch.cuda.synchronize()
+        begin = time.perf_counter()
+        e2e_length = e2e_step()
+        elapsed = time.perf_counter() - begin
+        if k >= max(args.warmup, 1):
+            e2e_times.append(elapsed)
     if not args.no_e2e:
-        assert h1.tobytes() == raw and h6.tobytes() == raw
-        assert host_stream.tobytes() == stream_bytes
+        assert out1_host.numpy().tobytes() == raw and out6_host.numpy().tobytes() == raw
+        assert comp_host[:e2e_length].numpy().tobytes() == stream_bytes
     e2e_seconds = sum(e2e_times) / len(e2e_times)
     if world > 1:
         t = torch.tensor([e2e_seconds], dtype=torch.float64, device=device)
@@ -409,7 +441,7 @@ def run_gpu(args, rank, world):
         "e2e": None if args.no_e2e else {
             "value": round(e2e_value, 4), "unit": "GB/s",
             "h2d_bytes_per_step": len(l1) + len(l6) + U,
-            "d2h_bytes_per_step": 2 * U + length + 16, "timer": "host wall clock"},
+            "d2h_bytes_per_step": 2 * U + length + 24, "timer": "host wall clock"},
         "cpu_baseline": cpu,
         "clocks": clocks.summary(),
         "gpu_launches": launched,

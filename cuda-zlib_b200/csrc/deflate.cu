@@ -908,55 +908,78 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
   }
 }
 
-// Finish, one warp per file: scan chunk sizes, check statuses and capacity,
+// Finish, one CTA per file: scan chunk sizes, check statuses and capacity,
 // combine Adler partials, write the wrapper bytes and metadata
 // [encoded_length, status] (FinishEncodedFile, batch_encode.cuh:39-112).
-__global__ void encode_finish_kernel(const EncodeFile* files, u32 nfiles, const u32* sizes,
-                                     const u32* status, const u64* adler, u64* offsets,
-                                     u8* out, u32* meta, u32* range_adler) {
-  const u32 lane = threadIdx.x & 31u;
-  const u32 f = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+// Each warp takes a contiguous range of the file's chunks: a first pass sums
+// its bytes, statuses and Adler terms (each chunk's term is independent of
+// the others), then, with the earlier warps' byte totals, a warp scan writes
+// every chunk's output offset.
+constexpr u32 kFinishWarps = 8;
+__global__ void __launch_bounds__(kFinishWarps * 32)
+encode_finish_kernel(const EncodeFile* files, u32 nfiles, const u32* sizes, const u32* status,
+                     const u64* adler, u64* offsets, u8* out, u32* meta, u32* range_adler) {
+  __shared__ u64 part_bytes[kFinishWarps], part_s1[kFinishWarps], part_s2[kFinishWarps];
+  __shared__ u32 part_bad[kFinishWarps];
+  const u32 lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+  const u32 f = blockIdx.x;
   if (f >= nfiles) return;
   const EncodeFile file = files[f];
   const bool raw = (file.flags & kEncodeRaw) != 0;
-  u64 running = raw ? 0 : 2;  // after the two-byte zlib header
+  const u32 per = (file.chunks + kFinishWarps - 1) / kFinishWarps;
+  const u32 c0 = min_u32(warp * per, file.chunks), c1 = min_u32(c0 + per, file.chunks);
+  u64 bytes = 0, s1 = 0, s2 = 0;
   u32 bad = 0;
-  u64 s1 = 0, s2 = 0;
-  for (u32 base = 0; base < file.chunks; base += 32) {
+  for (u32 c = c0 + lane; c < c1; c += 32) {
+    const u32 g = file.first_chunk + c;
+    bytes += sizes[g];
+    bad |= status[g];
+    const u64 a1 = adler[2 * u64(g)] % kAdlerMod, a2 = adler[2 * u64(g) + 1] % kAdlerMod;
+    const u64 chunk_end = min_u64(u64(c + 1) * file.chunk_bytes, file.in_size);
+    const u64 after = (file.in_size - chunk_end) % kAdlerMod;
+    s1 += a1;
+    s2 += (a2 + a1 * after) % kAdlerMod;
+  }
+  for (u32 o = 16; o; o >>= 1) {
+    bytes += __shfl_xor_sync(kFullMask, bytes, o);
+    s1 += __shfl_xor_sync(kFullMask, s1, o);
+    s2 += __shfl_xor_sync(kFullMask, s2, o);
+  }
+  bad = __reduce_or_sync(kFullMask, bad);
+  if (lane == 0) {
+    part_bytes[warp] = bytes;
+    part_s1[warp] = s1;
+    part_s2[warp] = s2;
+    part_bad[warp] = bad;
+  }
+  __syncthreads();
+  u64 running = raw ? 0 : 2;  // after the two-byte zlib header
+  for (u32 w = 0; w < warp; ++w) running += part_bytes[w];
+  for (u32 base = c0; base < c1; base += 32) {
     const u32 c = base + lane;
-    u32 size = 0, st = 0;
-    u64 a1 = 0, a2 = 0;
-    u64 after = 0;
-    if (c < file.chunks) {
-      const u32 g = file.first_chunk + c;
-      size = sizes[g];
-      st = status[g];
-      a1 = adler[2 * u64(g)] % kAdlerMod;
-      a2 = adler[2 * u64(g) + 1] % kAdlerMod;
-      const u64 chunk_end = min_u64(u64(c + 1) * file.chunk_bytes, file.in_size);
-      after = (file.in_size - chunk_end) % kAdlerMod;
-    }
-    bad |= __ballot_sync(kFullMask, st != 0);
+    const u64 size = c < c1 ? sizes[file.first_chunk + c] : 0u;
     u64 incl = size;
     for (u32 o = 1; o < 32; o <<= 1) {
       const u64 v = __shfl_up_sync(kFullMask, incl, o);
       if (lane >= o) incl += v;
     }
-    if (c < file.chunks) offsets[file.first_chunk + c] = running + incl - size;
+    if (c < c1) offsets[file.first_chunk + c] = running + incl - size;
     running += __shfl_sync(kFullMask, incl, 31);
-    s1 += a1;
-    s2 += (a2 + a1 * after) % kAdlerMod;
   }
-  for (u32 o = 16; o; o >>= 1) {
-    s1 += __shfl_xor_sync(kFullMask, s1, o);
-    s2 += __shfl_xor_sync(kFullMask, s2, o);
-  }
-  const u64 total = running + (raw ? 0 : 4);
-  u32 st = bad ? u32(kCompressionOverflow) : 0u;
-  if (!st && total > file.capacity) st = kCompressionOverflow;
-  if (lane == 0) {
+  if (threadIdx.x == 0) {
+    u64 body = 0, t1 = 0, t2 = 0;
+    u32 any_bad = 0;
+    for (u32 w = 0; w < kFinishWarps; ++w) {
+      body += part_bytes[w];
+      t1 += part_s1[w];
+      t2 += part_s2[w];
+      any_bad |= part_bad[w];
+    }
+    const u64 total = body + (raw ? 0 : 6);
+    u32 st = any_bad ? u32(kCompressionOverflow) : 0u;
+    if (!st && total > file.capacity) st = kCompressionOverflow;
     u8* dst = out + file.out_offset;
-    const u32 checksum = adler_finish(s1, s2, file.in_size);
+    const u32 checksum = adler_finish(t1, t2, file.in_size);
     if (range_adler) range_adler[f] = st ? 0u : checksum;
     if (!st && !raw) {
       dst[0] = 0x78;
@@ -1028,8 +1051,9 @@ cudaError_t launch_encode(const u8* in, const EncodeFile* files, u32 nfiles, u32
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   note_launch();
-  encode_finish_kernel<<<(nfiles + 7) / 8, 256, 0, stream>>>(files, nfiles, sizes, status, adler,
-                                                            offsets, out, meta, range_adler);
+  encode_finish_kernel<<<nfiles, kFinishWarps * 32, 0, stream>>>(files, nfiles, sizes, status,
+                                                                 adler, offsets, out, meta,
+                                                                 range_adler);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   profile_begin("encode_pack_kernel", stream);
