@@ -261,8 +261,6 @@ def run_gpu(args, rank, world):
     # The device-resident step runs its three parts in order on one stream
     # (each part fills the GPU; running them on three streams measured no
     # faster and blurs the per-kernel times).
-    lanes = [torch.cuda.Stream(device) for _ in range(3)]
-
     def step():
         o1, m1 = codec.decompress_zlib_checked(l1_dev, U, device)
         o6, m6 = codec.decompress_zlib_checked(l6_dev, U, device)
@@ -705,14 +703,42 @@ def run_gpu_sharded(args, rank, world):
         raw_pin = torch.frombuffer(bytearray(packed_raw + b"\0"), dtype=torch.uint8)[:len(packed_raw)].pin_memory()
         z_pin = torch.frombuffer(bytearray(packed_z), dtype=torch.uint8).pin_memory()
 
+        # End to end, pipelined: the compressed files go in first and decode
+        # while the raw files go in; the decoded files go out while the raw
+        # files compress.
+        copy_in, compute, copy_out = (torch.cuda.Stream(device) for _ in range(3))
+        host_out = torch.empty(sum(sizes), dtype=torch.uint8).pin_memory()
+        host_slots = torch.empty(d2h - sum(sizes), dtype=torch.uint8).pin_memory()
+        host_meta = torch.empty(2 * len(sizes), dtype=torch.int32).pin_memory()
+        host_emeta = torch.empty(2 * len(sizes), dtype=torch.int32).pin_memory()
+
         def e2e_step():
-            out, meta, slots, emeta = step(raw_pin, z_pin)
-            host_out = torch.empty(out.numel(), dtype=torch.uint8, pin_memory=True)
-            host_out.copy_(out, non_blocking=True)
-            host_slots = torch.empty(slots.numel(), dtype=torch.uint8, pin_memory=True)
-            host_slots.copy_(slots, non_blocking=True)
-            m, em = meta.cpu().numpy(), emeta.cpu().numpy()
-            assert not m.any() and not em[:, 1].any()
+            with torch.cuda.stream(copy_in):
+                z_in = z_pin.to(device, non_blocking=True)
+                z_ready = torch.cuda.Event()
+                z_ready.record(copy_in)
+                raw_in = raw_pin.to(device, non_blocking=True)
+                raw_ready = torch.cuda.Event()
+                raw_ready.record(copy_in)
+            with torch.cuda.stream(compute):
+                compute.wait_event(z_ready)
+                out, meta = codec.decompress_zlib_batch_checked(z_in, in_sizes, sizes, device)
+                decoded = torch.cuda.Event()
+                decoded.record(compute)
+                compute.wait_event(raw_ready)
+                slots, emeta = codec.compress_zlib_batch_padded(raw_in, sizes, device,
+                                                                chunk_bytes=CHUNK)
+                encoded = torch.cuda.Event()
+                encoded.record(compute)
+            with torch.cuda.stream(copy_out):
+                copy_out.wait_event(decoded)
+                host_out.copy_(out, non_blocking=True)
+                host_meta.copy_(meta.view(torch.int32).flatten(), non_blocking=True)
+                copy_out.wait_event(encoded)
+                host_slots.copy_(slots, non_blocking=True)
+                host_emeta.copy_(emeta.view(torch.int32).flatten(), non_blocking=True)
+                copy_out.synchronize()
+            assert not host_meta.numpy().any() and not host_emeta.numpy()[1::2].any()
 
         algorithmic = {"serial_inflate_kernel": len(packed_z) + sum(sizes),
                        "encode_chunks_kernel": sum(sizes)}
@@ -763,16 +789,57 @@ def run_gpu_sharded(args, rank, world):
                 total += length
             return total / max(1, hi - lo)
 
-        h2d = hi - lo
-        d2h = sum(o.numel() for o in outs)
         src_pin = mine.pin_memory()
+        # End to end, pipelined over pieces of at most 32 MiB (whole chunks):
+        # a piece goes in on a copy stream, compresses on a compute stream once
+        # it is in, and its body goes out at its exact length as soon as its
+        # metadata says how long it is, while later pieces copy and compress.
+        piece_bytes = 1024 * CHUNK
+        pieces = [(a, min(a + piece_bytes, stop)) for start, stop in ranges
+                  for a in range(start, stop, piece_bytes)] or [(lo, hi)]
+        piece_out = [torch.empty(b - a + 5 * max(1, -(-(b - a) // CHUNK)) + 6, dtype=torch.uint8,
+                                 device=device) for a, b in pieces]
+        piece_meta = [torch.zeros(3, dtype=torch.uint32, device=device) for _ in pieces]
+        host_meta = torch.empty(3 * len(pieces), dtype=torch.int32).pin_memory()
+        host_body = torch.empty(sum(o.numel() for o in piece_out), dtype=torch.uint8).pin_memory()
+        copy_in, compute, copy_out, body_out = (torch.cuda.Stream(device) for _ in range(4))
+        h2d = hi - lo
+        d2h_done = [0]
 
         def e2e_step():
-            step(src_pin)
-            for out, meta in zip(outs, metas):
-                length = int(meta[0].item())
-                host = torch.empty(length, dtype=torch.uint8, pin_memory=True)
-                host.copy_(out[:length])
+            done = []
+            for k, (a, b) in enumerate(pieces):
+                with torch.cuda.stream(copy_in):
+                    piece = src_pin[a - lo:b - lo].to(device, non_blocking=True)
+                    ready = torch.cuda.Event()
+                    ready.record(copy_in)
+                with torch.cuda.stream(compute):
+                    compute.wait_event(ready)
+                    last = rank == last_rank and b == hi
+                    _native.check(lib.cuda_zlib_compress_range(
+                        piece.data_ptr(), b - a, CHUNK, int(last), piece_out[k].data_ptr(),
+                        piece_out[k].numel(), piece_meta[k].data_ptr(), compute.cuda_stream),
+                        "range")
+                    finished = torch.cuda.Event()
+                    finished.record(compute)
+                with torch.cuda.stream(copy_out):
+                    copy_out.wait_event(finished)
+                    host_meta[3 * k:3 * k + 3].copy_(piece_meta[k].view(torch.int32),
+                                                     non_blocking=True)
+                    done.append((piece, torch.cuda.Event()))
+                    done[-1][1].record(copy_out)
+            # Bodies go out on their own stream, each once its piece's
+            # metadata (hence the piece) is done, not behind later pieces.
+            at = 0
+            with torch.cuda.stream(body_out):
+                for k, (piece, meta_in) in enumerate(done):
+                    meta_in.synchronize()
+                    length, status = int(host_meta[3 * k]), int(host_meta[3 * k + 1])
+                    assert status == 0
+                    host_body[at:at + length].copy_(piece_out[k][:length], non_blocking=True)
+                    at += length
+                body_out.synchronize()
+            d2h_done[0] = at + 12 * len(pieces)
 
         algorithmic = {"encode_chunks_kernel": hi - lo}
         names = ("encode_chunks_kernel", "encode_pack_kernel")
@@ -808,6 +875,8 @@ def run_gpu_sharded(args, rank, world):
         if k >= max(args.warmup, 1):
             e2e_times.append(time.perf_counter() - start)
     e2e_seconds = _max_over_ranks(torch, sum(e2e_times) / len(e2e_times), device, world)
+    if args.workload != "batch":
+        d2h = d2h_done[0]
     roofline = None
     if kernels:
         name, (total_ms, launches) = max(kernels.items(), key=lambda kv: kv[1][0])
