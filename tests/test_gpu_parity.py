@@ -269,6 +269,45 @@ def test_large_bytes_input_uses_threaded_staging(codec):
     assert codec.compress_zlib_host(raw, 0).tobytes() == oracle.compress(raw)
 
 
+@pytest.mark.parametrize("size, chunk, piece", [
+    (200000, 256, 4096),            # many pieces, ragged last chunk and piece
+    (3 * 65536, 32768, 65536),      # whole pieces only
+    (1000003, 65535, 300000),       # piece rounded down to whole 65535-byte chunks
+    (130000, 16384, 1 << 20),       # one piece
+])
+def test_pipelined_host_compress_matches_one_call(codec, monkeypatch, size, chunk, piece):
+    import torch
+    from cuda_zlib import _codec
+    monkeypatch.setattr(_codec, "_PIPE_MIN", 1)
+    monkeypatch.setattr(_codec, "_PIPE_PIECE", piece)
+    rng = random.Random(size)
+    raw = bytes(rng.choices(range(40), k=size // 2)) + rng.randbytes(size // 4) + \
+        b"\0" * (size - size // 2 - size // 4)
+    expected = oracle.compress(raw, chunk)
+    pinned = torch.frombuffer(bytearray(raw), dtype=torch.uint8).pin_memory()
+    # Pageable inputs take the pieces; a pinned tensor takes the one-call path.
+    for data in (raw, bytearray(raw), np.frombuffer(raw, dtype=np.uint8),
+                 torch.frombuffer(bytearray(raw), dtype=torch.uint8), pinned):
+        host = codec.compress_zlib_host(data, 0, chunk_bytes=chunk)
+        assert isinstance(host, np.ndarray) and not host.flags.writeable
+        assert host.tobytes() == expected
+    # A *_host result lives in pinned memory and goes in without staging.
+    again = codec.compress_zlib_host(codec.decompress_zlib_host(expected, size, 0), 0,
+                                     chunk_bytes=chunk)
+    assert again.tobytes() == expected
+
+
+def test_pipelined_host_compress_at_default_threshold(codec):
+    from cuda_zlib import _codec
+    rng = np.random.default_rng(11)
+    raw = np.cumsum(rng.integers(-2, 3, _codec._PIPE_MIN + 12345)).astype(np.uint8)
+    host = codec.compress_zlib_host(raw, 0)
+    device, meta = codec.compress_zlib_padded(raw, 0)
+    length = int(meta.cpu()[0])
+    assert host.tobytes() == device[:length].cpu().numpy().tobytes()
+    assert zlib.decompress(host.tobytes()) == raw.tobytes()
+
+
 # ---------------------------------------------------------------- token arena
 def _flushed_stream(raw, every, level=6):
     """A stream cut into many blocks by full flushes (a block + an empty stored block each)."""
