@@ -108,7 +108,12 @@ class ClockSampler:
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index):
-        self.index = index
+        # nvidia-smi numbers GPUs physically and ignores CUDA_VISIBLE_DEVICES:
+        # query the GPU that the CUDA device index maps to (a physical index
+        # or a UUID, both accepted by -i).
+        visible = [v.strip() for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
+                   if v.strip()]
+        self.index = visible[index] if index < len(visible) else str(index)
         self.proc = None
 
     def __enter__(self):

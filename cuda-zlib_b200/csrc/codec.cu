@@ -16,6 +16,7 @@
 #include <mutex>
 #include <numeric>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "../../include/cuda_zlib_b200.h"
@@ -157,23 +158,41 @@ class Workspace {
 struct ProfileRecord {
   const char* kernel;
   cudaEvent_t start, stop;
+  int device;
 };
 struct ProfileTotals {
   std::string kernel;
   double ms = 0;
   u64 launches = 0;
 };
+// Events are created ahead (when timing is switched on) and reused, so a
+// timed region makes no event-creation calls, which go through the driver
+// and can wait behind other processes' queries of the GPU.
+constexpr int kSpareEvents = 512;
 struct Profiler {
   std::mutex mutex;
   bool enabled = false;
   std::vector<ProfileRecord> pending;
   std::vector<ProfileTotals> totals;
+  std::vector<std::pair<int, cudaEvent_t>> spare;  // (device, event)
+  cudaEvent_t take(int device) {  // caller holds the mutex
+    for (size_t i = spare.size(); i-- > 0;) {
+      if (spare[i].first == device) {
+        const cudaEvent_t e = spare[i].second;
+        spare[i] = spare.back();
+        spare.pop_back();
+        return e;
+      }
+    }
+    cudaEvent_t e = nullptr;
+    return cudaEventCreate(&e) == cudaSuccess ? e : nullptr;
+  }
 };
 Profiler& profiler() {
   static Profiler* p = new Profiler;
   return *p;
 }
-thread_local ProfileRecord open_record{nullptr, nullptr, nullptr};
+thread_local ProfileRecord open_record{nullptr, nullptr, nullptr, 0};
 
 // Fold completed records into the totals (waits for their stop events).
 cudaError_t profile_drain(Profiler& p) {
@@ -189,8 +208,8 @@ cudaError_t profile_drain(Profiler& p) {
     }
     it->ms += ms;
     it->launches += 1;
-    cudaEventDestroy(r.start);
-    cudaEventDestroy(r.stop);
+    p.spare.emplace_back(r.device, r.start);
+    p.spare.emplace_back(r.device, r.stop);
   }
   p.pending.clear();
   return cudaSuccess;
@@ -206,15 +225,18 @@ void note_launch() { launches_issued.fetch_add(1, std::memory_order_relaxed); }
 
 void profile_begin(const char* kernel, cudaStream_t stream) {
   Profiler& p = profiler();
+  ProfileRecord r{kernel, nullptr, nullptr, 0};
   {
     std::lock_guard<std::mutex> lock(p.mutex);
     if (!p.enabled) return;
-  }
-  ProfileRecord r{kernel, nullptr, nullptr};
-  if (cudaEventCreate(&r.start) != cudaSuccess) return;
-  if (cudaEventCreate(&r.stop) != cudaSuccess) {
-    cudaEventDestroy(r.start);
-    return;
+    if (cudaGetDevice(&r.device) != cudaSuccess) return;
+    r.start = p.take(r.device);
+    r.stop = p.take(r.device);
+    if (!r.start || !r.stop) {
+      if (r.start) p.spare.emplace_back(r.device, r.start);
+      if (r.stop) p.spare.emplace_back(r.device, r.stop);
+      return;
+    }
   }
   cudaEventRecord(r.start, stream);
   open_record = r;
@@ -226,7 +248,7 @@ void profile_end(cudaStream_t stream) {
   Profiler& p = profiler();
   std::lock_guard<std::mutex> lock(p.mutex);
   p.pending.push_back(open_record);
-  open_record = ProfileRecord{nullptr, nullptr, nullptr};
+  open_record = ProfileRecord{nullptr, nullptr, nullptr, 0};
 }
 
 namespace {
@@ -633,6 +655,18 @@ int cuda_zlib_b200_profile(int enable) {
   cudaError_t e = cz::profile_drain(p);
   p.totals.clear();
   p.enabled = enable != 0;
+  // Spare events for the current device, made now rather than while timing.
+  int device = 0;
+  if (p.enabled && e == cudaSuccess && cudaGetDevice(&device) == cudaSuccess) {
+    int have = 0;
+    for (const auto& d : p.spare) have += d.first == device ? 1 : 0;
+    for (; have < cz::kSpareEvents; ++have) {
+      cudaEvent_t event = nullptr;
+      e = cudaEventCreate(&event);
+      if (e != cudaSuccess) break;
+      p.spare.emplace_back(device, event);
+    }
+  }
   return int(e);
 }
 

@@ -122,8 +122,10 @@ const char* cuda_zlib_b200_version(void);
 uint64_t cuda_zlib_b200_launches(void);
 
 /* Opt-in kernel timing, no reference counterpart (the reference profiles
- * with Nsight Systems only, PROFILING.md).  enable != 0 clears the totals and
- * brackets every named kernel launch with CUDA events on its stream;
+ * with Nsight Systems only, PROFILING.md).  enable != 0 clears the totals,
+ * creates a supply of events on the current device (so that timing a region
+ * creates none) and brackets every named kernel launch with CUDA events on
+ * its stream;
  * profile_read waits for the recorded events and returns the summed device
  * time and launch count of one kernel ("serial_inflate_kernel",
  * "encode_chunks_kernel", ...).  Off by default; costs two events a launch. */
