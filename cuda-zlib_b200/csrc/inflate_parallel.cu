@@ -65,7 +65,9 @@ constexpr u32 kPassPages = 40;     // pages one pass can reach (32 Ki tokens)
 // (phase 2) soon lands on a position some later lane marked, and from there
 // that lane's chain is its own.  Lane 0 links the lanes in order from the
 // true start, which gives each lane a region between two boundaries known to
-// be on the true chain; phase 3 decodes every region again, now exactly.  A
+// be on the true chain; phase 3 writes every region's tokens, copied from
+// the tokens the lane kept while decoding (or decoded again when it kept too
+// many to hold).  A
 // code the exact decoder must judge (or too few bits left) ends the round at
 // that token, and the serial decoder carries on from there, so statuses
 // stay the serial decoder's.  On config-1 streams half the lanes resynchronize
