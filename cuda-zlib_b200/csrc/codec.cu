@@ -26,6 +26,18 @@ namespace cz {
 namespace {
 
 constexpr u32 kMaxBytes = 1u << 28;
+// Single-stream bounds, a deliberate superset of the reference's 2**28
+// (_codec.py:13,28,103; codec_ffi.cu:42): a stream decodes to at most 2**31
+// bytes from at most 2**29 - 2**16 compressed bytes (body bit offsets stay
+// below 2**32), and compresses at most 2**31 input bytes.  Batch calls keep
+// the reference's 2**28 totals.
+constexpr u64 kMaxStreamBytes = u64(1) << 31;
+constexpr u64 kMaxStreamInput = (u64(1) << 29) - (u64(1) << 16);
+// Chunk sizes: the reference's [256, 65535] (_codec.py:158-159) and, beyond
+// it, chunks up to 2**18 whose stored fallback takes several blocks.
+constexpr int64_t kMinChunk = 256;
+constexpr int64_t kMaxChunk = 262144;
+constexpr u32 kStoredMax = 65535;
 constexpr u32 kMaxBlocks = 262144;
 constexpr u32 kMaxCandidates = 262144;
 constexpr u32 kTruncatedZlib = 14;
@@ -277,6 +289,26 @@ cudaError_t upload(Workspace& ws, T** out, const std::vector<T>& host, cudaStrea
 // ---------------------------------------------------------------------------
 // Encode (single stream and batch share one path).
 // ---------------------------------------------------------------------------
+// Worst-case layout of n input bytes at `chunk`: chunk count, stored blocks
+// of the chunks' stored fallbacks (one per chunk up to 65535 bytes), which
+// size the padded capacity n + 5 * stored + 6, and the most Deflate blocks the
+// stream can hold (the reference's 2 * chunks - 1 for chunks <= 65535:
+// every nonfinal chunk ends with an empty stored block).
+struct StreamLayout {
+  u64 chunks, stored, blocks, capacity;
+};
+u64 stored_blocks(u64 n) { return n ? (n + kStoredMax - 1) / kStoredMax : 1; }
+StreamLayout stream_layout(u64 n, u32 chunk) {
+  StreamLayout l{};
+  l.chunks = n ? (n + chunk - 1) / chunk : 1;
+  const u64 full = stored_blocks(chunk), tail = stored_blocks(n - (l.chunks - 1) * chunk);
+  l.stored = (l.chunks - 1) * full + tail;
+  l.blocks = (l.chunks - 1) * std::max<u64>(full, 2) + tail;
+  l.capacity = n + 5 * l.stored + 6;
+  return l;
+}
+bool chunk_ok(int64_t chunk_bytes) { return chunk_bytes >= kMinChunk && chunk_bytes <= kMaxChunk; }
+
 cudaError_t encode_files(const DeviceState& dev, const u8* in, u64 in_bytes,
                          std::vector<EncodeFile>& files, u32 chunk_bytes, u32 total_chunks,
                          u8* out, u32* meta, cudaStream_t stream, u32* range_adler = nullptr) {
@@ -285,8 +317,7 @@ cudaError_t encode_files(const DeviceState& dev, const u8* in, u64 in_bytes,
   u8* slots = nullptr;
   u32 *sizes = nullptr, *status = nullptr;
   u64 *adler = nullptr, *offsets = nullptr;
-  u16* spill_prev = nullptr;
-  u8* spill_len = nullptr;
+  EncodeSpill spill{};
   CZ_TRY(upload(ws, &d_files, files, stream));
   CZ_TRY(ws.allocate(&slots, in_bytes + 96 * (u64(total_chunks) + 2)));
   CZ_TRY(ws.allocate(&sizes, total_chunks));
@@ -294,13 +325,15 @@ cudaError_t encode_files(const DeviceState& dev, const u8* in, u64 in_bytes,
   CZ_TRY(ws.allocate(&adler, 2 * u64(total_chunks)));
   CZ_TRY(ws.allocate(&offsets, total_chunks));
   if (!encode_in_smem(chunk_bytes, dev.info)) {
-    const u64 entries = in_bytes + 16 * (u64(total_chunks) + 2);
-    CZ_TRY(ws.allocate(&spill_prev, entries));
-    CZ_TRY(ws.allocate(&spill_len, entries));
+    const u64 entries = encode_spill_entries(in_bytes, total_chunks);
+    u8* prev = nullptr;
+    CZ_TRY(ws.allocate(&prev, entries * (chunk_bytes >= kLargeChunk ? 4 : 2)));
+    CZ_TRY(ws.allocate(&spill.len, entries));
+    if (chunk_bytes >= kLargeChunk) CZ_TRY(ws.allocate(&spill.data, entries));
+    spill.prev = prev;
   }
   CZ_TRY(launch_encode(in, d_files, u32(files.size()), chunk_bytes, total_chunks, slots, sizes,
-                       status, adler, offsets, spill_prev, spill_len, out, meta, dev.info,
-                       stream, range_adler));
+                       status, adler, offsets, spill, out, meta, dev.info, stream, range_adler));
   return ws.release();
 }
 
@@ -330,22 +363,23 @@ cudaError_t compress(const u8* in, u64 size, int64_t chunk_bytes, u8* out, u64 c
   DeviceState* dev = nullptr;
   CZ_TRY(device_state(scope.device(), &dev));
   // Compress (codec_ffi.cu:551-571): output bound, then zero, then input and
-  // chunk bounds; any violation is metadata [0, 23].
-  if (capacity > kMaxBytes) return set_meta(meta, 0, kInvalidBounds, stream);
+  // chunk bounds; any violation is metadata [0, 23].  The bounds are this
+  // codec's single-stream ones (2**31 input bytes, chunks up to 2**18).
+  if (capacity > kMaxStreamBytes + 5 * stored_blocks(kMaxStreamBytes) + 6)
+    return set_meta(meta, 0, kInvalidBounds, stream);
   if (capacity) {
     if (!out) return cudaErrorInvalidValue;
     CZ_TRY(cudaMemsetAsync(out, 0, capacity, stream));
   }
-  if (size > kMaxBytes || chunk_bytes < 256 || chunk_bytes > 65535 || (size && !in))
+  if (size > kMaxStreamBytes || !chunk_ok(chunk_bytes) || (size && !in))
     return set_meta(meta, 0, kInvalidBounds, stream);
   const u32 chunk = u32(chunk_bytes);
-  const u64 chunks = std::max<u64>(1, (size + chunk - 1) / chunk);
-  if (2 * chunks - 1 > kMaxBlocks || size + chunks * 5 + 6 > kMaxBytes ||
-      capacity != size + chunks * 5 + 6)
+  const StreamLayout l = stream_layout(size, chunk);
+  if (l.blocks > kMaxBlocks || capacity != l.capacity)
     return set_meta(meta, 0, kInvalidBounds, stream);
   std::vector<EncodeFile> files(1);
-  files[0] = EncodeFile{0, size, 0, capacity, 0, u32(chunks), chunk, 0};
-  return encode_files(*dev, in, size, files, chunk, u32(chunks), out, meta, stream);
+  files[0] = EncodeFile{0, size, 0, capacity, 0, u32(l.chunks), chunk, 0};
+  return encode_files(*dev, in, size, files, chunk, u32(l.chunks), out, meta, stream);
 }
 
 // One contiguous range of a longer stream: raw Deflate chunks, the last one
@@ -356,12 +390,11 @@ cudaError_t compress(const u8* in, u64 size, int64_t chunk_bytes, u8* out, u64 c
 cudaError_t compress_range(const u8* in, u64 size, int64_t chunk_bytes, int last, u8* out,
                            u64 capacity, u32* meta, cudaStream_t stream) {
   if (!meta || !out || (size && !in)) return cudaErrorInvalidValue;
-  if (size > kMaxBytes || chunk_bytes < 256 || chunk_bytes > 65535)
-    return cudaErrorInvalidValue;
+  if (size > kMaxStreamBytes || !chunk_ok(chunk_bytes)) return cudaErrorInvalidValue;
   const u32 chunk = u32(chunk_bytes);
-  const u64 chunks = std::max<u64>(1, (size + chunk - 1) / chunk);
-  if (2 * chunks - 1 > kMaxBlocks || capacity != size + chunks * 5 + 6 ||
-      capacity > kMaxBytes || (!last && size % chunk))
+  const StreamLayout l = stream_layout(size, chunk);
+  const u64 chunks = l.chunks;
+  if (l.blocks > kMaxBlocks || capacity != l.capacity || (!last && size % chunk))
     return cudaErrorInvalidValue;
   DeviceScope scope(stream);
   CZ_TRY(scope.error());
@@ -379,7 +412,7 @@ cudaError_t compress_batch(const u8* in, u64 in_bytes, const int64_t* sizes, u64
                            cudaStream_t stream) {
   // CompressBatchImpl (codec_ffi.cu:1002-1063).
   if (!count || count > kMaxBlocks || !sizes || !meta) return cudaErrorInvalidValue;
-  if (in_bytes > kMaxBytes || out_bytes > kMaxBytes || chunk_bytes < 256 || chunk_bytes > 65535)
+  if (in_bytes > kMaxBytes || out_bytes > kMaxBytes || !chunk_ok(chunk_bytes))
     return cudaErrorInvalidValue;
   const u32 chunk = u32(chunk_bytes);
   std::vector<EncodeFile> files(count);
@@ -387,9 +420,9 @@ cudaError_t compress_batch(const u8* in, u64 in_bytes, const int64_t* sizes, u64
   for (u64 i = 0; i < count; ++i) {
     const int64_t size = sizes[i];
     if (size < 0 || size > int64_t(kMaxBytes)) return cudaErrorInvalidValue;
-    const u64 n = std::max<u64>(1, (u64(size) + chunk - 1) / chunk);
-    const u64 cap = u64(size) + n * 5 + 6;
-    if (2 * n - 1 > kMaxBlocks || in_extent + u64(size) > kMaxBytes ||
+    const StreamLayout l = stream_layout(u64(size), chunk);
+    const u64 n = l.chunks, cap = l.capacity;
+    if (l.blocks > kMaxBlocks || in_extent + u64(size) > kMaxBytes ||
         out_extent + cap > kMaxBytes || total_chunks + n > kMaxBlocks)
       return cudaErrorInvalidValue;
     files[i] = EncodeFile{in_extent, u64(size), out_extent, cap, u32(total_chunks), u32(n), chunk,
@@ -415,15 +448,16 @@ cudaError_t decompress(const u8* in, u64 size, int64_t max_candidates, int64_t m
   CZ_TRY(scope.error());
   DeviceState* dev = nullptr;
   CZ_TRY(device_state(scope.device(), &dev));
-  // Decompress (codec_ffi.cu:662-680).
-  if (expected > kMaxBytes) return set_meta(meta, kInvalidBounds, 0, stream);
+  // Decompress (codec_ffi.cu:662-680), with this codec's single-stream bounds.
+  if (expected > kMaxStreamBytes) return set_meta(meta, kInvalidBounds, 0, stream);
   if (expected && !out) return cudaErrorInvalidValue;
   auto fail = [&](u32 status) -> cudaError_t {
     if (expected) CZ_TRY(cudaMemsetAsync(out, 0, expected, stream));
     return set_meta(meta, status, 0, stream);
   };
-  if (size > kMaxBytes || max_candidates < 1 || max_candidates > int64_t(kMaxCandidates) ||
-      max_blocks < 1 || max_blocks > int64_t(kMaxBlocks))
+  if (size > kMaxStreamInput || max_candidates < 1 ||
+      max_candidates > int64_t(kMaxCandidates) || max_blocks < 1 ||
+      max_blocks > int64_t(kMaxBlocks))
     return fail(kInvalidBounds);
   if (size < 8) return fail(kTruncatedZlib);
   if (!in) return cudaErrorInvalidValue;

@@ -42,6 +42,8 @@ constexpr u32 kOwnerBits = 4;  // log2(kEncWarps): hash slots are split over the
 static_assert((1u << kOwnerBits) == kEncWarps, "one slot class per warp");
 constexpr u32 kRing = 256;     // per-warp ring of owned positions (a power of two)
 constexpr u32 kHashSlots = 8192;
+constexpr u32 kStoredMax = 65535;  // bytes of one stored block
+constexpr u32 kMaxChunkBytes = 262144;  // largest accepted chunk
 
 // Extra bits of a length or distance code (RFC 1951 section 3.2.5), by
 // arithmetic rather than table lookups: the lanes of a warp look up different
@@ -82,8 +84,15 @@ __device__ __forceinline__ u32 fixed_ll_code(u32 s) {  // bit-reversed, ready to
 __device__ __forceinline__ u32 extent_of(u32 bits, bool final) {
   return final ? (bits + 7) / 8 : (bits + 3 + 7) / 8 + 4;
 }
+// Stored blocks of an n-byte chunk's stored fallback (kStoredMax each).
+__host__ __device__ __forceinline__ u32 stored_blocks(u32 n) {
+  return n ? (n + kStoredMax - 1) / kStoredMax : 1u;
+}
 
-// Shared state of one chunk (beyond the dynamically sized arrays).
+// Shared state of one chunk (beyond the dynamically sized arrays).  Pos
+// holds a chunk position: u16 for chunks within the reference's 65535-byte
+// bound, u32 for the larger chunks this codec also accepts.
+template <typename Pos>
 struct EncodeShared {
   u32 freq[335];        // 0..285 lit/len, 286..315 dist, 316..334 code-length
   u8 lengths[336];
@@ -96,7 +105,7 @@ struct EncodeShared {
   u8 depth[2][576];
   u8 rle_sym[320];
   u8 rle_extra[320];
-  u16 owned[kEncWarps][kRing];  // per-warp ring of positions awaiting a batch
+  Pos owned[kEncWarps][kRing];  // per-warp ring of positions awaiting a batch
   u32 seg_exit[kEncThreads];
   u32 seg_entry[kEncThreads];
   u32 seg_bits[kEncThreads];
@@ -115,7 +124,8 @@ struct EncodeShared {
 // ranking, depths by pointer doubling, length counts, canonical codes) is
 // spread over the block.  Returns on all threads whether a tree within
 // `limit` was found.
-__device__ bool cta_tree(EncodeShared& s, const u32* freq, u32 alphabet, u32 limit, u8* lengths,
+template <typename Shared>
+__device__ bool cta_tree(Shared& s, const u32* freq, u32 alphabet, u32 limit, u8* lengths,
                          u16* codes) {
   const u32 tid = threadIdx.x;
   for (u32 shift = 0; shift <= 16; ++shift) {
@@ -309,13 +319,24 @@ __device__ __forceinline__ void for_each_token(const u32* member, const u32* ism
 __device__ __forceinline__ u64 slot_start(u64 in_pos, u32 g) {
   return ((in_pos + 15) & ~u64(15)) + 96 * u64(g);
 }
+// Entry of chunk g in the global spill: 16-aligned, kSpillGap entries after
+// the previous chunk's, so a chunk's slice holds its padded data (up to
+// chunk + 31 bytes) and all slices fit in in_bytes + kSpillGap * (chunks + 2).
+__device__ __forceinline__ u64 spill_offset(u64 in_pos, u32 g) {
+  return ((in_pos + 15) & ~u64(15)) + kSpillGap * u64(g);
+}
 
+// Chunks above 65535 bytes: Pos = u32, and the chunk, its candidates and
+// match lengths live in the global spill (256 KiB do not fit shared memory);
+// its stored fallback takes several blocks of at most 65535 bytes.
+template <typename Pos>
 __global__ void __launch_bounds__(kEncThreads)
 encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ files, u32 nfiles,
                      u32 chunk_bytes, u32 total_chunks, u8* slots, u32* sizes, u32* status,
-                     u64* adler, u16* spill_prev, u8* spill_len, u32 in_smem) {
+                     u64* adler, EncodeSpill spill, u32 in_smem) {
+  constexpr bool kLarge = sizeof(Pos) == 4;
   extern __shared__ __align__(16) u8 smem[];
-  __shared__ EncodeShared s;
+  __shared__ EncodeShared<Pos> s;
   const u32 tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
   const u32 g = blockIdx.x;
   if (g >= total_chunks) return;
@@ -333,24 +354,24 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
   const bool final = local + 1 == f.chunks && !(f.flags & kEncodeNotLast);
   const u8* src = in + f.in_offset + start;
 
-  // Shared layout: data | member bits | match bits | hash table | prev | len.
+  // Shared layout: data | member bits | match bits | hash table | prev | len
+  // (large chunks: member bits | match bits | hash table).
   const u32 data_bytes = (chunk_bytes + 16 + 15) & ~15u;
   const u32 bit_words = (chunk_bytes + 31) / 32 + 1;
-  u8* data = smem;
-  u32* member = reinterpret_cast<u32*>(smem + data_bytes);
+  const u64 spill_at = spill_offset(f.in_offset + start, g);
+  u8* data = kLarge ? spill.data + spill_at : smem;
+  u32* member = reinterpret_cast<u32*>(kLarge ? smem : smem + data_bytes);
   u32* ismatch = member + bit_words;
-  u16* table = reinterpret_cast<u16*>(ismatch + bit_words);
-  u16* prev;
+  Pos* table = reinterpret_cast<Pos*>(ismatch + bit_words);
+  Pos* prev;
   u8* lenv;
   if (in_smem) {
     prev = table + kHashSlots;
     lenv = reinterpret_cast<u8*>(prev + ((chunk_bytes + 7) & ~7u));
   } else {
-    // 16-byte aligned (lenv is read as words); at + n stays below the
-    // in_bytes + 16 * (chunks + 2) spill entries.
-    const u64 at = ((f.in_offset + start + 15) & ~u64(15)) + 16 * u64(g);
-    prev = spill_prev + at;
-    lenv = spill_len + at;
+    // 16-byte aligned (lenv is read as words), kSpillGap entries apart.
+    prev = reinterpret_cast<Pos*>(spill.prev) + spill_at;
+    lenv = spill.len + spill_at;
   }
 
   // 1. Stage the chunk (zero padded) and its Adler-32 partial sums.
@@ -393,11 +414,11 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
       const u32 lo = words[p >> 2], hi = words[(p >> 2) + 1];
       const u32 v = __funnelshift_r(lo, hi, (p & 3u) * 8u) & 0xffffffu;
       const u32 h = (v * 2654435761u) >> 19;
-      prev[p] = u16(h);
+      prev[p] = Pos(h);
       lenv[p] = u8(h);
     }
     __syncthreads();
-    u16* ring = s.owned[warp];
+    Pos* ring = s.owned[warp];
     u32 head = 0, fill = 0;
     auto batch = [&](u32 count) {
       const bool valid = lane < count;
@@ -415,8 +436,8 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
       if (valid) candidate = lower ? from + 1 : table[h];
       __syncwarp();
       if (valid) {
-        if (!(same & ~((2u << lane) - 1u))) table[h] = u16(pos + 1);
-        prev[pos] = u16(candidate);
+        if (!(same & ~((2u << lane) - 1u))) table[h] = Pos(pos + 1);
+        prev[pos] = Pos(candidate);
       }
       __syncwarp();
       head = (head + count) & (kRing - 1);
@@ -459,7 +480,7 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
         u32 at = head + fill + ((excl >> (8 * j)) & 0xffu);
         u32 m = owned[j];
         while (m) {
-          ring[at++ & (kRing - 1)] = u16(base + 128 * j + 4 * lane + ((__ffs(m) - 1) >> 3));
+          ring[at++ & (kRing - 1)] = Pos(base + 128 * j + 4 * lane + ((__ffs(m) - 1) >> 3));
           m &= m - 1;
         }
         fill += (totals >> (8 * j)) & 0xffu;
@@ -632,7 +653,7 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
     for (u32 i = 0; i < 286; ++i) fixed_bits += s.freq[i] * fixed_ll_len(i);
     fixed_bits += s.dist_tokens * 5;
     s.mode = 0;
-    s.extent = n + 5;
+    s.extent = n + 5 * stored_blocks(n);
     const u32 fixed_extent = extent_of(fixed_bits, final);
     if (fixed_extent < s.extent) { s.extent = fixed_extent; s.mode = 1; }
     s.ok = extent_of(29 + s.extra_bits + s.token_count + 1 + s.dist_tokens, final) < s.extent;
@@ -761,15 +782,22 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
     return;
   }
   if (mode == 0) {
-    for (u32 i = tid; i < n; i += kEncThreads) slot[5 + i] = data[i];
+    // Blocks of kStoredMax bytes (one for chunks within the reference's
+    // bound), the last one shorter; only the stream's last block is final.
+    const u32 blocks = stored_blocks(n);
+    for (u32 i = tid; i < n; i += kEncThreads) slot[5 * (i / kStoredMax + 1) + i] = data[i];
+    if (tid < blocks) {
+      const u32 len = min_u32(n - tid * kStoredMax, kStoredMax);
+      u8* head = slot + tid * (kStoredMax + 5);
+      head[0] = final && tid + 1 == blocks ? 1 : 0;
+      head[1] = u8(len);
+      head[2] = u8(len >> 8);
+      const u32 c = len ^ 0xffffu;
+      head[3] = u8(c);
+      head[4] = u8(c >> 8);
+    }
     if (tid == 0) {
-      slot[0] = final ? 1 : 0;
-      slot[1] = u8(n);
-      slot[2] = u8(n >> 8);
-      const u32 c = n ^ 0xffffu;
-      slot[3] = u8(c);
-      slot[4] = u8(c >> 8);
-      sizes[g] = n + 5;
+      sizes[g] = n + 5 * blocks;
       status[g] = 0;
     }
     return;
@@ -1018,6 +1046,8 @@ __global__ void encode_pack_kernel(const EncodeFile* files, u32 nfiles, const u8
 size_t encode_smem_bytes(u32 chunk_bytes, bool in_smem) {
   const size_t data_bytes = (chunk_bytes + 16 + 15) & ~15u;
   const size_t bit_words = (chunk_bytes + 31) / 32 + 1;
+  if (chunk_bytes >= kLargeChunk)  // bitmaps and a table of u32 positions
+    return (2 * bit_words * 4 + kHashSlots * 4 + 15) & ~size_t(15);
   size_t bytes = data_bytes + 2 * bit_words * 4 + kHashSlots * 2;
   if (in_smem) bytes += ((chunk_bytes + 7) & ~7u) * 2 + chunk_bytes + 16;
   return (bytes + 15) & ~size_t(15);
@@ -1029,24 +1059,33 @@ cudaError_t configure_encode(int* max_dynamic_smem) {
   if (e != cudaSuccess) return e;
   e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
   if (e != cudaSuccess) return e;
-  const int limit = optin - int(sizeof(EncodeShared)) - 1024;
-  e = cudaFuncSetAttribute(encode_chunks_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  const int limit = optin - int(sizeof(EncodeShared<u16>)) - 1024;
+  e = cudaFuncSetAttribute(encode_chunks_kernel<u16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            limit);
+  if (e != cudaSuccess) return e;
+  const int large = int(encode_smem_bytes(kMaxChunkBytes, false));
+  if (large > optin - int(sizeof(EncodeShared<u32>)) - 1024) return cudaErrorInvalidValue;
+  e = cudaFuncSetAttribute(encode_chunks_kernel<u32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           large);
   *max_dynamic_smem = limit;
   return e;
 }
 
 cudaError_t launch_encode(const u8* in, const EncodeFile* files, u32 nfiles, u32 chunk_bytes,
                           u32 total_chunks, u8* slots, u32* sizes, u32* status, u64* adler,
-                          u64* offsets, u16* spill_prev, u8* spill_len, u8* out, u32* meta,
+                          u64* offsets, const EncodeSpill& spill, u8* out, u32* meta,
                           const DeviceInfo& dev, cudaStream_t stream, u32* range_adler) {
   const bool in_smem = encode_in_smem(chunk_bytes, dev);
   const size_t smem = encode_smem_bytes(chunk_bytes, in_smem);
   profile_begin("encode_chunks_kernel", stream);
   note_launch();
-  encode_chunks_kernel<<<total_chunks, kEncThreads, smem, stream>>>(
-      in, files, nfiles, chunk_bytes, total_chunks, slots, sizes, status, adler, spill_prev,
-      spill_len, in_smem ? 1u : 0u);
+  if (chunk_bytes >= kLargeChunk)
+    encode_chunks_kernel<u32><<<total_chunks, kEncThreads, smem, stream>>>(
+        in, files, nfiles, chunk_bytes, total_chunks, slots, sizes, status, adler, spill, 0u);
+  else
+    encode_chunks_kernel<u16><<<total_chunks, kEncThreads, smem, stream>>>(
+        in, files, nfiles, chunk_bytes, total_chunks, slots, sizes, status, adler, spill,
+        in_smem ? 1u : 0u);
   profile_end(stream);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
@@ -1065,7 +1104,8 @@ cudaError_t launch_encode(const u8* in, const EncodeFile* files, u32 nfiles, u32
 }
 
 bool encode_in_smem(u32 chunk_bytes, const DeviceInfo& dev) {
-  return encode_smem_bytes(chunk_bytes, true) <= size_t(dev.encode_smem_limit);
+  return chunk_bytes < kLargeChunk &&
+         encode_smem_bytes(chunk_bytes, true) <= size_t(dev.encode_smem_limit);
 }
 
 }  // namespace cz
@@ -1186,7 +1226,7 @@ cudaError_t compress_noalloc(const u8* in, u64 size, int64_t chunk_bytes, u8* ou
                         reinterpret_cast<u32*>(base + l.sizes),
                         reinterpret_cast<u32*>(base + l.status),
                         reinterpret_cast<u64*>(base + l.adler),
-                        reinterpret_cast<u64*>(base + l.offsets), nullptr, nullptr, out, meta,
+                        reinterpret_cast<u64*>(base + l.offsets), EncodeSpill{}, out, meta,
                         d->info, stream);
   }
   if (device != previous) cudaSetDevice(previous);

@@ -40,7 +40,7 @@ struct DeviceInfo {
 // consecutively; files are ordered by first_chunk.
 struct EncodeFile {
   u64 in_offset, in_size;    // input bytes
-  u64 out_offset, capacity;  // padded output slot: size + 5 * chunks + 6
+  u64 out_offset, capacity;  // padded output slot: size + 5 * stored blocks + 6
   u32 first_chunk, chunks, chunk_bytes, flags;
 };
 // EncodeFile::flags.  A range of a longer stream leaves its last chunk
@@ -58,18 +58,30 @@ cudaError_t launch_serial_inflate(const u8* in, u8* out, const StreamDesc* descs
                                   u32* meta, const u32* encoded, u32 max_blocks,
                                   const DeviceInfo& dev, cudaStream_t stream);
 
-// Chunk encoder + device-side finish.  Slots: in_bytes + 96 * (chunks + 1)
+// Chunk encoder + device-side finish.  Slots: in_bytes + 96 * (chunks + 2)
 // bytes; `sizes`, `status` per chunk; `adler` 2 u64 per chunk; `offsets` 1 u64
 // per chunk.  When encode_in_smem() is false the per-position arrays live in
-// `spill_prev` (u16) and `spill_len` (u8), in_bytes + 16 * (chunks + 1)
-// entries each.  `out` must be zeroed; `meta` receives [encoded_length,
-// status] per file, and `range_adler` (optional) the Adler-32 of each
-// file's input bytes.
+// the global spill: `prev` (u16 entries, u32 for chunks above 65535 bytes)
+// and `len` (u8), and for chunks above 65535 bytes also `data` (u8), each
+// encode_spill_entries() entries.  `out` must be zeroed; `meta` receives
+// [encoded_length, status] per file, and `range_adler` (optional) the
+// Adler-32 of each file's input bytes.
+struct EncodeSpill {
+  void* prev;
+  u8* len;
+  u8* data;
+};
+constexpr u32 kSpillGap = 64;  // spill entries between consecutive chunks' slices
+inline u64 encode_spill_entries(u64 in_bytes, u32 chunks) {
+  return in_bytes + u64(kSpillGap) * (u64(chunks) + 2);
+}
+// Chunks above the reference's 65535 bytes use 32-bit positions.
+constexpr u32 kLargeChunk = 65536;
 cudaError_t configure_encode(int* max_dynamic_smem);
 bool encode_in_smem(u32 chunk_bytes, const DeviceInfo& dev);
 cudaError_t launch_encode(const u8* in, const EncodeFile* files, u32 nfiles, u32 chunk_bytes,
                           u32 total_chunks, u8* slots, u32* sizes, u32* status, u64* adler,
-                          u64* offsets, u16* spill_prev, u8* spill_len, u8* out, u32* meta,
+                          u64* offsets, const EncodeSpill& spill, u8* out, u32* meta,
                           const DeviceInfo& dev, cudaStream_t stream,
                           u32* range_adler = nullptr);
 

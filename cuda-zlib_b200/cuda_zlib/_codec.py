@@ -1,9 +1,17 @@
 """Bounded RFC 1950 codec on B200 through the native C ABI.
 
 Mirrors xangma/cuda-zlib's API module (src/cuda_zlib/_codec.py): the same
-bounds (2**28 bytes, 262144 blocks and files), the same validation order and
-errors, the same padded-slot formula and metadata layouts
-([encoded_length, status] for compression, [status, 0] for decompression).
+validation order and errors, the same padded-slot formula and metadata
+layouts ([encoded_length, status] for compression, [status, 0] for
+decompression), and the same batch bounds (2**28 bytes, 262144 blocks and
+files).  Two bounds are deliberate supersets of the reference's: a single
+stream may hold up to 2**31 uncompressed bytes (and, to decode, at most
+2**29 - 2**16 compressed bytes), where the reference stops at 2**28
+(_codec.py:13,28,103); and chunk_bytes may be up to 262144, where the
+reference stops at 65535 (_codec.py:158-159).  A chunk above 65535 bytes
+falls back to several stored blocks, so the padded slot is
+size + 5 * (stored blocks) + 6, which equals the reference's
+size + 5 * chunks + 6 whenever chunk_bytes <= 65535.
 Device arrays are PyTorch CUDA tensors; host results are read-only NumPy
 arrays backed by pinned memory.  Calls run on the device's current PyTorch
 stream; the *_padded / *_checked variants never synchronize the host.
@@ -19,6 +27,10 @@ from . import _native
 from ._errors import BackendUnavailable, CodecError, UnsupportedStream
 
 _MAX_BYTES = 2**28
+_MAX_STREAM = 2**31                  # one stream's uncompressed bytes
+_MAX_STREAM_PAYLOAD = 2**29 - 2**16  # one stream's compressed bytes, to decode
+_MAX_CHUNK = 262144
+_STORED_MAX = 65535
 _MAX_CANDIDATES = 262144
 _MAX_BLOCKS = 262144
 _MESSAGES = {
@@ -53,8 +65,13 @@ def _torch():
 
 
 def _validate_size(size):
-    if type(size) is not int or not 0 <= size <= _MAX_BYTES:
-        raise ValueError("expected_bytes must be an integer in [0, 2**28]")
+    if type(size) is not int or not 0 <= size <= _MAX_STREAM:
+        raise ValueError("expected_bytes must be an integer in [0, 2**31]")
+
+
+def _check_chunk(chunk_bytes):
+    if type(chunk_bytes) is not int or not 256 <= chunk_bytes <= _MAX_CHUNK:
+        raise ValueError("chunk_bytes must be an integer in [256, 262144]")
 
 
 def _validate_device(device):
@@ -84,7 +101,11 @@ def _is_tensor(data):
     return type(data).__module__.startswith("torch") and hasattr(data, "dtype")
 
 
-def _input_size(data, label="input"):
+_LIMIT_TEXT = {_MAX_BYTES: "2**28", _MAX_STREAM: "2**31",
+               _MAX_STREAM_PAYLOAD: "2**29 - 2**16"}
+
+
+def _input_size(data, label="input", limit=_MAX_BYTES):
     if isinstance(data, (bytes, bytearray, memoryview)):
         size = memoryview(data).nbytes
     elif isinstance(data, np.ndarray) or _is_tensor(data):
@@ -95,8 +116,8 @@ def _input_size(data, label="input"):
         size = int(data.shape[0])
     else:
         raise TypeError(label + " must be bytes or a one-dimensional uint8 array or tensor")
-    if size > _MAX_BYTES:
-        raise ValueError(label + " exceeds size limit (2**28 bytes)")
+    if size > limit:
+        raise ValueError(label + " exceeds size limit (%s bytes)" % _LIMIT_TEXT[limit])
     return size
 
 
@@ -181,8 +202,8 @@ def _check_framing(payload, expected_bytes):
     _validate_size(expected_bytes)
     if view.nbytes < 8:
         raise CodecError("truncated zlib payload")
-    if view.nbytes > _MAX_BYTES:
-        raise ValueError("compressed payload exceeds 2**28 bytes")
+    if view.nbytes > _MAX_STREAM_PAYLOAD:
+        raise ValueError("compressed payload exceeds 2**29 - 2**16 bytes")
     cmf, flg = view[0], view[1]
     if cmf == 0x1F and flg == 0x8B:
         raise UnsupportedStream("native CUDA codec supports RFC 1950 zlib")
@@ -235,9 +256,29 @@ def trim_workspace_pool(device=0):
     _native._check_pool_error(_native.library().CudaZlibTrimWorkspacePool(selected.index))
 
 
-def _capacity(size, chunk_bytes):
+def _stored_blocks(size):
+    return max(1, -(-size // _STORED_MAX))
+
+
+def _layout(size, chunk_bytes):
+    """(capacity, chunks, most Deflate blocks) of one stream.
+
+    The capacity is size + 5 * (stored blocks of every chunk's stored
+    fallback) + 6: size + 5 * chunks + 6 for chunks of at most 65535 bytes
+    (the reference's formula, _codec.py:151-177).  Every nonfinal chunk can
+    end with an empty stored block, so the stream holds at most
+    2 * chunks - 1 blocks, or the stored blocks when a chunk needs more.
+    """
     chunks = max(1, (size + chunk_bytes - 1) // chunk_bytes)
-    return size + chunks * 5 + 6, chunks
+    full, tail = _stored_blocks(chunk_bytes), _stored_blocks(size - (chunks - 1) * chunk_bytes)
+    stored = (chunks - 1) * full + tail
+    blocks = (chunks - 1) * max(full, 2) + tail
+    return size + 5 * stored + 6, chunks, blocks
+
+
+def _capacity(size, chunk_bytes):
+    capacity, chunks, _ = _layout(size, chunk_bytes)
+    return capacity, chunks
 
 
 def compress_zlib_padded(data, device=0, *, chunk_bytes=32768):
@@ -246,14 +287,11 @@ def compress_zlib_padded(data, device=0, *, chunk_bytes=32768):
     The fixed-size buffer holds a zlib stream followed by zero padding.
     Status zero means success; check it before using the stream.
     """
-    if type(chunk_bytes) is not int or not 256 <= chunk_bytes <= 65535:
-        raise ValueError("chunk_bytes must be an integer in [256, 65535]")
-    size = _input_size(data)
-    capacity, chunks = _capacity(size, chunk_bytes)
-    if 2 * chunks - 1 > _MAX_BLOCKS:
+    _check_chunk(chunk_bytes)
+    size = _input_size(data, limit=_MAX_STREAM)
+    capacity, chunks, blocks = _layout(size, chunk_bytes)
+    if blocks > _MAX_BLOCKS:
         raise ValueError("chunk count exceeds decoder block limit")
-    if capacity > _MAX_BYTES:
-        raise ValueError("worst-case compressed extent exceeds 2**28 bytes")
     selected = _select_device(device)
     torch = _torch()
     lib = _native.library()
@@ -279,12 +317,12 @@ def _batch_sizes(sizes, label):
 
 
 def _batch_capacities(sizes, chunk_bytes):
-    if type(chunk_bytes) is not int or not 256 <= chunk_bytes <= 65535:
-        raise ValueError("chunk_bytes must be an integer in [256, 65535]")
-    chunks = tuple(max(1, (size + chunk_bytes - 1) // chunk_bytes) for size in sizes)
-    if sum(chunks) > _MAX_BLOCKS or any(2 * n - 1 > _MAX_BLOCKS for n in chunks):
+    _check_chunk(chunk_bytes)
+    layouts = tuple(_layout(size, chunk_bytes) for size in sizes)
+    if (sum(chunks for _, chunks, _ in layouts) > _MAX_BLOCKS or
+            any(blocks > _MAX_BLOCKS for _, _, blocks in layouts)):
         raise ValueError("batch chunk count exceeds workspace limit")
-    capacities = tuple(size + n * 5 + 6 for size, n in zip(sizes, chunks))
+    capacities = tuple(capacity for capacity, _, _ in layouts)
     if sum(capacities) > _MAX_BYTES:
         raise ValueError("batch compressed capacity exceeds 2**28 bytes")
     return capacities
@@ -302,7 +340,8 @@ def compress_zlib_batch_padded(data, input_sizes, device=0, *, chunk_bytes=32768
     ``input_sizes`` lists the file lengths (their sum is len(data)).  Returns a
     flat uint8 buffer of consecutive padded slots and uint32 metadata of shape
     (files, 2) with [encoded_length, status] per file.  A slot has
-    ``size + 5 * max(1, ceil(size / chunk_bytes)) + 6`` bytes.
+    ``size + 5 * max(1, ceil(size / chunk_bytes)) + 6`` bytes for chunk_bytes
+    up to 65535 (larger chunks count ceil(chunk / 65535) stored blocks each).
     """
     sizes = _batch_sizes(input_sizes, "input_sizes")
     if _input_size(data) != sum(sizes):
@@ -455,7 +494,7 @@ def decompress_zlib_checked(payload, expected_bytes, device=0, *,
     and max_blocks are the reference handler's attributes (default 262144).
     """
     _validate_size(expected_bytes)
-    size = _input_size(payload, "compressed payload")
+    size = _input_size(payload, "compressed payload", _MAX_STREAM_PAYLOAD)
     if isinstance(payload, (bytes, bytearray, memoryview)):
         _check_framing(payload, expected_bytes)
     elif size < 8:
@@ -531,7 +570,7 @@ def _compress_host_pipelined(source, size, selected, chunk_bytes):
                 ready = torch.cuda.Event()
                 ready.record(copy_in)
             compute.wait_event(ready)
-            capacity = (b - a) + 5 * max(1, -(-(b - a) // chunk_bytes)) + 6
+            capacity = _capacity(b - a, chunk_bytes)[0]
             output = torch.empty(capacity, dtype=torch.uint8, device=selected)
             meta = torch.zeros(3, dtype=torch.uint32, device=selected)
             _native.check(lib.cuda_zlib_compress_range(
@@ -546,8 +585,7 @@ def _compress_host_pipelined(source, size, selected, chunk_bytes):
                 arrived.record(copy_out)
             kept.append((raw, output, meta))
             done.append(arrived)
-        host = torch.empty(size + 5 * max(1, -(-size // chunk_bytes)) + 6, dtype=torch.uint8,
-                           pin_memory=True)
+        host = torch.empty(_capacity(size, chunk_bytes)[0], dtype=torch.uint8, pin_memory=True)
         body_out = torch.cuda.Stream(selected)
         at, adlers = 2, []
         with torch.cuda.stream(body_out):
@@ -581,14 +619,12 @@ def compress_zlib_host(data, device=0, *, chunk_bytes=32768) -> np.ndarray:
     that staging them into pinned memory and copying them in overlap the
     kernels; the stream is the same byte for byte.
     """
-    if type(chunk_bytes) is not int or not 256 <= chunk_bytes <= 65535:
-        raise ValueError("chunk_bytes must be an integer in [256, 65535]")
-    size = _input_size(data)
+    _check_chunk(chunk_bytes)
+    size = _input_size(data, limit=_MAX_STREAM)
     if size >= _PIPE_MIN:
-        capacity, chunks = _capacity(size, chunk_bytes)
+        _, _, blocks = _layout(size, chunk_bytes)
         source = _host_view(data)
-        if (source is not None and not source.is_pinned() and capacity <= _MAX_BYTES and
-                2 * chunks - 1 <= _MAX_BLOCKS):
+        if source is not None and not source.is_pinned() and blocks <= _MAX_BLOCKS:
             if source.dtype != _torch().uint8 or source.ndim != 1:
                 raise TypeError("array input must be one-dimensional uint8")
             return _compress_host_pipelined(source, size, _select_device(device), chunk_bytes)

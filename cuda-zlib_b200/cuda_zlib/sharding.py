@@ -71,8 +71,7 @@ def plan_ranges(size, chunk_bytes, parts, max_range=None):
     """
     if type(parts) is not int or parts < 1:
         raise ValueError("parts must be a positive integer")
-    if type(chunk_bytes) is not int or not 256 <= chunk_bytes <= 65535:
-        raise ValueError("chunk_bytes must be an integer in [256, 65535]")
+    _codec._check_chunk(chunk_bytes)
     chunks = max(1, -(-size // chunk_bytes))
     limit = chunks if max_range is None else max(1, max_range // chunk_bytes)
     plan = []
@@ -144,8 +143,7 @@ def _range_call(torch, device, source, start, stop, chunk_bytes, last):
     """Encode input[start:stop) on `device`; returns (body tensor, length, adler)."""
     lib = _native.library()
     size = stop - start
-    chunks = max(1, -(-size // chunk_bytes))
-    capacity = size + 5 * chunks + 6
+    capacity = _codec._capacity(size, chunk_bytes)[0]
     with torch.cuda.device(device):
         if _codec._is_tensor(source):
             raw = source[start:stop].to(device, non_blocking=False)
@@ -166,7 +164,7 @@ def compress_zlib_host_sharded(data, devices, *, chunk_bytes=32768):
 
     Returns a read-only NumPy uint8 array in pinned host memory holding the
     zlib stream, byte-identical to compress_zlib_host on one device.  The
-    input may exceed the single-call bound (2**28 bytes): each device encodes
+    input may exceed the single-call bound (2**31 bytes): each device encodes
     its share in ranges that fit one call.
     """
     devices, torch = _devices(devices)
@@ -182,10 +180,9 @@ def compress_zlib_host_sharded(data, devices, *, chunk_bytes=32768):
         source, size = view, view.nbytes
     else:
         raise TypeError("input must be bytes or a one-dimensional uint8 array or tensor")
-    if type(chunk_bytes) is not int or not 256 <= chunk_bytes <= 65535:
-        raise ValueError("chunk_bytes must be an integer in [256, 65535]")
-    # Largest range whose padded output fits one call.
-    max_range = (_codec._MAX_BYTES - 6) * chunk_bytes // (chunk_bytes + 5)
+    _codec._check_chunk(chunk_bytes)
+    # Largest range one call takes (whole chunks).
+    max_range = _codec._MAX_STREAM // chunk_bytes * chunk_bytes
     plan = plan_ranges(size, chunk_bytes, len(devices), max_range)
     final_range = max((p, len(r) - 1) for p, r in enumerate(plan) if r)
 
@@ -298,10 +295,9 @@ def compress_zlib_batch_host_sharded(inputs, devices, *, chunk_bytes=32768):
     if not isinstance(inputs, (tuple, list)) or not inputs:
         raise ValueError("inputs must be a nonempty sequence of files")
     blobs = [bytes(x) if not isinstance(x, bytes) else x for x in inputs]
-    if type(chunk_bytes) is not int or not 256 <= chunk_bytes <= 65535:
-        raise ValueError("chunk_bytes must be an integer in [256, 65535]")
+    _codec._check_chunk(chunk_bytes)
     sizes = [len(b) for b in blobs]
-    capacities = [n + 5 * max(1, -(-n // chunk_bytes)) + 6 for n in sizes]
+    capacities = [_codec._capacity(n, chunk_bytes)[0] for n in sizes]
     plan = plan_files(sizes, len(devices))
     streams = [None] * len(blobs)
 

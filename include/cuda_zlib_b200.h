@@ -21,6 +21,16 @@
  * cudaMemPool workspace, codec_ffi.cu:132-273).  Concurrent calls from
  * several host threads are allowed.
  *
+ * Bounds.  Batch calls keep the reference's (totals of 2**28 bytes, 262144
+ * files and chunks).  Two bounds are deliberate supersets of the
+ * reference's (_codec.py:13,28,103,158-166): one stream may hold up to 2**31
+ * uncompressed bytes (decoding also needs at most 2**29 - 2**16 compressed
+ * bytes), and chunk_bytes may be up to 262144.  A chunk above 65535 bytes
+ * falls back to several stored blocks of at most 65535 bytes, so the padded
+ * capacity is size + 5 * S + 6 where S counts ceil(len / 65535) stored
+ * blocks per chunk -- exactly size + 5 * chunks + 6 for chunk_bytes up to
+ * 65535, the reference's formula.
+ *
  * Status codes: 0 ok; 1-13 Deflate parser (_decode_kernels.py:36-50);
  * 14 truncated zlib, 15 bad CMF/FLG, 16 gzip, 17 preset dictionary,
  * 18 candidate overflow, 19 initial block missing, 20 reference depth,
@@ -38,8 +48,9 @@ extern "C" {
 
 /* Replaces CudaZlibCompress / CompressImpl (codec_ffi.cu:1144-1151, 981-988,
  * 551-612).  output must have capacity = size + 5*max(1,ceil(size/chunk))+6
- * bytes (compress_zlib_padded, _codec.py:151-177); it is zero-filled past
- * the stream.  metadata: u32[2] = [encoded_length, status]. */
+ * bytes for chunk <= 65535 (compress_zlib_padded, _codec.py:151-177; the
+ * stored-block count above); it is zero-filled past the stream.  metadata:
+ * u32[2] = [encoded_length, status]. */
 int cuda_zlib_compress(const uint8_t* input, uint64_t size, int64_t chunk_bytes,
                        uint8_t* output, uint64_t capacity, uint32_t* metadata, void* stream);
 
@@ -58,7 +69,8 @@ int cuda_zlib_compress_range(const uint8_t* input, uint64_t size, int64_t chunk_
                              uint32_t* metadata, void* stream);
 
 /* Replaces CudaZlibDecompress / DecompressImpl (codec_ffi.cu:1153-1161,
- * 990-998, 662-950).  expected = exact output size; max_candidates and
+ * 990-998, 662-950).  expected = exact output size (at most 2**31; size
+ * at most 2**29 - 2**16); max_candidates and
  * max_blocks in [1, 262144] (defaults 262144 select the small route for
  * outputs <= 64 KiB with inputs <= 128 KiB).  metadata: u32[2] =
  * [status, 0].  A failed output is all zero. */
@@ -93,7 +105,11 @@ int cuda_zlib_decompress_batch(const uint8_t* input, uint64_t input_bytes,
  * cuda_zlib_compress (byte-identical streams), restricted to
  * size <= CUDA_ZLIB_NOALLOC_MAX_INPUT and
  * 256 <= chunk_bytes <= CUDA_ZLIB_NOALLOC_MAX_CHUNK; anything else returns
- * cudaErrorInvalidValue (1) and leaves output and metadata untouched.
+ * cudaErrorInvalidValue (1) and leaves output and metadata untouched.  The
+ * chunk must also fit the encoder's shared-memory path (every chunk up to
+ * 32 KiB does on a B200; a device with less shared memory per block rejects
+ * larger chunks the same way), because this entry point has no room for the
+ * global spill arrays larger chunks use.
  * Scratch lives in one static device array (about 1.6 MB) that every GPU
  * loading the library keeps until exit.  All calls share it: calls that
  * overlap on the GPU race with each other, so order them (one stream, or

@@ -98,9 +98,22 @@ def inflate_general(payload, expected, max_candidates=MAX_CANDIDATES, max_blocks
     return out[:expected].tobytes(), int(status)
 
 
+def stored_blocks(size):
+    """Stored blocks of a chunk's stored fallback (several above 65535 bytes)."""
+    return max(1, -(-size // 65535))
+
+
 def capacity(size, chunk_bytes=32768):
+    """Padded output size: size + 5 * (stored blocks of every chunk) + 6,
+    which is size + 5 * chunks + 6 for chunks of at most 65535 bytes."""
     chunks = max(1, (size + chunk_bytes - 1) // chunk_bytes)
-    return size + 5 * chunks + 6
+    last = size - (chunks - 1) * chunk_bytes
+    return size + 5 * ((chunks - 1) * stored_blocks(chunk_bytes) + stored_blocks(last)) + 6
+
+
+def slot_bytes(chunk_bytes):
+    """Per-chunk slot of oracle_compress_chunks (room for any chunk encoding)."""
+    return (chunk_bytes * 9 + 7) // 8 + 16 + 5 * stored_blocks(chunk_bytes)
 
 
 def compress_padded(data, chunk_bytes=32768):
@@ -119,3 +132,31 @@ def compress(data, chunk_bytes=32768):
     if meta[1]:
         raise ValueError("oracle compression status %d" % meta[1])
     return out[:meta[0]].tobytes()
+
+
+def compress_parallel(data, chunk_bytes=32768, threads=None):
+    """compress() for large inputs: the chunks are independent, so several
+    host threads encode disjoint chunk ranges (ctypes drops the GIL), then
+    the stream is assembled as compress() writes it: 78 01, every chunk's
+    encoding in order, the big-endian Adler-32."""
+    from concurrent.futures import ThreadPoolExecutor
+    source = _view(data)
+    n = source.size
+    chunks = max(1, -(-n // chunk_bytes))
+    slot = slot_bytes(chunk_bytes)
+    per = 64
+
+    def encode(first):
+        count = min(per, chunks - first)
+        out = np.zeros(count * slot, dtype=np.uint8)
+        sizes = np.zeros(count, dtype=np.uint32)
+        failed = lib().oracle_compress_chunks(
+            _u8(source), n, chunk_bytes, first, count, _u8(out), slot,
+            sizes.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)))
+        if failed:
+            raise ValueError("oracle chunk compression failed")
+        return b"".join(out[k * slot:k * slot + int(sizes[k])].tobytes() for k in range(count))
+
+    with ThreadPoolExecutor(max_workers=threads or os.cpu_count() or 1) as pool:
+        bodies = list(pool.map(encode, range(0, chunks, per)))
+    return b"\x78\x01" + b"".join(bodies) + adler32(source).to_bytes(4, "big")

@@ -26,6 +26,17 @@ typedef uint32_t u32;
 typedef uint64_t u64;
 
 #define MAX_BYTES (1u << 28)        /* _codec.py:13, codec_ffi.cu:42 */
+/* Single-stream bounds of this codec, a deliberate superset of the
+ * reference's 2**28 (_codec.py:13,28,103): one stream may decode to 2**31
+ * bytes from at most 2**29 - 2**16 compressed bytes (bit offsets stay below
+ * 2**32), and compress up to 2**31 input bytes.  Batch calls keep 2**28. */
+#define MAX_STREAM_BYTES (1u << 31)
+#define MAX_STREAM_INPUT ((1u << 29) - (1u << 16))
+/* Chunk sizes: the reference accepts [256, 65535] (_codec.py:158-159); this
+ * codec also accepts chunks up to 2**18, whose stored fallback is split into
+ * blocks of at most 65535 bytes. */
+#define MAX_CHUNK_BYTES 262144u
+#define STORED_MAX 65535u
 #define MAX_CANDIDATES 262144u      /* _codec.py:14 */
 #define MAX_BLOCKS 262144u          /* _codec.py:15 */
 
@@ -612,9 +623,9 @@ static u32 emit_chain(const u8* data, u32 bytes, const ChainEntry* chain, u32 co
 
 u32 oracle_inflate_general(const u8* in, u64 in_size, u8* out, u64 out_size,
                            u32 max_candidates, u32 max_blocks) {
-  if (out_size > MAX_BYTES) return ST_BOUNDS;
+  if (out_size > MAX_STREAM_BYTES) return ST_BOUNDS;
   memset(out, 0, out_size);
-  if (in_size > MAX_BYTES || max_candidates < 1 || max_candidates > MAX_CANDIDATES ||
+  if (in_size > MAX_STREAM_INPUT || max_candidates < 1 || max_candidates > MAX_CANDIDATES ||
       max_blocks < 1 || max_blocks > MAX_BLOCKS)
     return ST_BOUNDS;
   u32 window = 0, wanted = 0;
@@ -659,8 +670,8 @@ done:
  * fast routes only ever publish success, which the general route shares. */
 u32 oracle_decompress(const u8* in, u64 in_size, u8* out, u64 out_size,
                       u32 max_candidates, u32 max_blocks) {
-  if (out_size > MAX_BYTES) return ST_BOUNDS;
-  if (in_size > MAX_BYTES || max_candidates < 1 || max_candidates > MAX_CANDIDATES ||
+  if (out_size > MAX_STREAM_BYTES) return ST_BOUNDS;
+  if (in_size > MAX_STREAM_INPUT || max_candidates < 1 || max_candidates > MAX_CANDIDATES ||
       max_blocks < 1 || max_blocks > MAX_BLOCKS) {
     memset(out, 0, out_size);
     return ST_BOUNDS;
@@ -809,6 +820,24 @@ static int build_tree(const u32* freq, u32 alphabet, u32 limit, u8* lengths, u16
 
 static u32 extent_of(u32 bits, int final) { return final ? (bits + 7) / 8 : (bits + 3 + 7) / 8 + 4; }
 
+/* Stored blocks of an n-byte chunk's stored fallback: one for chunks within
+ * the reference's bound (n <= 65535), else ceil(n / 65535). */
+static u32 stored_blocks(u32 n) { return n ? (n + STORED_MAX - 1) / STORED_MAX : 1u; }
+
+/* Worst-case stream layout of n bytes at `chunk` (both a multiple of nothing
+ * in particular): stored blocks of every chunk's fallback, which size the
+ * padded capacity n + 5 * stored + 6 (compress_zlib_padded, _codec.py:
+ * 151-177, where every chunk has one), and the most Deflate blocks the
+ * stream can hold (2 * chunks - 1 for chunks <= 65535). */
+static void stream_layout(u64 n, u32 chunk, u64* chunks_out, u64* stored_out, u64* blocks_out) {
+  u64 chunks = n ? (n + chunk - 1) / chunk : 1;
+  u32 last = (u32)(n - (chunks - 1) * chunk);
+  u64 full = stored_blocks(chunk), tail = stored_blocks(last);
+  *chunks_out = chunks;
+  *stored_out = (chunks - 1) * full + tail;
+  *blocks_out = (chunks - 1) * (full > 2 ? full : 2) + tail;
+}
+
 /* Encodes one chunk into `slot`; returns the status (0 ok).  `size` gets
  * the encoded byte count. */
 static u32 encode_chunk(const u8* data, u32 n, int final, u8* slot, u32 slot_bytes, u32* size) {
@@ -862,8 +891,10 @@ static u32 encode_chunk(const u8* data, u32 n, int final, u8* slot, u32 slot_byt
   }
   freq[256]++;
 
-  /* Exact stored / fixed / dynamic extents (encode_chunk, :312-356). */
-  u32 mode = 0, extent = n + 5, status = 0;
+  /* Exact stored / fixed / dynamic extents (encode_chunk, :312-356); the
+   * stored fallback of a chunk above 65535 bytes takes several blocks. */
+  const u32 nstored = stored_blocks(n);
+  u32 mode = 0, extent = n + 5 * nstored, status = 0;
   u32 fixed_bits = 3 + extra_bits, dist_tokens = 0;
   for (u32 i = 0; i < 286; ++i)
     fixed_bits += freq[i] * (i <= 143 ? 8u : i <= 255 ? 9u : i <= 279 ? 7u : 8u);
@@ -923,11 +954,18 @@ static u32 encode_chunk(const u8* data, u32 n, int final, u8* slot, u32 slot_byt
   *size = 0;
   if (mode == 3) goto out;
   if (mode == 0) {
-    slot[0] = final ? 1 : 0;
-    slot[1] = (u8)n; slot[2] = (u8)(n >> 8);
-    u32 c = n ^ 65535u;
-    slot[3] = (u8)c; slot[4] = (u8)(c >> 8);
-    memcpy(slot + 5, data, n);
+    /* Blocks of 65535 bytes, the last one shorter; only the stream's very
+     * last block carries BFINAL. */
+    u32 at = 0;
+    for (u32 k = 0; k < nstored; ++k) {
+      u32 len = n - k * STORED_MAX < STORED_MAX ? n - k * STORED_MAX : STORED_MAX;
+      slot[at] = (final && k + 1 == nstored) ? 1 : 0;
+      slot[at + 1] = (u8)len; slot[at + 2] = (u8)(len >> 8);
+      u32 c = len ^ 65535u;
+      slot[at + 3] = (u8)c; slot[at + 4] = (u8)(c >> 8);
+      memcpy(slot + at + 5, data + k * STORED_MAX, len);
+      at += 5 + len;
+    }
     *size = extent;
     goto out;
   }
@@ -980,19 +1018,23 @@ out:
 }
 
 /* Whole-stream compression: metadata = [encoded_length, status].  The
- * capacity must be n + 5*chunks + 6 (compress_zlib_padded, _codec.py:151-177). */
+ * capacity must be n + 5 * stored_blocks + 6, i.e. n + 5*chunks + 6 for
+ * chunks <= 65535 (compress_zlib_padded, _codec.py:151-177). */
 u32 oracle_compress(const u8* in, u64 n, u32 chunk_bytes, u8* out, u64 capacity, u32* meta) {
   meta[0] = 0;
   meta[1] = 0;
   memset(out, 0, capacity);
-  if (n > MAX_BYTES || chunk_bytes < 256 || chunk_bytes > 65535) { meta[1] = ST_BOUNDS; return ST_BOUNDS; }
-  u64 chunks = (n + chunk_bytes - 1) / chunk_bytes;
-  if (!chunks) chunks = 1;
-  if (2 * chunks - 1 > MAX_BLOCKS || n + chunks * 5 + 6 > MAX_BYTES || capacity != n + chunks * 5 + 6) {
+  if (n > MAX_STREAM_BYTES || chunk_bytes < 256 || chunk_bytes > MAX_CHUNK_BYTES) {
     meta[1] = ST_BOUNDS;
     return ST_BOUNDS;
   }
-  u32 slot_bytes = (chunk_bytes * 9 + 7) / 8 + 16;
+  u64 chunks, stored, blocks;
+  stream_layout(n, chunk_bytes, &chunks, &stored, &blocks);
+  if (blocks > MAX_BLOCKS || capacity != n + stored * 5 + 6) {
+    meta[1] = ST_BOUNDS;
+    return ST_BOUNDS;
+  }
+  u32 slot_bytes = (chunk_bytes * 9 + 7) / 8 + 16 + 5 * stored_blocks(chunk_bytes);
   u8* slot = (u8*)malloc(slot_bytes);
   u64 total = 2;
   out[0] = 0x78;

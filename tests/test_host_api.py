@@ -82,10 +82,11 @@ def test_batch_invalid_extents_and_chunks(no_backend):
     with pytest.raises(ValueError, match="chunk_bytes"):
         codec.compress_zlib_batch_padded(b"", (0,), chunk_bytes=255)
     with pytest.raises(ValueError, match="chunk_bytes"):
-        codec.compress_zlib_batch_padded(b"", (0,), chunk_bytes=65536)
+        codec.compress_zlib_batch_padded(b"", (0,), chunk_bytes=262145)
 
 
-@pytest.mark.parametrize("chunk", [255, 65536, True, 1.0])
+# chunk_bytes is a superset of the reference's [256, 65535]: up to 262144.
+@pytest.mark.parametrize("chunk", [255, 262145, True, 1.0])
 def test_compress_rejects_bad_chunk_bytes(no_backend, chunk):
     with pytest.raises(ValueError, match="chunk_bytes"):
         no_backend.compress_zlib_padded(b"abc", chunk_bytes=chunk)
@@ -107,7 +108,7 @@ def _header(cmf=0x78, flags=0):
     (b"\x78\x00" + b"\x00" * 8, 0, "CodecError"),
     (b"", -1, ValueError),
     (b"", True, ValueError),
-    (b"\x78\x9c" + b"\x00" * 8, 2**28 + 1, ValueError),
+    (b"\x78\x9c" + b"\x00" * 8, 2**31 + 1, ValueError),
 ])
 def test_host_rejects_invalid_input_before_the_backend(no_backend, payload, expected, error):
     if isinstance(error, str):
@@ -164,3 +165,30 @@ def test_golden_payload_framing_matches_host_precheck():
     body = _stored_blocks(data, final=True)
     stream = b"\x78\x01" + body + struct.pack(">I", zlib.adler32(data))
     assert zlib.decompress(stream) == data
+
+
+def test_single_stream_bounds_are_the_documented_superset():
+    """One stream holds up to 2**31 uncompressed bytes (the reference stops at
+    2**28); chunks above 65535 bytes count one stored block per 65535 bytes in
+    the padded capacity, which otherwise keeps the reference's formula."""
+    from cuda_zlib import _codec
+    assert _codec._MAX_STREAM == 2**31
+    assert _codec._MAX_STREAM_PAYLOAD == 2**29 - 2**16
+    for size, chunk in [(0, 256), (1, 32768), (100000, 32768), (2**28, 65535)]:
+        chunks = max(1, -(-size // chunk))
+        assert _codec._capacity(size, chunk) == (size + 5 * chunks + 6, chunks)
+    # 2**30 at 262144: 4096 chunks of five stored blocks each.
+    assert _codec._capacity(2**30, 262144) == (2**30 + 5 * 4096 * 5 + 6, 4096)
+    assert _codec._capacity(262145, 262144) == (262145 + 5 * (5 + 1) + 6, 2)
+    with pytest.raises(ValueError, match="2\\*\\*29"):
+        _codec._check_framing(b"\x78\x9c" + bytes(2**29), 0)
+
+
+def test_oracle_capacity_matches_the_api():
+    from cuda_zlib import _codec
+    from oracle import oracle
+    for size in (0, 1, 65535, 65536, 262144, 262145, 10**6, 2**30):
+        for chunk in (256, 32768, 65535, 65536, 131072, 262144):
+            if size // chunk > 300000:
+                continue
+            assert oracle.capacity(size, chunk) == _codec._capacity(size, chunk)[0]

@@ -97,3 +97,56 @@ def test_noalloc_rejects_calls_beyond_its_limits(native):
     code, out, meta = _run(native.cuda_zlib_compress_noalloc, raw, 4096, stream)
     want = _run(native.cuda_zlib_compress, raw, 4096, stream)
     assert (code, out, meta) == want
+
+
+_FRESH_PROCESS = r"""
+import ctypes, json, sys
+import torch
+sys.path.insert(0, sys.argv[1])
+from cuda_zlib import _native
+lib = _native.library()
+entry = lib.cuda_zlib_compress_noalloc
+entry.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_int64, ctypes.c_void_p,
+                  ctypes.c_uint64, ctypes.c_void_p, ctypes.c_void_p]
+size, chunk = 1 << 20, 32768
+capacity = size + 5 * (size // chunk) + 6
+source = (torch.arange(size, device="cuda") % 251).to(torch.uint8)
+output = torch.zeros(capacity, dtype=torch.uint8, device="cuda")
+metadata = torch.zeros(2, dtype=torch.int32, device="cuda")
+stream = torch.cuda.current_stream().cuda_stream
+def call():
+    code = entry(source.data_ptr(), size, chunk, output.data_ptr(), capacity,
+                 metadata.data_ptr(), stream)
+    torch.cuda.synchronize()
+    return code
+first = call()                      # first call on the device: set-up
+free_before = torch.cuda.mem_get_info()[0]
+codes = [call() for _ in range(3)]  # warm calls
+free_after = torch.cuda.mem_get_info()[0]
+stats = (ctypes.c_uint64 * 4)()
+pool_code = lib.CudaZlibWorkspacePoolStats(0, stats)
+print(json.dumps({"codes": [first] + codes, "free_before": free_before,
+                  "free_after": free_after, "pool_code": pool_code,
+                  "stats": list(stats), "meta": metadata.cpu().tolist()}))
+"""
+
+
+def test_noalloc_allocates_nothing_in_a_fresh_process():
+    """The property the entry point exists for: in a process that has made no
+    other codec call, warm calls leave the device's free memory unchanged and
+    create no workspace pool (CudaZlibWorkspacePoolStats reports none)."""
+    import json
+    import os
+    import subprocess
+    import sys
+    package = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                           "cuda-zlib_b200")
+    result = subprocess.run([sys.executable, "-c", _FRESH_PROCESS, package],
+                            capture_output=True, text=True, timeout=300)
+    assert result.returncode == 0, result.stderr[-2000:]
+    report = json.loads(result.stdout.strip().splitlines()[-1])
+    assert report["codes"] == [0, 0, 0, 0]
+    assert report["meta"][1] == 0 and report["meta"][0] > 0
+    assert report["free_after"] == report["free_before"]
+    assert report["pool_code"] == 0
+    assert report["stats"][1:] == [0, 0, 0]  # reserved, used, pool count
