@@ -1,38 +1,40 @@
 #!/usr/bin/env python
-"""Codec benchmark on B200: BASELINE config 1 through the cuda_zlib API.
+"""Codec benchmark on B200: the BASELINE configurations through the cuda_zlib API.
 
-Workload (one step, N=1): the 64 MiB float32 random walk of config 1
-(16,777,216 samples, seed 1: x[i] = x[i-1] + N(0, 1e-3) plus
-1e-2 * sin(2 pi 60 i / 4096)), compressed by CPU zlib at levels 1 and 6
-outside the timed region.  A step decodes both streams
-(decompress_zlib_checked) and compresses the array at chunk_bytes=32768
-(compress_zlib_padded): 3 x 64 MiB of uncompressed bytes.
+Headline workload (default, any N): config 4a, 65,536 independent files of
+exactly 64 KiB (4 GiB) with the config-2 content mix (seed 4).  The files
+are assigned to ranks by the LPT planner (cuda_zlib.sharding) from their
+sizes and content kinds; each rank decodes its files' CPU-zlib level-6
+streams with decompress_zlib_batch_checked and compresses its files at
+chunk_bytes=32768 with compress_zlib_batch_padded, in calls within the batch
+bounds (4096 and 4095 files of 64 KiB).  One step = every rank's share:
+2 x 4 GiB of uncompressed bytes for the whole job.
 
-  value  = uncompressed GB/s (1e9 B/s) with inputs resident in HBM, timed
-           with CUDA events on the codec's stream, L2 flushed between steps;
-  e2e    = the same step from inputs in pinned host memory to results
-           (and statuses) in pinned host memory, with the H2D copies of the
-           inputs and the D2H copies of the results inside the timed region
-           (host wall clock): copies in on one stream, the three codec calls
-           in order on a compute stream, results out on a third stream as each
-           call finishes;
-  roofline = the dominant kernel's algorithmic bytes (U + C per launch)
-           over its event-timed device time, against the measured HBM copy
-           bandwidth;
-  cpu_baseline = the CPU oracle (the reference's algorithms restated in C)
-           on a 16 MiB sample of the same data.
+  value    uncompressed GB/s (1e9 B/s), whole job: 2 x 4 GiB / the slowest
+           rank's device time (CUDA events on the codec's stream), inputs
+           resident in HBM and larger than L2 (L2 also flushed per step);
+  e2e      the same step through the host-buffer calls
+           (decompress_zlib_batch_host, compress_zlib_batch_host) from inputs
+           in pinned host memory to results in host memory, copies inside the
+           timed region (host wall clock, slowest rank);
+  roofline the dominant kernel's algorithmic bytes (C + U of the calls it
+           served) over its event-timed device time, against the measured
+           HBM copy bandwidth (MEASURED_PEAKS.json);
+  cpu_baseline  Python's zlib on a bounded sample of the same files:
+           zlib.decompress of the level-6 streams and zlib.compress at level
+           1, one file per task in a multiprocessing pool (fork, inputs
+           inherited) over all host cores;
+  configs  (N = 1 only) the same measurements for configs 0, 1, 2, 3 and 4b.
 
---gpus N > 1 runs one process per GPU (torchrun); single-stream decode has
-no shard structure, so each rank runs an independent replica (weak scaling)
-and value = all ranks' bytes / the slowest rank's time.
---impl reference times the reference's CPU path: the reference has no CPU
-codec and its CUDA sources cannot be built here (generated from Python
-strings, needs XLA FFI headers), so the arm runs the oracle port with all
-host threads on the same workload.
+--impl reference times the reference's CPU path, which for this codec is
+Python's zlib (the reference's own CPU baseline, benchmarks/benchmark.py:
+126-169): the whole config-4a step (all 65,536 files, both directions) in a
+multiprocessing pool over all host cores, rank 0 only.
 """
 import argparse
-import hashlib
+import ctypes
 import json
+import multiprocessing
 import os
 import subprocess
 import sys
@@ -44,40 +46,27 @@ import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "cuda-zlib_b200"))
+sys.path.insert(0, ROOT)
+
+import workloads  # noqa: E402
 
 MIB = 1 << 20
 CHUNK = 32768
-L2_BYTES = 126 * MIB
+FILE = 65536
+FILES = 65536
+CPU_LEVEL = 1  # CPU-side compression level of the baseline (zlib's fastest)
 
-
-# ------------------------------------------------------------------ data
-def config1_float32(samples=16777216, seed=1):
-    """Config 1: float32 LE random walk plus a 60-cycle-per-4096 sine."""
-    rng = np.random.default_rng(seed)
-    walk = np.cumsum(rng.normal(0.0, 1e-3, samples))
-    i = np.arange(samples, dtype=np.float64)
-    x = walk + 1e-2 * np.sin(2 * np.pi * 60 * i / 4096)
-    return x.astype("<f4").tobytes()
-
-
-def zlib_stream(raw, level, strategy=zlib.Z_DEFAULT_STRATEGY):
-    c = zlib.compressobj(level, zlib.DEFLATED, zlib.MAX_WBITS, 8, strategy)
-    return c.compress(raw) + c.flush()
-
-
-def workload(size_mib=64):
-    raw = config1_float32()[:size_mib * MIB]
-    streams = {}
-
-    def make(level):
-        streams[level] = zlib_stream(raw, level)
-
-    threads = [threading.Thread(target=make, args=(level,)) for level in (1, 6)]
-    for t in threads:
-        t.start()
-    for t in threads:
-        t.join()
-    return raw, streams[1], streams[6]
+METRIC = "decompress & compress GB/s (uncompressed bytes)"
+CONFIG = {"workload": "config4a: 65,536 files x 64 KiB (seed 4), config-2 content mix; "
+                      "decode their zlib level-6 streams (decompress_zlib_batch_checked) and "
+                      "compress at chunk_bytes=32768 (compress_zlib_batch_padded)",
+          "files": FILES, "file_bytes": FILE, "chunk_bytes": CHUNK,
+          "uncompressed_bytes_per_step": 2 * FILES * FILE,
+          "parallelism": "files LPT-sharded over ranks",
+          "l2": "inputs larger than L2; L2 also flushed between steps"}
+# Estimated compressed fraction of each content kind (text, random, runs):
+# the LPT weights, known to every rank without compressing anything.
+KIND_RATIO = (0.36, 1.0, 0.05)
 
 
 # ------------------------------------------------------------------ helpers
@@ -90,13 +79,13 @@ def measured_peak():
         return 6650.0, "fallback"
 
 
-def committed_traffic(kernel):
+def committed_traffic(workload, kernel):
     """DRAM bytes per launch of `kernel` from the committed ncu summary."""
     path = os.path.join(ROOT, "profiles", "kernel_traffic.json")
     try:
         with open(path) as handle:
-            return json.load(handle).get(kernel)
-    except (OSError, ValueError):
+            return json.load(handle).get(workload, {}).get(kernel)
+    except (OSError, ValueError, AttributeError):
         return None
 
 
@@ -159,483 +148,135 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sms)}
 
 
-# ------------------------------------------------------------------ CPU side
-def cpu_port(raw, l1, l6, threads):
-    """One sample step of the oracle port: decode both streams (one thread
-    each: a single stream is serial) and compress the array chunk-parallel."""
-    from oracle import oracle
-    import ctypes
-    lib = oracle.lib()
-    results = {}
+# ------------------------------------------------------------------ config 4a inputs
+def plan_4a(world):
+    """LPT plan of the config-4a files over `world` ranks (same on every rank)."""
+    from cuda_zlib import sharding
+    kinds, _ = workloads.config4a_kinds(FILES)
+    weights = [FILE + int(FILE * KIND_RATIO[k]) for k in kinds.tolist()]
+    return sharding.plan_files(weights, world)
 
-    def decode(name, payload):
-        out, status = oracle.inflate_serial(payload, len(raw))
-        results[name] = status == 0 and out == raw
 
-    src = np.frombuffer(raw, dtype=np.uint8)
-    chunks = max(1, -(-len(raw) // CHUNK))
-    slot = (CHUNK * 9 + 7) // 8 + 16
-    slots = np.zeros(chunks * slot, dtype=np.uint8)
-    sizes = np.zeros(chunks, dtype=np.uint32)
-    per = -(-chunks // max(1, threads - 2))
+def inputs_4a(indices):
+    """(packed files, list of level-6 streams) of the given config-4a files."""
+    packed, _ = workloads.config4a_files(indices)
+    streams = workloads.zlib_files(packed, FILE, 6)
+    return packed, streams
 
-    def encode(first):
-        count = min(per, chunks - first)
-        if count <= 0:
-            return
-        lib.oracle_compress_chunks(
-            src.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)), len(raw), CHUNK, first, count,
-            slots[first * slot:].ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)), slot,
-            sizes[first:].ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)))
 
-    workers = [threading.Thread(target=decode, args=("l1", l1)),
-               threading.Thread(target=decode, args=("l6", l6))]
-    workers += [threading.Thread(target=encode, args=(first,))
-                for first in range(0, chunks, per)]
+# ------------------------------------------------------------------ CPU baseline
+# Inputs of the pool's tasks, set before the pool forks so that the workers
+# inherit them instead of receiving pickles.
+_CPU_INPUTS = {}
+
+
+def _cpu_task(k):
+    packed, streams = _CPU_INPUTS["files"], _CPU_INPUTS["streams"]
+    n = len(zlib.decompress(streams[k]))
+    n += len(zlib.compress(packed[k * FILE:(k + 1) * FILE], CPU_LEVEL))
+    return n
+
+
+def cpu_pool(packed, streams, processes):
+    """A fork pool whose workers hold the files and streams (made before any
+    CUDA call: a pool forked after CUDA initialisation can hang)."""
+    _CPU_INPUTS["files"], _CPU_INPUTS["streams"] = packed, streams
+    return multiprocessing.get_context("fork").Pool(processes)
+
+
+def cpu_step(pool, count):
+    """One pass of zlib.decompress + zlib.compress over files [0, count)."""
     start = time.perf_counter()
-    for w in workers:
-        w.start()
-    for w in workers:
-        w.join()
-    elapsed = time.perf_counter() - start
-    if not (results.get("l1") and results.get("l6")):
-        raise RuntimeError("CPU oracle decode mismatch")
-    return elapsed
-
-
-def cpu_sample():
-    """16 MiB of the config-1 data and its zlib streams (bounded CPU work)."""
-    raw = config1_float32()[:16 * MIB]
-    return raw, zlib_stream(raw, 1), zlib_stream(raw, 6)
+    pool.map(_cpu_task, range(count), chunksize=max(1, count // (8 * pool._processes)))
+    return time.perf_counter() - start
 
 
 def run_reference(args, rank, world):
+    """The reference arm: Python's zlib on the whole config-4a step."""
     if rank != 0:
         return
-    from oracle import oracle
-    oracle.build()
-    threads = os.cpu_count() or 1
-    raw, l1, l6 = cpu_sample()
-    for _ in range(args.warmup):
-        cpu_port(raw, l1, l6, threads)
-    times = [cpu_port(raw, l1, l6, threads) for _ in range(args.steps)]
+    cores = os.cpu_count() or 1
+    packed, streams = inputs_4a(range(FILES))
+    pool = cpu_pool(packed, streams, cores)
+    try:
+        for _ in range(args.warmup):
+            cpu_step(pool, FILES)
+        times = [cpu_step(pool, FILES) for _ in range(args.steps)]
+    finally:
+        pool.close()
+        pool.join()
     seconds = sum(times) / len(times)
-    value = 3 * len(raw) / seconds / 1e9
-    sample = ("16 MiB slice of config 1: zlib L1 + L6 decode (one thread per stream) and "
-              "chunk-parallel compress at 32 KiB, oracle port")
-    line = {
+    value = 2 * FILES * FILE / seconds / 1e9
+    sample = ("whole config-4a step: zlib.decompress of all 65,536 level-6 streams and "
+              "zlib.compress(level 1) of all 65,536 files, one file per task, "
+              "multiprocessing pool (fork) of %d processes" % cores)
+    print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(seconds * 1e3, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "u8", "data": "synthetic",
-        "config": CONFIG,
-        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads,
-                         "kind": "port", "sample": sample},
-        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
-    }
-    print(json.dumps(line), flush=True)
-
-
-# ------------------------------------------------------------------ GPU side
-METRIC = ("decompress & compress GB/s (uncompressed bytes; zlib L1+L6 decode and "
-          "chunk-32768 compress of config 1)")
-CONFIG = {"workload": "config1: 64 MiB float32 random walk (seed 1); decode zlib L1 and L6 "
-                      "streams, compress at chunk_bytes=32768",
-          "uncompressed_bytes_per_step": 3 * 64 * MIB, "chunk_bytes": CHUNK,
-          "l2": "flushed between steps (256 MiB write)"}
-
-
-def run_gpu(args, rank, world):
-    import torch
-    import cuda_zlib as codec
-    from cuda_zlib import _native
-    import ctypes
-
-    torch.cuda.set_device(rank % torch.cuda.device_count())
-    device = torch.device("cuda", torch.cuda.current_device())
-    codec.compile_kernels(device)
-    raw, l1, l6 = workload(args.size_mib)
-    U = len(raw)
-    raw_dev = torch.frombuffer(bytearray(raw), dtype=torch.uint8).to(device)
-    l1_dev = torch.frombuffer(bytearray(l1), dtype=torch.uint8).to(device)
-    l6_dev = torch.frombuffer(bytearray(l6), dtype=torch.uint8).to(device)
-    flush = torch.empty(256 * MIB, dtype=torch.uint8, device=device)
-    stream = torch.cuda.current_stream(device)
-
-    # The device-resident step runs its three parts in order on one stream
-    # (each part fills the GPU; running them on three streams measured no
-    # faster and blurs the per-kernel times).
-    def step():
-        o1, m1 = codec.decompress_zlib_checked(l1_dev, U, device)
-        o6, m6 = codec.decompress_zlib_checked(l6_dev, U, device)
-        c, mc = codec.compress_zlib_padded(raw_dev, device, chunk_bytes=CHUNK)
-        return o1, m1, o6, m6, c, mc
-
-    for _ in range(args.warmup):
-        result = step()
-    torch.cuda.synchronize()
-    o1, m1, o6, m6, c, mc = result
-    assert [int(v) for v in m1.cpu()] == [0, 0] and [int(v) for v in m6.cpu()] == [0, 0]
-    assert o1.cpu().numpy().tobytes() == raw and o6.cpu().numpy().tobytes() == raw
-    length, status = (int(v) for v in mc.cpu())
-    assert status == 0
-    stream_bytes = c[:length].cpu().numpy().tobytes()
-    assert zlib.decompress(stream_bytes) == raw
-    ratio = length / U
-
-    lib = _native.library()
-    lib.cuda_zlib_b200_profile.argtypes = [ctypes.c_int]
-    lib.cuda_zlib_b200_profile_read.argtypes = [ctypes.c_char_p, ctypes.POINTER(ctypes.c_double),
-                                                ctypes.POINTER(ctypes.c_uint64)]
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
-    lib.cuda_zlib_b200_launches.restype = ctypes.c_uint64
-    lib.cuda_zlib_b200_profile(1)
-    launches_before = lib.cuda_zlib_b200_launches()
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    with ClockSampler(device.index) as clocks:
-        for k in range(args.steps):
-            flush.fill_(k & 255)
-            starts[k].record(stream)
-            step()
-            ends[k].record(stream)
-        torch.cuda.synchronize()
-    launched = lib.cuda_zlib_b200_launches() - launches_before
-    if world > 1:
-        torch.distributed.barrier()
-    kernels = {}
-    for name in ("serial_inflate_kernel", "discover_kernel", "validate_kernel", "describe_kernel",
-                 "symbols_kernel", "expand_kernel", "resolve_kernel",
-                 "encode_chunks_kernel", "encode_pack_kernel"):
-        total, launches = ctypes.c_double(), ctypes.c_uint64()
-        lib.cuda_zlib_b200_profile_read(name.encode(), ctypes.byref(total), ctypes.byref(launches))
-        if launches.value:
-            kernels[name] = (total.value, launches.value)
-    lib.cuda_zlib_b200_profile(0)
-    seconds = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / 1e3
-    if world > 1:
-        t = torch.tensor([seconds], dtype=torch.float64, device=device)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        seconds = float(t.item())
-    per_step = seconds / args.steps
-    value = world * 3 * U / per_step / 1e9
-
-    # Dominant kernel's roofline: algorithmic bytes (U + C per launch).
-    algorithmic = {
-        "serial_inflate_kernel": (U + len(l1), U + len(l6)),
-        "symbols_kernel": (len(l1), len(l6)),
-        "expand_kernel": (U, U),
-        "resolve_kernel": (U // 8, U // 8),
-        "describe_kernel": (len(l1), len(l6)),
-        "encode_chunks_kernel": (U + length,),
-        "encode_pack_kernel": (2 * length,),
-        "discover_kernel": (len(l1), len(l6)),
-        "validate_kernel": (len(l1), len(l6)),
-    }
-    name, (total_ms, launches) = max(kernels.items(), key=lambda kv: kv[1][0])
-    per_launch = algorithmic.get(name, (U,))
-    bytes_per_launch = sum(per_launch) / len(per_launch)
-    achieved = bytes_per_launch / (total_ms / launches / 1e3) / 1e9
-    peak, peak_kind = measured_peak()
-    traffic = committed_traffic(name)
-
-    # End to end through the host-buffer API.
-    e2e_times = []
-    if args.no_e2e:
-        e2e_times.append(float("nan"))
-    # Step inputs sit in pinned host memory (page-locked CPU tensors) and the
-    # results end there.  The step is the pipeline a user of the device API
-    # writes: the inputs go in on a copy stream, the three codec calls run in
-    # order on one compute stream (each waiting for its own input only), and
-    # each result goes out on a third stream as soon as its call finishes, so
-    # copies overlap compute.  The compressed stream goes out at its exact
-    # length, read from the call's metadata.  The host wall clock spans the
-    # step from the first copy to the last result and status in host memory.
-    l1_host = torch.frombuffer(bytearray(l1), dtype=torch.uint8).pin_memory()
-    l6_host = torch.frombuffer(bytearray(l6), dtype=torch.uint8).pin_memory()
-    raw_host = torch.frombuffer(bytearray(raw), dtype=torch.uint8).pin_memory()
-    out1_host = torch.empty(U, dtype=torch.uint8).pin_memory()
-    out6_host = torch.empty(U, dtype=torch.uint8).pin_memory()
-    comp_host = torch.empty(U + 5 * (U // CHUNK + 1) + 6, dtype=torch.uint8).pin_memory()
-    meta_host = torch.empty(6, dtype=torch.int32).pin_memory()
-    copy_in, compute, copy_out = (torch.cuda.Stream(device) for _ in range(3))
-
-    def e2e_step():
-        inputs, results = [], []
-        with torch.cuda.stream(copy_in):
-            for host in (l1_host, l6_host, raw_host):
-                ready = torch.cuda.Event()
-                inputs.append((host.to(device, non_blocking=True), ready))
-                ready.record(copy_in)
-        with torch.cuda.stream(compute):
-            for k, (data, ready) in enumerate(inputs):
-                compute.wait_event(ready)
-                out, meta = (codec.decompress_zlib_checked(data, U, device) if k < 2 else
-                             codec.compress_zlib_padded(data, device, chunk_bytes=CHUNK))
-                done = torch.cuda.Event()
-                done.record(compute)
-                results.append((out, meta, done))
-        with torch.cuda.stream(copy_out):
-            for k, (out, meta, done) in enumerate(results[:2]):
-                copy_out.wait_event(done)
-                (out1_host, out6_host)[k].copy_(out, non_blocking=True)
-                meta_host[2 * k:2 * k + 2].copy_(meta.view(torch.int32), non_blocking=True)
-            c_out, c_meta, c_done = results[2]
-            copy_out.wait_event(c_done)
-            meta_host[4:6].copy_(c_meta.view(torch.int32), non_blocking=True)
-            copy_out.synchronize()
-            length = int(meta_host[4])
-            comp_host[:length].copy_(c_out[:length], non_blocking=True)
-            copy_out.synchronize()
-        status = meta_host.tolist()
-        assert status[0] == 0 and status[2] == 0 and status[5] == 0, status
-        return length
-
-    e2e_length = 0
-    for k in range(0 if args.no_e2e else max(args.warmup, 1) + args.steps):
-        flush.fill_(k & 255)
-        torch.cuda.synchronize()
-        begin = time.perf_counter()
-        e2e_length = e2e_step()
-        elapsed = time.perf_counter() - begin
-        if k >= max(args.warmup, 1):
-            e2e_times.append(elapsed)
-    if not args.no_e2e:
-        assert out1_host.numpy().tobytes() == raw and out6_host.numpy().tobytes() == raw
-        assert comp_host[:e2e_length].numpy().tobytes() == stream_bytes
-    e2e_seconds = sum(e2e_times) / len(e2e_times)
-    if world > 1:
-        t = torch.tensor([e2e_seconds], dtype=torch.float64, device=device)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        e2e_seconds = float(t.item())
-    e2e_value = world * 3 * U / e2e_seconds / 1e9
-
-    if rank != 0:
-        return
-    cpu = None
-    if world == 1 and not args.no_cpu:
-        sample_raw, s1, s6 = cpu_sample()
-        threads = os.cpu_count() or 1
-        cpu_port(sample_raw, s1, s6, threads)
-        cpu_time = cpu_port(sample_raw, s1, s6, threads)
-        cpu = {"value": round(3 * len(sample_raw) / cpu_time / 1e9, 4), "unit": "GB/s",
-               "cores": threads, "kind": "port",
-               "sample": "16 MiB slice of config 1: zlib L1 + L6 decode (one thread per "
-                         "stream) and chunk-parallel compress at 32 KiB, oracle port"}
-    line = {
-        "metric": METRIC, "value": round(value, 4), "unit": "GB/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step * 1e3, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
-        "data": "synthetic", "config": dict(CONFIG, uncompressed_bytes_per_step=3 * U,
-                                            parallelism="replicas" if world > 1 else "1 GPU",
-                                            compression_ratio=round(ratio, 5),
-                                            zlib_l1_ratio=round(len(l1) / U, 5),
-                                            zlib_l6_ratio=round(len(l6) / U, 5)),
-        "roofline": {"bound": "hbm", "kernel": name, "achieved": round(achieved, 2),
-                     "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
-                     "frac": round(achieved / peak, 5),
-                     "traffic": traffic,
-                     "algorithmic_bytes_per_launch": int(bytes_per_launch),
-                     "launch_ms": round(total_ms / launches, 4)},
-        "kernels_ms_per_step": {k: round(v[0] / args.steps, 3) for k, v in kernels.items()},
-        "e2e": None if args.no_e2e else {
-            "value": round(e2e_value, 4), "unit": "GB/s",
-            "h2d_bytes_per_step": len(l1) + len(l6) + U,
-            "d2h_bytes_per_step": 2 * U + length + 24, "timer": "host wall clock"},
-        "cpu_baseline": cpu,
-        "clocks": clocks.summary(),
-        "gpu_launches": launched,
-    }
-    print(json.dumps(line), flush=True)
-
-
-# ------------------------------------------------------------------ configs 0, 2, 3
-def zipf_vocabulary(seed=0):
-    """Config 0 vocabulary: 4096 random lowercase words of 3-10 letters and
-    their Zipf(s=1.1) rank weights."""
-    rng = np.random.default_rng(seed)
-    lengths = rng.integers(3, 11, 4096)
-    letters = rng.integers(97, 123, (4096, 10), dtype=np.uint8)
-    weights = np.arange(1, 4097, dtype=np.float64) ** -1.1
-    return letters, lengths, weights / weights.sum(), rng
-
-
-def zipf_text(size, seed=0):
-    """Config 0 corpus: Zipf words joined by single spaces, '\n' with p = 1/12."""
-    letters, lengths, p, rng = zipf_vocabulary(seed)
-    n = size // 6 + 64
-    while True:
-        idx = rng.choice(4096, n, p=p)
-        word_len = lengths[idx]
-        starts = np.concatenate(([0], np.cumsum(word_len + 1)[:-1]))
-        buf = np.empty(int(starts[-1] + word_len[-1] + 1), dtype=np.uint8)
-        for j in range(10):
-            m = word_len > j
-            buf[starts[m] + j] = letters[idx[m], j]
-        buf[starts + word_len] = np.where(rng.random(n) < 1 / 12, 10, 32).astype(np.uint8)
-        if buf.size >= size:
-            return buf[:size].tobytes()
-        n *= 2
-
-
-def config2_files(count=4096, seed=2):
-    """Config 2: log-uniform sizes on 256 B-256 KiB (1% empty); 50% slices of
-    the config-0 corpus, 25% uniform random bytes, 25% runs (geometric mean
-    length 64, values 0-15)."""
-    rng = np.random.default_rng(seed)
-    sizes = np.exp(rng.uniform(np.log(256), np.log(262144), count)).astype(np.int64)
-    sizes[rng.choice(count, count // 100, replace=False)] = 0
-    kinds = rng.choice(3, count, p=[0.5, 0.25, 0.25])
-    corpus = np.frombuffer(zipf_text(16 * MIB, 0), dtype=np.uint8)
-    files = []
-    for n, kind in zip(sizes.tolist(), kinds.tolist()):
-        if kind == 0:
-            start = int(rng.integers(0, corpus.size - n + 1))
-            data = corpus[start:start + n]
-        elif kind == 1:
-            data = rng.integers(0, 256, n, dtype=np.uint8)
-        else:
-            runs = rng.geometric(1 / 64, n // 32 + 64)
-            while runs.sum() < n:
-                runs = np.concatenate((runs, rng.geometric(1 / 64, n // 32 + 64)))
-            data = np.repeat(rng.integers(0, 16, runs.size, dtype=np.uint8), runs)[:n]
-        files.append(data.tobytes())
-    return files
-
-
-def config3_records(size=1 << 30, seed=3):
-    """Config 3: 64-byte records (i32 id, i32 timestamp += U{1..10}, 4 x i16
-    U[-100, 100], a 20-byte config-0 word, zero padded, 28 zero bytes)."""
-    n = size // 64
-    rng = np.random.default_rng(seed)
-    rec = np.zeros(n, dtype=[("id", "<i4"), ("ts", "<i4"), ("f", "<i2", (4,)),
-                             ("word", "S20"), ("pad", "V28")])
-    rec["id"] = np.arange(n, dtype=np.int32)
-    rec["ts"] = np.cumsum(rng.integers(1, 11, n), dtype=np.int64).astype(np.int32)
-    rec["f"] = rng.integers(-100, 101, (n, 4), dtype=np.int16)
-    letters, lengths, p, _ = zipf_vocabulary(0)
-    vocab = np.array([letters[i, :lengths[i]].tobytes() for i in range(4096)], dtype="S20")
-    rec["word"] = vocab[rng.choice(4096, n, p=p)]
-    return rec.view(np.uint8)
-
-
-def _parallel_map(fn, items, threads):
-    from concurrent.futures import ThreadPoolExecutor
-    with ThreadPoolExecutor(max_workers=threads) as pool:
-        return list(pool.map(fn, items))
-
-
-# ------------------------------------------------------------------ sharded workloads
-BATCH_METRIC = ("decompress & compress GB/s (uncompressed bytes; config-2 batch of 4096 "
-                "files: zlib L6 batch decode + chunk-32768 batch compress)")
-RECORDS_METRIC = ("compress GB/s (uncompressed bytes; config-3 1 GiB record stream, "
-                  "chunk-32768 ranges)")
-
-
-def batch_inputs():
-    files = config2_files()
-    streams = _parallel_map(lambda f: zlib_stream(f, 6), files, os.cpu_count() or 1)
-    return files, streams
-
-
-def cpu_batch(files, streams, threads):
-    """Oracle port over a file sample: serial-route decode and compress per file."""
-    from oracle import oracle
-
-    def one(k):
-        out, status = oracle.inflate_serial(streams[k], len(files[k]))
-        assert status == 0 and out == files[k]
-        oracle.compress(files[k], CHUNK)
-
-    start = time.perf_counter()
-    _parallel_map(one, range(len(files)), threads)
-    return time.perf_counter() - start
-
-
-def cpu_records(sample, threads):
-    """Oracle port: chunk-parallel compress of a record sample at 32 KiB."""
-    from oracle import oracle
-    import ctypes
-    lib = oracle.lib()
-    chunks = -(-len(sample) // CHUNK)
-    slot = (CHUNK * 9 + 7) // 8 + 16
-    slots = np.zeros(chunks * slot, dtype=np.uint8)
-    sizes = np.zeros(chunks, dtype=np.uint32)
-    src = np.frombuffer(sample, dtype=np.uint8)
-    per = -(-chunks // threads)
-
-    def encode(first):
-        count = min(per, chunks - first)
-        lib.oracle_compress_chunks(
-            src.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)), len(sample), CHUNK, first, count,
-            slots[first * slot:].ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)), slot,
-            sizes[first:].ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)))
-
-    start = time.perf_counter()
-    _parallel_map(encode, range(0, chunks, per), threads)
-    return time.perf_counter() - start
-
-
-def run_reference_sharded(args, rank, world):
-    if rank != 0:
-        return
-    from oracle import oracle
-    oracle.build()
-    threads = os.cpu_count() or 1
-    if args.workload == "batch":
-        files, streams = batch_inputs()
-        k = 512
-        files, streams = files[:k], streams[:k]
-        unit_bytes = 2 * sum(len(f) for f in files)
-        run = lambda: cpu_batch(files, streams, threads)
-        metric, sample = BATCH_METRIC, ("first 512 of the 4096 config-2 files: serial-route "
-                                        "decode + compress per file, oracle port, one file "
-                                        "per thread")
-    else:
-        data = config3_records(64 * MIB)
-        unit_bytes = data.size
-        run = lambda: cpu_records(data.tobytes(), threads)
-        metric, sample = RECORDS_METRIC, ("64 MiB of config-3 records, chunk-parallel "
-                                          "compress at 32 KiB, oracle port")
-    for _ in range(args.warmup):
-        run()
-    seconds = sum(run() for _ in range(args.steps)) / args.steps
-    value = unit_bytes / seconds / 1e9
-    print(json.dumps({
-        "impl": "reference", "metric": metric, "value": round(value, 4), "unit": "GB/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(seconds * 1e3, 3), "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "u8", "data": "synthetic",
-        "config": {"workload": args.workload},
-        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads,
-                         "kind": "port", "sample": sample},
+        "vs_baseline": None, "dtype": "u8", "data": "synthetic", "config": CONFIG,
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": cores,
+                         "kind": "reference", "sample": sample},
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0}}), flush=True)
 
 
-def _timed_steps(torch, args, step, stream, flush, device, world):
-    """K steps bracketed by barrier + synchronize; returns (seconds, clocks)."""
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    with ClockSampler(device.index) as clocks:
-        for k in range(args.steps):
-            flush.fill_(k & 255)
-            starts[k].record(stream)
-            step()
-            ends[k].record(stream)
+# ------------------------------------------------------------------ GPU timing
+class Timing:
+    """Device-time steps with the library's per-kernel event totals."""
+
+    NAMES = ("serial_inflate_kernel", "discover_kernel", "validate_kernel", "describe_kernel",
+             "symbols_kernel", "expand_kernel", "resolve_kernel", "encode_chunks_kernel",
+             "encode_pack_kernel")
+
+    def __init__(self, torch, lib, device, flush):
+        self.torch, self.lib, self.device, self.flush = torch, lib, device, flush
+        lib.cuda_zlib_b200_profile.argtypes = [ctypes.c_int]
+        lib.cuda_zlib_b200_profile_read.argtypes = [
+            ctypes.c_char_p, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_uint64)]
+        lib.cuda_zlib_b200_launches.restype = ctypes.c_uint64
+
+    def run(self, step, steps, world, clocks=True):
+        """Time `steps` calls of step(); returns (seconds, clock summary,
+        launches, {kernel: (total ms, launches)})."""
+        torch = self.torch
+        stream = torch.cuda.current_stream(self.device)
+        if world > 1:
+            torch.distributed.barrier()
         torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
-    return sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / 1e3, clocks
+        self.lib.cuda_zlib_b200_profile(1)
+        before = self.lib.cuda_zlib_b200_launches()
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        sampler = ClockSampler(self.device.index) if clocks else None
+        if sampler:
+            sampler.__enter__()
+        try:
+            for k in range(steps):
+                self.flush.fill_(k & 255)
+                starts[k].record(stream)
+                step()
+                ends[k].record(stream)
+            torch.cuda.synchronize()
+        finally:
+            if sampler:
+                sampler.__exit__(None, None, None)
+        launched = self.lib.cuda_zlib_b200_launches() - before
+        if world > 1:
+            torch.distributed.barrier()
+        kernels = {}
+        for name in self.NAMES:
+            total, count = ctypes.c_double(), ctypes.c_uint64()
+            self.lib.cuda_zlib_b200_profile_read(name.encode(), ctypes.byref(total),
+                                                 ctypes.byref(count))
+            if count.value:
+                kernels[name] = (total.value, count.value)
+        self.lib.cuda_zlib_b200_profile(0)
+        seconds = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / 1e3
+        return seconds, (sampler.summary() if sampler else None), launched, kernels
 
 
-def _max_over_ranks(torch, value, device, world):
+def max_over_ranks(torch, value, device, world):
     if world > 1:
         t = torch.tensor([value], dtype=torch.float64, device=device)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -643,284 +284,362 @@ def _max_over_ranks(torch, value, device, world):
     return value
 
 
-def _kernel_times(lib, names):
-    import ctypes
-    kernels = {}
-    for name in names:
-        total, launches = ctypes.c_double(), ctypes.c_uint64()
-        lib.cuda_zlib_b200_profile_read(name.encode(), ctypes.byref(total), ctypes.byref(launches))
-        if launches.value:
-            kernels[name] = (total.value, launches.value)
-    return kernels
+DECODE_KERNELS = ("serial_inflate_kernel", "discover_kernel", "validate_kernel",
+                  "describe_kernel", "symbols_kernel", "expand_kernel", "resolve_kernel")
 
 
-def run_gpu_sharded(args, rank, world):
-    import ctypes
-    import torch
-    import cuda_zlib as codec
-    from cuda_zlib import _native, sharding
+def roofline(workload, kernels, steps, decode_bytes, encode_bytes):
+    """Dominant kernel's achieved GB/s: the algorithmic bytes (C + U) of the
+    calls it served per step over its device time per step."""
+    if not kernels:
+        return None
+    name, (total_ms, launches) = max(kernels.items(), key=lambda kv: kv[1][0])
+    served = decode_bytes if name in DECODE_KERNELS else encode_bytes
+    per_step_s = total_ms / steps / 1e3
+    achieved = served / per_step_s / 1e9
+    peak, kind = measured_peak()
+    per_launch = served * steps / launches
+    return {"bound": "hbm", "kernel": name, "achieved": round(achieved, 2), "peak": peak,
+            "peak_kind": kind, "unit": "GB/s", "frac": round(achieved / peak, 5),
+            "traffic": committed_traffic(workload, name),
+            "algorithmic_bytes_per_launch": int(per_launch),
+            "launch_ms": round(total_ms / launches, 4),
+            "share_of_step": None}
 
-    torch.cuda.set_device(rank % torch.cuda.device_count())
-    device = torch.device("cuda", torch.cuda.current_device())
-    codec.compile_kernels(device)
-    stream = torch.cuda.current_stream(device)
-    flush = torch.empty(256 * MIB, dtype=torch.uint8, device=device)
-    lib = _native.library()
-    lib.cuda_zlib_b200_profile.argtypes = [ctypes.c_int]
-    lib.cuda_zlib_b200_profile_read.argtypes = [ctypes.c_char_p, ctypes.POINTER(ctypes.c_double),
-                                                ctypes.POINTER(ctypes.c_uint64)]
-    lib.cuda_zlib_b200_launches.restype = ctypes.c_uint64
 
-    if args.workload == "batch":
-        files, streams = batch_inputs()
-        total_units = 2 * sum(len(f) for f in files)
-        mine = sharding.rank_files([len(f) + len(s) for f, s in zip(files, streams)], rank, world)
-        my_files = [files[i] for i in mine] or [b""]
-        my_streams = [streams[i] for i in mine] or [zlib_stream(b"", 6)]
-        sizes = [len(f) for f in my_files]
-        in_sizes = [len(s) for s in my_streams]
-        packed_raw = b"".join(my_files)
-        packed_z = b"".join(my_streams)
-        raw_dev = torch.frombuffer(bytearray(packed_raw + b"\0"), dtype=torch.uint8)[:len(packed_raw)].to(device)
-        z_dev = torch.frombuffer(bytearray(packed_z), dtype=torch.uint8).to(device)
-
-        def step(raw_in=raw_dev, z_in=z_dev):
-            out, meta = codec.decompress_zlib_batch_checked(z_in, in_sizes, sizes, device)
-            slots, emeta = codec.compress_zlib_batch_padded(raw_in, sizes, device,
-                                                            chunk_bytes=CHUNK)
-            return out, meta, slots, emeta
-
-        def verify(result):
-            out, meta, slots, emeta = result
-            assert not meta.cpu().numpy().any()
-            assert out.cpu().numpy().tobytes() == packed_raw
-            emeta = emeta.cpu().numpy()
-            assert not emeta[:, 1].any()
-            host = slots.cpu().numpy().tobytes()
-            offset = 0
-            for f, (length, _) in zip(my_files, emeta):
-                assert zlib.decompress(host[offset:offset + int(length)]) == f
-                offset += len(f) + 5 * max(1, -(-len(f) // CHUNK)) + 6
-            return float(emeta[:, 0].sum()) / max(1, sum(sizes))
-
-        h2d = len(packed_raw) + len(packed_z)
-        d2h = sum(sizes) + sum(len(f) + 5 * max(1, -(-len(f) // CHUNK)) + 6 for f in my_files)
-        raw_pin = torch.frombuffer(bytearray(packed_raw + b"\0"), dtype=torch.uint8)[:len(packed_raw)].pin_memory()
-        z_pin = torch.frombuffer(bytearray(packed_z), dtype=torch.uint8).pin_memory()
-
-        # End to end, pipelined: the compressed files go in first and decode
-        # while the raw files go in; the decoded files go out while the raw
-        # files compress.
-        copy_in, compute, copy_out = (torch.cuda.Stream(device) for _ in range(3))
-        host_out = torch.empty(sum(sizes), dtype=torch.uint8).pin_memory()
-        host_slots = torch.empty(d2h - sum(sizes), dtype=torch.uint8).pin_memory()
-        host_meta = torch.empty(2 * len(sizes), dtype=torch.int32).pin_memory()
-        host_emeta = torch.empty(2 * len(sizes), dtype=torch.int32).pin_memory()
-
-        def e2e_step():
-            with torch.cuda.stream(copy_in):
-                z_in = z_pin.to(device, non_blocking=True)
-                z_ready = torch.cuda.Event()
-                z_ready.record(copy_in)
-                raw_in = raw_pin.to(device, non_blocking=True)
-                raw_ready = torch.cuda.Event()
-                raw_ready.record(copy_in)
-            with torch.cuda.stream(compute):
-                compute.wait_event(z_ready)
-                out, meta = codec.decompress_zlib_batch_checked(z_in, in_sizes, sizes, device)
-                decoded = torch.cuda.Event()
-                decoded.record(compute)
-                compute.wait_event(raw_ready)
-                slots, emeta = codec.compress_zlib_batch_padded(raw_in, sizes, device,
-                                                                chunk_bytes=CHUNK)
-                encoded = torch.cuda.Event()
-                encoded.record(compute)
-            with torch.cuda.stream(copy_out):
-                copy_out.wait_event(decoded)
-                host_out.copy_(out, non_blocking=True)
-                host_meta.copy_(meta.view(torch.int32).flatten(), non_blocking=True)
-                copy_out.wait_event(encoded)
-                host_slots.copy_(slots, non_blocking=True)
-                host_emeta.copy_(emeta.view(torch.int32).flatten(), non_blocking=True)
-                copy_out.synchronize()
-            assert not host_meta.numpy().any() and not host_emeta.numpy()[1::2].any()
-
-        algorithmic = {"serial_inflate_kernel": len(packed_z) + sum(sizes),
-                       "encode_chunks_kernel": sum(sizes)}
-        names = ("serial_inflate_kernel", "encode_chunks_kernel", "encode_pack_kernel")
-        metric = BATCH_METRIC
-        config = {"workload": "config2: 4096 files (seed 2), log-uniform 256 B-256 KiB, 1% empty; "
-                              "50% Zipf text, 25% random, 25% runs; zlib L6 decode + compress "
-                              "at chunk_bytes=32768",
-                  "files": len(files), "uncompressed_bytes_per_step": total_units,
-                  "parallelism": "files LPT-sharded over %d GPU(s)" % world,
-                  "l2": "flushed between steps (256 MiB write)"}
-    else:
-        data = config3_records()
-        total_units = data.size
-        max_range = ((1 << 28) - 6) * CHUNK // (CHUNK + 5)
-        ranges = sharding.rank_ranges(data.size, CHUNK, rank, world, max_range)
-        lo, hi = ranges[0][0], ranges[-1][1]
-        last_rank = max(r for r in range(world)
-                        if sharding.rank_ranges(data.size, CHUNK, r, world, max_range))
-        mine = torch.from_numpy(data[lo:hi])
-        src_dev = mine.to(device)
-        outs, metas = [], []
-        for start, stop in ranges:
-            n = stop - start
-            cap = n + 5 * max(1, -(-n // CHUNK)) + 6
-            outs.append(torch.empty(cap, dtype=torch.uint8, device=device))
-            metas.append(torch.zeros(3, dtype=torch.uint32, device=device))
-
-        def step(src=src_dev):
-            for k, (start, stop) in enumerate(ranges):
-                last = rank == last_rank and k == len(ranges) - 1
-                piece = src[start - lo:stop - lo]
-                if piece.device.type == "cpu":
-                    piece = piece.to(device)
-                _native.check(lib.cuda_zlib_compress_range(
-                    piece.data_ptr(), stop - start, CHUNK, int(last), outs[k].data_ptr(),
-                    outs[k].numel(), metas[k].data_ptr(), stream.cuda_stream), "range")
-            return outs, metas
-
-        def verify(result):
-            total = 0
-            for (start, stop), out, meta in zip(ranges, *result):
-                length, status, adler = (int(v) for v in meta.cpu())
-                assert status == 0 and adler == zlib.adler32(data[start:stop])
-                body = out[:length].cpu().numpy().tobytes()
-                d = zlib.decompressobj(-15)
-                assert d.decompress(body) == data[start:stop].tobytes()
-                total += length
-            return total / max(1, hi - lo)
-
-        src_pin = mine.pin_memory()
-        # End to end, pipelined over pieces of at most 32 MiB (whole chunks):
-        # a piece goes in on a copy stream, compresses on a compute stream once
-        # it is in, and its body goes out at its exact length as soon as its
-        # metadata says how long it is, while later pieces copy and compress.
-        piece_bytes = 1024 * CHUNK
-        pieces = [(a, min(a + piece_bytes, stop)) for start, stop in ranges
-                  for a in range(start, stop, piece_bytes)] or [(lo, hi)]
-        piece_out = [torch.empty(b - a + 5 * max(1, -(-(b - a) // CHUNK)) + 6, dtype=torch.uint8,
-                                 device=device) for a, b in pieces]
-        piece_meta = [torch.zeros(3, dtype=torch.uint32, device=device) for _ in pieces]
-        host_meta = torch.empty(3 * len(pieces), dtype=torch.int32).pin_memory()
-        host_body = torch.empty(sum(o.numel() for o in piece_out), dtype=torch.uint8).pin_memory()
-        copy_in, compute, copy_out, body_out = (torch.cuda.Stream(device) for _ in range(4))
-        h2d = hi - lo
-        d2h_done = [0]
-
-        def e2e_step():
-            done = []
-            for k, (a, b) in enumerate(pieces):
-                with torch.cuda.stream(copy_in):
-                    piece = src_pin[a - lo:b - lo].to(device, non_blocking=True)
-                    ready = torch.cuda.Event()
-                    ready.record(copy_in)
-                with torch.cuda.stream(compute):
-                    compute.wait_event(ready)
-                    last = rank == last_rank and b == hi
-                    _native.check(lib.cuda_zlib_compress_range(
-                        piece.data_ptr(), b - a, CHUNK, int(last), piece_out[k].data_ptr(),
-                        piece_out[k].numel(), piece_meta[k].data_ptr(), compute.cuda_stream),
-                        "range")
-                    finished = torch.cuda.Event()
-                    finished.record(compute)
-                with torch.cuda.stream(copy_out):
-                    copy_out.wait_event(finished)
-                    host_meta[3 * k:3 * k + 3].copy_(piece_meta[k].view(torch.int32),
-                                                     non_blocking=True)
-                    done.append((piece, torch.cuda.Event()))
-                    done[-1][1].record(copy_out)
-            # Bodies go out on their own stream, each once its piece's
-            # metadata (hence the piece) is done, not behind later pieces.
-            at = 0
-            with torch.cuda.stream(body_out):
-                for k, (piece, meta_in) in enumerate(done):
-                    meta_in.synchronize()
-                    length, status = int(host_meta[3 * k]), int(host_meta[3 * k + 1])
-                    assert status == 0
-                    host_body[at:at + length].copy_(piece_out[k][:length], non_blocking=True)
-                    at += length
-                body_out.synchronize()
-            d2h_done[0] = at + 12 * len(pieces)
-
-        algorithmic = {"encode_chunks_kernel": hi - lo}
-        names = ("encode_chunks_kernel", "encode_pack_kernel")
-        metric = RECORDS_METRIC
-        config = {"workload": "config3: 1 GiB of 64-byte records (seed 3), compressed as "
-                              "chunk-aligned ranges at chunk_bytes=32768 (the 262144 chunk of "
-                              "the config is outside the reference's [256, 65535] bound)",
-                  "uncompressed_bytes_per_step": total_units,
-                  "parallelism": "chunk ranges over %d GPU(s)" % world,
-                  "l2": "inputs larger than L2; also flushed between steps"}
-
-    for _ in range(args.warmup):
-        result = step()
+def wall_steps(torch, step, warmup, steps):
+    """Host wall-clock seconds per step (device synchronized around each)."""
+    for _ in range(warmup):
+        step()
     torch.cuda.synchronize()
-    ratio = verify(result)
-    lib.cuda_zlib_b200_profile(1)
-    launches_before = lib.cuda_zlib_b200_launches()
-    seconds, clocks = _timed_steps(torch, args, step, stream, flush, device, world)
-    launched = lib.cuda_zlib_b200_launches() - launches_before
-    kernels = _kernel_times(lib, names)
-    lib.cuda_zlib_b200_profile(0)
-    seconds = _max_over_ranks(torch, seconds, device, world)
-    per_step = seconds / args.steps
-    value = total_units / per_step / 1e9
-
-    e2e_times = []
-    for k in range(max(args.warmup, 1) + args.steps):
-        flush.fill_(k & 255)
+    times = []
+    for _ in range(steps):
         torch.cuda.synchronize()
         start = time.perf_counter()
-        e2e_step()
+        step()
         torch.cuda.synchronize()
-        if k >= max(args.warmup, 1):
-            e2e_times.append(time.perf_counter() - start)
-    e2e_seconds = _max_over_ranks(torch, sum(e2e_times) / len(e2e_times), device, world)
-    if args.workload != "batch":
-        d2h = d2h_done[0]
-    roofline = None
-    if kernels:
-        name, (total_ms, launches) = max(kernels.items(), key=lambda kv: kv[1][0])
-        per_launch = algorithmic.get(name, 0) / max(1, launches // args.steps)
-        achieved = per_launch / (total_ms / launches / 1e3) / 1e9
-        peak, peak_kind = measured_peak()
-        roofline = {"bound": "hbm", "kernel": name, "achieved": round(achieved, 2),
-                    "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
-                    "frac": round(achieved / peak, 5), "traffic": committed_traffic(name),
-                    "algorithmic_bytes_per_launch": int(per_launch),
-                    "launch_ms": round(total_ms / launches, 4)}
+        times.append(time.perf_counter() - start)
+    return sum(times) / len(times)
+
+
+# ------------------------------------------------------------------ config 4a on the GPU
+def groups_of(count, per):
+    return [(a, min(a + per, count)) for a in range(0, count, per)]
+
+
+def run_gpu(args, rank, world):
+    plan = plan_4a(world)
+    mine = plan[rank]
+    packed, streams = inputs_4a(mine)
+    count = len(mine)
+    cores = os.cpu_count() or 1
+    sample_files = min(count, args.cpu_files)
+    pool = None
+    if world == 1 and not args.no_cpu:
+        pool = cpu_pool(packed, streams, cores)
+
+    import torch
+    import cuda_zlib as codec
+    from cuda_zlib import _native
+
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)) % torch.cuda.device_count())
+    device = torch.device("cuda", torch.cuda.current_device())
+    codec.compile_kernels(device)
+    lib = _native.library()
+    flush = torch.empty(256 * MIB, dtype=torch.uint8, device=device)
+    timing = Timing(torch, lib, device, flush)
+
+    in_sizes = [len(s) for s in streams]
+    z_packed = np.frombuffer(b"".join(streams), dtype=np.uint8)
+    z_offsets = np.concatenate(([0], np.cumsum(in_sizes))).astype(np.int64)
+    raw_dev = torch.from_numpy(packed).to(device)
+    z_dev = torch.from_numpy(z_packed.copy()).to(device)
+    decode_groups = groups_of(count, (1 << 28) // FILE)
+    capacity = FILE + 5 * (FILE // CHUNK) + 6
+    encode_groups = groups_of(count, (1 << 28) // capacity)
+    results = {}
+
+    def step():
+        outs = []
+        for a, b in decode_groups:
+            outs.append(codec.decompress_zlib_batch_checked(
+                z_dev[int(z_offsets[a]):int(z_offsets[b])], in_sizes[a:b], [FILE] * (b - a),
+                device))
+        for a, b in encode_groups:
+            outs.append(codec.compress_zlib_batch_padded(
+                raw_dev[a * FILE:b * FILE], [FILE] * (b - a), device, chunk_bytes=CHUNK))
+        results["last"] = outs
+        return outs
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    # Verify the last warm-up step: decoded files equal the sources; every
+    # encoded stream decodes back to its file with the host's zlib.
+    outs = results["last"]
+    for (a, b), (out, meta) in zip(decode_groups, outs[:len(decode_groups)]):
+        assert not meta.cpu().numpy().any()
+        assert torch.equal(out, raw_dev[a * FILE:b * FILE])
+    encoded = 0
+    for (a, b), (slots, meta) in zip(encode_groups, outs[len(decode_groups):]):
+        meta = meta.cpu().numpy()
+        assert not meta[:, 1].any()
+        host = slots.cpu().numpy()
+        lengths = meta[:, 0].astype(np.int64)
+        encoded += int(lengths.sum())
+        ok = workloads.parallel_map(
+            lambda k: zlib.decompress(host[k * capacity:k * capacity + lengths[k]].tobytes()) ==
+            packed[(a + k) * FILE:(a + k + 1) * FILE].tobytes(), range(b - a))
+        assert all(ok)
+    results.clear()
+
+    seconds, clocks, launched, kernels = timing.run(step, args.steps, world)
+    seconds = max_over_ranks(torch, seconds, device, world)
+    per_step = seconds / args.steps
+    total_units = 2 * FILES * FILE
+    value = total_units / per_step / 1e9
+    my_u = count * FILE
+    line_roofline = roofline("config4a", kernels, args.steps, my_u + int(z_offsets[-1]),
+                             my_u + encoded)
+    if line_roofline:
+        name = line_roofline["kernel"]
+        line_roofline["share_of_step"] = round(kernels[name][0] / args.steps / (per_step * 1e3), 4)
+
+    # End to end through the host-buffer calls, inputs in pinned host memory.
+    e2e = None
+    if not args.no_e2e:
+        raw_pin = torch.from_numpy(packed).pin_memory().numpy()
+        z_pin = torch.from_numpy(z_packed).pin_memory().numpy()
+        z_views = [z_pin[int(z_offsets[k]):int(z_offsets[k + 1])] for k in range(count)]
+        raw_views = [raw_pin[k * FILE:(k + 1) * FILE] for k in range(count)]
+        sizes = [FILE] * count
+        box = {}
+
+        def e2e_step():
+            box["decoded"] = codec.decompress_zlib_batch_host(z_views, sizes, device)
+            box["encoded"] = codec.compress_zlib_batch_host(raw_views, device, chunk_bytes=CHUNK)
+
+        e2e_seconds = wall_steps(torch, e2e_step, 1, args.e2e_steps)
+        assert all(np.array_equal(d, r) for d, r in zip(box["decoded"][:64], raw_views[:64]))
+        assert sum(len(s) for s in box["encoded"]) == encoded
+        e2e_seconds = max_over_ranks(torch, e2e_seconds, device, world)
+        e2e = {"value": round(total_units / e2e_seconds / 1e9, 4), "unit": "GB/s",
+               "h2d_bytes_per_step": int(z_offsets[-1]) + my_u,
+               "d2h_bytes_per_step": my_u + count * capacity + 16 * count,
+               "timer": "host wall clock, slowest rank",
+               "calls": "decompress_zlib_batch_host + compress_zlib_batch_host",
+               "steps": args.e2e_steps}
+
+    configs = None
+    if world == 1 and not args.no_configs:
+        configs = run_configs(args, torch, codec, device, timing)
+
+    cpu = None
+    if pool is not None:
+        cpu_step(pool, min(sample_files, 1024))
+        t = cpu_step(pool, sample_files)
+        pool.close()
+        pool.join()
+        cpu = {"value": round(2 * sample_files * FILE / t / 1e9, 4), "unit": "GB/s",
+               "cores": cores, "kind": "reference",
+               "sample": "first %d of the 65,536 config-4a files: zlib.decompress of their "
+                         "level-6 streams + zlib.compress(level 1), one file per task, "
+                         "multiprocessing pool (fork) of %d processes" % (sample_files, cores)}
     if rank != 0:
         return
-    cpu = None
-    if world == 1 and not args.no_cpu:
-        threads = os.cpu_count() or 1
-        if args.workload == "batch":
-            k = 512
-            t = cpu_batch(files[:k], streams[:k], threads)
-            cpu = {"value": round(2 * sum(len(f) for f in files[:k]) / t / 1e9, 4),
-                   "sample": "first 512 config-2 files, decode + compress per file"}
-        else:
-            sample = data[:64 * MIB].tobytes()
-            t = cpu_records(sample, threads)
-            cpu = {"value": round(len(sample) / t / 1e9, 4),
-                   "sample": "64 MiB of config-3 records, chunk-parallel compress"}
-        cpu.update(unit="GB/s", cores=threads, kind="port")
-    config["compression_ratio_rank0"] = round(ratio, 5)
-    print(json.dumps({
-        "metric": metric, "value": round(value, 4), "unit": "GB/s", "n_gpus": world,
+    line = {
+        "metric": METRIC, "value": round(value, 4), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step * 1e3, 3),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8",
-        "data": "synthetic", "config": config, "roofline": roofline,
+        "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "u8", "data": "synthetic", "config": CONFIG,
+        "compression_ratio_rank0": round(encoded / my_u, 5),
+        "zlib6_ratio_rank0": round(int(z_offsets[-1]) / my_u, 5),
+        "roofline": line_roofline,
         "kernels_ms_per_step": {k: round(v[0] / args.steps, 3) for k, v in kernels.items()},
-        "e2e": {"value": round(total_units / e2e_seconds / 1e9, 4), "unit": "GB/s",
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "timer": "host wall clock"},
-        "cpu_baseline": cpu, "clocks": clocks.summary(), "gpu_launches": launched}), flush=True)
+        "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks, "gpu_launches": launched,
+        "configs": configs,
+    }
+    print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------ configs 0-3, 4b (N = 1)
+def _device_tensor(torch, array, device):
+    return torch.from_numpy(np.ascontiguousarray(array)).to(device)
+
+
+def _pinned(torch, data):
+    array = np.frombuffer(data, dtype=np.uint8) if not isinstance(data, np.ndarray) else data
+    return torch.from_numpy(np.ascontiguousarray(array)).pin_memory().numpy()
+
+
+def measure_config(args, torch, timing, name, step, e2e_step, units, decode_bytes,
+                   encode_bytes, extra):
+    """Device and end-to-end throughput of one configuration's step."""
+    steps, warmup = args.config_steps, args.config_warmup
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    seconds, _, launched, kernels = timing.run(step, steps, 1, clocks=False)
+    per_step = seconds / steps
+    result = {"value": round(units / per_step / 1e9, 4), "unit": "GB/s",
+              "ms_per_step": round(per_step * 1e3, 3), "steps": steps, "warmup": warmup,
+              "uncompressed_bytes_per_step": units, "gpu_launches": launched,
+              "roofline": roofline(name, kernels, steps, decode_bytes, encode_bytes),
+              "kernels_ms_per_step": {k: round(v[0] / steps, 3) for k, v in kernels.items()}}
+    if result["roofline"]:
+        k = result["roofline"]["kernel"]
+        result["roofline"]["share_of_step"] = round(kernels[k][0] / steps / (per_step * 1e3), 4)
+    if e2e_step is not None and not args.no_e2e:
+        e2e_seconds = wall_steps(torch, e2e_step, 1, min(steps, 3))
+        result["e2e"] = {"value": round(units / e2e_seconds / 1e9, 4), "unit": "GB/s",
+                         "timer": "host wall clock"}
+    result.update(extra)
+    return result
+
+
+def run_configs(args, torch, codec, device, timing):
+    """Configs 0, 1, 2, 3 and 4b on this GPU, each verified before timing."""
+    wanted = [c for c in args.configs.split(",") if c]
+    out = {}
+    # CPU-zlib streams of the large configs are made on host threads while
+    # the smaller configs run on the GPU.
+    pending = {}
+    from concurrent.futures import ThreadPoolExecutor
+    background = ThreadPoolExecutor(max_workers=4)
+    if "3" in wanted:
+        records = workloads.config3_records()
+        raw3 = records.tobytes()
+        pending["3l9"] = background.submit(workloads.zlib_stream, raw3, 9)
+        pending["3fixed"] = background.submit(workloads.zlib_stream, raw3, 1, zlib.Z_FIXED)
+    if "4b" in wanted:
+        streams4b = workloads.config4b_streams()
+        for key, raw in streams4b.items():
+            pending["4b" + key] = background.submit(workloads.zlib_stream, raw.tobytes(), 6)
+
+    def single(name, raws, payloads, chunks):
+        """Decode every payload to its raw; compress every (raw, chunk)."""
+        dev_payloads = [(_device_tensor(torch, np.frombuffer(p, dtype=np.uint8), device), n)
+                        for p, n in payloads]
+        dev_raws = [(_device_tensor(torch, r, device), c) for r, c in zip(raws, chunks)]
+
+        def step():
+            res = [codec.decompress_zlib_checked(p, n, device) for p, n in dev_payloads]
+            res += [codec.compress_zlib_padded(r, device, chunk_bytes=c) for r, c in dev_raws]
+            return res
+
+        res = step()
+        torch.cuda.synchronize()
+        lengths = []
+        for (p, n), (o, m) in zip(payloads, res[:len(payloads)]):
+            assert [int(v) for v in m.cpu()] == [0, 0], name
+        for r, (o, m) in zip(raws, res[len(payloads):]):
+            length, status = (int(v) for v in m.cpu())
+            assert status == 0, name
+            assert zlib.decompress(o[:length].cpu().numpy().tobytes()) == r.tobytes(), name
+            lengths.append(length)
+        pin_payloads = [(_pinned(torch, p), n) for p, n in payloads]
+        pin_raws = [(_pinned(torch, r), c) for r, c in zip(raws, chunks)]
+
+        def e2e_step():
+            for p, n in pin_payloads:
+                codec.decompress_zlib_host(p, n, device)
+            for r, c in pin_raws:
+                codec.compress_zlib_host(r, device, chunk_bytes=c)
+
+        units = sum(n for _, n in payloads) + sum(r.size for r in raws)
+        decode_bytes = sum(len(p) + n for p, n in payloads)
+        encode_bytes = sum(r.size for r in raws) + sum(lengths)
+        return step, e2e_step, units, decode_bytes, encode_bytes, lengths
+
+    if "0" in wanted:
+        text = np.frombuffer(workloads.zipf_text(16 * MIB, 0), dtype=np.uint8)
+        l6 = workloads.zlib_stream(text.tobytes(), 6)
+        step, e2e, units, db, eb, lengths = single("config0", [text], [(l6, text.size)], [CHUNK])
+        out["config0"] = measure_config(
+            args, torch, timing, "config0", step, e2e, units, db, eb,
+            {"workload": "16 MiB Zipf text (seed 0): decode its zlib level-6 stream, compress "
+                         "at chunk_bytes=32768",
+             "compression_ratio": round(lengths[0] / text.size, 5),
+             "zlib6_ratio": round(len(l6) / text.size, 5)})
+    if "1" in wanted:
+        samples = np.frombuffer(workloads.config1_float32(), dtype=np.uint8)
+        l1 = workloads.zlib_stream(samples.tobytes(), 1)
+        l6 = workloads.zlib_stream(samples.tobytes(), 6)
+        step, e2e, units, db, eb, lengths = single(
+            "config1", [samples], [(l1, samples.size), (l6, samples.size)], [CHUNK])
+        out["config1"] = measure_config(
+            args, torch, timing, "config1", step, e2e, units, db, eb,
+            {"workload": "64 MiB float32 random walk (seed 1): decode its zlib level-1 and "
+                         "level-6 streams (to pinned host in e2e), compress at 32768",
+             "compression_ratio": round(lengths[0] / samples.size, 5),
+             "zlib1_ratio": round(len(l1) / samples.size, 5),
+             "zlib6_ratio": round(len(l6) / samples.size, 5)})
+    if "2" in wanted:
+        files = workloads.config2_files()
+        streams = workloads.parallel_map(lambda f: workloads.zlib_stream(f, 6), files)
+        sizes, in_sizes = [len(f) for f in files], [len(s) for s in streams]
+        raw_dev = _device_tensor(torch, np.frombuffer(b"".join(files), dtype=np.uint8), device)
+        z_dev = _device_tensor(torch, np.frombuffer(b"".join(streams), dtype=np.uint8), device)
+
+        def step2():
+            return (codec.decompress_zlib_batch_checked(z_dev, in_sizes, sizes, device),
+                    codec.compress_zlib_batch_padded(raw_dev, sizes, device, chunk_bytes=CHUNK))
+
+        (out2, meta2), (slots2, emeta2) = step2()
+        assert not meta2.cpu().numpy().any()
+        assert torch.equal(out2, raw_dev)
+        emeta2 = emeta2.cpu().numpy()
+        assert not emeta2[:, 1].any()
+        z_pin = _pinned(torch, np.frombuffer(b"".join(streams), dtype=np.uint8))
+        r_pin = _pinned(torch, np.frombuffer(b"".join(files), dtype=np.uint8))
+        zo = np.concatenate(([0], np.cumsum(in_sizes)))
+        ro = np.concatenate(([0], np.cumsum(sizes)))
+        z_views = [z_pin[zo[k]:zo[k + 1]] for k in range(len(files))]
+        r_views = [r_pin[ro[k]:ro[k + 1]] for k in range(len(files))]
+
+        def e2e2():
+            codec.decompress_zlib_batch_host(z_views, sizes, device)
+            codec.compress_zlib_batch_host(r_views, device, chunk_bytes=CHUNK)
+
+        total = sum(sizes)
+        out["config2"] = measure_config(
+            args, torch, timing, "config2", step2, e2e2, 2 * total,
+            total + sum(in_sizes), total + int(emeta2[:, 0].sum()),
+            {"workload": "4096 files (seed 2), log-uniform 256 B-256 KiB, 1% empty, config-2 "
+                         "mix: batch decode of their zlib level-6 streams, batch compress at "
+                         "32768",
+             "compression_ratio": round(int(emeta2[:, 0].sum()) / total, 5),
+             "zlib6_ratio": round(sum(in_sizes) / total, 5)})
+    if "3" in wanted:
+        l9, fixed = pending["3l9"].result(), pending["3fixed"].result()
+        step, e2e, units, db, eb, lengths = single(
+            "config3", [records, records], [(l9, records.size), (fixed, records.size)],
+            [CHUNK, 262144])
+        out["config3"] = measure_config(
+            args, torch, timing, "config3", step, e2e, units, db, eb,
+            {"workload": "1 GiB of 64-byte records (seed 3): decode its zlib level-9 and "
+                         "level-1 Z_FIXED streams, compress at 32768 and 262144",
+             "compression_ratio_32768": round(lengths[0] / records.size, 5),
+             "compression_ratio_262144": round(lengths[1] / records.size, 5),
+             "zlib9_ratio": round(len(l9) / records.size, 5),
+             "zlib1_fixed_ratio": round(len(fixed) / records.size, 5)})
+    if "4b" in wanted:
+        keys = ("zeros", "random", "period")
+        raws = [streams4b[k] for k in keys]
+        payloads = [(pending["4b" + k].result(), streams4b[k].size) for k in keys]
+        step, e2e, units, db, eb, lengths = single("config4b", raws, payloads, [65535] * 3)
+        out["config4b"] = measure_config(
+            args, torch, timing, "config4b", step, e2e, units, db, eb,
+            {"workload": "three 256 MiB streams (seed 4): all-zero, uniform random, period-32768 "
+                         "repeats; decode their zlib level-6 streams, compress at 65535",
+             "compression_ratio": {k: round(n / (256 * MIB), 5) for k, n in zip(keys, lengths)},
+             "zlib6_ratio": {k: round(len(p) / (256 * MIB), 5)
+                             for k, (p, _) in zip(keys, payloads)}})
+    background.shutdown()
+    return out
+
+
+# ------------------------------------------------------------------ main
 def main():
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     parser.add_argument("--gpus", type=int, default=1)
@@ -928,33 +647,29 @@ def main():
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    parser.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg")
-    parser.add_argument("--workload", choices=["config1", "batch", "records"], default="config1",
-                        help="config1 (default; replicas at N>1), batch (config 2, files "
-                             "LPT-sharded over ranks) or records (config 3, chunk ranges "
-                             "sharded over ranks)")
-    parser.add_argument("--size-mib", type=int, default=64,
-                        help="leading MiB of the config-1 array (64 = the full workload; "
-                             "smaller sizes are for profiler captures)")
+    parser.add_argument("--no-e2e", action="store_true", help="skip the host-buffer legs")
+    parser.add_argument("--no-configs", action="store_true",
+                        help="skip the per-config sub-results (N = 1)")
+    parser.add_argument("--configs", default="0,1,2,3,4b",
+                        help="configs measured beside the headline at N = 1")
+    parser.add_argument("--e2e-steps", type=int, default=3)
+    parser.add_argument("--config-steps", type=int, default=3)
+    parser.add_argument("--config-warmup", type=int, default=3)
+    parser.add_argument("--cpu-files", type=int, default=8192,
+                        help="config-4a files in the CPU baseline's bounded sample")
     args = parser.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":
-        if args.workload == "config1":
-            run_reference(args, rank, world)
-        else:
-            run_reference_sharded(args, rank, world)
+        run_reference(args, rank, world)
         return
     if world > 1:
         import datetime
         import torch
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
     try:
-        if args.workload == "config1":
-            run_gpu(args, rank, world)
-        else:
-            run_gpu_sharded(args, rank, world)
+        run_gpu(args, rank, world)
     finally:
         if world > 1:
             import torch

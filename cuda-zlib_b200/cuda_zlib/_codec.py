@@ -23,7 +23,7 @@ from concurrent.futures import ThreadPoolExecutor
 
 import numpy as np
 
-from . import _native
+from . import _hostio, _native
 from ._errors import BackendUnavailable, CodecError, UnsupportedStream
 
 _MAX_BYTES = 2**28
@@ -459,30 +459,88 @@ def decompress_zlib_batch(payloads, expected_sizes, device=0):
     return _split_batch(output, expected)
 
 
+def _host_batch_files(inputs, label):
+    """Host views of a batch's files (None when some file is a CUDA tensor),
+    each within the per-file bound; the total is not bounded here."""
+    if not isinstance(inputs, (tuple, list)) or not inputs:
+        raise ValueError(label + " must be a nonempty sequence of files")
+    views = _hostio.host_views(inputs)
+    if views is not None and any(v.size > _MAX_BYTES for v in views):
+        raise ValueError(label + " exceeds size limit (2**28 bytes)")
+    return views
+
+
+def _first_failure(meta, column, operation):
+    """Raise for the first nonzero status of an int32 (files, 2) metadata view."""
+    statuses = meta.reshape(-1, 2)[:, column]
+    bad = np.flatnonzero(statuses)
+    if bad.size:
+        i = int(bad[0])
+        _check_value(int(statuses[i]) & 0xFFFFFFFF, "%s file %d" % (operation, i))
+
+
 def compress_zlib_batch_host(inputs, device=0, *, chunk_bytes=32768):
-    """Return a tuple of bytes streams, using one packed output transfer."""
+    """Return a tuple of bytes streams, one per file, through pinned memory.
+
+    Host files go through in pipelined groups (staging, copy in, encode, copy
+    out overlap; see _hostio), so the batch may exceed one device call's
+    2**28-byte totals; each file keeps the per-file bounds.  Files given as
+    CUDA tensors take one device call.
+    """
+    views = _host_batch_files(inputs, "inputs")
+    if views is None:
+        selected = _select_device(device)
+        packed, sizes = _pack_batch(inputs, selected)
+        capacities = _batch_capacities(sizes, chunk_bytes)
+        output, metadata = compress_zlib_batch_padded(packed, sizes, selected,
+                                                      chunk_bytes=chunk_bytes)
+        lengths = _check_batch(metadata, "CUDA batch compression", True)[:, 0]
+        host = _to_pinned_host(output)
+        return tuple(view.tobytes() for view in _split_batch(host, capacities, lengths))
+    _check_chunk(chunk_bytes)
+    layouts = [_layout(v.size, chunk_bytes) for v in views]
+    if any(blocks > _MAX_BLOCKS or chunks > _MAX_BLOCKS for _, chunks, blocks in layouts):
+        raise ValueError("batch chunk count exceeds workspace limit")
+    capacities = [capacity for capacity, _, _ in layouts]
     selected = _select_device(device)
-    packed, sizes = _pack_batch(inputs, selected)
-    capacities = _batch_capacities(sizes, chunk_bytes)
-    output, metadata = compress_zlib_batch_padded(packed, sizes, selected, chunk_bytes=chunk_bytes)
-    lengths = _check_batch(metadata, "CUDA batch compression", True)[:, 0]
-    host = _to_pinned_host(output)
-    return tuple(view.tobytes() for view in _split_batch(host, capacities, lengths))
+    host, meta, offsets = _hostio.encode(views, capacities, [c for _, c, _ in layouts],
+                                         chunk_bytes, selected, _torch(),
+                                         (_MAX_BLOCKS, _MAX_BYTES, _MAX_BYTES))
+    _first_failure(meta, 1, "CUDA batch compression")
+    array = host.numpy()
+    lengths = meta.reshape(-1, 2)[:, 0].astype(np.int64) & 0xFFFFFFFF
+    return tuple(array[offsets[i]:offsets[i] + int(lengths[i])].tobytes()
+                 for i in range(len(views)))
 
 
 def decompress_zlib_batch_host(payloads, expected_sizes, device=0):
-    """Return read-only NumPy views backed by one packed pinned-host transfer.
+    """Return read-only NumPy views into one pinned host buffer.
 
-    Every stream is decoded and checked independently on CUDA.
+    Every stream is decoded and checked independently on CUDA.  Host
+    payloads go through in pipelined groups (staging, copy in, decode, copy
+    out overlap; see _hostio), so the batch may exceed one device call's
+    2**28-byte totals; each file keeps the per-file bounds.  Payloads given
+    as CUDA tensors take one device call.
     """
-    selected = _select_device(device)
-    packed, sizes = _pack_batch(payloads, selected)
-    expected = _batch_sizes(expected_sizes, "expected_sizes")
-    if len(sizes) != len(expected):
+    views = _host_batch_files(payloads, "payloads")
+    if not isinstance(expected_sizes, (tuple, list)) or any(
+            type(n) is not int or not 0 <= n <= _MAX_BYTES for n in expected_sizes):
+        raise ValueError("expected_sizes must contain integers in [0, 2**28]")
+    expected = tuple(expected_sizes)
+    if len(payloads) != len(expected):
         raise ValueError("input_sizes and expected_sizes must have matching lengths")
-    output, metadata = decompress_zlib_batch_checked(packed, sizes, expected, selected)
-    _check_batch(metadata, "CUDA batch decompression")
-    return _split_batch(_to_pinned_host(output), expected)
+    selected = _select_device(device)
+    if views is None:
+        packed, sizes = _pack_batch(payloads, selected)
+        output, metadata = decompress_zlib_batch_checked(packed, sizes, expected, selected)
+        _check_batch(metadata, "CUDA batch decompression")
+        return _split_batch(_to_pinned_host(output), expected)
+    host, meta = _hostio.decode(views, list(expected), selected, _torch(),
+                                (_MAX_BLOCKS, _MAX_BYTES, _MAX_BYTES))
+    _first_failure(meta, 0, "CUDA batch decompression")
+    array = host.numpy()
+    array.flags.writeable = False
+    return _split_batch(array, expected)
 
 
 def decompress_zlib_checked(payload, expected_bytes, device=0, *,
