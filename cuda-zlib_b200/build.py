@@ -6,7 +6,10 @@
 Output: cuda-zlib_b200/cuda_zlib/libcuda_zlib_b200.so, with the CUDA runtime
 linked statically so it shares the driver's primary context with PyTorch (or
 any other runtime) without depending on a particular libcudart version.
-Objects go to cuda-zlib_b200/_build/.
+Objects go to cuda-zlib_b200/_build/.  Also builds
+cuda-zlib_b200/cuda_zlib/libcuda_zlib_xla.so, the four XLA FFI handlers over
+that C ABI (ffi/cuda_zlib_xla.cc), against jaxlib's FFI header when jax is
+installed and against the stand-in header in ffi/standin otherwise.
 """
 import concurrent.futures
 import os
@@ -18,6 +21,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIBRARY = os.path.join(HERE, "cuda_zlib", "libcuda_zlib_b200.so")
+FFI = os.path.join(HERE, "ffi")
+XLA_LIBRARY = os.path.join(HERE, "cuda_zlib", "libcuda_zlib_xla.so")
 SOURCES = ["codec.cu", "deflate.cu", "inflate_serial.cu", "inflate_general.cu",
            "inflate_parallel.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -73,7 +78,38 @@ def build(force=False, verbose=False):
     if force or jobs or _stale(LIBRARY, objects):
         run([nvcc, *ARCH, "-shared", "-cudart", "static", "-o", LIBRARY, *objects,
              "-Xlinker", "--no-undefined", "-lrt", "-ldl", "-lpthread"])
+    build_xla(force)
     return LIBRARY
+
+
+def xla_include():
+    """(include dir of xla/ffi/api/ffi.h, "jaxlib" | "stand-in")."""
+    try:
+        import jax.ffi
+        return jax.ffi.include_dir(), "jaxlib"
+    except Exception:  # jax is not installed: the stand-in declarations
+        return os.path.join(FFI, "standin"), "stand-in"
+
+
+def build_xla(force=False):
+    """The XLA FFI handler library (ffi/cuda_zlib_xla.cc) over the C ABI."""
+    include, _ = xla_include()
+    source = os.path.join(FFI, "cuda_zlib_xla.cc")
+    headers = [os.path.join(include, "xla", "ffi", "api", "ffi.h"),
+               os.path.join(os.path.dirname(HERE), "include", "cuda_zlib_b200.h"), LIBRARY]
+    if not force and not _stale(XLA_LIBRARY, [source] + [h for h in headers if os.path.exists(h)]):
+        return XLA_LIBRARY
+    cuda = os.path.dirname(os.path.dirname(_nvcc()))
+    command = [os.environ.get("CXX", "g++"), "-std=c++17", "-O2", "-fPIC", "-shared", "-Wall",
+               "-I" + include, "-I" + os.path.join(os.path.dirname(HERE), "include"),
+               "-I" + os.path.join(cuda, "include"), source, "-o", XLA_LIBRARY,
+               "-L" + os.path.dirname(LIBRARY), "-l:" + os.path.basename(LIBRARY),
+               "-Wl,-rpath,$ORIGIN", "-Wl,--no-undefined"]
+    result = subprocess.run(command, capture_output=True, text=True)
+    if result.returncode:
+        raise RuntimeError("XLA FFI handler build failed:\n" + " ".join(command) + "\n" +
+                           result.stderr)
+    return XLA_LIBRARY
 
 
 if __name__ == "__main__":

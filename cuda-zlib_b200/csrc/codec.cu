@@ -324,7 +324,9 @@ cudaError_t encode_files(const DeviceState& dev, const u8* in, u64 in_bytes,
   CZ_TRY(ws.allocate(&status, total_chunks));
   CZ_TRY(ws.allocate(&adler, 2 * u64(total_chunks)));
   CZ_TRY(ws.allocate(&offsets, total_chunks));
-  if (!encode_in_smem(chunk_bytes, dev.info)) {
+  {
+    // Pooled calls always use the global spill: with the per-position arrays
+    // there, two encoder CTAs fit an SM's shared memory instead of one.
     const u64 entries = encode_spill_entries(in_bytes, total_chunks);
     u8* prev = nullptr;
     CZ_TRY(ws.allocate(&prev, entries * (chunk_bytes >= kLargeChunk ? 4 : 2)));

@@ -1075,7 +1075,10 @@ cudaError_t launch_encode(const u8* in, const EncodeFile* files, u32 nfiles, u32
                           u32 total_chunks, u8* slots, u32* sizes, u32* status, u64* adler,
                           u64* offsets, const EncodeSpill& spill, u8* out, u32* meta,
                           const DeviceInfo& dev, cudaStream_t stream, u32* range_adler) {
-  const bool in_smem = encode_in_smem(chunk_bytes, dev);
+  // Without spill buffers (the allocation-free entry point) the per-position
+  // arrays stay in shared memory.
+  const bool in_smem = spill.prev == nullptr;
+  if (in_smem && !encode_in_smem(chunk_bytes, dev)) return cudaErrorInvalidValue;
   const size_t smem = encode_smem_bytes(chunk_bytes, in_smem);
   profile_begin("encode_chunks_kernel", stream);
   note_launch();

@@ -60,10 +60,11 @@ cudaError_t launch_serial_inflate(const u8* in, u8* out, const StreamDesc* descs
 
 // Chunk encoder + device-side finish.  Slots: in_bytes + 96 * (chunks + 2)
 // bytes; `sizes`, `status` per chunk; `adler` 2 u64 per chunk; `offsets` 1 u64
-// per chunk.  When encode_in_smem() is false the per-position arrays live in
+// per chunk.  With a spill (spill.prev set) the per-position arrays live in
 // the global spill: `prev` (u16 entries, u32 for chunks above 65535 bytes)
 // and `len` (u8), and for chunks above 65535 bytes also `data` (u8), each
-// encode_spill_entries() entries.  `out` must be zeroed; `meta` receives
+// encode_spill_entries() entries; without one they stay in shared memory,
+// which encode_in_smem() says the chunk fits.  `out` must be zeroed; `meta` receives
 // [encoded_length, status] per file, and `range_adler` (optional) the
 // Adler-32 of each file's input bytes.
 struct EncodeSpill {
