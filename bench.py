@@ -13,10 +13,12 @@ bounds (4096 and 4095 files of 64 KiB).  One step = every rank's share:
   value    uncompressed GB/s (1e9 B/s), whole job: 2 x 4 GiB / the slowest
            rank's device time (CUDA events on the codec's stream), inputs
            resident in HBM and larger than L2 (L2 also flushed per step);
-  e2e      the same step through the host-buffer calls
-           (decompress_zlib_batch_host, compress_zlib_batch_host) from inputs
-           in pinned host memory to results in host memory, copies inside the
-           timed region (host wall clock, slowest rank);
+  e2e      the same step through the host-buffer counterparts of those calls
+           (decompress_zlib_batch_checked_host, compress_zlib_batch_padded_host:
+           same packed layouts and metadata, copies pipelined with the
+           kernels) from inputs in pinned host memory to results in pinned
+           host memory, copies inside the timed region (host wall clock,
+           slowest rank);
   roofline the dominant kernel's algorithmic bytes (C + U of the calls it
            served) over its event-timed device time, against the measured
            HBM copy bandwidth (MEASURED_PEAKS.json);
@@ -405,29 +407,32 @@ def run_gpu(args, rank, world):
         name = line_roofline["kernel"]
         line_roofline["share_of_step"] = round(kernels[name][0] / args.steps / (per_step * 1e3), 4)
 
-    # End to end through the host-buffer calls, inputs in pinned host memory.
+    # End to end through the host-buffer counterparts of the two packed
+    # calls, inputs in pinned host memory, results in pinned host memory.
     e2e = None
     if not args.no_e2e:
         raw_pin = torch.from_numpy(packed).pin_memory().numpy()
-        z_pin = torch.from_numpy(z_packed).pin_memory().numpy()
-        z_views = [z_pin[int(z_offsets[k]):int(z_offsets[k + 1])] for k in range(count)]
-        raw_views = [raw_pin[k * FILE:(k + 1) * FILE] for k in range(count)]
-        sizes = [FILE] * count
+        z_pin = torch.from_numpy(z_packed.copy()).pin_memory().numpy()
+        sizes = np.full(count, FILE, dtype=np.int64)
+        z_sizes = np.asarray(in_sizes, dtype=np.int64)
         box = {}
 
         def e2e_step():
-            box["decoded"] = codec.decompress_zlib_batch_host(z_views, sizes, device)
-            box["encoded"] = codec.compress_zlib_batch_host(raw_views, device, chunk_bytes=CHUNK)
+            out, meta = codec.decompress_zlib_batch_checked_host(z_pin, z_sizes, sizes, device)
+            slots, emeta = codec.compress_zlib_batch_padded_host(raw_pin, sizes, device,
+                                                                 chunk_bytes=CHUNK)
+            assert not meta.any() and not emeta[:, 1].any()
+            box["result"] = (out, slots, emeta)
 
         e2e_seconds = wall_steps(torch, e2e_step, 1, args.e2e_steps)
-        assert all(np.array_equal(d, r) for d, r in zip(box["decoded"][:64], raw_views[:64]))
-        assert sum(len(s) for s in box["encoded"]) == encoded
+        out, slots, emeta = box["result"]
+        assert np.array_equal(out, packed) and int(emeta[:, 0].sum()) == encoded
         e2e_seconds = max_over_ranks(torch, e2e_seconds, device, world)
         e2e = {"value": round(total_units / e2e_seconds / 1e9, 4), "unit": "GB/s",
                "h2d_bytes_per_step": int(z_offsets[-1]) + my_u,
                "d2h_bytes_per_step": my_u + count * capacity + 16 * count,
                "timer": "host wall clock, slowest rank",
-               "calls": "decompress_zlib_batch_host + compress_zlib_batch_host",
+               "calls": "decompress_zlib_batch_checked_host + compress_zlib_batch_padded_host",
                "steps": args.e2e_steps}
 
     configs = None

@@ -84,6 +84,11 @@ __device__ __forceinline__ u32 fixed_ll_code(u32 s) {  // bit-reversed, ready to
 __device__ __forceinline__ u32 extent_of(u32 bits, bool final) {
   return final ? (bits + 7) / 8 : (bits + 3 + 7) / 8 + 4;
 }
+// Words of a chunk's member and match bitmaps, padded to 16 bytes so that the
+// arrays after them (hash table, candidates) start 16-byte aligned.
+__host__ __device__ __forceinline__ u32 bitmap_words(u32 chunk_bytes) {
+  return ((chunk_bytes + 31) / 32 + 1 + 3) & ~3u;
+}
 // Stored blocks of an n-byte chunk's stored fallback (kStoredMax each).
 __host__ __device__ __forceinline__ u32 stored_blocks(u32 n) {
   return n ? (n + kStoredMax - 1) / kStoredMax : 1u;
@@ -115,7 +120,7 @@ struct EncodeShared {
   u64 adler_s2[kEncWarps];
   u32 extra_bits, token_count, dist_tokens;
   u32 mode, extent, status, ok, nll, ndist, ncl, rle_size, header_bits, leaves, only;
-  u32 first_fail, more, lcount[16];
+  u32 more, lcount[16];
 };
 
 // Two-queue Huffman build with the reference's (weight, id) order and
@@ -357,7 +362,7 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
   // Shared layout: data | member bits | match bits | hash table | prev | len
   // (large chunks: member bits | match bits | hash table).
   const u32 data_bytes = (chunk_bytes + 16 + 15) & ~15u;
-  const u32 bit_words = (chunk_bytes + 31) / 32 + 1;
+  const u32 bit_words = bitmap_words(chunk_bytes);
   const u64 spill_at = spill_offset(f.in_offset + start, g);
   u8* data = kLarge ? spill.data + spill_at : smem;
   u32* member = reinterpret_cast<u32*>(kLarge ? smem : smem + data_bytes);
@@ -374,9 +379,14 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
     lenv = spill.len + spill_at;
   }
 
-  // 1. Stage the chunk (zero padded) and its Adler-32 partial sums.
+  // 1. Stage the chunk (zero padded) and its Adler-32 partial sums.  Reads
+  // never go past byte n + 7 (hashing reads the word after a position's
+  // own); a spilled chunk pads only to n + 16, the end of its own slice's
+  // guaranteed room (a chunk shorter than chunk_bytes is followed closely by
+  // the next file's slice).
   u64 s1 = 0, s2 = 0;
-  for (u32 i = tid; i < data_bytes; i += kEncThreads) {
+  const u32 stage_bytes = kLarge ? min_u32(data_bytes, (n + 16 + 15) & ~15u) : data_bytes;
+  for (u32 i = tid; i < stage_bytes; i += kEncThreads) {
     const u32 x = i < n ? u32(src[i]) : 0u;
     data[i] = u8(x);
     s1 += x;
@@ -497,9 +507,29 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
 
   // 3. Speculative greedy walks, one segment per thread.
   const u32 seg = (n + kEncThreads - 1) / kEncThreads;
+  // Candidates through a register window of the 16 bytes of `prev` around
+  // a position: walks move forward through their segment, so one load
+  // serves 8 (u16) or 4 (u32) positions instead of one dependent load each.
+  // `prev` is 16-byte aligned in every layout.
+  constexpr u32 kPerWindow = 16 / sizeof(Pos);
+  u32 window_base = ~0u;
+  uint4 window = make_uint4(0, 0, 0, 0);
+  auto candidate_of = [&](u32 p) -> u32 {
+    const u32 base = p & ~(kPerWindow - 1);
+    if (base != window_base) {
+      window_base = base;
+      window = *reinterpret_cast<const uint4*>(prev + base);
+    }
+    const u32 k = p - base;
+    if (kPerWindow == 8) {
+      const u32 word = k < 4 ? (k < 2 ? window.x : window.y) : (k < 6 ? window.z : window.w);
+      return (k & 1) ? word >> 16 : word & 0xffffu;
+    }
+    return k < 2 ? (k == 0 ? window.x : window.y) : (k == 2 ? window.z : window.w);
+  };
   auto token_at = [&](u32 p) -> u32 {  // match length at p, or 0 for a literal
     if (p >= hashed) return 0;
-    const u32 c = prev[p];
+    const u32 c = candidate_of(p);
     if (!c) return 0;
     const u32 q = c - 1, dist = p - q;
     if (dist > 32768u || data[q] != data[p] || data[q + 1] != data[p + 1] ||
@@ -529,13 +559,17 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
   __syncthreads();
 
   // 4. Stitch.  The true entry of a segment is the first token boundary at
-  // or after its start on the chain from position 0.  A re-walk from a wrong
-  // start meets the true chain within a token or two, so assume every
-  // segment's re-walk merges into its speculative chain: then each entry
-  // follows from the speculative exits alone (thread 0, a scan of 256
-  // values), every segment checks its assumption in parallel, and segments
-  // before the first failed check apply their re-walk in parallel.  From the
-  // first failure on, segments are stitched in order as a fallback.
+  // or after its start on the chain from position 0.  A walk from a wrong
+  // start usually lands on the segment's speculative chain within a token or
+  // two, and from there follows it to the speculative exit.  So the entries
+  // are found in parallel rounds: every segment whose entry changed walks
+  // from it until it lands on one of its speculative token starts (its exit
+  // is then the speculative exit) or passes its end (its exit is where the
+  // walk stopped); then each entry becomes the previous segment's exit.
+  // Round r makes the first r segments exact; the rounds stop when no entry
+  // changes, normally after two (data whose chains take longer to re-join,
+  // such as long byte runs, take a few more), and every segment applies its
+  // re-walk in parallel.
   auto is_member = [&](u32 p) { return ((member[p >> 5] >> (p & 31)) & 1u) != 0; };
   auto clear_members = [&](u32 from, u32 to) {  // member bits of [from, to)
     while (from < to) {
@@ -547,33 +581,31 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
     }
   };
   const u32 nseg = seg ? (n + seg - 1) / seg : 0;
-  if (tid == 0) {
-    u32 exit = nseg ? s.seg_exit[0] : 0;
-    for (u32 t = 1; t < nseg; ++t) {
-      s.seg_entry[t] = exit;
-      const u32 b_t = min_u32((t + 1) * seg, n);
-      if (exit < b_t) exit = s.seg_exit[t];
-    }
-    s.first_fail = nseg;
-  }
-  __syncthreads();
   const u32 my_a = min_u32(tid * seg, n), my_b = min_u32(my_a + seg, n);
-  u32 merge_at = my_b;
-  if (tid > 0 && tid < nseg) {
-    const u32 entry = s.seg_entry[tid];
-    if (entry < my_b) {
-      u32 p = entry;
-      while (p < my_b && !is_member(p)) {
-        const u32 m = token_at(p);
-        p += m ? m : 1u;
+  const bool mine = tid < nseg;
+  u32 entry = mine && tid ? s.seg_exit[tid - 1] : 0u, merge_at = my_b;
+  for (bool dirty = true;;) {
+    if (mine && dirty) {
+      u32 exit = entry;  // an earlier token covers the whole segment
+      merge_at = my_b;
+      if (entry < my_b) {
+        u32 p = entry;
+        while (p < my_b && !is_member(p)) {
+          const u32 m = token_at(p);
+          p += m ? m : 1u;
+        }
+        merge_at = p;
+        exit = p < my_b ? s.seg_exit[tid] : p;
       }
-      merge_at = p;
-      if (p >= my_b) atomicMin(&s.first_fail, tid);
+      s.seg_entry[tid] = exit;  // this round's exit
     }
+    __syncthreads();
+    const u32 next = mine && tid ? s.seg_entry[tid - 1] : 0u;
+    dirty = mine && next != entry;
+    entry = next;
+    if (!__syncthreads_or(dirty)) break;
   }
-  __syncthreads();
-  if (tid > 0 && tid < s.first_fail) {
-    const u32 entry = s.seg_entry[tid];
+  if (mine && tid > 0) {
     if (entry >= my_b) {
       clear_members(my_a, my_b);  // one earlier token covers the segment
     } else {
@@ -591,34 +623,6 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
           ++p;
         }
       }
-    }
-  }
-  __syncthreads();
-  if (tid == 0 && s.first_fail < nseg) {
-    const u32 f = s.first_fail;
-    u32 entry = s.seg_entry[f];
-    for (u32 t = f; t < nseg; ++t) {
-      const u32 a = t * seg, b = min_u32(a + seg, n);
-      if (entry >= b) {
-        clear_members(a, b);
-        continue;
-      }
-      clear_members(a, entry);
-      u32 p = entry;
-      while (p < b && !is_member(p)) {
-        const u32 m = token_at(p);
-        member[p >> 5] |= 1u << (p & 31);
-        if (m) {
-          ismatch[p >> 5] |= 1u << (p & 31);
-          lenv[p] = u8(m - 3);
-          clear_members(p + 1, min_u32(p + m, b));
-          p += m;
-        } else {
-          ismatch[p >> 5] &= ~(1u << (p & 31));
-          ++p;
-        }
-      }
-      entry = p < b ? s.seg_exit[t] : p;
     }
   }
   __syncthreads();
@@ -1045,7 +1049,7 @@ __global__ void encode_pack_kernel(const EncodeFile* files, u32 nfiles, const u8
 
 size_t encode_smem_bytes(u32 chunk_bytes, bool in_smem) {
   const size_t data_bytes = (chunk_bytes + 16 + 15) & ~15u;
-  const size_t bit_words = (chunk_bytes + 31) / 32 + 1;
+  const size_t bit_words = bitmap_words(chunk_bytes);
   if (chunk_bytes >= kLargeChunk)  // bitmaps and a table of u32 positions
     return (2 * bit_words * 4 + kHashSlots * 4 + 15) & ~size_t(15);
   size_t bytes = data_bytes + 2 * bit_words * 4 + kHashSlots * 2;

@@ -10,6 +10,7 @@ kernels through libcuda_zlib_b200.so; there is no CPU codec fallback.
 from ._codec import (compress_zlib, compress_zlib_host, decompress_zlib, compile_kernels,
                      compress_zlib_padded, decompress_zlib_checked,
                      decompress_zlib_host, workspace_pool_stats, trim_workspace_pool)
+from ._codec import (compress_zlib_batch_padded_host, decompress_zlib_batch_checked_host)
 from ._codec import (compress_zlib_batch_padded, decompress_zlib_batch_checked,
                      compress_zlib_batch, decompress_zlib_batch,
                      compress_zlib_batch_host, decompress_zlib_batch_host)
@@ -21,5 +22,6 @@ __all__ = ["compress_zlib", "compress_zlib_host", "decompress_zlib", "compile_ke
            "compress_zlib_batch_padded", "decompress_zlib_batch_checked",
            "compress_zlib_batch", "decompress_zlib_batch",
            "compress_zlib_batch_host", "decompress_zlib_batch_host",
+           "compress_zlib_batch_padded_host", "decompress_zlib_batch_checked_host",
            "BackendUnavailable", "CodecError", "UnsupportedStream"]
 __version__ = "0.1.0"

@@ -459,35 +459,125 @@ def decompress_zlib_batch(payloads, expected_sizes, device=0):
     return _split_batch(output, expected)
 
 
-def _host_batch_files(inputs, label):
-    """Host views of a batch's files (None when some file is a CUDA tensor),
-    each within the per-file bound; the total is not bounded here."""
-    if not isinstance(inputs, (tuple, list)) or not inputs:
-        raise ValueError(label + " must be a nonempty sequence of files")
-    views = _hostio.host_views(inputs)
-    if views is not None and any(v.size > _MAX_BYTES for v in views):
-        raise ValueError(label + " exceeds size limit (2**28 bytes)")
-    return views
+def _host_sizes(sizes, label):
+    """Per-file sizes of a host batch call as int64 (each in [0, 2**28]; the
+    total is not bounded: the call splits into device calls)."""
+    if isinstance(sizes, np.ndarray):
+        if sizes.ndim != 1 or sizes.dtype.kind not in "iu":
+            raise ValueError(label + " must contain integers in [0, 2**28]")
+        values = sizes.astype(np.int64)
+    elif isinstance(sizes, (tuple, list)) and all(type(v) is int for v in sizes):
+        values = np.array(sizes, dtype=np.int64) if sizes else np.empty(0, np.int64)
+    else:
+        raise ValueError(label + " must contain integers in [0, 2**28]")
+    if values.size and (values.min() < 0 or values.max() > _MAX_BYTES):
+        raise ValueError(label + " must contain integers in [0, 2**28]")
+    if not 1 <= values.size:
+        raise ValueError(label + " must contain at least one size")
+    return values
+
+
+def _host_packed(data, sizes, label):
+    packed = _hostio.as_host_array(data)
+    if packed is None:
+        raise ValueError(label + " must be in host memory")
+    if packed.size != int(sizes.sum()):
+        raise ValueError("packed input length differs from input_sizes total")
+    return packed
+
+
+_HOST_LIMITS = (_MAX_BLOCKS, _MAX_BYTES, _MAX_BYTES)
+
+
+def decompress_zlib_batch_checked_host(payload, input_sizes, expected_sizes, device=0):
+    """Host-buffer counterpart of decompress_zlib_batch_checked.
+
+    Packed streams in host memory (bytes, NumPy uint8 or a CPU tensor; page-
+    locked memory is copied in directly) -> ``(output, metadata)``: the packed
+    outputs and (files, 2) uint32 [status, 0], read-only NumPy arrays in
+    pinned memory.  The files go through in pipelined groups (see _hostio),
+    so the batch may exceed one device call's 2**28-byte totals; each file
+    keeps the per-file bounds.  Statuses are returned, not raised.
+    """
+    sizes = _host_sizes(input_sizes, "input_sizes")
+    expected = _host_sizes(expected_sizes, "expected_sizes")
+    if sizes.size != expected.size:
+        raise ValueError("input_sizes and expected_sizes must have matching lengths")
+    packed = _host_packed(payload, sizes, "compressed payload")
+    selected = _select_device(device)
+    host, meta = _hostio.decode(_torch(), selected, packed, sizes, expected, _HOST_LIMITS)
+    output = host.numpy()[:int(expected.sum())]
+    output.flags.writeable = False
+    meta = meta.view(np.uint32)
+    meta.flags.writeable = False
+    return output, meta
+
+
+def compress_zlib_batch_padded_host(data, input_sizes, device=0, *, chunk_bytes=32768):
+    """Host-buffer counterpart of compress_zlib_batch_padded.
+
+    Packed files in host memory -> ``(slots, metadata)``: consecutive padded
+    slots (the same layout as the device call's) and (files, 2) uint32
+    [encoded_length, status], read-only NumPy arrays in pinned memory.
+    Pipelined in groups like decompress_zlib_batch_checked_host; statuses
+    are returned, not raised.
+    """
+    sizes = _host_sizes(input_sizes, "input_sizes")
+    _check_chunk(chunk_bytes)
+    packed = _host_packed(data, sizes, "input")
+    capacities, chunks, blocks = _host_layouts(sizes, chunk_bytes)
+    selected = _select_device(device)
+    host, meta = _hostio.encode(_torch(), selected, packed, sizes, capacities, chunks,
+                                chunk_bytes, _HOST_LIMITS)
+    slots = host.numpy()[:int(capacities.sum())]
+    slots.flags.writeable = False
+    meta = meta.view(np.uint32)
+    meta.flags.writeable = False
+    return slots, meta
+
+
+def _host_layouts(sizes, chunk_bytes):
+    """Vectorised _layout: (capacities, chunks, blocks) per file."""
+    chunks = np.maximum(1, -(-sizes // chunk_bytes))
+    full = max(1, -(-chunk_bytes // _STORED_MAX))
+    tail = np.maximum(1, -(-(sizes - (chunks - 1) * chunk_bytes) // _STORED_MAX))
+    stored = (chunks - 1) * full + tail
+    blocks = (chunks - 1) * max(full, 2) + tail
+    if blocks.max() > _MAX_BLOCKS or chunks.max() > _MAX_BLOCKS:
+        raise ValueError("batch chunk count exceeds workspace limit")
+    return sizes + 5 * stored + 6, chunks, blocks
 
 
 def _first_failure(meta, column, operation):
-    """Raise for the first nonzero status of an int32 (files, 2) metadata view."""
-    statuses = meta.reshape(-1, 2)[:, column]
+    """Raise for the first nonzero status of a (files, 2) metadata array."""
+    statuses = meta[:, column]
     bad = np.flatnonzero(statuses)
     if bad.size:
         i = int(bad[0])
-        _check_value(int(statuses[i]) & 0xFFFFFFFF, "%s file %d" % (operation, i))
+        _check_value(int(statuses[i]), "%s file %d" % (operation, i))
+
+
+def _host_files(inputs, label):
+    """Host views of a batch's files, or None when some file is a CUDA tensor."""
+    if not isinstance(inputs, (tuple, list)) or not inputs:
+        raise ValueError(label + " must be a nonempty sequence of files")
+    views = []
+    for item in inputs:
+        view = _hostio.as_host_array(item)
+        if view is None:
+            return None
+        views.append(view)
+    return views
 
 
 def compress_zlib_batch_host(inputs, device=0, *, chunk_bytes=32768):
     """Return a tuple of bytes streams, one per file, through pinned memory.
 
-    Host files go through in pipelined groups (staging, copy in, encode, copy
-    out overlap; see _hostio), so the batch may exceed one device call's
-    2**28-byte totals; each file keeps the per-file bounds.  Files given as
-    CUDA tensors take one device call.
+    Host files go through compress_zlib_batch_padded_host (pipelined groups;
+    the batch may exceed one device call's 2**28-byte totals, each file keeps
+    the per-file bounds).  Files given as CUDA tensors take one device call.
     """
-    views = _host_batch_files(inputs, "inputs")
+    views = _host_files(inputs, "inputs")
     if views is None:
         selected = _select_device(device)
         packed, sizes = _pack_batch(inputs, selected)
@@ -497,50 +587,44 @@ def compress_zlib_batch_host(inputs, device=0, *, chunk_bytes=32768):
         lengths = _check_batch(metadata, "CUDA batch compression", True)[:, 0]
         host = _to_pinned_host(output)
         return tuple(view.tobytes() for view in _split_batch(host, capacities, lengths))
-    _check_chunk(chunk_bytes)
-    layouts = [_layout(v.size, chunk_bytes) for v in views]
-    if any(blocks > _MAX_BLOCKS or chunks > _MAX_BLOCKS for _, chunks, blocks in layouts):
-        raise ValueError("batch chunk count exceeds workspace limit")
-    capacities = [capacity for capacity, _, _ in layouts]
-    selected = _select_device(device)
-    host, meta, offsets = _hostio.encode(views, capacities, [c for _, c, _ in layouts],
-                                         chunk_bytes, selected, _torch(),
-                                         (_MAX_BLOCKS, _MAX_BYTES, _MAX_BYTES))
+    sizes = np.fromiter((v.size for v in views), dtype=np.int64, count=len(views))
+    if sizes.max() > _MAX_BYTES:
+        raise ValueError("inputs exceeds size limit (2**28 bytes)")
+    packed = _hostio.pack(views, _torch())
+    slots, meta = compress_zlib_batch_padded_host(packed, sizes, device, chunk_bytes=chunk_bytes)
     _first_failure(meta, 1, "CUDA batch compression")
-    array = host.numpy()
-    lengths = meta.reshape(-1, 2)[:, 0].astype(np.int64) & 0xFFFFFFFF
-    return tuple(array[offsets[i]:offsets[i] + int(lengths[i])].tobytes()
-                 for i in range(len(views)))
+    starts = np.concatenate(([0], np.cumsum(_host_layouts(sizes, chunk_bytes)[0])))
+    ends = starts[:-1] + meta[:, 0]
+    return tuple(slots[a:b].tobytes() for a, b in zip(starts[:-1].tolist(), ends.tolist()))
 
 
 def decompress_zlib_batch_host(payloads, expected_sizes, device=0):
     """Return read-only NumPy views into one pinned host buffer.
 
     Every stream is decoded and checked independently on CUDA.  Host
-    payloads go through in pipelined groups (staging, copy in, decode, copy
-    out overlap; see _hostio), so the batch may exceed one device call's
-    2**28-byte totals; each file keeps the per-file bounds.  Payloads given
-    as CUDA tensors take one device call.
+    payloads go through decompress_zlib_batch_checked_host (pipelined groups;
+    the batch may exceed one device call's 2**28-byte totals, each file keeps
+    the per-file bounds).  Payloads given as CUDA tensors take one device call.
     """
-    views = _host_batch_files(payloads, "payloads")
-    if not isinstance(expected_sizes, (tuple, list)) or any(
-            type(n) is not int or not 0 <= n <= _MAX_BYTES for n in expected_sizes):
-        raise ValueError("expected_sizes must contain integers in [0, 2**28]")
-    expected = tuple(expected_sizes)
-    if len(payloads) != len(expected):
+    views = _host_files(payloads, "payloads")
+    expected = _host_sizes(expected_sizes, "expected_sizes")
+    if len(payloads) != expected.size:
         raise ValueError("input_sizes and expected_sizes must have matching lengths")
-    selected = _select_device(device)
     if views is None:
+        selected = _select_device(device)
         packed, sizes = _pack_batch(payloads, selected)
+        expected = _batch_sizes(tuple(int(v) for v in expected), "expected_sizes")
         output, metadata = decompress_zlib_batch_checked(packed, sizes, expected, selected)
         _check_batch(metadata, "CUDA batch decompression")
         return _split_batch(_to_pinned_host(output), expected)
-    host, meta = _hostio.decode(views, list(expected), selected, _torch(),
-                                (_MAX_BLOCKS, _MAX_BYTES, _MAX_BYTES))
+    sizes = np.fromiter((v.size for v in views), dtype=np.int64, count=len(views))
+    if sizes.max() > _MAX_BYTES:
+        raise ValueError("payloads exceeds size limit (2**28 bytes)")
+    output, meta = decompress_zlib_batch_checked_host(_hostio.pack(views, _torch()), sizes,
+                                                      expected, device)
     _first_failure(meta, 0, "CUDA batch decompression")
-    array = host.numpy()
-    array.flags.writeable = False
-    return _split_batch(array, expected)
+    bounds = np.concatenate(([0], np.cumsum(expected))).tolist()
+    return tuple(output[bounds[i]:bounds[i + 1]] for i in range(len(views)))
 
 
 def decompress_zlib_checked(payload, expected_bytes, device=0, *,

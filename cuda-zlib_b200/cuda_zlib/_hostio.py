@@ -1,25 +1,29 @@
 """Pipelined host-to-host batch calls.
 
-decompress_zlib_batch_host and compress_zlib_batch_host take files in host
-memory and return results in pinned host memory.  Done as one device call,
-the copies and the kernels run one after another.  Here the files go
-through in groups (consecutive files within the batch call's bounds, 2**28
-bytes and 262144 files or chunks per call) and each group moves through
-four stages that overlap with the neighbouring groups' stages:
+The batch calls with host buffers (decompress_zlib_batch_checked_host,
+compress_zlib_batch_padded_host, and the per-file decompress_zlib_batch_host
+and compress_zlib_batch_host built on them) take packed files in host
+memory and return packed results in pinned host memory.  Done as one device
+call, the copies and the kernels would run one after another.  Here the
+files go through in groups (consecutive files within one batch call's
+bounds: 2**28 bytes in and out, 262144 files or chunks) and each group
+moves through four stages that overlap with the neighbouring groups':
 
-  stage     host threads copy the group's files into a pinned buffer
-            (skipped when the files already lie back to back in pinned
-            memory, e.g. views of one page-locked array);
+  stage     host threads copy the group's bytes into a pinned buffer
+            (skipped when the packed input already lives in pinned memory);
   copy in   one cudaMemcpyAsync on a copy stream;
   codec     the batch entry point on the caller's stream;
-  copy out  results and metadata to one pinned host buffer on a third stream.
+  copy out  results and metadata to pinned host memory on a third stream.
 
 Two sets of buffers alternate between groups; events order each reuse after
 the work that last read the buffer.  Because the groups are separate device
-calls, a batch may exceed one call's 2**28-byte totals (the reference's
-host calls stop there); every file keeps the per-file bounds.
+calls, a batch may exceed one call's 2**28-byte totals; every file keeps the
+per-file bounds.  All per-file bookkeeping is vectorised (numpy), so a batch
+of many small files costs no per-file Python work.
 """
+import ctypes
 import os
+import warnings
 from concurrent.futures import ThreadPoolExecutor
 
 import numpy as np
@@ -27,6 +31,7 @@ import numpy as np
 from . import _native
 
 _GROUP_MIN = 32 << 20   # a group holds at least this many bytes (unless the batch is smaller)
+_STAGE_PIECE = 8 << 20  # bytes per host staging task
 _STAGE_THREADS = max(1, min(16, os.cpu_count() or 1))
 _pool = None
 
@@ -38,130 +43,86 @@ def _stage_pool():
     return _pool
 
 
-def host_views(items):
-    """Each item as a flat uint8 NumPy array without copying, or None if some
-    item is not a host buffer (e.g. a CUDA tensor)."""
-    views = []
-    for item in items:
-        if isinstance(item, (bytes, bytearray, memoryview)):
-            views.append(np.frombuffer(item, dtype=np.uint8))
-        elif isinstance(item, np.ndarray):
-            if item.dtype != np.uint8 or item.ndim != 1:
-                raise TypeError("array input must be one-dimensional uint8")
-            views.append(np.ascontiguousarray(item))
-        elif type(item).__module__.startswith("torch") and hasattr(item, "device"):
-            if item.device.type != "cpu":
-                return None
-            if item.dtype.is_floating_point or item.element_size() != 1 or item.ndim != 1:
-                raise TypeError("array input must be one-dimensional uint8")
-            views.append(item.contiguous().numpy().view(np.uint8))
-        else:
-            raise TypeError("input must be bytes or a one-dimensional uint8 array or tensor")
-    return views
-
-
-def _address(view):
-    return view.__array_interface__["data"][0]
-
-
-def _packed_span(views):
-    """(owner array, byte offset) when the views lie back to back in one
-    array's memory (e.g. slices of one packed buffer), else None."""
-    if not views:
-        return None
-    owner = views[0]
-    while isinstance(owner.base, np.ndarray):
-        owner = owner.base
-    if owner.dtype != np.uint8 or owner.ndim != 1 or not owner.flags.c_contiguous:
-        return None
-    start = _address(owner)
-    at = _address(views[0])
-    if at < start:
-        return None
-    for view in views:
-        if view.size and _address(view) != at:
+def as_host_array(data):
+    """A flat uint8 host array over `data` without copying (bytes-like,
+    NumPy array or CPU tensor); None for a CUDA tensor."""
+    if isinstance(data, (bytes, bytearray, memoryview)):
+        return np.frombuffer(data, dtype=np.uint8)
+    if isinstance(data, np.ndarray):
+        if data.dtype != np.uint8 or data.ndim != 1:
+            raise TypeError("array input must be one-dimensional uint8")
+        return np.ascontiguousarray(data)
+    if type(data).__module__.startswith("torch") and hasattr(data, "device"):
+        if data.device.type != "cpu":
             return None
-        at += view.size
-    if at > start + owner.size:
-        return None
-    return owner, _address(views[0]) - start
+        if data.dtype.is_floating_point or data.element_size() != 1 or data.ndim != 1:
+            raise TypeError("array input must be one-dimensional uint8")
+        return data.contiguous().numpy().view(np.uint8)
+    raise TypeError("input must be bytes or a one-dimensional uint8 array or tensor")
+
+
+def _tensor(torch, array):
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore", UserWarning)  # read-only arrays are only read
+        return torch.from_numpy(array)
 
 
 def plan_groups(in_sizes, out_sizes, units, limits):
-    """Consecutive groups [a, b) of files whose totals stay within `limits`
-    = (units, input bytes, output bytes) of one call, cut into at least four
-    groups of at least _GROUP_MIN output bytes when the batch is large
-    enough to overlap its stages."""
-    total = sum(out_sizes)
-    target = min(limits[2], max(_GROUP_MIN, -(-total // 4)))
-    groups, a = [], 0
+    """Boundaries [a, b) of consecutive files whose totals stay within
+    `limits` = (units, input bytes, output bytes) of one call; groups are cut
+    at about a quarter of the batch (at least _GROUP_MIN output bytes) so
+    that a large batch has stages to overlap."""
     n = len(in_sizes)
+    if n == 0:
+        return []
+    cin = np.concatenate(([0], np.cumsum(in_sizes, dtype=np.int64)))
+    cout = np.concatenate(([0], np.cumsum(out_sizes, dtype=np.int64)))
+    cunit = np.concatenate(([0], np.cumsum(units, dtype=np.int64)))
+    target = min(limits[2], max(_GROUP_MIN, -(-int(cout[-1]) // 4)))
+    groups, a = [], 0
     while a < n:
-        b, used_u, used_in, used_out = a, 0, 0, 0
-        while b < n:
-            u, i, o = units[b], in_sizes[b], out_sizes[b]
-            if b > a and (used_u + u > limits[0] or used_in + i > limits[1] or
-                          used_out + o > limits[2] or used_out >= target):
-                break
-            used_u, used_in, used_out = used_u + u, used_in + i, used_out + o
-            b += 1
+        # Largest b with every total within its limit (at least one file).
+        b = min(int(np.searchsorted(cin, cin[a] + limits[1], "right")) - 1,
+                int(np.searchsorted(cout, cout[a] + limits[2], "right")) - 1,
+                int(np.searchsorted(cunit, cunit[a] + limits[0], "right")) - 1,
+                int(np.searchsorted(cout, cout[a] + target, "left")))
+        b = max(a + 1, min(b, n))
         groups.append((a, b))
         a = b
     return groups
 
 
-class _Staging:
-    """Where each group's input comes from: views of pinned memory as they
-    are, else copies into two alternating pinned buffers by host threads."""
+class _Source:
+    """Each group's input as a pinned tensor: slices of the packed input when
+    it is pinned, else copies into two alternating pinned buffers."""
 
-    def __init__(self, torch, views, groups, offsets):
-        self.torch, self.views, self.offsets = torch, views, offsets
-        span = _packed_span(views)
-        self.owner = None
-        if span is not None:
-            owner, base = span
-            import warnings
-            with warnings.catch_warnings():
-                warnings.simplefilter("ignore", UserWarning)  # read-only owners are only read
-                tensor = torch.from_numpy(owner)
-            self.owner, self.base, self.pinned = tensor, base, tensor.is_pinned()
-        need = max((offsets[b] - offsets[a] for a, b in groups), default=0)
-        self.buffers = []
-        if self.owner is None or not self.pinned:
-            self.buffers = [torch.empty(max(1, need), dtype=torch.uint8, pin_memory=True)
-                            for _ in range(2 if len(groups) > 1 else 1)]
-        self.released = [None] * 2  # event after the last copy out of buffer j
+    def __init__(self, torch, packed, groups, offsets):
+        self.packed, self.offsets = packed, offsets
+        tensor = _tensor(torch, packed)
+        self.tensor = tensor if packed.size and tensor.is_pinned() else None
+        need = max((int(offsets[b] - offsets[a]) for a, b in groups), default=0)
+        self.buffers = [] if self.tensor is not None else [
+            torch.empty(max(1, need), dtype=torch.uint8, pin_memory=True)
+            for _ in range(2 if len(groups) > 1 else 1)]
+        self.released = [None, None]
 
-    def source(self, k, a, b):
-        """Pinned host tensor holding files [a, b) back to back."""
-        lo, hi = self.offsets[a], self.offsets[b]
-        if self.owner is not None and self.pinned:
-            return self.owner[self.base + lo:self.base + hi]
+    def get(self, k, a, b):
+        lo, hi = int(self.offsets[a]), int(self.offsets[b])
+        if self.tensor is not None:
+            return self.tensor[lo:hi]
         j = k % len(self.buffers)
         if self.released[j] is not None:
-            self.released[j].synchronize()
+            self.released[j].synchronize()  # the copy of group k - 2 has left this buffer
         buf = self.buffers[j][:hi - lo]
-        host = buf.numpy()
-        if self.owner is not None:
-            packed = self.owner.numpy()[self.base + lo:self.base + hi]
-            pieces = [(s, min(s + (8 << 20), hi - lo)) for s in range(0, hi - lo, 8 << 20)]
-
-            def fill(piece):
-                host[piece[0]:piece[1]] = packed[piece[0]:piece[1]]
-        else:
-            per = max(1, -(-(b - a) // _STAGE_THREADS))
-            pieces = [(i, min(i + per, b)) for i in range(a, b, per)]
-
-            def fill(piece):
-                for i in range(piece[0], piece[1]):
-                    at = self.offsets[i] - lo
-                    host[at:at + self.views[i].size] = self.views[i]
-        if hi - lo >= (4 << 20) and len(pieces) > 1:
-            for future in [_stage_pool().submit(fill, p) for p in pieces]:
+        host, src = buf.numpy(), self.packed[lo:hi]
+        pieces = range(0, hi - lo, _STAGE_PIECE)
+        if len(pieces) > 1:
+            def fill(s):
+                host[s:s + _STAGE_PIECE] = src[s:s + _STAGE_PIECE]
+            for future in [_stage_pool().submit(fill, s) for s in pieces]:
                 future.result()
-        else:
-            for p in pieces:
-                fill(p)
+        elif hi > lo:
+            host[:] = src
         return buf
 
     def mark(self, k, event):
@@ -169,113 +130,128 @@ class _Staging:
             self.released[k % len(self.buffers)] = event
 
 
-def _offsets(sizes):
-    offsets = [0]
-    for size in sizes:
-        offsets.append(offsets[-1] + size)
-    return offsets
+def _i64(values):
+    return (ctypes.c_int64 * len(values))(*values)
 
 
-def run_groups(torch, device, views, groups, in_offsets, out_offsets, dev_out_sizes, call,
-               host_out, meta_words):
-    """Push every group through stage -> copy in -> call -> copy out.
+def run(torch, device, packed, in_sizes, out_sizes, units, limits, call):
+    """Push the packed files through stage -> copy in -> call -> copy out.
 
-    call(k, a, b, dev_in, dev_out, dev_meta, stream) issues the codec call of
-    group k; its results are dev_out[:out_offsets[b] - out_offsets[a]] and
-    dev_meta (2 u32 per file).  Results land in host_out at out_offsets[a]
-    and host metadata (returned, int32 pairs) at 2 a.
+    call(a, b, dev_in, in_bytes, dev_out, out_bytes, dev_meta, stream) issues
+    the batch call of files [a, b).  Returns (pinned host output holding every
+    group's dev_out, int32 metadata of shape (files, 2)).
     """
-    staging = _Staging(torch, views, groups, in_offsets)
-    host_meta = torch.empty(max(1, meta_words), dtype=torch.int32, pin_memory=True)
+    in_sizes = np.asarray(in_sizes, dtype=np.int64)
+    out_sizes = np.asarray(out_sizes, dtype=np.int64)
+    groups = plan_groups(in_sizes, out_sizes, units, limits)
+    in_off = np.concatenate(([0], np.cumsum(in_sizes)))
+    out_off = np.concatenate(([0], np.cumsum(out_sizes)))
+    files = len(in_sizes)
+    host_out = torch.empty(max(1, int(out_off[-1])), dtype=torch.uint8, pin_memory=True)
+    host_meta = torch.empty((max(1, files), 2), dtype=torch.int32, pin_memory=True)
+    if not groups:
+        return host_out, host_meta.numpy()[:0]
+    source = _Source(torch, packed, groups, in_off)
     with torch.cuda.device(device):
         compute = torch.cuda.current_stream(device)
         copy_in, copy_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
         sets = 2 if len(groups) > 1 else 1
-        max_in = max(in_offsets[b] - in_offsets[a] for a, b in groups)
-        max_files = max(b - a for a, b in groups)
-        dev_in = [torch.empty(max(1, max_in), dtype=torch.uint8, device=device)
+        most_in = max(int(in_off[b] - in_off[a]) for a, b in groups)
+        most_out = max(int(out_off[b] - out_off[a]) for a, b in groups)
+        most_files = max(b - a for a, b in groups)
+        dev_in = [torch.empty(max(1, most_in), dtype=torch.uint8, device=device)
                   for _ in range(sets)]
-        dev_out = [torch.empty(max(1, dev_out_sizes), dtype=torch.uint8, device=device)
+        dev_out = [torch.empty(max(1, most_out), dtype=torch.uint8, device=device)
                    for _ in range(sets)]
-        dev_meta = [torch.empty((max_files, 2), dtype=torch.uint32, device=device)
+        dev_meta = [torch.empty((most_files, 2), dtype=torch.int32, device=device)
                     for _ in range(sets)]
         consumed = [None] * sets   # the call that last read dev_in[j]
         drained = [None] * sets    # the copy out that last read dev_out[j]
         for k, (a, b) in enumerate(groups):
             j = k % sets
-            source = staging.source(k, a, b)
-            size_in = in_offsets[b] - in_offsets[a]
+            src = source.get(k, a, b)
+            n_in, n_out = int(in_off[b] - in_off[a]), int(out_off[b] - out_off[a])
             with torch.cuda.stream(copy_in):
                 if consumed[j] is not None:
                     copy_in.wait_event(consumed[j])
-                if size_in:
-                    dev_in[j][:size_in].copy_(source, non_blocking=True)
+                if n_in:
+                    dev_in[j][:n_in].copy_(src, non_blocking=True)
                 arrived = torch.cuda.Event()
                 arrived.record(copy_in)
-            staging.mark(k, arrived)
+            source.mark(k, arrived)
             compute.wait_event(arrived)
             if drained[j] is not None:
                 compute.wait_event(drained[j])
-            call(k, a, b, dev_in[j], dev_out[j], dev_meta[j], compute)
+            call(a, b, dev_in[j], n_in, dev_out[j], n_out, dev_meta[j], compute)
             done = torch.cuda.Event()
             done.record(compute)
             consumed[j] = done
             with torch.cuda.stream(copy_out):
                 copy_out.wait_event(done)
-                size_out = out_offsets[b] - out_offsets[a]
-                if size_out:
-                    host_out[out_offsets[a]:out_offsets[b]].copy_(dev_out[j][:size_out],
-                                                                  non_blocking=True)
-                host_meta[2 * a:2 * b].copy_(dev_meta[j][:b - a].view(torch.int32).reshape(-1),
-                                             non_blocking=True)
+                if n_out:
+                    host_out[int(out_off[a]):int(out_off[b])].copy_(dev_out[j][:n_out],
+                                                                    non_blocking=True)
+                host_meta[a:b].copy_(dev_meta[j][:b - a], non_blocking=True)
                 finished = torch.cuda.Event()
                 finished.record(copy_out)
             drained[j] = finished
         copy_out.synchronize()
         compute.wait_stream(copy_in)
-    return host_meta.numpy()
+    return host_out, host_meta.numpy()[:files]
 
 
-def decode(views, expected, device, torch, limits):
-    """decompress_zlib_batch_host over host views: (pinned output, int32 meta)."""
+def decode(torch, device, packed, in_sizes, out_sizes, limits):
+    """Packed host streams -> (pinned packed outputs, int32 [status, 0] pairs)."""
     lib = _native.library()
-    in_sizes = [v.size for v in views]
-    groups = plan_groups(in_sizes, expected, [1] * len(views), limits)
-    in_offsets, out_offsets = _offsets(in_sizes), _offsets(expected)
-    host_out = torch.empty(max(1, out_offsets[-1]), dtype=torch.uint8, pin_memory=True)
-    import ctypes
+    in_list, out_list = [int(v) for v in in_sizes], [int(v) for v in out_sizes]
 
-    def call(k, a, b, dev_in, dev_out, dev_meta, stream):
-        sizes = (ctypes.c_int64 * (b - a))(*in_sizes[a:b])
-        outs = (ctypes.c_int64 * (b - a))(*expected[a:b])
+    def call(a, b, dev_in, n_in, dev_out, n_out, dev_meta, stream):
         _native.check(lib.cuda_zlib_decompress_batch(
-            dev_in.data_ptr(), in_offsets[b] - in_offsets[a], sizes, outs, b - a, None,
-            dev_out.data_ptr(), out_offsets[b] - out_offsets[a], dev_meta.data_ptr(),
-            stream.cuda_stream), "CUDA batch decompression")
+            dev_in.data_ptr(), n_in, _i64(in_list[a:b]), _i64(out_list[a:b]), b - a, None,
+            dev_out.data_ptr(), n_out, dev_meta.data_ptr(), stream.cuda_stream),
+            "CUDA batch decompression")
 
-    most_out = max(out_offsets[b] - out_offsets[a] for a, b in groups)
-    meta = run_groups(torch, device, views, groups, in_offsets, out_offsets, most_out, call,
-                      host_out, 2 * len(views))
-    return host_out, meta
+    return run(torch, device, packed, in_list, out_list, np.ones(len(in_list), np.int64),
+               limits, call)
 
 
-def encode(views, capacities, chunk_units, chunk_bytes, device, torch, limits):
-    """compress_zlib_batch_host over host views: (pinned slots, int32 meta)."""
+def encode(torch, device, packed, in_sizes, capacities, chunks, chunk_bytes, limits):
+    """Packed host files -> (pinned padded slots, int32 [length, status] pairs)."""
     lib = _native.library()
-    in_sizes = [v.size for v in views]
-    groups = plan_groups(in_sizes, capacities, chunk_units, limits)
-    in_offsets, out_offsets = _offsets(in_sizes), _offsets(capacities)
-    host_out = torch.empty(max(1, out_offsets[-1]), dtype=torch.uint8, pin_memory=True)
-    import ctypes
+    in_list = [int(v) for v in in_sizes]
 
-    def call(k, a, b, dev_in, dev_out, dev_meta, stream):
-        sizes = (ctypes.c_int64 * (b - a))(*in_sizes[a:b])
+    def call(a, b, dev_in, n_in, dev_out, n_out, dev_meta, stream):
         _native.check(lib.cuda_zlib_compress_batch(
-            dev_in.data_ptr(), in_offsets[b] - in_offsets[a], sizes, b - a, chunk_bytes,
-            dev_out.data_ptr(), out_offsets[b] - out_offsets[a], dev_meta.data_ptr(),
-            stream.cuda_stream), "CUDA batch compression")
+            dev_in.data_ptr(), n_in, _i64(in_list[a:b]), b - a, chunk_bytes,
+            dev_out.data_ptr(), n_out, dev_meta.data_ptr(), stream.cuda_stream),
+            "CUDA batch compression")
 
-    most_out = max(out_offsets[b] - out_offsets[a] for a, b in groups)
-    meta = run_groups(torch, device, views, groups, in_offsets, out_offsets, most_out, call,
-                      host_out, 2 * len(views))
-    return host_out, meta, out_offsets
+    return run(torch, device, packed, in_list, capacities, chunks, limits, call)
+
+
+def pack(views, torch):
+    """The files back to back in one array: the owner's span when they
+    already lie back to back in one array (e.g. slices of one buffer), else
+    a pinned concatenation."""
+    if not views:
+        return np.empty(0, dtype=np.uint8)
+    sizes = np.fromiter((v.size for v in views), dtype=np.int64, count=len(views))
+    addresses = np.fromiter((v.__array_interface__["data"][0] for v in views), dtype=np.uint64,
+                            count=len(views))
+    owner = views[0]
+    while isinstance(owner.base, np.ndarray):
+        owner = owner.base
+    start = owner.__array_interface__["data"][0]
+    nonempty = sizes > 0
+    expected = addresses[0] + np.concatenate(([0], np.cumsum(sizes[:-1]))).astype(np.uint64)
+    if (owner.dtype == np.uint8 and owner.ndim == 1 and owner.flags.c_contiguous and
+            addresses[0] >= start and
+            int(addresses[0]) + int(sizes.sum()) <= start + owner.size and
+            np.array_equal(addresses[nonempty], expected[nonempty])):
+        first = int(addresses[0]) - start
+        return owner[first:first + int(sizes.sum())]
+    out = torch.empty(max(1, int(sizes.sum())), dtype=torch.uint8, pin_memory=True).numpy()
+    out = out[:int(sizes.sum())]
+    if len(views):
+        np.concatenate(views, out=out)
+    return out

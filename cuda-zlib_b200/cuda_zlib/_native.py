@@ -56,7 +56,16 @@ def _configure(library):
     library.CudaZlibTrimWorkspacePool.argtypes = [ctypes.c_int]
     library.CudaZlibTrimWorkspacePool.restype = ctypes.c_int
     library.cuda_zlib_b200_version.restype = ctypes.c_char_p
-    _check_pool_error(library.CudaZlibSetWorkspaceRetention(_workspace_retention()))
+    retention = _workspace_retention()
+    code = library.CudaZlibSetWorkspaceRetention(retention)
+    if code:
+        # Retention is fixed once a pool exists (e.g. the library was already
+        # loaded and used through its XLA FFI handlers); that is fine when the
+        # value in force is the one asked for.
+        stats = (ctypes.c_uint64 * 4)()
+        if library.CudaZlibWorkspacePoolStats(0, stats) == 0 and stats[0] == retention:
+            code = 0
+    _check_pool_error(code)
 
 
 def library():

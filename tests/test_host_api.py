@@ -192,3 +192,38 @@ def test_oracle_capacity_matches_the_api():
             if size // chunk > 300000:
                 continue
             assert oracle.capacity(size, chunk) == _codec._capacity(size, chunk)[0]
+
+
+def test_host_batch_groups_respect_call_bounds():
+    """The pipelined host calls cut a batch into device calls within the
+    batch bounds (files/chunks, input and output bytes) and cover it."""
+    import numpy as np
+    from cuda_zlib import _hostio
+    rng = np.random.default_rng(3)
+    for n in (1, 2, 7, 5000):
+        ins = rng.integers(0, 1 << 22, n)
+        outs = rng.integers(0, 1 << 22, n)
+        units = rng.integers(1, 9, n)
+        limits = (1000, 1 << 28, 1 << 28)
+        groups = _hostio.plan_groups(ins, outs, units, limits)
+        assert groups[0][0] == 0 and groups[-1][1] == n
+        assert all(b > a for a, b in groups)
+        assert all(g[1] == h[0] for g, h in zip(groups, groups[1:]))
+        for a, b in groups:
+            if b - a > 1:
+                assert units[a:b].sum() <= limits[0]
+                assert ins[a:b].sum() <= limits[1] and outs[a:b].sum() <= limits[2]
+    # A large batch of equal files splits into at least four groups.
+    groups = _hostio.plan_groups([1000] * 65536, [65536] * 65536, [2] * 65536,
+                                 (262144, 1 << 28, 1 << 28))
+    assert len(groups) >= 16 and max(b - a for a, b in groups) <= 4096
+
+
+def test_host_batch_pack_reuses_back_to_back_views():
+    import numpy as np
+    from cuda_zlib import _hostio
+    owner = np.arange(1000, dtype=np.uint8)
+    views = [owner[10:20], owner[20:20], owner[20:95], owner[95:96]]
+    packed = _hostio.pack(views, None)  # no copy: torch is not needed
+    assert packed.base is owner or packed.base is owner.base or np.shares_memory(packed, owner)
+    assert np.array_equal(packed, owner[10:96])

@@ -42,6 +42,8 @@ class Error(ctypes.Structure):
 
 @pytest.fixture(scope="module")
 def handlers():
+    from cuda_zlib import _native
+    _native.library()  # the package configures the codec library before any handler runs
     spec = importlib.util.spec_from_file_location(
         "cuda_zlib_b200_build", os.path.join(ROOT, "cuda-zlib_b200", "build.py"))
     build = importlib.util.module_from_spec(spec)
