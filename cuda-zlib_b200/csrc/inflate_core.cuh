@@ -90,10 +90,7 @@ struct BitCursor {
 // ---------------------------------------------------------------------------
 // Bits: the hot-loop reader.  A 64-bit accumulator holds 33..64 unread bits
 // after refill(), filled from 4-byte-aligned 32-bit words; positions are u32
-// (a stream's body is below 2^29 bytes, so its bit offsets fit).  The four
-// words after the accumulator are requested ahead in a queue: a lone
-// decoding lane waits on global memory once per queue length, not once per
-// word, since a word lasts only two or three tokens.  The token loops read
+// (a stream's body is below 2^29 bytes, so its bit offsets fit).  The token loops read
 // fields straight from the low word of the accumulator.
 // ---------------------------------------------------------------------------
 struct Bits {
@@ -101,10 +98,9 @@ struct Bits {
   u32 shift;         // bit offset of body bit 0 inside words[0]
   u32 last;          // index of the last word holding a body byte
   u32 end;           // body length in bits
-  u32 idx;           // index of q0, the next word to append
+  u32 idx;           // next word to load
   u32 nbits;         // valid bits in (hi:lo)
   u32 lo, hi;        // 64-bit accumulator; lo holds the next bits
-  u32 q0, q1, q2, q3;  // words idx .. idx + 3, already requested
 
   __device__ __forceinline__ u32 load(u32 i) const { return i <= last ? __ldg(words + i) : 0u; }
 
@@ -124,16 +120,12 @@ struct Bits {
   }
   __device__ __forceinline__ void seek(u32 p) {
     const u32 a = shift + p;
-    const u32 first = a >> 5;
+    idx = a >> 5;
     const u32 off = a & 31;
-    lo = load(first) >> off;
+    lo = load(idx) >> off;
     hi = 0;
     nbits = 32 - off;
-    idx = first + 1;
-    q0 = load(idx);
-    q1 = load(idx + 1);
-    q2 = load(idx + 2);
-    q3 = load(idx + 3);
+    ++idx;
     refill();
   }
   // Append one 32-bit word at bit nbits (nbits <= 32).
@@ -144,16 +136,17 @@ struct Bits {
   }
   __device__ __forceinline__ void refill() {
     if (nbits <= 32) {
-      append(q0);
-      q0 = q1;
-      q1 = q2;
-      q2 = q3;
-      q3 = load(idx + 4);
+      append(load(idx));
       ++idx;
     }
   }
-  // The token loops' refill (loads past the body read as zero either way).
-  __device__ __forceinline__ void refill_fast() { refill(); }
+  // Unguarded refill: only while idx < last is known (fast loops).
+  __device__ __forceinline__ void refill_fast() {
+    if (nbits <= 32) {
+      append(__ldg(words + idx));
+      ++idx;
+    }
+  }
   // Drop n < 32 bits.
   __device__ __forceinline__ void consume(u32 n) {
     lo = __funnelshift_r(lo, hi, n);

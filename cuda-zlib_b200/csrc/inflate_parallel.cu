@@ -723,7 +723,8 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
             continue;
           }
           if (kind != kLength) break;
-          const Bits saved = c;
+          const u32 saved_lo = c.lo, saved_hi = c.hi;
+          const u32 saved_bits = c.nbits, saved_idx = c.idx;
           const u32 L = entry_len(e), E = entry_extra(e);
           const u32 length = entry_value(e) + ((v >> L) & ((1u << E) - 1u));
           c.consume(L + E);
@@ -733,7 +734,10 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
           const u32 Ld = entry_len(d), Ed = entry_extra(d);
           const u32 span = entry_value(d) + ((w >> Ld) & ((1u << Ed) - 1u));
           if (entry_kind(d) != kLiteral || span > window) {
-            c = saved;
+            c.lo = saved_lo;
+            c.hi = saved_hi;
+            c.nbits = saved_bits;
+            c.idx = saved_idx;
             break;
           }
           c.consume(Ld + Ed);
