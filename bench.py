@@ -418,6 +418,11 @@ def run_gpu(args, rank, world):
         box = {}
 
         def e2e_step():
+            # The previous step's results are released first, as a caller
+            # reusing its result buffers would, so the pinned host memory of
+            # the results comes from the allocator's cache rather than new
+            # page locking.
+            box.clear()
             out, meta = codec.decompress_zlib_batch_checked_host(z_pin, z_sizes, sizes, device)
             slots, emeta = codec.compress_zlib_batch_padded_host(raw_pin, sizes, device,
                                                                  chunk_bytes=CHUNK)

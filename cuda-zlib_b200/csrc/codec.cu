@@ -483,9 +483,14 @@ cudaError_t decompress(const u8* in, u64 size, int64_t max_candidates, int64_t m
   const u32 capacity = u32(std::min<u64>(u64(max_candidates), body * 9 + 1));
   const ParallelScratch layout = parallel_scratch_layout(size, expected, capacity,
                                                          token_arena_slack());
+  const u32 nodes = layout.node_capacity;
   ParallelBuffers b{};
   u32* count = nullptr;
   CZ_TRY(ws.allocate(&b.bitmap, layout.bitmap_words));
+  CZ_TRY(ws.allocate(&b.extra, layout.bitmap_words));
+  CZ_TRY(ws.allocate(&b.seed_raw, layout.tiles));
+  CZ_TRY(ws.allocate(&b.seeds, layout.tiles));
+  CZ_TRY(ws.allocate(&b.seed_total, 1));
   CZ_TRY(ws.allocate(&count, 1));
   const u32 queue_cap = discover_queue_capacity(size);
   u32 *queue = nullptr, *queued = nullptr;
@@ -493,18 +498,18 @@ cudaError_t decompress(const u8* in, u64 size, int64_t max_candidates, int64_t m
   CZ_TRY(ws.allocate(&queued, 2));
   CZ_TRY(ws.allocate(&b.block_counts, layout.compact_blocks));
   CZ_TRY(ws.allocate(&b.total, 1));
-  CZ_TRY(ws.allocate(&b.cands, capacity));
-  CZ_TRY(ws.allocate(&b.ends, capacity));
-  CZ_TRY(ws.allocate(&b.sizes, capacity));
-  CZ_TRY(ws.allocate(&b.blocks, capacity));
-  CZ_TRY(ws.allocate(&b.infos, capacity));
-  CZ_TRY(ws.allocate(&b.tokens, capacity));
-  CZ_TRY(ws.allocate(&b.jump, (u64(capacity) + 2) * layout.levels));
-  CZ_TRY(ws.allocate(&b.path, capacity));
-  CZ_TRY(ws.allocate(&b.prefix, capacity));
-  CZ_TRY(ws.allocate(&b.tprefix, capacity));
+  CZ_TRY(ws.allocate(&b.cands, layout.capacity));
+  CZ_TRY(ws.allocate(&b.ends, nodes));
+  CZ_TRY(ws.allocate(&b.sizes, nodes));
+  CZ_TRY(ws.allocate(&b.blocks, nodes));
+  CZ_TRY(ws.allocate(&b.infos, nodes));
+  CZ_TRY(ws.allocate(&b.tokens, nodes));
+  CZ_TRY(ws.allocate(&b.jump, (u64(nodes) + 2) * layout.levels));
+  CZ_TRY(ws.allocate(&b.path, nodes));
+  CZ_TRY(ws.allocate(&b.prefix, nodes));
+  CZ_TRY(ws.allocate(&b.tprefix, nodes));
   CZ_TRY(ws.allocate(&b.syms, u64(layout.pages) * 1024));
-  CZ_TRY(ws.allocate(&b.first_page, capacity));
+  CZ_TRY(ws.allocate(&b.first_page, nodes));
   CZ_TRY(ws.allocate(&b.page_next, layout.pages));
   CZ_TRY(ws.allocate(&b.page_used, layout.pages));
   CZ_TRY(ws.allocate(&b.page_cursor, 1));
@@ -516,13 +521,14 @@ cudaError_t decompress(const u8* in, u64 size, int64_t max_candidates, int64_t m
   CZ_TRY(ws.allocate(&b.fail, 1));
   CZ_TRY(ws.allocate(&b.stash, round_stash_words(dev->info)));
   CZ_TRY(cudaMemsetAsync(b.bitmap, 0, layout.bitmap_words * sizeof(u32), stream));
+  CZ_TRY(cudaMemsetAsync(b.extra, 0, layout.bitmap_words * sizeof(u32), stream));
   CZ_TRY(cudaMemsetAsync(count, 0, sizeof(u32), stream));
   CZ_TRY(cudaMemsetAsync(queued, 0, 2 * sizeof(u32), stream));
   CZ_TRY(cudaMemsetAsync(b.counters, 0, 3 * sizeof(u32), stream));
   CZ_TRY(cudaMemsetAsync(b.page_cursor, 0, sizeof(u32), stream));
   CZ_TRY(cudaMemsetAsync(b.unresolved, 0, layout.out_words * sizeof(u32), stream));
   CZ_TRY(cudaMemsetAsync(b.fail, 0, sizeof(u32), stream));
-  CZ_TRY(launch_discover(in, size, b.bitmap, count, queue, queue_cap, queued, nullptr,
+  CZ_TRY(launch_discover(in, size, b.bitmap, b.extra, count, queue, queue_cap, queued, nullptr,
                          dev->info, stream));
   CZ_TRY(launch_parallel_inflate(in, size, out, expected, u32(max_blocks), layout, b, meta,
                                  dev->info, stream));

@@ -177,6 +177,32 @@ __device__ bool stored_seed(const u8* body, u64 bytes, u64 byte, u64* endpoint) 
   return true;
 }
 
+// Stored-run seed at body byte `byte`: a stored block of at least 1024 bytes
+// whose LEN/NLEN start there and that another stored block follows.  Its
+// endpoint (the next block's header, byte aligned) is a fast-path candidate,
+// so that a long run of stored blocks splits into nodes of one block each;
+// the reference's candidate rule seeds only stored blocks followed by a
+// fixed one (stored_seed above), and its event count ignores these.
+__device__ bool stored_chain(const u8* body, u64 bytes, u64 byte, u64* endpoint) {
+  if (!byte || bytes - byte < 5) return false;
+  const u32 n = u32(body[byte]) | (u32(body[byte + 1]) << 8);
+  const u32 comp = u32(body[byte + 2]) | (u32(body[byte + 3]) << 8);
+  if ((n ^ comp) != 0xffffu || n < 1024) return false;
+  const u64 e = byte + 4 + n;
+  if (e + 5 > bytes) return false;
+  u32 before = u32(body[byte - 1]) << 8;
+  if (byte >= 2) before |= body[byte - 2];
+  bool possible = false;
+  for (u32 gap = 3; gap <= 10; ++gap)
+    if (byte * 8 >= gap && ((before >> (17 - gap)) & 3u) == 0) possible = true;
+  if (!possible || ((body[e] >> 1) & 3u) != 0) return false;
+  const u32 n2 = u32(body[e + 1]) | (u32(body[e + 2]) << 8);
+  const u32 c2 = u32(body[e + 3]) | (u32(body[e + 4]) << 8);
+  if ((n2 ^ c2) != 0xffffu) return false;
+  *endpoint = e;
+  return true;
+}
+
 constexpr u32 kDiscoverTile = 4096;     // body bytes per CTA step
 constexpr u32 kDiscoverThreads = 256;
 constexpr u32 kDiscoverWarps = kDiscoverThreads / 32;
@@ -200,8 +226,8 @@ constexpr u32 kDiscoverPending = 2 * 32 * 16;
 // true headers run side by side across the GPU.  Offsets beyond the queue's
 // capacity are validated here.
 __global__ void __launch_bounds__(kDiscoverThreads)
-discover_kernel(const u8* in, u64 in_size, u32* bitmap, u32* count, u32* queue, u32 queue_cap,
-                u32* queued, const u32* gate) {
+discover_kernel(const u8* in, u64 in_size, u32* bitmap, u32* extra, u32* count, u32* queue,
+                u32 queue_cap, u32* queued, const u32* gate) {
   __shared__ u32 tile[kDiscoverTile / 4 + 8];
   __shared__ u8 kraft3[512];
   __shared__ u16 pending[kDiscoverWarps][kDiscoverPending];  // tile bit offsets
@@ -257,6 +283,8 @@ discover_kernel(const u8* in, u64 in_size, u32* bitmap, u32* count, u32* queue, 
             if (stored_seed(body, bytes, base + first + k, &e)) {
               ++events;
               atomicOr(&bitmap[(e * 8) >> 5], 1u << ((e * 8) & 31));
+            } else if (extra && stored_chain(body, bytes, base + first + k, &e)) {
+              atomicOr(&extra[(e * 8) >> 5], 1u << ((e * 8) & 31));
             }
           }
         }
@@ -732,9 +760,9 @@ __global__ void clear_on_failure_kernel(const u32* meta, u8* out, u64 n) {
   for (u64 i = u64(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) out[i] = 0;
 }
 
-cudaError_t launch_discover(const u8* in, u64 in_size, u32* bitmap, u32* count, u32* queue,
-                            u32 queue_cap, u32* queued, const u32* gate, const DeviceInfo& dev,
-                            cudaStream_t stream) {
+cudaError_t launch_discover(const u8* in, u64 in_size, u32* bitmap, u32* extra, u32* count,
+                            u32* queue, u32 queue_cap, u32* queued, const u32* gate,
+                            const DeviceInfo& dev, cudaStream_t stream) {
   if (in_size < 8) return cudaSuccess;
   const u64 bytes = in_size - 6;
   u64 blocks = (bytes + kDiscoverTile - 1) / kDiscoverTile;
@@ -743,8 +771,8 @@ cudaError_t launch_discover(const u8* in, u64 in_size, u32* bitmap, u32* count, 
   if (blocks < 1) blocks = 1;
   profile_begin("discover_kernel", stream);
   note_launch();
-  discover_kernel<<<u32(blocks), kDiscoverThreads, 0, stream>>>(in, in_size, bitmap, count, queue,
-                                                                queue_cap, queued, gate);
+  discover_kernel<<<u32(blocks), kDiscoverThreads, 0, stream>>>(in, in_size, bitmap, extra, count,
+                                                                queue, queue_cap, queued, gate);
   profile_end(stream);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;

@@ -50,10 +50,17 @@ constexpr u32 kOwnFlag = 0x20000000u;
 constexpr u32 kEmitRing = 4096;    // u16 history entries per emitting warp
 constexpr u32 kEmitMask = kEmitRing - 1;
 constexpr u32 kEmitFlush = 2048;   // pending symbols that trigger a flush
-constexpr u32 kInfoFinal = 1u, kInfoOk = 2u, kInfoSpilled = 4u;
+// Node facts (infos[]): the node decoded cleanly (ok), ended the stream
+// (final), ran out of arena pages (spilled), ended on a fixed-region seed
+// (fixed stop; the next node is that seed's), and whether the block in
+// progress at its end is the final one (exit final).
+constexpr u32 kInfoFinal = 1u, kInfoOk = 2u, kInfoSpilled = 4u, kInfoFixedStop = 8u,
+              kInfoExitFinal = 16u;
 constexpr u32 kPageWords = 1024;   // token words per arena page
 constexpr u32 kNoPage = 0xffffffffu;
 constexpr u32 kPassPages = 40;     // pages one pass can reach (32 Ki tokens)
+constexpr u32 kSeedTileBits = 1u << 18;  // body bits per fixed-region seed probe (32 KiB)
+constexpr u32 kSeedProbeBits = 1024;     // bits a probe decodes before its seed
 
 // ---------------------------------------------------------------------------
 // Lane-parallel rounds over a Huffman block body.
@@ -85,8 +92,11 @@ enum LaneEnd : u32 {
   kLaneBlockEnd = 1,   // end-of-block code at the recorded position
   kLaneIrregular = 2,  // a token for the serial decoder at the recorded position
   kLaneMerged = 3,     // landed on a later lane's mark
+  kLaneFixedStop = 4,  // reached the round's fixed-region seed (a token starts there)
 };
-enum RoundOutcome : u32 { kRoundMore = 0, kRoundBlockEnd = 1, kRoundFallback = 2 };
+enum RoundOutcome : u32 {
+  kRoundMore = 0, kRoundBlockEnd = 1, kRoundFallback = 2, kRoundFixedStop = 3
+};
 
 // Mark rows are padded by a word: lanes work through their windows in near
 // lockstep, and rows 32 words apart would put them all in one bank.
@@ -320,13 +330,19 @@ __device__ __forceinline__ u32 marks_between(const u32* row, u32 a, u32 b) {
 // body end, so no token needs the end check.
 template <bool kChecked>
 __device__ __forceinline__ void window_pass(AheadBits& c, const Tables& t, u32 window, u32 s,
-                                            u32 wend, u32* my_marks, u32* kept_at, u32& kept,
-                                            u32& stop, u32& stop_at, u32& block_end) {
+                                            u32 wend, u32 fixed_stop, u32* my_marks,
+                                            u32* kept_at, u32& kept, u32& stop, u32& stop_at,
+                                            u32& block_end) {
   u32 mark_index = 0, mark_word = 0, bytes = 0, sym = 0;
   for (;;) {
     const u32 p = c.pos();
     if (p >= wend) {
       stop = kLaneWindow;
+      stop_at = p;
+      break;
+    }
+    if (p == fixed_stop) {
+      stop = kLaneFixedStop;
       stop_at = p;
       break;
     }
@@ -355,14 +371,19 @@ __device__ __forceinline__ void window_pass(AheadBits& c, const Tables& t, u32 w
 // say which.  kChecked as for window_pass, over the whole round.
 template <bool kChecked>
 __device__ __forceinline__ void run_on(AheadBits& c, const Tables& t, u32 window, u32 start,
-                                       u32 round_end, const RoundShared& r, u32* kept_at,
-                                       u32& kept, u32& cont_tokens, u32& link, u32& link_at,
-                                       u32& link_to, u32& block_end) {
+                                       u32 round_end, u32 fixed_stop, const RoundShared& r,
+                                       u32* kept_at, u32& kept, u32& cont_tokens, u32& link,
+                                       u32& link_at, u32& link_to, u32& block_end) {
   u32 bytes = 0, sym = 0;
   for (;;) {
     const u32 p = c.pos();
     if (p >= round_end) {
       link = kLaneWindow;
+      link_at = p;
+      break;
+    }
+    if (p == fixed_stop) {
+      link = kLaneFixedStop;
       link_at = p;
       break;
     }
@@ -397,10 +418,13 @@ __device__ __forceinline__ void run_on(AheadBits& c, const Tables& t, u32 window
 // lane's decoded tokens, token k of lane i at word 32 k + i, so that the
 // stores of one loop step are coalesced; phase 3 copies a region from there,
 // starting at the token its entry mark counts to.
+// fixed_stop: a position inside a fixed-Huffman block at which the node
+// must end if its token chain starts a token there (~0u for none); the
+// round then ends there with kRoundFixedStop.
 template <bool kWrite>
 __device__ RoundResult warp_round(const u8* body, u32 body_bytes, u32 start, u32 window,
-                                  const Tables& t, RoundShared& r, SymbolSink& sink,
-                                  u32* stash) {
+                                  u32 fixed_stop, const Tables& t, RoundShared& r,
+                                  SymbolSink& sink, u32* stash) {
   const u32 lane = threadIdx.x & 31u;
   u32* const kept_at = stash ? stash + lane : nullptr;
   u32 kept = 0;         // tokens decoded in phases 1 and 2
@@ -420,20 +444,22 @@ __device__ RoundResult warp_round(const u8* body, u32 body_bytes, u32 start, u32
   if (s < c.end) {
     c.seek(s);
     if (wend + 48 <= c.end)
-      window_pass<false>(c, t, window, s, wend, my_marks, kept_at, kept, stop, stop_at, block_end);
+      window_pass<false>(c, t, window, s, wend, fixed_stop, my_marks, kept_at, kept, stop,
+                         stop_at, block_end);
     else
-      window_pass<true>(c, t, window, s, wend, my_marks, kept_at, kept, stop, stop_at, block_end);
+      window_pass<true>(c, t, window, s, wend, fixed_stop, my_marks, kept_at, kept, stop,
+                        stop_at, block_end);
   }
   __syncwarp();
   // Phase 2: run on until landing on a later lane's mark (or past the round).
   u32 link = stop, link_at = stop_at, link_to = lane, cont_tokens = 0;
   if (stop == kLaneWindow) {
     if (round_end + 48 <= c.end)
-      run_on<false>(c, t, window, start, round_end, r, kept_at, kept, cont_tokens, link, link_at,
-                    link_to, block_end);
+      run_on<false>(c, t, window, start, round_end, fixed_stop, r, kept_at, kept, cont_tokens,
+                    link, link_at, link_to, block_end);
     else
-      run_on<true>(c, t, window, start, round_end, r, kept_at, kept, cont_tokens, link, link_at,
-                   link_to, block_end);
+      run_on<true>(c, t, window, start, round_end, fixed_stop, r, kept_at, kept, cont_tokens,
+                   link, link_at, link_to, block_end);
   }
   r.link[lane] = link;
   r.link_at[lane] = link_at;
@@ -536,7 +562,8 @@ __device__ RoundResult warp_round(const u8* body, u32 body_bytes, u32 start, u32
     out.bytes = total;
     out.tokens = count;
     out.outcome = outcome_end == kLaneWindow ? kRoundMore
-                : outcome_end == kLaneBlockEnd ? kRoundBlockEnd : kRoundFallback;
+                : outcome_end == kLaneBlockEnd ? kRoundBlockEnd
+                : outcome_end == kLaneFixedStop ? kRoundFixedStop : kRoundFallback;
   }
   __syncwarp();
   return out;
@@ -557,12 +584,15 @@ struct ExpandShared {
 // ---------------------------------------------------------------------------
 constexpr u32 kCompactWords = 4096;  // bitmap words per CTA (131072 offsets)
 
-__global__ void cand_count_kernel(const u32* bitmap, u32 words, u32* block_counts) {
+// The fast path's candidates are the reference rule's (bitmap) and the
+// fast-only stored-run seeds (extra), one bit per body bit offset each.
+__global__ void cand_count_kernel(const u32* bitmap, const u32* extra, u32 words,
+                                  u32* block_counts) {
   __shared__ u32 warp_sum[8];
   const u32 base = blockIdx.x * kCompactWords;
   u32 count = 0;
   for (u32 i = threadIdx.x; i < kCompactWords && base + i < words; i += blockDim.x)
-    count += __popc(bitmap[base + i]);
+    count += __popc(bitmap[base + i] | extra[base + i]);
   for (u32 o = 16; o; o >>= 1) count += __shfl_xor_sync(kFullMask, count, o);
   if ((threadIdx.x & 31) == 0) warp_sum[threadIdx.x >> 5] = count;
   __syncthreads();
@@ -571,6 +601,12 @@ __global__ void cand_count_kernel(const u32* bitmap, u32 words, u32* block_count
     for (u32 w = 0; w < blockDim.x / 32; ++w) total += warp_sum[w];
     block_counts[blockIdx.x] = total;
   }
+}
+
+// extra |= bitmap, grid-stride: the candidate headers nodes stop at.
+__global__ void bitmap_or_kernel(const u32* bitmap, u32* extra, u32 words) {
+  for (u32 i = blockIdx.x * blockDim.x + threadIdx.x; i < words; i += gridDim.x * blockDim.x)
+    extra[i] |= bitmap[i];
 }
 
 // Exclusive scan of block_counts in place (one CTA); total -> *total.
@@ -608,15 +644,15 @@ __global__ void cand_scan_kernel(u32* block_counts, u32 blocks, u32* total) {
   if (threadIdx.x == 0) *total = carry;
 }
 
-__global__ void cand_write_kernel(const u32* bitmap, u32 words, const u32* block_offsets,
-                                  u32* cands, u32 capacity) {
+__global__ void cand_write_kernel(const u32* bitmap, const u32* extra, u32 words,
+                                  const u32* block_offsets, u32* cands, u32 capacity) {
   __shared__ u32 warp_sum[8];
   const u32 base = blockIdx.x * kCompactWords;
   const u32 per = kCompactWords / blockDim.x;  // contiguous words per thread
   const u32 first = base + threadIdx.x * per;
   u32 count = 0;
   for (u32 k = 0; k < per; ++k)
-    if (first + k < words) count += __popc(bitmap[first + k]);
+    if (first + k < words) count += __popc(bitmap[first + k] | extra[first + k]);
   u32 incl = count;
   for (u32 o = 1; o < 32; o <<= 1) {
     const u32 t = __shfl_up_sync(kFullMask, incl, o);
@@ -628,7 +664,7 @@ __global__ void cand_write_kernel(const u32* bitmap, u32 words, const u32* block
   for (u32 w = 0; w < (threadIdx.x >> 5); ++w) before += warp_sum[w];
   for (u32 k = 0; k < per; ++k) {
     if (first + k >= words) break;
-    u32 bits = bitmap[first + k];
+    u32 bits = bitmap[first + k] | extra[first + k];
     while (bits) {
       const u32 b = __ffs(bits) - 1;
       bits &= bits - 1;
@@ -645,23 +681,61 @@ __global__ void cand_write_kernel(const u32* bitmap, u32 words, const u32* block
 // ---------------------------------------------------------------------------
 struct NodeResult {
   u32 end, size, blocks, info, tokens;
+  // First end-of-block code of a node that starts inside a fixed block:
+  // where the node ends if that block is the stream's final one.
+  u32 has_eob, eob_end, eob_size, eob_tokens;
 };
 
+// Where nodes stop besides the stream end: at a block header that is a
+// candidate (header_bits: one bit per body bit offset), and, while inside a
+// fixed-Huffman block, exactly at a fixed-region seed (sorted positions).
+struct NodeStops {
+  const u32* header_bits;
+  const u32* fixed;
+  u32 fixed_count;
+};
+
+__device__ __forceinline__ bool bit_set(const u32* bits, u32 p) {
+  return (__ldg(bits + (p >> 5)) >> (p & 31)) & 1u;
+}
+
+// First fixed seed strictly after p, or ~0u.
+__device__ __forceinline__ u32 seed_after(const NodeStops& stops, u32 p) {
+  u32 lo = 0, hi = stops.fixed_count;
+  while (lo < hi) {
+    const u32 mid = (lo + hi) >> 1;
+    if (__ldg(stops.fixed + mid) <= p) lo = mid + 1;
+    else hi = mid;
+  }
+  return lo < stops.fixed_count ? __ldg(stops.fixed + lo) : ~0u;
+}
+
+// Decode one node.  A node starts at a header candidate, or (fixed_entry)
+// at a fixed-region seed inside a fixed-Huffman block whose final flag is
+// entry_final; it runs through blocks until the stream ends, the next block
+// header is a candidate, or, inside a fixed block, its token chain starts a
+// token exactly at a fixed seed.
 template <bool kWrite>
-__device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expected, u32 window,
+__device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, bool fixed_entry,
+                                u32 entry_final, u32 expected, u32 window, const NodeStops& stops,
                                 const Tables& fixed, Tables& dyn, RoundShared& rounds,
                                 SymbolSink& sink, u32* stash) {
   const u32 lane = threadIdx.x & 31u;
-  NodeResult r{start, 0, 0, 0, 0};
+  NodeResult r{start, 0, 0, 0, 0, 0, 0, 0, 0};
   Bits c;
-  u32 produced = 0, tokens = 0, final = 0, blocks = 0, full_words = 0;
-  u32 fail = 0, stop = 0;
-  bool need_header = true;
-  bool parallel = false;  // this block's body goes through lane-parallel rounds
+  u32 produced = 0, tokens = 0, final = entry_final, blocks = 0, full_words = 0;
+  u32 fail = 0, stop = 0, ended_final = 0, fixed_hit = 0;
+  u32 has_eob = 0, eob_end = 0, eob_size = 0, eob_tokens = 0;
+  bool need_header = !fixed_entry;
+  bool parallel = fixed_entry;  // this block's body goes through lane-parallel rounds
+  bool in_fixed = fixed_entry;  // inside a fixed-Huffman block body
+  u32 next_stop = ~0u;          // first fixed seed past the position (inside fixed blocks)
+  if (fixed_entry) warp_load_fixed(dyn, fixed);
   if (lane == 0) {
     c.init(body, bytes);
     c.seek(start);
     full_words = (c.shift + c.end) >> 5;
+    if (fixed_entry) next_stop = seed_after(stops, start);
   }
   const u32 limit = expected;  // output bound of a node
   // Lane 0 appends one symbol word.
@@ -669,20 +743,44 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
     if (kWrite) sink.put(word);
     ++tokens;
   };
+  // Lane 0, at a token boundary p inside a fixed block: is p the next seed?
+  // (Seeds the chain jumps over are skipped.)
+  auto at_seed = [&](u32 p) -> bool {
+    if (p < next_stop) return false;
+    if (p == next_stop) return true;
+    next_stop = seed_after(stops, p - 1);
+    return p == next_stop;
+  };
+  // Lane 0, after an end-of-block code: the first one is kept for the
+  // final-block reading of a fixed-entry node.
+  auto block_end = [&]() {
+    need_header = true;
+    in_fixed = false;
+    next_stop = ~0u;
+    if (fixed_entry && !has_eob) {
+      has_eob = 1;
+      eob_end = c.pos();
+      eob_size = produced;
+      eob_tokens = tokens;
+    }
+    if (final) {
+      stop = 1;
+      ended_final = 1;
+    }
+  };
   for (;;) {
     u32 action = kNone;
     if (lane == 0) {
       while (!fail && !stop) {
         if (need_header) {
           const u32 header = c.pos();
+          if (header != start && bit_set(stops.header_bits, header)) {
+            stop = 1;  // the next node starts at this candidate
+            break;
+          }
           u32 err = 0;
           const u32 f = c.take(1, &err), type = c.take(2, &err);
           if (err || type == 3) { fail = 1; break; }
-          if (type == 2 && blocks) {  // the next node starts here
-            c.seek(header);
-            stop = 1;
-            break;
-          }
           final = f;
           ++blocks;
           if (type == 0) {
@@ -697,7 +795,10 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
             }
             produced += n;
             c.seek(at + n * 8);
-            if (final) stop = 1;
+            if (final) {
+              stop = 1;
+              ended_final = 1;
+            }
             continue;
           }
           action = type == 2 ? kDynamic : kFixed;
@@ -707,11 +808,21 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
           action = kRound;
           break;
         }
+        if (in_fixed && at_seed(c.pos())) {
+          stop = 1;
+          fixed_hit = 1;
+          break;
+        }
         const Tables& t = dyn;
         // One bound for the fast loop: room for a maximal match.
         const u32 stop_at = limit >= 258 ? limit - 258 : 0;
         const u32 idx_limit = full_words >= 2 ? full_words - 1 : 0;
+        bool seed = false;
         while (c.idx < idx_limit && produced < stop_at) {
+          if (in_fixed && at_seed(c.pos())) {
+            seed = true;
+            break;
+          }
           c.refill_fast();
           const u32 v = c.lo;
           const u32 e = t.ll.lut[v & kLLMask];
@@ -744,12 +855,21 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
           put(match_symbol(length, span));
           produced += length;
         }
+        if (seed) {
+          stop = 1;
+          fixed_hit = 1;
+          break;
+        }
         if (fail) break;
+        if (in_fixed && at_seed(c.pos())) {
+          stop = 1;
+          fixed_hit = 1;
+          break;
+        }
         const Token tok = take_token(c, t);
         if (tok.kind == kTokError) { fail = 1; break; }
         if (tok.kind == kTokEnd) {
-          need_header = true;
-          if (final) stop = 1;
+          block_end();
           continue;
         }
         const u32 size = tok.kind == kTokLiteral ? 1u : tok.length;
@@ -774,17 +894,30 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
       if (lane == 0) {
         need_header = false;
         parallel = true;
+        in_fixed = false;
+        next_stop = ~0u;
       }
     } else if (action == kFixed) {
       warp_load_fixed(dyn, fixed);
       if (lane == 0) {
         need_header = false;
         parallel = true;
+        in_fixed = true;
+        next_stop = seed_after(stops, c.pos() - 1);
       }
     } else if (action == kRound) {
-      const u32 from = __shfl_sync(kFullMask, lane == 0 ? c.pos() : 0u, 0);
-      const RoundResult rr = warp_round<kWrite>(body, bytes, from, window, dyn, rounds, sink,
-                                                stash);
+      u32 from = 0, seed = ~0u;
+      if (lane == 0) {
+        from = c.pos();
+        if (in_fixed) {
+          if (from > next_stop) next_stop = seed_after(stops, from - 1);
+          seed = next_stop;
+        }
+      }
+      from = __shfl_sync(kFullMask, from, 0);
+      seed = __shfl_sync(kFullMask, seed, 0);
+      const RoundResult rr = warp_round<kWrite>(body, bytes, from, window, seed, dyn, rounds,
+                                                sink, stash);
       if (lane == 0) {
         if (rr.bytes > limit - produced) {
           // The round would pass the output bound: the serial decoder takes
@@ -799,55 +932,102 @@ __device__ NodeResult warp_node(const u8* body, u32 bytes, u32 start, u32 expect
             // boundary known to be on the true chain.
             parallel = false;
           } else if (rr.outcome == kRoundBlockEnd) {
-            need_header = true;
             parallel = false;
-            if (final) stop = 1;
+            block_end();
+          } else if (rr.outcome == kRoundFixedStop) {
+            stop = 1;
+            fixed_hit = 1;
           }
         }
       }
     }
     __syncwarp();
-    if (done) break;
+    if (done || __shfl_sync(kFullMask, stop, 0)) break;
   }
   if (kWrite && lane == 0) sink.finish();
   r.end = __shfl_sync(kFullMask, c.pos(), 0);
   r.size = __shfl_sync(kFullMask, produced, 0);
   r.blocks = __shfl_sync(kFullMask, blocks, 0);
   r.tokens = __shfl_sync(kFullMask, tokens, 0);
+  r.has_eob = __shfl_sync(kFullMask, has_eob, 0);
+  r.eob_end = __shfl_sync(kFullMask, eob_end, 0);
+  r.eob_size = __shfl_sync(kFullMask, eob_size, 0);
+  r.eob_tokens = __shfl_sync(kFullMask, eob_tokens, 0);
   const u32 spilled = kWrite ? __shfl_sync(kFullMask, sink.spilled, 0) : 0u;
-  r.info = (fail ? 0u : kInfoOk) | (__shfl_sync(kFullMask, final, 0) ? kInfoFinal : 0u) |
-           (spilled ? kInfoSpilled : 0u);
+  const u32 hit = __shfl_sync(kFullMask, fixed_hit, 0);
+  r.info = (fail ? 0u : kInfoOk) | (__shfl_sync(kFullMask, ended_final, 0) ? kInfoFinal : 0u) |
+           (spilled ? kInfoSpilled : 0u) | (hit ? kInfoFixedStop : 0u) |
+           (hit && __shfl_sync(kFullMask, final, 0) ? kInfoExitFinal : 0u);
   return r;
 }
 
-// Describe every candidate (warp per candidate, work stealing).
+// Node ids: header candidates 0 .. K-1 (K = min(total, capacity)), then two
+// per fixed seed j: K + 2j (the seed's block is not the final one) and
+// K + 2j + 1 (it is).
+struct NodeSpace {
+  u32 headers, seeds;
+  __device__ __forceinline__ u32 count() const { return headers + 2 * seeds; }
+};
+__device__ __forceinline__ NodeSpace node_space(const u32* total, u32 capacity,
+                                                const u32* fixed_total, u32 fixed_capacity) {
+  return NodeSpace{min_u32(*total, capacity), min_u32(*fixed_total, fixed_capacity)};
+}
+
+// Describe every candidate and fixed seed (warp per item, work stealing).
+// A seed is decoded once, for the non-final reading; its final-block
+// reading ends at the first end-of-block code, or, without one, where the
+// other ends.
 __global__ void __launch_bounds__(kNodeWarps * 32)
 describe_kernel(const u8* in, u32 in_size, u64 expected, const u32* cands, const u32* total,
-                u32 capacity, u32* next_item, u32* ends, u32* sizes, u32* blocks, u32* infos,
-                u32* tokens, u32* first_page, u32* pool, u32* page_next, u32* page_used,
-                u32* page_cursor, u32 npages, const Tables* fixed, u32* stash) {
+                u32 capacity, const u32* fixed, const u32* fixed_total, u32 fixed_capacity,
+                const u32* header_bits, u32* next_item, u32* ends, u32* sizes, u32* blocks,
+                u32* infos, u32* tokens, u32* first_page, u32* pool, u32* page_next,
+                u32* page_used, u32* page_cursor, u32 npages, const Tables* fixed_tables,
+                u32* stash) {
   __shared__ NodeShared sh;
   const u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   u32* const warp_stash = stash + (u64(blockIdx.x) * kNodeWarps + warp) * (32 * kStash);
   u32 window = 0, wanted = 0;
   if (zlib_framing(in, in_size, &window, &wanted)) return;
-  const u32 count = min_u32(*total, capacity);
+  const NodeSpace ns = node_space(total, capacity, fixed_total, fixed_capacity);
+  const NodeStops stops{header_bits, fixed, ns.seeds};
   for (;;) {
     u32 item = 0;
     if (lane == 0) item = atomicAdd(next_item, 1u);
     item = __shfl_sync(kFullMask, item, 0);
-    if (item >= count) break;
+    if (item >= ns.headers + ns.seeds) break;
+    const bool seed = item >= ns.headers;
+    const u32 node = seed ? ns.headers + 2 * (item - ns.headers) : item;
+    const u32 start = seed ? fixed[item - ns.headers] : cands[item];
     SymbolSink sink{SymbolSink::kPages, pool, 0, page_next, page_used, page_cursor, npages,
                     kNoPage, 0, kNoPage, 0, 0};
-    const NodeResult r = warp_node<true>(in + 2, in_size - 6, cands[item], u32(expected), window,
-                                         *fixed, sh.dyn[warp], sh.round[warp], sink, warp_stash);
+    const NodeResult r = warp_node<true>(in + 2, in_size - 6, start, seed, 0u, u32(expected),
+                                         window, stops, *fixed_tables, sh.dyn[warp],
+                                         sh.round[warp], sink, warp_stash);
     if (lane == 0) {
-      first_page[item] = sink.first;
-      ends[item] = r.end;
-      sizes[item] = r.size;
-      blocks[item] = r.blocks;
-      infos[item] = r.info;
-      tokens[item] = r.tokens;
+      first_page[node] = sink.first;
+      ends[node] = r.end;
+      sizes[node] = r.size;
+      blocks[node] = r.blocks;
+      infos[node] = r.info;
+      tokens[node] = r.tokens;
+      if (seed) {
+        const u32 v = node + 1;
+        first_page[v] = sink.first;
+        if (r.has_eob) {
+          ends[v] = r.eob_end;
+          sizes[v] = r.eob_size;
+          blocks[v] = 0;
+          infos[v] = kInfoOk | kInfoFinal | (r.info & kInfoSpilled);
+          tokens[v] = r.eob_tokens;
+        } else {
+          ends[v] = r.end;
+          sizes[v] = r.size;
+          blocks[v] = r.blocks;
+          infos[v] = r.info | ((r.info & kInfoFixedStop) ? kInfoExitFinal : 0u);
+          tokens[v] = r.tokens;
+        }
+      }
     }
   }
 }
@@ -859,21 +1039,25 @@ describe_kernel(const u8* in, u32 in_size, u64 expected, const u32* cands, const
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(1024)
 chain_kernel(const u8* in, u32 in_size, u64 expected, u32 max_blocks, const u32* cands,
-             const u32* total, u32 capacity, const u32* ends, const u32* sizes,
-             const u32* blocks, const u32* infos, const u32* tokens, u32* jump, u32 levels,
-             u32* path, u32* prefix, u32* tprefix, u32* state) {
+             const u32* total, u32 capacity, const u32* fixed, const u32* fixed_total,
+             u32 fixed_capacity, const u32* ends, const u32* sizes, const u32* blocks,
+             const u32* infos, const u32* tokens, u32* jump, u32 levels, u32* path, u32* prefix,
+             u32* tprefix, u32* state) {
   __shared__ u32 warp_sum[32], warp_tsum[32];
   __shared__ u32 s_len, s_ok, s_carry, s_tcarry, s_blocks;
   const u32 tid = threadIdx.x;
   u32 window = 0, wanted = 0;
-  const u32 count = min_u32(*total, capacity);
-  if (zlib_framing(in, in_size, &window, &wanted) || *total > capacity || !count ||
+  const NodeSpace ns = node_space(total, capacity, fixed_total, fixed_capacity);
+  if (zlib_framing(in, in_size, &window, &wanted) || *total > capacity || !ns.headers ||
       cands[0] != 0) {
     if (tid == 0) { state[0] = 0; state[1] = 0; state[2] = 0; }
     return;
   }
+  const u32 count = ns.count();
   const u32 end_node = count, bad_node = count + 1, nodes = count + 2;
-  // Level 0: successors.
+  // Level 0: successors.  A node that ended on a fixed seed continues at that
+  // seed's node for the final flag of the block in progress; any other
+  // ending position must be a header candidate.
   for (u32 i = tid; i < nodes; i += blockDim.x) {
     u32 next = bad_node;
     if (i == end_node) next = end_node;
@@ -884,13 +1068,17 @@ chain_kernel(const u8* in, u32 in_size, u64 expected, u32 max_blocks, const u32*
           next = end_node;
         } else {
           const u32 target = ends[i];
-          u32 lo = i + 1, hi = count;  // successors start strictly later
+          const bool to_seed = (info & kInfoFixedStop) != 0;
+          const u32* list = to_seed ? fixed : cands;
+          const u32 n = to_seed ? ns.seeds : ns.headers;
+          u32 lo = 0, hi = n;
           while (lo < hi) {
             const u32 mid = (lo + hi) >> 1;
-            if (cands[mid] < target) lo = mid + 1;
+            if (list[mid] < target) lo = mid + 1;
             else hi = mid;
           }
-          if (lo < count && cands[lo] == target) next = lo;
+          if (lo < n && list[lo] == target)
+            next = to_seed ? ns.headers + 2 * lo + ((info & kInfoExitFinal) ? 1u : 0u) : lo;
         }
       }
     }
@@ -985,9 +1173,11 @@ chain_kernel(const u8* in, u32 in_size, u64 expected, u32 max_blocks, const u32*
 // Decode every path node again, writing its tokens at its place in the
 // symbol arena (warp per node, work stealing).
 __global__ void __launch_bounds__(kNodeWarps * 32)
-symbols_kernel(const u8* in, u32 in_size, u64 expected, const u32* cands, const u32* path,
-               const u32* tprefix, const u32* sizes, const u32* tokens, const u32* state,
-               u32* next_item, u32* syms, u32* fail_flag, const Tables* fixed, u32* stash) {
+symbols_kernel(const u8* in, u32 in_size, u64 expected, const u32* cands, const u32* total,
+               u32 capacity, const u32* fixed, const u32* fixed_total, u32 fixed_capacity,
+               const u32* header_bits, const u32* path, const u32* tprefix, const u32* sizes,
+               const u32* tokens, const u32* state, u32* next_item, u32* syms, u32* fail_flag,
+               const Tables* fixed_tables, u32* stash) {
   __shared__ NodeShared sh;
   const u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   u32* const warp_stash = stash + (u64(blockIdx.x) * kNodeWarps + warp) * (32 * kStash);
@@ -995,16 +1185,22 @@ symbols_kernel(const u8* in, u32 in_size, u64 expected, const u32* cands, const 
   const u32 len = state[0];
   u32 window = 0, wanted = 0;
   zlib_framing(in, in_size, &window, &wanted);
+  const NodeSpace ns = node_space(total, capacity, fixed_total, fixed_capacity);
+  const NodeStops stops{header_bits, fixed, ns.seeds};
   for (;;) {
     u32 item = 0;
     if (lane == 0) item = atomicAdd(next_item, 1u);
     item = __shfl_sync(kFullMask, item, 0);
     if (item >= len) break;
     const u32 node = path[item];
+    const bool seed = node >= ns.headers;
+    const u32 start = seed ? fixed[(node - ns.headers) >> 1] : cands[node];
+    const u32 entry_final = seed ? (node - ns.headers) & 1u : 0u;
     SymbolSink sink{SymbolSink::kContiguous, syms + tprefix[item], tokens[node], nullptr, nullptr,
                     nullptr, 0, kNoPage, 0, kNoPage, 0, 0};
-    const NodeResult r = warp_node<true>(in + 2, in_size - 6, cands[node], u32(expected), window,
-                                         *fixed, sh.dyn[warp], sh.round[warp], sink, warp_stash);
+    const NodeResult r = warp_node<true>(in + 2, in_size - 6, start, seed, entry_final,
+                                         u32(expected), window, stops, *fixed_tables,
+                                         sh.dyn[warp], sh.round[warp], sink, warp_stash);
     if (lane == 0 && (!(r.info & kInfoOk) || (r.info & kInfoSpilled) || r.size != sizes[node] ||
                       r.tokens != tokens[node]))
       atomicOr(fail_flag, 1u);
@@ -1073,17 +1269,21 @@ expand_kernel(const u8* in, u32 in_size, const u32* path, const u32* prefix,
     const bool contiguous = state[2] != 0;
     u32 page = contiguous ? kNoPage : first_page[node], last_page = 0;
     u32 pos = 0, flushed = 0, bad = 0;
+    // A seed's final-block reading shares the pages of its other reading and
+    // takes only its own (leading) tokens.
+    u32 left = tokens[node];
     for (bool first_run = true;; first_run = false) {
     const u32* sy = syms + tprefix[item];
     u32 n = tokens[node];
     if (!contiguous) {
-      if (page == kNoPage) break;
+      if (page == kNoPage || !left) break;
       if (page >= npages || (!first_run && page <= last_page) || page_used[page] > kPageWords) {
         bad = 1;
         break;
       }
       sy = syms + u64(page) * kPageWords;
-      n = page_used[page];
+      n = min_u32(page_used[page], left);
+      left -= n;
       last_page = page;
     }
     // Tokens of the chunk after the current one are loaded while the current
@@ -1117,10 +1317,25 @@ expand_kernel(const u8* in, u32 in_size, const u32* path, const u32* prefix,
         // Stored bytes: flush, then copy straight from the input.
         const u32 count = head & 0xffffu, src = sy[first + 1];
         flush_symbols(ring, out, source, unresolved, start, flushed, pos);
-        for (u32 j = lane; j < count; j += 32) {
-          const u8 v = body[src + j];
-          out[start + pos + j] = v;
-          ring[(pos + j) & kEmitMask] = v;
+        // Eight independent loads per lane before the stores; only the last
+        // kEmitRing bytes can still be read through the ring.
+        constexpr u32 kUnroll = 8;
+        const u32 ring_from = count > kEmitRing ? count - kEmitRing : 0u;
+        for (u32 base = 0; base < count; base += 32 * kUnroll) {
+          u8 v[kUnroll];
+#pragma unroll
+          for (u32 k = 0; k < kUnroll; ++k) {
+            const u32 j = base + 32 * k + lane;
+            v[k] = j < count ? body[src + j] : u8(0);
+          }
+#pragma unroll
+          for (u32 k = 0; k < kUnroll; ++k) {
+            const u32 j = base + 32 * k + lane;
+            if (j < count) {
+              out[start + pos + j] = v[k];
+              if (j >= ring_from) ring[(pos + j) & kEmitMask] = v[k];
+            }
+          }
         }
         pos += count;
         flushed = pos;
@@ -1401,6 +1616,82 @@ __global__ void parallel_finish_kernel(const u8* in, u32 in_size, const u32* sta
   }
 }
 
+// ---------------------------------------------------------------------------
+// Fixed-region seeds.  A fixed-Huffman block has no header to discover, so a
+// long run of fixed blocks (a Z_FIXED stream) would be one node decoded by
+// one warp.  Instead, every tile of kSeedTileBits body bits gets one thread
+// that decodes with the fixed tables from the tile start, through further
+// fixed blocks, for kSeedProbeBits bits; if every token is valid, the first
+// token start past that is a seed.  Huffman decoding resynchronises within a
+// few tokens, so the probe's chain has almost surely joined the true chain
+// there when the tile lies inside fixed blocks.  Nothing depends on that: a
+// node stops at a seed only if its own (true) chain starts a token exactly
+// there, and a seed no true chain reaches is a node no path visits.
+// ---------------------------------------------------------------------------
+__global__ void seed_probe_kernel(const u8* in, u64 in_size, const Tables* fixed, u32 tiles,
+                                  u32* raw) {
+  const u32 k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= tiles) return;
+  u32 seed = ~0u;
+  if (k > 0 && in_size >= 8) {
+    const u8* body = in + 2;
+    const u64 bytes = in_size - 6;
+    const u64 start = u64(k) * kSeedTileBits, goal = start + kSeedProbeBits;
+    if (goal + 64 < bytes * 8) {
+      BitCursor c;
+      c.init(body, bytes, start);
+      bool valid = true;
+      while (valid && c.pos < goal) {
+        const Token tok = decode_token(c, *fixed);
+        if (tok.kind == kTokError) {
+          valid = false;
+          break;
+        }
+        c.skip(tok.bits);
+        if (tok.kind == kTokEnd) {  // the next block must be fixed-Huffman too
+          u32 err = 0;
+          c.take(1, &err);
+          const u32 type = c.take(2, &err);
+          valid = !err && type == 1;
+        }
+      }
+      if (valid && c.pos >= goal && c.pos < bytes * 8) seed = u32(c.pos);
+    }
+  }
+  raw[k] = seed;
+}
+
+// Sorted seeds from the per-tile probe results (one CTA).
+__global__ void __launch_bounds__(1024)
+seed_compact_kernel(const u32* raw, u32 tiles, u32* seeds, u32* total) {
+  __shared__ u32 warp_sum[32];
+  const u32 per = (tiles + blockDim.x - 1) / blockDim.x;
+  const u32 first = min_u32(threadIdx.x * per, tiles), last = min_u32(first + per, tiles);
+  u32 count = 0;
+  for (u32 k = first; k < last; ++k) count += raw[k] != ~0u ? 1u : 0u;
+  u32 incl = count;
+  for (u32 o = 1; o < 32; o <<= 1) {
+    const u32 v = __shfl_up_sync(kFullMask, incl, o);
+    if ((threadIdx.x & 31) >= o) incl += v;
+  }
+  if ((threadIdx.x & 31) == 31) warp_sum[threadIdx.x >> 5] = incl;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    u32 w = threadIdx.x < blockDim.x / 32 ? warp_sum[threadIdx.x] : 0u;
+    for (u32 o = 1; o < 32; o <<= 1) {
+      const u32 v = __shfl_up_sync(kFullMask, w, o);
+      if (threadIdx.x >= o) w += v;
+    }
+    warp_sum[threadIdx.x] = w;
+  }
+  __syncthreads();
+  const u32 warp = threadIdx.x >> 5;
+  u32 at = (warp ? warp_sum[warp - 1] : 0u) + incl - count;
+  for (u32 k = first; k < last; ++k)
+    if (raw[k] != ~0u) seeds[at++] = raw[k];
+  if (threadIdx.x == blockDim.x - 1) *total = at;
+}
+
 // The fixed Huffman tables, built once per device into global memory.
 __global__ void build_fixed_kernel(Tables* fixed) { warp_build_fixed(*fixed); }
 
@@ -1437,8 +1728,13 @@ ParallelScratch parallel_scratch_layout(u64 in_size, u64 expected, u32 capacity,
   const u64 body = in_size - 6;
   s.bitmap_words = (body * 8 + 31) / 32 + 1;
   s.compact_blocks = u32((s.bitmap_words + kCompactWords - 1) / kCompactWords);
-  s.capacity = capacity;
-  s.levels = chain_levels(capacity);
+  // Candidates: the reference rule's (at most `capacity`, else the stream
+  // fails as the reference's does) plus the stored-run seeds, at most one per
+  // 1029 body bytes (each ends a stored block of at least 1024 bytes).
+  s.capacity = capacity + u32(body / 1024) + 64;
+  s.tiles = u32((body * 8 + kSeedTileBits - 1) / kSeedTileBits);
+  s.node_capacity = s.capacity + 2 * s.tiles;
+  s.levels = chain_levels(s.node_capacity);
   s.out_words = (expected + 31) / 32 + 1;
   s.segments = u32((expected + kAdlerSegment - 1) / kAdlerSegment);
   // Path tokens of a chain that passes its checks: at most one per output
@@ -1462,33 +1758,44 @@ cudaError_t launch_parallel_inflate(const u8* in, u64 in_size, u8* out, u64 expe
                                     u32 max_blocks, const ParallelScratch& s,
                                     const ParallelBuffers& b, u32* meta, const DeviceInfo& dev,
                                     cudaStream_t stream) {
-  const u32 nodes = s.capacity + 2;
+  const Tables* fixed = static_cast<const Tables*>(dev.fixed_tables);
   note_launch();
-  cand_count_kernel<<<s.compact_blocks, 256, 0, stream>>>(b.bitmap, u32(s.bitmap_words),
-                                                          b.block_counts);
+  seed_probe_kernel<<<(s.tiles + 255) / 256, 256, 0, stream>>>(in, in_size, fixed, s.tiles,
+                                                               b.seed_raw);
+  note_launch();
+  seed_compact_kernel<<<1, 1024, 0, stream>>>(b.seed_raw, s.tiles, b.seeds, b.seed_total);
+  note_launch();
+  cand_count_kernel<<<s.compact_blocks, 256, 0, stream>>>(b.bitmap, b.extra,
+                                                          u32(s.bitmap_words), b.block_counts);
   note_launch();
   cand_scan_kernel<<<1, 1024, 0, stream>>>(b.block_counts, s.compact_blocks, b.total);
   note_launch();
-  cand_write_kernel<<<s.compact_blocks, 256, 0, stream>>>(b.bitmap, u32(s.bitmap_words),
+  cand_write_kernel<<<s.compact_blocks, 256, 0, stream>>>(b.bitmap, b.extra, u32(s.bitmap_words),
                                                           b.block_counts, b.cands, s.capacity);
+  // Nodes stop at any candidate header: the reference rule's and the
+  // stored-run seeds (b.extra holds their union after the OR kernel).
+  note_launch();
+  bitmap_or_kernel<<<u32(dev.sms) * 4, 256, 0, stream>>>(b.bitmap, b.extra,
+                                                         u32(s.bitmap_words));
   const u32 node_grid = node_ctas(dev);
   profile_begin("describe_kernel", stream);
   note_launch();
   describe_kernel<<<node_grid, kNodeWarps * 32, 0, stream>>>(
-      in, u32(in_size), expected, b.cands, b.total, s.capacity, b.counters, b.ends, b.sizes,
-      b.blocks, b.infos, b.tokens, b.first_page, b.syms, b.page_next, b.page_used,
-      b.page_cursor, s.pages, static_cast<const Tables*>(dev.fixed_tables), b.stash);
+      in, u32(in_size), expected, b.cands, b.total, s.capacity, b.seeds, b.seed_total, s.tiles,
+      b.extra, b.counters, b.ends, b.sizes, b.blocks, b.infos, b.tokens, b.first_page, b.syms,
+      b.page_next, b.page_used, b.page_cursor, s.pages, fixed, b.stash);
   profile_end(stream);
   note_launch();
   chain_kernel<<<1, 1024, 0, stream>>>(in, u32(in_size), expected, max_blocks, b.cands, b.total,
-                                       s.capacity, b.ends, b.sizes, b.blocks, b.infos, b.tokens,
-                                       b.jump, s.levels, b.path, b.prefix, b.tprefix, b.state);
-  (void)nodes;
+                                       s.capacity, b.seeds, b.seed_total, s.tiles, b.ends,
+                                       b.sizes, b.blocks, b.infos, b.tokens, b.jump, s.levels,
+                                       b.path, b.prefix, b.tprefix, b.state);
   profile_begin("symbols_kernel", stream);
   note_launch();
   symbols_kernel<<<node_grid, kNodeWarps * 32, 0, stream>>>(
-      in, u32(in_size), expected, b.cands, b.path, b.tprefix, b.sizes, b.tokens, b.state,
-      b.counters + 1, b.syms, b.fail, static_cast<const Tables*>(dev.fixed_tables), b.stash);
+      in, u32(in_size), expected, b.cands, b.total, s.capacity, b.seeds, b.seed_total, s.tiles,
+      b.extra, b.path, b.tprefix, b.sizes, b.tokens, b.state, b.counters + 1, b.syms, b.fail,
+      fixed, b.stash);
   profile_end(stream);
   const u32 expand_grid = u32(dev.sms) * u32(dev.emit_per_sm > 0 ? dev.emit_per_sm : 1);
   profile_begin("expand_kernel", stream);

@@ -90,25 +90,31 @@ cudaError_t launch_encode(const u8* in, const EncodeFile* files, u32 nfiles, u32
 struct ParallelScratch {
   u64 bitmap_words;   // candidate bitmap words (one bit per body bit offset)
   u32 compact_blocks; // CTAs of the candidate compaction
-  u32 capacity;       // candidate capacity = min(max_candidates, 9 * body + 1)
-  u32 levels;         // pointer-doubling levels over capacity + 2 nodes
+  u32 capacity;       // candidates: min(max_candidates, 9 * body + 1) + stored-run seeds
+  u32 tiles;          // fixed-region seed probes (one per 32 KiB of body)
+  u32 node_capacity;  // nodes: capacity + 2 per seed
+  u32 levels;         // pointer-doubling levels over node_capacity + 2 nodes
   u64 out_words;      // unresolved-position bitmap words
   u32 segments;       // Adler-32 segments of the output
   u64 symbol_words;   // contiguous token layout of the path nodes
   u32 pages;          // token arena pages (1024 words each, at least symbol_words)
 };
 struct ParallelBuffers {
-  u32* bitmap;        // bitmap_words, from discover_kernel
+  u32* bitmap;        // bitmap_words, from discover_kernel (the reference's rule)
+  u32* extra;         // bitmap_words, zeroed: stored-run seeds (fast path only)
+  u32* seed_raw;      // tiles: probe result per tile
+  u32* seeds;         // tiles: sorted fixed-region seeds
+  u32* seed_total;    // 1
   u32* block_counts;  // compact_blocks
   u32* total;         // 1: distinct candidates
   u32* cands;         // capacity
-  u32 *ends, *sizes, *blocks, *infos, *tokens;  // capacity each
-  u32* jump;          // (capacity + 2) * levels
-  u32 *path, *prefix, *tprefix;  // capacity each: path nodes, output and token offsets
+  u32 *ends, *sizes, *blocks, *infos, *tokens;  // node_capacity each
+  u32* jump;          // (node_capacity + 2) * levels
+  u32 *path, *prefix, *tprefix;  // node_capacity each: path nodes, output and token offsets
   u32* state;         // 3: path length, chain ok, contiguous-layout fallback
   u32* counters;      // 3, zeroed: describe / symbols / expand work counters
   u32* syms;          // pages * 1024 words: the token arena
-  u32 *first_page, *page_next, *page_used;  // capacity, pages, pages
+  u32 *first_page, *page_next, *page_used;  // node_capacity, pages, pages
   u32* page_cursor;   // 1, zeroed: next free arena page
   u32* source;        // expected: absolute source of unresolved positions
   u32* unresolved;    // out_words, zeroed
@@ -133,9 +139,11 @@ cudaError_t launch_parallel_inflate(const u8* in, u64 in_size, u8* out, u64 expe
 // queue: discover_queue_capacity(in_size) u32; queued: zeroed u32[2] (offsets
 // queued, validation cursor).
 u32 discover_queue_capacity(u64 in_size);
-cudaError_t launch_discover(const u8* in, u64 in_size, u32* bitmap, u32* count, u32* queue,
-                            u32 queue_cap, u32* queued, const u32* gate, const DeviceInfo& dev,
-                            cudaStream_t stream);
+// extra: zeroed bitmap that receives the stored-run seeds (fast path only;
+// the reference's candidate rule and event count are in bitmap / count).
+cudaError_t launch_discover(const u8* in, u64 in_size, u32* bitmap, u32* extra, u32* count,
+                            u32* queue, u32 queue_cap, u32* queued, const u32* gate,
+                            const DeviceInfo& dev, cudaStream_t stream);
 // meta[0] holds the fast path status; rewritten with the route's status;
 // a failed output is zeroed.
 cudaError_t launch_general_status(const u8* in, u64 in_size, u64 expected, u32 max_candidates,
