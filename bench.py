@@ -228,8 +228,8 @@ class Timing:
     """Device-time steps with the library's per-kernel event totals."""
 
     NAMES = ("serial_inflate_kernel", "discover_kernel", "validate_kernel", "describe_kernel",
-             "symbols_kernel", "expand_kernel", "resolve_kernel", "encode_chunks_kernel",
-             "encode_pack_kernel")
+             "symbols_kernel", "expand_kernel", "resolve_kernel", "stage_resolve_kernel",
+             "encode_chunks_kernel", "encode_pack_kernel")
 
     def __init__(self, torch, lib, device, flush):
         self.torch, self.lib, self.device, self.flush = torch, lib, device, flush
@@ -287,7 +287,8 @@ def max_over_ranks(torch, value, device, world):
 
 
 DECODE_KERNELS = ("serial_inflate_kernel", "discover_kernel", "validate_kernel",
-                  "describe_kernel", "symbols_kernel", "expand_kernel", "resolve_kernel")
+                  "describe_kernel", "symbols_kernel", "expand_kernel", "resolve_kernel",
+                  "stage_resolve_kernel")
 
 
 def roofline(workload, kernels, steps, decode_bytes, encode_bytes):
@@ -651,6 +652,12 @@ def run_configs(args, torch, codec, device, timing):
 
 # ------------------------------------------------------------------ main
 def main():
+    # Scratch kept by the codec's workspace pool between calls (the
+    # reference's CUDA_ZLIB_WORKSPACE_RETENTION_BYTES, default 1 GiB): the
+    # single-stream configs need several GiB of scratch per call, which a
+    # 1 GiB release threshold would unmap and map again every step.  A
+    # caller's own setting wins.
+    os.environ.setdefault("CUDA_ZLIB_WORKSPACE_RETENTION_BYTES", str(32 << 30))
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=5)

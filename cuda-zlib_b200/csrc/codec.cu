@@ -12,6 +12,7 @@
 #include <array>
 #include <cstdint>
 #include <cstdlib>
+#include <cstring>
 #include <atomic>
 #include <mutex>
 #include <numeric>
@@ -53,10 +54,29 @@ constexpr int kMaxDevices = 64;
 // ---------------------------------------------------------------------------
 // Per-device state: launch facts and the scratch pool.
 // ---------------------------------------------------------------------------
+// Page-locked staging for the small host tables a call uploads (file and
+// stream descriptors).  A copy from pageable memory makes CUDA wait for the
+// stream to drain before it starts, which would stall every batch call
+// behind the previous call's kernels; from here the copy is asynchronous.
+// Slots are reused round robin once the copy that last read them is done.
+constexpr int kStagingSlots = 16;
+constexpr size_t kStagingSlotBytes = size_t(512) << 10;
+struct StagingSlot {
+  std::mutex mutex;  // held while the slot is filled and its copy issued
+  cudaEvent_t done = nullptr;
+};
+struct Staging {
+  std::mutex mutex;
+  u8* host = nullptr;  // kStagingSlots * kStagingSlotBytes, page-locked
+  int next = 0;
+  StagingSlot slots[kStagingSlots];
+};
+
 struct DeviceState {
   bool ready = false;
   DeviceInfo info{};
   cudaMemPool_t pool = nullptr;
+  Staging* staging = nullptr;
 };
 
 struct Registry {
@@ -98,8 +118,18 @@ cudaError_t device_state(int device, DeviceState** out) {
       cudaMemPoolDestroy(pool);
       return e;
     }
+    Staging* staging = new Staging;
+    e = cudaHostAlloc(reinterpret_cast<void**>(&staging->host),
+                      kStagingSlots * kStagingSlotBytes, cudaHostAllocPortable);
+    for (int k = 0; e == cudaSuccess && k < kStagingSlots; ++k)
+      e = cudaEventCreateWithFlags(&staging->slots[k].done, cudaEventDisableTiming);
+    if (e != cudaSuccess) {
+      cudaMemPoolDestroy(pool);
+      return e;  // the staging block is kept: a failed set-up is not retried cheaply
+    }
     d.info = info;
     d.pool = pool;
+    d.staging = staging;
     d.ready = true;
     r.pools_created = true;
   }
@@ -277,13 +307,30 @@ cudaError_t set_meta(u32* meta, u32 first, u32 second, cudaStream_t stream) {
 }
 
 template <typename T>
-cudaError_t upload(Workspace& ws, T** out, const std::vector<T>& host, cudaStream_t stream) {
+cudaError_t upload(const DeviceState& dev, Workspace& ws, T** out, const std::vector<T>& host,
+                   cudaStream_t stream) {
   CZ_TRY(ws.allocate(out, host.size()));
   if (host.empty()) return cudaSuccess;
-  // Pageable source: the copy stages the bytes before returning, so the
-  // vector may be released right after.
-  return cudaMemcpyAsync(*out, host.data(), host.size() * sizeof(T), cudaMemcpyHostToDevice,
-                         stream);
+  const size_t bytes = host.size() * sizeof(T);
+  if (bytes > kStagingSlotBytes || !dev.staging) {
+    // Larger tables copy from pageable memory: the copy stages the bytes
+    // before returning, so the vector may be released right after.
+    return cudaMemcpyAsync(*out, host.data(), bytes, cudaMemcpyHostToDevice, stream);
+  }
+  Staging& st = *dev.staging;
+  int k = 0;
+  {
+    std::lock_guard<std::mutex> lock(st.mutex);
+    k = st.next;
+    st.next = (st.next + 1) % kStagingSlots;
+  }
+  StagingSlot& slot = st.slots[k];
+  std::lock_guard<std::mutex> hold(slot.mutex);
+  CZ_TRY(cudaEventSynchronize(slot.done));  // the slot's previous copy has read it
+  u8* pinned = st.host + size_t(k) * kStagingSlotBytes;
+  std::memcpy(pinned, host.data(), bytes);
+  CZ_TRY(cudaMemcpyAsync(*out, pinned, bytes, cudaMemcpyHostToDevice, stream));
+  return cudaEventRecord(slot.done, stream);
 }
 
 // ---------------------------------------------------------------------------
@@ -318,7 +365,7 @@ cudaError_t encode_files(const DeviceState& dev, const u8* in, u64 in_bytes,
   u32 *sizes = nullptr, *status = nullptr;
   u64 *adler = nullptr, *offsets = nullptr;
   EncodeSpill spill{};
-  CZ_TRY(upload(ws, &d_files, files, stream));
+  CZ_TRY(upload(dev, ws, &d_files, files, stream));
   CZ_TRY(ws.allocate(&slots, in_bytes + 96 * (u64(total_chunks) + 2)));
   CZ_TRY(ws.allocate(&sizes, total_chunks));
   CZ_TRY(ws.allocate(&status, total_chunks));
@@ -515,10 +562,13 @@ cudaError_t decompress(const u8* in, u64 size, int64_t max_candidates, int64_t m
   CZ_TRY(ws.allocate(&b.page_cursor, 1));
   CZ_TRY(ws.allocate(&b.state, 3));
   CZ_TRY(ws.allocate(&b.counters, 3));
-  CZ_TRY(ws.allocate(&b.source, expected));
+  CZ_TRY(ws.allocate(&b.source, expected + 32));  // read in 32-entry words
   CZ_TRY(ws.allocate(&b.unresolved, layout.out_words));
   CZ_TRY(ws.allocate(&b.parts, 2 * u64(layout.segments)));
   CZ_TRY(ws.allocate(&b.fail, 1));
+  CZ_TRY(ws.allocate(&b.deep, 1));
+  CZ_TRY(ws.allocate(&b.longs, layout.out_words));
+  CZ_TRY(ws.allocate(&b.stage_done, u64(layout.stages) + 1));
   CZ_TRY(ws.allocate(&b.stash, round_stash_words(dev->info)));
   CZ_TRY(cudaMemsetAsync(b.bitmap, 0, layout.bitmap_words * sizeof(u32), stream));
   CZ_TRY(cudaMemsetAsync(b.extra, 0, layout.bitmap_words * sizeof(u32), stream));
@@ -528,6 +578,8 @@ cudaError_t decompress(const u8* in, u64 size, int64_t max_candidates, int64_t m
   CZ_TRY(cudaMemsetAsync(b.page_cursor, 0, sizeof(u32), stream));
   CZ_TRY(cudaMemsetAsync(b.unresolved, 0, layout.out_words * sizeof(u32), stream));
   CZ_TRY(cudaMemsetAsync(b.fail, 0, sizeof(u32), stream));
+  CZ_TRY(cudaMemsetAsync(b.deep, 0, sizeof(u32), stream));
+  CZ_TRY(cudaMemsetAsync(b.stage_done, 0, (u64(layout.stages) + 1) * sizeof(u32), stream));
   CZ_TRY(launch_discover(in, size, b.bitmap, b.extra, count, queue, queue_cap, queued, nullptr,
                          dev->info, stream));
   CZ_TRY(launch_parallel_inflate(in, size, out, expected, u32(max_blocks), layout, b, meta,
@@ -570,8 +622,8 @@ cudaError_t decompress_batch(const u8* in, u64 in_bytes, const int64_t* in_sizes
   Workspace ws(dev->pool, stream);
   StreamDesc* d_descs = nullptr;
   u32 *d_order = nullptr, *counter = nullptr;
-  CZ_TRY(upload(ws, &d_descs, descs, stream));
-  CZ_TRY(upload(ws, &d_order, order, stream));
+  CZ_TRY(upload(*dev, ws, &d_descs, descs, stream));
+  CZ_TRY(upload(*dev, ws, &d_order, order, stream));
   CZ_TRY(ws.allocate(&counter, 1));
   CZ_TRY(cudaMemsetAsync(counter, 0, sizeof(u32), stream));
   CZ_TRY(launch_serial_inflate(in, out, d_descs, descs[0], u32(count), d_order, counter, meta,

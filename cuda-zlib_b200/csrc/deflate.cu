@@ -42,6 +42,7 @@ constexpr u32 kOwnerBits = 4;  // log2(kEncWarps): hash slots are split over the
 static_assert((1u << kOwnerBits) == kEncWarps, "one slot class per warp");
 constexpr u32 kRing = 256;     // per-warp ring of owned positions (a power of two)
 constexpr u32 kHashSlots = 8192;
+constexpr u32 kStitchRounds = 8;  // parallel stitch rounds before the serial finish
 constexpr u32 kStoredMax = 65535;  // bytes of one stored block
 constexpr u32 kMaxChunkBytes = 262144;  // largest accepted chunk
 
@@ -584,26 +585,55 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
   const u32 my_a = min_u32(tid * seg, n), my_b = min_u32(my_a + seg, n);
   const bool mine = tid < nseg;
   u32 entry = mine && tid ? s.seg_exit[tid - 1] : 0u, merge_at = my_b;
-  for (bool dirty = true;;) {
-    if (mine && dirty) {
-      u32 exit = entry;  // an earlier token covers the whole segment
-      merge_at = my_b;
-      if (entry < my_b) {
-        u32 p = entry;
-        while (p < my_b && !is_member(p)) {
-          const u32 m = token_at(p);
-          p += m ? m : 1u;
-        }
-        merge_at = p;
-        exit = p < my_b ? s.seg_exit[tid] : p;
-      }
-      s.seg_entry[tid] = exit;  // this round's exit
+  // Exit of a segment entered at e (merge point in *merge).
+  auto segment_exit = [&](u32 t, u32 e, u32 a_t, u32 b_t, u32* merge) -> u32 {
+    *merge = b_t;
+    if (e >= b_t) return e;  // an earlier token covers the whole segment
+    u32 p = e;
+    while (p < b_t && !is_member(p)) {
+      const u32 m = token_at(p);
+      p += m ? m : 1u;
     }
+    *merge = p;
+    return p < b_t ? s.seg_exit[t] : p;
+  };
+  u32 rounds = 0;
+  bool unsettled = false;
+  for (bool dirty = true;;) {
+    if (mine && dirty) s.seg_entry[tid] = segment_exit(tid, entry, my_a, my_b, &merge_at);
     __syncthreads();
     const u32 next = mine && tid ? s.seg_entry[tid - 1] : 0u;
     dirty = mine && next != entry;
     entry = next;
+    ++rounds;
     if (!__syncthreads_or(dirty)) break;
+    // Chains that do not re-join for many segments (long runs of one byte)
+    // would cost a round per segment, each re-walking every later segment:
+    // after kStitchRounds rounds the first kStitchRounds entries are exact
+    // and one thread walks the rest in order.
+    if (rounds == kStitchRounds) {
+      unsettled = true;
+      break;
+    }
+  }
+  if (unsettled) {
+    __syncthreads();
+    if (tid == 0) {
+      u32 e = s.seg_entry[kStitchRounds - 1];  // exit of the last exact segment
+      for (u32 t = kStitchRounds; t < nseg; ++t) {
+        const u32 a_t = min_u32(t * seg, n), b_t = min_u32(a_t + seg, n);
+        u32 merge = b_t;
+        const u32 exit = segment_exit(t, e, a_t, b_t, &merge);
+        s.seg_entry[t] = e;
+        s.seg_bits[t] = merge;
+        e = exit;
+      }
+    }
+    __syncthreads();
+    if (mine && tid >= kStitchRounds) {
+      entry = s.seg_entry[tid];
+      merge_at = s.seg_bits[tid];
+    }
   }
   if (mine && tid > 0) {
     if (entry >= my_b) {

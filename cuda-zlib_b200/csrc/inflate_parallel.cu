@@ -1488,8 +1488,15 @@ expand_kernel(const u8* in, u32 in_size, const u32* path, const u32* prefix,
 // once, one lane per bit position, the four chases interleaved so their
 // loads overlap.
 constexpr u32 kResolveWays = 4;
-__global__ void resolve_kernel(const u32* state, u32 words, const u32* unresolved,
-                               const u32* source, u8* out) {
+// Hops a chase may take.  A marker's source lies before its own path node,
+// so every hop moves at least one node back.  Data whose every byte copies
+// from the previous record (long runs of records, zero padding) chains each
+// marker through every earlier node; such a chase stops here, records the
+// position it reached (at least kResolveHops nodes back) in source[], sets
+// its bit in `longs` and raises *deep for the staged pass below.
+constexpr u32 kResolveHops = 32;
+__global__ void resolve_kernel(const u32* state, u32 words, const u32* unresolved, u32* source,
+                               u8* out, u32* longs, u32* deep) {
   if (!state[1]) return;
   const u32 lane = threadIdx.x & 31u;
   const u64 warp = (u64(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
@@ -1497,21 +1504,25 @@ __global__ void resolve_kernel(const u32* state, u32 words, const u32* unresolve
   auto marked = [&](u32 q) { return ((unresolved[q >> 5] >> (q & 31)) & 1u) != 0; };
   for (u64 w0 = warp * 32; w0 < words; w0 += warps * 32) {
     const u32 mine = w0 + lane < words ? unresolved[w0 + lane] : 0u;
+    if (w0 + lane < words && !mine) longs[w0 + lane] = 0;
     for (u32 nonzero = __ballot_sync(kFullMask, mine != 0); nonzero;) {
-      u32 at[kResolveWays], q[kResolveWays];
-      bool live[kResolveWays];
+      u32 at[kResolveWays], q[kResolveWays], word[kResolveWays];
+      bool live[kResolveWays], has[kResolveWays];
 #pragma unroll
       for (u32 k = 0; k < kResolveWays; ++k) {
         const u32 i = nonzero ? __ffs(nonzero) - 1 : 0u;
         const u32 bits = __shfl_sync(kFullMask, mine, i);
-        live[k] = nonzero && ((bits >> lane) & 1u);
+        has[k] = nonzero != 0;
+        live[k] = has[k] && ((bits >> lane) & 1u);
         nonzero &= nonzero - 1;
-        at[k] = u32(w0 + i) * 32 + lane;
+        word[k] = u32(w0) + i;
+        at[k] = word[k] * 32 + lane;
         q[k] = live[k] ? source[at[k]] : 0u;
       }
       // Sources strictly decrease along a chase, so each ends at a position
-      // that emission wrote directly.
-      for (bool more = true; more;) {
+      // that emission wrote directly, unless it runs out of hops.
+      bool more = true;
+      for (u32 hop = 0; more && hop < kResolveHops; ++hop) {
         bool step[kResolveWays];
 #pragma unroll
         for (u32 k = 0; k < kResolveWays; ++k) step[k] = live[k] && marked(q[k]);
@@ -1524,9 +1535,110 @@ __global__ void resolve_kernel(const u32* state, u32 words, const u32* unresolve
           }
         }
       }
+      // A chase reading source[] while another warp shortens it follows
+      // either value: both are positions of the same chain.
+      bool any_long = false;
 #pragma unroll
-      for (u32 k = 0; k < kResolveWays; ++k)
-        if (live[k]) out[at[k]] = out[q[k]];
+      for (u32 k = 0; k < kResolveWays; ++k) {
+        const bool is_long = live[k] && marked(q[k]);
+        if (is_long) source[at[k]] = q[k];
+        else if (live[k]) out[at[k]] = out[q[k]];
+        const u32 ballot = __ballot_sync(kFullMask, is_long);
+        if (has[k] && lane == 0) longs[word[k]] = ballot;
+        any_long |= ballot != 0;
+      }
+      if (any_long && lane == 0) atomicOr(deep, 1u);
+    }
+  }
+}
+
+// After resolve_kernel raised *deep: the long markers, in stages of
+// kResolveHops consecutive path nodes.  A long marker of path node i reads
+// source[] = a position in node i - kResolveHops or earlier, which is either
+// final since resolve_kernel or a long marker of an earlier stage, so the
+// markers of one stage resolve in parallel once every earlier stage is done.
+// CTAs take (stage, tile) tickets in order; a tile waits for its previous
+// stage's kStageTiles tiles.  Every earlier ticket belongs to a running CTA
+// that waits only on even earlier ones, so the waits end; each is bounded
+// anyway and sets *fail when it gives up.  Output bytes written in this
+// kernel are read with L2-coherent loads (ld.global.cg).
+constexpr u32 kStageThreads = 256;
+constexpr u32 kStageWaitLimit = 1u << 22;  // polls of ~256 ns: about a second
+__global__ void __launch_bounds__(kStageThreads)
+stage_resolve_kernel(const u32* state, const u32* prefix, u32 expected, const u32* longs,
+                     const u32* source, u8* out, u32 tiles_per_stage, u32* stage_done,
+                     u32* ticket, u32* fail, const u32* deep) {
+  __shared__ u32 s_ticket, s_go;
+  if (!state[1] || !*deep) return;
+  const u32 len = state[0];
+  const u32 stages = (len + kResolveHops - 1) / kResolveHops;
+  const u64 total = u64(stages) * tiles_per_stage;
+  const bool vec = (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
+  for (;;) {
+    if (threadIdx.x == 0) {
+      const u32 t = atomicAdd(ticket, 1u);
+      u32 go = t < total;
+      if (go && t >= tiles_per_stage) {
+        const u32* done = stage_done + (t / tiles_per_stage - 1);
+        for (u32 polls = 0;; ++polls) {
+          if (*reinterpret_cast<volatile const u32*>(done) >= tiles_per_stage) break;
+          if (*reinterpret_cast<volatile const u32*>(fail) || polls >= kStageWaitLimit) {
+            atomicOr(fail, 1u);
+            go = 0;
+            break;
+          }
+          __nanosleep(256);
+        }
+        __threadfence();
+      }
+      s_ticket = t;
+      s_go = go;
+    }
+    __syncthreads();
+    const u32 t = s_ticket;
+    if (!s_go) return;
+    const u32 stage = t / tiles_per_stage, tile = t % tiles_per_stage;
+    const u32 first = stage * kResolveHops, last = first + kResolveHops;
+    const u32 lo = prefix[first], hi = last < len ? prefix[last] : expected;
+    if (hi > lo) {
+      const u32 w_lo = lo >> 5, w_hi = (hi - 1) / 32 + 1;
+      const u32 per = (w_hi - w_lo + tiles_per_stage - 1) / tiles_per_stage;
+      const u32 a = w_lo + tile * per, b = min_u32(w_hi, a + per);
+      for (u32 w = a + threadIdx.x; w < b; w += kStageThreads) {
+        u32 bits = longs[w];
+        const u32 base = w * 32;
+        if (base < lo) bits &= ~0u << (lo - base);
+        if (hi - base < 32) bits &= (1u << (hi - base)) - 1u;
+        if (!bits) continue;
+        if (vec && base + 32 <= expected) {
+          // The word's 32 bytes in two 16-byte halves: read, patch the
+          // long markers, write back (bytes outside the stage are final or
+          // rewritten unchanged; nothing else writes them meanwhile).
+          const uint4 h0 = __ldcg(reinterpret_cast<const uint4*>(out + base));
+          const uint4 h1 = __ldcg(reinterpret_cast<const uint4*>(out + base + 16));
+          u32 v[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+          for (u32 i = 0; i < 32; ++i) {
+            if ((bits >> i) & 1u) {
+              const u32 byte = __ldcg(reinterpret_cast<const unsigned char*>(out + source[base + i]));
+              const u32 shift = 8 * (i & 3);
+              v[i >> 2] = (v[i >> 2] & ~(0xffu << shift)) | (byte << shift);
+            }
+          }
+          reinterpret_cast<uint4*>(out + base)[0] = make_uint4(v[0], v[1], v[2], v[3]);
+          reinterpret_cast<uint4*>(out + base)[1] = make_uint4(v[4], v[5], v[6], v[7]);
+        } else {
+          for (u32 m = bits; m; m &= m - 1) {
+            const u32 i = __ffs(m) - 1;
+            out[base + i] = u8(__ldcg(reinterpret_cast<const unsigned char*>(out + source[base + i])));
+          }
+        }
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      atomicAdd(stage_done + stage, 1u);
     }
   }
 }
@@ -1736,6 +1848,7 @@ ParallelScratch parallel_scratch_layout(u64 in_size, u64 expected, u32 capacity,
   s.node_capacity = s.capacity + 2 * s.tiles;
   s.levels = chain_levels(s.node_capacity);
   s.out_words = (expected + 31) / 32 + 1;
+  s.stages = (s.node_capacity + kResolveHops - 1) / kResolveHops + 1;
   s.segments = u32((expected + kAdlerSegment - 1) / kAdlerSegment);
   // Path tokens of a chain that passes its checks: at most one per output
   // byte, plus two words per stored block (at most kMaxBlocks blocks).
@@ -1808,7 +1921,13 @@ cudaError_t launch_parallel_inflate(const u8* in, u64 in_size, u8* out, u64 expe
   profile_begin("resolve_kernel", stream);
   note_launch();
   resolve_kernel<<<u32(dev.sms) * 8, 256, 0, stream>>>(b.state, u32(s.out_words), b.unresolved,
-                                                       b.source, out);
+                                                       b.source, out, b.longs, b.deep);
+  profile_end(stream);
+  profile_begin("stage_resolve_kernel", stream);
+  note_launch();
+  stage_resolve_kernel<<<u32(dev.sms) * 2, kStageThreads, 0, stream>>>(
+      b.state, b.prefix, u32(expected), b.longs, b.source, out, u32(dev.sms) * 2, b.stage_done,
+      b.stage_done + s.stages, b.fail, b.deep);
   profile_end(stream);
   if (s.segments) {
     note_launch();

@@ -98,6 +98,7 @@ struct ParallelScratch {
   u32 segments;       // Adler-32 segments of the output
   u64 symbol_words;   // contiguous token layout of the path nodes
   u32 pages;          // token arena pages (1024 words each, at least symbol_words)
+  u32 stages;         // staged-resolve stages (32 path nodes each) over node_capacity
 };
 struct ParallelBuffers {
   u32* bitmap;        // bitmap_words, from discover_kernel (the reference's rule)
@@ -116,10 +117,13 @@ struct ParallelBuffers {
   u32* syms;          // pages * 1024 words: the token arena
   u32 *first_page, *page_next, *page_used;  // node_capacity, pages, pages
   u32* page_cursor;   // 1, zeroed: next free arena page
-  u32* source;        // expected: absolute source of unresolved positions
+  u32* source;        // expected + 32: absolute source of unresolved positions
   u32* unresolved;    // out_words, zeroed
   u64* parts;         // 2 * segments
   u32* fail;          // 1, zeroed
+  u32* deep;          // 1, zeroed: some marker chain is too long to chase
+  u32* longs;         // out_words: markers whose chase ran out of hops
+  u32* stage_done;    // stages + 1, zeroed: tiles done per stage, then the ticket
   u32* stash;         // round_stash_words: tokens the node warps keep per round
 };
 ParallelScratch parallel_scratch_layout(u64 in_size, u64 expected, u32 capacity,

@@ -317,15 +317,19 @@ def _batch_sizes(sizes, label):
 
 
 def _batch_capacities(sizes, chunk_bytes):
+    """Padded slot sizes of a batch (_layout per file, vectorised)."""
     _check_chunk(chunk_bytes)
-    layouts = tuple(_layout(size, chunk_bytes) for size in sizes)
-    if (sum(chunks for _, chunks, _ in layouts) > _MAX_BLOCKS or
-            any(blocks > _MAX_BLOCKS for _, _, blocks in layouts)):
+    sizes = np.asarray(sizes, dtype=np.int64)
+    chunks = np.maximum(1, -(-sizes // chunk_bytes))
+    full = max(1, -(-chunk_bytes // _STORED_MAX))
+    tail = np.maximum(1, -(-(sizes - (chunks - 1) * chunk_bytes) // _STORED_MAX))
+    blocks = (chunks - 1) * max(full, 2) + tail
+    if int(chunks.sum()) > _MAX_BLOCKS or (blocks.size and int(blocks.max()) > _MAX_BLOCKS):
         raise ValueError("batch chunk count exceeds workspace limit")
-    capacities = tuple(capacity for capacity, _, _ in layouts)
-    if sum(capacities) > _MAX_BYTES:
+    capacities = sizes + 5 * ((chunks - 1) * full + tail) + 6
+    if int(capacities.sum()) > _MAX_BYTES:
         raise ValueError("batch compressed capacity exceeds 2**28 bytes")
-    return capacities
+    return tuple(capacities.tolist())
 
 
 def _i64_array(values):
