@@ -23,7 +23,7 @@ BUILD = os.path.join(HERE, "_build")
 LIBRARY = os.path.join(HERE, "cuda_zlib", "libcuda_zlib_b200.so")
 FFI = os.path.join(HERE, "ffi")
 XLA_LIBRARY = os.path.join(HERE, "cuda_zlib", "libcuda_zlib_xla.so")
-SOURCES = ["codec.cu", "deflate.cu", "inflate_serial.cu", "inflate_general.cu",
+SOURCES = ["codec.cu", "deflate.cu", "inflate_serial.cu", "inflate_general.cu", "crc32.cu",
            "inflate_parallel.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",

@@ -41,8 +41,10 @@ constexpr int64_t kMaxChunk = 262144;
 constexpr u32 kStoredMax = 65535;
 constexpr u32 kMaxBlocks = 262144;
 constexpr u32 kMaxCandidates = 262144;
+constexpr u32 kTruncated = 1;
 constexpr u32 kTruncatedZlib = 14;
 constexpr u32 kInvalidBounds = 23;
+constexpr u32 kGzipHeader = 24;
 constexpr int kMaxDevices = 64;
 
 #define CZ_TRY(expression)                     \
@@ -491,7 +493,8 @@ cudaError_t compress_batch(const u8* in, u64 in_bytes, const int64_t* sizes, u64
 }
 
 cudaError_t decompress(const u8* in, u64 size, int64_t max_candidates, int64_t max_blocks,
-                       u8* out, u64 expected, u32* meta, cudaStream_t stream) {
+                       u8* out, u64 expected, u32* meta, cudaStream_t stream,
+                       bool checksum = true) {
   if (!meta) return cudaErrorInvalidValue;
   DeviceScope scope(stream);
   CZ_TRY(scope.error());
@@ -520,7 +523,7 @@ cudaError_t decompress(const u8* in, u64 size, int64_t max_candidates, int64_t m
   if (expected <= 65536 && size <= 131072 && defaults) {
     // Small route: serial semantics (codec_ffi.cu:681-695).
     CZ_TRY(launch_serial_inflate(in, out, nullptr, single, 1, nullptr, counter, meta, nullptr,
-                                 u32(max_blocks), dev->info, stream));
+                                 u32(max_blocks), dev->info, stream, checksum));
     return ws.release();
   }
   // General route: candidate discovery (always: its count alone can fail a
@@ -583,9 +586,148 @@ cudaError_t decompress(const u8* in, u64 size, int64_t max_candidates, int64_t m
   CZ_TRY(launch_discover(in, size, b.bitmap, b.extra, count, queue, queue_cap, queued, nullptr,
                          dev->info, stream));
   CZ_TRY(launch_parallel_inflate(in, size, out, expected, u32(max_blocks), layout, b, meta,
-                                 dev->info, stream));
+                                 dev->info, stream, checksum));
   CZ_TRY(launch_general_status(in, size, expected, u32(max_candidates), u32(max_blocks), b.bitmap,
                                count, meta, out, stream));
+  return ws.release();
+}
+
+// ---------------------------------------------------------------------------
+// gzip (RFC 1952) and raw Deflate (RFC 1951) wrappers around the same body
+// codec.  The reference supports RFC 1950 only; these are this codec's.
+// ---------------------------------------------------------------------------
+enum Format : int32_t { kFormatZlib = 0, kFormatRaw = 1, kFormatGzip = 2 };
+
+// Wrapper bytes of a member around its Deflate body.
+u64 wrapper_bytes(int32_t format) {
+  return format == kFormatRaw ? 0 : format == kFormatGzip ? 18 : 6;
+}
+
+// Bitwise CRC-32 for the few bytes of a gzip header (FHCRC).
+u32 host_crc32(const u8* p, u64 n) {
+  u32 r = 0xFFFFFFFFu;
+  for (u64 i = 0; i < n; ++i) {
+    r ^= p[i];
+    for (int k = 0; k < 8; ++k) r = (r >> 1) ^ ((r & 1u) ? 0xEDB88320u : 0u);
+  }
+  return r ^ 0xFFFFFFFFu;
+}
+
+// Length of the gzip member header at host bytes [0, available): magic,
+// CM = 8, no reserved flag bits, the optional FEXTRA / FNAME / FCOMMENT
+// fields and, with FHCRC, the header CRC-16.  0 when valid and complete,
+// else kGzipHeader.
+u32 gzip_header(const u8* p, u64 available, u64* header_bytes) {
+  *header_bytes = 0;
+  if (!p || available < 10 || p[0] != 0x1f || p[1] != 0x8b || p[2] != 8 || (p[3] & 0xe0))
+    return kGzipHeader;
+  const u32 flags = p[3];
+  u64 at = 10;
+  if (flags & 4) {  // FEXTRA: XLEN, then XLEN bytes
+    if (available < at + 2) return kGzipHeader;
+    at += 2 + (u64(p[at]) | (u64(p[at + 1]) << 8));
+  }
+  for (u32 field : {8u, 16u}) {  // FNAME, FCOMMENT: zero-terminated
+    if (!(flags & field)) continue;
+    while (at < available && p[at]) ++at;
+    if (at >= available) return kGzipHeader;
+    ++at;
+  }
+  if (flags & 2) {  // FHCRC: the low 16 bits of the CRC-32 of the bytes before
+    if (available < at + 2) return kGzipHeader;
+    const u32 want = u32(p[at]) | (u32(p[at + 1]) << 8);
+    if ((host_crc32(p, at) & 0xffffu) != want) return kGzipHeader;
+    at += 2;
+  }
+  if (at > available) return kGzipHeader;
+  *header_bytes = at;
+  return 0;
+}
+
+cudaError_t compress_format(const u8* in, u64 size, int64_t chunk_bytes, int32_t format, u8* out,
+                            u64 capacity, u32* meta, cudaStream_t stream) {
+  if (format == kFormatZlib) return compress(in, size, chunk_bytes, out, capacity, meta, stream);
+  if (!meta || (format != kFormatRaw && format != kFormatGzip)) return cudaErrorInvalidValue;
+  DeviceScope scope(stream);
+  CZ_TRY(scope.error());
+  DeviceState* dev = nullptr;
+  CZ_TRY(device_state(scope.device(), &dev));
+  // compress()'s order: output bound, zero, input and chunk bounds.
+  const u64 wrap = wrapper_bytes(format);
+  if (capacity > kMaxStreamBytes + 5 * stored_blocks(kMaxStreamBytes) + wrap)
+    return set_meta(meta, 0, kInvalidBounds, stream);
+  if (capacity) {
+    if (!out) return cudaErrorInvalidValue;
+    CZ_TRY(cudaMemsetAsync(out, 0, capacity, stream));
+  }
+  if (size > kMaxStreamBytes || !chunk_ok(chunk_bytes) || (size && !in))
+    return set_meta(meta, 0, kInvalidBounds, stream);
+  const u32 chunk = u32(chunk_bytes);
+  const StreamLayout l = stream_layout(size, chunk);
+  if (l.blocks > kMaxBlocks || capacity != l.capacity - 6 + wrap)
+    return set_meta(meta, 0, kInvalidBounds, stream);
+  std::vector<EncodeFile> files(1);
+  files[0] = EncodeFile{0, size, 0, capacity, 0, u32(l.chunks), chunk,
+                        format == kFormatRaw ? kEncodeRaw : kEncodeGzip};
+  if (format == kFormatRaw)
+    return encode_files(*dev, in, size, files, chunk, u32(l.chunks), out, meta, stream);
+  Workspace ws(dev->pool, stream);
+  u32 *parts = nullptr, *crc = nullptr;
+  CZ_TRY(ws.allocate(&parts, std::max<u32>(1, crc_segments(size))));
+  CZ_TRY(ws.allocate(&crc, 1));
+  CZ_TRY(launch_crc32(in, size, parts, crc, dev->info, stream));
+  CZ_TRY(encode_files(*dev, in, size, files, chunk, u32(l.chunks), out, meta, stream));
+  CZ_TRY(launch_gzip_trailer(out, meta, crc, size, stream));
+  return ws.release();
+}
+
+// A raw body or a gzip member decodes as the body of a zlib-framed copy in
+// scratch (two header bytes before it, four after) with the Adler-32 check
+// off; a gzip member then checks CRC-32 and ISIZE on the output.
+cudaError_t decompress_format(const u8* in, u64 size, int32_t format, u64 header_bytes,
+                              int64_t max_candidates, int64_t max_blocks, u8* out, u64 expected,
+                              u32* meta, cudaStream_t stream) {
+  if (format == kFormatZlib)
+    return decompress(in, size, max_candidates, max_blocks, out, expected, meta, stream);
+  if (!meta || (format != kFormatRaw && format != kFormatGzip)) return cudaErrorInvalidValue;
+  DeviceScope scope(stream);
+  CZ_TRY(scope.error());
+  DeviceState* dev = nullptr;
+  CZ_TRY(device_state(scope.device(), &dev));
+  if (expected > kMaxStreamBytes) return set_meta(meta, kInvalidBounds, 0, stream);
+  if (expected && !out) return cudaErrorInvalidValue;
+  auto fail = [&](u32 status) -> cudaError_t {
+    if (expected) CZ_TRY(cudaMemsetAsync(out, 0, expected, stream));
+    return set_meta(meta, status, 0, stream);
+  };
+  const u64 wrap = wrapper_bytes(format);
+  if (size > kMaxStreamInput - 6 + wrap) return fail(kInvalidBounds);
+  u64 head = 0, body = size;
+  if (format == kFormatGzip) {
+    if (header_bytes < 10 || size < header_bytes + 8) return fail(kGzipHeader);
+    head = header_bytes;
+    body = size - header_bytes - 8;
+  }
+  // A complete Deflate body has at least two bytes (an empty fixed block).
+  if (body < 2) return fail(kTruncated);
+  if (!in) return cudaErrorInvalidValue;
+  Workspace ws(dev->pool, stream);
+  u8* view = nullptr;
+  CZ_TRY(ws.allocate(&view, body + 6 + 64));
+  CZ_TRY(cudaMemsetAsync(view, 0x78, 1, stream));
+  CZ_TRY(cudaMemsetAsync(view + 1, 0x9c, 1, stream));
+  CZ_TRY(cudaMemcpyAsync(view + 2, in + head, body, cudaMemcpyDeviceToDevice, stream));
+  CZ_TRY(cudaMemsetAsync(view + 2 + body, 0, 4 + 64, stream));
+  CZ_TRY(decompress(view, body + 6, max_candidates, max_blocks, out, expected, meta, stream,
+                    false));
+  if (format == kFormatGzip) {
+    u32 *parts = nullptr, *crc = nullptr;
+    CZ_TRY(ws.allocate(&parts, std::max<u32>(1, crc_segments(expected))));
+    CZ_TRY(ws.allocate(&crc, 1));
+    CZ_TRY(launch_crc32(out, expected, parts, crc, dev->info, stream));
+    CZ_TRY(launch_gzip_check(in, size, expected, crc, meta, stream));
+    CZ_TRY(launch_clear_on_failure(meta, out, expected, stream));
+  }
   return ws.release();
 }
 
@@ -687,6 +829,35 @@ int cuda_zlib_decompress(const uint8_t* input, uint64_t size, int64_t max_candid
   } catch (...) {
     return int(cudaErrorUnknown);
   }
+}
+
+int cuda_zlib_compress_format(const uint8_t* input, uint64_t size, int64_t chunk_bytes,
+                              int32_t format, uint8_t* output, uint64_t capacity,
+                              uint32_t* metadata, void* stream) {
+  try {
+    return int(cz::compress_format(input, size, chunk_bytes, format, output, capacity, metadata,
+                                   static_cast<cudaStream_t>(stream)));
+  } catch (...) {
+    return int(cudaErrorUnknown);
+  }
+}
+
+int cuda_zlib_decompress_format(const uint8_t* input, uint64_t size, int32_t format,
+                                uint64_t header_bytes, int64_t max_candidates,
+                                int64_t max_blocks, uint8_t* output, uint64_t expected,
+                                uint32_t* metadata, void* stream) {
+  try {
+    return int(cz::decompress_format(input, size, format, header_bytes, max_candidates,
+                                     max_blocks, output, expected, metadata,
+                                     static_cast<cudaStream_t>(stream)));
+  } catch (...) {
+    return int(cudaErrorUnknown);
+  }
+}
+
+int cuda_zlib_gzip_header(const uint8_t* bytes, uint64_t available, uint64_t* header_bytes) {
+  if (!header_bytes) return int(cz::kGzipHeader);
+  return int(cz::gzip_header(bytes, available, header_bytes));
 }
 
 int cuda_zlib_compress_batch(const uint8_t* input, uint64_t input_bytes,

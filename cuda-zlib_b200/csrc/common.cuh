@@ -44,6 +44,10 @@ enum Status : u32 {
   kAdlerMismatch = 21,
   kCompressionOverflow = 22,
   kInvalidBounds = 23,
+  // gzip wrapper (this codec only; the reference rejects gzip with 16).
+  kGzipHeader = 24,
+  kGzipCrcMismatch = 25,
+  kGzipSizeMismatch = 26,
 };
 
 constexpr u32 kFullMask = 0xffffffffu;

@@ -987,7 +987,9 @@ encode_finish_kernel(const EncodeFile* files, u32 nfiles, const u32* sizes, cons
   const u32 f = blockIdx.x;
   if (f >= nfiles) return;
   const EncodeFile file = files[f];
-  const bool raw = (file.flags & kEncodeRaw) != 0;
+  const bool raw = (file.flags & kEncodeRaw) != 0, gzip = (file.flags & kEncodeGzip) != 0;
+  // Wrapper bytes before and after the body: zlib 2 + 4, gzip 10 + 8, raw none.
+  const u32 head = raw ? 0 : gzip ? 10 : 2, tail = raw ? 0 : gzip ? 8 : 4;
   const u32 per = (file.chunks + kFinishWarps - 1) / kFinishWarps;
   const u32 c0 = min_u32(warp * per, file.chunks), c1 = min_u32(c0 + per, file.chunks);
   u64 bytes = 0, s1 = 0, s2 = 0;
@@ -1015,7 +1017,7 @@ encode_finish_kernel(const EncodeFile* files, u32 nfiles, const u32* sizes, cons
     part_bad[warp] = bad;
   }
   __syncthreads();
-  u64 running = raw ? 0 : 2;  // after the two-byte zlib header
+  u64 running = head;
   for (u32 w = 0; w < warp; ++w) running += part_bytes[w];
   for (u32 base = c0; base < c1; base += 32) {
     const u32 c = base + lane;
@@ -1037,13 +1039,18 @@ encode_finish_kernel(const EncodeFile* files, u32 nfiles, const u32* sizes, cons
       t2 += part_s2[w];
       any_bad |= part_bad[w];
     }
-    const u64 total = body + (raw ? 0 : 6);
+    const u64 total = body + head + tail;
     u32 st = any_bad ? u32(kCompressionOverflow) : 0u;
     if (!st && total > file.capacity) st = kCompressionOverflow;
     u8* dst = out + file.out_offset;
     const u32 checksum = adler_finish(t1, t2, file.in_size);
     if (range_adler) range_adler[f] = st ? 0u : checksum;
-    if (!st && !raw) {
+    if (!st && gzip) {
+      // ID1 ID2 CM=8 FLG=0 MTIME=0 XFL=0 OS=255 (unknown); the trailer
+      // (CRC-32, ISIZE) comes from launch_gzip_trailer.
+      const u8 header[10] = {0x1f, 0x8b, 8, 0, 0, 0, 0, 0, 0, 0xff};
+      for (u32 i = 0; i < 10; ++i) dst[i] = header[i];
+    } else if (!st && !raw) {
       dst[0] = 0x78;
       dst[1] = 0x01;
       dst[total - 4] = u8(checksum >> 24);

@@ -13,8 +13,8 @@
 //     (discover, _decode_kernels.py:998-1054), always run, because a count
 //     above the capacity fails even a valid stream with status 18;
 //   * general_status_kernel: one thread restating the chain walk and the
-//     emission history check, run only after the fast path failed, to report
-//     the status the reference's route reports.
+//     emission history check, run only after the fast path failed before
+//     its checksum, to report the status the reference's route reports.
 #include <algorithm>
 
 #include "kernels.h"
@@ -735,6 +735,10 @@ __global__ void general_status_kernel(const u8* in, u64 in_size, u64 expected, u
     if (*count > capacity) status = kCandidateOverflow;
     else if (!*count) status = kInitialBlockMissing;
   }
+  // A fast path that reached the checksum accepted the chain and its history
+  // with the reference's checks (the trailer plays no part in them), so the
+  // route's status is the checksum's: no replay.
+  if (!status && fast == kAdlerMismatch) status = kAdlerMismatch;
   if (!status && fast) {
     const u8* body = in + 2;
     const u64 bytes = in_size - 6;
@@ -746,8 +750,7 @@ __global__ void general_status_kernel(const u8* in, u64 in_size, u64 expected, u
     if (status == kFixedTiles)
       status = chain_walk(body, bytes, bitmap, u32(expected), max_blocks, true, sh.fixed, sh.dyn);
     if (!status) status = history_walk(body, bytes, window, sh.fixed, sh.dyn);
-    // An accepted chain with valid history fails only on its checksum.
-    if (!status) status = fast == kAdlerMismatch ? u32(kAdlerMismatch) : fast;
+    if (!status) status = fast;
   }
   meta[0] = status;
   meta[1] = 0;
@@ -799,14 +802,16 @@ cudaError_t launch_general_status(const u8* in, u64 in_size, u64 expected, u32 m
                                               bitmap, count, meta);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  if (expected) {
-    u64 blocks = (expected + 255) / 256;
-    if (blocks > 4096) blocks = 4096;
-    note_launch();
-    clear_on_failure_kernel<<<u32(blocks), 256, 0, stream>>>(meta, out, expected);
-    e = cudaGetLastError();
-  }
-  return e;
+  return launch_clear_on_failure(meta, out, expected, stream);
+}
+
+cudaError_t launch_clear_on_failure(const u32* meta, u8* out, u64 expected, cudaStream_t stream) {
+  if (!expected) return cudaSuccess;
+  u64 blocks = (expected + 255) / 256;
+  if (blocks > 4096) blocks = 4096;
+  note_launch();
+  clear_on_failure_kernel<<<u32(blocks), 256, 0, stream>>>(meta, out, expected);
+  return cudaGetLastError();
 }
 
 }  // namespace cz

@@ -1696,13 +1696,13 @@ __global__ void adler_parts_kernel(const u32* state, const u8* out, u32 n, u64* 
 // Fast-path verdict into meta[0] (0 or 1), for general_status_kernel.
 __global__ void parallel_finish_kernel(const u8* in, u32 in_size, const u32* state,
                                        const u32* fail_flag, const u64* parts, u32 segments,
-                                       u32 n, u32* meta) {
+                                       u32 n, u32 checksum, u32* meta) {
   __shared__ u64 a1[32], a2[32];
   u32 window = 0, wanted = 0;
   const bool framed = zlib_framing(in, in_size, &window, &wanted) == 0;
   const bool ok = framed && state[1] && !*fail_flag;
   u64 s1 = 0, s2 = 0;
-  if (ok) {
+  if (ok && checksum) {
     for (u32 s = threadIdx.x; s < segments; s += blockDim.x) {
       const u32 end = min_u32((s + 1) * kAdlerSegment, n);
       const u64 after = (n - end) % kAdlerMod;
@@ -1722,7 +1722,7 @@ __global__ void parallel_finish_kernel(const u8* in, u32 in_size, const u32* sta
     u64 t1 = 0, t2 = 0;
     for (u32 w = 0; w < blockDim.x / 32; ++w) { t1 += a1[w]; t2 += a2[w]; }
     u32 status = 1;
-    if (ok) status = adler_finish(t1, t2, n) == wanted ? 0u : u32(kAdlerMismatch);
+    if (ok) status = !checksum || adler_finish(t1, t2, n) == wanted ? 0u : u32(kAdlerMismatch);
     meta[0] = status;
     meta[1] = 0;
   }
@@ -1870,7 +1870,7 @@ u64 round_stash_words(const DeviceInfo& dev) {
 cudaError_t launch_parallel_inflate(const u8* in, u64 in_size, u8* out, u64 expected,
                                     u32 max_blocks, const ParallelScratch& s,
                                     const ParallelBuffers& b, u32* meta, const DeviceInfo& dev,
-                                    cudaStream_t stream) {
+                                    cudaStream_t stream, bool checksum) {
   const Tables* fixed = static_cast<const Tables*>(dev.fixed_tables);
   note_launch();
   seed_probe_kernel<<<(s.tiles + 255) / 256, 256, 0, stream>>>(in, in_size, fixed, s.tiles,
@@ -1929,13 +1929,14 @@ cudaError_t launch_parallel_inflate(const u8* in, u64 in_size, u8* out, u64 expe
       b.state, b.prefix, u32(expected), b.longs, b.source, out, u32(dev.sms) * 2, b.stage_done,
       b.stage_done + s.stages, b.fail, b.deep);
   profile_end(stream);
-  if (s.segments) {
+  if (s.segments && checksum) {
     note_launch();
     adler_parts_kernel<<<s.segments, 256, 0, stream>>>(b.state, out, u32(expected), b.parts);
   }
   note_launch();
   parallel_finish_kernel<<<1, 1024, 0, stream>>>(in, u32(in_size), b.state, b.fail, b.parts,
-                                                 s.segments, u32(expected), meta);
+                                                 s.segments, u32(expected), checksum ? 1u : 0u,
+                                                 meta);
   return cudaGetLastError();
 }
 

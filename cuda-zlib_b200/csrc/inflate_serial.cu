@@ -98,7 +98,8 @@ __device__ void warp_fill_zero(u8* out, u64 n) {
 // flushed` stays below kFlushBytes + 258, so every byte older than the ring
 // is already in global memory when a far match reads it.
 __device__ u32 warp_inflate_one(const u8* in, u64 in_size64, u8* out, u64 out_size64,
-                                u32 max_blocks, const Tables& fixed, Tables& dyn, u8* ring) {
+                                u32 max_blocks, bool checksum, const Tables& fixed, Tables& dyn,
+                                u8* ring) {
   const u32 lane = threadIdx.x & 31u;
   if (in_size64 > kMaxBytes || out_size64 > kMaxBytes || !max_blocks || max_blocks > kMaxBlocks)
     return kInvalidBounds;
@@ -301,7 +302,7 @@ __device__ u32 warp_inflate_one(const u8* in, u64 in_size64, u8* out, u64 out_si
       s1 += __shfl_xor_sync(kFullMask, s1, o);
       s2 += __shfl_xor_sync(kFullMask, s2, o);
     }
-    if (adler_finish(s1, s2, out_size) != wanted) error = kAdlerMismatch;
+    if (checksum && adler_finish(s1, s2, out_size) != wanted) error = kAdlerMismatch;
   }
   return error;
 }
@@ -309,7 +310,7 @@ __device__ u32 warp_inflate_one(const u8* in, u64 in_size64, u8* out, u64 out_si
 __global__ void __launch_bounds__(kSerialWarps * 32)
 serial_inflate_kernel(const u8* in, u8* out, const StreamDesc* descs, StreamDesc single,
                       u32 count, const u32* order, u32* next, u32* meta, const u32* encoded,
-                      u32 max_blocks, const Tables* fixed) {
+                      u32 max_blocks, u32 checksum, const Tables* fixed) {
   extern __shared__ __align__(16) u8 smem_raw[];
   SerialShared& sh = *reinterpret_cast<SerialShared*>(smem_raw);
   const u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
@@ -333,7 +334,7 @@ serial_inflate_kernel(const u8* in, u8* out, const StreamDesc* descs, StreamDesc
     }
     if (!status)
       status = warp_inflate_one(in + d.in_offset, in_size, out + d.out_offset, d.out_size,
-                                max_blocks, *fixed, sh.dyn[warp], sh.ring[warp]);
+                                max_blocks, checksum != 0, *fixed, sh.dyn[warp], sh.ring[warp]);
     // A failed stream publishes an all-zero output.
     if (status && d.out_size <= kMaxBytes) warp_fill_zero(out + d.out_offset, d.out_size);
     if (lane == 0) {
@@ -356,7 +357,7 @@ cudaError_t configure_serial_inflate(int* per_sm) {
 cudaError_t launch_serial_inflate(const u8* in, u8* out, const StreamDesc* descs,
                                   const StreamDesc& single, u32 count, const u32* order, u32* next,
                                   u32* meta, const u32* encoded, u32 max_blocks,
-                                  const DeviceInfo& dev, cudaStream_t stream) {
+                                  const DeviceInfo& dev, cudaStream_t stream, bool checksum) {
   const size_t smem = sizeof(SerialShared);
   u32 grid = u32(dev.sms) * u32(dev.serial_per_sm > 0 ? dev.serial_per_sm : 1);
   const u32 needed = (count + kSerialWarps - 1) / kSerialWarps;
@@ -365,7 +366,7 @@ cudaError_t launch_serial_inflate(const u8* in, u8* out, const StreamDesc* descs
   profile_begin("serial_inflate_kernel", stream);
   note_launch();
   serial_inflate_kernel<<<grid, kSerialWarps * 32, smem, stream>>>(
-      in, out, descs, single, count, order, next, meta, encoded, max_blocks,
+      in, out, descs, single, count, order, next, meta, encoded, max_blocks, checksum ? 1u : 0u,
       static_cast<const Tables*>(dev.fixed_tables));
   profile_end(stream);
   return cudaGetLastError();

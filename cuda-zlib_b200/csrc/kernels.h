@@ -47,6 +47,24 @@ struct EncodeFile {
 // nonfinal (the stream continues) and/or omits the zlib header and trailer.
 constexpr uint32_t kEncodeNotLast = 1u;
 constexpr uint32_t kEncodeRaw = 2u;
+// A gzip member: the 10-byte header before the body; launch_gzip_trailer
+// writes the 8-byte trailer (the capacity counts 18 wrapper bytes).
+constexpr uint32_t kEncodeGzip = 4u;
+
+// CRC-32 (gzip) over a device buffer (crc32.cu).  parts: crc_segments(n)
+// words of scratch; crc: the result, written on the stream.
+constexpr u32 kCrcSegment = 65536;
+u32 crc_segments(u64 n);
+cudaError_t launch_crc32(const u8* buf, u64 n, u32* parts, u32* crc, const DeviceInfo& dev,
+                         cudaStream_t stream);
+// Writes CRC-32 and ISIZE into the last 8 bytes of an encoded member whose
+// metadata is [length, status] (nothing when status != 0).
+cudaError_t launch_gzip_trailer(u8* out, const u32* meta, const u32* crc, u64 isize,
+                                cudaStream_t stream);
+// After a member's body decoded with meta[0] == 0: checks its magic bytes,
+// CRC-32 and ISIZE and sets meta[0] to 24, 25 or 26 on a mismatch.
+cudaError_t launch_gzip_check(const u8* member, u64 size, u64 expected, const u32* crc, u32* meta,
+                              cudaStream_t stream);
 
 // Warp-per-stream inflate (serial route semantics).  `next` is a zeroed
 // device counter; `order` (optional) lists stream indices largest first;
@@ -56,7 +74,8 @@ cudaError_t configure_serial_inflate(int* per_sm);
 cudaError_t launch_serial_inflate(const u8* in, u8* out, const StreamDesc* descs,
                                   const StreamDesc& single, u32 count, const u32* order, u32* next,
                                   u32* meta, const u32* encoded, u32 max_blocks,
-                                  const DeviceInfo& dev, cudaStream_t stream);
+                                  const DeviceInfo& dev, cudaStream_t stream,
+                                  bool checksum = true);
 
 // Chunk encoder + device-side finish.  Slots: in_bytes + 96 * (chunks + 2)
 // bytes; `sizes`, `status` per chunk; `adler` 2 u64 per chunk; `offsets` 1 u64
@@ -133,10 +152,11 @@ u64 round_stash_words(const DeviceInfo& dev);
 cudaError_t build_fixed_tables(void** out);
 cudaError_t configure_parallel_inflate(int* emit_per_sm);
 // Writes the fast-path verdict to meta[0]: 0 ok, 21 checksum, 1 other failure.
+// checksum false skips the Adler-32 trailer (a body framed for decoding).
 cudaError_t launch_parallel_inflate(const u8* in, u64 in_size, u8* out, u64 expected,
                                     u32 max_blocks, const ParallelScratch& s,
                                     const ParallelBuffers& b, u32* meta, const DeviceInfo& dev,
-                                    cudaStream_t stream);
+                                    cudaStream_t stream, bool checksum = true);
 
 // General-route status path (single streams outside the small route).
 // bitmap: one bit per body bit offset, zeroed; count: zeroed u32.
@@ -153,5 +173,7 @@ cudaError_t launch_discover(const u8* in, u64 in_size, u32* bitmap, u32* extra, 
 cudaError_t launch_general_status(const u8* in, u64 in_size, u64 expected, u32 max_candidates,
                                   u32 max_blocks, const u32* bitmap, const u32* count, u32* meta,
                                   u8* out, cudaStream_t stream);
+// Zeroes out[0, expected) when meta[0] != 0.
+cudaError_t launch_clear_on_failure(const u32* meta, u8* out, u64 expected, cudaStream_t stream);
 
 }  // namespace cz

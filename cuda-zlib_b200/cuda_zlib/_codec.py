@@ -53,6 +53,7 @@ _MESSAGES = {
     18: "Deflate candidate workspace overflow", 19: "Deflate initial block missing",
     20: "Deflate back-reference depth exceeded", 21: "CUDA Adler32 mismatch",
     22: "CUDA compression workspace overflow", 23: "invalid codec bounds",
+    24: "invalid gzip header", 25: "gzip CRC32 mismatch", 26: "gzip ISIZE mismatch",
 }
 
 

@@ -46,8 +46,19 @@ def _configure(library):
     library.cuda_zlib_compress_range.argtypes = [_u8p, ctypes.c_uint64, ctypes.c_int64,
                                                  ctypes.c_int32, _u8p, ctypes.c_uint64, _u8p,
                                                  ctypes.c_void_p]
+    library.cuda_zlib_compress_format.argtypes = [_u8p, ctypes.c_uint64, ctypes.c_int64,
+                                                  ctypes.c_int32, _u8p, ctypes.c_uint64, _u8p,
+                                                  ctypes.c_void_p]
+    library.cuda_zlib_decompress_format.argtypes = [_u8p, ctypes.c_uint64, ctypes.c_int32,
+                                                    ctypes.c_uint64, ctypes.c_int64,
+                                                    ctypes.c_int64, _u8p, ctypes.c_uint64, _u8p,
+                                                    ctypes.c_void_p]
+    library.cuda_zlib_gzip_header.argtypes = [ctypes.c_void_p, ctypes.c_uint64,
+                                              ctypes.POINTER(ctypes.c_uint64)]
     for name in ("cuda_zlib_compress", "cuda_zlib_decompress", "cuda_zlib_compress_batch",
-                 "cuda_zlib_decompress_batch", "cuda_zlib_compress_range"):
+                 "cuda_zlib_decompress_batch", "cuda_zlib_compress_range",
+                 "cuda_zlib_compress_format", "cuda_zlib_decompress_format",
+                 "cuda_zlib_gzip_header"):
         getattr(library, name).restype = ctypes.c_int
     library.CudaZlibSetWorkspaceRetention.argtypes = [ctypes.c_uint64]
     library.CudaZlibSetWorkspaceRetention.restype = ctypes.c_int

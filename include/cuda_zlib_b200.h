@@ -35,7 +35,8 @@
  * 14 truncated zlib, 15 bad CMF/FLG, 16 gzip, 17 preset dictionary,
  * 18 candidate overflow, 19 initial block missing, 20 reference depth,
  * 21 Adler-32 mismatch, 22 compression overflow, 23 invalid bounds
- * (codec_ffi.cu:51-62).
+ * (codec_ffi.cu:51-62); gzip wrapper only: 24 invalid gzip header,
+ * 25 gzip CRC-32 mismatch, 26 gzip ISIZE mismatch.
  */
 #ifndef CUDA_ZLIB_B200_H
 #define CUDA_ZLIB_B200_H
@@ -96,6 +97,42 @@ int cuda_zlib_decompress_batch(const uint8_t* input, uint64_t input_bytes,
                                const int64_t* input_sizes, const int64_t* output_sizes,
                                uint64_t files, const uint32_t* encoded_metadata, uint8_t* output,
                                uint64_t output_bytes, uint32_t* metadata, void* stream);
+
+/* gzip (RFC 1952) and raw Deflate (RFC 1951) wrappers around the same body
+ * codec.  No counterpart in the reference, which supports RFC 1950 only and
+ * rejects gzip members with status 16 (_codec.py:105-111).
+ * format: 0 zlib (exactly cuda_zlib_compress / cuda_zlib_decompress),
+ * 1 raw Deflate, 2 gzip (one member).  Any other format returns
+ * cudaErrorInvalidValue (1).
+ *
+ * cuda_zlib_compress_format: the zlib stream's body, bare (format 1) or as a
+ * gzip member (format 2: header 1f 8b 08 00, MTIME 0, XFL 0, OS 255, then the
+ * body, CRC-32 and ISIZE).  capacity = size + 5 * S + W with S as for
+ * cuda_zlib_compress and W = 0 (raw) or 18 (gzip); metadata u32[2] =
+ * [encoded_length, status], bounds failures [0, 23] as cuda_zlib_compress. */
+int cuda_zlib_compress_format(const uint8_t* input, uint64_t size, int64_t chunk_bytes,
+                              int32_t format, uint8_t* output, uint64_t capacity,
+                              uint32_t* metadata, void* stream);
+
+/* cuda_zlib_decompress_format: decodes a raw Deflate stream (its final
+ * block ends in its last byte) or one gzip member whose header is
+ * header_bytes long (from cuda_zlib_gzip_header; ignored for formats 0 and
+ * 1).  Same bounds, routes and statuses as cuda_zlib_decompress, except that
+ * the Adler-32 check is replaced by none (raw) or by CRC-32 (25) and ISIZE
+ * (26) checks (gzip); a member shorter than header_bytes + 8 is 24 and a
+ * body shorter than two bytes is 1.  metadata u32[2] = [status, 0]; a failed
+ * output is all zero. */
+int cuda_zlib_decompress_format(const uint8_t* input, uint64_t size, int32_t format,
+                                uint64_t header_bytes, int64_t max_candidates,
+                                int64_t max_blocks, uint8_t* output, uint64_t expected,
+                                uint32_t* metadata, void* stream);
+
+/* Host-side gzip header parse over HOST bytes [0, available): checks the
+ * magic bytes, CM = 8, the reserved flag bits and, with FHCRC, the header
+ * CRC-16, and skips FEXTRA, FNAME and FCOMMENT.  Returns 0 and the header
+ * length in *header_bytes, or 24 (invalid, or not complete within
+ * `available` bytes: pass more of the member). */
+int cuda_zlib_gzip_header(const uint8_t* bytes, uint64_t available, uint64_t* header_bytes);
 
 /* Compression that allocates no device memory.  No counterpart in the
  * reference: it exists for callers that cannot allocate while they run, such

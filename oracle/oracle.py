@@ -160,3 +160,71 @@ def compress_parallel(data, chunk_bytes=32768, threads=None):
     with ThreadPoolExecutor(max_workers=threads or os.cpu_count() or 1) as pool:
         bodies = list(pool.map(encode, range(0, chunks, per)))
     return b"\x78\x01" + b"".join(bodies) + adler32(source).to_bytes(4, "big")
+
+
+# ---------------------------------------------------------------- gzip / raw
+# The reference has no gzip or raw-Deflate path; the checker for this codec's
+# wrappers is the stdlib zlib (the RFC 1950-1952 reference implementation)
+# plus the restatements below.
+GZIP_HEADER = bytes([0x1F, 0x8B, 8, 0, 0, 0, 0, 0, 0, 0xFF])
+CRC_POLY = 0xEDB88320
+
+
+def raw_deflate(data, chunk_bytes=32768):
+    """The codec's raw Deflate stream: the zlib stream's body."""
+    source = _view(data)
+    whole = compress_parallel(source, chunk_bytes) if source.size > (4 << 20) else \
+        compress(source, chunk_bytes)
+    return whole[2:-4]
+
+
+def gzip_member(data, chunk_bytes=32768, crc=None):
+    """The codec's gzip member: fixed header, body, CRC-32, ISIZE (LE)."""
+    import zlib
+    source = _view(data)
+    value = zlib.crc32(source) if crc is None else crc
+    return (GZIP_HEADER + raw_deflate(source, chunk_bytes) + value.to_bytes(4, "little")
+            + (source.size & 0xFFFFFFFF).to_bytes(4, "little"))
+
+
+def _gf2_times_x(v):
+    return (v >> 1) ^ (CRC_POLY if v & 1 else 0)
+
+
+def gf2_mul(a, b):
+    """a * b mod P in the reflected representation (bit 31 is x^0)."""
+    product = 0
+    for k in range(32):
+        if a & (0x80000000 >> k):
+            product ^= b
+        b = _gf2_times_x(b)
+    return product
+
+
+def gf2_shift_bytes(n):
+    """x^(8 n) mod P."""
+    result, power = 0x80000000, 0x00800000
+    while n:
+        if n & 1:
+            result = gf2_mul(result, power)
+        power = gf2_mul(power, power)
+        n >>= 1
+    return result
+
+
+def crc32_segmented(data, segment=65536):
+    """CRC-32 as the GPU computes it: zero-register CRCs of segments (the
+    buffer padded in front to whole segments), combined by shifts, then the
+    initial value and final XOR applied as one shift term."""
+    import zlib
+    source = _view(data)
+    n = source.size
+    segments = -(-n // segment)
+    pad = segments * segment - n
+    reg = 0
+    for s in range(segments):
+        lo, hi = max(0, s * segment - pad), (s + 1) * segment - pad
+        # Zero-register CRC of the piece: crc32 with init 0 and no final XOR.
+        part = zlib.crc32(source[lo:hi], 0xFFFFFFFF) ^ 0xFFFFFFFF
+        reg = gf2_mul(reg, gf2_shift_bytes(segment)) ^ part
+    return reg ^ gf2_mul(0xFFFFFFFF, gf2_shift_bytes(n)) ^ 0xFFFFFFFF

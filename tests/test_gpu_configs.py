@@ -90,6 +90,30 @@ def test_config1_float32_decode_to_pinned_host(codec, samples, level):
     assert np.array_equal(host.view("<f4"), samples.view("<f4"))
 
 
+def test_config1_checksum_mismatch_reports_21_without_replay(codec, samples):
+    """A 64 MiB stream whose only fault is its Adler-32: status 21 (the
+    reference route's status once chain and history pass) and a zeroed
+    output, reported by the block-parallel path without a serial replay of
+    the stream (which takes seconds at this size)."""
+    import time
+    import torch
+    payload = bytearray(workloads.zlib_stream(samples.tobytes(), 6))
+    payload[-1] ^= 0x40
+    dev = torch.device("cuda", 0)
+    z = _device(np.frombuffer(bytes(payload), dtype=np.uint8))
+    codec.decompress_zlib_checked(z, int(samples.size), dev)  # warm the workspace
+    torch.cuda.synchronize()
+    begin = time.perf_counter()
+    out, meta = codec.decompress_zlib_checked(z, int(samples.size), dev)
+    torch.cuda.synchronize()
+    elapsed = time.perf_counter() - begin
+    assert [int(v) for v in meta.cpu()] == [21, 0]
+    assert not out.any()
+    assert elapsed < 0.5, elapsed
+    with pytest.raises(codec.CodecError, match="status 21"):
+        codec.decompress_zlib_host(bytes(payload), int(samples.size), 0)
+
+
 def test_config1_float32_compress_matches_oracle(codec, samples):
     stream = _encode_equal(codec, samples, 32768)
     _decode_equal(codec, stream, samples)
