@@ -360,7 +360,8 @@ bool chunk_ok(int64_t chunk_bytes) { return chunk_bytes >= kMinChunk && chunk_by
 
 cudaError_t encode_files(const DeviceState& dev, const u8* in, u64 in_bytes,
                          std::vector<EncodeFile>& files, u32 chunk_bytes, u32 total_chunks,
-                         u8* out, u32* meta, cudaStream_t stream, u32* range_adler = nullptr) {
+                         u8* out, u32* meta, cudaStream_t stream, u32* range_adler = nullptr,
+                         u32 level = 1) {
   Workspace ws(dev.pool, stream);
   EncodeFile* d_files = nullptr;
   u8* slots = nullptr;
@@ -374,14 +375,19 @@ cudaError_t encode_files(const DeviceState& dev, const u8* in, u64 in_bytes,
   CZ_TRY(ws.allocate(&adler, 2 * u64(total_chunks)));
   CZ_TRY(ws.allocate(&offsets, total_chunks));
   {
-    // Pooled calls always use the global spill: with the per-position arrays
-    // there, two encoder CTAs fit an SM's shared memory instead of one.
+    // Pooled calls use the global spill: with the per-position arrays there,
+    // two encoder CTAs fit an SM's shared memory instead of one.  Level 2
+    // follows hash chains through prev[], so it keeps them in shared memory
+    // where they fit, and stores its match distances in the spill.
     const u64 entries = encode_spill_entries(in_bytes, total_chunks);
-    u8* prev = nullptr;
-    CZ_TRY(ws.allocate(&prev, entries * (chunk_bytes >= kLargeChunk ? 4 : 2)));
-    CZ_TRY(ws.allocate(&spill.len, entries));
-    if (chunk_bytes >= kLargeChunk) CZ_TRY(ws.allocate(&spill.data, entries));
-    spill.prev = prev;
+    if (level == 2) CZ_TRY(ws.allocate(&spill.dist, entries));
+    if (level != 2 || !encode_in_smem(chunk_bytes, dev.info)) {
+      u8* prev = nullptr;
+      CZ_TRY(ws.allocate(&prev, entries * (chunk_bytes >= kLargeChunk ? 4 : 2)));
+      CZ_TRY(ws.allocate(&spill.len, entries));
+      if (chunk_bytes >= kLargeChunk) CZ_TRY(ws.allocate(&spill.data, entries));
+      spill.prev = prev;
+    }
   }
   CZ_TRY(launch_encode(in, d_files, u32(files.size()), chunk_bytes, total_chunks, slots, sizes,
                        status, adler, offsets, spill, out, meta, dev.info, stream, range_adler));
@@ -644,10 +650,13 @@ u32 gzip_header(const u8* p, u64 available, u64* header_bytes) {
   return 0;
 }
 
-cudaError_t compress_format(const u8* in, u64 size, int64_t chunk_bytes, int32_t format, u8* out,
-                            u64 capacity, u32* meta, cudaStream_t stream) {
-  if (format == kFormatZlib) return compress(in, size, chunk_bytes, out, capacity, meta, stream);
-  if (!meta || (format != kFormatRaw && format != kFormatGzip)) return cudaErrorInvalidValue;
+cudaError_t compress_format(const u8* in, u64 size, int64_t chunk_bytes, int32_t format,
+                            int32_t level, u8* out, u64 capacity, u32* meta, cudaStream_t stream) {
+  if (level != 1 && level != 2) return cudaErrorInvalidValue;
+  if (format == kFormatZlib && level == 1)
+    return compress(in, size, chunk_bytes, out, capacity, meta, stream);
+  if (!meta || (format != kFormatZlib && format != kFormatRaw && format != kFormatGzip))
+    return cudaErrorInvalidValue;
   DeviceScope scope(stream);
   CZ_TRY(scope.error());
   DeviceState* dev = nullptr;
@@ -668,15 +677,18 @@ cudaError_t compress_format(const u8* in, u64 size, int64_t chunk_bytes, int32_t
     return set_meta(meta, 0, kInvalidBounds, stream);
   std::vector<EncodeFile> files(1);
   files[0] = EncodeFile{0, size, 0, capacity, 0, u32(l.chunks), chunk,
-                        format == kFormatRaw ? kEncodeRaw : kEncodeGzip};
-  if (format == kFormatRaw)
-    return encode_files(*dev, in, size, files, chunk, u32(l.chunks), out, meta, stream);
+                        format == kFormatRaw ? kEncodeRaw
+                                             : format == kFormatGzip ? kEncodeGzip : 0u};
+  if (format != kFormatGzip)
+    return encode_files(*dev, in, size, files, chunk, u32(l.chunks), out, meta, stream, nullptr,
+                        u32(level));
   Workspace ws(dev->pool, stream);
   u32 *parts = nullptr, *crc = nullptr;
   CZ_TRY(ws.allocate(&parts, std::max<u32>(1, crc_segments(size))));
   CZ_TRY(ws.allocate(&crc, 1));
   CZ_TRY(launch_crc32(in, size, parts, crc, dev->info, stream));
-  CZ_TRY(encode_files(*dev, in, size, files, chunk, u32(l.chunks), out, meta, stream));
+  CZ_TRY(encode_files(*dev, in, size, files, chunk, u32(l.chunks), out, meta, stream, nullptr,
+                      u32(level)));
   CZ_TRY(launch_gzip_trailer(out, meta, crc, size, stream));
   return ws.release();
 }
@@ -832,11 +844,11 @@ int cuda_zlib_decompress(const uint8_t* input, uint64_t size, int64_t max_candid
 }
 
 int cuda_zlib_compress_format(const uint8_t* input, uint64_t size, int64_t chunk_bytes,
-                              int32_t format, uint8_t* output, uint64_t capacity,
+                              int32_t format, int32_t level, uint8_t* output, uint64_t capacity,
                               uint32_t* metadata, void* stream) {
   try {
-    return int(cz::compress_format(input, size, chunk_bytes, format, output, capacity, metadata,
-                                   static_cast<cudaStream_t>(stream)));
+    return int(cz::compress_format(input, size, chunk_bytes, format, level, output, capacity,
+                                   metadata, static_cast<cudaStream_t>(stream)));
   } catch (...) {
     return int(cudaErrorUnknown);
   }

@@ -45,6 +45,13 @@ constexpr u32 kHashSlots = 8192;
 constexpr u32 kStitchRounds = 8;  // parallel stitch rounds before the serial finish
 constexpr u32 kStoredMax = 65535;  // bytes of one stored block
 constexpr u32 kMaxChunkBytes = 262144;  // largest accepted chunk
+// Opt-in level 2 (EncodeSpill::dist set; no reference counterpart): the
+// longest of a position's first kChainDepth hash-chain candidates within the
+// window, length-3 matches farther than kTooFar dropped, and one-step lazy
+// evaluation below kLazyLength.  oracle/zlib_oracle.c restates the same parse.
+constexpr u32 kChainDepth = 32;
+constexpr u32 kLazyLength = 32;
+constexpr u32 kTooFar = 4096;
 
 // Extra bits of a length or distance code (RFC 1951 section 3.2.5), by
 // arithmetic rather than table lookups: the lanes of a warp look up different
@@ -528,7 +535,42 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
     }
     return k < 2 ? (k == 0 ? window.x : window.y) : (k == 2 ? window.z : window.w);
   };
+  // Level 2: the chain of p runs through prev[] (each entry is 1 + the last
+  // earlier position with the same hash).  Comparing the byte at the current
+  // best length first skips candidates that cannot be longer.
+  u16* distv = spill.dist ? spill.dist + spill_at : nullptr;
+  const bool thorough = distv != nullptr;
+  u32 token_q = 0;  // level 2: source of the last match token_at returned
+  auto chain_best = [&](u32 p, u32* where) -> u32 {
+    if (p >= hashed) return 0;
+    const u32 limit = min_u32(n - p, 258u);
+    u32 best = 0, at = 0, c = prev[p];
+    for (u32 step = 0; c && step < kChainDepth; ++step) {
+      const u32 q = c - 1;
+      if (p - q > 32768u) break;
+      if ((best < 3 || data[q + best] == data[p + best]) && data[q] == data[p] &&
+          data[q + 1] == data[p + 1] && data[q + 2] == data[p + 2]) {
+        u32 m = 3;
+        while (m < limit && data[q + m] == data[p + m]) ++m;
+        if (m > best) {
+          best = m;
+          at = q;
+          if (m >= limit) break;
+        }
+      }
+      c = prev[q];
+    }
+    if (best == 3 && p - at > kTooFar) best = 0;
+    *where = at;
+    return best;
+  };
   auto token_at = [&](u32 p) -> u32 {  // match length at p, or 0 for a literal
+    if (thorough) {
+      const u32 m = chain_best(p, &token_q);
+      if (!m || m >= kLazyLength) return m;
+      u32 next = 0;
+      return chain_best(p + 1, &next) > m ? 0u : m;
+    }
     if (p >= hashed) return 0;
     const u32 c = candidate_of(p);
     if (!c) return 0;
@@ -550,6 +592,7 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
       if (m) {
         atomicOr(&ismatch[p >> 5], 1u << (p & 31));
         lenv[p] = u8(m - 3);
+        if (thorough) distv[p] = u16(p - token_q);
         p += m;
       } else {
         ++p;
@@ -646,6 +689,7 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
         if (m) {
           atomicOr(&ismatch[p >> 5], 1u << (p & 31));
           lenv[p] = u8(m - 3);
+          if (thorough) distv[p] = u16(p - token_q);
           clear_members(p + 1, min_u32(p + m, my_b));
           p += m;
         } else {
@@ -664,7 +708,7 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
     for_each_token(member, ismatch, a, b, [&](u32 p, bool match) {
       ++tokens;
       if (match) {
-        const u32 m = u32(lenv[p]) + 3, dist = p - (u32(prev[p]) - 1);
+        const u32 m = u32(lenv[p]) + 3, dist = thorough ? u32(distv[p]) : p - (u32(prev[p]) - 1);
         const u32 li = length_symbol(m), di = dist_symbol(dist);
         atomicAdd(&s.freq[257 + li], 1u);
         atomicAdd(&s.freq[286 + di], 1u);
@@ -842,7 +886,7 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
   u32 my_bits = 0;
   for_each_token(member, ismatch, a, b, [&](u32 p, bool match) {
     if (match) {
-      const u32 m = u32(lenv[p]) + 3, dist = p - (u32(prev[p]) - 1);
+      const u32 m = u32(lenv[p]) + 3, dist = thorough ? u32(distv[p]) : p - (u32(prev[p]) - 1);
       const u32 li = length_symbol(m), di = dist_symbol(dist);
       my_bits += (dyn ? s.lengths[257 + li] : fixed_ll_len(257 + li)) + length_extra_bits(li) +
                  (dyn ? s.lengths[286 + di] : 5u) + dist_extra_bits(di);
@@ -916,7 +960,7 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
     pk.start(words, my_start, my_start + my_bits, used_words);
     for_each_token(member, ismatch, a, b, [&](u32 p, bool match) {
       if (match) {
-        const u32 m = u32(lenv[p]) + 3, dist = p - (u32(prev[p]) - 1);
+        const u32 m = u32(lenv[p]) + 3, dist = thorough ? u32(distv[p]) : p - (u32(prev[p]) - 1);
         const u32 li = length_symbol(m), di = dist_symbol(dist);
         if (dyn) pk.put(s.codes[257 + li], s.lengths[257 + li]);
         else pk.put(fixed_ll_code(257 + li), fixed_ll_len(257 + li));

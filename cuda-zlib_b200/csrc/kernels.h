@@ -90,6 +90,9 @@ struct EncodeSpill {
   void* prev;
   u8* len;
   u8* data;
+  // Set: level 2 (hash-chain search, lazy evaluation), each match's distance
+  // stored here (u16, same entries as prev).  Null: the reference's parse.
+  u16* dist;
 };
 constexpr u32 kSpillGap = 64;  // spill entries between consecutive chunks' slices
 inline u64 encode_spill_entries(u64 in_bytes, u32 chunks) {

@@ -282,12 +282,24 @@ def _capacity(size, chunk_bytes):
     return capacity, chunks
 
 
-def compress_zlib_padded(data, device=0, *, chunk_bytes=32768):
+def _check_level(level):
+    if type(level) is not int or level not in (1, 2):
+        raise ValueError("level must be 1 (the reference encoder) or 2")
+
+
+def compress_zlib_padded(data, device=0, *, chunk_bytes=32768, level=1):
     """Return ``(buffer, [encoded_length, status])`` without a host sync.
 
     The fixed-size buffer holds a zlib stream followed by zero padding.
-    Status zero means success; check it before using the stream.
+    Status zero means success; check it before using the stream.  level 1
+    (the default) is the reference's encoder, byte for byte; level 2, which
+    the reference does not have, searches hash chains with lazy evaluation
+    for smaller streams at a lower rate.
     """
+    _check_level(level)
+    if level != 1:
+        from . import formats
+        return formats._compress_padded(data, device, chunk_bytes, formats.FORMAT_ZLIB, level)
     _check_chunk(chunk_bytes)
     size = _input_size(data, limit=_MAX_STREAM)
     capacity, chunks, blocks = _layout(size, chunk_bytes)
@@ -660,9 +672,9 @@ def decompress_zlib_checked(payload, expected_bytes, device=0, *,
     return output, metadata
 
 
-def compress_zlib(data, device=0, *, chunk_bytes=32768):
+def compress_zlib(data, device=0, *, chunk_bytes=32768, level=1):
     """Encode bytes/uint8 data to a completed, exact-length CUDA tensor."""
-    output, metadata = compress_zlib_padded(data, device, chunk_bytes=chunk_bytes)
+    output, metadata = compress_zlib_padded(data, device, chunk_bytes=chunk_bytes, level=level)
     length, status = (int(v) for v in metadata.cpu().numpy())
     _check_value(status, "CUDA compression")
     return output[:length]
@@ -756,7 +768,7 @@ def _compress_host_pipelined(source, size, selected, chunk_bytes):
     return array
 
 
-def compress_zlib_host(data, device=0, *, chunk_bytes=32768) -> np.ndarray:
+def compress_zlib_host(data, device=0, *, chunk_bytes=32768, level=1) -> np.ndarray:
     """Encode to a completed, read-only NumPy uint8 array in pinned memory.
 
     The single-stream counterpart of compress_zlib_batch_host (the reference
@@ -767,15 +779,16 @@ def compress_zlib_host(data, device=0, *, chunk_bytes=32768) -> np.ndarray:
     kernels; the stream is the same byte for byte.
     """
     _check_chunk(chunk_bytes)
+    _check_level(level)
     size = _input_size(data, limit=_MAX_STREAM)
-    if size >= _PIPE_MIN:
+    if size >= _PIPE_MIN and level == 1:
         _, _, blocks = _layout(size, chunk_bytes)
         source = _host_view(data)
         if source is not None and not source.is_pinned() and blocks <= _MAX_BLOCKS:
             if source.dtype != _torch().uint8 or source.ndim != 1:
                 raise TypeError("array input must be one-dimensional uint8")
             return _compress_host_pipelined(source, size, _select_device(device), chunk_bytes)
-    output, metadata = compress_zlib_padded(data, device, chunk_bytes=chunk_bytes)
+    output, metadata = compress_zlib_padded(data, device, chunk_bytes=chunk_bytes, level=level)
     length, status = (int(v) for v in metadata.cpu().numpy())
     _check_value(status, "CUDA compression")
     return _to_pinned_host(output[:length])

@@ -47,8 +47,8 @@ def _configure(library):
                                                  ctypes.c_int32, _u8p, ctypes.c_uint64, _u8p,
                                                  ctypes.c_void_p]
     library.cuda_zlib_compress_format.argtypes = [_u8p, ctypes.c_uint64, ctypes.c_int64,
-                                                  ctypes.c_int32, _u8p, ctypes.c_uint64, _u8p,
-                                                  ctypes.c_void_p]
+                                                  ctypes.c_int32, ctypes.c_int32, _u8p,
+                                                  ctypes.c_uint64, _u8p, ctypes.c_void_p]
     library.cuda_zlib_decompress_format.argtypes = [_u8p, ctypes.c_uint64, ctypes.c_int32,
                                                     ctypes.c_uint64, ctypes.c_int64,
                                                     ctypes.c_int64, _u8p, ctypes.c_uint64, _u8p,

@@ -19,7 +19,9 @@ metadata layouts and errors.
                end.
 
 Padded capacities: size + 5 * S + W, with S the stored-block count of the
-zlib formula and W = 0 (raw) or 18 (gzip) instead of zlib's 6.
+zlib formula and W = 0 (raw) or 18 (gzip) instead of zlib's 6.  Every
+encoder call takes level 1 (the reference's parse) or 2 (hash chains with
+lazy evaluation, as compress_zlib_padded's level 2).
 """
 import ctypes
 
@@ -29,8 +31,7 @@ from . import _codec, _native
 from ._errors import CodecError
 
 FORMAT_ZLIB, FORMAT_RAW, FORMAT_GZIP = 0, 1, 2
-_WRAPPER = {FORMAT_RAW: 0, FORMAT_GZIP: 18}
-_NAMES = {FORMAT_RAW: "raw Deflate", FORMAT_GZIP: "gzip"}
+_WRAPPER = {FORMAT_ZLIB: 6, FORMAT_RAW: 0, FORMAT_GZIP: 18}
 _GZIP_PROBE = 65536  # header bytes read first from a device-resident member
 
 
@@ -68,7 +69,8 @@ def _member_header(payload, size):
         return gzip_header_size(payload.cpu().numpy())
 
 
-def _compress_padded(data, device, chunk_bytes, fmt):
+def _compress_padded(data, device, chunk_bytes, fmt, level=1):
+    _codec._check_level(level)
     _codec._check_chunk(chunk_bytes)
     size = _codec._input_size(data, limit=_codec._MAX_STREAM)
     capacity, blocks = _capacity(size, chunk_bytes, fmt)
@@ -82,7 +84,7 @@ def _compress_padded(data, device, chunk_bytes, fmt):
         output = torch.empty(max(capacity, 1), dtype=torch.uint8, device=selected)[:capacity]
         metadata = torch.empty(2, dtype=torch.uint32, device=selected)
         _native.check(lib.cuda_zlib_compress_format(
-            _codec._ptr(raw), size, chunk_bytes, fmt, output.data_ptr(), capacity,
+            _codec._ptr(raw), size, chunk_bytes, fmt, level, output.data_ptr(), capacity,
             metadata.data_ptr(), _codec._stream(selected)), "CUDA compression")
     return output, metadata
 
@@ -115,16 +117,16 @@ def _finished(output, metadata, operation):
 
 
 # ---------------------------------------------------------------- raw Deflate
-def compress_deflate_padded(data, device=0, *, chunk_bytes=32768):
+def compress_deflate_padded(data, device=0, *, chunk_bytes=32768, level=1):
     """Return ``(buffer, [encoded_length, status])``: a raw Deflate stream
     (the zlib stream's body) and zero padding, without a host sync."""
-    return _compress_padded(data, device, chunk_bytes, FORMAT_RAW)
+    return _compress_padded(data, device, chunk_bytes, FORMAT_RAW, level)
 
 
-def compress_deflate(data, device=0, *, chunk_bytes=32768):
+def compress_deflate(data, device=0, *, chunk_bytes=32768, level=1):
     """Encode to a completed, exact-length raw Deflate CUDA tensor."""
-    return _finished(*compress_deflate_padded(data, device, chunk_bytes=chunk_bytes),
-                     "CUDA compression")
+    output, metadata = compress_deflate_padded(data, device, chunk_bytes=chunk_bytes, level=level)
+    return _finished(output, metadata, "CUDA compression")
 
 
 def decompress_deflate_checked(payload, expected_bytes, device=0, *,
@@ -143,21 +145,22 @@ def decompress_deflate(payload, expected_bytes, device=0):
 
 
 # ---------------------------------------------------------------- gzip
-def compress_gzip_padded(data, device=0, *, chunk_bytes=32768):
+def compress_gzip_padded(data, device=0, *, chunk_bytes=32768, level=1):
     """Return ``(buffer, [encoded_length, status])``: one gzip member and zero
     padding, without a host sync."""
-    return _compress_padded(data, device, chunk_bytes, FORMAT_GZIP)
+    return _compress_padded(data, device, chunk_bytes, FORMAT_GZIP, level)
 
 
-def compress_gzip(data, device=0, *, chunk_bytes=32768):
+def compress_gzip(data, device=0, *, chunk_bytes=32768, level=1):
     """Encode to a completed, exact-length gzip member (CUDA tensor)."""
-    return _finished(*compress_gzip_padded(data, device, chunk_bytes=chunk_bytes),
-                     "CUDA compression")
+    output, metadata = compress_gzip_padded(data, device, chunk_bytes=chunk_bytes, level=level)
+    return _finished(output, metadata, "CUDA compression")
 
 
-def compress_gzip_host(data, device=0, *, chunk_bytes=32768) -> np.ndarray:
+def compress_gzip_host(data, device=0, *, chunk_bytes=32768, level=1) -> np.ndarray:
     """compress_gzip, then one transfer into pinned host memory."""
-    return _codec._to_pinned_host(compress_gzip(data, device, chunk_bytes=chunk_bytes))
+    return _codec._to_pinned_host(compress_gzip(data, device, chunk_bytes=chunk_bytes,
+                                                level=level))
 
 
 def decompress_gzip_checked(payload, expected_bytes, device=0, *,

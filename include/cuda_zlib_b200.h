@@ -105,14 +105,20 @@ int cuda_zlib_decompress_batch(const uint8_t* input, uint64_t input_bytes,
  * 1 raw Deflate, 2 gzip (one member).  Any other format returns
  * cudaErrorInvalidValue (1).
  *
- * cuda_zlib_compress_format: the zlib stream's body, bare (format 1) or as a
- * gzip member (format 2: header 1f 8b 08 00, MTIME 0, XFL 0, OS 255, then the
- * body, CRC-32 and ISIZE).  capacity = size + 5 * S + W with S as for
- * cuda_zlib_compress and W = 0 (raw) or 18 (gzip); metadata u32[2] =
- * [encoded_length, status], bounds failures [0, 23] as cuda_zlib_compress. */
+ * cuda_zlib_compress_format: a zlib stream (format 0), its body bare
+ * (format 1) or as a gzip member (format 2: header 1f 8b 08 00, MTIME 0,
+ * XFL 0, OS 255, then the body, CRC-32 and ISIZE).  level 1 is the
+ * reference's encoder (format 0 at level 1 is exactly cuda_zlib_compress);
+ * level 2, with no reference counterpart, searches up to 32 hash-chain
+ * candidates per position with one-step lazy evaluation (smaller output,
+ * slower; the chunking, block choice and trees are level 1's).  Any other
+ * level returns cudaErrorInvalidValue (1).  capacity = size + 5 * S + W
+ * with S as for cuda_zlib_compress and W = 6 (zlib), 0 (raw) or 18 (gzip);
+ * metadata u32[2] = [encoded_length, status], bounds failures [0, 23] as
+ * cuda_zlib_compress. */
 int cuda_zlib_compress_format(const uint8_t* input, uint64_t size, int64_t chunk_bytes,
-                              int32_t format, uint8_t* output, uint64_t capacity,
-                              uint32_t* metadata, void* stream);
+                              int32_t format, int32_t level, uint8_t* output,
+                              uint64_t capacity, uint32_t* metadata, void* stream);
 
 /* cuda_zlib_decompress_format: decodes a raw Deflate stream (its final
  * block ends in its last byte) or one gzip member whose header is

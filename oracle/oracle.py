@@ -52,6 +52,14 @@ def lib():
                                                   ctypes.c_uint64, ctypes.c_uint64, u8p,
                                                   ctypes.c_uint32, u32p]
         handle.oracle_compress_chunks.restype = ctypes.c_uint32
+        handle.oracle_compress_level.argtypes = [u8p, ctypes.c_uint64, ctypes.c_uint32,
+                                                 ctypes.c_uint32, u8p, ctypes.c_uint64, u32p]
+        handle.oracle_compress_level.restype = ctypes.c_uint32
+        handle.oracle_compress_chunks_level.argtypes = [u8p, ctypes.c_uint64, ctypes.c_uint32,
+                                                        ctypes.c_uint32, ctypes.c_uint64,
+                                                        ctypes.c_uint64, u8p, ctypes.c_uint32,
+                                                        u32p]
+        handle.oracle_compress_chunks_level.restype = ctypes.c_uint32
         _lib = handle
     return _lib
 
@@ -116,25 +124,27 @@ def slot_bytes(chunk_bytes):
     return (chunk_bytes * 9 + 7) // 8 + 16 + 5 * stored_blocks(chunk_bytes)
 
 
-def compress_padded(data, chunk_bytes=32768):
-    """Reference encoder restated: (padded buffer, [encoded_length, status])."""
+def compress_padded(data, chunk_bytes=32768, level=1):
+    """Reference encoder restated: (padded buffer, [encoded_length, status]).
+    level 2 is the codec's opt-in parse (hash chains, lazy evaluation),
+    which the reference does not have."""
     source = _view(data)
     cap = capacity(source.size, chunk_bytes)
     out = np.zeros(cap, dtype=np.uint8)
     meta = np.zeros(2, dtype=np.uint32)
-    lib().oracle_compress(_u8(source), source.size, chunk_bytes, _u8(out), cap,
-                          meta.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)))
+    lib().oracle_compress_level(_u8(source), source.size, chunk_bytes, level, _u8(out), cap,
+                                meta.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)))
     return out, meta
 
 
-def compress(data, chunk_bytes=32768):
-    out, meta = compress_padded(data, chunk_bytes)
+def compress(data, chunk_bytes=32768, level=1):
+    out, meta = compress_padded(data, chunk_bytes, level)
     if meta[1]:
         raise ValueError("oracle compression status %d" % meta[1])
     return out[:meta[0]].tobytes()
 
 
-def compress_parallel(data, chunk_bytes=32768, threads=None):
+def compress_parallel(data, chunk_bytes=32768, threads=None, level=1):
     """compress() for large inputs: the chunks are independent, so several
     host threads encode disjoint chunk ranges (ctypes drops the GIL), then
     the stream is assembled as compress() writes it: 78 01, every chunk's
@@ -150,8 +160,8 @@ def compress_parallel(data, chunk_bytes=32768, threads=None):
         count = min(per, chunks - first)
         out = np.zeros(count * slot, dtype=np.uint8)
         sizes = np.zeros(count, dtype=np.uint32)
-        failed = lib().oracle_compress_chunks(
-            _u8(source), n, chunk_bytes, first, count, _u8(out), slot,
+        failed = lib().oracle_compress_chunks_level(
+            _u8(source), n, chunk_bytes, level, first, count, _u8(out), slot,
             sizes.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)))
         if failed:
             raise ValueError("oracle chunk compression failed")
@@ -170,20 +180,20 @@ GZIP_HEADER = bytes([0x1F, 0x8B, 8, 0, 0, 0, 0, 0, 0, 0xFF])
 CRC_POLY = 0xEDB88320
 
 
-def raw_deflate(data, chunk_bytes=32768):
+def raw_deflate(data, chunk_bytes=32768, level=1):
     """The codec's raw Deflate stream: the zlib stream's body."""
     source = _view(data)
-    whole = compress_parallel(source, chunk_bytes) if source.size > (4 << 20) else \
-        compress(source, chunk_bytes)
+    whole = compress_parallel(source, chunk_bytes, level=level) if source.size > (4 << 20) \
+        else compress(source, chunk_bytes, level)
     return whole[2:-4]
 
 
-def gzip_member(data, chunk_bytes=32768, crc=None):
+def gzip_member(data, chunk_bytes=32768, crc=None, level=1):
     """The codec's gzip member: fixed header, body, CRC-32, ISIZE (LE)."""
     import zlib
     source = _view(data)
     value = zlib.crc32(source) if crc is None else crc
-    return (GZIP_HEADER + raw_deflate(source, chunk_bytes) + value.to_bytes(4, "little")
+    return (GZIP_HEADER + raw_deflate(source, chunk_bytes, level) + value.to_bytes(4, "little")
             + (source.size & 0xFFFFFFFF).to_bytes(4, "little"))
 
 

@@ -838,9 +838,62 @@ static void stream_layout(u64 n, u32 chunk, u64* chunks_out, u64* stored_out, u6
   *blocks_out = (chunks - 1) * (full > 2 ? full : 2) + tail;
 }
 
+/* Opt-in level 2 (no reference counterpart; the GPU encoder's restated
+ * parse).  Every position below n - 2 has its hash chain: prev[p] = 1 + the
+ * last earlier position with its hash, or 0.  A position's best match is the
+ * longest of its first L2_CHAIN chain candidates within 32768 bytes (the
+ * nearest among equal lengths; the search stops at L2_NICE bytes or the end
+ * of the chunk), a length-3 match farther than L2_TOO_FAR bytes counts as
+ * none, and the token at p is a literal when p's best match is shorter than
+ * L2_LAZY and p + 1 has a longer one (one-step lazy evaluation).  The token
+ * at p is a function of the data alone, which the GPU's speculative walks
+ * need. */
+#ifndef L2_CHAIN
+#define L2_CHAIN 32u
+#endif
+#ifndef L2_LAZY
+#define L2_LAZY 32u
+#endif
+#ifndef L2_NICE
+#define L2_NICE 258u
+#endif
+#define L2_TOO_FAR 4096u
+
+static u32 l2_best(const u8* d, u32 n, const u32* prev, u32 p, u32* where) {
+  if (n < 3 || p >= n - 2) return 0;
+  const u32 limit = n - p < 258 ? n - p : 258;
+  u32 best = 0, at = 0, c = prev[p];
+  for (u32 step = 0; c && step < L2_CHAIN; ++step) {
+    const u32 q = c - 1;
+    if (p - q > 32768u) break;
+    if (d[q] == d[p] && d[q + 1] == d[p + 1] && d[q + 2] == d[p + 2]) {
+      u32 m = 3;
+      while (m < limit && d[q + m] == d[p + m]) ++m;
+      if (m > best) {
+        best = m;
+        at = q;
+        if (m >= limit || m >= L2_NICE) break;
+      }
+    }
+    c = prev[q];
+  }
+  if (best == 3 && p - at > L2_TOO_FAR) best = 0;
+  *where = at;
+  return best;
+}
+
+static u32 l2_token(const u8* d, u32 n, const u32* prev, u32 p, u32* where) {
+  const u32 m = l2_best(d, n, prev, p, where);
+  if (!m || m >= L2_LAZY) return m;
+  u32 next = 0;
+  return l2_best(d, n, prev, p + 1, &next) > m ? 0u : m;
+}
+
 /* Encodes one chunk into `slot`; returns the status (0 ok).  `size` gets
- * the encoded byte count. */
-static u32 encode_chunk(const u8* data, u32 n, int final, u8* slot, u32 slot_bytes, u32* size) {
+ * the encoded byte count.  level 1 is the reference's parse, level 2 the
+ * parse above. */
+static u32 encode_chunk(const u8* data, u32 n, int final, u8* slot, u32 slot_bytes, u32* size,
+                        u32 level) {
   u32* last = (u32*)calloc(8192, sizeof(u32));
   u32* tokens = (u32*)malloc(sizeof(u32) * (n ? n : 1));
   u32 freq[335];
@@ -852,9 +905,36 @@ static u32 encode_chunk(const u8* data, u32 n, int final, u8* slot, u32 slot_byt
   memset(lengths, 0, sizeof(lengths));
   memset(codes, 0, sizeof(codes));
   u32 extra_bits = 0, count = 0, pos = 0;
+  if (level == 2) {
+    u32* prev = (u32*)calloc(n ? n : 1, sizeof(u32));
+    for (u32 p = 0; n >= 3 && p < n - 2; ++p) {
+      const u32 h = hash3(data, p);
+      prev[p] = last[h];
+      last[h] = p + 1;
+    }
+    while (pos < n) {
+      u32 earlier = 0;
+      const u32 match = l2_token(data, n, prev, pos, &earlier);
+      if (!match) {
+        freq[data[pos]]++;
+        tokens[count++] = data[pos++];
+        continue;
+      }
+      u32 dist = pos - earlier, li = 0, di = 0;
+      while (li < 28 && match >= kLenBase[li + 1]) ++li;
+      while (di < 29 && dist >= kDistBase[di + 1]) ++di;
+      freq[257 + li]++;
+      freq[286 + di]++;
+      extra_bits += kLenExtra[li] + kDistExtra[di];
+      tokens[count++] = 0x80000000u | li | (di << 5) | ((match - kLenBase[li]) << 10) |
+                        ((dist - kDistBase[di]) << 15);
+      pos += match;
+    }
+    free(prev);
+  }
   /* Greedy one-candidate parse.  Every position is inserted in order, so the
    * candidate of a position is the last earlier position with its hash. */
-  for (;;) {
+  for (; level != 2;) {
     u32 earlier = 0;
     int candidate = 0;
     while (pos < n) {
@@ -1020,7 +1100,8 @@ out:
 /* Whole-stream compression: metadata = [encoded_length, status].  The
  * capacity must be n + 5 * stored_blocks + 6, i.e. n + 5*chunks + 6 for
  * chunks <= 65535 (compress_zlib_padded, _codec.py:151-177). */
-u32 oracle_compress(const u8* in, u64 n, u32 chunk_bytes, u8* out, u64 capacity, u32* meta) {
+u32 oracle_compress_level(const u8* in, u64 n, u32 chunk_bytes, u32 level, u8* out,
+                          u64 capacity, u32* meta) {
   meta[0] = 0;
   meta[1] = 0;
   memset(out, 0, capacity);
@@ -1043,7 +1124,7 @@ u32 oracle_compress(const u8* in, u64 n, u32 chunk_bytes, u8* out, u64 capacity,
     u64 start = c * chunk_bytes;
     u32 len = (u32)(n - start < chunk_bytes ? n - start : chunk_bytes);
     u32 size = 0;
-    u32 st = encode_chunk(in + start, len, c + 1 == chunks, slot, slot_bytes, &size);
+    u32 st = encode_chunk(in + start, len, c + 1 == chunks, slot, slot_bytes, &size, level);
     if (st || size > slot_bytes || total + size + 4 > capacity) {
       free(slot);
       memset(out, 0, capacity);
@@ -1064,11 +1145,15 @@ u32 oracle_compress(const u8* in, u64 n, u32 chunk_bytes, u8* out, u64 capacity,
   return 0;
 }
 
+u32 oracle_compress(const u8* in, u64 n, u32 chunk_bytes, u8* out, u64 capacity, u32* meta) {
+  return oracle_compress_level(in, n, chunk_bytes, 1, out, capacity, meta);
+}
+
 /* Compress a chunk range [first, first+count) of one stream into the
  * caller's slots (used for a multi-threaded CPU baseline; each chunk is
  * independent).  Returns the number of failed chunks. */
-u32 oracle_compress_chunks(const u8* in, u64 n, u32 chunk_bytes, u64 first, u64 count,
-                           u8* slots, u32 slot_bytes, u32* sizes) {
+u32 oracle_compress_chunks_level(const u8* in, u64 n, u32 chunk_bytes, u32 level, u64 first,
+                                 u64 count, u8* slots, u32 slot_bytes, u32* sizes) {
   u64 chunks = (n + chunk_bytes - 1) / chunk_bytes;
   if (!chunks) chunks = 1;
   u32 failed = 0;
@@ -1076,7 +1161,13 @@ u32 oracle_compress_chunks(const u8* in, u64 n, u32 chunk_bytes, u64 first, u64 
     u64 start = c * chunk_bytes;
     u32 len = (u32)(n - start < chunk_bytes ? n - start : chunk_bytes);
     failed += encode_chunk(in + start, len, c + 1 == chunks, slots + (c - first) * slot_bytes,
-                           slot_bytes, &sizes[c - first]) != 0;
+                           slot_bytes, &sizes[c - first], level) != 0;
   }
   return failed;
+}
+
+u32 oracle_compress_chunks(const u8* in, u64 n, u32 chunk_bytes, u64 first, u64 count,
+                           u8* slots, u32 slot_bytes, u32* sizes) {
+  return oracle_compress_chunks_level(in, n, chunk_bytes, 1, first, count, slots, slot_bytes,
+                                      sizes);
 }

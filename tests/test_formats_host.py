@@ -136,3 +136,21 @@ def test_oracle_members_decode_with_stdlib():
     data = bytes(range(256)) * 300
     assert zlib.decompress(oracle.raw_deflate(data, 4096), -15) == data
     assert zlib.decompress(oracle.gzip_member(data, 4096), 31) == data
+
+
+def test_level_argument_checks():
+    import cuda_zlib
+    for bad in (0, 3, "2", 2.0):
+        with pytest.raises(ValueError, match="level"):
+            cuda_zlib.compress_zlib_padded(b"abc", 0, level=bad)
+        with pytest.raises(ValueError, match="level"):
+            cuda_zlib.compress_gzip_padded(b"abc", 0, level=bad)
+
+
+@pytest.mark.parametrize("chunk", [256, 32768, 262144])
+def test_oracle_level2_streams_decode_and_shrink_text(chunk):
+    import workloads
+    text = workloads.corpus()[:1 << 20].tobytes()
+    one, two = oracle.compress(text, chunk), oracle.compress(text, chunk, 2)
+    assert zlib.decompress(two) == text
+    assert len(two) < len(one)

@@ -169,10 +169,12 @@ def test_format_bounds_through_the_c_abi(codec):
     assert lib.cuda_zlib_decompress_format(member.data_ptr(), member.numel(), 3, 0, 262144,
                                            262144, out.data_ptr(), 3, meta.data_ptr(),
                                            stream) == 1
-    assert lib.cuda_zlib_compress_format(member.data_ptr(), 3, 32768, 5, out.data_ptr(), 16,
+    assert lib.cuda_zlib_compress_format(member.data_ptr(), 3, 32768, 5, 1, out.data_ptr(), 16,
+                                         meta.data_ptr(), stream) == 1
+    assert lib.cuda_zlib_compress_format(member.data_ptr(), 3, 32768, 0, 3, out.data_ptr(), 16,
                                          meta.data_ptr(), stream) == 1
     # A capacity that is not the format's: [0, 23].
-    assert lib.cuda_zlib_compress_format(member.data_ptr(), 3, 32768, 2, out.data_ptr(), 16,
+    assert lib.cuda_zlib_compress_format(member.data_ptr(), 3, 32768, 2, 1, out.data_ptr(), 16,
                                          meta.data_ptr(), stream) == 0
     assert status() == [0, 23]
 
