@@ -7,8 +7,8 @@
 // hash (enc_hash, :47-51).  This kernel exploits that:
 //
 //   1. stage the chunk in shared memory and fuse its Adler-32 partial sums;
-//   2. one warp computes every position's candidate with __match_any_sync
-//      over 32 positions at a time (lanes sharing a hash see each other);
+//   2. every position's candidate: warp w takes the positions whose hash
+//      is w mod 16, in order, and finds equal hashes 32 at a time by ballots;
 //   3. 256 threads each walk the greedy parse from the start of their own
 //      segment of the chunk, speculatively;
 //   4. one thread stitches the segments: an entry point that differs from the
@@ -97,6 +97,12 @@ __device__ __forceinline__ u32 extent_of(u32 bits, bool final) {
 __host__ __device__ __forceinline__ u32 bitmap_words(u32 chunk_bytes) {
   return ((chunk_bytes + 31) / 32 + 1 + 3) & ~3u;
 }
+// Words of a chunk's owner-nibble array (8 positions a word), padded to 16
+// bytes so that the array after it starts 16-byte aligned.
+__host__ __device__ __forceinline__ u32 owner_words(u32 chunk_bytes) {
+  return ((chunk_bytes + 7) / 8 + 3) & ~3u;
+}
+
 // Stored blocks of an n-byte chunk's stored fallback (kStoredMax each).
 __host__ __device__ __forceinline__ u32 stored_blocks(u32 n) {
   return n ? (n + kStoredMax - 1) / kStoredMax : 1u;
@@ -343,7 +349,7 @@ __device__ __forceinline__ u64 spill_offset(u64 in_pos, u32 g) {
 // match lengths live in the global spill (256 KiB do not fit shared memory);
 // its stored fallback takes several blocks of at most 65535 bytes.
 template <typename Pos>
-__global__ void __launch_bounds__(kEncThreads)
+__global__ void __launch_bounds__(kEncThreads, 2)
 encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ files, u32 nfiles,
                      u32 chunk_bytes, u32 total_chunks, u8* slots, u32* sizes, u32* status,
                      u64* adler, EncodeSpill spill, u32 in_smem) {
@@ -367,8 +373,8 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
   const bool final = local + 1 == f.chunks && !(f.flags & kEncodeNotLast);
   const u8* src = in + f.in_offset + start;
 
-  // Shared layout: data | member bits | match bits | hash table | prev | len
-  // (large chunks: member bits | match bits | hash table).
+  // Shared layout: data | member bits | match bits | hash table | owner
+  // nibbles | prev | len (large chunks: member bits | match bits | hash table).
   const u32 data_bytes = (chunk_bytes + 16 + 15) & ~15u;
   const u32 bit_words = bitmap_words(chunk_bytes);
   const u64 spill_at = spill_offset(f.in_offset + start, g);
@@ -376,10 +382,11 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
   u32* member = reinterpret_cast<u32*>(kLarge ? smem : smem + data_bytes);
   u32* ismatch = member + bit_words;
   Pos* table = reinterpret_cast<Pos*>(ismatch + bit_words);
+  u32* owner_nibbles = reinterpret_cast<u32*>(table + kHashSlots);
   Pos* prev;
   u8* lenv;
   if (in_smem) {
-    prev = table + kHashSlots;
+    prev = reinterpret_cast<Pos*>(owner_nibbles + owner_words(chunk_bytes));
     lenv = reinterpret_cast<u8*>(prev + ((chunk_bytes + 7) & ~7u));
   } else {
     // 16-byte aligned (lenv is read as words), kSpillGap entries apart.
@@ -417,23 +424,36 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
     adler[2 * u64(g) + 1] = b;
   }
 
-  // 2. Candidates: prev[p] = 1 + last earlier position with hash(p), or 0.
-  // First every position's hash goes to prev[p] (its low byte also to
-  // lenv[p]).  Then warp w handles the table slots h with h % 8 == w: it
-  // gathers the positions it owns in order into batches of 32 and, per
-  // batch, finds equal hashes among the lanes by ballots over the hash bits.
-  // A lane's candidate is its last earlier equal lane, else the table; the
-  // last lane of each hash writes the table.  Slots are disjoint between
-  // warps, so the eight warps never wait on one another.
+  // 2. Candidates: prev[p] = 1 + the last earlier position with hash(p), or
+  // 0 (the reference inserts every position into its one-entry table in
+  // order, so this is the table's entry when p is reached).  First every
+  // position's owner, its hash mod 16, goes to a nibble array (8 positions a
+  // word).  Then warp w handles the table slots h with h % 16 == w: it
+  // gathers the positions it owns in order into batches of 32, hashes them
+  // again from the staged chunk and, per batch, finds equal hashes among the
+  // lanes by ballots over the hash bits.  A lane's candidate is its last
+  // earlier equal lane, else the table; the last lane of each hash writes the
+  // table.  Slots are disjoint between warps, so the warps never wait on one
+  // another, and nothing on a batch's path waits for global memory (chunks
+  // above 64 KiB keep the nibbles in the spill, in place of the lengths).
   const u32 hashed = n >= 3 ? n - 2 : 0;  // positions 0..n-3 are hashed
   {
     const u32* words = reinterpret_cast<const u32*>(data);
-    for (u32 p = tid; p < hashed; p += kEncThreads) {
+    auto hash_at = [&](u32 p) -> u32 {
       const u32 lo = words[p >> 2], hi = words[(p >> 2) + 1];
       const u32 v = __funnelshift_r(lo, hi, (p & 3u) * 8u) & 0xffffffu;
-      const u32 h = (v * 2654435761u) >> 19;
-      prev[p] = Pos(h);
-      lenv[p] = u8(h);
+      return (v * 2654435761u) >> 19;
+    };
+    u32* owners = kLarge ? reinterpret_cast<u32*>(lenv) : owner_nibbles;
+    const u32 owner_words = (hashed + 7) / 8;
+    for (u32 w = tid; w < owner_words; w += kEncThreads) {
+      u32 nibbles = 0;
+#pragma unroll
+      for (u32 k = 0; k < 8; ++k) {
+        const u32 p = 8 * w + k;
+        if (p < hashed) nibbles |= (hash_at(p) & (kEncWarps - 1)) << (4 * k);
+      }
+      owners[w] = nibbles;
     }
     __syncthreads();
     Pos* ring = s.owned[warp];
@@ -441,9 +461,10 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
     auto batch = [&](u32 count) {
       const bool valid = lane < count;
       const u32 pos = valid ? ring[(head + lane) & (kRing - 1)] : 0u;
-      const u32 h = valid ? prev[pos] : 0u;
+      const u32 h = valid ? hash_at(pos) : 0u;
       const u32 key = h >> kOwnerBits;  // the low bits equal the warp index
       u32 same = __ballot_sync(kFullMask, valid);
+#pragma unroll
       for (u32 bit = 0; bit < 13 - kOwnerBits; ++bit) {
         const u32 ones = __ballot_sync(kFullMask, valid && ((key >> bit) & 1u));
         same &= ((key >> bit) & 1u) ? ones : ~ones;
@@ -460,48 +481,41 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
       __syncwarp();
       head = (head + count) & (kRing - 1);
     };
-    // An iteration covers 512 positions: lane i looks at the words of lenv
-    // holding positions base + 128 j + 4 i .. + 3 (j = 0..3).  A byte is
-    // owned when its low kOwnerBits bits equal the warp index: with those
-    // bits xor-ed with the index and the others masked off, adding 0x7f to
-    // each byte sets its top bit exactly when the byte is nonzero.  The four
-    // per-word counts (at most 4 each, 128 over the warp) are packed in one
-    // word, so one warp scan places every owned position in order.
-    const u32* low_bytes = reinterpret_cast<const u32*>(lenv);
-    const u32 pattern = warp * 0x01010101u;
-    constexpr u32 kOwnerMask = (kEncWarps - 1) * 0x01010101u;
-    for (u32 base = 0; base < hashed; base += 512) {
-      u32 owned[4], packed = 0;
-#pragma unroll
-      for (u32 j = 0; j < 4; ++j) {
-        const u32 q = base + 128 * j + 4 * lane;
-        u32 m = 0;
-        if (q < hashed) {
-          const u32 x = (low_bytes[q >> 2] ^ pattern) & kOwnerMask;
-          m = ~(x + 0x7f7f7f7fu) & 0x80808080u;
-          if (hashed - q < 4) m &= (1u << (8 * (hashed - q))) - 1u;
-        }
-        owned[j] = m;
-        packed |= u32(__popc(m)) << (8 * j);
+    // An iteration covers 256 positions: lane i reads the nibble word of
+    // positions base + 8 i .. + 7.  A nibble is owned when it equals the warp
+    // index: xor-ed with the index, (x & 7) + 7 sets its top bit exactly when
+    // its low bits are nonzero, so ~(t | x) keeps the top bit of zero
+    // nibbles.  One warp scan of the per-lane counts places every owned
+    // position in order; lanes 0-15 and 16-31 fill the ring in two halves
+    // (at most 128 positions each, with fewer than 32 waiting before), each
+    // followed by the batches it completes.
+    const u32 pattern = warp * 0x11111111u;
+    for (u32 base = 0; base < hashed; base += 256) {
+      const u32 q = base + 8 * lane;
+      u32 m = 0;
+      if (q < hashed) {
+        const u32 x = owners[q >> 3] ^ pattern;
+        const u32 t = (x & 0x77777777u) + 0x77777777u;
+        m = ~(t | x) & 0x88888888u;
+        if (hashed - q < 8) m &= (1u << (4 * (hashed - q))) - 1u;
       }
-      u32 incl = packed;
+      const u32 count = __popc(m);
+      u32 incl = count;
 #pragma unroll
       for (u32 o = 1; o < 32; o <<= 1) {
         const u32 v = __shfl_up_sync(kFullMask, incl, o);
         if (lane >= o) incl += v;
       }
-      const u32 totals = __shfl_sync(kFullMask, incl, 31), excl = incl - packed;
+      const u32 first_half = __shfl_sync(kFullMask, incl, 15);
+      const u32 total = __shfl_sync(kFullMask, incl, 31);
 #pragma unroll
-      for (u32 j = 0; j < 4; ++j) {
-        // fill < 32 here and a word adds at most 128: the ring never wraps
-        // onto positions still waiting.
-        u32 at = head + fill + ((excl >> (8 * j)) & 0xffu);
-        u32 m = owned[j];
-        while (m) {
-          ring[at++ & (kRing - 1)] = Pos(base + 128 * j + 4 * lane + ((__ffs(m) - 1) >> 3));
-          m &= m - 1;
+      for (u32 half = 0; half < 2; ++half) {
+        if ((lane >> 4) == half) {
+          u32 at = head + fill + incl - count - (half ? first_half : 0u);
+          for (u32 bits = m; bits; bits &= bits - 1)
+            ring[at++ & (kRing - 1)] = Pos(q + ((__ffs(bits) - 1) >> 2));
         }
-        fill += (totals >> (8 * j)) & 0xffu;
+        fill += half ? total - first_half : first_half;
         __syncwarp();
         while (fill >= 32) {
           batch(32);
@@ -535,6 +549,26 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
     }
     return k < 2 ? (k == 0 ? window.x : window.y) : (k == 2 ? window.z : window.w);
   };
+  // Match length of p against q < p, from 3 bytes known equal up to
+  // `limit`: four bytes a step from funnel-shifted word loads, the first
+  // differing byte from the lowest set bit of their difference.  Reads stay
+  // within the staged chunk's zero padding (position + limit + 7 <= n + 7).
+  const u32* chunk_words = reinterpret_cast<const u32*>(data);
+  auto load4 = [&](u32 x) -> u32 {
+    return __funnelshift_r(chunk_words[x >> 2], chunk_words[(x >> 2) + 1], (x & 3u) * 8u);
+  };
+  auto match_from = [&](u32 q, u32 p, u32 limit) -> u32 {
+    u32 m = 3;
+    while (m < limit) {
+      const u32 diff = load4(q + m) ^ load4(p + m);
+      if (diff) {
+        m += (__ffs(diff) - 1) >> 3;
+        break;
+      }
+      m += 4;
+    }
+    return min_u32(m, limit);
+  };
   // Level 2: the chain of p runs through prev[] (each entry is 1 + the last
   // earlier position with the same hash).  Comparing the byte at the current
   // best length first skips candidates that cannot be longer.
@@ -550,8 +584,7 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
       if (p - q > 32768u) break;
       if ((best < 3 || data[q + best] == data[p + best]) && data[q] == data[p] &&
           data[q + 1] == data[p + 1] && data[q + 2] == data[p + 2]) {
-        u32 m = 3;
-        while (m < limit && data[q + m] == data[p + m]) ++m;
+        const u32 m = match_from(q, p, limit);
         if (m > best) {
           best = m;
           at = q;
@@ -578,10 +611,7 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
     if (dist > 32768u || data[q] != data[p] || data[q + 1] != data[p + 1] ||
         data[q + 2] != data[p + 2])
       return 0;
-    const u32 limit = min_u32(n - p, 258u);
-    u32 m = 3;
-    while (m < limit && data[q + m] == data[p + m]) ++m;
-    return m;
+    return match_from(q, p, min_u32(n - p, 258u));
   };
   {
     const u32 a = min_u32(tid * seg, n), b = min_u32(a + seg, n);
@@ -1133,7 +1163,7 @@ size_t encode_smem_bytes(u32 chunk_bytes, bool in_smem) {
   const size_t bit_words = bitmap_words(chunk_bytes);
   if (chunk_bytes >= kLargeChunk)  // bitmaps and a table of u32 positions
     return (2 * bit_words * 4 + kHashSlots * 4 + 15) & ~size_t(15);
-  size_t bytes = data_bytes + 2 * bit_words * 4 + kHashSlots * 2;
+  size_t bytes = data_bytes + 2 * bit_words * 4 + kHashSlots * 2 + owner_words(chunk_bytes) * 4;
   if (in_smem) bytes += ((chunk_bytes + 7) & ~7u) * 2 + chunk_bytes + 16;
   return (bytes + 15) & ~size_t(15);
 }
