@@ -14,11 +14,11 @@ bounds (4096 and 4095 files of 64 KiB).  One step = every rank's share:
            rank's device time (CUDA events on the codec's stream), inputs
            resident in HBM and larger than L2 (L2 also flushed per step);
   e2e      the same step through the host-buffer counterparts of those calls
-           (decompress_zlib_batch_checked_host, compress_zlib_batch_padded_host:
-           same packed layouts and metadata, copies pipelined with the
-           kernels) from inputs in pinned host memory to results in pinned
-           host memory, copies inside the timed region (host wall clock,
-           slowest rank);
+           (decompress_zlib_batch_checked_host, and
+           compress_zlib_batch_packed_host, which returns the streams back
+           to back; copies pipelined with the kernels) from inputs in pinned
+           host memory to results in pinned host memory, copies inside the
+           timed region (host wall clock, slowest rank);
   roofline the dominant kernel's algorithmic bytes (C + U of the calls it
            served) over its event-timed device time, against the measured
            HBM copy bandwidth (MEASURED_PEAKS.json);
@@ -332,6 +332,9 @@ def groups_of(count, per):
 
 def run_gpu(args, rank, world):
     plan = plan_4a(world)
+    if args.profile_files:
+        # A small case of the same kernels for ncu captures: not a bench line.
+        plan = [p[:args.profile_files] for p in plan]
     mine = plan[rank]
     packed, streams = inputs_4a(mine)
     count = len(mine)
@@ -399,7 +402,7 @@ def run_gpu(args, rank, world):
     seconds, clocks, launched, kernels = timing.run(step, args.steps, world)
     seconds = max_over_ranks(torch, seconds, device, world)
     per_step = seconds / args.steps
-    total_units = 2 * FILES * FILE
+    total_units = 2 * sum(len(p) for p in plan) * FILE
     value = total_units / per_step / 1e9
     my_u = count * FILE
     line_roofline = roofline("config4a", kernels, args.steps, my_u + int(z_offsets[-1]),
@@ -425,20 +428,21 @@ def run_gpu(args, rank, world):
             # page locking.
             box.clear()
             out, meta = codec.decompress_zlib_batch_checked_host(z_pin, z_sizes, sizes, device)
-            slots, emeta = codec.compress_zlib_batch_padded_host(raw_pin, sizes, device,
-                                                                 chunk_bytes=CHUNK)
+            streams, emeta = codec.compress_zlib_batch_packed_host(raw_pin, sizes, device,
+                                                                   chunk_bytes=CHUNK)
             assert not meta.any() and not emeta[:, 1].any()
-            box["result"] = (out, slots, emeta)
+            box["result"] = (out, streams, emeta)
 
         e2e_seconds = wall_steps(torch, e2e_step, 1, args.e2e_steps)
-        out, slots, emeta = box["result"]
+        out, streams, emeta = box["result"]
         assert np.array_equal(out, packed) and int(emeta[:, 0].sum()) == encoded
+        assert streams.size == encoded
         e2e_seconds = max_over_ranks(torch, e2e_seconds, device, world)
         e2e = {"value": round(total_units / e2e_seconds / 1e9, 4), "unit": "GB/s",
                "h2d_bytes_per_step": int(z_offsets[-1]) + my_u,
-               "d2h_bytes_per_step": my_u + count * capacity + 16 * count,
+               "d2h_bytes_per_step": my_u + encoded + 16 * count,
                "timer": "host wall clock, slowest rank",
-               "calls": "decompress_zlib_batch_checked_host + compress_zlib_batch_padded_host",
+               "calls": "decompress_zlib_batch_checked_host + compress_zlib_batch_packed_host",
                "steps": args.e2e_steps}
 
     configs = None
@@ -470,6 +474,9 @@ def run_gpu(args, rank, world):
         "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks, "gpu_launches": launched,
         "configs": configs,
     }
+    if args.profile_files:
+        line["config"] = dict(CONFIG, profile_case_files_per_rank=args.profile_files)
+        line["profile_case"] = "a small case for profiler captures, not a benchmark result"
     print(json.dumps(line), flush=True)
 
 
@@ -603,14 +610,10 @@ def run_configs(args, torch, codec, device, timing):
         assert not emeta2[:, 1].any()
         z_pin = _pinned(torch, np.frombuffer(b"".join(streams), dtype=np.uint8))
         r_pin = _pinned(torch, np.frombuffer(b"".join(files), dtype=np.uint8))
-        zo = np.concatenate(([0], np.cumsum(in_sizes)))
-        ro = np.concatenate(([0], np.cumsum(sizes)))
-        z_views = [z_pin[zo[k]:zo[k + 1]] for k in range(len(files))]
-        r_views = [r_pin[ro[k]:ro[k + 1]] for k in range(len(files))]
 
         def e2e2():
-            codec.decompress_zlib_batch_host(z_views, sizes, device)
-            codec.compress_zlib_batch_host(r_views, device, chunk_bytes=CHUNK)
+            codec.decompress_zlib_batch_checked_host(z_pin, in_sizes, sizes, device)
+            codec.compress_zlib_batch_packed_host(r_pin, sizes, device, chunk_bytes=CHUNK)
 
         total = sum(sizes)
         out["config2"] = measure_config(
@@ -619,6 +622,8 @@ def run_configs(args, torch, codec, device, timing):
             {"workload": "4096 files (seed 2), log-uniform 256 B-256 KiB, 1% empty, config-2 "
                          "mix: batch decode of their zlib level-6 streams, batch compress at "
                          "32768",
+             "e2e_calls": "decompress_zlib_batch_checked_host + "
+                          "compress_zlib_batch_packed_host",
              "compression_ratio": round(int(emeta2[:, 0].sum()) / total, 5),
              "zlib6_ratio": round(sum(in_sizes) / total, 5)})
     if "3" in wanted:
@@ -674,6 +679,9 @@ def main():
     parser.add_argument("--config-warmup", type=int, default=3)
     parser.add_argument("--cpu-files", type=int, default=8192,
                         help="config-4a files in the CPU baseline's bounded sample")
+    parser.add_argument("--profile-files", type=int, default=0,
+                        help="only this many config-4a files per rank: a small case for "
+                             "profiler captures (its line is not a benchmark result)")
     args = parser.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -361,7 +361,7 @@ bool chunk_ok(int64_t chunk_bytes) { return chunk_bytes >= kMinChunk && chunk_by
 cudaError_t encode_files(const DeviceState& dev, const u8* in, u64 in_bytes,
                          std::vector<EncodeFile>& files, u32 chunk_bytes, u32 total_chunks,
                          u8* out, u32* meta, cudaStream_t stream, u32* range_adler = nullptr,
-                         u32 level = 1) {
+                         u32 level = 1, bool packed = false) {
   Workspace ws(dev.pool, stream);
   EncodeFile* d_files = nullptr;
   u8* slots = nullptr;
@@ -389,8 +389,14 @@ cudaError_t encode_files(const DeviceState& dev, const u8* in, u64 in_bytes,
       spill.prev = prev;
     }
   }
+  u64* bases = nullptr;
+  if (packed) {
+    CZ_TRY(ws.allocate(&bases, files.size()));
+    CZ_TRY(ws.allocate(&range_adler, files.size()));
+  }
   CZ_TRY(launch_encode(in, d_files, u32(files.size()), chunk_bytes, total_chunks, slots, sizes,
-                       status, adler, offsets, spill, out, meta, dev.info, stream, range_adler));
+                       status, adler, offsets, spill, out, meta, dev.info, stream, range_adler,
+                       bases));
   return ws.release();
 }
 
@@ -466,7 +472,7 @@ cudaError_t compress_range(const u8* in, u64 size, int64_t chunk_bytes, int last
 
 cudaError_t compress_batch(const u8* in, u64 in_bytes, const int64_t* sizes, u64 count,
                            int64_t chunk_bytes, u8* out, u64 out_bytes, u32* meta,
-                           cudaStream_t stream) {
+                           cudaStream_t stream, bool packed = false) {
   // CompressBatchImpl (codec_ffi.cu:1002-1063).
   if (!count || count > kMaxBlocks || !sizes || !meta) return cudaErrorInvalidValue;
   if (in_bytes > kMaxBytes || out_bytes > kMaxBytes || !chunk_ok(chunk_bytes))
@@ -495,7 +501,8 @@ cudaError_t compress_batch(const u8* in, u64 in_bytes, const int64_t* sizes, u64
   DeviceState* dev = nullptr;
   CZ_TRY(device_state(scope.device(), &dev));
   CZ_TRY(cudaMemsetAsync(out, 0, out_bytes, stream));
-  return encode_files(*dev, in, in_bytes, files, chunk, u32(total_chunks), out, meta, stream);
+  return encode_files(*dev, in, in_bytes, files, chunk, u32(total_chunks), out, meta, stream,
+                      nullptr, 1, packed);
 }
 
 cudaError_t decompress(const u8* in, u64 size, int64_t max_candidates, int64_t max_blocks,
@@ -879,6 +886,19 @@ int cuda_zlib_compress_batch(const uint8_t* input, uint64_t input_bytes,
   try {
     return int(cz::compress_batch(input, input_bytes, input_sizes, files, chunk_bytes, output,
                                   output_bytes, metadata, static_cast<cudaStream_t>(stream)));
+  } catch (...) {
+    return int(cudaErrorUnknown);
+  }
+}
+
+int cuda_zlib_compress_batch_packed(const uint8_t* input, uint64_t input_bytes,
+                                    const int64_t* input_sizes, uint64_t files,
+                                    int64_t chunk_bytes, uint8_t* output, uint64_t output_bytes,
+                                    uint32_t* metadata, void* stream) {
+  try {
+    return int(cz::compress_batch(input, input_bytes, input_sizes, files, chunk_bytes, output,
+                                  output_bytes, metadata, static_cast<cudaStream_t>(stream),
+                                  true));
   } catch (...) {
     return int(cudaErrorUnknown);
   }

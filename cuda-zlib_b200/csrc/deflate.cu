@@ -7,8 +7,9 @@
 // hash (enc_hash, :47-51).  This kernel exploits that:
 //
 //   1. stage the chunk in shared memory and fuse its Adler-32 partial sums;
-//   2. every position's candidate: warp w takes the positions whose hash
-//      is w mod 16, in order, and finds equal hashes 32 at a time by ballots;
+//   2. every position's candidate: rounds of 4096 positions are sorted into
+//      per-warp lists by hash mod 16; each warp takes its list in order and
+//      finds equal hashes 32 at a time by ballots;
 //   3. 256 threads each walk the greedy parse from the start of their own
 //      segment of the chunk, speculatively;
 //   4. one thread stitches the segments: an entry point that differs from the
@@ -40,7 +41,8 @@ constexpr u32 kEncThreads = 512;
 constexpr u32 kEncWarps = kEncThreads / 32;
 constexpr u32 kOwnerBits = 4;  // log2(kEncWarps): hash slots are split over the warps
 static_assert((1u << kOwnerBits) == kEncWarps, "one slot class per warp");
-constexpr u32 kRing = 256;     // per-warp ring of owned positions (a power of two)
+constexpr u32 kPerThread = 8;  // candidate rounds: consecutive positions per thread
+constexpr u32 kRoundPositions = kEncThreads * kPerThread;
 constexpr u32 kHashSlots = 8192;
 constexpr u32 kStitchRounds = 8;  // parallel stitch rounds before the serial finish
 constexpr u32 kStoredMax = 65535;  // bytes of one stored block
@@ -97,12 +99,6 @@ __device__ __forceinline__ u32 extent_of(u32 bits, bool final) {
 __host__ __device__ __forceinline__ u32 bitmap_words(u32 chunk_bytes) {
   return ((chunk_bytes + 31) / 32 + 1 + 3) & ~3u;
 }
-// Words of a chunk's owner-nibble array (8 positions a word), padded to 16
-// bytes so that the array after it starts 16-byte aligned.
-__host__ __device__ __forceinline__ u32 owner_words(u32 chunk_bytes) {
-  return ((chunk_bytes + 7) / 8 + 3) & ~3u;
-}
-
 // Stored blocks of an n-byte chunk's stored fallback (kStoredMax each).
 __host__ __device__ __forceinline__ u32 stored_blocks(u32 n) {
   return n ? (n + kStoredMax - 1) / kStoredMax : 1u;
@@ -124,7 +120,10 @@ struct EncodeShared {
   u8 depth[2][576];
   u8 rle_sym[320];
   u8 rle_extra[320];
-  Pos owned[kEncWarps][kRing];  // per-warp ring of positions awaiting a batch
+  Pos round_list[kRoundPositions];     // candidate round: positions by owner
+  u16 owner_count[kEncWarps][kEncWarps];   // per warp, per owner
+  u16 owner_before[kEncWarps][kEncWarps];  // per warp, per owner: earlier warps' count
+  u16 owner_total[kEncWarps], owner_start[kEncWarps];
   u32 seg_exit[kEncThreads];
   u32 seg_entry[kEncThreads];
   u32 seg_bits[kEncThreads];
@@ -373,8 +372,8 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
   const bool final = local + 1 == f.chunks && !(f.flags & kEncodeNotLast);
   const u8* src = in + f.in_offset + start;
 
-  // Shared layout: data | member bits | match bits | hash table | owner
-  // nibbles | prev | len (large chunks: member bits | match bits | hash table).
+  // Shared layout: data | member bits | match bits | hash table | prev | len
+  // (large chunks: member bits | match bits | hash table).
   const u32 data_bytes = (chunk_bytes + 16 + 15) & ~15u;
   const u32 bit_words = bitmap_words(chunk_bytes);
   const u64 spill_at = spill_offset(f.in_offset + start, g);
@@ -382,11 +381,10 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
   u32* member = reinterpret_cast<u32*>(kLarge ? smem : smem + data_bytes);
   u32* ismatch = member + bit_words;
   Pos* table = reinterpret_cast<Pos*>(ismatch + bit_words);
-  u32* owner_nibbles = reinterpret_cast<u32*>(table + kHashSlots);
   Pos* prev;
   u8* lenv;
   if (in_smem) {
-    prev = reinterpret_cast<Pos*>(owner_nibbles + owner_words(chunk_bytes));
+    prev = table + kHashSlots;
     lenv = reinterpret_cast<u8*>(prev + ((chunk_bytes + 7) & ~7u));
   } else {
     // 16-byte aligned (lenv is read as words), kSpillGap entries apart.
@@ -426,16 +424,17 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
 
   // 2. Candidates: prev[p] = 1 + the last earlier position with hash(p), or
   // 0 (the reference inserts every position into its one-entry table in
-  // order, so this is the table's entry when p is reached).  First every
-  // position's owner, its hash mod 16, goes to a nibble array (8 positions a
-  // word).  Then warp w handles the table slots h with h % 16 == w: it
-  // gathers the positions it owns in order into batches of 32, hashes them
-  // again from the staged chunk and, per batch, finds equal hashes among the
-  // lanes by ballots over the hash bits.  A lane's candidate is its last
-  // earlier equal lane, else the table; the last lane of each hash writes the
-  // table.  Slots are disjoint between warps, so the warps never wait on one
-  // another, and nothing on a batch's path waits for global memory (chunks
-  // above 64 KiB keep the nibbles in the spill, in place of the lengths).
+  // order, so this is the table's entry when p is reached).  Warp w owns the
+  // table slots h with h % 16 == w.  Rounds of kRoundPositions positions,
+  // eight consecutive ones per thread: the block sorts the round's positions
+  // into per-owner lists in position order (counts per owner packed four to
+  // a u64 in 16-bit fields, a warp scan, then per-warp and per-owner
+  // offsets), and each warp takes its list in batches of 32.  In a batch the
+  // lanes hash their positions again from the staged chunk and find equal
+  // hashes by ballots over the hash bits; a lane's candidate is its last
+  // earlier equal lane, else the table, and the last lane of each hash writes
+  // the table.  Slots are disjoint between warps, so within a round the
+  // warps never wait on one another.
   const u32 hashed = n >= 3 ? n - 2 : 0;  // positions 0..n-3 are hashed
   {
     const u32* words = reinterpret_cast<const u32*>(data);
@@ -444,23 +443,10 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
       const u32 v = __funnelshift_r(lo, hi, (p & 3u) * 8u) & 0xffffffu;
       return (v * 2654435761u) >> 19;
     };
-    u32* owners = kLarge ? reinterpret_cast<u32*>(lenv) : owner_nibbles;
-    const u32 owner_words = (hashed + 7) / 8;
-    for (u32 w = tid; w < owner_words; w += kEncThreads) {
-      u32 nibbles = 0;
-#pragma unroll
-      for (u32 k = 0; k < 8; ++k) {
-        const u32 p = 8 * w + k;
-        if (p < hashed) nibbles |= (hash_at(p) & (kEncWarps - 1)) << (4 * k);
-      }
-      owners[w] = nibbles;
-    }
-    __syncthreads();
-    Pos* ring = s.owned[warp];
-    u32 head = 0, fill = 0;
-    auto batch = [&](u32 count) {
+    Pos* list = s.round_list;
+    auto batch = [&](u32 first, u32 count) {
       const bool valid = lane < count;
-      const u32 pos = valid ? ring[(head + lane) & (kRing - 1)] : 0u;
+      const u32 pos = valid ? u32(list[first + lane]) : 0u;
       const u32 h = valid ? hash_at(pos) : 0u;
       const u32 key = h >> kOwnerBits;  // the low bits equal the warp index
       u32 same = __ballot_sync(kFullMask, valid);
@@ -479,51 +465,87 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
         prev[pos] = Pos(candidate);
       }
       __syncwarp();
-      head = (head + count) & (kRing - 1);
     };
-    // An iteration covers 256 positions: lane i reads the nibble word of
-    // positions base + 8 i .. + 7.  A nibble is owned when it equals the warp
-    // index: xor-ed with the index, (x & 7) + 7 sets its top bit exactly when
-    // its low bits are nonzero, so ~(t | x) keeps the top bit of zero
-    // nibbles.  One warp scan of the per-lane counts places every owned
-    // position in order; lanes 0-15 and 16-31 fill the ring in two halves
-    // (at most 128 positions each, with fewer than 32 waiting before), each
-    // followed by the batches it completes.
-    const u32 pattern = warp * 0x11111111u;
-    for (u32 base = 0; base < hashed; base += 256) {
-      const u32 q = base + 8 * lane;
-      u32 m = 0;
-      if (q < hashed) {
-        const u32 x = owners[q >> 3] ^ pattern;
-        const u32 t = (x & 0x77777777u) + 0x77777777u;
-        m = ~(t | x) & 0x88888888u;
-        if (hashed - q < 8) m &= (1u << (4 * (hashed - q))) - 1u;
+    for (u32 base = 0; base < hashed; base += kRoundPositions) {
+      const u32 p0 = base + kPerThread * tid;
+      // Owner o's count in 16-bit field o % 4 of c[o / 4] (no runtime
+      // indexing, so the four words stay in registers).  Owners are hashed
+      // again for the scatter below rather than kept across the barriers.
+      auto owner_of = [&](u32 p) -> u32 {
+        return p < hashed ? hash_at(p) & (kEncWarps - 1) : kEncWarps;
+      };
+      u64 c0 = 0, c1 = 0, c2 = 0, c3 = 0;
+#pragma unroll
+      for (u32 k = 0; k < kPerThread; ++k) {
+        const u32 o = owner_of(p0 + k);
+        const u32 q = o >> 2;
+        const u64 one = 1ull << (16 * (o & 3u));
+        c0 += q == 0 ? one : 0;
+        c1 += q == 1 ? one : 0;
+        c2 += q == 2 ? one : 0;
+        c3 += q == 3 ? one : 0;
       }
-      const u32 count = __popc(m);
-      u32 incl = count;
+      u64 i0 = c0, i1 = c1, i2 = c2, i3 = c3;
 #pragma unroll
       for (u32 o = 1; o < 32; o <<= 1) {
-        const u32 v = __shfl_up_sync(kFullMask, incl, o);
-        if (lane >= o) incl += v;
+        const u64 v0 = __shfl_up_sync(kFullMask, i0, o), v1 = __shfl_up_sync(kFullMask, i1, o);
+        const u64 v2 = __shfl_up_sync(kFullMask, i2, o), v3 = __shfl_up_sync(kFullMask, i3, o);
+        if (lane >= o) {
+          i0 += v0;
+          i1 += v1;
+          i2 += v2;
+          i3 += v3;
+        }
       }
-      const u32 first_half = __shfl_sync(kFullMask, incl, 15);
-      const u32 total = __shfl_sync(kFullMask, incl, 31);
+      const u64 incl[4] = {i0, i1, i2, i3};
+      if (lane == 31) {
 #pragma unroll
-      for (u32 half = 0; half < 2; ++half) {
-        if ((lane >> 4) == half) {
-          u32 at = head + fill + incl - count - (half ? first_half : 0u);
-          for (u32 bits = m; bits; bits &= bits - 1)
-            ring[at++ & (kRing - 1)] = Pos(q + ((__ffs(bits) - 1) >> 2));
+        for (u32 o = 0; o < kEncWarps; ++o)
+          s.owner_count[warp][o] = u16(incl[o >> 2] >> (16 * (o & 3u)));
+      }
+      __syncthreads();
+      if (warp == 0) {
+        // Lane o < 16: owner o's offset before each warp, its total, and the
+        // start of its list (owners' lists one after another).
+        u32 running = 0;
+        if (lane < kEncWarps) {
+          for (u32 w = 0; w < kEncWarps; ++w) {
+            s.owner_before[w][lane] = u16(running);
+            running += s.owner_count[w][lane];
+          }
         }
-        fill += half ? total - first_half : first_half;
-        __syncwarp();
-        while (fill >= 32) {
-          batch(32);
-          fill -= 32;
+        u32 start = running;
+#pragma unroll
+        for (u32 o = 1; o < 32; o <<= 1) {
+          const u32 v = __shfl_up_sync(kFullMask, start, o);
+          if (lane >= o) start += v;
+        }
+        if (lane < kEncWarps) {
+          s.owner_total[lane] = u16(running);
+          s.owner_start[lane] = u16(start - running);
         }
       }
+      __syncthreads();
+      u64 n0 = i0 - c0, n1 = i1 - c1, n2 = i2 - c2, n3 = i3 - c3;  // earlier lanes' counts
+#pragma unroll
+      for (u32 k = 0; k < kPerThread; ++k) {
+        const u32 o = owner_of(p0 + k);
+        if (o >= kEncWarps) continue;
+        const u32 q = o >> 2, field = 16 * (o & 3u);
+        const u64 seen = q == 0 ? n0 : q == 1 ? n1 : q == 2 ? n2 : n3;
+        const u32 at = s.owner_start[o] + s.owner_before[warp][o] + u32((seen >> field) & 0xffffu);
+        const u64 one = 1ull << field;
+        n0 += q == 0 ? one : 0;
+        n1 += q == 1 ? one : 0;
+        n2 += q == 2 ? one : 0;
+        n3 += q == 3 ? one : 0;
+        list[at] = Pos(p0 + k);
+      }
+      __syncthreads();
+      const u32 first = s.owner_start[warp], total = s.owner_total[warp];
+      for (u32 i = 0; i < total; i += 32) batch(first + i, min_u32(32, total - i));
+      __syncthreads();
     }
-    if (fill) batch(fill);
   }
   __syncthreads();
 
@@ -1054,7 +1076,8 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
 constexpr u32 kFinishWarps = 8;
 __global__ void __launch_bounds__(kFinishWarps * 32)
 encode_finish_kernel(const EncodeFile* files, u32 nfiles, const u32* sizes, const u32* status,
-                     const u64* adler, u64* offsets, u8* out, u32* meta, u32* range_adler) {
+                     const u64* adler, u64* offsets, u8* out, u32* meta, u32* range_adler,
+                     u32 defer_wrapper) {
   __shared__ u64 part_bytes[kFinishWarps], part_s1[kFinishWarps], part_s2[kFinishWarps];
   __shared__ u32 part_bad[kFinishWarps];
   const u32 lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
@@ -1119,7 +1142,10 @@ encode_finish_kernel(const EncodeFile* files, u32 nfiles, const u32* sizes, cons
     u8* dst = out + file.out_offset;
     const u32 checksum = adler_finish(t1, t2, file.in_size);
     if (range_adler) range_adler[f] = st ? 0u : checksum;
-    if (!st && gzip) {
+    if (defer_wrapper) {
+      // Packed output: encode_wrap_kernel writes the wrapper once the file's
+      // place is known (range_adler holds the checksum).
+    } else if (!st && gzip) {
       // ID1 ID2 CM=8 FLG=0 MTIME=0 XFL=0 OS=255 (unknown); the trailer
       // (CRC-32, ISIZE) comes from launch_gzip_trailer.
       const u8 header[10] = {0x1f, 0x8b, 8, 0, 0, 0, 0, 0, 0, 0xff};
@@ -1137,11 +1163,55 @@ encode_finish_kernel(const EncodeFile* files, u32 nfiles, const u32* sizes, cons
   }
 }
 
+// Packed output: each file's stream starts where the previous file's ends
+// (failed files take no bytes).  One CTA scans the encoded lengths.
+__global__ void encode_scan_kernel(u32 nfiles, const u32* meta, u64* bases) {
+  __shared__ u64 warp_total[32];
+  __shared__ u64 carry;
+  const u32 lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  for (u32 base = 0; base < nfiles; base += blockDim.x) {
+    const u32 f = base + threadIdx.x;
+    const u64 v = f < nfiles && !meta[2 * f + 1] ? u64(meta[2 * f]) : 0u;
+    u64 incl = v;
+    for (u32 o = 1; o < 32; o <<= 1) {
+      const u64 t = __shfl_up_sync(kFullMask, incl, o);
+      if (lane >= o) incl += t;
+    }
+    if (lane == 31) warp_total[warp] = incl;
+    __syncthreads();
+    u64 before = carry;
+    for (u32 w = 0; w < warp; ++w) before += warp_total[w];
+    if (f < nfiles) bases[f] = before + incl - v;
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) carry = before + incl;
+    __syncthreads();
+  }
+}
+
+// Packed output: the zlib header and Adler-32 trailer of every file that
+// encoded, at its packed place.
+__global__ void encode_wrap_kernel(u32 nfiles, const u32* meta, const u64* bases,
+                                   const u32* checksums, u8* out) {
+  const u32 f = blockIdx.x * blockDim.x + threadIdx.x;
+  if (f >= nfiles || meta[2 * f + 1]) return;
+  u8* dst = out + bases[f];
+  const u32 total = meta[2 * f], checksum = checksums[f];
+  dst[0] = 0x78;
+  dst[1] = 0x01;
+  dst[total - 4] = u8(checksum >> 24);
+  dst[total - 3] = u8(checksum >> 16);
+  dst[total - 2] = u8(checksum >> 8);
+  dst[total - 1] = u8(checksum);
+}
+
 // Copy every chunk's slot to its place in its file's output (skipped for
-// files whose finish reported an error).
+// files whose finish reported an error): the file's padded slot, or with
+// `bases` its packed place.
 __global__ void encode_pack_kernel(const EncodeFile* files, u32 nfiles, const u8* slots,
                                    const u32* sizes, const u64* offsets, const u32* meta, u8* out,
-                                   u32 chunk_bytes, u32 total_chunks) {
+                                   u32 chunk_bytes, u32 total_chunks, const u64* bases) {
   const u32 g = blockIdx.x;
   if (g >= total_chunks) return;
   u32 lo = 0, hi = nfiles;
@@ -1154,7 +1224,7 @@ __global__ void encode_pack_kernel(const EncodeFile* files, u32 nfiles, const u8
   const u32 size = sizes[g];
   const u64 start = u64(g - files[lo].first_chunk) * chunk_bytes;
   const u8* src = slots + slot_start(files[lo].in_offset + start, g);
-  u8* dst = out + files[lo].out_offset + offsets[g];
+  u8* dst = out + (bases ? bases[lo] : files[lo].out_offset) + offsets[g];
   for (u32 i = threadIdx.x; i < size; i += blockDim.x) dst[i] = src[i];
 }
 
@@ -1163,7 +1233,7 @@ size_t encode_smem_bytes(u32 chunk_bytes, bool in_smem) {
   const size_t bit_words = bitmap_words(chunk_bytes);
   if (chunk_bytes >= kLargeChunk)  // bitmaps and a table of u32 positions
     return (2 * bit_words * 4 + kHashSlots * 4 + 15) & ~size_t(15);
-  size_t bytes = data_bytes + 2 * bit_words * 4 + kHashSlots * 2 + owner_words(chunk_bytes) * 4;
+  size_t bytes = data_bytes + 2 * bit_words * 4 + kHashSlots * 2;
   if (in_smem) bytes += ((chunk_bytes + 7) & ~7u) * 2 + chunk_bytes + 16;
   return (bytes + 15) & ~size_t(15);
 }
@@ -1189,7 +1259,8 @@ cudaError_t configure_encode(int* max_dynamic_smem) {
 cudaError_t launch_encode(const u8* in, const EncodeFile* files, u32 nfiles, u32 chunk_bytes,
                           u32 total_chunks, u8* slots, u32* sizes, u32* status, u64* adler,
                           u64* offsets, const EncodeSpill& spill, u8* out, u32* meta,
-                          const DeviceInfo& dev, cudaStream_t stream, u32* range_adler) {
+                          const DeviceInfo& dev, cudaStream_t stream, u32* range_adler,
+                          u64* packed_bases) {
   // Without spill buffers (the allocation-free entry point) the per-position
   // arrays stay in shared memory.
   const bool in_smem = spill.prev == nullptr;
@@ -1208,15 +1279,25 @@ cudaError_t launch_encode(const u8* in, const EncodeFile* files, u32 nfiles, u32
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   note_launch();
-  encode_finish_kernel<<<nfiles, kFinishWarps * 32, 0, stream>>>(files, nfiles, sizes, status,
-                                                                 adler, offsets, out, meta,
-                                                                 range_adler);
+  encode_finish_kernel<<<nfiles, kFinishWarps * 32, 0, stream>>>(
+      files, nfiles, sizes, status, adler, offsets, out, meta, range_adler,
+      packed_bases ? 1u : 0u);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
+  if (packed_bases) {
+    note_launch();
+    encode_scan_kernel<<<1, 1024, 0, stream>>>(nfiles, meta, packed_bases);
+    note_launch();
+    encode_wrap_kernel<<<(nfiles + 255) / 256, 256, 0, stream>>>(nfiles, meta, packed_bases,
+                                                                 range_adler, out);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
   profile_begin("encode_pack_kernel", stream);
   note_launch();
   encode_pack_kernel<<<total_chunks, 256, 0, stream>>>(files, nfiles, slots, sizes, offsets, meta,
-                                                       out, chunk_bytes, total_chunks);
+                                                       out, chunk_bytes, total_chunks,
+                                                       packed_bases);
   profile_end(stream);
   return cudaGetLastError();
 }

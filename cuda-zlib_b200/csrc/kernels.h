@@ -106,7 +106,10 @@ cudaError_t launch_encode(const u8* in, const EncodeFile* files, u32 nfiles, u32
                           u32 total_chunks, u8* slots, u32* sizes, u32* status, u64* adler,
                           u64* offsets, const EncodeSpill& spill, u8* out, u32* meta,
                           const DeviceInfo& dev, cudaStream_t stream,
-                          u32* range_adler = nullptr);
+                          u32* range_adler = nullptr, u64* packed_bases = nullptr);
+// packed_bases (files u64): the streams go back to back from out[0] in file
+// order (failed files take no bytes); range_adler must then be set (files
+// u32: each file's Adler-32 for its trailer).
 
 // Block-parallel inflate of one large stream (inflate_parallel.cu).
 struct ParallelScratch {

@@ -12,7 +12,8 @@ CPU codec fallback.
 from ._codec import (compress_zlib, compress_zlib_host, decompress_zlib, compile_kernels,
                      compress_zlib_padded, decompress_zlib_checked,
                      decompress_zlib_host, workspace_pool_stats, trim_workspace_pool)
-from ._codec import (compress_zlib_batch_padded_host, decompress_zlib_batch_checked_host)
+from ._codec import (compress_zlib_batch_padded_host, decompress_zlib_batch_checked_host,
+                     compress_zlib_batch_packed, compress_zlib_batch_packed_host)
 from ._codec import (compress_zlib_batch_padded, decompress_zlib_batch_checked,
                      compress_zlib_batch, decompress_zlib_batch,
                      compress_zlib_batch_host, decompress_zlib_batch_host)
@@ -29,6 +30,7 @@ __all__ = ["compress_zlib", "compress_zlib_host", "decompress_zlib", "compile_ke
            "compress_zlib_batch", "decompress_zlib_batch",
            "compress_zlib_batch_host", "decompress_zlib_batch_host",
            "compress_zlib_batch_padded_host", "decompress_zlib_batch_checked_host",
+           "compress_zlib_batch_packed", "compress_zlib_batch_packed_host",
            "compress_deflate", "compress_deflate_padded", "decompress_deflate",
            "decompress_deflate_checked", "compress_gzip", "compress_gzip_padded",
            "compress_gzip_host", "decompress_gzip", "decompress_gzip_checked",

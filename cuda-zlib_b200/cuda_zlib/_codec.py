@@ -351,15 +351,7 @@ def _i64_array(values):
     return array
 
 
-def compress_zlib_batch_padded(data, input_sizes, device=0, *, chunk_bytes=32768):
-    """Compress packed independent files in one call, without a host sync.
-
-    ``input_sizes`` lists the file lengths (their sum is len(data)).  Returns a
-    flat uint8 buffer of consecutive padded slots and uint32 metadata of shape
-    (files, 2) with [encoded_length, status] per file.  A slot has
-    ``size + 5 * max(1, ceil(size / chunk_bytes)) + 6`` bytes for chunk_bytes
-    up to 65535 (larger chunks count ceil(chunk / 65535) stored blocks each).
-    """
+def _batch_encode_call(data, input_sizes, device, chunk_bytes, entry):
     sizes = _batch_sizes(input_sizes, "input_sizes")
     if _input_size(data) != sum(sizes):
         raise ValueError("packed input length differs from input_sizes total")
@@ -372,11 +364,37 @@ def compress_zlib_batch_padded(data, input_sizes, device=0, *, chunk_bytes=32768
     with torch.cuda.device(selected):
         output = torch.empty(total, dtype=torch.uint8, device=selected)
         metadata = torch.empty((len(sizes), 2), dtype=torch.uint32, device=selected)
-        _native.check(lib.cuda_zlib_compress_batch(
+        _native.check(getattr(lib, entry)(
             _ptr(raw), sum(sizes), _i64_array(sizes), len(sizes), chunk_bytes,
             _ptr(output), total, metadata.data_ptr(), _stream(selected)),
             "CUDA batch compression")
     return output, metadata
+
+
+def compress_zlib_batch_packed(data, input_sizes, device=0, *, chunk_bytes=32768):
+    """compress_zlib_batch_padded with the streams back to back.
+
+    No reference counterpart.  Same arguments, bounds and metadata; the
+    output buffer has the padded size, but file k's stream starts at the sum
+    of the earlier files' encoded lengths (failed files take no bytes) and the
+    rest is zero, so copying ``output[:metadata[:, 0].sum()]`` moves only the
+    encoded bytes.  No host sync.
+    """
+    return _batch_encode_call(data, input_sizes, device, chunk_bytes,
+                              "cuda_zlib_compress_batch_packed")
+
+
+def compress_zlib_batch_padded(data, input_sizes, device=0, *, chunk_bytes=32768):
+    """Compress packed independent files in one call, without a host sync.
+
+    ``input_sizes`` lists the file lengths (their sum is len(data)).  Returns a
+    flat uint8 buffer of consecutive padded slots and uint32 metadata of shape
+    (files, 2) with [encoded_length, status] per file.  A slot has
+    ``size + 5 * max(1, ceil(size / chunk_bytes)) + 6`` bytes for chunk_bytes
+    up to 65535 (larger chunks count ceil(chunk / 65535) stored blocks each).
+    """
+    return _batch_encode_call(data, input_sizes, device, chunk_bytes,
+                              "cuda_zlib_compress_batch")
 
 
 def decompress_zlib_batch_checked(payload, input_sizes, expected_sizes, device=0,
@@ -553,6 +571,30 @@ def compress_zlib_batch_padded_host(data, input_sizes, device=0, *, chunk_bytes=
     return slots, meta
 
 
+def compress_zlib_batch_packed_host(data, input_sizes, device=0, *, chunk_bytes=32768):
+    """Host-buffer batch compression returning the streams back to back.
+
+    No reference counterpart.  Packed files in host memory -> ``(streams,
+    metadata)``: every file's stream in file order with nothing between them
+    (a failed file takes no bytes) and (files, 2) uint32 [encoded_length,
+    status], read-only NumPy arrays in pinned memory.  Pipelined like
+    compress_zlib_batch_padded_host, but each group copies only its encoded
+    bytes back (the device packs them with compress_zlib_batch_packed).
+    """
+    sizes = _host_sizes(input_sizes, "input_sizes")
+    _check_chunk(chunk_bytes)
+    packed = _host_packed(data, sizes, "input")
+    capacities, chunks, blocks = _host_layouts(sizes, chunk_bytes)
+    selected = _select_device(device)
+    host, meta = _hostio.encode(_torch(), selected, packed, sizes, capacities, chunks,
+                                chunk_bytes, _HOST_LIMITS, compact=True)
+    streams = host.numpy()
+    streams.flags.writeable = False
+    meta = meta.view(np.uint32)
+    meta.flags.writeable = False
+    return streams, meta
+
+
 def _host_layouts(sizes, chunk_bytes):
     """Vectorised _layout: (capacities, chunks, blocks) per file."""
     chunks = np.maximum(1, -(-sizes // chunk_bytes))
@@ -608,11 +650,11 @@ def compress_zlib_batch_host(inputs, device=0, *, chunk_bytes=32768):
     if sizes.max() > _MAX_BYTES:
         raise ValueError("inputs exceeds size limit (2**28 bytes)")
     packed = _hostio.pack(views, _torch())
-    slots, meta = compress_zlib_batch_padded_host(packed, sizes, device, chunk_bytes=chunk_bytes)
+    streams, meta = compress_zlib_batch_packed_host(packed, sizes, device,
+                                                    chunk_bytes=chunk_bytes)
     _first_failure(meta, 1, "CUDA batch compression")
-    starts = np.concatenate(([0], np.cumsum(_host_layouts(sizes, chunk_bytes)[0])))
-    ends = starts[:-1] + meta[:, 0]
-    return tuple(slots[a:b].tobytes() for a, b in zip(starts[:-1].tolist(), ends.tolist()))
+    bounds = np.concatenate(([0], np.cumsum(meta[:, 0], dtype=np.int64))).tolist()
+    return tuple(streams[bounds[i]:bounds[i + 1]].tobytes() for i in range(len(views)))
 
 
 def decompress_zlib_batch_host(payloads, expected_sizes, device=0):

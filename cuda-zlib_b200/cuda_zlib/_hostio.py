@@ -134,12 +134,18 @@ def _i64(values):
     return (ctypes.c_int64 * len(values))(*values)
 
 
-def run(torch, device, packed, in_sizes, out_sizes, units, limits, call):
+def run(torch, device, packed, in_sizes, out_sizes, units, limits, call, compact=False):
     """Push the packed files through stage -> copy in -> call -> copy out.
 
     call(a, b, dev_in, in_bytes, dev_out, out_bytes, dev_meta, stream) issues
     the batch call of files [a, b).  Returns (pinned host output holding every
     group's dev_out, int32 metadata of shape (files, 2)).
+
+    compact: the call packs its files' streams at the front of dev_out
+    (metadata [length, status]); each group's copy out then takes only the
+    sum of its lengths, read from its metadata.  The host waits for a
+    group's metadata only after issuing the next group's call, so the GPU
+    stays busy; the returned output holds the streams back to back.
     """
     in_sizes = np.asarray(in_sizes, dtype=np.int64)
     out_sizes = np.asarray(out_sizes, dtype=np.int64)
@@ -167,6 +173,22 @@ def run(torch, device, packed, in_sizes, out_sizes, units, limits, call):
                     for _ in range(sets)]
         consumed = [None] * sets   # the call that last read dev_in[j]
         drained = [None] * sets    # the copy out that last read dev_out[j]
+        waiting = None             # compact: (j, a, b, metadata event) of the last group
+        written = 0
+
+        def copy_compact(j, a, b, meta_ready):
+            nonlocal written
+            meta_ready.synchronize()
+            meta = host_meta.numpy()[a:b]
+            n = int(meta[:, 0][meta[:, 1] == 0].astype(np.int64).sum())
+            with torch.cuda.stream(copy_out):
+                if n:
+                    host_out[written:written + n].copy_(dev_out[j][:n], non_blocking=True)
+                finished = torch.cuda.Event()
+                finished.record(copy_out)
+            drained[j] = finished
+            written += n
+
         for k, (a, b) in enumerate(groups):
             j = k % sets
             src = source.get(k, a, b)
@@ -188,15 +210,24 @@ def run(torch, device, packed, in_sizes, out_sizes, units, limits, call):
             consumed[j] = done
             with torch.cuda.stream(copy_out):
                 copy_out.wait_event(done)
-                if n_out:
+                if n_out and not compact:
                     host_out[int(out_off[a]):int(out_off[b])].copy_(dev_out[j][:n_out],
                                                                     non_blocking=True)
                 host_meta[a:b].copy_(dev_meta[j][:b - a], non_blocking=True)
                 finished = torch.cuda.Event()
                 finished.record(copy_out)
-            drained[j] = finished
+            if not compact:
+                drained[j] = finished
+                continue
+            if waiting is not None:
+                copy_compact(*waiting)
+            waiting = (j, a, b, finished)
+        if waiting is not None:
+            copy_compact(*waiting)
         copy_out.synchronize()
         compute.wait_stream(copy_in)
+    if compact:
+        return host_out[:written], host_meta.numpy()[:files]
     return host_out, host_meta.numpy()[:files]
 
 
@@ -215,18 +246,21 @@ def decode(torch, device, packed, in_sizes, out_sizes, limits):
                limits, call)
 
 
-def encode(torch, device, packed, in_sizes, capacities, chunks, chunk_bytes, limits):
-    """Packed host files -> (pinned padded slots, int32 [length, status] pairs)."""
+def encode(torch, device, packed, in_sizes, capacities, chunks, chunk_bytes, limits,
+           compact=False):
+    """Packed host files -> (pinned padded slots, int32 [length, status] pairs);
+    compact: the streams back to back instead of padded slots."""
     lib = _native.library()
     in_list = [int(v) for v in in_sizes]
+    entry = lib.cuda_zlib_compress_batch_packed if compact else lib.cuda_zlib_compress_batch
 
     def call(a, b, dev_in, n_in, dev_out, n_out, dev_meta, stream):
-        _native.check(lib.cuda_zlib_compress_batch(
+        _native.check(entry(
             dev_in.data_ptr(), n_in, _i64(in_list[a:b]), b - a, chunk_bytes,
             dev_out.data_ptr(), n_out, dev_meta.data_ptr(), stream.cuda_stream),
             "CUDA batch compression")
 
-    return run(torch, device, packed, in_list, capacities, chunks, limits, call)
+    return run(torch, device, packed, in_list, capacities, chunks, limits, call, compact)
 
 
 def pack(views, torch):

@@ -40,6 +40,9 @@ def _configure(library):
     library.cuda_zlib_compress_batch.argtypes = [_u8p, ctypes.c_uint64, _i64p, ctypes.c_uint64,
                                                  ctypes.c_int64, _u8p, ctypes.c_uint64, _u8p,
                                                  ctypes.c_void_p]
+    library.cuda_zlib_compress_batch_packed.argtypes = [_u8p, ctypes.c_uint64, _i64p,
+                                                        ctypes.c_uint64, ctypes.c_int64, _u8p,
+                                                        ctypes.c_uint64, _u8p, ctypes.c_void_p]
     library.cuda_zlib_decompress_batch.argtypes = [_u8p, ctypes.c_uint64, _i64p, _i64p,
                                                    ctypes.c_uint64, _u8p, _u8p, ctypes.c_uint64,
                                                    _u8p, ctypes.c_void_p]
@@ -57,6 +60,7 @@ def _configure(library):
                                               ctypes.POINTER(ctypes.c_uint64)]
     for name in ("cuda_zlib_compress", "cuda_zlib_decompress", "cuda_zlib_compress_batch",
                  "cuda_zlib_decompress_batch", "cuda_zlib_compress_range",
+                 "cuda_zlib_compress_batch_packed",
                  "cuda_zlib_compress_format", "cuda_zlib_decompress_format",
                  "cuda_zlib_gzip_header"):
         getattr(library, name).restype = ctypes.c_int

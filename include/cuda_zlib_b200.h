@@ -98,6 +98,17 @@ int cuda_zlib_decompress_batch(const uint8_t* input, uint64_t input_bytes,
                                uint64_t files, const uint32_t* encoded_metadata, uint8_t* output,
                                uint64_t output_bytes, uint32_t* metadata, void* stream);
 
+/* Batch compression with packed output.  No counterpart in the reference.
+ * Same arguments, bounds and metadata as cuda_zlib_compress_batch (output
+ * sized for the padded slots), but the streams go back to back from
+ * output[0] in file order (a failed file takes no bytes; the rest of output
+ * is zero), so a caller copying the streams to the host copies only the
+ * encoded bytes: the sum of metadata's lengths. */
+int cuda_zlib_compress_batch_packed(const uint8_t* input, uint64_t input_bytes,
+                                    const int64_t* input_sizes, uint64_t files,
+                                    int64_t chunk_bytes, uint8_t* output,
+                                    uint64_t output_bytes, uint32_t* metadata, void* stream);
+
 /* gzip (RFC 1952) and raw Deflate (RFC 1951) wrappers around the same body
  * codec.  No counterpart in the reference, which supports RFC 1950 only and
  * rejects gzip members with status 16 (_codec.py:105-111).

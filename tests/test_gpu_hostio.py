@@ -98,3 +98,33 @@ def test_host_batch_statuses(codec):
     assert meta[:, 0].tolist() == want and want[5] == 21
     with pytest.raises(codec.CodecError, match="file 5"):
         codec.decompress_zlib_batch_host(streams, expected, 0)
+
+
+@pytest.mark.parametrize("chunk", [4096, 32768])
+def test_packed_batch_compression(codec, monkeypatch, chunk):
+    """compress_zlib_batch_packed: the padded call's streams back to back,
+    zeros after; the host variant copies only those bytes, group by group
+    (many groups here), and compress_zlib_batch_host builds on it."""
+    from cuda_zlib import _hostio
+    monkeypatch.setattr(_hostio, "_GROUP_MIN", 1 << 20)
+    files = _files(500, 5)
+    sizes = [len(f) for f in files]
+    joined = b"".join(files)
+    padded, pmeta = codec.compress_zlib_batch_padded(joined, sizes, 0, chunk_bytes=chunk)
+    packed, meta = codec.compress_zlib_batch_packed(joined, sizes, 0, chunk_bytes=chunk)
+    pmeta, meta = pmeta.cpu().numpy(), meta.cpu().numpy()
+    assert np.array_equal(meta, pmeta) and not meta[:, 1].any()
+    capacities = [oracle.capacity(n, chunk) for n in sizes]
+    starts = np.concatenate(([0], np.cumsum(capacities)))
+    slots = padded.cpu().numpy()
+    want = b"".join(slots[starts[k]:starts[k] + meta[k, 0]].tobytes() for k in range(len(files)))
+    host_packed = packed.cpu().numpy()
+    total = int(meta[:, 0].sum())
+    assert host_packed[:total].tobytes() == want and not host_packed[total:].any()
+    streams, hmeta = codec.compress_zlib_batch_packed_host(joined, sizes, 0, chunk_bytes=chunk)
+    assert not streams.flags.writeable and np.array_equal(hmeta, meta)
+    assert streams.tobytes() == want
+    expected = [oracle.compress(f, chunk) for f in files[:50]]
+    per_file = codec.compress_zlib_batch_host(files, 0, chunk_bytes=chunk)
+    assert list(per_file[:50]) == expected
+    assert b"".join(per_file) == want
