@@ -71,7 +71,8 @@ def plan_groups(in_sizes, out_sizes, units, limits):
     """Boundaries [a, b) of consecutive files whose totals stay within
     `limits` = (units, input bytes, output bytes) of one call; groups are cut
     at about a quarter of the batch (at least _GROUP_MIN output bytes) so
-    that a large batch has stages to overlap."""
+    that a large batch has stages to overlap; the first two groups are a
+    quarter and a half of that."""
     n = len(in_sizes)
     if n == 0:
         return []
@@ -81,11 +82,14 @@ def plan_groups(in_sizes, out_sizes, units, limits):
     target = min(limits[2], max(_GROUP_MIN, -(-int(cout[-1]) // 4)))
     groups, a = [], 0
     while a < n:
+        # The first two groups take a quarter and a half of the target, so
+        # the kernels start after a short first copy.
+        want = max(1, target >> max(0, 2 - len(groups)))
         # Largest b with every total within its limit (at least one file).
         b = min(int(np.searchsorted(cin, cin[a] + limits[1], "right")) - 1,
                 int(np.searchsorted(cout, cout[a] + limits[2], "right")) - 1,
                 int(np.searchsorted(cunit, cunit[a] + limits[0], "right")) - 1,
-                int(np.searchsorted(cout, cout[a] + target, "left")))
+                int(np.searchsorted(cout, cout[a] + want, "left")))
         b = max(a + 1, min(b, n))
         groups.append((a, b))
         a = b
@@ -131,7 +135,8 @@ class _Source:
 
 
 def _i64(values):
-    return (ctypes.c_int64 * len(values))(*values)
+    """A ctypes int64 pointer over a contiguous int64 NumPy slice (no copy)."""
+    return values.ctypes.data_as(ctypes.POINTER(ctypes.c_int64))
 
 
 def run(torch, device, packed, in_sizes, out_sizes, units, limits, call, compact=False):
@@ -161,6 +166,11 @@ def run(torch, device, packed, in_sizes, out_sizes, units, limits, call, compact
     with torch.cuda.device(device):
         compute = torch.cuda.current_stream(device)
         copy_in, copy_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+        # Compact mode: metadata goes out on its own stream, so that a group's
+        # stream copy, issued once the host has read that group's metadata,
+        # never queues behind the next group's metadata copy (which waits for
+        # the next group's kernels).
+        meta_out = torch.cuda.Stream(device) if compact else copy_out
         sets = 2 if len(groups) > 1 else 1
         most_in = max(int(in_off[b] - in_off[a]) for a, b in groups)
         most_out = max(int(out_off[b] - out_off[a]) for a, b in groups)
@@ -208,14 +218,14 @@ def run(torch, device, packed, in_sizes, out_sizes, units, limits, call, compact
             done = torch.cuda.Event()
             done.record(compute)
             consumed[j] = done
-            with torch.cuda.stream(copy_out):
-                copy_out.wait_event(done)
+            with torch.cuda.stream(meta_out):
+                meta_out.wait_event(done)
                 if n_out and not compact:
                     host_out[int(out_off[a]):int(out_off[b])].copy_(dev_out[j][:n_out],
                                                                     non_blocking=True)
                 host_meta[a:b].copy_(dev_meta[j][:b - a], non_blocking=True)
                 finished = torch.cuda.Event()
-                finished.record(copy_out)
+                finished.record(meta_out)
             if not compact:
                 drained[j] = finished
                 continue
@@ -225,6 +235,7 @@ def run(torch, device, packed, in_sizes, out_sizes, units, limits, call, compact
         if waiting is not None:
             copy_compact(*waiting)
         copy_out.synchronize()
+        meta_out.synchronize()
         compute.wait_stream(copy_in)
     if compact:
         return host_out[:written], host_meta.numpy()[:files]
@@ -234,16 +245,16 @@ def run(torch, device, packed, in_sizes, out_sizes, units, limits, call, compact
 def decode(torch, device, packed, in_sizes, out_sizes, limits):
     """Packed host streams -> (pinned packed outputs, int32 [status, 0] pairs)."""
     lib = _native.library()
-    in_list, out_list = [int(v) for v in in_sizes], [int(v) for v in out_sizes]
+    ins = np.ascontiguousarray(in_sizes, dtype=np.int64)
+    outs = np.ascontiguousarray(out_sizes, dtype=np.int64)
 
     def call(a, b, dev_in, n_in, dev_out, n_out, dev_meta, stream):
         _native.check(lib.cuda_zlib_decompress_batch(
-            dev_in.data_ptr(), n_in, _i64(in_list[a:b]), _i64(out_list[a:b]), b - a, None,
+            dev_in.data_ptr(), n_in, _i64(ins[a:b]), _i64(outs[a:b]), b - a, None,
             dev_out.data_ptr(), n_out, dev_meta.data_ptr(), stream.cuda_stream),
             "CUDA batch decompression")
 
-    return run(torch, device, packed, in_list, out_list, np.ones(len(in_list), np.int64),
-               limits, call)
+    return run(torch, device, packed, ins, outs, np.ones(ins.size, np.int64), limits, call)
 
 
 def encode(torch, device, packed, in_sizes, capacities, chunks, chunk_bytes, limits,
@@ -251,16 +262,16 @@ def encode(torch, device, packed, in_sizes, capacities, chunks, chunk_bytes, lim
     """Packed host files -> (pinned padded slots, int32 [length, status] pairs);
     compact: the streams back to back instead of padded slots."""
     lib = _native.library()
-    in_list = [int(v) for v in in_sizes]
+    ins = np.ascontiguousarray(in_sizes, dtype=np.int64)
     entry = lib.cuda_zlib_compress_batch_packed if compact else lib.cuda_zlib_compress_batch
 
     def call(a, b, dev_in, n_in, dev_out, n_out, dev_meta, stream):
         _native.check(entry(
-            dev_in.data_ptr(), n_in, _i64(in_list[a:b]), b - a, chunk_bytes,
+            dev_in.data_ptr(), n_in, _i64(ins[a:b]), b - a, chunk_bytes,
             dev_out.data_ptr(), n_out, dev_meta.data_ptr(), stream.cuda_stream),
             "CUDA batch compression")
 
-    return run(torch, device, packed, in_list, capacities, chunks, limits, call, compact)
+    return run(torch, device, packed, ins, capacities, chunks, limits, call, compact)
 
 
 def pack(views, torch):
