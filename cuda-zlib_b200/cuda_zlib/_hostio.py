@@ -31,6 +31,7 @@ import numpy as np
 from . import _native
 
 _GROUP_MIN = 32 << 20   # a group holds at least this many bytes (unless the batch is smaller)
+_TAIL_FILES = 2048      # decode groups hold at least this many of the batch's largest files
 _STAGE_PIECE = 8 << 20  # bytes per host staging task
 _STAGE_THREADS = max(1, min(16, os.cpu_count() or 1))
 _pool = None
@@ -67,12 +68,14 @@ def _tensor(torch, array):
         return torch.from_numpy(array)
 
 
-def plan_groups(in_sizes, out_sizes, units, limits):
+def plan_groups(in_sizes, out_sizes, units, limits, floor=0):
     """Boundaries [a, b) of consecutive files whose totals stay within
     `limits` = (units, input bytes, output bytes) of one call; groups are cut
     at about a quarter of the batch (at least _GROUP_MIN output bytes) so
     that a large batch has stages to overlap; the first two groups are a
-    quarter and a half of that."""
+    quarter and a half of that.  No group is cut below `floor` output bytes
+    (the batch decoder gives each file one warp, so a group's time has a tail
+    set by its largest file; a group must be large enough to hide it)."""
     n = len(in_sizes)
     if n == 0:
         return []
@@ -84,7 +87,7 @@ def plan_groups(in_sizes, out_sizes, units, limits):
     while a < n:
         # The first two groups take a quarter and a half of the target, so
         # the kernels start after a short first copy.
-        want = max(1, target >> max(0, 2 - len(groups)))
+        want = max(1, target >> max(0, 2 - len(groups)), min(int(floor), limits[2]))
         # Largest b with every total within its limit (at least one file).
         b = min(int(np.searchsorted(cin, cin[a] + limits[1], "right")) - 1,
                 int(np.searchsorted(cout, cout[a] + limits[2], "right")) - 1,
@@ -139,7 +142,8 @@ def _i64(values):
     return values.ctypes.data_as(ctypes.POINTER(ctypes.c_int64))
 
 
-def run(torch, device, packed, in_sizes, out_sizes, units, limits, call, compact=False):
+def run(torch, device, packed, in_sizes, out_sizes, units, limits, call, compact=False,
+        floor=0):
     """Push the packed files through stage -> copy in -> call -> copy out.
 
     call(a, b, dev_in, in_bytes, dev_out, out_bytes, dev_meta, stream) issues
@@ -154,7 +158,7 @@ def run(torch, device, packed, in_sizes, out_sizes, units, limits, call, compact
     """
     in_sizes = np.asarray(in_sizes, dtype=np.int64)
     out_sizes = np.asarray(out_sizes, dtype=np.int64)
-    groups = plan_groups(in_sizes, out_sizes, units, limits)
+    groups = plan_groups(in_sizes, out_sizes, units, limits, floor)
     in_off = np.concatenate(([0], np.cumsum(in_sizes)))
     out_off = np.concatenate(([0], np.cumsum(out_sizes)))
     files = len(in_sizes)
@@ -254,7 +258,11 @@ def decode(torch, device, packed, in_sizes, out_sizes, limits):
             dev_out.data_ptr(), n_out, dev_meta.data_ptr(), stream.cuda_stream),
             "CUDA batch decompression")
 
-    return run(torch, device, packed, ins, outs, np.ones(ins.size, np.int64), limits, call)
+    # One warp decodes a file: groups of at least 2048 largest files keep a
+    # group's tail (its largest file) small against its throughput time.
+    floor = _TAIL_FILES * int(outs.max()) if outs.size else 0
+    return run(torch, device, packed, ins, outs, np.ones(ins.size, np.int64), limits, call,
+               floor=floor)
 
 
 def encode(torch, device, packed, in_sizes, capacities, chunks, chunk_bytes, limits,
