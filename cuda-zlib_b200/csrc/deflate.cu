@@ -41,6 +41,8 @@ constexpr u32 kEncThreads = 512;
 constexpr u32 kEncWarps = kEncThreads / 32;
 constexpr u32 kOwnerBits = 4;  // log2(kEncWarps): hash slots are split over the warps
 static_assert((1u << kOwnerBits) == kEncWarps, "one slot class per warp");
+constexpr u32 kSortKeys = 512;  // bitonic sort width of the leaf ranking (>= 286)
+static_assert(kSortKeys <= kEncThreads, "one sort key per thread");
 constexpr u32 kPerThread = 8;  // candidate rounds: consecutive positions per thread
 constexpr u32 kRoundPositions = kEncThreads * kPerThread;
 constexpr u32 kHashSlots = 8192;
@@ -117,6 +119,7 @@ struct EncodeShared {
   u16 ancestor[2][576];
   u16 sorted[288];
   u32 leafw[288];      // weights in leaf rank order
+  u32 sort_keys[kSortKeys];  // leaf ranking: (weight << 9 | id) keys
   u8 depth[2][576];
   u8 rle_sym[320];
   u8 rle_extra[320];
@@ -173,17 +176,33 @@ __device__ bool cta_tree(Shared& s, const u32* freq, u32 alphabet, u32 limit, u8
       s.leaves = m;
     }
     __syncthreads();
-    // Rank leaves by (weight, id).
-    for (u32 i = tid; i < alphabet; i += kEncThreads) {
-      const u32 w = s.weight[i];
-      if (!w) continue;
-      u32 rank = 0;
-      for (u32 j = 0; j < alphabet; ++j) {
-        const u32 v = s.weight[j];
-        rank += (v && (v < w || (v == w && j < i))) ? 1u : 0u;
+    // Rank leaves by (weight, id): a bitonic sort of (weight << 9 | id) keys,
+    // zero weights last (weights stay below 2^19, ids below 2^9).
+    const u32 sort_n = alphabet > 32 ? kSortKeys : 32u;
+    for (u32 i = tid; i < sort_n; i += kEncThreads) {
+      const u32 w = i < alphabet ? s.weight[i] : 0u;
+      s.sort_keys[i] = w ? (w << 9) | i : ~0u;
+    }
+    __syncthreads();
+    for (u32 k = 2; k <= sort_n; k <<= 1) {
+      for (u32 j = k >> 1; j; j >>= 1) {
+        for (u32 i = tid; i < sort_n; i += kEncThreads) {
+          const u32 partner = i ^ j;
+          if (partner > i) {
+            const u32 a = s.sort_keys[i], b = s.sort_keys[partner];
+            if ((a > b) == ((i & k) == 0)) {
+              s.sort_keys[i] = b;
+              s.sort_keys[partner] = a;
+            }
+          }
+        }
+        __syncthreads();
       }
-      s.sorted[rank] = u16(i);
-      s.leafw[rank] = w;
+    }
+    for (u32 r = tid; r < s.leaves; r += kEncThreads) {
+      const u32 key = s.sort_keys[r];
+      s.sorted[r] = u16(key & 511u);
+      s.leafw[r] = key >> 9;
     }
     __syncthreads();
     const u32 m = s.leaves;
@@ -399,11 +418,40 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
   // the next file's slice).
   u64 s1 = 0, s2 = 0;
   const u32 stage_bytes = kLarge ? min_u32(data_bytes, (n + 16 + 15) & ~15u) : data_bytes;
-  for (u32 i = tid; i < stage_bytes; i += kEncThreads) {
-    const u32 x = i < n ? u32(src[i]) : 0u;
-    data[i] = u8(x);
-    s1 += x;
-    s2 += u64(n - i) * x;  // x == 0 beyond n
+  if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+    // 16 bytes a step; a word's bytes b0..b3 at positions p..p+3 add
+    // sum to s1 and (n - p) * sum - (b1 + 2 b2 + 3 b3) to s2 (zeros beyond n
+    // add nothing, so the weight may wrap there).
+    for (u32 i = 16 * tid; i < stage_bytes; i += 16 * kEncThreads) {
+      uint4 q = make_uint4(0, 0, 0, 0);
+      if (i + 16 <= n) {
+        q = *reinterpret_cast<const uint4*>(src + i);
+      } else if (i < n) {
+        u64 lo = 0, hi = 0;
+        for (u32 b = 0; i + b < n; ++b) {
+          if (b < 8) lo |= u64(src[i + b]) << (8 * b);
+          else hi |= u64(src[i + b]) << (8 * (b - 8));
+        }
+        q = make_uint4(u32(lo), u32(lo >> 32), u32(hi), u32(hi >> 32));
+      }
+      *reinterpret_cast<uint4*>(data + i) = q;
+      const u32 words4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (u32 k = 0; k < 4; ++k) {
+        const u32 w = words4[k];
+        const u32 b0 = w & 255u, b1 = (w >> 8) & 255u, b2 = (w >> 16) & 255u, b3 = w >> 24;
+        const u32 sum = b0 + b1 + b2 + b3;
+        s1 += sum;
+        s2 += u64(n - (i + 4 * k)) * sum - (b1 + 2 * b2 + 3 * b3);
+      }
+    }
+  } else {
+    for (u32 i = tid; i < stage_bytes; i += kEncThreads) {
+      const u32 x = i < n ? u32(src[i]) : 0u;
+      data[i] = u8(x);
+      s1 += x;
+      s2 += u64(n - i) * x;  // x == 0 beyond n
+    }
   }
   for (u32 i = tid; i < bit_words; i += kEncThreads) { member[i] = 0; ismatch[i] = 0; }
   for (u32 i = tid; i < kHashSlots; i += kEncThreads) table[i] = 0;
