@@ -585,6 +585,11 @@ cudaError_t decompress(const u8* in, u64 size, int64_t max_candidates, int64_t m
   CZ_TRY(ws.allocate(&b.deep, 1));
   CZ_TRY(ws.allocate(&b.longs, layout.out_words));
   CZ_TRY(ws.allocate(&b.stage_done, u64(layout.stages) + 1));
+  CZ_TRY(ws.allocate(&b.unit_counts, nodes));
+  CZ_TRY(ws.allocate(&b.item_units, u64(nodes) + 1));
+  for (u32** unit_array : {&b.unit_item, &b.unit_page, &b.unit_first, &b.unit_tokens,
+                           &b.unit_start, &b.unit_bytes})
+    CZ_TRY(ws.allocate(unit_array, layout.max_units));
   CZ_TRY(ws.allocate(&b.stash, round_stash_words(dev->info)));
   CZ_TRY(cudaMemsetAsync(b.bitmap, 0, layout.bitmap_words * sizeof(u32), stream));
   CZ_TRY(cudaMemsetAsync(b.extra, 0, layout.bitmap_words * sizeof(u32), stream));

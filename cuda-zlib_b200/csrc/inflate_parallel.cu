@@ -1235,6 +1235,212 @@ __device__ __forceinline__ u32 flushed_symbol(const u8* out, const u32* source,
   return byte;
 }
 
+// Expansion units.  A path node is expanded in units of about 2^unit_shift
+// output bytes, cut at token boundaries, so that nodes much longer than the
+// window (long fixed or stored runs, zeros, highly compressible data) still
+// spread over many warps.  A unit starts with an empty history like a node:
+// its references before its own start become markers, so every hop of a
+// marker chase moves at least one unit back and the staged resolution runs
+// over units.  Unit j of a node ends after the first token that reaches
+// (j + 1) << unit_shift node bytes; a stored block's two words stay together.
+// The unit is at least kUnitBytes and grows with the stream, so that large
+// streams, whose nodes already fill the GPU, are not cut into more markers.
+constexpr u32 kUnitBytes = 32768;
+constexpr u32 kUnitsPerSm = 32;  // units a stream aims for per SM
+constexpr u32 kPlanTokens = 8;   // token words per lane per step of the unit planner
+
+u32 unit_shift_for(u64 expected, u32 sms) {
+  u32 shift = 15;  // kUnitBytes
+  while ((u64(1) << shift) * sms * kUnitsPerSm < expected && shift < 31) ++shift;
+  return shift;
+}
+
+// Bytes of token word t whose preceding word is `prev` (a stored block's
+// source word follows its header and takes no bytes).
+__device__ __forceinline__ u32 token_bytes(u32 t, u32 prev, bool has_prev) {
+  if (has_prev && (prev & kStoredFlag) && !(prev & kMatchFlag)) return 0;
+  if (t & kMatchFlag) return t & 511u;
+  if (t & kStoredFlag) return t & 0xffffu;
+  return 1;
+}
+
+// Warp per path item: walk the node's tokens in order.  Count pass (units ==
+// nullptr): units per item into `counts` and the node size check.  Write
+// pass: the item's units at item_units[item] onwards.
+__global__ void __launch_bounds__(256)
+unit_plan_kernel(const u32* state, const u32* path, const u32* prefix, const u32* tprefix,
+                 const u32* sizes, const u32* tokens, const u32* syms, const u32* first_page,
+                 const u32* page_next, const u32* page_used, u32 npages, u32 unit_shift,
+                 u32* counts, const u32* item_units, u32* unit_item, u32* unit_page,
+                 u32* unit_first, u32* unit_tokens, u32* unit_start, u32* unit_bytes,
+                 u32* fail_flag) {
+  if (!state[1] || *fail_flag) return;
+  const u32 len = state[0];
+  const bool contiguous = state[2] != 0;
+  const bool write = unit_item != nullptr;
+  const u32 lane = threadIdx.x & 31u;
+  const u32 warps = gridDim.x * (blockDim.x >> 5);
+  for (u32 item = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; item < len; item += warps) {
+    const u32 node = path[item], node_tokens = tokens[node];
+    u32 left = node_tokens;
+    u32 page = contiguous ? kNoPage : first_page[node];
+    u64 bytes = 0;          // node bytes before the current word
+    u32 units = 1, token_index = 0, bad = 0;
+    u32 open_page = page, open_first = 0, open_token = 0;
+    u64 open_bytes = 0;
+    auto close_unit = [&](u32 end_token, u64 end_bytes, u32 next_page, u32 next_first) {
+      if (write && lane == 0) {
+        const u32 u = item_units[item] + units - 1;
+        unit_item[u] = item;
+        unit_page[u] = open_page;
+        unit_first[u] = open_first;
+        unit_tokens[u] = end_token - open_token;
+        unit_start[u] = prefix[item] + u32(open_bytes);
+        unit_bytes[u] = u32(end_bytes - open_bytes);
+      }
+      open_page = next_page;
+      open_first = next_first;
+      open_token = end_token;
+      open_bytes = end_bytes;
+    };
+    // A node of at most one unit's bytes is one unit (no token can reach a
+    // multiple of the unit before its last), so only longer nodes are
+    // walked.
+    if ((u64(sizes[node]) >> unit_shift) == 0 || sizes[node] == (1u << unit_shift)) {
+      left = 0;
+      token_index = node_tokens;
+      bytes = sizes[node];
+    }
+    for (bool first_run = true; left && !bad; first_run = false) {
+      const u32* sy;
+      u32 n;
+      if (contiguous) {
+        sy = syms + tprefix[item];
+        n = left;
+      } else {
+        if (page == kNoPage || page >= npages || page_used[page] > kPageWords) {
+          bad = 1;
+          break;
+        }
+        sy = syms + u64(page) * kPageWords;
+        n = min_u32(page_used[page], left);
+      }
+      u32 carry = 0;  // the page's previous word (pairs never cross pages)
+      // kPlanTokens consecutive words per lane a step; the next step's words
+      // are loaded while this step's are scanned.
+      u32 ahead[kPlanTokens];
+#pragma unroll
+      for (u32 k = 0; k < kPlanTokens; ++k) {
+        const u32 i = kPlanTokens * lane + k;
+        ahead[k] = i < n ? sy[i] : 0u;
+      }
+      for (u32 base = 0; base < n; base += 32 * kPlanTokens) {
+        const u32 i0 = base + kPlanTokens * lane;
+        u32 t[kPlanTokens], size[kPlanTokens];
+#pragma unroll
+        for (u32 k = 0; k < kPlanTokens; ++k) {
+          t[k] = ahead[k];
+          const u32 i = i0 + 32 * kPlanTokens + k;
+          ahead[k] = i < n ? sy[i] : 0u;
+        }
+        u32 prev = __shfl_up_sync(kFullMask, t[kPlanTokens - 1], 1);
+        if (lane == 0) prev = carry;
+        u32 lane_bytes = 0;
+#pragma unroll
+        for (u32 k = 0; k < kPlanTokens; ++k) {
+          size[k] = i0 + k < n ? token_bytes(t[k], k ? t[k - 1] : prev, i0 + k > 0) : 0u;
+          lane_bytes += size[k];
+        }
+        u64 incl = lane_bytes;
+        for (u32 o = 1; o < 32; o <<= 1) {
+          const u64 v = __shfl_up_sync(kFullMask, incl, o);
+          if (lane >= o) incl += v;
+        }
+        // A token reaching a multiple of kUnitBytes ends its unit; the next
+        // unit starts after it (after a stored block's source word).
+        u64 before = bytes + incl - lane_bytes;
+        u32 ends = 0;
+#pragma unroll
+        for (u32 k = 0; k < kPlanTokens; ++k) {
+          const u64 after = before + size[k];
+          if (size[k] && (after >> unit_shift) > (before >> unit_shift)) ends |= 1u << k;
+          before = after;
+        }
+        for (u32 ballot = __ballot_sync(kFullMask, ends != 0); ballot; ballot &= ballot - 1) {
+          const u32 l = __ffs(ballot) - 1;
+          u32 lane_ends = __shfl_sync(kFullMask, ends, l);
+          u64 at = __shfl_sync(kFullMask, bytes + incl - lane_bytes, l);
+#pragma unroll
+          for (u32 k = 0; k < kPlanTokens; ++k) {
+            const u32 tk = __shfl_sync(kFullMask, t[k], l);
+            at += __shfl_sync(kFullMask, size[k], l);
+            if (!((lane_ends >> k) & 1u)) continue;
+            const bool header = (tk & kStoredFlag) && !(tk & kMatchFlag);
+            const u32 next = base + kPlanTokens * l + k + (header ? 2u : 1u);
+            if (token_index + next < node_tokens) {
+              // A next unit that starts on the following page starts at
+              // that page's word 0.
+              const bool on_next = next >= n && !contiguous;
+              close_unit(token_index + next, at, on_next ? page_next[page] : page,
+                         on_next ? 0u : next);
+              ++units;
+            }
+          }
+        }
+        bytes += __shfl_sync(kFullMask, incl, 31);
+        carry = __shfl_sync(kFullMask, t[kPlanTokens - 1], 31);
+      }
+      token_index += n;
+      left -= n;
+      if (contiguous) break;
+      page = page_next[page];
+    }
+    if (!bad) {
+      close_unit(token_index, bytes, kNoPage, 0);
+      if (bytes != sizes[node]) bad = 1;
+    }
+    if (lane == 0) {
+      if (bad) atomicOr(fail_flag, 1u);
+      if (!write) counts[item] = units;
+    }
+  }
+}
+
+// Exclusive prefix of the units per item (one CTA); item_units[len] is the
+// total.
+__global__ void unit_scan_kernel(const u32* state, const u32* counts, u32* item_units) {
+  __shared__ u32 warp_total[32];
+  __shared__ u32 carry;
+  if (!state[1]) return;
+  const u32 len = state[0];
+  const u32 lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    carry = 0;
+    if (!len) item_units[0] = 0;
+  }
+  __syncthreads();
+  for (u32 base = 0; base < len; base += blockDim.x) {
+    const u32 i = base + threadIdx.x;
+    const u32 v = i < len ? counts[i] : 0u;
+    u32 incl = v;
+    for (u32 o = 1; o < 32; o <<= 1) {
+      const u32 t = __shfl_up_sync(kFullMask, incl, o);
+      if (lane >= o) incl += t;
+    }
+    if (lane == 31) warp_total[warp] = incl;
+    __syncthreads();
+    u32 before = carry;
+    for (u32 w = 0; w < warp; ++w) before += warp_total[w];
+    if (i < len) item_units[i] = before + incl - v;
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) {
+      carry = before + incl;
+      if (base + blockDim.x >= len) item_units[len] = carry;
+    }
+    __syncthreads();
+  }
+}
+
 // Expand every path node's tokens into the output (warp per node, work
 // stealing).  The warp takes kChunkTokens tokens at a time, kLaneTokens
 // consecutive ones per lane: a scan of their sizes places them, then every
@@ -1245,44 +1451,46 @@ __device__ __forceinline__ u32 flushed_symbol(const u8* out, const u32* source,
 // stretches of the ring flush to the output, markers as source positions in
 // `source` plus a bit in `unresolved`.
 __global__ void __launch_bounds__(kExpandWarps * 32)
-expand_kernel(const u8* in, u32 in_size, const u32* path, const u32* prefix,
-              const u32* tprefix, const u32* sizes, const u32* tokens, const u32* state,
-              const u32* syms, const u32* first_page, const u32* page_next,
-              const u32* page_used, u32 npages, u32* next_item, u8* out, u32* source,
-              u32* unresolved, u32* fail_flag) {
+expand_kernel(const u8* in, u32 in_size, const u32* tprefix, const u32* state,
+              const u32* syms, const u32* page_next, const u32* page_used, u32 npages,
+              const u32* item_units, const u32* unit_item, const u32* unit_page,
+              const u32* unit_first, const u32* unit_tokens, const u32* unit_start,
+              const u32* unit_bytes, u32* next_item, u8* out, u32* source, u32* unresolved,
+              u32* fail_flag) {
   __shared__ ExpandShared sh;
   const u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   // A failed chain or symbol pass leaves nothing to expand (the status path
   // reports the stream).
   if (!state[1] || *fail_flag) return;
-  const u32 len = state[0];
+  const u32 units = item_units[state[0]];
   const u8* body = in + 2;
   u16* ring = sh.ring[warp];
   for (;;) {
-    u32 item = 0;
-    if (lane == 0) item = atomicAdd(next_item, 1u);
-    item = __shfl_sync(kFullMask, item, 0);
-    if (item >= len) break;
-    const u32 node = path[item], start = prefix[item];
-    // The node's tokens: one contiguous run, or its chain of arena pages
-    // (allocated in order, so page numbers strictly increase along it).
+    u32 unit = 0;
+    if (lane == 0) unit = atomicAdd(next_item, 1u);
+    unit = __shfl_sync(kFullMask, unit, 0);
+    if (unit >= units) break;
+    const u32 item = unit_item[unit], start = unit_start[unit];
+    // The unit's tokens: a stretch of the node's contiguous run, or of its
+    // chain of arena pages (allocated in order, so page numbers strictly
+    // increase along it), from word `skip` of its first page.
     const bool contiguous = state[2] != 0;
-    u32 page = contiguous ? kNoPage : first_page[node], last_page = 0;
+    u32 page = unit_page[unit], last_page = 0, skip = unit_first[unit];
     u32 pos = 0, flushed = 0, bad = 0;
-    // A seed's final-block reading shares the pages of its other reading and
-    // takes only its own (leading) tokens.
-    u32 left = tokens[node];
+    u32 left = unit_tokens[unit];
     for (bool first_run = true;; first_run = false) {
-    const u32* sy = syms + tprefix[item];
-    u32 n = tokens[node];
+    const u32* sy = syms + tprefix[item] + skip;
+    u32 n = left;
     if (!contiguous) {
       if (page == kNoPage || !left) break;
-      if (page >= npages || (!first_run && page <= last_page) || page_used[page] > kPageWords) {
+      if (page >= npages || (!first_run && page <= last_page) || page_used[page] > kPageWords ||
+          (first_run && skip > page_used[page])) {
         bad = 1;
         break;
       }
-      sy = syms + u64(page) * kPageWords;
-      n = min_u32(page_used[page], left);
+      const u32 from = first_run ? skip : 0u;
+      sy = syms + u64(page) * kPageWords + from;
+      n = min_u32(page_used[page] - from, left);
       left -= n;
       last_page = page;
     }
@@ -1478,7 +1686,7 @@ expand_kernel(const u8* in, u32 in_size, const u32* path, const u32* prefix,
     }
     if (!bad) flush_symbols(ring, out, source, unresolved, start, flushed, pos);
     __syncwarp();
-    if (lane == 0 && (bad || pos != sizes[node])) atomicOr(fail_flag, 1u);
+    if (lane == 0 && (bad || pos != unit_bytes[unit])) atomicOr(fail_flag, 1u);
   }
 }
 
@@ -1488,8 +1696,8 @@ expand_kernel(const u8* in, u32 in_size, const u32* path, const u32* prefix,
 // once, one lane per bit position, the four chases interleaved so their
 // loads overlap.
 constexpr u32 kResolveWays = 4;
-// Hops a chase may take.  A marker's source lies before its own path node,
-// so every hop moves at least one node back.  Data whose every byte copies
+// Hops a chase may take.  A marker's source lies before its own expansion
+// unit, so every hop moves at least one unit back.  Data whose every byte copies
 // from the previous record (long runs of records, zero padding) chains each
 // marker through every earlier node; such a chase stops here, records the
 // position it reached (at least kResolveHops nodes back) in source[], sets
@@ -1553,8 +1761,8 @@ __global__ void resolve_kernel(const u32* state, u32 words, const u32* unresolve
 }
 
 // After resolve_kernel raised *deep: the long markers, in stages of
-// kResolveHops consecutive path nodes.  A long marker of path node i reads
-// source[] = a position in node i - kResolveHops or earlier, which is either
+// kResolveHops consecutive expansion units.  A long marker of unit i reads
+// source[] = a position in unit i - kResolveHops or earlier, which is either
 // final since resolve_kernel or a long marker of an earlier stage, so the
 // markers of one stage resolve in parallel once every earlier stage is done.
 // CTAs take (stage, tile) tickets in order; a tile waits for its previous
@@ -1565,12 +1773,13 @@ __global__ void resolve_kernel(const u32* state, u32 words, const u32* unresolve
 constexpr u32 kStageThreads = 256;
 constexpr u32 kStageWaitLimit = 1u << 22;  // polls of ~256 ns: about a second
 __global__ void __launch_bounds__(kStageThreads)
-stage_resolve_kernel(const u32* state, const u32* prefix, u32 expected, const u32* longs,
-                     const u32* source, u8* out, u32 tiles_per_stage, u32* stage_done,
-                     u32* ticket, u32* fail, const u32* deep) {
+stage_resolve_kernel(const u32* state, const u32* item_units, const u32* unit_start,
+                     u32 expected, const u32* longs, const u32* source, u8* out,
+                     u32 tiles_per_stage, u32* stage_done, u32* ticket, u32* fail,
+                     const u32* deep) {
   __shared__ u32 s_ticket, s_go;
   if (!state[1] || !*deep) return;
-  const u32 len = state[0];
+  const u32 len = item_units[state[0]];  // expansion units, in output order
   const u32 stages = (len + kResolveHops - 1) / kResolveHops;
   const u64 total = u64(stages) * tiles_per_stage;
   const bool vec = (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
@@ -1599,7 +1808,7 @@ stage_resolve_kernel(const u32* state, const u32* prefix, u32 expected, const u3
     if (!s_go) return;
     const u32 stage = t / tiles_per_stage, tile = t % tiles_per_stage;
     const u32 first = stage * kResolveHops, last = first + kResolveHops;
-    const u32 lo = prefix[first], hi = last < len ? prefix[last] : expected;
+    const u32 lo = unit_start[first], hi = last < len ? unit_start[last] : expected;
     if (hi > lo) {
       const u32 w_lo = lo >> 5, w_hi = (hi - 1) / 32 + 1;
       const u32 per = (w_hi - w_lo + tiles_per_stage - 1) / tiles_per_stage;
@@ -1848,7 +2057,9 @@ ParallelScratch parallel_scratch_layout(u64 in_size, u64 expected, u32 capacity,
   s.node_capacity = s.capacity + 2 * s.tiles;
   s.levels = chain_levels(s.node_capacity);
   s.out_words = (expected + 31) / 32 + 1;
-  s.stages = (s.node_capacity + kResolveHops - 1) / kResolveHops + 1;
+  // Units: at most one per node plus one per kUnitBytes of output.
+  s.max_units = u32(expected / kUnitBytes) + s.node_capacity + 2;
+  s.stages = (s.max_units + kResolveHops - 1) / kResolveHops + 1;
   s.segments = u32((expected + kAdlerSegment - 1) / kAdlerSegment);
   // Path tokens of a chain that passes its checks: at most one per output
   // byte, plus two words per stored block (at most kMaxBlocks blocks).
@@ -1910,13 +2121,28 @@ cudaError_t launch_parallel_inflate(const u8* in, u64 in_size, u8* out, u64 expe
       b.extra, b.path, b.tprefix, b.sizes, b.tokens, b.state, b.counters + 1, b.syms, b.fail,
       fixed, b.stash);
   profile_end(stream);
+  // Expansion units: count per path node, scan, write.
+  const u32 plan_grid = u32(dev.sms) * 8;
+  const u32 unit_shift = unit_shift_for(expected, u32(dev.sms));
+  note_launch();
+  unit_plan_kernel<<<plan_grid, 256, 0, stream>>>(
+      b.state, b.path, b.prefix, b.tprefix, b.sizes, b.tokens, b.syms, b.first_page, b.page_next,
+      b.page_used, s.pages, unit_shift, b.unit_counts, nullptr, nullptr, nullptr, nullptr,
+      nullptr, nullptr, nullptr, b.fail);
+  note_launch();
+  unit_scan_kernel<<<1, 1024, 0, stream>>>(b.state, b.unit_counts, b.item_units);
+  note_launch();
+  unit_plan_kernel<<<plan_grid, 256, 0, stream>>>(
+      b.state, b.path, b.prefix, b.tprefix, b.sizes, b.tokens, b.syms, b.first_page, b.page_next,
+      b.page_used, s.pages, unit_shift, b.unit_counts, b.item_units, b.unit_item, b.unit_page,
+      b.unit_first, b.unit_tokens, b.unit_start, b.unit_bytes, b.fail);
   const u32 expand_grid = u32(dev.sms) * u32(dev.emit_per_sm > 0 ? dev.emit_per_sm : 1);
   profile_begin("expand_kernel", stream);
   note_launch();
   expand_kernel<<<expand_grid, kExpandWarps * 32, 0, stream>>>(
-      in, u32(in_size), b.path, b.prefix, b.tprefix, b.sizes, b.tokens, b.state, b.syms,
-      b.first_page, b.page_next, b.page_used, s.pages, b.counters + 2, out, b.source,
-      b.unresolved, b.fail);
+      in, u32(in_size), b.tprefix, b.state, b.syms, b.page_next, b.page_used, s.pages,
+      b.item_units, b.unit_item, b.unit_page, b.unit_first, b.unit_tokens, b.unit_start,
+      b.unit_bytes, b.counters + 2, out, b.source, b.unresolved, b.fail);
   profile_end(stream);
   profile_begin("resolve_kernel", stream);
   note_launch();
@@ -1926,8 +2152,8 @@ cudaError_t launch_parallel_inflate(const u8* in, u64 in_size, u8* out, u64 expe
   profile_begin("stage_resolve_kernel", stream);
   note_launch();
   stage_resolve_kernel<<<u32(dev.sms) * 2, kStageThreads, 0, stream>>>(
-      b.state, b.prefix, u32(expected), b.longs, b.source, out, u32(dev.sms) * 2, b.stage_done,
-      b.stage_done + s.stages, b.fail, b.deep);
+      b.state, b.item_units, b.unit_start, u32(expected), b.longs, b.source, out,
+      u32(dev.sms) * 2, b.stage_done, b.stage_done + s.stages, b.fail, b.deep);
   profile_end(stream);
   if (s.segments && checksum) {
     note_launch();

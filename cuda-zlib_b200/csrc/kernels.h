@@ -123,7 +123,8 @@ struct ParallelScratch {
   u32 segments;       // Adler-32 segments of the output
   u64 symbol_words;   // contiguous token layout of the path nodes
   u32 pages;          // token arena pages (1024 words each, at least symbol_words)
-  u32 stages;         // staged-resolve stages (32 path nodes each) over node_capacity
+  u32 max_units;      // expansion units: node_capacity + expected / 32 KiB + 2
+  u32 stages;         // staged-resolve stages (32 units each) over max_units
 };
 struct ParallelBuffers {
   u32* bitmap;        // bitmap_words, from discover_kernel (the reference's rule)
@@ -149,6 +150,9 @@ struct ParallelBuffers {
   u32* deep;          // 1, zeroed: some marker chain is too long to chase
   u32* longs;         // out_words: markers whose chase ran out of hops
   u32* stage_done;    // stages + 1, zeroed: tiles done per stage, then the ticket
+  u32* unit_counts;   // node_capacity: expansion units per path item
+  u32* item_units;    // node_capacity + 1: their exclusive prefix, then the total
+  u32 *unit_item, *unit_page, *unit_first, *unit_tokens, *unit_start, *unit_bytes;  // max_units
   u32* stash;         // round_stash_words: tokens the node warps keep per round
 };
 ParallelScratch parallel_scratch_layout(u64 in_size, u64 expected, u32 capacity,
