@@ -53,6 +53,7 @@ enum Status : u32 {
 constexpr u32 kFullMask = 0xffffffffu;
 
 __host__ __device__ inline u32 min_u32(u32 a, u32 b) { return a < b ? a : b; }
+__host__ __device__ inline u32 max_u32(u32 a, u32 b) { return a > b ? a : b; }
 __host__ __device__ inline u64 min_u64(u64 a, u64 b) { return a < b ? a : b; }
 
 // zlib wrapper check shared by every decode route (DecompressionFraming,

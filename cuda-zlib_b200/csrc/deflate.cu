@@ -42,7 +42,8 @@ constexpr u32 kEncWarps = kEncThreads / 32;
 constexpr u32 kOwnerBits = 4;  // log2(kEncWarps): hash slots are split over the warps
 static_assert((1u << kOwnerBits) == kEncWarps, "one slot class per warp");
 constexpr u32 kSortKeys = 512;  // bitonic sort width of the leaf ranking (>= 286)
-static_assert(kSortKeys <= kEncThreads, "one sort key per thread");
+static_assert(kSortKeys == kEncThreads, "one sort key per thread");
+constexpr u32 kCodeWarps = (286 + 31) / 32;  // warps covering the largest alphabet
 constexpr u32 kPerThread = 8;  // candidate rounds: consecutive positions per thread
 constexpr u32 kRoundPositions = kEncThreads * kPerThread;
 constexpr u32 kHashSlots = 8192;
@@ -120,6 +121,8 @@ struct EncodeShared {
   u16 sorted[288];
   u32 leafw[288];      // weights in leaf rank order
   u32 sort_keys[kSortKeys];  // leaf ranking: (weight << 9 | id) keys
+  u32 sort_swap[kSortKeys];  // the ranking's second exchange buffer
+  u16 warp_len[kCodeWarps][16];  // codes: per warp, symbols of each length
   u8 depth[2][576];
   u8 rle_sym[320];
   u8 rle_extra[320];
@@ -136,22 +139,30 @@ struct EncodeShared {
   u64 adler_s2[kEncWarps];
   u32 extra_bits, token_count, dist_tokens;
   u32 mode, extent, status, ok, nll, ndist, ncl, rle_size, header_bits, leaves, only;
-  u32 more, lcount[16];
+  u32 more, lcount[16], fixed_sum, ll_sum;
 };
 
-// Two-queue Huffman build with the reference's (weight, id) order and
-// flattening retries.  All threads call; the merge itself runs on thread 0
-// with both queue heads in registers, and everything around it (leaf
-// ranking, depths by pointer doubling, length counts, canonical codes) is
-// spread over the block.  Returns on all threads whether a tree within
-// `limit` was found.
+// Huffman build with the reference's (weight, id) order and flattening
+// retries, spread over the block.  The reference pops its heap by (weight,
+// node id); with leaves ranked by (weight, id) and inner nodes queued in
+// creation order (their weights never decrease), a two-queue merge that takes
+// the leaf on equal weights picks the same pair at every step.  That merge
+// runs in rounds: with t the weight of the next node (the sum of the next two
+// picks), every node created from then on weighs at least t, so all queued
+// leaves and inner nodes of weight <= t are picked before any of them, in the
+// order of a stable merge of the two queues.  A round merges those in
+// parallel (an odd last one waits for the next round) and pairs them into new
+// nodes; t at least doubles every two rounds.  Depths follow by pointer
+// doubling, codes by per-warp ranks.  All threads call; returns on all
+// threads whether a tree within `limit` was found.
 template <typename Shared>
 __device__ bool cta_tree(Shared& s, const u32* freq, u32 alphabet, u32 limit, u8* lengths,
                          u16* codes) {
-  const u32 tid = threadIdx.x;
+  const u32 tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
   for (u32 shift = 0; shift <= 16; ++shift) {
     if (tid == 0) { s.leaves = 0; s.only = 0; }
     if (tid < 16) s.lcount[tid] = 0;
+    if (tid < kCodeWarps * 16) (&s.warp_len[0][0])[tid] = 0;
     __syncthreads();
     for (u32 i = tid; i < alphabet; i += kEncThreads) {
       lengths[i] = 0;
@@ -177,75 +188,116 @@ __device__ bool cta_tree(Shared& s, const u32* freq, u32 alphabet, u32 limit, u8
     }
     __syncthreads();
     // Rank leaves by (weight, id): a bitonic sort of (weight << 9 | id) keys,
-    // zero weights last (weights stay below 2^19, ids below 2^9).
-    const u32 sort_n = alphabet > 32 ? kSortKeys : 32u;
-    for (u32 i = tid; i < sort_n; i += kEncThreads) {
-      const u32 w = i < alphabet ? s.weight[i] : 0u;
-      s.sort_keys[i] = w ? (w << 9) | i : ~0u;
-    }
-    __syncthreads();
-    for (u32 k = 2; k <= sort_n; k <<= 1) {
-      for (u32 j = k >> 1; j; j >>= 1) {
-        for (u32 i = tid; i < sort_n; i += kEncThreads) {
-          const u32 partner = i ^ j;
-          if (partner > i) {
-            const u32 a = s.sort_keys[i], b = s.sort_keys[partner];
-            if ((a > b) == ((i & k) == 0)) {
-              s.sort_keys[i] = b;
-              s.sort_keys[partner] = a;
-            }
+    // zero weights last (weights stay below 2^19, ids below 2^9), one key per
+    // thread.  Partners within a warp are exchanged by shuffles; farther ones
+    // through two shared buffers used in turn, one barrier a stage.
+    if (alphabet <= 32) {
+      if (warp == 0) {
+        const u32 w = lane < alphabet ? s.weight[lane] : 0u;
+        u32 key = w ? (w << 9) | lane : ~0u;
+        for (u32 k = 2; k <= 32; k <<= 1) {
+          for (u32 j = k >> 1; j; j >>= 1) {
+            const u32 other = __shfl_xor_sync(kFullMask, key, j);
+            key = (((lane & j) == 0) == ((lane & k) == 0)) ? min_u32(key, other)
+                                                            : max_u32(key, other);
           }
         }
-        __syncthreads();
+        if (lane < s.leaves) {
+          s.sorted[lane] = u16(key & 511u);
+          s.leafw[lane] = key >> 9;
+        }
       }
-    }
-    for (u32 r = tid; r < s.leaves; r += kEncThreads) {
-      const u32 key = s.sort_keys[r];
-      s.sorted[r] = u16(key & 511u);
-      s.leafw[r] = key >> 9;
+    } else {
+      const u32 w = tid < alphabet ? s.weight[tid] : 0u;
+      u32 key = w ? (w << 9) | tid : ~0u;
+      bool flip = false;
+      for (u32 k = 2; k <= kSortKeys; k <<= 1) {
+        for (u32 j = k >> 1; j; j >>= 1) {
+          u32 other;
+          if (j >= 32) {
+            u32* buf = flip ? s.sort_swap : s.sort_keys;
+            buf[tid] = key;
+            __syncthreads();
+            other = buf[tid ^ j];
+            flip = !flip;
+          } else {
+            other = __shfl_xor_sync(kFullMask, key, j);
+          }
+          key = (((tid & j) == 0) == ((tid & k) == 0)) ? min_u32(key, other) : max_u32(key, other);
+        }
+      }
+      if (tid < s.leaves) {
+        s.sorted[tid] = u16(key & 511u);
+        s.leafw[tid] = key >> 9;
+      }
     }
     __syncthreads();
     const u32 m = s.leaves;
     const u32 nodes = alphabet + m - 1;  // leaves' ids stay below alphabet
-    if (tid == 0) {
-      // Leaf ids are below every inner id, so equal weights take the leaf.
-      // The head of each queue and the element after it stay in registers,
-      // so a pick compares registers and the shared-memory load it starts
-      // is needed only a pick later.
-      u32 leaf = 0, inner = alphabet, next = alphabet;
-      u32 leaf_id = s.sorted[0], leaf_w = s.leafw[0];
-      u32 leaf2_id = m > 1 ? u32(s.sorted[1]) : 0u, leaf2_w = m > 1 ? s.leafw[1] : 0u;
-      u32 inner_w = 0, inner2_w = 0;  // nodes `inner` and `inner + 1`, when they exist
-      for (u32 step = 0; step + 1 < m; ++step) {
-        u32 pick[2], picked_w[2];
+    {
+      const u32* leafw = s.leafw;
+      u32* inner_w = s.weight + alphabet;  // inner node k has id alphabet + k
+      u16* merged = s.ancestor[0];         // a round's picks, in order
+      u32* merged_w = s.sort_keys;
+      // First index in [lo, hi) whose weight is above (upper) or at least
+      // (lower) w.
+      auto upper = [](const u32* v, u32 lo, u32 hi, u32 w) {
+        while (lo < hi) {
+          const u32 mid = (lo + hi) >> 1;
+          if (v[mid] <= w) lo = mid + 1;
+          else hi = mid;
+        }
+        return lo;
+      };
+      auto lower = [](const u32* v, u32 lo, u32 hi, u32 w) {
+        while (lo < hi) {
+          const u32 mid = (lo + hi) >> 1;
+          if (v[mid] < w) lo = mid + 1;
+          else hi = mid;
+        }
+        return lo;
+      };
+      u32 a = 0, b = 0, c = 0;  // next leaf, next queued inner node, inner nodes made
+      while ((m - a) + (c - b) > 1) {
+        u32 la = a, ib = b, t = 0;
 #pragma unroll
         for (u32 k = 0; k < 2; ++k) {
-          const bool take_leaf = leaf < m && (inner == next || leaf_w <= inner_w);
-          if (take_leaf) {
-            pick[k] = leaf_id;
-            picked_w[k] = leaf_w;
-            ++leaf;
-            leaf_id = leaf2_id;
-            leaf_w = leaf2_w;
-            if (leaf + 1 < m) { leaf2_id = s.sorted[leaf + 1]; leaf2_w = s.leafw[leaf + 1]; }
-          } else {
-            pick[k] = inner;
-            picked_w[k] = inner_w;
-            ++inner;
-            inner_w = inner2_w;
-            if (inner + 1 < next) inner2_w = s.weight[inner + 1];
-          }
+          const bool leaf = la < m && (ib == c || leafw[la] <= inner_w[ib]);
+          t += leaf ? leafw[la++] : inner_w[ib++];
         }
-        const u32 w = picked_w[0] + picked_w[1];
-        s.weight[next] = w;
-        s.parent[pick[0]] = u16(next);
-        s.parent[pick[1]] = u16(next);
-        if (inner == next) inner_w = w;             // the queue was empty
-        else if (inner + 1 == next) inner2_w = w;   // it follows the head
-        ++next;
+        u32 nl = upper(leafw, a, m, t) - a, ni = upper(inner_w, b, c, t) - b;
+        if ((nl + ni) & 1u) {
+          if (ni && (!nl || inner_w[b + ni - 1] >= leafw[a + nl - 1])) --ni;
+          else --nl;
+        }
+        for (u32 i = tid; i < nl + ni; i += kEncThreads) {
+          u32 pos, id, w;
+          if (i < nl) {
+            w = leafw[a + i];
+            pos = i + lower(inner_w, b, b + ni, w) - b;
+            id = s.sorted[a + i];
+          } else {
+            const u32 j = i - nl;
+            w = inner_w[b + j];
+            pos = j + upper(leafw, a, a + nl, w) - a;
+            id = alphabet + b + j;
+          }
+          merged[pos] = u16(id);
+          merged_w[pos] = w;
+        }
+        __syncthreads();
+        const u32 pairs = (nl + ni) >> 1;
+        for (u32 k = tid; k < pairs; k += kEncThreads) {
+          inner_w[c + k] = merged_w[2 * k] + merged_w[2 * k + 1];
+          s.parent[merged[2 * k]] = u16(alphabet + c + k);
+          s.parent[merged[2 * k + 1]] = u16(alphabet + c + k);
+        }
+        __syncthreads();
+        a += nl;
+        b += ni;
+        c += pairs;
       }
     }
-    __syncthreads();
     // Depth of every node by pointer doubling towards the root.
     const u32 root = nodes - 1;
     for (u32 i = tid; i < nodes; i += kEncThreads) {
@@ -276,16 +328,22 @@ __device__ bool cta_tree(Shared& s, const u32* freq, u32 alphabet, u32 limit, u8
       atomicAdd(&s.lcount[d], 1u);
     }
     if (__syncthreads_or(overlong)) continue;
-    // Canonical codes: first code of each length, then the rank of a symbol
-    // among the lower symbols of its length.
-    for (u32 i = tid; i < alphabet; i += kEncThreads) {
-      const u32 len = lengths[i];
-      if (!len) continue;
+    // Canonical codes: the first code of a symbol's length plus its rank
+    // among the lower symbols of that length (within its warp by a match,
+    // then the earlier warps' counts of that length).
+    const u32 len = tid < alphabet ? lengths[tid] : 0u;
+    u32 rank = 0;
+    if (warp < kCodeWarps) {
+      const u32 same = __match_any_sync(kFullMask, tid < alphabet ? len : 0xffu);
+      rank = __popc(same & ((1u << lane) - 1u));
+      if (len && !rank) s.warp_len[warp][len] = u16(__popc(same));
+    }
+    __syncthreads();
+    if (len) {
       u32 code = 0;  // lcount[0] is zero: no leaf sits at the root
-      for (u32 b = 1; b <= len; ++b) code = (code + s.lcount[b - 1]) << 1;
-      u32 rank = 0;
-      for (u32 j = 0; j < i; ++j) rank += lengths[j] == len ? 1u : 0u;
-      codes[i] = u16(reverse_bits(code + rank, len));
+      for (u32 bit = 1; bit <= len; ++bit) code = (code + s.lcount[bit - 1]) << 1;
+      for (u32 w = 0; w < warp; ++w) rank += s.warp_len[w][len];
+      codes[tid] = u16(reverse_bits(code + rank, len));
     }
     __syncthreads();
     return true;
@@ -461,7 +519,14 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
     s2 += __shfl_xor_sync(kFullMask, s2, o);
   }
   if (lane == 0) { s.adler_s1[warp] = s1; s.adler_s2[warp] = s2; }
-  if (tid == 0) { s.extra_bits = 0; s.token_count = 0; s.dist_tokens = 0; s.status = 0; }
+  if (tid == 0) {
+    s.extra_bits = 0;
+    s.token_count = 0;
+    s.dist_tokens = 0;
+    s.status = 0;
+    s.fixed_sum = 0;
+    s.ll_sum = 0;
+  }
   __syncthreads();
   if (tid == 0) {
     u64 a = 0, b = 0;
@@ -825,11 +890,21 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
   __syncthreads();
 
   // 6-7. Block type by exact extent (encode_chunk, _encode_kernels.py:312-356).
+  // Sums over the alphabet are warp reductions (unsigned, so the order of
+  // the terms cannot change them).
+  {
+    u32 term = 0;
+    if (tid < 286) {
+      u32 f = s.freq[tid];
+      if (tid == 256) s.freq[256] = ++f;  // the end-of-block code
+      term = f * fixed_ll_len(tid);
+    }
+    term = __reduce_add_sync(kFullMask, term);
+    if (lane == 0 && term) atomicAdd(&s.fixed_sum, term);
+  }
+  __syncthreads();
   if (tid == 0) {
-    s.freq[256] += 1;
-    u32 fixed_bits = 3 + s.extra_bits;
-    for (u32 i = 0; i < 286; ++i) fixed_bits += s.freq[i] * fixed_ll_len(i);
-    fixed_bits += s.dist_tokens * 5;
+    const u32 fixed_bits = 3 + s.extra_bits + s.fixed_sum + s.dist_tokens * 5;
     s.mode = 0;
     s.extent = n + 5 * stored_blocks(n);
     const u32 fixed_extent = extent_of(fixed_bits, final);
@@ -841,9 +916,12 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
   bool dynamic = s.ok != 0;
   if (dynamic) {
     trees = cta_tree(s, s.freq, 286, 15, s.lengths, s.codes);
+    u32 term = tid < 286 ? s.freq[tid] * s.lengths[tid] : 0u;
+    term = __reduce_add_sync(kFullMask, term);
+    if (lane == 0 && term) atomicAdd(&s.ll_sum, term);
+    __syncthreads();
     if (tid == 0) {
-      u32 ll_bits = 0;
-      for (u32 i = 0; i < 286; ++i) ll_bits += s.freq[i] * s.lengths[i];
+      const u32 ll_bits = s.ll_sum;
       s.header_bits = ll_bits;  // reused below as ll_bits
       s.ok = extent_of(29 + s.extra_bits + ll_bits + s.dist_tokens, final) < s.extent;
     }
@@ -937,18 +1015,28 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
     }
     __syncthreads();
   }
-  if (tid == 0) {
-    if (!trees) {
-      s.mode = 3;
-      s.status = 1;
-    } else if (dynamic) {
-      u32 bits = 17 + 3 * s.ncl + s.extra_bits + s.header_bits;
-      for (u32 i = 0; i < 30; ++i) bits += s.freq[286 + i] * s.lengths[286 + i];
-      for (u32 i = 0; i < 19; ++i)
-        bits += s.freq[316 + i] *
-                (s.lengths[316 + i] + (i == 16 ? 2u : i == 17 ? 3u : i == 18 ? 7u : 0u));
-      const u32 dyn_extent = extent_of(bits, final);
-      if (dyn_extent < s.extent) { s.extent = dyn_extent; s.mode = 2; }
+  if (warp == 0) {
+    // Distance and code-length symbol bits (the latter with their repeat
+    // codes' extra bits), two terms a lane.
+    u32 tail_bits = 0;
+    if (trees && dynamic) {
+      for (u32 i = lane; i < 49; i += 32) {
+        const u32 j = i - 30;
+        tail_bits += i < 30 ? s.freq[286 + i] * s.lengths[286 + i]
+                            : s.freq[316 + j] * (s.lengths[316 + j] +
+                                                 (j == 16 ? 2u : j == 17 ? 3u : j == 18 ? 7u : 0u));
+      }
+      tail_bits = __reduce_add_sync(kFullMask, tail_bits);
+    }
+    if (lane == 0) {
+      if (!trees) {
+        s.mode = 3;
+        s.status = 1;
+      } else if (dynamic) {
+        const u32 bits = 17 + 3 * s.ncl + s.extra_bits + s.header_bits + tail_bits;
+        const u32 dyn_extent = extent_of(bits, final);
+        if (dyn_extent < s.extent) { s.extent = dyn_extent; s.mode = 2; }
+      }
     }
   }
   __syncthreads();
