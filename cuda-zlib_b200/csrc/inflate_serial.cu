@@ -154,8 +154,18 @@ __device__ u32 warp_inflate_one(const u8* in, u64 in_size64, u8* out, u64 out_si
         const u32 stop_at =
             min_u32(out_size >= 258 ? out_size - 258 : 0, flushed + kFlushBytes);
         const u32 idx_limit = full_words >= 2 ? full_words - 1 : 0;
+        // The next input word is loaded one refill ahead, so a refill
+        // appends a register instead of waiting on its load.
+        u32 ahead = c.load(c.idx);
+        auto refill_ahead = [&]() {
+          if (c.nbits <= 32) {
+            c.append(ahead);
+            ++c.idx;
+            ahead = c.load(c.idx);
+          }
+        };
         while (c.idx < idx_limit && produced < stop_at) {
-          c.refill_fast();
+          refill_ahead();
           const u32 v = c.lo;
           const u32 e = t.ll.lut[v & kLLMask];
           const u32 kind = entry_kind(e);
@@ -171,7 +181,7 @@ __device__ u32 warp_inflate_one(const u8* in, u64 in_size64, u8* out, u64 out_si
           const u32 L = entry_len(e), E = entry_extra(e);
           const u32 length = entry_value(e) + ((v >> L) & ((1u << E) - 1u));
           c.consume(L + E);
-          c.refill_fast();
+          refill_ahead();
           const u32 w = c.lo;
           const u32 d = t.d.lut[w & 255u];
           const u32 Ld = entry_len(d), Ed = entry_extra(d);
