@@ -44,6 +44,7 @@ static_assert((1u << kOwnerBits) == kEncWarps, "one slot class per warp");
 constexpr u32 kSortKeys = 512;  // bitonic sort width of the leaf ranking (>= 286)
 static_assert(kSortKeys == kEncThreads, "one sort key per thread");
 constexpr u32 kCodeWarps = (286 + 31) / 32;  // warps covering the largest alphabet
+constexpr u32 kSerialMergeLeaves = 96;  // at most this many leaves: one-thread merge
 constexpr u32 kPerThread = 8;  // candidate rounds: consecutive positions per thread
 constexpr u32 kRoundPositions = kEncThreads * kPerThread;
 constexpr u32 kHashSlots = 8192;
@@ -139,8 +140,132 @@ struct EncodeShared {
   u64 adler_s2[kEncWarps];
   u32 extra_bits, token_count, dist_tokens;
   u32 mode, extent, status, ok, nll, ndist, ncl, rle_size, header_bits, leaves, only;
-  u32 more, lcount[16], fixed_sum, ll_sum;
+  u32 more, lcount[16], fixed_sum, ll_sum, tree_ok;
 };
+
+// Two-queue merge of m ranked leaves (s.sorted / s.leafw) on one thread:
+// inner node k (id alphabet + k) gets its weight in s.weight and its
+// children's s.parent.  Leaf ids are below every inner id, so equal weights
+// take the leaf.  The head of each queue and the element after it stay in
+// registers, so a pick compares registers and the shared-memory load it
+// starts is needed only a pick later.
+template <typename Shared>
+__device__ void serial_merge(Shared& s, u32 alphabet, u32 m) {
+  u32 leaf = 0, inner = alphabet, next = alphabet;
+  u32 leaf_id = s.sorted[0], leaf_w = s.leafw[0];
+  u32 leaf2_id = m > 1 ? u32(s.sorted[1]) : 0u, leaf2_w = m > 1 ? s.leafw[1] : 0u;
+  u32 inner_w = 0, inner2_w = 0;  // nodes `inner` and `inner + 1`, when they exist
+  for (u32 step = 0; step + 1 < m; ++step) {
+    u32 pick[2], picked_w[2];
+#pragma unroll
+    for (u32 k = 0; k < 2; ++k) {
+      const bool take_leaf = leaf < m && (inner == next || leaf_w <= inner_w);
+      if (take_leaf) {
+        pick[k] = leaf_id;
+        picked_w[k] = leaf_w;
+        ++leaf;
+        leaf_id = leaf2_id;
+        leaf_w = leaf2_w;
+        if (leaf + 1 < m) { leaf2_id = s.sorted[leaf + 1]; leaf2_w = s.leafw[leaf + 1]; }
+      } else {
+        pick[k] = inner;
+        picked_w[k] = inner_w;
+        ++inner;
+        inner_w = inner2_w;
+        if (inner + 1 < next) inner2_w = s.weight[inner + 1];
+      }
+    }
+    const u32 w = picked_w[0] + picked_w[1];
+    s.weight[next] = w;
+    s.parent[pick[0]] = u16(next);
+    s.parent[pick[1]] = u16(next);
+    if (inner == next) inner_w = w;             // the queue was empty
+    else if (inner + 1 == next) inner2_w = w;   // it follows the head
+    ++next;
+  }
+}
+
+// The same build for an alphabet of at most 32 symbols (distances, code
+// lengths) inside one warp, one symbol a lane: ballots count and place the
+// leaves, a shuffle bitonic sort ranks them, lane 0 merges, and depths and
+// canonical codes follow without block barriers.  The calling warp only;
+// returns on its lanes whether a tree within `limit` was found.
+template <typename Shared>
+__device__ bool warp_tree(Shared& s, const u32* freq, u32 alphabet, u32 limit, u8* lengths,
+                          u16* codes) {
+  const u32 lane = threadIdx.x & 31u;
+  const bool symbol = lane < alphabet;
+  const u32 f = symbol ? freq[lane] : 0u;
+  for (u32 shift = 0; shift <= 16; ++shift) {
+    u32 w = f ? ((f + (1u << shift) - 1u) >> shift) : 0u;
+    const u32 present = __ballot_sync(kFullMask, w != 0);
+    u32 m = __popc(present), only = present ? 31 - __clz(present) : 0u;
+    // The reference's dummy leaves for empty and one-symbol alphabets.
+    if (!m) {
+      if (lane == 0) w = 1;
+      m = 1;
+      only = 0;
+    }
+    if (m == 1) {
+      if (lane == (only ? 0u : 1u)) w = 1;
+      m = 2;
+    }
+    if (symbol) s.weight[lane] = w;
+    u32 key = w ? (w << 9) | lane : ~0u;
+    for (u32 k = 2; k <= 32; k <<= 1) {
+      for (u32 j = k >> 1; j; j >>= 1) {
+        const u32 other = __shfl_xor_sync(kFullMask, key, j);
+        key = (((lane & j) == 0) == ((lane & k) == 0)) ? min_u32(key, other) : max_u32(key, other);
+      }
+    }
+    if (lane < m) {
+      s.sorted[lane] = u16(key & 511u);
+      s.leafw[lane] = key >> 9;
+    }
+    __syncwarp();
+    if (lane == 0) serial_merge(s, alphabet, m);
+    __syncwarp();
+    // Depths by pointer doubling over the alphabet + m - 1 <= 63 nodes.
+    const u32 nodes = alphabet + m - 1, root = nodes - 1;
+    for (u32 i = lane; i < nodes; i += 32) {
+      const bool live = i >= alphabet || s.weight[i];
+      const bool top = i == root || !live;
+      s.ancestor[0][i] = u16(top ? root : s.parent[i]);
+      s.depth[0][i] = top ? 0 : 1;
+    }
+    u32 cur = 0;
+    for (;;) {
+      __syncwarp();
+      bool moved = false;
+      for (u32 i = lane; i < nodes; i += 32) {
+        const u32 up = s.ancestor[cur][i];
+        s.depth[cur ^ 1][i] = u8(s.depth[cur][i] + (up == root ? 0u : s.depth[cur][up]));
+        s.ancestor[cur ^ 1][i] = up == root ? u16(root) : s.ancestor[cur][up];
+        moved |= up != root;
+      }
+      cur ^= 1;
+      if (!__any_sync(kFullMask, moved)) break;
+    }
+    __syncwarp();
+    const u32 d = w ? u32(s.depth[cur][lane]) : 0u;
+    const bool overlong = __any_sync(kFullMask, d > limit);
+    // Canonical codes: the first code of each length from the ballot counts,
+    // plus the rank among the lower symbols of the same length.
+    u32 code = 0, first = 0;
+    for (u32 len = 1; len <= 15; ++len) {
+      code = (code + __popc(__ballot_sync(kFullMask, d == len - 1 && len > 1))) << 1;
+      if (len == d) first = code;
+    }
+    const u32 rank = __popc(__match_any_sync(kFullMask, d) & ((1u << lane) - 1u));
+    if (symbol) {
+      lengths[lane] = d <= limit ? u8(d) : 0;
+      codes[lane] = overlong || !d ? 0 : u16(reverse_bits(first + rank, d));
+    }
+    __syncwarp();
+    if (!overlong) return true;
+  }
+  return false;
+}
 
 // Huffman build with the reference's (weight, id) order and flattening
 // retries, spread over the block.  The reference pops its heap by (weight,
@@ -153,8 +278,9 @@ struct EncodeShared {
 // order of a stable merge of the two queues.  A round merges those in
 // parallel (an odd last one waits for the next round) and pairs them into new
 // nodes; t at least doubles every two rounds.  Depths follow by pointer
-// doubling, codes by per-warp ranks.  All threads call; returns on all
-// threads whether a tree within `limit` was found.
+// doubling, codes by per-warp ranks.  For the literal/length alphabet (more
+// than 32 symbols); all threads call; returns on all threads whether a tree
+// within `limit` was found.
 template <typename Shared>
 __device__ bool cta_tree(Shared& s, const u32* freq, u32 alphabet, u32 limit, u8* lengths,
                          u16* codes) {
@@ -191,23 +317,7 @@ __device__ bool cta_tree(Shared& s, const u32* freq, u32 alphabet, u32 limit, u8
     // zero weights last (weights stay below 2^19, ids below 2^9), one key per
     // thread.  Partners within a warp are exchanged by shuffles; farther ones
     // through two shared buffers used in turn, one barrier a stage.
-    if (alphabet <= 32) {
-      if (warp == 0) {
-        const u32 w = lane < alphabet ? s.weight[lane] : 0u;
-        u32 key = w ? (w << 9) | lane : ~0u;
-        for (u32 k = 2; k <= 32; k <<= 1) {
-          for (u32 j = k >> 1; j; j >>= 1) {
-            const u32 other = __shfl_xor_sync(kFullMask, key, j);
-            key = (((lane & j) == 0) == ((lane & k) == 0)) ? min_u32(key, other)
-                                                            : max_u32(key, other);
-          }
-        }
-        if (lane < s.leaves) {
-          s.sorted[lane] = u16(key & 511u);
-          s.leafw[lane] = key >> 9;
-        }
-      }
-    } else {
+    {
       const u32 w = tid < alphabet ? s.weight[tid] : 0u;
       u32 key = w ? (w << 9) | tid : ~0u;
       bool flip = false;
@@ -234,7 +344,11 @@ __device__ bool cta_tree(Shared& s, const u32* freq, u32 alphabet, u32 limit, u8
     __syncthreads();
     const u32 m = s.leaves;
     const u32 nodes = alphabet + m - 1;  // leaves' ids stay below alphabet
-    {
+    if (m <= kSerialMergeLeaves) {
+      // Few leaves: one thread's merge costs less than the rounds' barriers.
+      if (tid == 0) serial_merge(s, alphabet, m);
+      __syncthreads();
+    } else {
       const u32* leafw = s.leafw;
       u32* inner_w = s.weight + alphabet;  // inner node k has id alphabet + k
       u16* merged = s.ancestor[0];         // a round's picks, in order
@@ -929,15 +1043,19 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
     dynamic = s.ok != 0;
   }
   if (trees && dynamic) {
-    trees = cta_tree(s, s.freq + 286, 30, 15, s.lengths + 286, s.codes + 286);
-    if (tid == 0) {
-      u32 nll = 286, ndist = 30;
-      while (nll > 257 && !s.lengths[nll - 1]) --nll;
-      while (ndist > 1 && !s.lengths[286 + ndist - 1]) --ndist;
-      s.nll = nll;
-      s.ndist = ndist;
+    if (warp == 0) {
+      const bool built = warp_tree(s, s.freq + 286, 30, 15, s.lengths + 286, s.codes + 286);
+      if (lane == 0) {
+        u32 nll = 286, ndist = 30;
+        while (nll > 257 && !s.lengths[nll - 1]) --nll;
+        while (ndist > 1 && !s.lengths[286 + ndist - 1]) --ndist;
+        s.nll = nll;
+        s.ndist = ndist;
+        s.tree_ok = built;
+      }
     }
     __syncthreads();
+    trees = s.tree_ok != 0;
     // Run-length code the code lengths (enc_rle, _encode_kernels.py:163-191):
     // the thread at the start of each run of equal lengths emits that run's
     // symbols, in the reference's order, at the place a block scan gives.
@@ -1007,13 +1125,18 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
     }
     if (tid == 0) s.rle_size = rle_size;
     __syncthreads();
-    if (trees) trees = cta_tree(s, s.freq + 316, 19, 7, s.lengths + 316, s.codes + 316);
-    if (tid == 0) {
-      u32 ncl = 19;
-      while (ncl > 4 && !s.lengths[316 + kClOrder[ncl - 1]]) --ncl;
-      s.ncl = ncl;
+    if (warp == 0) {
+      const bool built =
+          trees && warp_tree(s, s.freq + 316, 19, 7, s.lengths + 316, s.codes + 316);
+      if (lane == 0) {
+        u32 ncl = 19;
+        while (ncl > 4 && !s.lengths[316 + kClOrder[ncl - 1]]) --ncl;
+        s.ncl = ncl;
+        s.tree_ok = built;
+      }
     }
     __syncthreads();
+    trees = s.tree_ok != 0;
   }
   if (warp == 0) {
     // Distance and code-length symbol bits (the latter with their repeat
