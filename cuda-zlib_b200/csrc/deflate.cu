@@ -9,7 +9,7 @@
 //   1. stage the chunk in shared memory and fuse its Adler-32 partial sums;
 //   2. every position's candidate: rounds of 4096 positions are sorted into
 //      per-warp lists by hash mod 16; each warp takes its list in order and
-//      finds equal hashes 32 at a time by ballots;
+//      finds equal hashes 32 at a time with a warp match;
 //   3. 256 threads each walk the greedy parse from the start of their own
 //      segment of the chunk, speculatively;
 //   4. one thread stitches the segments: an entry point that differs from the
@@ -658,7 +658,7 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
   // a u64 in 16-bit fields, a warp scan, then per-warp and per-owner
   // offsets), and each warp takes its list in batches of 32.  In a batch the
   // lanes hash their positions again from the staged chunk and find equal
-  // hashes by ballots over the hash bits; a lane's candidate is its last
+  // hashes with one warp match; a lane's candidate is its last
   // earlier equal lane, else the table, and the last lane of each hash writes
   // the table.  Slots are disjoint between warps, so within a round the
   // warps never wait on one another.
@@ -676,12 +676,7 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
       const u32 pos = valid ? u32(list[first + lane]) : 0u;
       const u32 h = valid ? hash_at(pos) : 0u;
       const u32 key = h >> kOwnerBits;  // the low bits equal the warp index
-      u32 same = __ballot_sync(kFullMask, valid);
-#pragma unroll
-      for (u32 bit = 0; bit < 13 - kOwnerBits; ++bit) {
-        const u32 ones = __ballot_sync(kFullMask, valid && ((key >> bit) & 1u));
-        same &= ((key >> bit) & 1u) ? ones : ~ones;
-      }
+      const u32 same = __match_any_sync(kFullMask, valid ? key : ~0u);
       const u32 lower = same & ((1u << lane) - 1u);
       const u32 from = __shfl_sync(kFullMask, pos, lower ? 31 - __clz(lower) : lane);
       u32 candidate = 0;
@@ -697,10 +692,26 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
       const u32 p0 = base + kPerThread * tid;
       // Owner o's count in 16-bit field o % 4 of c[o / 4] (no runtime
       // indexing, so the four words stay in registers).  Owners are hashed
-      // again for the scatter below rather than kept across the barriers.
-      auto owner_of = [&](u32 p) -> u32 {
-        return p < hashed ? hash_at(p) & (kEncWarps - 1) : kEncWarps;
+      // again for the scatter below rather than kept across the barriers:
+      // the thread's positions lie in three aligned words (p0 is a multiple
+      // of 8), read once a pass, and position p0 + k hashes from them by
+      // funnel shifts (a thread wholly past the hashed positions reads
+      // nothing).
+      u32 x0 = 0, x1 = 0, x2 = 0;
+      auto load_words = [&]() {
+        if (p0 < hashed) {
+          const u32* wp = words + (p0 >> 2);
+          x0 = wp[0];
+          x1 = wp[1];
+          x2 = wp[2];
+        }
       };
+      auto owner_of = [&](u32 p) -> u32 {
+        const u32 k = p - p0;
+        const u32 v = __funnelshift_r(k < 4 ? x0 : x1, k < 4 ? x1 : x2, (k & 3u) * 8u) & 0xffffffu;
+        return p < hashed ? ((v * 2654435761u) >> 19) & (kEncWarps - 1) : kEncWarps;
+      };
+      load_words();
       u64 c0 = 0, c1 = 0, c2 = 0, c3 = 0;
 #pragma unroll
       for (u32 k = 0; k < kPerThread; ++k) {
@@ -754,6 +765,7 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
       }
       __syncthreads();
       u64 n0 = i0 - c0, n1 = i1 - c1, n2 = i2 - c2, n3 = i3 - c3;  // earlier lanes' counts
+      load_words();
 #pragma unroll
       for (u32 k = 0; k < kPerThread; ++k) {
         const u32 o = owner_of(p0 + k);
