@@ -8,8 +8,9 @@
 // matches, computes Adler-32 and clears a failed output.
 //
 // Work distribution: a persistent grid; each warp pops stream indices from a
-// device counter in largest-first order, so a few long streams never sit
-// behind a queue of short ones.
+// device counter in order of estimated decode cost, costliest first (the
+// host's order in decompress_batch), so a few long streams never sit behind
+// a queue of short ones and the last streams taken are quick.
 //
 // History: every produced byte is written to the output and to a per-warp
 // shared-memory ring of kRing bytes.  Matches within the ring read shared
