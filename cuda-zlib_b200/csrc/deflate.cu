@@ -45,8 +45,10 @@ constexpr u32 kSortKeys = 512;  // bitonic sort width of the leaf ranking (>= 28
 static_assert(kSortKeys == kEncThreads, "one sort key per thread");
 constexpr u32 kCodeWarps = (286 + 31) / 32;  // warps covering the largest alphabet
 constexpr u32 kSerialMergeLeaves = 96;  // at most this many leaves: one-thread merge
-constexpr u32 kPerThread = 8;  // candidate rounds: consecutive positions per thread
-constexpr u32 kRoundPositions = kEncThreads * kPerThread;
+// Candidate rounds: consecutive positions per thread (fewer for u32
+// positions, whose round list would not fit the static shared limit).
+template <typename Pos>
+__host__ __device__ constexpr u32 per_thread() { return sizeof(Pos) == 2 ? 16u : 8u; }
 constexpr u32 kHashSlots = 8192;
 constexpr u32 kStitchRounds = 8;  // parallel stitch rounds before the serial finish
 constexpr u32 kStoredMax = 65535;  // bytes of one stored block
@@ -127,7 +129,7 @@ struct EncodeShared {
   u8 depth[2][576];
   u8 rle_sym[320];
   u8 rle_extra[320];
-  Pos round_list[kRoundPositions];     // candidate round: positions by owner
+  Pos round_list[kEncThreads * per_thread<Pos>()];  // candidate round: positions by owner
   u16 owner_count[kEncWarps][kEncWarps];   // per warp, per owner
   u16 owner_before[kEncWarps][kEncWarps];  // per warp, per owner: earlier warps' count
   u16 owner_total[kEncWarps], owner_start[kEncWarps];
@@ -652,8 +654,8 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
   // 2. Candidates: prev[p] = 1 + the last earlier position with hash(p), or
   // 0 (the reference inserts every position into its one-entry table in
   // order, so this is the table's entry when p is reached).  Warp w owns the
-  // table slots h with h % 16 == w.  Rounds of kRoundPositions positions,
-  // eight consecutive ones per thread: the block sorts the round's positions
+  // table slots h with h % 16 == w.  Rounds of 8192 positions (4096 for u32
+  // positions), 16 (8) consecutive ones per thread: the block sorts the round's positions
   // into per-owner lists in position order (counts per owner packed four to
   // a u64 in 16-bit fields, a warp scan, then per-warp and per-owner
   // offsets), and each warp takes its list in batches of 32.  In a batch the
@@ -688,27 +690,25 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
       }
       __syncwarp();
     };
+    constexpr u32 kPerThread = per_thread<Pos>(), kRoundPositions = kEncThreads * kPerThread;
     for (u32 base = 0; base < hashed; base += kRoundPositions) {
       const u32 p0 = base + kPerThread * tid;
       // Owner o's count in 16-bit field o % 4 of c[o / 4] (no runtime
       // indexing, so the four words stay in registers).  Owners are hashed
       // again for the scatter below rather than kept across the barriers:
-      // the thread's positions lie in three aligned words (p0 is a multiple
-      // of 8), read once a pass, and position p0 + k hashes from them by
-      // funnel shifts (a thread wholly past the hashed positions reads
-      // nothing).
-      u32 x0 = 0, x1 = 0, x2 = 0;
+      // the thread's positions lie in kPerThread / 4 + 1 aligned words (p0
+      // is a multiple of 8), read once a pass, and position p0 + k hashes
+      // from them by funnel shifts (a thread wholly past the hashed
+      // positions reads nothing).
+      constexpr u32 kWords = kPerThread / 4 + 1;
+      u32 x[kWords];
       auto load_words = [&]() {
-        if (p0 < hashed) {
-          const u32* wp = words + (p0 >> 2);
-          x0 = wp[0];
-          x1 = wp[1];
-          x2 = wp[2];
-        }
+#pragma unroll
+        for (u32 i = 0; i < kWords; ++i) x[i] = p0 < hashed ? words[(p0 >> 2) + i] : 0u;
       };
       auto owner_of = [&](u32 p) -> u32 {
-        const u32 k = p - p0;
-        const u32 v = __funnelshift_r(k < 4 ? x0 : x1, k < 4 ? x1 : x2, (k & 3u) * 8u) & 0xffffffu;
+        const u32 k = p - p0;  // a constant once the callers' loops unroll
+        const u32 v = __funnelshift_r(x[k >> 2], x[(k >> 2) + 1], (k & 3u) * 8u) & 0xffffffu;
         return p < hashed ? ((v * 2654435761u) >> 19) & (kEncWarps - 1) : kEncWarps;
       };
       load_words();
