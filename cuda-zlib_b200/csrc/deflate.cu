@@ -46,9 +46,10 @@ static_assert(kSortKeys == kEncThreads, "one sort key per thread");
 constexpr u32 kCodeWarps = (286 + 31) / 32;  // warps covering the largest alphabet
 constexpr u32 kSerialMergeLeaves = 96;  // at most this many leaves: one-thread merge
 // Candidate rounds: consecutive positions per thread (fewer for u32
-// positions, whose round list would not fit the static shared limit).
+// positions, whose round list would not fit the static shared limit).  The
+// round list shares its shared memory with the arrays of the later phases.
 template <typename Pos>
-__host__ __device__ constexpr u32 per_thread() { return sizeof(Pos) == 2 ? 16u : 8u; }
+__host__ __device__ constexpr u32 per_thread() { return sizeof(Pos) == 2 ? 32u : 16u; }
 constexpr u32 kHashSlots = 8192;
 constexpr u32 kStitchRounds = 8;  // parallel stitch rounds before the serial finish
 constexpr u32 kStoredMax = 65535;  // bytes of one stored block
@@ -116,26 +117,30 @@ __host__ __device__ __forceinline__ u32 stored_blocks(u32 n) {
 template <typename Pos>
 struct EncodeShared {
   u32 freq[335];        // 0..285 lit/len, 286..315 dist, 316..334 code-length
-  u8 lengths[336];
-  u16 codes[336];
-  u32 weight[576];
-  u16 parent[576];
-  u16 ancestor[2][576];
-  u16 sorted[288];
-  u32 leafw[288];      // weights in leaf rank order
-  u32 sort_keys[kSortKeys];  // leaf ranking: (weight << 9 | id) keys
-  u32 sort_swap[kSortKeys];  // the ranking's second exchange buffer
-  u16 warp_len[kCodeWarps][16];  // codes: per warp, symbols of each length
-  u8 depth[2][576];
-  u8 rle_sym[320];
-  u8 rle_extra[320];
-  Pos round_list[kEncThreads * per_thread<Pos>()];  // candidate round: positions by owner
   u16 owner_count[kEncWarps][kEncWarps];   // per warp, per owner
   u16 owner_before[kEncWarps][kEncWarps];  // per warp, per owner: earlier warps' count
   u16 owner_total[kEncWarps], owner_start[kEncWarps];
-  u32 seg_exit[kEncThreads];
-  u32 seg_entry[kEncThreads];
-  u32 seg_bits[kEncThreads];
+  union {
+    Pos round_list[kEncThreads * per_thread<Pos>()];  // candidate round: positions by owner
+    struct {  // the phases after the candidates
+      u8 lengths[336];
+      u16 codes[336];
+      u32 weight[576];
+      u16 parent[576];
+      u16 ancestor[2][576];
+      u16 sorted[288];
+      u32 leafw[288];      // weights in leaf rank order
+      u32 sort_keys[kSortKeys];  // leaf ranking: (weight << 9 | id) keys
+      u32 sort_swap[kSortKeys];  // the ranking's second exchange buffer
+      u16 warp_len[kCodeWarps][16];  // codes: per warp, symbols of each length
+      u8 depth[2][576];
+      u8 rle_sym[320];
+      u8 rle_extra[320];
+      u32 seg_exit[kEncThreads];
+      u32 seg_entry[kEncThreads];
+      u32 seg_bits[kEncThreads];
+    };
+  };
   u32 warp_sums[kEncWarps];
   u32 rle_sums[kEncWarps];
   u64 adler_s1[kEncWarps];
@@ -654,8 +659,8 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
   // 2. Candidates: prev[p] = 1 + the last earlier position with hash(p), or
   // 0 (the reference inserts every position into its one-entry table in
   // order, so this is the table's entry when p is reached).  Warp w owns the
-  // table slots h with h % 16 == w.  Rounds of 8192 positions (4096 for u32
-  // positions), 16 (8) consecutive ones per thread: the block sorts the round's positions
+  // table slots h with h % 16 == w.  Rounds of 16384 positions (8192 for
+  // u32 positions), 32 (16) consecutive ones per thread: the block sorts the round's positions
   // into per-owner lists in position order (counts per owner packed four to
   // a u64 in 16-bit fields, a warp scan, then per-warp and per-owner
   // offsets), and each warp takes its list in batches of 32.  In a batch the
