@@ -1290,14 +1290,15 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
       if (match) {
         const u32 m = u32(lenv[p]) + 3, dist = thorough ? u32(distv[p]) : p - (u32(prev[p]) - 1);
         const u32 li = length_symbol(m), di = dist_symbol(dist);
-        if (dyn) pk.put(s.codes[257 + li], s.lengths[257 + li]);
-        else pk.put(fixed_ll_code(257 + li), fixed_ll_len(257 + li));
+        // Each code with its extra bits in one put (at most 20 and 28 bits).
+        const u32 lc = dyn ? u32(s.codes[257 + li]) : fixed_ll_code(257 + li);
+        const u32 ll = dyn ? u32(s.lengths[257 + li]) : fixed_ll_len(257 + li);
         const u32 le = length_extra_bits(li);
-        pk.put(low_bits(m - 3, le), le);
-        if (dyn) pk.put(s.codes[286 + di], s.lengths[286 + di]);
-        else pk.put(reverse_bits(di, 5), 5);
+        pk.put(lc | (low_bits(m - 3, le) << ll), ll + le);
+        const u32 dc = dyn ? u32(s.codes[286 + di]) : reverse_bits(di, 5);
+        const u32 dl = dyn ? u32(s.lengths[286 + di]) : 5u;
         const u32 de = dist_extra_bits(di);
-        pk.put(low_bits(dist - 1, de), de);
+        pk.put(dc | (low_bits(dist - 1, de) << dl), dl + de);
       } else {
         const u32 lit = data[p];
         if (dyn) pk.put(s.codes[lit], s.lengths[lit]);
