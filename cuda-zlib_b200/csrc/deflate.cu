@@ -139,6 +139,7 @@ struct EncodeShared {
       u32 seg_exit[kEncThreads];
       u32 seg_entry[kEncThreads];
       u32 seg_bits[kEncThreads];
+      u32 sym_code[316];  // packing: code | length << 16 per symbol
     };
   };
   u32 warp_sums[kEncWarps];
@@ -478,15 +479,15 @@ struct Packer {
   u32* words;
   u64 acc;
   u32 nacc;   // bits in acc
-  u64 word;   // index of the word acc starts at
-  u64 first_word, last_word;  // this thread's shared edge words
-  u64 limit;  // words past the slot are dropped (the size check then fails)
+  u32 word;   // index of the word acc starts at (a slot holds under 2^16 words)
+  u32 first_word, last_word;  // this thread's shared edge words
+  u32 limit;  // words past the slot are dropped (the size check then fails)
 
-  __device__ __forceinline__ void start(u32* w, u64 bit, u64 end_bit, u64 limit_words) {
+  __device__ __forceinline__ void start(u32* w, u32 bit, u32 end_bit, u32 limit_words) {
     limit = limit_words;
     words = w;
     word = bit >> 5;
-    nacc = u32(bit & 31);
+    nacc = bit & 31u;
     acc = 0;
     first_word = word;
     last_word = end_bit ? (end_bit - 1) >> 5 : 0;
@@ -1211,15 +1212,32 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
 
   // 8. Parallel bit packing.
   const bool dyn = mode == 2;
+  // Each literal/length and distance symbol's code (low 16 bits, ready to
+  // put) and code length (high bits), dynamic or fixed, read once a token.
+  for (u32 i = tid; i < 316; i += kEncThreads) {
+    u32 code, len;
+    if (dyn) {
+      code = s.codes[i];
+      len = s.lengths[i];
+    } else if (i < 286) {
+      code = fixed_ll_code(i);
+      len = fixed_ll_len(i);
+    } else {
+      code = reverse_bits(i - 286, 5);
+      len = 5;
+    }
+    s.sym_code[i] = code | (len << 16);
+  }
+  __syncthreads();
   u32 my_bits = 0;
   for_each_token(member, ismatch, a, b, [&](u32 p, bool match) {
     if (match) {
       const u32 m = u32(lenv[p]) + 3, dist = thorough ? u32(distv[p]) : p - (u32(prev[p]) - 1);
       const u32 li = length_symbol(m), di = dist_symbol(dist);
-      my_bits += (dyn ? s.lengths[257 + li] : fixed_ll_len(257 + li)) + length_extra_bits(li) +
-                 (dyn ? s.lengths[286 + di] : 5u) + dist_extra_bits(di);
+      my_bits += (s.sym_code[257 + li] >> 16) + length_extra_bits(li) +
+                 (s.sym_code[286 + di] >> 16) + dist_extra_bits(di);
     } else {
-      my_bits += dyn ? s.lengths[data[p]] : fixed_ll_len(data[p]);
+      my_bits += s.sym_code[data[p]] >> 16;
     }
   });
   // Bits of this thread's run-length coded length (a dynamic header codes at
@@ -1291,18 +1309,15 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
         const u32 m = u32(lenv[p]) + 3, dist = thorough ? u32(distv[p]) : p - (u32(prev[p]) - 1);
         const u32 li = length_symbol(m), di = dist_symbol(dist);
         // Each code with its extra bits in one put (at most 20 and 28 bits).
-        const u32 lc = dyn ? u32(s.codes[257 + li]) : fixed_ll_code(257 + li);
-        const u32 ll = dyn ? u32(s.lengths[257 + li]) : fixed_ll_len(257 + li);
+        const u32 lsym = s.sym_code[257 + li], ll = lsym >> 16;
         const u32 le = length_extra_bits(li);
-        pk.put(lc | (low_bits(m - 3, le) << ll), ll + le);
-        const u32 dc = dyn ? u32(s.codes[286 + di]) : reverse_bits(di, 5);
-        const u32 dl = dyn ? u32(s.lengths[286 + di]) : 5u;
+        pk.put((lsym & 0xffffu) | (low_bits(m - 3, le) << ll), ll + le);
+        const u32 dsym = s.sym_code[286 + di], dl = dsym >> 16;
         const u32 de = dist_extra_bits(di);
-        pk.put(dc | (low_bits(dist - 1, de) << dl), dl + de);
+        pk.put((dsym & 0xffffu) | (low_bits(dist - 1, de) << dl), dl + de);
       } else {
-        const u32 lit = data[p];
-        if (dyn) pk.put(s.codes[lit], s.lengths[lit]);
-        else pk.put(fixed_ll_code(lit), fixed_ll_len(lit));
+        const u32 lsym = s.sym_code[data[p]];
+        pk.put(lsym & 0xffffu, lsym >> 16);
       }
     });
     pk.finish();
@@ -1314,7 +1329,7 @@ encode_chunks_kernel(const u8* __restrict__ in, const EncodeFile* __restrict__ f
     u32 tail_bits = dyn ? s.lengths[256] : 7u;
     pk.start(words, at, at + tail_bits + 3, used_words);
     pk.first_word = pk.word;
-    pk.last_word = ~0ull;
+    pk.last_word = ~0u;
     if (dyn) pk.put(s.codes[256], s.lengths[256]);
     else pk.put(fixed_ll_code(256), 7);
     u32 end = at + tail_bits;
