@@ -322,7 +322,10 @@ def _batch_sizes(sizes, label):
     if not isinstance(sizes, (tuple, list)) or not 1 <= len(sizes) <= _MAX_BLOCKS:
         raise ValueError(label + " must contain between 1 and 262144 static sizes")
     sizes = tuple(sizes)
-    if any(type(size) is not int or not 0 <= size <= _MAX_BYTES for size in sizes):
+    # Exact ints only (bool and NumPy integers are refused), each in range;
+    # checked by C-level passes, a batch call issues thousands of sizes.
+    if (not set(map(type, sizes)) <= {int} or min(sizes) < 0 or
+            max(sizes) > _MAX_BYTES):
         raise ValueError(label + " must contain integers in [0, 2**28]")
     if sum(sizes) > _MAX_BYTES:
         raise ValueError(label + " total exceeds 2**28 bytes")
@@ -346,9 +349,9 @@ def _batch_capacities(sizes, chunk_bytes):
 
 
 def _i64_array(values):
-    import ctypes
-    array = (ctypes.c_int64 * len(values))(*values)
-    return array
+    """The values as a C int64 array (one C-level copy through NumPy; the
+    ctypes array keeps its buffer alive)."""
+    return np.ctypeslib.as_ctypes(np.array(values, dtype=np.int64))
 
 
 def _batch_encode_call(data, input_sizes, device, chunk_bytes, entry):
