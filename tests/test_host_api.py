@@ -13,6 +13,7 @@ import re
 import struct
 import subprocess
 
+import numpy as np
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -69,6 +70,21 @@ def test_batch_invalid_static_sizes(no_backend, sizes):
         no_backend.compress_zlib_batch_padded(b"", sizes)
     with pytest.raises(ValueError):
         no_backend.decompress_zlib_batch_checked(b"", sizes, (0,))
+
+
+@pytest.mark.parametrize("sizes, message", [
+    ((3, True), "must contain integers"),        # bool after good sizes
+    ((np.int64(3),), "must contain integers"),   # NumPy integers are not ints
+    ((1, 2, -1), "must contain integers"),
+    ((1, 2**28 + 1), "must contain integers"),
+    ((2**27, 2**27, 1), "total exceeds 2\\*\\*28"),
+    (tuple([1] * 262145), "between 1 and 262144"),
+])
+def test_batch_static_sizes_messages(no_backend, sizes, message):
+    """The size checks run as C-level passes over the whole list; each
+    failure keeps the message of its class, wherever the bad size sits."""
+    with pytest.raises(ValueError, match=message):
+        no_backend.decompress_zlib_batch_checked(b"", list(sizes), list(sizes))
 
 
 def test_batch_invalid_extents_and_chunks(no_backend):
